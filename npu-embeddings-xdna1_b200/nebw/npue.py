@@ -1,0 +1,188 @@
+"""The `.npue` weight container, written and read without the reference tree.
+
+The container is the reference's model file (tools/lib/npue.py:1-35, :261,
+:790-872; C++ reader runtime/src/model.cpp:214-380).  This module is an
+independent implementation of the same on-disk format, because the format is
+the interface: a container written here must be readable by the reference's
+own `npue::File`, and the B200 library stages its weights from one.
+
+  [0:64]                  header "<4sIII QQQQ 16s": magic b"NPUE", version 1,
+                          arch, flags, json_offset, json_length, data_offset,
+                          data_length, 16 reserved bytes
+  [json_offset:+len]      UTF-8 JSON {"config": {...}, "tensors": [entry...]}
+  [data_offset:+len]      tensor bytes, each tensor 4096-byte aligned;
+                          data_offset itself 4096-aligned
+
+An entry is {name, role, dtype, logical_shape, padded_shape, offset, nbytes}
+with `offset` relative to data_offset.  tests/test_npue_format.py checks that
+this writer produces byte-identical files to the reference writer.
+"""
+
+from __future__ import annotations
+
+import json
+import mmap
+import struct
+from pathlib import Path
+
+import numpy as np
+
+MAGIC = b"NPUE"
+VERSION = 1
+HEADER = struct.Struct("<4sIII QQQQ 16s")
+ALIGN = 4096
+ARCH_BERT = 0
+FLAG_PRETILED = 1
+
+DTYPES = {
+    "F32": np.dtype("<f4"),
+    "I32": np.dtype("<i4"),
+    "I64": np.dtype("<i8"),
+    "U16": np.dtype("<u2"),
+    "BF16": np.dtype("<u2"),
+    "I8": np.dtype("<i1"),
+    "U8": np.dtype("<u1"),
+}
+
+
+def _pad(n: int) -> int:
+    return (-n) % ALIGN
+
+
+class ContainerWriter:
+    """Collects tensors, then writes header + directory + aligned data."""
+
+    def __init__(self, config: dict, arch: int = ARCH_BERT, flags: int = FLAG_PRETILED):
+        self.config = dict(config)
+        self.arch = arch
+        self.flags = flags
+        self._entries: list[dict] = []
+        self._arrays: list[np.ndarray] = []
+        self._cursor = 0
+
+    def add(self, name: str, array, dtype: str, role: str, shape) -> dict:
+        arr = np.ascontiguousarray(array, dtype=DTYPES[dtype])
+        nbytes = arr.nbytes
+        entry = {
+            "name": name,
+            "role": role,
+            "dtype": dtype,
+            "logical_shape": [int(s) for s in shape],
+            "padded_shape": [int(s) for s in shape],
+            "offset": self._cursor,
+            "nbytes": nbytes,
+        }
+        self._entries.append(entry)
+        self._arrays.append(arr)
+        self._cursor += nbytes + _pad(nbytes)
+        return entry
+
+    def write(self, path) -> int:
+        directory = json.dumps({"config": self.config, "tensors": self._entries},
+                               separators=(",", ":")).encode("utf-8")
+        json_offset = HEADER.size
+        data_offset = json_offset + len(directory)
+        data_offset += _pad(data_offset)
+        head = HEADER.pack(MAGIC, VERSION, self.arch, self.flags, json_offset,
+                           len(directory), data_offset, self._cursor, b"\0" * 16)
+        with open(path, "wb") as f:
+            f.write(head)
+            f.write(directory)
+            f.write(b"\0" * (data_offset - json_offset - len(directory)))
+            for arr in self._arrays:
+                # tofile streams without building a second copy of big tensors
+                arr.tofile(f)
+                f.write(b"\0" * _pad(arr.nbytes))
+        return data_offset + self._cursor
+
+
+class ContainerReader:
+    """mmap reader; `tensor(name)` returns a read-only numpy view."""
+
+    def __init__(self, path):
+        self.path = str(path)
+        self._file = open(self.path, "rb")
+        self._map = mmap.mmap(self._file.fileno(), 0, access=mmap.ACCESS_READ)
+        (magic, version, self.arch, self.flags, jo, jl, self.data_offset,
+         self.data_length, _) = HEADER.unpack_from(self._map, 0)
+        if magic != MAGIC:
+            raise ValueError(f"{path}: not a .npue container (magic {magic!r})")
+        if version != VERSION:
+            raise ValueError(f"{path}: container version {version}, expected {VERSION}")
+        if self.data_offset % ALIGN:
+            raise ValueError(f"{path}: data_offset is not {ALIGN}-aligned")
+        d = json.loads(bytes(self._map[jo:jo + jl]).decode("utf-8"))
+        self.config = d["config"]
+        self.entries = {e["name"]: e for e in d["tensors"]}
+
+    def tensor(self, name: str) -> np.ndarray:
+        e = self.entries[name]
+        start = self.data_offset + e["offset"]
+        a = np.frombuffer(self._map, dtype=DTYPES[e["dtype"]],
+                          count=e["nbytes"] // DTYPES[e["dtype"]].itemsize, offset=start)
+        return a.reshape(e["logical_shape"])
+
+    def close(self):
+        self._map.close()
+        self._file.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False
+
+
+def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synthetic/random-init"):
+    """Write a BERT (arch 0) container in the host layout the reference's CPU
+    path reads: GEMM operands F32 row-major [K, N] (`gemm_b_host`), biases and
+    LayerNorm F32, embeddings F32.  Tensor names and config keys follow the
+    reference packer's BERT branch (tools/pack/pack_npue.py:2640-2790); the
+    config keys are the ones set_model_shape() requires
+    (runtime/include/common/app_state.hpp:380-631)."""
+    H, F, L = model.hidden, model.ffn, model.layers
+    config = {
+        "arch": "bert_abs_gelu_postln",
+        "source_repo": source_repo,
+        "source_sha256": model.fingerprint(),
+        "num_layers": L, "num_heads": model.heads, "hidden": H,
+        "head_dim": model.head_dim, "intermediate": F,
+        "layer_norm_eps": 1e-12,
+        "vocab_size": model.vocab,
+        "max_seq_len": int(max_seq_len),
+        "pooling": "cls" if model.cls_pool else "mean",
+        "l2_normalize": True,
+        "activation": "gelu_erf_exact",
+        "gemm_layout": "host",
+        "a_dtype": "f32",
+        "fusions": {
+            "qkv_fused": True,
+            "transposed_to_kn": True,
+            "qk_scale_folded_into_q": True,
+            "gemm_operands_bf16": False,
+            "biases_and_layernorm_fp32": True,
+            "position_embeddings_presliced_to": int(max_seq_len),
+        },
+    }
+    w = ContainerWriter(config)
+    w.add("embeddings.word", model.word, "F32", "embedding", [model.vocab, H])
+    w.add("embeddings.position", model.pos[:max_seq_len], "F32", "embedding", [max_seq_len, H])
+    w.add("embeddings.token_type", model.typ, "F32", "embedding", [model.typ.shape[0], H])
+    w.add("embeddings.ln.weight", model.emb_ln_g, "F32", "layernorm", [H])
+    w.add("embeddings.ln.bias", model.emb_ln_b, "F32", "layernorm", [H])
+    for i in range(L):
+        p = f"layer.{i}."
+        w.add(p + "qkv", model.w_qkv[i], "F32", "gemm_b_host", [H, 3 * H])
+        w.add(p + "qkv.bias", model.b_qkv[i], "F32", "bias", [3 * H])
+        w.add(p + "attn_out", model.w_ao[i], "F32", "gemm_b_host", [H, H])
+        w.add(p + "attn_out.bias", model.b_ao[i], "F32", "bias", [H])
+        w.add(p + "ln1.weight", model.ln1_g[i], "F32", "layernorm", [H])
+        w.add(p + "ln1.bias", model.ln1_b[i], "F32", "layernorm", [H])
+        w.add(p + "ffn_up", model.w_up[i], "F32", "gemm_b_host", [H, F])
+        w.add(p + "ffn_up.bias", model.b_up[i], "F32", "bias", [F])
+        w.add(p + "ffn_down", model.w_dn[i], "F32", "gemm_b_host", [F, H])
+        w.add(p + "ffn_down.bias", model.b_dn[i], "F32", "bias", [H])
+        w.add(p + "ln2.weight", model.ln2_g[i], "F32", "layernorm", [H])
+        w.add(p + "ln2.bias", model.ln2_b[i], "F32", "layernorm", [H])
+    return w.write(path)

@@ -1,0 +1,399 @@
+/* TEST INFRASTRUCTURE ONLY -- the parity oracle, never shipped.
+ *
+ * Plain-C restatement of the reference's host-CPU BERT path.  Each function
+ * names the reference code it follows.  The reference build is
+ * -O2 -march=x86-64-v3 (runtime/CMakeLists.txt:297-302), so its host kernels
+ * take their AVX2 branches; this file restates the ARITHMETIC ORDER of those
+ * branches in scalar C -- eight-lane partial sums reduced the way hsum256
+ * reduces them, fused multiply-adds exactly where _mm256_fmadd_ps stands --
+ * so that it reproduces the compiled reference closely (bit-exactly where the
+ * compiler contracts the same way; tests/test_oracle_pin.py measures it).
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load
+ * this library.
+ */
+#define _GNU_SOURCE
+#include "bert_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+static __thread char g_err[512];
+
+const char *nebw_oracle_last_error(void) { return g_err; }
+
+static int fail(const char *msg) {
+  snprintf(g_err, sizeof g_err, "%s", msg);
+  return 1;
+}
+
+/* ---- a tiny static-chunk parallel-for (stands in for app::Pool) ---------- */
+
+typedef void (*range_fn)(void *ctx, int64_t lo, int64_t hi);
+typedef struct {
+  range_fn fn;
+  void *ctx;
+  int64_t lo, hi;
+} job_t;
+
+static void *job_main(void *p) {
+  job_t *j = (job_t *)p;
+  if (j->lo < j->hi) j->fn(j->ctx, j->lo, j->hi);
+  return NULL;
+}
+
+static void parallel_for(int64_t n, int32_t threads, range_fn fn, void *ctx) {
+  if (threads <= 1 || n <= 1) {
+    fn(ctx, 0, n);
+    return;
+  }
+  if (threads > 256) threads = 256;
+  if ((int64_t)threads > n) threads = (int32_t)n;
+  pthread_t tid[256];
+  job_t jobs[256];
+  const int64_t chunk = (n + threads - 1) / threads;
+  for (int32_t w = 0; w < threads; ++w) {
+    int64_t lo = chunk * w, hi = lo + chunk;
+    if (lo > n) lo = n;
+    if (hi > n) hi = n;
+    jobs[w] = (job_t){fn, ctx, lo, hi};
+    if (w > 0) pthread_create(&tid[w], NULL, job_main, &jobs[w]);
+  }
+  job_main(&jobs[0]);
+  for (int32_t w = 1; w < threads; ++w) pthread_join(tid[w], NULL);
+}
+
+/* ---- arithmetic primitives ----------------------------------------------- */
+
+/* hsum256 (runtime/include/common/host_kernels.hpp:617-623): lo = v[0:4] +
+ * v[4:8], then two horizontal adds. */
+static inline float hsum8(const float s[8]) {
+  const float lo0 = s[0] + s[4], lo1 = s[1] + s[5];
+  const float lo2 = s[2] + s[6], lo3 = s[3] + s[7];
+  return (lo0 + lo1) + (lo2 + lo3);
+}
+
+/* exp2_avx2 (host_kernels.hpp:354-380): k = trunc(x), f = x - k, degree-7
+ * Horner polynomial in f with the reference's own coefficients, times 2^k
+ * built from the exponent bits. */
+static inline float exp2_ref(float x) {
+  const int32_t k = (int32_t)x;
+  const float f = x - (float)k;
+  float pl = fmaf(1.5483275463e-05f, f, 1.5669833174e-04f);
+  pl = fmaf(pl, f, 1.3331825236e-03f);
+  pl = fmaf(pl, f, 9.6164605538e-03f);
+  pl = fmaf(pl, f, 5.5504156855e-02f);
+  pl = fmaf(pl, f, 2.4022684109e-01f);
+  pl = fmaf(pl, f, 6.9314717694e-01f);
+  pl = fmaf(pl, f, 9.9999998955e-01f);
+  const uint32_t bits = (uint32_t)(k + 127) << 23;
+  float p2;
+  memcpy(&p2, &bits, sizeof p2);
+  return pl * p2;
+}
+
+/* gelu8 (host_kernels.hpp:322-352; gelu_cpu bert_encoder.cpp:532-580):
+ * max(v,0) + P(min(|v|,4)), degree-8 Horner with fused multiply-adds. */
+static inline float gelu8_ref(float v) {
+  const float u = fminf(fabsf(v), 4.0f);
+  float pl = fmaf(-7.2340282171e-05f, u, 1.8179518005e-03f);
+  pl = fmaf(pl, u, -1.7707383379e-02f);
+  pl = fmaf(pl, u, 8.4577147641e-02f);
+  pl = fmaf(pl, u, -1.9228671834e-01f);
+  pl = fmaf(pl, u, 9.8431124458e-02f);
+  pl = fmaf(pl, u, 3.6137852062e-01f);
+  pl = fmaf(pl, u, -4.9454128936e-01f);
+  pl = fmaf(pl, u, -1.3007010117e-04f);
+  return (v > 0.0f ? v : 0.0f) + pl;
+}
+
+/* app::gelu_erf_exact (app_state.hpp:116-120): erf GELU in double, one
+ * rounding at the end. */
+static inline float gelu_erf_ref(float x) {
+  const double xd = (double)x;
+  return (float)(0.5 * xd * (1.0 + erf(xd * 0.70710678118654752440)));
+}
+
+/* app::to_bf16 (host_kernels.hpp:157-161): round-to-nearest-even. */
+static inline uint16_t to_bf16_ref(float x) {
+  uint32_t u;
+  memcpy(&u, &x, sizeof u);
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+/* ---- GEMM: hostconv::gemm_nt (conv_host.hpp:150-181) ---------------------
+ * C[M,N] = A[M,K] . B[K,N] + bias.  Per output element the products are
+ * accumulated in k order (the k-outer, n-inner axpy) and the bias is added
+ * last. */
+typedef struct {
+  const float *A, *B, *bias;
+  float *C;
+  int64_t K, N;
+} gemm_ctx;
+
+static void gemm_rows(void *p, int64_t lo, int64_t hi) {
+  const gemm_ctx *g = (const gemm_ctx *)p;
+  const int64_t K = g->K, N = g->N;
+  float *acc = (float *)malloc((size_t)N * sizeof(float));
+  for (int64_t r = lo; r < hi; ++r) {
+    memset(acc, 0, (size_t)N * sizeof(float));
+    const float *a = g->A + r * K;
+    for (int64_t k = 0; k < K; ++k) {
+      const float av = a[k];
+      const float *brow = g->B + k * N;
+      for (int64_t n = 0; n < N; ++n) acc[n] = fmaf(av, brow[n], acc[n]);
+    }
+    float *crow = g->C + r * N;
+    for (int64_t n = 0; n < N; ++n) crow[n] = acc[n] + g->bias[n];
+  }
+  free(acc);
+}
+
+void nebw_oracle_gemm_nt(const float *A, int64_t M, const float *B, int64_t K,
+                         int64_t N, const float *bias, float *C,
+                         int32_t threads) {
+  gemm_ctx g = {A, B, bias, C, K, N};
+  parallel_for(M, threads, gemm_rows, &g);
+}
+
+/* ---- LayerNorm: layer_norm_cpu, AVX2 branch (bert_encoder.cpp:416-463) ---
+ * Eight-lane partial sums of x, mean = hsum/H; eight-lane fma sums of
+ * (x-mean)^2, var = hsum/H (biased); y = fma((x-mean)*is, g, b) with
+ * is = 1/sqrt(var + eps). */
+static void ln_row(float *row, int64_t H, const float *g, const float *b,
+                   float eps) {
+  float s[8] = {0};
+  for (int64_t j = 0; j < H; j += 8)
+    for (int l = 0; l < 8; ++l) s[l] = s[l] + row[j + l];
+  const float mean = hsum8(s) / (float)H;
+  float v[8] = {0};
+  for (int64_t j = 0; j < H; j += 8)
+    for (int l = 0; l < 8; ++l) {
+      const float d = row[j + l] - mean;
+      v[l] = fmaf(d, d, v[l]);
+    }
+  const float var = hsum8(v) / (float)H;
+  const float is = 1.0f / sqrtf(var + eps);
+  for (int64_t j = 0; j < H; ++j) {
+    const float d = row[j] - mean;
+    row[j] = fmaf(d * is, g[j], b[j]);
+  }
+}
+
+typedef struct {
+  float *x;
+  int64_t H;
+  const float *g, *b;
+  float eps;
+} ln_ctx;
+
+static void ln_rows(void *p, int64_t lo, int64_t hi) {
+  const ln_ctx *c = (const ln_ctx *)p;
+  for (int64_t r = lo; r < hi; ++r) ln_row(c->x + r * c->H, c->H, c->g, c->b, c->eps);
+}
+
+void nebw_oracle_layer_norm(float *x, int64_t rows, int64_t hidden,
+                            const float *g, const float *b, float eps) {
+  ln_ctx c = {x, hidden, g, b, eps};
+  ln_rows(&c, 0, rows);
+}
+
+/* ---- attention: qk_impl / softmax_cpu / av_impl, AVX2 branches -----------
+ * (bert_encoder.cpp:995-1135, :481-530).  Scores are not scaled: the packer
+ * folded 1/sqrt(head_dim) into Q (pack_npue.py:2742-2750). */
+typedef struct {
+  const float *qkv;
+  const float *add_mask; /* [batch, seq] of 0 / -1e30 */
+  float *ctx;
+  int64_t seq, H, heads, hd;
+} attn_ctx;
+
+static void attn_pairs(void *p, int64_t lo, int64_t hi) {
+  const attn_ctx *a = (const attn_ctx *)p;
+  const int64_t S = a->seq, H = a->H, hd = a->hd, nv = hd / 8;
+  float *sc = (float *)malloc((size_t)S * sizeof(float));
+  for (int64_t pr = lo; pr < hi; ++pr) {
+    const int64_t b = pr / a->heads, h = pr % a->heads;
+    const float *mk = a->add_mask + b * S;
+    for (int64_t i = 0; i < S; ++i) {
+      const float *q = a->qkv + (b * S + i) * 3 * H + h * hd;
+      /* qk_impl: lane l holds q[l]*k[l] + sum_v q[8v+l]*k[8v+l] (fma). */
+      for (int64_t j = 0; j < S; ++j) {
+        const float *k = a->qkv + (b * S + j) * 3 * H + H + h * hd;
+        float s[8];
+        for (int l = 0; l < 8; ++l) s[l] = q[l] * k[l];
+        for (int64_t v = 1; v < nv; ++v)
+          for (int l = 0; l < 8; ++l) s[l] = fmaf(q[8 * v + l], k[8 * v + l], s[l]);
+        sc[j] = hsum8(s);
+      }
+      /* softmax_cpu: add mask, row max, exp2((x-max)*log2e floored at -120),
+       * eight-lane sum, multiply by 1/sum. */
+      for (int64_t j = 0; j < S; ++j) sc[j] += mk[j];
+      float mx = sc[0];
+      for (int64_t j = 1; j < S; ++j) mx = sc[j] > mx ? sc[j] : mx;
+      float sum[8] = {0};
+      for (int64_t j = 0; j < S; j += 8)
+        for (int l = 0; l < 8; ++l) {
+          float t = (sc[j + l] - mx) * 1.4426950408889634f;
+          t = t > -120.0f ? t : -120.0f;
+          const float e = exp2_ref(t);
+          sc[j + l] = e;
+          sum[l] = sum[l] + e;
+        }
+      const float inv = 1.0f / hsum8(sum);
+      for (int64_t j = 0; j < S; ++j) sc[j] = sc[j] * inv;
+      /* av_impl: per output element, fma over j in order. */
+      float *o = a->ctx + (b * S + i) * H + h * hd;
+      for (int64_t d = 0; d < hd; ++d) o[d] = 0.0f;
+      for (int64_t j = 0; j < S; ++j) {
+        const float *v = a->qkv + (b * S + j) * 3 * H + 2 * H + h * hd;
+        const float pj = sc[j];
+        for (int64_t d = 0; d < hd; ++d) o[d] = fmaf(pj, v[d], o[d]);
+      }
+    }
+  }
+  free(sc);
+}
+
+/* ---- pooling: app::pool_rows (app_state.hpp:335-374) -------------------- */
+int nebw_oracle_pool_rows(const float *h, const float *am, int64_t take,
+                          int64_t seq, int64_t hidden, int32_t cls, int32_t l2,
+                          float *out) {
+  double *acc = (double *)malloc((size_t)hidden * sizeof(double));
+  for (int64_t b = 0; b < take; ++b) {
+    const float *amb = am + b * seq;
+    const float *hb = h + b * seq * hidden;
+    if (cls) {
+      if (amb[0] == 0.f) {
+        free(acc);
+        return fail("CLS pooling on a sequence whose first token is masked");
+      }
+      for (int64_t c = 0; c < hidden; ++c) acc[c] = hb[c];
+    } else {
+      float denom = 0.f;
+      for (int64_t s = 0; s < seq; ++s) denom += amb[s];
+      denom = denom > 1e-9f ? denom : 1e-9f;
+      for (int64_t c = 0; c < hidden; ++c) acc[c] = 0.0;
+      for (int64_t s = 0; s < seq; ++s) {
+        const float m = amb[s];
+        if (m == 0.f) continue;
+        const float *hr = hb + s * hidden;
+        for (int64_t c = 0; c < hidden; ++c) acc[c] += hr[c] * m;
+      }
+      for (int64_t c = 0; c < hidden; ++c) acc[c] /= denom;
+    }
+    float *o = out + b * hidden;
+    if (l2) {
+      double nrm = 0.0;
+      for (int64_t c = 0; c < hidden; ++c) nrm += acc[c] * acc[c];
+      nrm = sqrt(nrm > 1e-24 ? nrm : 1e-24);
+      for (int64_t c = 0; c < hidden; ++c) o[c] = (float)(acc[c] / nrm);
+    } else {
+      for (int64_t c = 0; c < hidden; ++c) o[c] = (float)acc[c];
+    }
+  }
+  free(acc);
+  return 0;
+}
+
+/* ---- elementwise passes --------------------------------------------------- */
+typedef struct {
+  float *x;
+  int erf;
+} act_ctx;
+
+static void act_range(void *p, int64_t lo, int64_t hi) {
+  const act_ctx *c = (const act_ctx *)p;
+  if (c->erf)
+    for (int64_t i = lo; i < hi; ++i) c->x[i] = gelu_erf_ref(c->x[i]);
+  else
+    for (int64_t i = lo; i < hi; ++i) c->x[i] = gelu8_ref(c->x[i]);
+}
+
+void nebw_oracle_gelu8(float *x, int64_t n) {
+  act_ctx c = {x, 0};
+  act_range(&c, 0, n);
+}
+
+void nebw_oracle_exp2(float *x, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) x[i] = exp2_ref(x[i]);
+}
+
+void nebw_oracle_to_bf16(const float *x, uint16_t *out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = to_bf16_ref(x[i]);
+}
+
+/* ---- the encoder: BertEncoder::run (bert_encoder.cpp:1419-1598) ----------
+ * host_ln/host_sm/host_gelu, no --npu-ops:
+ *   x = LN(emb)
+ *   per layer: residual = x; qkv = gemm(x); ctx = attention(qkv)
+ *              proj = gemm(ctx); x = proj + residual; x = LN1(x); residual = x
+ *              up = gelu(gemm(x)); down = gemm(up); x = down + residual;
+ *              x = LN2(x) */
+int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
+                       const int32_t *mask, int32_t batch, int32_t seq,
+                       int32_t threads, float *out, float *hidden_out) {
+  const int64_t H = m->hidden, F = m->ffn, S = seq, B = batch;
+  const int64_t rows = B * S;
+  if (seq <= 0 || seq % 8) return fail("seq must be positive and a multiple of 8");
+  if (H % 8 || m->head_dim % 8 || m->head_dim * m->heads != H)
+    return fail("hidden/head_dim geometry refused (multiples of 8, heads*head_dim == hidden)");
+
+  float *x = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *res = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *qkv = (float *)malloc((size_t)rows * 3 * H * sizeof(float));
+  float *ctx = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *tmp = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *up = (float *)malloc((size_t)rows * F * sizeof(float));
+  float *amask = (float *)malloc((size_t)rows * sizeof(float));
+  float *cam = (float *)malloc((size_t)rows * sizeof(float));
+  if (!x || !res || !qkv || !ctx || !tmp || !up || !amask || !cam) {
+    free(x); free(res); free(qkv); free(ctx); free(tmp); free(up); free(amask); free(cam);
+    return fail("out of host memory");
+  }
+
+  /* EmbedService::chunk (embed_service.cpp:29-64). */
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t s = 0; s < S; ++s) {
+      const int32_t id = ids[b * S + s];
+      const float mk = (float)mask[b * S + s];
+      cam[b * S + s] = mk;
+      amask[b * S + s] = mk > 0 ? 0.f : -1.0e30f;
+      float *dst = x + (b * S + s) * H;
+      const float *wv = m->word + (int64_t)id * H;
+      const float *pv = m->pos + s * H;
+      for (int64_t c = 0; c < H; ++c) dst[c] = wv[c] + pv[c] + m->typ[c];
+    }
+
+  ln_ctx lc = {x, H, m->emb_ln_g, m->emb_ln_b, m->ln_eps};
+  parallel_for(rows, threads, ln_rows, &lc);
+
+  for (int32_t L = 0; L < m->layers; ++L) {
+    memcpy(res, x, (size_t)rows * H * sizeof(float));
+    nebw_oracle_gemm_nt(x, rows, m->w_qkv[L], H, 3 * H, m->b_qkv[L], qkv, threads);
+    attn_ctx ac = {qkv, amask, ctx, S, H, m->heads, m->head_dim};
+    parallel_for(B * m->heads, threads, attn_pairs, &ac);
+    nebw_oracle_gemm_nt(ctx, rows, m->w_ao[L], H, H, m->b_ao[L], tmp, threads);
+    for (int64_t i = 0; i < rows * H; ++i) x[i] = tmp[i] + res[i];
+    lc.g = m->ln1_g[L];
+    lc.b = m->ln1_b[L];
+    parallel_for(rows, threads, ln_rows, &lc);
+    memcpy(res, x, (size_t)rows * H * sizeof(float));
+    nebw_oracle_gemm_nt(x, rows, m->w_up[L], H, F, m->b_up[L], up, threads);
+    act_ctx gc = {up, m->gelu_erf};
+    parallel_for(rows * F, threads, act_range, &gc);
+    nebw_oracle_gemm_nt(up, rows, m->w_dn[L], F, H, m->b_dn[L], tmp, threads);
+    for (int64_t i = 0; i < rows * H; ++i) x[i] = tmp[i] + res[i];
+    lc.g = m->ln2_g[L];
+    lc.b = m->ln2_b[L];
+    parallel_for(rows, threads, ln_rows, &lc);
+  }
+
+  if (hidden_out) memcpy(hidden_out, x, (size_t)rows * H * sizeof(float));
+  const int rc = nebw_oracle_pool_rows(x, cam, B, S, H, m->cls_pool, m->l2_normalize, out);
+  free(x); free(res); free(qkv); free(ctx); free(tmp); free(up); free(amask); free(cam);
+  return rc;
+}

@@ -1,0 +1,240 @@
+"""TEST INFRASTRUCTURE ONLY -- Python front of the parity oracle.
+
+Two CPU implementations of the reference's host-CPU BERT path, both behind
+ctypes:
+
+  PortOracle  oracle/libnebw_oracle.so -- the plain-C restatement
+              (oracle/bert_oracle.c).  Travels with the repository, so it is
+              the checker on the GPU box.
+  RefOracle   oracle/_ref/libnebw_ref.so -- the reference's own
+              bert_encoder.cpp/pool.cpp/model.cpp compiled from its tree with
+              its own flags (oracle/Makefile).  Built only where the
+              reference tree exists; used to pin PortOracle and to make the
+              golden fixtures, and as bench.py's reference arm when present.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module.  Nothing on the product path may.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+PORT_LIB = HERE / "libnebw_oracle.so"
+REF_LIB = HERE / "_ref" / "libnebw_ref.so"
+
+_f32p = C.POINTER(C.c_float)
+_i32p = C.POINTER(C.c_int32)
+
+
+def _ptr(a: np.ndarray, t=_f32p):
+    return a.ctypes.data_as(t)
+
+
+class _Model(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("layers", "hidden", "heads", "head_dim", "ffn",
+                                          "cls_pool", "l2_normalize", "gelu_erf")] + [
+        ("ln_eps", C.c_float)] + [
+        (n, _f32p) for n in ("word", "pos", "typ", "emb_ln_g", "emb_ln_b")] + [
+        (n, C.POINTER(_f32p)) for n in ("w_qkv", "b_qkv", "w_ao", "b_ao", "ln1_g", "ln1_b",
+                                         "w_up", "b_up", "w_dn", "b_dn", "ln2_g", "ln2_b")]
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+class PortOracle:
+    """The C restatement, fed from in-memory weights."""
+
+    def __init__(self, lib_path: Path = PORT_LIB):
+        if not Path(lib_path).exists():
+            raise FileNotFoundError(f"{lib_path} is not built (make -C oracle port)")
+        self.lib = C.CDLL(str(lib_path))
+        L = self.lib
+        L.nebw_oracle_encode.argtypes = [C.POINTER(_Model), _i32p, _i32p, C.c_int32, C.c_int32,
+                                         C.c_int32, _f32p, _f32p]
+        L.nebw_oracle_encode.restype = C.c_int
+        L.nebw_oracle_last_error.restype = C.c_char_p
+        L.nebw_oracle_gemm_nt.argtypes = [_f32p, C.c_int64, _f32p, C.c_int64, C.c_int64, _f32p,
+                                          _f32p, C.c_int32]
+        L.nebw_oracle_gelu8.argtypes = [_f32p, C.c_int64]
+        L.nebw_oracle_exp2.argtypes = [_f32p, C.c_int64]
+        L.nebw_oracle_to_bf16.argtypes = [_f32p, C.POINTER(C.c_uint16), C.c_int64]
+        L.nebw_oracle_layer_norm.argtypes = [_f32p, C.c_int64, C.c_int64, _f32p, _f32p, C.c_float]
+        L.nebw_oracle_pool_rows.argtypes = [_f32p, _f32p, C.c_int64, C.c_int64, C.c_int64,
+                                            C.c_int32, C.c_int32, _f32p]
+        L.nebw_oracle_pool_rows.restype = C.c_int
+
+    def _struct(self, w):
+        keep = []
+
+        def arr(lst):
+            a = (_f32p * len(lst))(*[_ptr(np.ascontiguousarray(x, np.float32)) for x in lst])
+            keep.append(a)
+            return a
+
+        m = _Model(layers=w.layers, hidden=w.hidden, heads=w.heads, head_dim=w.head_dim,
+                   ffn=w.ffn, cls_pool=int(w.cls_pool), l2_normalize=1,
+                   gelu_erf=int(getattr(w, "gelu_erf", False)), ln_eps=1e-12,
+                   word=_ptr(w.word), pos=_ptr(w.pos), typ=_ptr(w.typ),
+                   emb_ln_g=_ptr(w.emb_ln_g), emb_ln_b=_ptr(w.emb_ln_b),
+                   w_qkv=arr(w.w_qkv), b_qkv=arr(w.b_qkv), w_ao=arr(w.w_ao), b_ao=arr(w.b_ao),
+                   ln1_g=arr(w.ln1_g), ln1_b=arr(w.ln1_b), w_up=arr(w.w_up), b_up=arr(w.b_up),
+                   w_dn=arr(w.w_dn), b_dn=arr(w.b_dn), ln2_g=arr(w.ln2_g), ln2_b=arr(w.ln2_b))
+        return m, keep
+
+    def encode(self, w, ids, mask, threads: int | None = None, hidden: bool = False):
+        ids = np.ascontiguousarray(ids, np.int32)
+        mask = np.ascontiguousarray(mask, np.int32)
+        B, S = ids.shape
+        out = np.zeros((B, w.hidden), np.float32)
+        hid = np.zeros((B * S, w.hidden), np.float32) if hidden else None
+        m, keep = self._struct(w)
+        rc = self.lib.nebw_oracle_encode(C.byref(m), _ptr(ids, _i32p), _ptr(mask, _i32p), B, S,
+                                         threads or host_threads(), _ptr(out),
+                                         _ptr(hid) if hidden else None)
+        del keep
+        if rc:
+            raise RuntimeError(self.lib.nebw_oracle_last_error().decode())
+        return (out, hid) if hidden else out
+
+    def gemm_nt(self, A, B, bias, threads=1):
+        A = np.ascontiguousarray(A, np.float32)
+        B = np.ascontiguousarray(B, np.float32)
+        bias = np.ascontiguousarray(bias, np.float32)
+        M, K = A.shape
+        N = B.shape[1]
+        Cm = np.zeros((M, N), np.float32)
+        self.lib.nebw_oracle_gemm_nt(_ptr(A), M, _ptr(B), K, N, _ptr(bias), _ptr(Cm), threads)
+        return Cm
+
+    def gelu8(self, x):
+        y = np.array(x, np.float32, copy=True)
+        self.lib.nebw_oracle_gelu8(_ptr(y), y.size)
+        return y
+
+    def exp2(self, x):
+        y = np.array(x, np.float32, copy=True)
+        self.lib.nebw_oracle_exp2(_ptr(y), y.size)
+        return y
+
+    def to_bf16(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        o = np.zeros(x.shape, np.uint16)
+        self.lib.nebw_oracle_to_bf16(_ptr(x), o.ctypes.data_as(C.POINTER(C.c_uint16)), x.size)
+        return o
+
+    def layer_norm(self, x, g, b, eps=1e-12):
+        y = np.array(x, np.float32, copy=True)
+        self.lib.nebw_oracle_layer_norm(_ptr(y), y.shape[0], y.shape[1],
+                                        _ptr(np.ascontiguousarray(g, np.float32)),
+                                        _ptr(np.ascontiguousarray(b, np.float32)), eps)
+        return y
+
+    def pool_rows(self, h, am, seq, cls, l2=True):
+        h = np.ascontiguousarray(h, np.float32)
+        am = np.ascontiguousarray(am, np.float32)
+        take = am.shape[0]
+        hidden = h.shape[-1]
+        out = np.zeros((take, hidden), np.float32)
+        rc = self.lib.nebw_oracle_pool_rows(_ptr(h), _ptr(am), take, seq, hidden, int(cls),
+                                            int(l2), _ptr(out))
+        if rc:
+            raise RuntimeError(self.lib.nebw_oracle_last_error().decode())
+        return out
+
+
+class RefOracle:
+    """The reference's own host path, compiled from its tree."""
+
+    def __init__(self, lib_path: Path = REF_LIB):
+        if not Path(lib_path).exists():
+            raise FileNotFoundError(f"{lib_path} is not built (make -C oracle ref)")
+        self.lib = C.CDLL(str(lib_path))
+        L = self.lib
+        L.nebw_ref_encode.argtypes = [C.c_char_p, C.c_int32, _i32p, _i32p, C.c_int32, C.c_int32,
+                                      _f32p, _f32p, C.c_char_p, C.c_int32]
+        L.nebw_ref_encode.restype = C.c_int
+        L.nebw_ref_gemm_nt.argtypes = [_f32p, C.c_int64, _f32p, C.c_int64, C.c_int64, _f32p,
+                                       _f32p, C.c_int32]
+        L.nebw_ref_gelu8.argtypes = [_f32p, C.c_int64]
+        L.nebw_ref_exp2.argtypes = [_f32p, C.c_int64]
+        L.nebw_ref_to_bf16.argtypes = [_f32p, C.POINTER(C.c_uint16), C.c_int64]
+        L.nebw_ref_pool_rows.argtypes = [_f32p, _f32p, C.c_int64, C.c_int64, C.c_int64, C.c_int32,
+                                         C.c_int32, _f32p, C.c_char_p, C.c_int32]
+        L.nebw_ref_pool_rows.restype = C.c_int
+
+    def encode_container(self, path, seq, ids, mask, threads=None, hidden=False, hidden_size=None):
+        ids = np.ascontiguousarray(ids, np.int32)
+        mask = np.ascontiguousarray(mask, np.int32)
+        B, S = ids.shape
+        assert S == seq
+        out = np.zeros((B, hidden_size), np.float32)
+        hid = np.zeros((B * S, hidden_size), np.float32) if hidden else None
+        err = C.create_string_buffer(4096)
+        rc = self.lib.nebw_ref_encode(str(path).encode(), seq, _ptr(ids, _i32p), _ptr(mask, _i32p),
+                                      B, threads or host_threads(), _ptr(out),
+                                      _ptr(hid) if hidden else None, err, 4096)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return (out, hid) if hidden else out
+
+    def encode(self, w, ids, mask, threads=None, hidden=False, workdir=None):
+        """Write `w` as a host-layout container, then run the reference."""
+        import sys
+        sys.path.insert(0, str(HERE.parent / "npu-embeddings-xdna1_b200"))
+        from nebw.npue import write_bert_container  # noqa: E402
+        S = np.asarray(ids).shape[1]
+        with tempfile.TemporaryDirectory(dir=workdir) as td:
+            path = Path(td) / "oracle.npue"
+            write_bert_container(path, w, max_seq_len=max(S, 8))
+            return self.encode_container(path, S, ids, mask, threads, hidden, w.hidden)
+
+    def gemm_nt(self, A, B, bias, threads=1):
+        A = np.ascontiguousarray(A, np.float32)
+        B = np.ascontiguousarray(B, np.float32)
+        bias = np.ascontiguousarray(bias, np.float32)
+        M, K = A.shape
+        N = B.shape[1]
+        Cm = np.zeros((M, N), np.float32)
+        self.lib.nebw_ref_gemm_nt(_ptr(A), M, _ptr(B), K, N, _ptr(bias), _ptr(Cm), threads)
+        return Cm
+
+    def gelu8(self, x):
+        y = np.array(x, np.float32, copy=True)
+        self.lib.nebw_ref_gelu8(_ptr(y), y.size)
+        return y
+
+    def exp2(self, x):
+        y = np.array(x, np.float32, copy=True)
+        self.lib.nebw_ref_exp2(_ptr(y), y.size)
+        return y
+
+    def to_bf16(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        o = np.zeros(x.shape, np.uint16)
+        self.lib.nebw_ref_to_bf16(_ptr(x), o.ctypes.data_as(C.POINTER(C.c_uint16)), x.size)
+        return o
+
+    def pool_rows(self, h, am, seq, cls, l2=True):
+        h = np.ascontiguousarray(h, np.float32)
+        am = np.ascontiguousarray(am, np.float32)
+        take = am.shape[0]
+        hidden = h.shape[-1]
+        out = np.zeros((take, hidden), np.float32)
+        err = C.create_string_buffer(1024)
+        rc = self.lib.nebw_ref_pool_rows(_ptr(h), _ptr(am), take, seq, hidden, int(cls), int(l2),
+                                         _ptr(out), err, 1024)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return out

@@ -1,0 +1,155 @@
+// TEST INFRASTRUCTURE ONLY -- part of the parity oracle, never shipped.
+//
+// A C-ABI front for the reference's OWN host-CPU encoder, compiled from the
+// reference tree (see oracle/Makefile).  It drives exactly the call sequence
+// the reference's embedding service uses:
+//
+//   EmbedService::chunk          runtime/src/server/embed_service.cpp:29-64
+//     x[b,s,:] = (word[id] + pos[s]) + type[0]      (:51-57, order kept)
+//     add_mask  = 0 / -1e30 from the 1/0 attention mask (:49)
+//     h = BertEncoder::run(x)    runtime/src/encoders/bert_encoder.cpp:1419-1598
+//     pool_rows(h, mask)         runtime/include/common/app_state.hpp:335-374
+//
+// with the encoder set up the way setup_encoder() does for an all-host run:
+// set_model_shape (app_state.hpp:380), set_design_seq (:637), host_ln /
+// host_sm / host_gelu true, stage_all() (bert_encoder.cpp:41-172) on a
+// `gemm_layout:"host"` container so every GEMM is hostconv::gemm_nt over the
+// container's F32 [K,N] operand.
+//
+// It also exposes a few of the reference's inline host kernels one by one
+// (gemm_nt, gelu8, to_bf16, exp2_avx2, pool_rows) so the CPU restatement in
+// oracle/bert_oracle.c can be pinned op by op as well as end to end.
+
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common/app_state.hpp"
+#include "common/conv_host.hpp"
+#include "common/host_kernels.hpp"
+#include "encoders/bert_encoder.hpp"
+#include "runtime/design.hpp"
+#include "runtime/device.hpp"
+#include "runtime/model.hpp"
+#include "runtime/pool.hpp"
+
+namespace {
+void set_err(char *err, int32_t errlen, const char *msg) {
+  if (!err || errlen <= 0) return;
+  std::strncpy(err, msg, static_cast<size_t>(errlen) - 1);
+  err[errlen - 1] = '\0';
+}
+}  // namespace
+
+extern "C" {
+
+// Encode `batch` sequences of `seq` token ids through the reference host path.
+//   ids        [batch, seq] int32, tokenizer output (pad id in padded slots)
+//   attn_mask  [batch, seq] int32 1/0
+//   out        [batch, hidden] fp32, pooled (+L2 as the container says)
+//   hidden_out optional [batch*seq, hidden] fp32: BertEncoder::run's output
+// Returns 0, or 1 with `err` holding the reference's exception text.
+int nebw_ref_encode(const char *npue_path, int32_t seq, const int32_t *ids,
+                    const int32_t *attn_mask, int32_t batch, int32_t threads,
+                    float *out, float *hidden_out, char *err, int32_t errlen) {
+  try {
+    npue::File f(npue_path);
+    app::set_model_shape(f);
+    app::set_design_seq(seq);
+    app::Pool pool(threads > 0 ? threads : 1);
+    npu::Device dev;
+    npu::Design d(dev, "oracle-host");
+    npue::BertEncoder enc(f, d, d, d, d, d, d, d, pool);
+    enc.host_ln = enc.host_sm = enc.host_gelu = true;
+    enc.batch = batch;
+    enc.rows = static_cast<int64_t>(batch) * seq;
+    enc.stage_all();
+
+    const int64_t H = app::g_hidden;
+    const float *w_word = f.raw("embeddings.word").as<float>();
+    const float *w_pos = f.raw("embeddings.position").as<float>();
+    const float *w_typ = f.raw("embeddings.token_type").as<float>();
+    std::vector<float> buf(static_cast<size_t>(batch) * seq * H, 0.f);
+    std::vector<float> cmask(static_cast<size_t>(batch) * seq, -1.0e30f);
+    std::vector<float> cam(static_cast<size_t>(batch) * seq, 0.f);
+    for (int64_t b = 0; b < batch; ++b) {
+      for (int64_t s = 0; s < seq; ++s) {
+        const int32_t id = ids[b * seq + s];
+        const float m = static_cast<float>(attn_mask[b * seq + s]);
+        cam[b * seq + s] = m;
+        cmask[b * seq + s] = m > 0 ? 0.f : -1.0e30f;
+        float *dst = buf.data() + (b * seq + s) * H;
+        const float *wv = w_word + static_cast<size_t>(id) * H;
+        const float *pv = w_pos + static_cast<size_t>(s) * H;
+        for (int64_t c = 0; c < H; ++c) dst[c] = wv[c] + pv[c] + w_typ[c];
+      }
+    }
+    enc.add_mask = cmask;
+    std::vector<float> h = enc.run(buf);
+    if (hidden_out) std::memcpy(hidden_out, h.data(), h.size() * sizeof(float));
+    app::pool_rows(h.data(), cam.data(), batch, out);
+    return 0;
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return 1;
+  }
+}
+
+// npue::hostconv::gemm_nt (runtime/include/common/conv_host.hpp:150-181):
+// C[M,N] = A[M,K] . B[K,N] + bias, fp32.
+int nebw_ref_gemm_nt(const float *A, int64_t M, const float *B, int64_t K,
+                     int64_t N, const float *bias, float *C, int32_t threads) {
+  app::Pool pool(threads > 0 ? threads : 1);
+  npue::hostconv::gemm_nt(A, M, B, K, N, bias, C, pool);
+  return 0;
+}
+
+// app::gelu8, scalar form (runtime/include/common/host_kernels.hpp:340-352),
+// and the 8-wide AVX2 form gelu_cpu() uses for all but the tail
+// (bert_encoder.cpp:532-580).
+void nebw_ref_gelu8(float *x, int64_t n) {
+  int64_t i = 0;
+#if defined(__AVX2__)
+  for (; i + 8 <= n; i += 8)
+    _mm256_storeu_ps(x + i, app::gelu8(_mm256_loadu_ps(x + i)));
+#endif
+  for (; i < n; ++i) x[i] = app::gelu8(x[i]);
+}
+
+// app::exp2_avx2 (host_kernels.hpp:354-380), 8 lanes at a time; n % 8 == 0.
+void nebw_ref_exp2(float *x, int64_t n) {
+#if defined(__AVX2__)
+  for (int64_t i = 0; i + 8 <= n; i += 8)
+    _mm256_storeu_ps(x + i, app::exp2_avx2(_mm256_loadu_ps(x + i)));
+#else
+  (void)x; (void)n;
+#endif
+}
+
+// app::to_bf16 (host_kernels.hpp:157-161), fp32 -> bf16 RNE bit pattern.
+void nebw_ref_to_bf16(const float *x, uint16_t *out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = app::to_bf16(x[i]);
+}
+
+// app::pool_rows (app_state.hpp:335-374) with the geometry globals it reads
+// set from the arguments.
+int nebw_ref_pool_rows(const float *h, const float *am, int64_t take,
+                       int64_t seq, int64_t hidden, int32_t cls, int32_t l2,
+                       float *out, char *err, int32_t errlen) {
+  try {
+    app::g_seq = seq;
+    app::g_hidden = hidden;
+    app::g_cls_pool = cls != 0;
+    app::g_l2_normalize = l2 != 0;
+    app::pool_rows(h, am, take, out);
+    return 0;
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return 1;
+  }
+}
+
+}  // extern "C"

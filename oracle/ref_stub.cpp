@@ -1,0 +1,85 @@
+// TEST INFRASTRUCTURE ONLY -- part of the parity oracle, never shipped.
+//
+// Host-side stand-ins for the reference's XRT device layer, so that the
+// reference's own host-CPU encoder (runtime/src/encoders/bert_encoder.cpp,
+// compiled from the reference tree where it lies) links without XRT.
+//
+// The oracle runs the reference with `--npu-ops` empty, which is its default
+// (runtime/include/common/npu_ops_flag.hpp:96-103): every GEMM goes to
+// hostconv::gemm_nt, every LayerNorm/softmax/GELU to the *_cpu passes.  None of
+// the array methods below is reachable on that path, so each one throws by
+// name: reaching one means the oracle is not running the host path and its
+// answer must not be trusted.
+//
+// Symbols provided (the set the linker reports missing when bert_encoder.cpp,
+// pool.cpp, model.cpp, json_min.cpp and tokenizers/*.cpp are linked alone):
+//   npu::Device::{Device,~Device}                    runtime/include/runtime/device.hpp:29-38
+//   npu::Design::{Design,~Design,stage,bind,...}     runtime/include/runtime/design.hpp:199-263
+//   npue::whisper::NpuAttention::run                 runtime/include/whisper/attention_npu.hpp:162
+//   npue::gemma_rope_tables                          runtime/include/encoders/gemma_kernels.hpp:88
+
+#include <stdexcept>
+#include <string>
+
+#include "encoders/gemma_kernels.hpp"
+#include "runtime/design.hpp"
+#include "runtime/device.hpp"
+#include "whisper/attention_npu.hpp"
+
+namespace {
+[[noreturn]] void unreachable(const char *what) {
+  throw std::runtime_error(std::string("oracle host stub: ") + what +
+                           " reached -- the oracle must run the reference's "
+                           "host-CPU path only (--npu-ops empty)");
+}
+}  // namespace
+
+namespace npu {
+
+struct Device::Impl {};
+Device::Device() {}
+Device::~Device() {}
+
+struct Design::Impl {};
+Design::Design(Device &dev, const std::string &dir) : dev_(&dev) {
+  info_.name = dir;  // used only as a cache-key label by host_b.hpp
+}
+Design::~Design() {}
+
+void Design::run(const std::vector<const void *> &, void *) { unreachable("Design::run"); }
+void Design::dispatch_only() { unreachable("Design::dispatch_only"); }
+void Design::bind_instr(size_t) { unreachable("Design::bind_instr"); }
+size_t Design::stage(size_t, const void *, size_t) { unreachable("Design::stage"); }
+size_t Design::stage_alloc(size_t, size_t) { unreachable("Design::stage_alloc"); }
+// The one method that does not throw: BertEncoder::run() takes the FFN-down
+// A-slot address unconditionally when it builds its FusedNext/FusedNextBf16
+// descriptors (bert_encoder.cpp:1529-1541) and only writes through it when
+// the GEMMs are on the array.  On the host path the address is built and
+// never used, so a null answer is exact; a write through it would fault
+// loudly rather than corrupt anything.
+void *Design::slot_ptr(size_t, size_t) { return nullptr; }
+void Design::bind(size_t, size_t) { unreachable("Design::bind"); }
+void *Design::host_ptr(size_t) { unreachable("Design::host_ptr"); }
+void Design::sync_to_device(size_t, size_t) { unreachable("Design::sync_to_device"); }
+void Design::sync_from_device(size_t, size_t) { unreachable("Design::sync_from_device"); }
+void Design::sync_slot_to_device(size_t, size_t, size_t) {
+  unreachable("Design::sync_slot_to_device");
+}
+void Design::sync_slot_from_device(size_t, size_t, size_t) {
+  unreachable("Design::sync_slot_from_device");
+}
+
+}  // namespace npu
+
+namespace npue {
+namespace whisper {
+void NpuAttention::run(const float *, int64_t, const float *, int64_t, int64_t,
+                       int64_t, int64_t, float, float *) {
+  unreachable("NpuAttention::run");
+}
+}  // namespace whisper
+
+void gemma_rope_tables(int64_t, int64_t, double, float *, float *) {
+  unreachable("gemma_rope_tables");
+}
+}  // namespace npue
