@@ -1,0 +1,204 @@
+/* nebw -- the B200 (sm_100a) BERT-encoder library behind a plain C ABI.
+ *
+ * This is the device side of the reference's embedding runtime, rebuilt for
+ * the GPU: everything the reference dispatches to its NPU (or runs on the
+ * host when --npu-ops is empty) for a BERT-family encoder pass.  The entry
+ * points are the ones the reference's op funnels would bind; each comment
+ * names the reference interface it replaces (paths inside the reference
+ * project).
+ *
+ * Conventions
+ *   - Every function returns 0 (NEBW_OK) or a nebw_status; the message for
+ *     the calling thread's last failure is nebw_last_error().  Nothing falls
+ *     back to the CPU: a missing device, a refused shape or a device-side
+ *     fault is an error by name (the reference's "fail loudly" rule,
+ *     README.md:2111-2140).
+ *   - Pointers named *_dev / documented "device" are CUDA device pointers;
+ *     "host" pointers are ordinary memory.  `stream` is a cudaStream_t passed
+ *     as void* (NULL = the device handle's own stream).
+ *   - One nebw_dev per GPU.  Calls on different nebw_dev handles may run
+ *     concurrently from different host threads; calls on one handle must not
+ *     overlap.  Staged weights are immutable after staging.
+ */
+#ifndef NEBW_H
+#define NEBW_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEBW_ABI_VERSION 1
+
+typedef enum nebw_status {
+  NEBW_OK = 0,
+  NEBW_EINVAL = 1,   /* an argument or shape is refused                     */
+  NEBW_ECUDA = 2,    /* a CUDA runtime call failed (message names it)       */
+  NEBW_ENOMEM = 3,   /* device or pinned-host allocation failed             */
+  NEBW_ESTATE = 4,   /* the object is not in a state to do this (e.g. a
+                        model with unstaged tensors)                         */
+  NEBW_EDEVICE = 5,  /* a kernel reported an error (bad token id, bad
+                        length, a bounded wait that timed out)              */
+  NEBW_EIO = 6       /* a container file could not be read or is malformed */
+} nebw_status;
+
+enum { NEBW_F32 = 0, NEBW_BF16 = 1 };
+enum { NEBW_ACT_NONE = 0, NEBW_ACT_GELU8 = 1, NEBW_ACT_GELU_ERF = 2 };
+enum { NEBW_POOL_MEAN = 0, NEBW_POOL_CLS = 1 };
+
+typedef struct nebw_dev nebw_dev;
+typedef struct nebw_model nebw_model;
+
+/* Message of the calling thread's last failure ("" if none). */
+const char *nebw_last_error(void);
+int nebw_abi_version(void);
+
+/* ---- device ------------------------------------------------------------
+ * Replaces npu::Device (runtime/include/runtime/device.hpp:29-38) and the
+ * XRT buffer plumbing of npu::Design (runtime/include/runtime/design.hpp:
+ * 199-263).  nebw_open refuses a GPU that is not sm_100 by name. */
+int nebw_open(int device, nebw_dev **out);
+int nebw_close(nebw_dev *dev);
+/* Wait for the handle's stream, then report (and clear) any error a kernel
+ * recorded since the last check. */
+int nebw_sync(nebw_dev *dev);
+int nebw_alloc(nebw_dev *dev, size_t bytes, void **dptr);
+int nebw_free(nebw_dev *dev, void *dptr);
+int nebw_copy_h2d(nebw_dev *dev, void *dst_dev, const void *src_host, size_t bytes);
+int nebw_copy_d2h(nebw_dev *dev, void *dst_host, const void *src_dev, size_t bytes);
+int nebw_device_info(nebw_dev *dev, int *sm_count, int *cc_major, int *cc_minor);
+
+/* ---- weights -------------------------------------------------------------
+ * Replaces npu::Design::stage(arg, data, bytes) (design.hpp:199-263,
+ * design.cpp:394) for a GEMM operand.  `host_kn` is the container's operand
+ * layout, row-major [K, N] (tools/pack/pack_npue.py add_gemm_b_host
+ * :411-428), fp32 or bf16; it is staged once as bf16 RNE [N, K] (K-major,
+ * the tensor-core B layout).  K % 8 == 0 and N % 8 == 0 are required. */
+int nebw_stage_weight(nebw_dev *dev, const void *host_kn, int dtype, int64_t K, int64_t N,
+                      uint64_t *handle);
+int nebw_release_weight(nebw_dev *dev, uint64_t handle);
+
+/* ---- ops (device pointers, asynchronous on `stream`) ---------------------- */
+
+/* The unified GEMM.  Replaces BertEncoder::gemm / host_gemm
+ * (runtime/src/encoders/bert_encoder.cpp:714-924, bert_encoder.hpp:269-274)
+ * and the gemm_rtp design set, with the elementwise passes that follow a
+ * GEMM fused in:
+ *   C = A . W + bias                  (hostconv::gemm_nt, conv_host.hpp:150-181)
+ *   act: NEBW_ACT_GELU8 / _GELU_ERF   (gelu_cpu :532-580; gelu_erf_exact,
+ *                                      app_state.hpp:116-120)
+ *   residual (fp32, may alias C):     C = (A.W + bias) + residual  (add_into :1183-1194)
+ *   c_dtype NEBW_BF16: RNE narrow     (kernels/narrow_f32_bf16.cc)
+ * A is bf16 [M, K] device; C is [M, N] device, bf16 or fp32.  `residual`
+ * requires c_dtype NEBW_F32 and act NONE; act requires NEBW_BF16. */
+int nebw_gemm(nebw_dev *dev, uint64_t weight, const void *A, int64_t M, int64_t K, int64_t N,
+              const float *bias, const float *residual, int act, void *C, int c_dtype,
+              void *stream);
+
+/* LayerNorm over rows of width H, in place: x = LN(x + y) (y may be NULL).
+ * Replaces layer_norm / layer_norm_cpu / add_norm_bf16
+ * (bert_encoder.cpp:370-463, :1304-1361; kernels/layernorm{,_rne}.cc):
+ * two-pass fp32, biased variance, eps inside the square root.  If a_bf16 is
+ * not NULL the normalised rows are also written as bf16 RNE (the next
+ * GEMM's A).  H % 128 == 0, H <= 2048. */
+int nebw_layernorm(nebw_dev *dev, float *x, const float *y, const float *gamma,
+                   const float *beta, float eps, int64_t rows, int64_t H, void *a_bf16,
+                   void *stream);
+
+/* Fused masked attention over packed sequences.  Replaces qk / softmax_cpu /
+ * av and attention_npu (bert_encoder.cpp:481-530, :995-1181).
+ *   qkv_bf16 [T, 3H] device (Q|K|V per row, Q pre-scaled by 1/sqrt(d))
+ *   seq_off [B+1], seq_len [B] int32 device: sequence b owns packed rows
+ *   [seq_off[b], seq_off[b] + seq_len[b])
+ *   ctx_bf16 [T, H] device.  head_dim in {32, 64}; max_len bounds seq_len. */
+int nebw_attention(nebw_dev *dev, const void *qkv_bf16, const int32_t *seq_off,
+                   const int32_t *seq_len, int32_t B, int32_t max_len, int32_t heads,
+                   int32_t head_dim, void *ctx_bf16, void *stream);
+
+/* Packing scan: seq_off[0..B] = exclusive prefix sum of seq_len (device).
+ * Lengths outside [1, S] are an NEBW_EDEVICE error at the next sync. */
+int nebw_pack_offsets(nebw_dev *dev, const int32_t *seq_len_in, int32_t B, int32_t S,
+                      int32_t *seq_len_out, int32_t *seq_off, void *stream);
+
+/* Embedding gather + LayerNorm into packed rows.  Replaces the gather of
+ * EmbedService::chunk (runtime/src/server/embed_service.cpp:29-64,
+ * x = (word[id] + pos[s]) + type[0]) and the embedding LayerNorm
+ * (BertEncoder::run :1429).  ids [B, S] int32 device (padded tokenizer
+ * output); x fp32 [T, H] and a_bf16 [T, H] device outputs. */
+int nebw_embed_ln(nebw_dev *dev, const int32_t *ids, const int32_t *seq_off,
+                  const int32_t *seq_len, int32_t B, int32_t S, const float *word,
+                  int32_t vocab, const float *pos, const float *typ, const float *gamma,
+                  const float *beta, float eps, int32_t H, float *x, void *a_bf16,
+                  void *stream);
+
+/* Pooling + L2 normalisation.  Replaces app::pool_rows
+ * (runtime/include/common/app_state.hpp:335-374): NEBW_POOL_CLS takes each
+ * sequence's first packed row, NEBW_POOL_MEAN the masked mean; both
+ * accumulate in double.  out fp32 [B, H] device. */
+int nebw_pool_l2(nebw_dev *dev, const float *h, const int32_t *seq_off, const int32_t *seq_len,
+                 int32_t B, int32_t H, int pooling, int l2, float *out, void *stream);
+
+/* fp32 -> bf16 RNE narrow (kernels/narrow_f32_bf16.cc; app::to_bf16,
+ * host_kernels.hpp:157-161). */
+int nebw_narrow_bf16(nebw_dev *dev, const float *x, int64_t n, void *y_bf16, void *stream);
+
+/* ---- the whole encoder -------------------------------------------------- */
+
+/* Geometry a container's config carries (set_model_shape,
+ * app_state.hpp:380-631). */
+typedef struct nebw_config {
+  int32_t num_layers;
+  int32_t hidden;
+  int32_t num_heads;
+  int32_t head_dim;
+  int32_t intermediate;
+  int32_t vocab_size;
+  int32_t max_seq_len;     /* position-table rows                        */
+  int32_t type_vocab_size;
+  int32_t pooling;         /* NEBW_POOL_MEAN / NEBW_POOL_CLS             */
+  int32_t l2_normalize;    /* 0 / 1                                      */
+  int32_t activation;      /* NEBW_ACT_GELU8 (the reference BERT host
+                              path) or NEBW_ACT_GELU_ERF                 */
+  float layer_norm_eps;    /* the reference BERT host path uses 1e-12    */
+} nebw_config;
+
+/* Model = npue::BertEncoder's staged state (stage_all,
+ * bert_encoder.cpp:41-172) on one GPU.  Tensors are set by their container
+ * names ("embeddings.word", "layer.3.qkv", "layer.3.qkv.bias", ...,
+ * pack_npue.py:2684-2790); GEMM operands are [K, N] as in the container. */
+int nebw_model_create(nebw_dev *dev, const nebw_config *cfg, nebw_model **out);
+int nebw_model_set_tensor(nebw_model *m, const char *name, const void *host, int dtype,
+                          int64_t rows, int64_t cols);
+/* Stage every tensor of a `.npue` container (gemm_layout "host": F32 [K,N]
+ * operands) -- the reference's npue::File + set_model_shape + stage_all
+ * (runtime/src/model.cpp:214-380). */
+int nebw_model_load_npue(nebw_dev *dev, const char *path, nebw_model **out);
+int nebw_model_destroy(nebw_model *m);
+int nebw_model_get_config(const nebw_model *m, nebw_config *cfg);
+
+/* Encode B padded sequences end to end: host ids [B, S] int32 and host
+ * lengths [B] (the attention mask as a prefix length; the tokenizer's mask is
+ * always a prefix, wordpiece.cpp:354-378) in, host fp32 [B, hidden] pooled
+ * (+L2) embeddings out.  Synchronous.  Replaces EmbedService::chunk's
+ * run + pool_rows (embed_service.cpp:29-64; BertEncoder::run
+ * bert_encoder.cpp:1419-1598). */
+int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B, int32_t S,
+                float *out);
+
+/* The same pass with everything device-resident and asynchronous on
+ * `stream`: ids_dev [B, S], lens_dev [B], out_dev [B, hidden].  No host
+ * synchronisation inside; call nebw_sync (or synchronise the stream and call
+ * nebw_sync) to collect device-side errors. */
+int nebw_encode_device(nebw_model *m, const int32_t *ids_dev, const int32_t *lens_dev,
+                       int32_t B, int32_t S, float *out_dev, void *stream);
+
+/* Number of kernel launches one nebw_encode_device call makes for a model
+ * (for launch accounting). */
+int nebw_encode_launch_count(const nebw_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEBW_H */

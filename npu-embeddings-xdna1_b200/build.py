@@ -1,0 +1,67 @@
+"""Build step: compile libnebw.so (CUDA, sm_100a) in-tree, and the CPU oracle.
+
+    python npu-embeddings-xdna1_b200/build.py            # library + oracle
+    python npu-embeddings-xdna1_b200/build.py --lib      # library only
+
+The library is compiled with nvcc directly for
+`-gencode arch=compute_100a,code=sm_100a`; nothing else is targeted.  The
+oracle (test infrastructure) is built with oracle/Makefile: the C
+restatement always, the reference's own host path only where the reference
+tree exists.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+REPO = PKG.parent
+SOURCES = ["csrc/nebw.cu", "csrc/npue_file.cpp"]
+DEPS = SOURCES + ["csrc/gemm_tc.cuh", "csrc/attention.cuh", "csrc/rowops.cuh", "csrc/ptx.cuh",
+                  "csrc/npue_file.h", "../include/nebw.h"]
+NVCC_FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
+              "-Xcompiler", "-fPIC", "-shared"]
+
+
+def nvcc() -> str:
+    for c in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if c and Path(c).exists():
+            return c
+    raise FileNotFoundError("nvcc not found")
+
+
+def build_lib(force: bool = False, verbose: bool = False) -> Path:
+    out = PKG / "libnebw.so"
+    newest = max((PKG / d).stat().st_mtime for d in DEPS)
+    if out.exists() and out.stat().st_mtime >= newest and not force:
+        return out
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(out), *[str(PKG / s) for s in SOURCES]]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True, cwd=PKG)
+    return out
+
+
+def build_oracle(verbose: bool = False):
+    make = shutil.which("make")
+    if not make:
+        raise FileNotFoundError("make not found")
+    subprocess.run([make, "-s", "-C", str(REPO / "oracle"), "port"], check=True)
+    ref = Path(os.environ.get("NEBW_REFERENCE", "/root/reference"))
+    if (ref / "runtime" / "src" / "encoders" / "bert_encoder.cpp").exists():
+        subprocess.run([make, "-s", "-j8", "-C", str(REPO / "oracle"), "ref", f"REF={ref}"],
+                       check=True)
+
+
+def main(argv):
+    build_lib(force="--force" in argv, verbose=True)
+    if "--lib" not in argv:
+        build_oracle(verbose=True)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])

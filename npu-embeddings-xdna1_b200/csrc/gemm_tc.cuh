@@ -1,0 +1,324 @@
+// The unified bf16 GEMM of the encoder (QKV, attention-out, FFN-up,
+// FFN-down) on the sm_100a tensor cores.
+//
+//   C[M, N] = epilogue( A[M, K] . W[N, K]^T )        A, W bf16; accumulate fp32
+//
+// This replaces the reference's gemm_rtp design set (AIE MMAC over
+// pre-tiled B panels, tools/lib/gemm_pretiled.py:1-60, dispatched from
+// BertEncoder::gemm, runtime/src/encoders/bert_encoder.cpp:741-924) and its
+// host twin hostconv::gemm_nt (runtime/include/common/conv_host.hpp:150-181),
+// with the elementwise passes that follow a GEMM in BertEncoder::run folded
+// into the epilogue:
+//   + bias                      (gemm_nt adds it last, conv_host.hpp:177)
+//   + gelu8 / erf GELU          (gelu_cpu, bert_encoder.cpp:532-580;
+//                                gelu_erf_exact, app_state.hpp:116-120)
+//   + residual, fp32 out        (add_into, bert_encoder.cpp:1183-1194)
+//   fp32 -> bf16 RNE narrow     (kernels/narrow_f32_bf16.cc; to_bf16,
+//                                host_kernels.hpp:157-161)
+//
+// Design (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: A and W tiles of 64 K-elements, 128-byte
+//               swizzled, into a STAGES-deep ring of shared-memory stages
+//   warp 1      allocates TMEM, issues tcgen05.mma (M=128, N=BN, K=16) from
+//               one thread, commits each stage back to the producer and each
+//               finished tile to the epilogue
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (one row per thread),
+//               bias / activation / residual in fp32, store
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// M may be read from device memory at kernel start (the packed token count
+// of a varlen batch), so a whole encoder pass needs no host round trip.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace nebw {
+
+enum GemmEpi : int {
+  kEpiBf16 = 0,       // out bf16 = acc + bias
+  kEpiBf16Gelu8 = 1,  // out bf16 = gelu8(acc + bias)
+  kEpiBf16Erf = 2,    // out bf16 = erf-gelu(acc + bias)
+  kEpiF32 = 3,        // out f32  = acc + bias
+  kEpiF32Resid = 4,   // out f32  = (acc + bias) + resid   (resid may alias out)
+};
+
+struct GemmArgs {
+  int M;             // row bound (the A tensor map's row extent)
+  const int *M_dev;  // if set, the live row count is min(*M_dev, M)
+  int N, K;
+  const float *bias;   // [N] or null
+  const float *resid;  // [M, N] fp32 for kEpiF32Resid
+  void *out;           // [M, N], bf16 or fp32 by epilogue
+  int *err;            // device error word
+};
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmShape {
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
+  static constexpr int kBBytes = BN * kGemmBK * 2;       // 16 or 32 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;               // 256 or 512
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kBarBytes;
+};
+
+// ---- activation functions of the epilogue ------------------------------------
+
+// gelu8: max(v,0) + P(min(|v|,4)), the reference's degree-8 polynomial with
+// its own coefficients (host_kernels.hpp:322-352), Horner with fused
+// multiply-adds exactly as its AVX2 form evaluates it.
+__device__ __forceinline__ float gelu8(float v) {
+  const float u = fminf(fabsf(v), 4.0f);
+  float pl = fmaf(-7.2340282171e-05f, u, 1.8179518005e-03f);
+  pl = fmaf(pl, u, -1.7707383379e-02f);
+  pl = fmaf(pl, u, 8.4577147641e-02f);
+  pl = fmaf(pl, u, -1.9228671834e-01f);
+  pl = fmaf(pl, u, 9.8431124458e-02f);
+  pl = fmaf(pl, u, 3.6137852062e-01f);
+  pl = fmaf(pl, u, -4.9454128936e-01f);
+  pl = fmaf(pl, u, -1.3007010117e-04f);
+  return fmaxf(v, 0.0f) + pl;
+}
+
+// Exact-erf GELU, 0.5 x (1 + erf(x / sqrt 2)), through CUDA's erff.
+__device__ __forceinline__ float gelu_erf(float v) {
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+}
+
+template <int EPI>
+__device__ __forceinline__ float epi_act(float v) {
+  if constexpr (EPI == kEpiBf16Gelu8) return gelu8(v);
+  else if constexpr (EPI == kEpiBf16Erf) return gelu_erf(v);
+  else return v;
+}
+
+// Store 32 accumulator columns [col0, col0+32) of one output row.
+template <int EPI>
+__device__ __forceinline__ void epi_store32(const GemmArgs &p, int row, int col0,
+                                            const uint32_t (&r)[32]) {
+  const int N = p.N;
+  const int ncols = min(32, N - col0);  // N % 8 == 0, so ncols % 8 == 0
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (p.bias) {
+    const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i * 4 < ncols) {
+        const float4 b = __ldg(b4 + i);
+        v[4 * i + 0] += b.x;
+        v[4 * i + 1] += b.y;
+        v[4 * i + 2] += b.z;
+        v[4 * i + 3] += b.w;
+      }
+    }
+  }
+  const size_t base = static_cast<size_t>(row) * N + col0;
+  if constexpr (EPI == kEpiF32 || EPI == kEpiF32Resid) {
+    float *o = static_cast<float *>(p.out) + base;
+    if constexpr (EPI == kEpiF32Resid) {
+      const float4 *r4 = reinterpret_cast<const float4 *>(p.resid + base);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i * 4 < ncols) {
+          const float4 x = r4[i];
+          v[4 * i + 0] += x.x;
+          v[4 * i + 1] += x.y;
+          v[4 * i + 2] += x.z;
+          v[4 * i + 3] += x.w;
+        }
+      }
+    }
+    float4 *o4 = reinterpret_cast<float4 *>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i * 4 < ncols) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out) + base);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i * 8 < ncols) {
+        uint4 w;
+        w.x = pack_bf16x2(epi_act<EPI>(v[8 * i + 0]), epi_act<EPI>(v[8 * i + 1]));
+        w.y = pack_bf16x2(epi_act<EPI>(v[8 * i + 2]), epi_act<EPI>(v[8 * i + 3]));
+        w.z = pack_bf16x2(epi_act<EPI>(v[8 * i + 4]), epi_act<EPI>(v[8 * i + 5]));
+        w.w = pack_bf16x2(epi_act<EPI>(v[8 * i + 6]), epi_act<EPI>(v[8 * i + 7]));
+        o4[i] = w;
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const GemmArgs p) {
+  using S = GemmShape<BN>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sW = smem + kStages * S::kABytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *tfull = empty + kStages;   // [2] accumulator ready for the epilogue
+  uint64_t *tempty = tfull + 2;        // [2] accumulator drained by the epilogue
+  uint64_t *drain = tempty + 2;        // [1] MMA-side drain at exit
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int M = p.M;
+  if (p.M_dev) M = min(M, __ldg(p.M_dev));
+  const int m_blocks = (M + kGemmBM - 1) / kGemmBM;
+  const int n_blocks = (p.N + BN - 1) / BN;
+  const int num_tiles = m_blocks * n_blocks;
+  const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase = 0;  // per stage: ever issued, parity of last issue
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile / n_blocks, nb = tile % n_blocks;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          tma_load_2d(sA + stage * S::kABytes, &tmA, &full[stage], kb * kGemmBK, mb * kGemmBM);
+          tma_load_2d(sW + stage * S::kBBytes, &tmW, &full[stage], kb * kGemmBK, nb * BN);
+          issued_mask |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: every stage this thread loaded has landed before the CTA may
+      // exit (normally already true -- the MMA thread waited on each).
+      for (int s = 0; s < kStages; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_phase >> s) & 1u, p.err);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kGemmBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued_any = false, ok = true;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
+          const uint32_t w0 = smem_u32(sW + stage * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma_bf16(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(w0 + k * 32),
+                      idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);  // stage reusable once these MMAs retire
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+      // Drain: all MMAs this thread issued have retired before TMEM is freed.
+      if (issued_any) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, p.err);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      // warp-uniform outcome: the tcgen05.ld below is warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, p.err))) break;
+      tc_fence_after();
+      const int mb = tile / n_blocks, nb = tile % n_blocks;
+      const int row = mb * kGemmBM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_wait_ld();
+        const int col0 = nb * BN + c;
+        if (row < M && col0 < p.N) epi_store32<EPI>(p, row, col0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+}  // namespace nebw

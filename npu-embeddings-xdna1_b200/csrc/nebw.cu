@@ -1,0 +1,972 @@
+// The C ABI of include/nebw.h: device handles, weight staging, the op entry
+// points, and the whole-encoder pass for one GPU.
+//
+// The encoder pass mirrors BertEncoder::run (runtime/src/encoders/
+// bert_encoder.cpp:1419-1598) on packed variable-length rows:
+//
+//   pack_offsets   lens -> seq_off (T = seq_off[B] stays on the device)
+//   embed_ln       x = LN_emb((word[id] + pos[s]) + type[0]);  a = bf16(x)
+//   per layer L:
+//     gemm QKV     qkv = bf16(a . Wqkv + b)
+//     attention    ctx = softmax(Q K^T) V           (per sequence, per head)
+//     gemm AO      x   = (ctx . Wao + b) + x        (fp32 residual, in place)
+//     layernorm    x   = LN1(x);  a = bf16(x)
+//     gemm UP      h   = bf16(gelu(a . Wup + b))
+//     gemm DOWN    x   = (h . Wdn + b) + x
+//     layernorm    x   = LN2(x);  a = bf16(x)
+//   pool_l2        out = normalise(pool(x))
+//
+// Nothing in a pass needs the host to know T: every kernel bounds itself by
+// the device-resident count, so the pass is one asynchronous launch
+// sequence.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/nebw.h"
+#include "attention.cuh"
+#include "gemm_tc.cuh"
+#include "npue_file.h"
+#include "ptx.cuh"
+#include "rowops.cuh"
+
+using nebw::GemmArgs;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_error(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define NEBW_CUDA(call)                                                                   \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return set_error(NEBW_ECUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                       __FILE__, __LINE__);                                               \
+  } while (0)
+
+#define NEBW_REQUIRE(cond, ...)                        \
+  do {                                                 \
+    if (!(cond)) return set_error(NEBW_EINVAL, __VA_ARGS__); \
+  } while (0)
+
+const char *dev_err_name(int code) {
+  switch (code) {
+    case nebw::kDevWaitTimeout: return "a bounded device wait timed out";
+    case nebw::kDevBadTokenId: return "a token id is outside [0, vocab_size)";
+    case nebw::kDevBadLength: return "a sequence length is outside [1, seq]";
+    case nebw::kDevBadShape: return "a kernel was handed a shape its launch cannot cover";
+    default: return "unknown device error";
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+std::once_flag g_encode_once;
+
+int load_tensor_map_encoder() {
+  std::call_once(g_encode_once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode_tiled)
+    return set_error(NEBW_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return NEBW_OK;
+}
+
+// A 2-D bf16 K-major tensor map [rows, K] with a {64, box_rows} box and
+// 128-byte swizzle (the GEMM's A and W operand tiles).
+int make_tmap_kmajor(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int box_rows) {
+  if (int rc = load_tensor_map_encoder()) return rc;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return set_error(NEBW_EINVAL, "GEMM operand address is not 16-byte aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(nebw::kGemmBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NEBW_ECUDA, "cuTensorMapEncodeTiled failed (%d) for [%lld, %lld] box %d",
+                     static_cast<int>(r), static_cast<long long>(rows),
+                     static_cast<long long>(K), box_rows);
+  return NEBW_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// device handle
+// ---------------------------------------------------------------------------
+
+struct Weight {
+  __nv_bfloat16 *ptr = nullptr;  // [N, K] bf16
+  int64_t K = 0, N = 0;
+  CUtensorMap map128, map256;    // box rows 128 / 256
+};
+
+struct nebw_dev {
+  int device = 0;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  cudaStream_t stream = nullptr;
+  int *d_err = nullptr;
+  std::map<uint64_t, Weight> weights;
+  uint64_t next_handle = 1;
+};
+
+namespace {
+
+int use_dev(nebw_dev *d) {
+  NEBW_REQUIRE(d != nullptr, "null device handle");
+  NEBW_CUDA(cudaSetDevice(d->device));
+  return NEBW_OK;
+}
+
+cudaStream_t pick_stream(nebw_dev *d, void *stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : d->stream;
+}
+
+template <int BN, int EPI>
+int set_gemm_attr() {
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_tc_kernel<BN, EPI>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::GemmShape<BN>::kSmemBytes));
+  return NEBW_OK;
+}
+
+int set_all_gemm_attrs() {
+  int rc = 0;
+  rc |= set_gemm_attr<128, nebw::kEpiBf16>();
+  rc |= set_gemm_attr<128, nebw::kEpiBf16Gelu8>();
+  rc |= set_gemm_attr<128, nebw::kEpiBf16Erf>();
+  rc |= set_gemm_attr<128, nebw::kEpiF32>();
+  rc |= set_gemm_attr<128, nebw::kEpiF32Resid>();
+  rc |= set_gemm_attr<256, nebw::kEpiBf16>();
+  rc |= set_gemm_attr<256, nebw::kEpiBf16Gelu8>();
+  rc |= set_gemm_attr<256, nebw::kEpiBf16Erf>();
+  rc |= set_gemm_attr<256, nebw::kEpiF32>();
+  rc |= set_gemm_attr<256, nebw::kEpiF32Resid>();
+  return rc ? NEBW_ECUDA : NEBW_OK;
+}
+
+// ---- launchers shared by the op entry points and the encoder pass ----------
+
+int pick_epi(int act, int c_dtype, bool resid) {
+  if (c_dtype == NEBW_F32) return resid ? nebw::kEpiF32Resid : nebw::kEpiF32;
+  if (act == NEBW_ACT_GELU8) return nebw::kEpiBf16Gelu8;
+  if (act == NEBW_ACT_GELU_ERF) return nebw::kEpiBf16Erf;
+  return nebw::kEpiBf16;
+}
+
+template <int BN>
+int launch_gemm_bn(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensorMap &mW,
+                   const GemmArgs &a, cudaStream_t st) {
+  const int64_t tiles = ((static_cast<int64_t>(a.M) + nebw::kGemmBM - 1) / nebw::kGemmBM) *
+                        ((a.N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, d->sm_count));
+  if (grid <= 0) return NEBW_OK;
+  const dim3 g(grid), b(nebw::kGemmThreads);
+  const size_t smem = nebw::GemmShape<BN>::kSmemBytes;
+  switch (epi) {
+    case nebw::kEpiBf16: nebw::gemm_tc_kernel<BN, nebw::kEpiBf16><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiBf16Gelu8: nebw::gemm_tc_kernel<BN, nebw::kEpiBf16Gelu8><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiBf16Erf: nebw::gemm_tc_kernel<BN, nebw::kEpiBf16Erf><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiF32: nebw::gemm_tc_kernel<BN, nebw::kEpiF32><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiF32Resid: nebw::gemm_tc_kernel<BN, nebw::kEpiF32Resid><<<g, b, smem, st>>>(mA, mW, a); break;
+    default: return set_error(NEBW_EINVAL, "unknown GEMM epilogue %d", epi);
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+// Tile width: 256 when N is a multiple of 256, else 128 (N % 128 == 0 keeps
+// every tile full; other N % 8 == 0 widths run a masked last tile).
+int gemm_bn_for(int64_t N) { return N % 256 == 0 ? 256 : 128; }
+
+int launch_gemm(nebw_dev *d, const Weight &w, const CUtensorMap &mA128, int epi,
+                const GemmArgs &a, cudaStream_t st) {
+  if (gemm_bn_for(a.N) == 256) return launch_gemm_bn<256>(d, epi, mA128, w.map256, a, st);
+  return launch_gemm_bn<128>(d, epi, mA128, w.map128, a, st);
+}
+
+template <int NV>
+void launch_ln_nv(float *x, const float *y, const float *g, const float *b, float eps, int rows,
+                  const int *rows_dev, __nv_bfloat16 *a, cudaStream_t st) {
+  const int grid = (rows + nebw::kRowWarps - 1) / nebw::kRowWarps;
+  nebw::layernorm_kernel<NV><<<grid, nebw::kRowWarps * 32, 0, st>>>(x, y, g, b, eps, rows, rows_dev, a);
+}
+
+int launch_layernorm(float *x, const float *y, const float *g, const float *b, float eps,
+                     int64_t rows, int64_t H, const int *rows_dev, __nv_bfloat16 *a,
+                     cudaStream_t st) {
+  NEBW_REQUIRE(H % 128 == 0 && H >= 128 && H <= 2048,
+               "LayerNorm width %lld refused: a multiple of 128 up to 2048 is required",
+               static_cast<long long>(H));
+  if (rows <= 0) return NEBW_OK;
+  const int r = static_cast<int>(rows);
+  switch (H / 128) {
+#define NEBW_LN_CASE(n) \
+  case n: launch_ln_nv<n>(x, y, g, b, eps, r, rows_dev, a, st); break;
+    NEBW_LN_CASE(1) NEBW_LN_CASE(2) NEBW_LN_CASE(3) NEBW_LN_CASE(4) NEBW_LN_CASE(5)
+    NEBW_LN_CASE(6) NEBW_LN_CASE(7) NEBW_LN_CASE(8) NEBW_LN_CASE(9) NEBW_LN_CASE(10)
+    NEBW_LN_CASE(11) NEBW_LN_CASE(12) NEBW_LN_CASE(13) NEBW_LN_CASE(14) NEBW_LN_CASE(15)
+    NEBW_LN_CASE(16)
+#undef NEBW_LN_CASE
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+template <int NV>
+void launch_embed_nv(const int *ids, int B, int S, const int *off, const int *len,
+                     const float *word, int vocab, const float *pos, const float *typ,
+                     const float *g, const float *b, float eps, float *x, __nv_bfloat16 *a,
+                     int *err, cudaStream_t st) {
+  const dim3 grid((S + nebw::kRowWarps - 1) / nebw::kRowWarps, B);
+  nebw::embed_ln_kernel<NV><<<grid, nebw::kRowWarps * 32, 0, st>>>(ids, S, off, len, word, vocab,
+                                                                  pos, typ, g, b, eps, x, a, err);
+}
+
+int launch_embed_ln(const int *ids, int B, int S, const int *off, const int *len,
+                    const float *word, int vocab, const float *pos, const float *typ,
+                    const float *g, const float *b, float eps, int H, float *x,
+                    __nv_bfloat16 *a, int *err, cudaStream_t st) {
+  NEBW_REQUIRE(H % 128 == 0 && H >= 128 && H <= 2048,
+               "hidden %d refused: a multiple of 128 up to 2048 is required", H);
+  NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
+  switch (H / 128) {
+#define NEBW_EMB_CASE(n) \
+  case n: launch_embed_nv<n>(ids, B, S, off, len, word, vocab, pos, typ, g, b, eps, x, a, err, st); break;
+    NEBW_EMB_CASE(1) NEBW_EMB_CASE(2) NEBW_EMB_CASE(3) NEBW_EMB_CASE(4) NEBW_EMB_CASE(5)
+    NEBW_EMB_CASE(6) NEBW_EMB_CASE(7) NEBW_EMB_CASE(8) NEBW_EMB_CASE(9) NEBW_EMB_CASE(10)
+    NEBW_EMB_CASE(11) NEBW_EMB_CASE(12) NEBW_EMB_CASE(13) NEBW_EMB_CASE(14) NEBW_EMB_CASE(15)
+    NEBW_EMB_CASE(16)
+#undef NEBW_EMB_CASE
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+int launch_attention(const __nv_bfloat16 *qkv, const int *off, const int *len, int B, int max_len,
+                     int heads, int hd, __nv_bfloat16 *ctx, cudaStream_t st) {
+  NEBW_REQUIRE(hd == 32 || hd == 64, "head_dim %d refused: 32 or 64", hd);
+  NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0,
+               "attention grid refused (B %d, heads %d, max_len %d)", B, heads, max_len);
+  const int H = heads * hd;
+  const dim3 grid((max_len + nebw::kAttnQTile - 1) / nebw::kAttnQTile, heads, B);
+  if (hd == 64)
+    nebw::attention_kernel<64><<<grid, nebw::kAttnThreads, 0, st>>>(qkv, off, len, H, ctx);
+  else
+    nebw::attention_kernel<32><<<grid, nebw::kAttnThreads, 0, st>>>(qkv, off, len, H, ctx);
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+int launch_pool(const float *h, const int *off, const int *len, int B, int H, int pooling, int l2,
+                float *out, cudaStream_t st) {
+  NEBW_REQUIRE(H > 0 && H <= 16 * nebw::kPoolThreads, "pool width %d refused (<= 4096)", H);
+  if (B <= 0) return NEBW_OK;
+  nebw::pool_l2_kernel<<<B, nebw::kPoolThreads, 0, st>>>(h, off, len, H,
+                                                         pooling == NEBW_POOL_CLS, l2, out);
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+int launch_pack(const int *len_in, int B, int S, int *len_out, int *off, int *err,
+                cudaStream_t st) {
+  NEBW_REQUIRE(B > 0 && B <= (1 << 24), "batch %d refused", B);
+  nebw::pack_offsets_kernel<<<1, 1024, 0, st>>>(len_in, B, S, len_out, off, err);
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI: device
+// ---------------------------------------------------------------------------
+
+extern "C" const char *nebw_last_error(void) { return g_last_error.c_str(); }
+extern "C" int nebw_abi_version(void) { return NEBW_ABI_VERSION; }
+
+extern "C" int nebw_open(int device, nebw_dev **out) {
+  NEBW_REQUIRE(out != nullptr, "null output handle");
+  *out = nullptr;
+  int n = 0;
+  NEBW_CUDA(cudaGetDeviceCount(&n));
+  NEBW_REQUIRE(device >= 0 && device < n, "device %d refused: %d CUDA device(s) visible", device, n);
+  NEBW_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  NEBW_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10 || prop.minor != 0)
+    return set_error(NEBW_EINVAL,
+                     "device %d is %s (sm_%d%d); this library is built for sm_100a (B200) only",
+                     device, prop.name, prop.major, prop.minor);
+  std::unique_ptr<nebw_dev> d(new nebw_dev());
+  d->device = device;
+  d->sm_count = prop.multiProcessorCount;
+  d->cc_major = prop.major;
+  d->cc_minor = prop.minor;
+  NEBW_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+  NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
+  NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
+  if (int rc = set_all_gemm_attrs()) return rc;
+  if (int rc = load_tensor_map_encoder()) return rc;
+  *out = d.release();
+  return NEBW_OK;
+}
+
+extern "C" int nebw_close(nebw_dev *d) {
+  if (!d) return NEBW_OK;
+  cudaSetDevice(d->device);
+  cudaStreamSynchronize(d->stream);
+  for (auto &kv : d->weights) cudaFree(kv.second.ptr);
+  cudaFree(d->d_err);
+  cudaStreamDestroy(d->stream);
+  delete d;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_sync(nebw_dev *d) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_CUDA(cudaStreamSynchronize(d->stream));
+  int code = 0;
+  NEBW_CUDA(cudaMemcpy(&code, d->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
+    return set_error(NEBW_EDEVICE, "device error %d: %s", code, dev_err_name(code));
+  }
+  return NEBW_OK;
+}
+
+extern "C" int nebw_alloc(nebw_dev *d, size_t bytes, void **p) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(p != nullptr, "null output pointer");
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(NEBW_ENOMEM, "cudaMalloc of %zu bytes failed", bytes);
+  }
+  return NEBW_OK;
+}
+
+extern "C" int nebw_free(nebw_dev *d, void *p) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_CUDA(cudaFree(p));
+  return NEBW_OK;
+}
+
+extern "C" int nebw_copy_h2d(nebw_dev *d, void *dst, const void *src, size_t bytes) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d->stream));
+  NEBW_CUDA(cudaStreamSynchronize(d->stream));
+  return NEBW_OK;
+}
+
+extern "C" int nebw_copy_d2h(nebw_dev *d, void *dst, const void *src, size_t bytes) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, d->stream));
+  NEBW_CUDA(cudaStreamSynchronize(d->stream));
+  return NEBW_OK;
+}
+
+extern "C" int nebw_device_info(nebw_dev *d, int *sm, int *maj, int *min) {
+  NEBW_REQUIRE(d != nullptr, "null device handle");
+  if (sm) *sm = d->sm_count;
+  if (maj) *maj = d->cc_major;
+  if (min) *min = d->cc_minor;
+  return NEBW_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: weights
+// ---------------------------------------------------------------------------
+
+namespace {
+
+int stage_weight(nebw_dev *d, const void *host_kn, int dtype, int64_t K, int64_t N, Weight *w) {
+  NEBW_REQUIRE(host_kn != nullptr, "null weight data");
+  NEBW_REQUIRE(dtype == NEBW_F32 || dtype == NEBW_BF16, "weight dtype %d refused", dtype);
+  NEBW_REQUIRE(K >= 64 && N >= 8 && K % 8 == 0 && N % 8 == 0 && K < (1 << 30) && N < (1 << 30),
+               "weight [K=%lld, N=%lld] refused: K >= 64, K %% 8 == 0, N %% 8 == 0",
+               static_cast<long long>(K), static_cast<long long>(N));
+  const size_t esz = dtype == NEBW_F32 ? 4 : 2;
+  const size_t src_bytes = static_cast<size_t>(K) * N * esz;
+  void *tmp = nullptr;
+  NEBW_CUDA(cudaMalloc(&tmp, src_bytes));
+  __nv_bfloat16 *dst = nullptr;
+  if (cudaMalloc(&dst, static_cast<size_t>(K) * N * 2) != cudaSuccess) {
+    cudaFree(tmp);
+    return set_error(NEBW_ENOMEM, "cudaMalloc for a [%lld, %lld] weight failed",
+                     static_cast<long long>(N), static_cast<long long>(K));
+  }
+  cudaError_t e = cudaMemcpyAsync(tmp, host_kn, src_bytes, cudaMemcpyHostToDevice, d->stream);
+  if (e == cudaSuccess) {
+    const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32));
+    nebw::stage_weight_kernel<<<grid, dim3(32, 8), 0, d->stream>>>(
+        tmp, dtype == NEBW_BF16, static_cast<int>(K), static_cast<int>(N), dst);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+  cudaFree(tmp);
+  if (e != cudaSuccess) {
+    cudaFree(dst);
+    return set_error(NEBW_ECUDA, "weight staging failed: %s", cudaGetErrorString(e));
+  }
+  w->ptr = dst;
+  w->K = K;
+  w->N = N;
+  if (int rc = make_tmap_kmajor(&w->map128, dst, N, K, 128)) {
+    cudaFree(dst);
+    return rc;
+  }
+  if (int rc = make_tmap_kmajor(&w->map256, dst, N, K, 256)) {
+    cudaFree(dst);
+    return rc;
+  }
+  return NEBW_OK;
+}
+
+}  // namespace
+
+extern "C" int nebw_stage_weight(nebw_dev *d, const void *host_kn, int dtype, int64_t K, int64_t N,
+                                 uint64_t *handle) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(handle != nullptr, "null handle output");
+  Weight w;
+  if (int rc = stage_weight(d, host_kn, dtype, K, N, &w)) return rc;
+  *handle = d->next_handle++;
+  d->weights[*handle] = w;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_release_weight(nebw_dev *d, uint64_t handle) {
+  if (int rc = use_dev(d)) return rc;
+  auto it = d->weights.find(handle);
+  NEBW_REQUIRE(it != d->weights.end(), "unknown weight handle %llu",
+               static_cast<unsigned long long>(handle));
+  NEBW_CUDA(cudaStreamSynchronize(d->stream));
+  cudaFree(it->second.ptr);
+  d->weights.erase(it);
+  return NEBW_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: ops
+// ---------------------------------------------------------------------------
+
+extern "C" int nebw_gemm(nebw_dev *d, uint64_t weight, const void *A, int64_t M, int64_t K,
+                         int64_t N, const float *bias, const float *residual, int act, void *C,
+                         int c_dtype, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  auto it = d->weights.find(weight);
+  NEBW_REQUIRE(it != d->weights.end(), "unknown weight handle %llu",
+               static_cast<unsigned long long>(weight));
+  const Weight &w = it->second;
+  NEBW_REQUIRE(K == w.K && N == w.N, "GEMM [M, %lld] x [%lld, %lld] does not match the staged "
+               "weight [K=%lld, N=%lld]", static_cast<long long>(K), static_cast<long long>(K),
+               static_cast<long long>(N), static_cast<long long>(w.K), static_cast<long long>(w.N));
+  NEBW_REQUIRE(M >= 0 && M < (1 << 30), "M %lld refused", static_cast<long long>(M));
+  NEBW_REQUIRE(A != nullptr && C != nullptr, "null GEMM operand");
+  NEBW_REQUIRE(c_dtype == NEBW_F32 || c_dtype == NEBW_BF16, "output dtype %d refused", c_dtype);
+  NEBW_REQUIRE(act == NEBW_ACT_NONE || act == NEBW_ACT_GELU8 || act == NEBW_ACT_GELU_ERF,
+               "activation %d refused", act);
+  NEBW_REQUIRE(!(residual && c_dtype != NEBW_F32), "a residual needs fp32 output");
+  NEBW_REQUIRE(!(act != NEBW_ACT_NONE && c_dtype != NEBW_BF16),
+               "an activation epilogue writes bf16 output");
+  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+                   (!residual || reinterpret_cast<uintptr_t>(residual) % 16 == 0) &&
+                   (!bias || reinterpret_cast<uintptr_t>(bias) % 16 == 0),
+               "GEMM output, residual and bias must be 16-byte aligned");
+  if (M == 0) return NEBW_OK;
+  CUtensorMap mA;
+  if (int rc = make_tmap_kmajor(&mA, A, M, K, nebw::kGemmBM)) return rc;
+  GemmArgs a{};
+  a.M = static_cast<int>(M);
+  a.M_dev = nullptr;
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.bias = bias;
+  a.resid = residual;
+  a.out = C;
+  a.err = d->d_err;
+  return launch_gemm(d, w, mA, pick_epi(act, c_dtype, residual != nullptr), a,
+                     pick_stream(d, stream));
+}
+
+extern "C" int nebw_layernorm(nebw_dev *d, float *x, const float *y, const float *gamma,
+                              const float *beta, float eps, int64_t rows, int64_t H, void *a_bf16,
+                              void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(x && gamma && beta, "null LayerNorm operand");
+  NEBW_REQUIRE(rows >= 0 && rows < (1ll << 31) / 2, "rows %lld refused", static_cast<long long>(rows));
+  return launch_layernorm(x, y, gamma, beta, eps, rows, H, nullptr,
+                          static_cast<__nv_bfloat16 *>(a_bf16), pick_stream(d, stream));
+}
+
+extern "C" int nebw_attention(nebw_dev *d, const void *qkv, const int32_t *off, const int32_t *len,
+                              int32_t B, int32_t max_len, int32_t heads, int32_t hd, void *ctx,
+                              void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(qkv && off && len && ctx, "null attention operand");
+  return launch_attention(static_cast<const __nv_bfloat16 *>(qkv), off, len, B, max_len, heads, hd,
+                          static_cast<__nv_bfloat16 *>(ctx), pick_stream(d, stream));
+}
+
+extern "C" int nebw_pack_offsets(nebw_dev *d, const int32_t *len_in, int32_t B, int32_t S,
+                                 int32_t *len_out, int32_t *off, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(len_in && len_out && off, "null packing operand");
+  return launch_pack(len_in, B, S, len_out, off, d->d_err, pick_stream(d, stream));
+}
+
+extern "C" int nebw_embed_ln(nebw_dev *d, const int32_t *ids, const int32_t *off,
+                             const int32_t *len, int32_t B, int32_t S, const float *word,
+                             int32_t vocab, const float *pos, const float *typ, const float *gamma,
+                             const float *beta, float eps, int32_t H, float *x, void *a_bf16,
+                             void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(ids && off && len && word && pos && typ && gamma && beta && x,
+               "null embedding operand");
+  return launch_embed_ln(ids, B, S, off, len, word, vocab, pos, typ, gamma, beta, eps, H, x,
+                         static_cast<__nv_bfloat16 *>(a_bf16), d->d_err, pick_stream(d, stream));
+}
+
+extern "C" int nebw_pool_l2(nebw_dev *d, const float *h, const int32_t *off, const int32_t *len,
+                            int32_t B, int32_t H, int pooling, int l2, float *out, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(h && off && len && out, "null pooling operand");
+  NEBW_REQUIRE(pooling == NEBW_POOL_MEAN || pooling == NEBW_POOL_CLS, "pooling %d refused", pooling);
+  return launch_pool(h, off, len, B, H, pooling, l2, out, pick_stream(d, stream));
+}
+
+extern "C" int nebw_narrow_bf16(nebw_dev *d, const float *x, int64_t n, void *y, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(x && y && n >= 0, "bad narrow operand");
+  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 8 == 0,
+               "narrow operands must be 16/8-byte aligned");
+  if (n == 0) return NEBW_OK;
+  const int64_t threads = 256, per = 4;
+  const int64_t blocks = (n + threads * per - 1) / (threads * per);
+  nebw::narrow_bf16_kernel<<<static_cast<unsigned>(blocks), threads, 0, pick_stream(d, stream)>>>(
+      x, n, static_cast<__nv_bfloat16 *>(y));
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI: the whole encoder
+// ---------------------------------------------------------------------------
+
+struct LayerW {
+  Weight qkv, ao, up, dn;
+  float *b_qkv = nullptr, *b_ao = nullptr, *b_up = nullptr, *b_dn = nullptr;
+  float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+};
+
+struct nebw_model {
+  nebw_dev *dev = nullptr;
+  nebw_config cfg{};
+  float *word = nullptr, *pos = nullptr, *typ = nullptr, *emb_g = nullptr, *emb_b = nullptr;
+  std::vector<LayerW> layers;
+  std::map<std::string, bool> staged;  // container name -> set
+  // workspace (capacity rows_cap = B * S of the largest call so far)
+  int64_t rows_cap = 0, batch_cap = 0, ids_cap = 0;
+  float *x = nullptr;
+  __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
+  int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
+  float *out = nullptr;
+  CUtensorMap map_a, map_ctx, map_h;
+};
+
+namespace {
+
+void free_workspace(nebw_model *m) {
+  cudaFree(m->x);
+  cudaFree(m->a);
+  cudaFree(m->qkv);
+  cudaFree(m->ctx);
+  cudaFree(m->h);
+  cudaFree(m->ids);
+  cudaFree(m->len_in);
+  cudaFree(m->len);
+  cudaFree(m->off);
+  cudaFree(m->out);
+  m->x = nullptr;
+  m->a = m->qkv = m->ctx = m->h = nullptr;
+  m->ids = m->len_in = m->len = m->off = nullptr;
+  m->out = nullptr;
+  m->rows_cap = m->batch_cap = m->ids_cap = 0;
+}
+
+int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
+  const int64_t rows = B * S;
+  if (rows <= m->rows_cap && B <= m->batch_cap) return NEBW_OK;
+  NEBW_CUDA(cudaStreamSynchronize(m->dev->stream));
+  free_workspace(m);
+  const int64_t H = m->cfg.hidden, F = m->cfg.intermediate;
+  const int64_t R = std::max(rows, m->rows_cap), Bc = std::max(B, m->batch_cap);
+  auto alloc = [&](void **p, size_t bytes) -> int {
+    if (cudaMalloc(p, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(NEBW_ENOMEM, "workspace allocation of %zu bytes failed", bytes);
+    }
+    return NEBW_OK;
+  };
+  int rc = 0;
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->x), R * H * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->a), R * H * 2);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->qkv), R * 3 * H * 2);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ctx), R * H * 2);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->h), R * F * 2);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ids), R * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len_in), Bc * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len), Bc * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->off), (Bc + 1) * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->out), Bc * H * 4);
+  if (rc) {
+    free_workspace(m);
+    return rc;
+  }
+  m->rows_cap = R;
+  m->batch_cap = Bc;
+  m->ids_cap = R;
+  if ((rc = make_tmap_kmajor(&m->map_a, m->a, R, H, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_kmajor(&m->map_ctx, m->ctx, R, H, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_kmajor(&m->map_h, m->h, R, F, nebw::kGemmBM))) return rc;
+  return NEBW_OK;
+}
+
+int upload_f32(nebw_dev *d, float **dst, const void *src, int dtype, int64_t n) {
+  NEBW_REQUIRE(dtype == NEBW_F32, "this tensor must be F32 (as the container stores it)");
+  if (*dst == nullptr) NEBW_CUDA(cudaMalloc(dst, n * 4));
+  NEBW_CUDA(cudaMemcpyAsync(*dst, src, n * 4, cudaMemcpyHostToDevice, d->stream));
+  NEBW_CUDA(cudaStreamSynchronize(d->stream));
+  return NEBW_OK;
+}
+
+std::vector<std::string> required_names(const nebw_config &c) {
+  std::vector<std::string> v = {"embeddings.word", "embeddings.position", "embeddings.token_type",
+                                "embeddings.ln.weight", "embeddings.ln.bias"};
+  for (int L = 0; L < c.num_layers; ++L) {
+    const std::string p = "layer." + std::to_string(L) + ".";
+    for (const char *s : {"qkv", "qkv.bias", "attn_out", "attn_out.bias", "ln1.weight", "ln1.bias",
+                          "ffn_up", "ffn_up.bias", "ffn_down", "ffn_down.bias", "ln2.weight",
+                          "ln2.bias"})
+      v.push_back(p + s);
+  }
+  return v;
+}
+
+int model_ready(const nebw_model *m) {
+  for (const auto &n : required_names(m->cfg))
+    if (!m->staged.count(n))
+      return set_error(NEBW_ESTATE, "model tensor '%s' has not been staged", n.c_str());
+  return NEBW_OK;
+}
+
+int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S, float *out,
+                  cudaStream_t st) {
+  nebw_dev *d = m->dev;
+  const nebw_config &c = m->cfg;
+  if (int rc = model_ready(m)) return rc;
+  NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
+  NEBW_REQUIRE(S > 0 && S <= c.max_seq_len, "seq %d refused: 1..max_seq_len (%d)", S,
+               c.max_seq_len);
+  if (int rc = ensure_workspace(m, B, S)) return rc;
+  const int64_t H = c.hidden, F = c.intermediate;
+  const int rows = static_cast<int>(static_cast<int64_t>(B) * S);
+  const int *T_dev = m->off + B;
+  int rc;
+  if ((rc = launch_pack(len_in, B, S, m->len, m->off, d->d_err, st))) return rc;
+  if ((rc = launch_embed_ln(ids, B, S, m->off, m->len, m->word, c.vocab_size, m->pos, m->typ,
+                            m->emb_g, m->emb_b, c.layer_norm_eps, c.hidden, m->x, m->a, d->d_err,
+                            st)))
+    return rc;
+  const int up_epi = c.activation == NEBW_ACT_GELU_ERF ? nebw::kEpiBf16Erf : nebw::kEpiBf16Gelu8;
+  for (int L = 0; L < c.num_layers; ++L) {
+    const LayerW &w = m->layers[L];
+    GemmArgs a{};
+    a.M = rows;
+    a.M_dev = T_dev;
+    a.err = d->d_err;
+    // QKV
+    a.N = static_cast<int>(3 * H);
+    a.K = static_cast<int>(H);
+    a.bias = w.b_qkv;
+    a.resid = nullptr;
+    a.out = m->qkv;
+    if ((rc = launch_gemm(d, w.qkv, m->map_a, nebw::kEpiBf16, a, st))) return rc;
+    // attention
+    if ((rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st)))
+      return rc;
+    // attention-out + bias + residual (fp32, in place)
+    a.N = static_cast<int>(H);
+    a.K = static_cast<int>(H);
+    a.bias = w.b_ao;
+    a.resid = m->x;
+    a.out = m->x;
+    if ((rc = launch_gemm(d, w.ao, m->map_ctx, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = launch_layernorm(m->x, nullptr, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
+                               m->a, st)))
+      return rc;
+    // FFN up + bias + GELU -> bf16
+    a.N = static_cast<int>(F);
+    a.K = static_cast<int>(H);
+    a.bias = w.b_up;
+    a.resid = nullptr;
+    a.out = m->h;
+    if ((rc = launch_gemm(d, w.up, m->map_a, up_epi, a, st))) return rc;
+    // FFN down + bias + residual (fp32, in place)
+    a.N = static_cast<int>(H);
+    a.K = static_cast<int>(F);
+    a.bias = w.b_dn;
+    a.resid = m->x;
+    a.out = m->x;
+    if ((rc = launch_gemm(d, w.dn, m->map_h, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = launch_layernorm(m->x, nullptr, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
+                               L + 1 < c.num_layers ? m->a : nullptr, st)))
+      return rc;
+  }
+  return launch_pool(m->x, m->off, m->len, B, c.hidden, c.pooling, c.l2_normalize, out, st);
+}
+
+}  // namespace
+
+extern "C" int nebw_model_create(nebw_dev *d, const nebw_config *cfg, nebw_model **out) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(cfg && out, "null argument");
+  const nebw_config &c = *cfg;
+  NEBW_REQUIRE(c.num_layers > 0 && c.hidden > 0 && c.num_heads > 0 && c.max_seq_len > 0 &&
+                   c.vocab_size > 0 && c.intermediate > 0 && c.type_vocab_size > 0,
+               "the model reports a non-positive shape");
+  NEBW_REQUIRE(c.head_dim * c.num_heads == c.hidden, "head_dim * heads != hidden");
+  NEBW_REQUIRE(c.head_dim == 32 || c.head_dim == 64, "head_dim %d refused: 32 or 64", c.head_dim);
+  NEBW_REQUIRE(c.hidden % 128 == 0 && c.hidden <= 2048, "hidden %d refused: multiple of 128, <= 2048",
+               c.hidden);
+  NEBW_REQUIRE(c.intermediate % 64 == 0, "intermediate %d refused: multiple of 64", c.intermediate);
+  NEBW_REQUIRE(c.pooling == NEBW_POOL_MEAN || c.pooling == NEBW_POOL_CLS, "pooling %d refused",
+               c.pooling);
+  NEBW_REQUIRE(c.activation == NEBW_ACT_GELU8 || c.activation == NEBW_ACT_GELU_ERF,
+               "activation %d refused", c.activation);
+  std::unique_ptr<nebw_model> m(new nebw_model());
+  m->dev = d;
+  m->cfg = c;
+  m->layers.resize(c.num_layers);
+  *out = m.release();
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_set_tensor(nebw_model *m, const char *name, const void *host, int dtype,
+                                     int64_t rows, int64_t cols) {
+  NEBW_REQUIRE(m && name && host, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  const nebw_config &c = m->cfg;
+  const std::string n(name);
+  const int64_t H = c.hidden, F = c.intermediate;
+  auto expect = [&](int64_t r, int64_t cc) -> int {
+    if (rows != r || cols != cc)
+      return set_error(NEBW_EINVAL, "tensor '%s' is [%lld, %lld], expected [%lld, %lld]", name,
+                       static_cast<long long>(rows), static_cast<long long>(cols),
+                       static_cast<long long>(r), static_cast<long long>(cc));
+    return NEBW_OK;
+  };
+  int rc = NEBW_OK;
+  if (n == "embeddings.word") {
+    if (!(rc = expect(c.vocab_size, H))) rc = upload_f32(m->dev, &m->word, host, dtype, rows * cols);
+  } else if (n == "embeddings.position") {
+    NEBW_REQUIRE(cols == H && rows >= c.max_seq_len, "position table '%s' needs >= %d rows of %lld",
+                 name, c.max_seq_len, static_cast<long long>(H));
+    rc = upload_f32(m->dev, &m->pos, host, dtype, static_cast<int64_t>(c.max_seq_len) * H);
+  } else if (n == "embeddings.token_type") {
+    NEBW_REQUIRE(cols == H && rows >= 1, "token-type table must be [>=1, hidden]");
+    rc = upload_f32(m->dev, &m->typ, host, dtype, H);  // type id 0 only
+  } else if (n == "embeddings.ln.weight") {
+    if (!(rc = expect(1, H)) || !(rc = expect(H, 1)) || true) {
+      NEBW_REQUIRE(rows * cols == H, "'%s' must hold hidden values", name);
+      rc = upload_f32(m->dev, &m->emb_g, host, dtype, H);
+    }
+  } else if (n == "embeddings.ln.bias") {
+    NEBW_REQUIRE(rows * cols == H, "'%s' must hold hidden values", name);
+    rc = upload_f32(m->dev, &m->emb_b, host, dtype, H);
+  } else if (n.rfind("layer.", 0) == 0) {
+    const size_t dot = n.find('.', 6);
+    NEBW_REQUIRE(dot != std::string::npos, "malformed tensor name '%s'", name);
+    const int L = std::atoi(n.substr(6, dot - 6).c_str());
+    NEBW_REQUIRE(L >= 0 && L < c.num_layers, "tensor '%s' names a layer outside [0, %d)", name,
+                 c.num_layers);
+    const std::string leaf = n.substr(dot + 1);
+    LayerW &w = m->layers[L];
+    auto vec = [&](float **dst, int64_t len) -> int {
+      if (rows * cols != len)
+        return set_error(NEBW_EINVAL, "tensor '%s' must hold %lld values", name,
+                         static_cast<long long>(len));
+      return upload_f32(m->dev, dst, host, dtype, len);
+    };
+    auto gemm_w = [&](Weight *dst, int64_t K, int64_t N) -> int {
+      if (int e = expect(K, N)) return e;
+      if (dst->ptr) {
+        cudaFree(dst->ptr);
+        dst->ptr = nullptr;
+      }
+      return stage_weight(m->dev, host, dtype, K, N, dst);
+    };
+    if (leaf == "qkv") rc = gemm_w(&w.qkv, H, 3 * H);
+    else if (leaf == "qkv.bias") rc = vec(&w.b_qkv, 3 * H);
+    else if (leaf == "attn_out") rc = gemm_w(&w.ao, H, H);
+    else if (leaf == "attn_out.bias") rc = vec(&w.b_ao, H);
+    else if (leaf == "ffn_up") rc = gemm_w(&w.up, H, F);
+    else if (leaf == "ffn_up.bias") rc = vec(&w.b_up, F);
+    else if (leaf == "ffn_down") rc = gemm_w(&w.dn, F, H);
+    else if (leaf == "ffn_down.bias") rc = vec(&w.b_dn, H);
+    else if (leaf == "ln1.weight") rc = vec(&w.ln1_g, H);
+    else if (leaf == "ln1.bias") rc = vec(&w.ln1_b, H);
+    else if (leaf == "ln2.weight") rc = vec(&w.ln2_g, H);
+    else if (leaf == "ln2.bias") rc = vec(&w.ln2_b, H);
+    else return set_error(NEBW_EINVAL, "unknown tensor '%s'", name);
+  } else {
+    return set_error(NEBW_EINVAL, "unknown tensor '%s'", name);
+  }
+  if (rc == NEBW_OK) m->staged[n] = true;
+  return rc;
+}
+
+extern "C" int nebw_model_destroy(nebw_model *m) {
+  if (!m) return NEBW_OK;
+  cudaSetDevice(m->dev->device);
+  cudaStreamSynchronize(m->dev->stream);
+  free_workspace(m);
+  for (float *p : {m->word, m->pos, m->typ, m->emb_g, m->emb_b}) cudaFree(p);
+  for (auto &w : m->layers) {
+    for (Weight *x : {&w.qkv, &w.ao, &w.up, &w.dn}) cudaFree(x->ptr);
+    for (float *p : {w.b_qkv, w.b_ao, w.b_up, w.b_dn, w.ln1_g, w.ln1_b, w.ln2_g, w.ln2_b})
+      cudaFree(p);
+  }
+  delete m;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_get_config(const nebw_model *m, nebw_config *cfg) {
+  NEBW_REQUIRE(m && cfg, "null argument");
+  *cfg = m->cfg;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **out) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(path && out, "null argument");
+  *out = nullptr;
+  try {
+    nebw::NpueFile f(path);
+    const std::string arch = f.config_string("arch");
+    if (arch != "bert_abs_gelu_postln")
+      return set_error(NEBW_EINVAL,
+                       "container architecture '%s' has no encoder in this library; only "
+                       "bert_abs_gelu_postln is implemented", arch.c_str());
+    std::string layout = "pretiled_bf16";
+    if (f.has_config("gemm_layout")) layout = f.config_string("gemm_layout");
+    if (layout != "host")
+      return set_error(NEBW_EINVAL,
+                       "container gemm_layout '%s' refused: this library stages the plain "
+                       "row-major [K, N] operands of a gemm_layout \"host\" container and "
+                       "re-tiles them itself", layout.c_str());
+    nebw_config c{};
+    c.num_layers = static_cast<int32_t>(f.config_int("num_layers"));
+    c.hidden = static_cast<int32_t>(f.config_int("hidden"));
+    c.num_heads = static_cast<int32_t>(f.config_int("num_heads"));
+    c.head_dim = static_cast<int32_t>(f.config_int("head_dim"));
+    c.intermediate = static_cast<int32_t>(f.config_int("intermediate"));
+    c.max_seq_len = static_cast<int32_t>(f.config_int("max_seq_len"));
+    const auto &word = f.tensor("embeddings.word");
+    c.vocab_size = static_cast<int32_t>(word.shape.at(0));
+    c.type_vocab_size = static_cast<int32_t>(f.tensor("embeddings.token_type").shape.at(0));
+    const std::string pool = f.config_string("pooling");
+    if (pool == "cls") c.pooling = NEBW_POOL_CLS;
+    else if (pool == "mean") c.pooling = NEBW_POOL_MEAN;
+    else return set_error(NEBW_EINVAL, "unknown pooling mode '%s' in the container", pool.c_str());
+    c.l2_normalize = f.has_config("l2_normalize") ? f.config_string("l2_normalize") == "true" : 1;
+    c.activation = NEBW_ACT_GELU8;  // what the reference's BERT host path runs (gelu_cpu)
+    c.layer_norm_eps = 1e-12f;      // hard-coded by layer_norm_cpu (bert_encoder.cpp:438)
+    nebw_model *m = nullptr;
+    if (int rc = nebw_model_create(d, &c, &m)) return rc;
+    for (const auto &n : required_names(c)) {
+      const auto &t = f.tensor(n);
+      if (t.dtype != "F32" && t.dtype != "BF16") {
+        nebw_model_destroy(m);
+        return set_error(NEBW_EINVAL, "tensor '%s' has dtype %s; F32 or BF16 expected",
+                         n.c_str(), t.dtype.c_str());
+      }
+      const int64_t r = t.shape.size() >= 1 ? t.shape[0] : 1;
+      const int64_t cc = t.shape.size() >= 2 ? t.shape[1] : 1;
+      const int dt = t.dtype == "F32" ? NEBW_F32 : NEBW_BF16;
+      int rc = nebw_model_set_tensor(m, n.c_str(), t.data, dt, r, cc);
+      if (rc) {
+        const std::string msg = g_last_error;
+        nebw_model_destroy(m);
+        return set_error(rc, "%s", msg.c_str());
+      }
+    }
+    *out = m;
+    return NEBW_OK;
+  } catch (const std::exception &e) {
+    return set_error(NEBW_EIO, "%s", e.what());
+  }
+}
+
+extern "C" int nebw_encode_device(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B,
+                                  int32_t S, float *out, void *stream) {
+  NEBW_REQUIRE(m && ids && lens && out, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  return encode_device(m, ids, lens, B, S, out, pick_stream(m->dev, stream));
+}
+
+extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B,
+                           int32_t S, float *out) {
+  NEBW_REQUIRE(m && ids && lens && out, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  NEBW_REQUIRE(B > 0 && S > 0, "empty batch refused");
+  if (int rc = model_ready(m)) return rc;
+  if (int rc = ensure_workspace(m, B, S)) return rc;
+  nebw_dev *d = m->dev;
+  cudaStream_t st = d->stream;
+  NEBW_CUDA(cudaMemcpyAsync(m->ids, ids, static_cast<size_t>(B) * S * 4, cudaMemcpyHostToDevice, st));
+  NEBW_CUDA(cudaMemcpyAsync(m->len_in, lens, static_cast<size_t>(B) * 4, cudaMemcpyHostToDevice, st));
+  if (int rc = encode_device(m, m->ids, m->len_in, B, S, m->out, st)) return rc;
+  NEBW_CUDA(cudaMemcpyAsync(out, m->out, static_cast<size_t>(B) * m->cfg.hidden * 4,
+                            cudaMemcpyDeviceToHost, st));
+  return nebw_sync(d);
+}
+
+extern "C" int nebw_encode_launch_count(const nebw_model *m) {
+  if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
+  return 3 + 7 * m->cfg.num_layers;
+}

@@ -1,0 +1,277 @@
+"""Python front of libnebw (include/nebw.h) through ctypes.
+
+This module is plumbing for tests, the benchmark and Python callers: the
+product is the C ABI and the CUDA kernels behind it.  There is no CPU path
+here: if libnebw.so is missing or no sm_100 GPU is present, the calls fail
+by name.
+
+Device buffers may be torch CUDA tensors (their data_ptr is passed) or raw
+integer device addresses.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+from pathlib import Path
+
+import numpy as np
+
+PKG_DIR = Path(__file__).resolve().parent.parent          # npu-embeddings-xdna1_b200/
+REPO_DIR = PKG_DIR.parent
+LIB_PATH = PKG_DIR / "libnebw.so"
+HEADER_PATH = REPO_DIR / "include" / "nebw.h"
+
+F32, BF16 = 0, 1
+ACT_NONE, ACT_GELU8, ACT_GELU_ERF = 0, 1, 2
+POOL_MEAN, POOL_CLS = 0, 1
+
+
+class NebwError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"nebw error {code}: {msg}")
+        self.code = code
+
+
+class Config(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "num_layers", "hidden", "num_heads", "head_dim", "intermediate", "vocab_size",
+        "max_seq_len", "type_vocab_size", "pooling", "l2_normalize", "activation")] + [
+        ("layer_norm_eps", C.c_float)]
+
+
+_lib = None
+
+
+def header_functions() -> list[str]:
+    """Names of every function include/nebw.h declares."""
+    text = HEADER_PATH.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(nebw_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib() -> C.CDLL:
+    """Load libnebw.so (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise FileNotFoundError(
+            f"{LIB_PATH} is not built; run `python __graft_entry__.py build` (or build()) first")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i64, i32 = C.c_void_p, C.c_int64, C.c_int32
+    sig = {
+        "nebw_last_error": ([], C.c_char_p),
+        "nebw_abi_version": ([], C.c_int),
+        "nebw_open": ([C.c_int, C.POINTER(vp)], C.c_int),
+        "nebw_close": ([vp], C.c_int),
+        "nebw_sync": ([vp], C.c_int),
+        "nebw_alloc": ([vp, C.c_size_t, C.POINTER(vp)], C.c_int),
+        "nebw_free": ([vp, vp], C.c_int),
+        "nebw_copy_h2d": ([vp, vp, vp, C.c_size_t], C.c_int),
+        "nebw_copy_d2h": ([vp, vp, vp, C.c_size_t], C.c_int),
+        "nebw_device_info": ([vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)], C.c_int),
+        "nebw_stage_weight": ([vp, vp, C.c_int, i64, i64, C.POINTER(C.c_uint64)], C.c_int),
+        "nebw_release_weight": ([vp, C.c_uint64], C.c_int),
+        "nebw_gemm": ([vp, C.c_uint64, vp, i64, i64, i64, vp, vp, C.c_int, vp, C.c_int, vp], C.c_int),
+        "nebw_layernorm": ([vp, vp, vp, vp, vp, C.c_float, i64, i64, vp, vp], C.c_int),
+        "nebw_attention": ([vp, vp, vp, vp, i32, i32, i32, i32, vp, vp], C.c_int),
+        "nebw_pack_offsets": ([vp, vp, i32, i32, vp, vp, vp], C.c_int),
+        "nebw_embed_ln": ([vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, vp, vp, C.c_float, i32, vp,
+                           vp, vp], C.c_int),
+        "nebw_pool_l2": ([vp, vp, vp, vp, i32, i32, C.c_int, C.c_int, vp, vp], C.c_int),
+        "nebw_narrow_bf16": ([vp, vp, i64, vp, vp], C.c_int),
+        "nebw_model_create": ([vp, C.POINTER(Config), C.POINTER(vp)], C.c_int),
+        "nebw_model_set_tensor": ([vp, C.c_char_p, vp, C.c_int, i64, i64], C.c_int),
+        "nebw_model_load_npue": ([vp, C.c_char_p, C.POINTER(vp)], C.c_int),
+        "nebw_model_destroy": ([vp], C.c_int),
+        "nebw_model_get_config": ([vp, C.POINTER(Config)], C.c_int),
+        "nebw_encode": ([vp, vp, vp, i32, i32, vp], C.c_int),
+        "nebw_encode_device": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
+        "nebw_encode_launch_count": ([vp], C.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise NebwError(rc, lib().nebw_last_error().decode())
+
+
+def _addr(x):
+    """Device/host address of a torch tensor, numpy array, int or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+def _stream(s):
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream  # torch.cuda.Stream
+
+
+class Device:
+    """One GPU (nebw_dev)."""
+
+    def __init__(self, index: int = 0):
+        h = C.c_void_p()
+        _check(lib().nebw_open(index, C.byref(h)))
+        self.h = h
+        self.index = index
+        self._weights = {}
+
+    def close(self):
+        if self.h:
+            lib().nebw_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def sync(self):
+        _check(lib().nebw_sync(self.h))
+
+    def info(self):
+        sm, ma, mi = C.c_int(), C.c_int(), C.c_int()
+        _check(lib().nebw_device_info(self.h, C.byref(sm), C.byref(ma), C.byref(mi)))
+        return {"sm_count": sm.value, "cc": (ma.value, mi.value)}
+
+    # ---- weights and ops -------------------------------------------------
+    def stage_weight(self, w_kn: np.ndarray) -> int:
+        w = np.ascontiguousarray(w_kn)
+        dt = F32 if w.dtype == np.float32 else BF16
+        if w.dtype not in (np.float32, np.uint16):
+            raise TypeError("weights are fp32, or bf16 bit patterns as uint16")
+        K, N = w.shape
+        hnd = C.c_uint64()
+        _check(lib().nebw_stage_weight(self.h, w.ctypes.data, dt, K, N, C.byref(hnd)))
+        return hnd.value
+
+    def release_weight(self, handle: int):
+        _check(lib().nebw_release_weight(self.h, handle))
+
+    def gemm(self, weight, A, M, K, N, C_out, bias=None, residual=None, act=ACT_NONE,
+             c_dtype=BF16, stream=None):
+        _check(lib().nebw_gemm(self.h, weight, _addr(A), M, K, N, _addr(bias), _addr(residual),
+                               act, _addr(C_out), c_dtype, _stream(stream)))
+
+    def layernorm(self, x, gamma, beta, rows, H, y=None, a_bf16=None, eps=1e-12, stream=None):
+        _check(lib().nebw_layernorm(self.h, _addr(x), _addr(y), _addr(gamma), _addr(beta), eps,
+                                    rows, H, _addr(a_bf16), _stream(stream)))
+
+    def attention(self, qkv, seq_off, seq_len, B, max_len, heads, head_dim, ctx, stream=None):
+        _check(lib().nebw_attention(self.h, _addr(qkv), _addr(seq_off), _addr(seq_len), B,
+                                    max_len, heads, head_dim, _addr(ctx), _stream(stream)))
+
+    def pack_offsets(self, len_in, B, S, len_out, seq_off, stream=None):
+        _check(lib().nebw_pack_offsets(self.h, _addr(len_in), B, S, _addr(len_out),
+                                       _addr(seq_off), _stream(stream)))
+
+    def embed_ln(self, ids, seq_off, seq_len, B, S, word, vocab, pos, typ, gamma, beta, H, x,
+                 a_bf16=None, eps=1e-12, stream=None):
+        _check(lib().nebw_embed_ln(self.h, _addr(ids), _addr(seq_off), _addr(seq_len), B, S,
+                                   _addr(word), vocab, _addr(pos), _addr(typ), _addr(gamma),
+                                   _addr(beta), eps, H, _addr(x), _addr(a_bf16), _stream(stream)))
+
+    def pool_l2(self, h, seq_off, seq_len, B, H, pooling, out, l2=True, stream=None):
+        _check(lib().nebw_pool_l2(self.h, _addr(h), _addr(seq_off), _addr(seq_len), B, H,
+                                  pooling, int(l2), _addr(out), _stream(stream)))
+
+    def narrow_bf16(self, x, n, y, stream=None):
+        _check(lib().nebw_narrow_bf16(self.h, _addr(x), n, _addr(y), _stream(stream)))
+
+
+class Model:
+    """A staged BERT encoder on one Device (nebw_model)."""
+
+    def __init__(self, dev: Device, handle):
+        self.dev = dev
+        self.h = handle
+        cfg = Config()
+        _check(lib().nebw_model_get_config(self.h, C.byref(cfg)))
+        self.cfg = cfg
+
+    @classmethod
+    def from_weights(cls, dev: Device, w, max_seq_len: int = 512, activation: int = ACT_GELU8):
+        """Stage a nebw.synth.BertWeights (container layout) on `dev`."""
+        cfg = Config(num_layers=w.layers, hidden=w.hidden, num_heads=w.heads,
+                     head_dim=w.head_dim, intermediate=w.ffn, vocab_size=w.vocab,
+                     max_seq_len=max_seq_len, type_vocab_size=w.typ.shape[0],
+                     pooling=POOL_CLS if w.cls_pool else POOL_MEAN, l2_normalize=1,
+                     activation=ACT_GELU_ERF if getattr(w, "gelu_erf", False) else activation,
+                     layer_norm_eps=1e-12)
+        h = C.c_void_p()
+        _check(lib().nebw_model_create(dev.h, C.byref(cfg), C.byref(h)))
+        m = cls(dev, h)
+        try:
+            for name, arr in w.tensors():
+                a = np.ascontiguousarray(arr, np.float32)
+                rows, cols = (a.shape[0], a.shape[1]) if a.ndim == 2 else (1, a.shape[0])
+                if name == "embeddings.position":
+                    a = np.ascontiguousarray(a[:max_seq_len])
+                    rows = a.shape[0]
+                _check(lib().nebw_model_set_tensor(m.h, name.encode(), a.ctypes.data, F32, rows,
+                                                   cols))
+        except Exception:
+            m.close()
+            raise
+        return m
+
+    @classmethod
+    def from_npue(cls, dev: Device, path):
+        h = C.c_void_p()
+        _check(lib().nebw_model_load_npue(dev.h, str(path).encode(), C.byref(h)))
+        return cls(dev, h)
+
+    def close(self):
+        if self.h:
+            lib().nebw_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def hidden(self) -> int:
+        return self.cfg.hidden
+
+    def launch_count(self) -> int:
+        return lib().nebw_encode_launch_count(self.h)
+
+    def encode(self, ids: np.ndarray, lens: np.ndarray) -> np.ndarray:
+        """Host in, host out: ids [B, S] int32, lens [B] int32 -> [B, hidden]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        lens = np.ascontiguousarray(lens, np.int32)
+        B, S = ids.shape
+        out = np.empty((B, self.hidden), np.float32)
+        _check(lib().nebw_encode(self.h, ids.ctypes.data, lens.ctypes.data, B, S, out.ctypes.data))
+        return out
+
+    def encode_into(self, ids, lens, out, B: int, S: int, host=False, stream=None):
+        """Host or device buffers by address; the device form is asynchronous."""
+        if host:
+            _check(lib().nebw_encode(self.h, _addr(ids), _addr(lens), B, S, _addr(out)))
+        else:
+            _check(lib().nebw_encode_device(self.h, _addr(ids), _addr(lens), B, S, _addr(out),
+                                            _stream(stream)))

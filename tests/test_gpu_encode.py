@@ -1,0 +1,120 @@
+"""Whole-encoder parity on a B200: the CUDA path, called through the C ABI,
+against the CPU oracle on the same seeded weights and tokens.
+
+Gate (the north star's): per row cosine >= 0.9999 and max-abs <= 2e-3 after
+L2 normalisation; NaN or Inf fails explicitly.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import parity
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAX_ABS = 2e-3
+
+
+def check(got, want, what):
+    assert np.isfinite(got).all(), f"{what}: non-finite embedding"
+    cos, err = parity(got, want)
+    assert cos >= COS_MIN and err <= MAX_ABS, f"{what}: min cos {cos:.7f}, max abs {err:.3e}"
+    return cos, err
+
+
+@pytest.fixture(scope="module")
+def minilm():
+    from nebw import synth
+    cfg = synth.CONFIGS["minilm"]
+    return cfg, synth.config_weights(cfg)
+
+
+def test_minilm_full_batch_vs_oracle(device, port_oracle, minilm):
+    """BASELINE config 1 in full: 32 x 128, 6 layers, mean pooling."""
+    import nebw
+    from nebw import synth
+    cfg, w = minilm
+    ids, mask, lens = synth.config_batch(cfg)
+    m = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)
+    got = m.encode(ids, lens)
+    want = port_oracle.encode(w, ids, mask)
+    check(got, want, "minilm")
+    m.close()
+
+
+def test_ragged_edges_vs_oracle(device, port_oracle, minilm):
+    """Lengths at the edges: 1 (CLS only), 2, the 64-key tile edges, seq."""
+    import nebw
+    from nebw import synth
+    cfg, w = minilm
+    lens = np.array([1, 2, 8, 63, 64, 65, 127, 128], np.int32)
+    ids, mask = synth.make_tokens(len(lens), cfg.seq, lens, seed=77)
+    m = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)
+    got = m.encode(ids, lens)
+    want = port_oracle.encode(w, ids, mask)
+    check(got, want, "ragged")
+    m.close()
+
+
+def test_cls_pooling_and_erf_variant(device, port_oracle):
+    """CLS pooling (bge configs) and the exact-erf GELU variant."""
+    import nebw
+    from nebw import synth
+    w = synth.make_weights(synth.BGE_SMALL, seed=5, cls_pool=True, layers=3, gelu_erf=True)
+    lens = np.array([16, 100, 256, 33], np.int32)
+    ids, mask = synth.make_tokens(len(lens), 256, lens, seed=6)
+    m = nebw.Model.from_weights(device, w, max_seq_len=256)
+    got = m.encode(ids, lens)
+    want = port_oracle.encode(w, ids, mask)
+    check(got, want, "cls+erf")
+    m.close()
+
+
+def test_bge_base_geometry_vs_oracle(device, port_oracle):
+    """hidden 768 / head_dim 64 geometry, 2 layers, full-length rows."""
+    import nebw
+    from nebw import synth
+    w = synth.make_weights(synth.BGE_BASE, seed=9, cls_pool=True, layers=2)
+    lens = np.array([512, 300, 8], np.int32)
+    ids, mask = synth.make_tokens(len(lens), 512, lens, seed=10)
+    m = nebw.Model.from_weights(device, w, max_seq_len=512)
+    got = m.encode(ids, lens)
+    want = port_oracle.encode(w, ids, mask)
+    check(got, want, "bge-base-2L")
+    m.close()
+
+
+def test_npue_container_roundtrip(device, port_oracle, minilm, tmp_path):
+    """The same model staged from a .npue container (the reference's file
+    format) encodes identically to the in-memory staging."""
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    cfg, w = minilm
+    path = tmp_path / "m.npue"
+    write_bert_container(path, w, max_seq_len=cfg.seq)
+    ids, mask, lens = synth.config_batch(cfg)
+    a = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)
+    b = nebw.Model.from_npue(device, path)
+    np.testing.assert_array_equal(a.encode(ids, lens), b.encode(ids, lens))
+    a.close()
+    b.close()
+
+
+def test_deterministic_and_batch_independent(device, minilm):
+    """Rows are computed independently: a row's embedding is bit-identical
+    whether it is encoded in the full batch, alone, or in a shuffled batch,
+    and repeated runs are bit-identical."""
+    import nebw
+    from nebw import synth
+    cfg, w = minilm
+    ids, mask, lens = synth.config_batch(cfg)
+    m = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)
+    full = m.encode(ids, lens)
+    np.testing.assert_array_equal(full, m.encode(ids, lens))
+    perm = np.random.default_rng(0).permutation(len(lens))
+    np.testing.assert_array_equal(full[perm], m.encode(ids[perm], lens[perm]))
+    for r in (0, 5, 31):
+        np.testing.assert_array_equal(full[r:r + 1], m.encode(ids[r:r + 1], lens[r:r + 1]))
+    m.close()
