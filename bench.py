@@ -1,0 +1,488 @@
+#!/usr/bin/env python
+"""Benchmark: embeddings/s of the BERT-encoder hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config bge-large]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+    python bench.py --impl reference ...     # the reference's own CPU path
+
+Workload: bge-large architecture (24 layers, hidden
+1024, 16 heads, FFN 4096), random-init N(0, 0.02), a batch of 1024 sequences
+padded to 512 with log-normal lengths (median 96, sigma 0.8, clipped to
+[8, 512]), CLS pooling + L2.  One step = one encoder pass over the whole
+batch.  At N GPUs the batch is sharded by a length-balanced plan (one weight
+replica per GPU, no collective on the data path) and the [1024, 1024] fp32
+embeddings are gathered to rank 0 with NCCL; the total batch is fixed, so
+scaling is strong.
+
+Reported, on one JSON line from rank 0:
+  value       embeddings/s with inputs resident in HBM (CUDA events on the
+              launching stream, max over ranks)
+  e2e         the same through the public C ABI with host buffers: H2D of the
+              ids and lengths, the pass, the gather, D2H of the embeddings
+  roofline    the GEMM family (tcgen05 kernel): algorithmic FLOPs / measured
+              device time per launch, against MEASURED_PEAKS.json
+  kernels     per-kernel-kind device time, share and roofline
+  cpu_baseline  the reference's own host-CPU path (oracle/_ref, built from
+              the reference tree) -- or the oracle port where it is absent --
+              on a bounded sample of the same batch, on this host's cores
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "npu-embeddings-xdna1_b200"
+sys.path.insert(0, str(PKG))
+sys.path.insert(0, str(REPO))
+
+from nebw import synth  # noqa: E402
+
+METRIC = "embeddings/sec at bge-large seq512"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+PROFILE_TRAFFIC = REPO / "profiles" / "traffic.json"
+
+
+# ---------------------------------------------------------------------------
+# workload arithmetic
+# ---------------------------------------------------------------------------
+
+def gemm_flops_per_token(a: synth.Arch) -> float:
+    H, F = a.hidden, a.ffn
+    return 2.0 * a.layers * (3 * H * H + H * H + H * F + F * H)
+
+
+def attn_flops(a: synth.Arch, lens) -> float:
+    lens = np.asarray(lens, np.float64)
+    return float(a.layers * 4.0 * (lens ** 2).sum() * a.hidden)
+
+
+def seq_flops(a: synth.Arch, lens) -> np.ndarray:
+    lens = np.asarray(lens, np.float64)
+    return gemm_flops_per_token(a) * lens + a.layers * 4.0 * lens ** 2 * a.hidden
+
+
+def plan_shards(lens, n: int):
+    """Length-balanced shard plan: sequences in decreasing FLOPs order, each
+    to the rank with the least work so far (ties to the lowest rank).
+    Returns n sorted index arrays that partition range(len(lens))."""
+    lens = np.asarray(lens)
+    if n == 1:
+        return [np.arange(len(lens))]
+    cost = 1.0 * lens + lens.astype(np.float64) ** 2 / 2048.0  # any monotone FLOPs proxy
+    order = np.argsort(-cost, kind="stable")
+    load = np.zeros(n)
+    owner = np.empty(len(lens), np.int64)
+    for i in order:
+        r = int(np.argmin(load))
+        owner[i] = r
+        load[r] += cost[i]
+    return [np.nonzero(owner == r)[0] for r in range(n)]
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {k: float(d[k]) for k in FALLBACK_PEAKS if k in d}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.rows = []
+        self.proc = None
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.t:
+            self.t.join(timeout=5)
+
+    def summary(self):
+        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.gpus]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "power_w_max": max(pw) if pw else None, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# the CPU arms
+# ---------------------------------------------------------------------------
+
+def cpu_reference_setup(cfg: synth.Config, w, workdir):
+    """(runner, kind, threads): runner(ids, mask) -> embeddings."""
+    from oracle.oracle import REF_LIB, PortOracle, RefOracle, host_threads
+    threads = host_threads()
+    if REF_LIB.exists():
+        from nebw.npue import write_bert_container
+        path = Path(workdir) / "bench_ref.npue"
+        write_bert_container(path, w, max_seq_len=cfg.seq)
+        sess = RefOracle().session(path, cfg.seq, threads)
+        return (lambda ids, mask: sess.run(ids, mask, w.hidden)), "reference", threads
+    port = PortOracle()
+    return (lambda ids, mask: port.encode(w, ids, mask, threads=threads)), "port", threads
+
+
+def pick_sample(lens, n):
+    """n row indices spread over the batch, including the longest and the
+    shortest row (the host path pads every row to seq, so cost is flat)."""
+    idx = {int(np.argmax(lens)), int(np.argmin(lens))}
+    for i in np.linspace(0, len(lens) - 1, num=max(n, 2)).astype(int):
+        if len(idx) >= n:
+            break
+        idx.add(int(i))
+    return np.array(sorted(idx))[:n]
+
+
+def run_cpu_baseline(cfg, w, ids, mask, lens, budget_s=15.0):
+    with tempfile.TemporaryDirectory() as td:
+        run, kind, threads = cpu_reference_setup(cfg, w, td)
+        first = pick_sample(lens, 1)
+        t0 = time.perf_counter()
+        run(ids[first], mask[first])  # warm: builds the reference's weight cache
+        t1 = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        run(ids[first], mask[first])
+        per_seq = time.perf_counter() - t0
+        n = int(max(1, min(32, budget_s // max(per_seq, 1e-3))))
+        n = int(min(32, max(n, -(-threads * 8 // cfg.seq))))  # occupy every host thread
+        sample = pick_sample(lens, n)
+        t0 = time.perf_counter()
+        run(ids[sample], mask[sample])
+        el = time.perf_counter() - t0 + per_seq
+        n_total = len(sample) + 1
+    return {"value": n_total / el, "unit": "embeddings/s", "cores": threads, "kind": kind,
+            "sample": f"{n_total} sequences of the {cfg.batch}-row batch, each padded to "
+                      f"seq {cfg.seq} as the reference pads every request; "
+                      f"{el:.1f} s timed after a {t1:.1f} s warm-up",
+            "full_batch_s_extrapolated": cfg.batch * el / n_total}
+
+
+def reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    w = synth.config_weights(cfg)
+    ids, mask, lens = synth.config_batch(cfg)
+    with tempfile.TemporaryDirectory() as td:
+        run, kind, threads = cpu_reference_setup(cfg, w, td)
+        # enough rows per step to occupy every host thread: the reference
+        # parallelises its GEMMs over 8-row blocks (conv_host.hpp:154-160)
+        per_step = int(max(1, min(cfg.batch, -(-threads * 8 // cfg.seq))))
+        order = pick_sample(lens, min(len(lens), per_step * (args.warmup + args.steps)))
+
+        def rows(i):
+            return np.array([order[(i * per_step + k) % len(order)] for k in range(per_step)])
+
+        for i in range(args.warmup):
+            r = rows(i)
+            run(ids[r], mask[r])
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            r = rows(args.warmup + i)
+            run(ids[r], mask[r])
+        el = time.perf_counter() - t0
+    value = args.steps * per_step / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "embeddings/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg.key}: batch {cfg.batch} x seq {cfg.seq}, "
+                               f"{cfg.arch.layers}L/{cfg.arch.hidden}H, lengths {cfg.lengths}",
+                   "global_batch": cfg.batch, "seq_len": cfg.seq, "parallelism": "host threads",
+                   "step": f"{per_step} sequence(s) of the batch per step (bounded sample)"},
+        "cpu_baseline": {"value": value, "unit": "embeddings/s", "cores": threads, "kind": kind,
+                         "sample": f"{args.warmup} warm + {args.steps} timed steps of "
+                                   f"{per_step} sequence(s) of the batch, padded to {cfg.seq}"},
+        "e2e": {"value": value, "unit": "embeddings/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# the GPU arm
+# ---------------------------------------------------------------------------
+
+def gpu_arm(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    import nebw
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    arch = cfg.arch
+    w = synth.config_weights(cfg)
+    ids, mask, lens = synth.config_batch(cfg)
+    B, S, H = cfg.batch, cfg.seq, arch.hidden
+    shards = plan_shards(lens, world)
+    mine = shards[rank]
+    b_r = len(mine)
+    max_b = max(len(s) for s in shards)
+    T_r = int(lens[mine].sum())
+
+    dev = nebw.Device(local)
+    model = nebw.Model.from_weights(dev, w, max_seq_len=S)
+    launches_per_step = model.launch_count()
+    stream = torch.cuda.current_stream()
+
+    ids_h = torch.from_numpy(np.ascontiguousarray(ids[mine])).pin_memory()
+    lens_h = torch.from_numpy(np.ascontiguousarray(lens[mine])).pin_memory()
+    ids_d = ids_h.cuda()
+    lens_d = lens_h.cuda()
+    out_d = torch.zeros((max_b, H), dtype=torch.float32, device="cuda")
+    gather_d = torch.zeros((world * max_b, H), dtype=torch.float32, device="cuda") if rank == 0 else None
+    gather_list = list(gather_d.chunk(world)) if rank == 0 else None
+    out_h = torch.empty((world * max_b if world > 1 else b_r, H), dtype=torch.float32).pin_memory()
+
+    def step():
+        model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
+        if world > 1:
+            dist.gather(out_d, gather_list, dst=0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident throughput --------------------------------------
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.6)
+    model.profile(True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    if sampler:
+        sampler.stop()
+    model.profile(False)
+    prof = model.profile_collect()
+    ms = e0.elapsed_time(e1)
+    dev.sync()
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---- end to end through the public API with host buffers ------------
+    def step_e2e():
+        if world == 1:
+            model.encode_into(ids_h, lens_h, out_h, b_r, S, host=True)  # nebw_encode: H2D, pass, D2H
+            return out_h.numpy()
+        ids_d.copy_(ids_h, non_blocking=True)
+        lens_d.copy_(lens_h, non_blocking=True)
+        model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
+        dist.gather(out_d, gather_list, dst=0)
+        if rank == 0:
+            out_h.copy_(gather_d, non_blocking=True)
+        stream.synchronize()
+        if rank != 0:
+            return None
+        full = np.empty((B, H), np.float32)
+        g = out_h.numpy()
+        for r, idx in enumerate(shards):
+            full[idx] = g[r * max_b:r * max_b + len(idx)]
+        return full
+
+    for _ in range(max(1, args.warmup)):
+        res = step_e2e()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        res = step_e2e()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t.item())
+
+    # per-rank profile -> the slowest rank's numbers are the ones reported
+    prof_t = torch.tensor([[prof[k][1] for k in model.KERNEL_KINDS]], dtype=torch.float64,
+                          device="cuda")
+    tok_t = torch.tensor([float(T_r), float((lens[mine].astype(np.float64) ** 2).sum())],
+                         dtype=torch.float64, device="cuda")
+    if world > 1:
+        all_prof = [torch.zeros_like(prof_t) for _ in range(world)]
+        all_tok = [torch.zeros_like(tok_t) for _ in range(world)]
+        dist.all_gather(all_prof, prof_t)
+        dist.all_gather(all_tok, tok_t)
+    else:
+        all_prof, all_tok = [prof_t], [tok_t]
+
+    ok = res is not None and bool(np.isfinite(res).all()) if rank == 0 else True
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu_baseline(cfg, w, ids, mask, lens)
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        slow = int(np.argmax([p.sum().item() for p in all_prof]))
+        pms = dict(zip(model.KERNEL_KINDS, all_prof[slow][0].tolist()))
+        T_s, L2_s = all_tok[slow].tolist()
+        steps = args.steps
+        Hf, F, L = float(H), float(arch.ffn), arch.layers
+        gemm_fl = {"gemm_qkv": 2 * T_s * Hf * 3 * Hf * L, "gemm_ao": 2 * T_s * Hf * Hf * L,
+                   "gemm_up": 2 * T_s * Hf * F * L, "gemm_down": 2 * T_s * F * Hf * L}
+        gemm_ms = sum(pms[k] for k in gemm_fl) / steps
+        gemm_tflops = sum(gemm_fl.values()) / (gemm_ms / 1e3) / 1e12
+        peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        total_prof_ms = sum(pms.values()) / steps
+        kernels = {}
+        for k in model.KERNEL_KINDS:
+            kernels[k] = {"ms_per_step": pms[k] / steps,
+                          "share": pms[k] / steps / total_prof_ms if total_prof_ms else None}
+        for k, fl in gemm_fl.items():
+            kernels[k]["tflops"] = fl / (pms[k] / steps / 1e3) / 1e12
+            kernels[k]["frac_of_peak"] = kernels[k]["tflops"] / peak_t
+        att_fl = 4.0 * L2_s * Hf * L
+        kernels["attention"]["tflops"] = att_fl / (pms["attention"] / steps / 1e3) / 1e12
+        kernels["attention"]["frac_of_peak"] = kernels["attention"]["tflops"] / peak_t
+        ln_bytes = T_s * Hf * (4 + 4 + 2) * 2 * L  # read x, write x + bf16 copy; 2 per layer
+        kernels["layernorm"]["gbs"] = ln_bytes / (pms["layernorm"] / steps / 1e3) / 1e9
+        kernels["layernorm"]["frac_of_peak"] = kernels["layernorm"]["gbs"] / peaks["hbm_gbs"]
+        traffic = None
+        if PROFILE_TRAFFIC.exists():
+            tr = json.loads(PROFILE_TRAFFIC.read_text())
+            traffic = tr.get("gemm_bytes_per_launch_scaled")
+        n_gemm_launches = 4 * L * steps
+        value = B * steps / (ms_max / 1e3)
+        e2e = B * steps / e2e_s
+        all_flops = float(seq_flops(arch, lens).sum())
+        line = {
+            "metric": METRIC, "value": value, "unit": "embeddings/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": ms_max / steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"{cfg.key}: {arch.name} architecture ({arch.layers}L, hidden "
+                                   f"{arch.hidden}, {arch.heads} heads, FFN {arch.ffn}), random-init "
+                                   f"N(0,0.02); batch {B} x seq {S}, lengths {cfg.lengths} "
+                                   f"clipped [8,{S}]; CLS pooling + L2",
+                       "global_batch": B, "seq_len": S, "real_tokens": int(lens.sum()),
+                       "parallelism": f"dp{world} (length-balanced shards, NCCL gather to rank 0)"
+                       if world > 1 else "single GPU",
+                       "l2": "no flush: every step streams the 0.6 GB bf16 weights and GBs of "
+                             "activations, far above the 126 MB L2"},
+            "e2e": {"value": e2e, "unit": "embeddings/s",
+                    "h2d_bytes_per_step": int(B * S * 4 + B * 4),
+                    "d2h_bytes_per_step": int(B * H * 4) if world == 1 else int(world * max_b * H * 4),
+                    "timer": "wall clock, synchronous per step, max over ranks"},
+            "gpu_launches": int(launches_per_step * steps * world),
+            "roofline": {"kernel": "gemm_tc (tcgen05 QKV/AO/UP/DOWN, launch-weighted)",
+                         "bound": "tensor", "achieved": gemm_tflops, "peak": peak_t,
+                         "unit": "TFLOP/s", "frac": gemm_tflops / peak_t,
+                         "peak_source": f"{peak_src} bf16 dense (sustained)",
+                         "traffic": traffic,
+                         "launches": n_gemm_launches,
+                         "flops_per_step": sum(gemm_fl.values())},
+            "end_to_end_frac": {"real_token_tflops": all_flops / (ms_max / steps / 1e3) / 1e12,
+                                "frac": all_flops / (ms_max / steps / 1e3) / 1e12 / peak_t,
+                                "padded_equivalent_tflops": float(seq_flops(arch, np.full(B, S)).sum())
+                                / (ms_max / steps / 1e3) / 1e12},
+            "kernels": kernels,
+            "outputs_finite": ok,
+        }
+        if sampler:
+            line["clocks"] = sampler.summary()
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+    model.close()
+    dev.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["nebw", "reference"], default="nebw")
+    ap.add_argument("--config", default="bge-large", choices=sorted(synth.CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    cfg = synth.CONFIGS[args.config]
+    if args.impl == "reference":
+        return reference_arm(args, cfg)
+    return gpu_arm(args, cfg)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

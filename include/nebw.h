@@ -198,6 +198,21 @@ int nebw_encode_device(nebw_model *m, const int32_t *ids_dev, const int32_t *len
  * (for launch accounting). */
 int nebw_encode_launch_count(const nebw_model *m);
 
+/* ---- per-kernel timing (the reference's BertEncoder::Timings,
+ * bert_encoder.hpp:67-87, measured on the device) ------------------------
+ * While enabled, every encoder pass brackets each kernel launch with CUDA
+ * events on the launching stream.  nebw_model_profile_collect synchronises,
+ * and returns, per kernel kind, the number of launches and their summed
+ * device time since the last collect. */
+enum {
+  NEBW_K_PACK = 0, NEBW_K_EMBED_LN = 1, NEBW_K_GEMM_QKV = 2, NEBW_K_ATTENTION = 3,
+  NEBW_K_GEMM_AO = 4, NEBW_K_LN = 5, NEBW_K_GEMM_UP = 6, NEBW_K_GEMM_DOWN = 7,
+  NEBW_K_POOL = 8, NEBW_K_COUNT = 9
+};
+int nebw_model_profile(nebw_model *m, int enable);
+int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K_COUNT],
+                               double ms[NEBW_K_COUNT]);
+
 #ifdef __cplusplus
 }
 #endif

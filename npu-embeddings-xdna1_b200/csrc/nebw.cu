@@ -606,6 +606,12 @@ struct nebw_model {
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
   float *out = nullptr;
   CUtensorMap map_a, map_ctx, map_h;
+  // per-kernel timing: one event before each launch (tagged with the kernel
+  // kind) and one after the last; interval i belongs to marks[i].kind
+  bool prof = false;
+  std::vector<std::pair<cudaEvent_t, int>> marks;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
 };
 
 namespace {
@@ -694,6 +700,19 @@ int model_ready(const nebw_model *m) {
   return NEBW_OK;
 }
 
+int prof_mark(nebw_model *m, int kind, cudaStream_t st) {
+  if (!m->prof) return NEBW_OK;
+  if (m->ev_used == m->ev_pool.size()) {
+    cudaEvent_t e;
+    NEBW_CUDA(cudaEventCreate(&e));
+    m->ev_pool.push_back(e);
+  }
+  cudaEvent_t e = m->ev_pool[m->ev_used++];
+  NEBW_CUDA(cudaEventRecord(e, st));
+  m->marks.emplace_back(e, kind);
+  return NEBW_OK;
+}
+
 int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S, float *out,
                   cudaStream_t st) {
   nebw_dev *d = m->dev;
@@ -707,7 +726,9 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   const int rows = static_cast<int>(static_cast<int64_t>(B) * S);
   const int *T_dev = m->off + B;
   int rc;
+  if ((rc = prof_mark(m, NEBW_K_PACK, st))) return rc;
   if ((rc = launch_pack(len_in, B, S, m->len, m->off, d->d_err, st))) return rc;
+  if ((rc = prof_mark(m, NEBW_K_EMBED_LN, st))) return rc;
   if ((rc = launch_embed_ln(ids, B, S, m->off, m->len, m->word, c.vocab_size, m->pos, m->typ,
                             m->emb_g, m->emb_b, c.layer_norm_eps, c.hidden, m->x, m->a, d->d_err,
                             st)))
@@ -725,8 +746,10 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.bias = w.b_qkv;
     a.resid = nullptr;
     a.out = m->qkv;
+    if ((rc = prof_mark(m, NEBW_K_GEMM_QKV, st))) return rc;
     if ((rc = launch_gemm(d, w.qkv, m->map_a, nebw::kEpiBf16, a, st))) return rc;
     // attention
+    if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if ((rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st)))
       return rc;
     // attention-out + bias + residual (fp32, in place)
@@ -735,7 +758,9 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.bias = w.b_ao;
     a.resid = m->x;
     a.out = m->x;
+    if ((rc = prof_mark(m, NEBW_K_GEMM_AO, st))) return rc;
     if ((rc = launch_gemm(d, w.ao, m->map_ctx, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
     if ((rc = launch_layernorm(m->x, nullptr, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
                                m->a, st)))
       return rc;
@@ -745,6 +770,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.bias = w.b_up;
     a.resid = nullptr;
     a.out = m->h;
+    if ((rc = prof_mark(m, NEBW_K_GEMM_UP, st))) return rc;
     if ((rc = launch_gemm(d, w.up, m->map_a, up_epi, a, st))) return rc;
     // FFN down + bias + residual (fp32, in place)
     a.N = static_cast<int>(H);
@@ -752,12 +778,17 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.bias = w.b_dn;
     a.resid = m->x;
     a.out = m->x;
+    if ((rc = prof_mark(m, NEBW_K_GEMM_DOWN, st))) return rc;
     if ((rc = launch_gemm(d, w.dn, m->map_h, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
     if ((rc = launch_layernorm(m->x, nullptr, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
                                L + 1 < c.num_layers ? m->a : nullptr, st)))
       return rc;
   }
-  return launch_pool(m->x, m->off, m->len, B, c.hidden, c.pooling, c.l2_normalize, out, st);
+  if ((rc = prof_mark(m, NEBW_K_POOL, st))) return rc;
+  if ((rc = launch_pool(m->x, m->off, m->len, B, c.hidden, c.pooling, c.l2_normalize, out, st)))
+    return rc;
+  return prof_mark(m, -1, st);
 }
 
 }  // namespace
@@ -865,6 +896,7 @@ extern "C" int nebw_model_destroy(nebw_model *m) {
   cudaSetDevice(m->dev->device);
   cudaStreamSynchronize(m->dev->stream);
   free_workspace(m);
+  for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
   for (float *p : {m->word, m->pos, m->typ, m->emb_g, m->emb_b}) cudaFree(p);
   for (auto &w : m->layers) {
     for (Weight *x : {&w.qkv, &w.ao, &w.up, &w.dn}) cudaFree(x->ptr);
@@ -969,4 +1001,32 @@ extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *len
 extern "C" int nebw_encode_launch_count(const nebw_model *m) {
   if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
   return 3 + 7 * m->cfg.num_layers;
+}
+
+extern "C" int nebw_model_profile(nebw_model *m, int enable) {
+  NEBW_REQUIRE(m != nullptr, "null model");
+  m->prof = enable != 0;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K_COUNT],
+                                          double ms[NEBW_K_COUNT]) {
+  NEBW_REQUIRE(m && launches && ms, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  for (int k = 0; k < NEBW_K_COUNT; ++k) {
+    launches[k] = 0;
+    ms[k] = 0.0;
+  }
+  for (size_t i = 0; i + 1 < m->marks.size(); ++i) {
+    const int kind = m->marks[i].second;
+    if (kind < 0) continue;  // end of one pass -> start of the next
+    NEBW_CUDA(cudaEventSynchronize(m->marks[i + 1].first));
+    float t = 0.f;
+    NEBW_CUDA(cudaEventElapsedTime(&t, m->marks[i].first, m->marks[i + 1].first));
+    launches[kind] += 1;
+    ms[kind] += t;
+  }
+  m->marks.clear();
+  m->ev_used = 0;
+  return NEBW_OK;
 }

@@ -90,6 +90,8 @@ def lib() -> C.CDLL:
         "nebw_encode": ([vp, vp, vp, i32, i32, vp], C.c_int),
         "nebw_encode_device": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
         "nebw_encode_launch_count": ([vp], C.c_int),
+        "nebw_model_profile": ([vp, C.c_int], C.c_int),
+        "nebw_model_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -258,6 +260,20 @@ class Model:
 
     def launch_count(self) -> int:
         return lib().nebw_encode_launch_count(self.h)
+
+    KERNEL_KINDS = ("pack", "embed_ln", "gemm_qkv", "attention", "gemm_ao", "layernorm",
+                    "gemm_up", "gemm_down", "pool")
+
+    def profile(self, enable: bool = True):
+        _check(lib().nebw_model_profile(self.h, int(enable)))
+
+    def profile_collect(self) -> dict:
+        """{kind: (launches, device ms)} since the last collect."""
+        n = len(self.KERNEL_KINDS)
+        launches = (C.c_int64 * n)()
+        ms = (C.c_double * n)()
+        _check(lib().nebw_model_profile_collect(self.h, launches, ms))
+        return {k: (int(launches[i]), float(ms[i])) for i, k in enumerate(self.KERNEL_KINDS)}
 
     def encode(self, ids: np.ndarray, lens: np.ndarray) -> np.ndarray:
         """Host in, host out: ids [B, S] int32, lens [B] int32 -> [B, hidden]."""

@@ -1,0 +1,144 @@
+"""Single-kernel timing through the C ABI, for tuning and for profiler runs.
+
+    python -m nebw.kernel_bench gemm --M 16384 --K 1024 --N 4096 --epi gelu8
+    python -m nebw.kernel_bench attention --B 64 --len 512 --heads 16 --hd 64
+    python -m nebw.kernel_bench layernorm --M 131072 --H 1024
+
+(run with npu-embeddings-xdna1_b200/ on sys.path).  Each case runs a few
+warm-up launches and then times --iters launches with CUDA events on the
+launching stream, printing one JSON line with the per-launch time and the
+achieved TFLOP/s or GB/s.  Operand buffers are sized so that, across the
+rotation of --copies buffers, the working set exceeds the 126 MB L2.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+
+def _bits(a):
+    import torch
+    return torch.from_numpy(a.view(np.int16).copy()).cuda().view(torch.bfloat16)
+
+
+def bench_gemm(dev, M, K, N, epi, iters, copies):
+    import torch
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((K, N), np.float32) * 0.02).astype(np.float32)
+    h = dev.stage_weight(w)
+    bias = torch.randn(N, device="cuda")
+    As = [torch.randn(M, K, device="cuda").to(torch.bfloat16) for _ in range(copies)]
+    f32 = epi in ("f32", "resid")
+    Cs = [torch.empty(M, N, device="cuda", dtype=torch.float32 if f32 else torch.bfloat16)
+          for _ in range(copies)]
+    act = {"gelu8": 1, "erf": 2}.get(epi, 0)
+
+    def run(i):
+        c = Cs[i % copies]
+        dev.gemm(h, As[i % copies], M, K, N, c, bias=bias, residual=c if epi == "resid" else None,
+                 act=act, c_dtype=0 if f32 else 1, stream=torch.cuda.current_stream())
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    ms = e0.elapsed_time(e1) / iters
+    fl = 2.0 * M * N * K
+    return {"kernel": "gemm_tc", "M": M, "K": K, "N": N, "epi": epi, "ms": ms,
+            "tflops": fl / ms / 1e9}
+
+
+def bench_attention(dev, B, L, heads, hd, iters, copies):
+    import torch
+    H = heads * hd
+    lens = np.full(B, L, np.int32)
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(off[-1])
+    qkv = [(torch.randn(T, 3 * H, device="cuda") * 0.5).to(torch.bfloat16) for _ in range(copies)]
+    ctx = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    off_d = torch.from_numpy(off).cuda()
+    len_d = torch.from_numpy(lens).cuda()
+
+    def run(i):
+        dev.attention(qkv[i % copies], off_d, len_d, B, L, heads, hd, ctx,
+                      stream=torch.cuda.current_stream())
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    ms = e0.elapsed_time(e1) / iters
+    fl = 4.0 * B * L * L * H
+    return {"kernel": "attention", "B": B, "len": L, "heads": heads, "hd": hd, "ms": ms,
+            "tflops": fl / ms / 1e9}
+
+
+def bench_layernorm(dev, M, H, iters, copies):
+    import torch
+    xs = [torch.randn(M, H, device="cuda") for _ in range(copies)]
+    a = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    g = torch.ones(H, device="cuda")
+    b = torch.zeros(H, device="cuda")
+
+    def run(i):
+        dev.layernorm(xs[i % copies], g, b, M, H, a_bf16=a, stream=torch.cuda.current_stream())
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    ms = e0.elapsed_time(e1) / iters
+    by = M * H * (4 + 4 + 2)
+    return {"kernel": "layernorm", "M": M, "H": H, "ms": ms, "gbs": by / ms / 1e6}
+
+
+def main(argv=None):
+    import nebw
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=["gemm", "attention", "layernorm"])
+    ap.add_argument("--M", type=int, default=16384)
+    ap.add_argument("--K", type=int, default=1024)
+    ap.add_argument("--N", type=int, default=4096)
+    ap.add_argument("--H", type=int, default=1024)
+    ap.add_argument("--B", type=int, default=64)
+    ap.add_argument("--len", type=int, default=512)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--hd", type=int, default=64)
+    ap.add_argument("--epi", default="bf16", choices=["bf16", "gelu8", "erf", "f32", "resid"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--copies", type=int, default=2)
+    a = ap.parse_args(argv)
+    dev = nebw.Device(0)
+    if a.op == "gemm":
+        r = bench_gemm(dev, a.M, a.K, a.N, a.epi, a.iters, a.copies)
+    elif a.op == "attention":
+        r = bench_attention(dev, a.B, a.len, a.heads, a.hd, a.iters, a.copies)
+    else:
+        r = bench_layernorm(dev, a.M, a.H, a.iters, a.copies)
+    print(json.dumps(r), flush=True)
+    dev.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -173,6 +173,13 @@ class RefOracle:
         L.nebw_ref_pool_rows.argtypes = [_f32p, _f32p, C.c_int64, C.c_int64, C.c_int64, C.c_int32,
                                          C.c_int32, _f32p, C.c_char_p, C.c_int32]
         L.nebw_ref_pool_rows.restype = C.c_int
+        L.nebw_ref_session_open.argtypes = [C.c_char_p, C.c_int32, C.c_int32, C.c_char_p,
+                                            C.c_int32]
+        L.nebw_ref_session_open.restype = C.c_void_p
+        L.nebw_ref_session_run.argtypes = [C.c_void_p, _i32p, _i32p, C.c_int32, _f32p, C.c_char_p,
+                                           C.c_int32]
+        L.nebw_ref_session_run.restype = C.c_int
+        L.nebw_ref_session_close.argtypes = [C.c_void_p]
 
     def encode_container(self, path, seq, ids, mask, threads=None, hidden=False, hidden_size=None):
         ids = np.ascontiguousarray(ids, np.int32)
@@ -199,6 +206,10 @@ class RefOracle:
             path = Path(td) / "oracle.npue"
             write_bert_container(path, w, max_seq_len=max(S, 8))
             return self.encode_container(path, S, ids, mask, threads, hidden, w.hidden)
+
+    def session(self, path, seq, threads=None):
+        """A persistent reference encoder over a container (for timing)."""
+        return _RefSession(self.lib, path, seq, threads or host_threads())
 
     def gemm_nt(self, A, B, bias, threads=1):
         A = np.ascontiguousarray(A, np.float32)
@@ -238,3 +249,28 @@ class RefOracle:
         if rc:
             raise RuntimeError(err.value.decode())
         return out
+
+
+class _RefSession:
+    def __init__(self, lib, path, seq, threads):
+        self.lib, self.seq, self.threads = lib, seq, threads
+        err = C.create_string_buffer(4096)
+        self.h = lib.nebw_ref_session_open(str(path).encode(), seq, threads, err, 4096)
+        if not self.h:
+            raise RuntimeError(err.value.decode())
+
+    def run(self, ids, mask, hidden_size):
+        ids = np.ascontiguousarray(ids, np.int32)
+        mask = np.ascontiguousarray(mask, np.int32)
+        assert ids.shape[1] == self.seq
+        out = np.zeros((ids.shape[0], hidden_size), np.float32)
+        err = C.create_string_buffer(4096)
+        if self.lib.nebw_ref_session_run(self.h, _ptr(ids, _i32p), _ptr(mask, _i32p), ids.shape[0],
+                                         _ptr(out), err, 4096):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def close(self):
+        if self.h:
+            self.lib.nebw_ref_session_close(self.h)
+            self.h = None

@@ -98,6 +98,78 @@ int nebw_ref_encode(const char *npue_path, int32_t seq, const int32_t *ids,
   }
 }
 
+// A persistent reference encoder, for timing: the container is mapped, the
+// encoder constructed and its weights staged (stage_all; the first run()
+// also builds host_b.hpp's fp32 weight cache) once, and every
+// nebw_ref_session_run() is then the reference's steady-state per-request
+// work -- the gather, BertEncoder::run and pool_rows of EmbedService::chunk.
+struct RefSession {
+  npue::File file;
+  app::Pool pool;
+  npu::Device dev;
+  npu::Design design;
+  npue::BertEncoder enc;
+  int32_t seq;
+  RefSession(const char *path, int32_t s, int32_t threads)
+      : file(path), pool(threads > 0 ? threads : 1), design(dev, "oracle-host"),
+        enc(file, design, design, design, design, design, design, design, pool), seq(s) {}
+};
+
+void *nebw_ref_session_open(const char *npue_path, int32_t seq, int32_t threads, char *err,
+                            int32_t errlen) {
+  try {
+    // geometry globals first: the encoder's constructor and stage_all read them
+    {
+      npue::File probe(npue_path);
+      app::set_model_shape(probe);
+      app::set_design_seq(seq);
+    }
+    auto *s = new RefSession(npue_path, seq, threads);
+    s->enc.host_ln = s->enc.host_sm = s->enc.host_gelu = true;
+    s->enc.stage_all();
+    return s;
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return nullptr;
+  }
+}
+
+int nebw_ref_session_run(void *handle, const int32_t *ids, const int32_t *attn_mask,
+                         int32_t batch, float *out, char *err, int32_t errlen) {
+  try {
+    auto *s = static_cast<RefSession *>(handle);
+    const int64_t seq = s->seq, H = app::g_hidden;
+    s->enc.batch = batch;
+    s->enc.rows = static_cast<int64_t>(batch) * seq;
+    const float *w_word = s->file.raw("embeddings.word").as<float>();
+    const float *w_pos = s->file.raw("embeddings.position").as<float>();
+    const float *w_typ = s->file.raw("embeddings.token_type").as<float>();
+    std::vector<float> buf(static_cast<size_t>(batch) * seq * H, 0.f);
+    std::vector<float> cmask(static_cast<size_t>(batch) * seq, -1.0e30f);
+    std::vector<float> cam(static_cast<size_t>(batch) * seq, 0.f);
+    for (int64_t b = 0; b < batch; ++b)
+      for (int64_t t = 0; t < seq; ++t) {
+        const int32_t id = ids[b * seq + t];
+        const float m = static_cast<float>(attn_mask[b * seq + t]);
+        cam[b * seq + t] = m;
+        cmask[b * seq + t] = m > 0 ? 0.f : -1.0e30f;
+        float *dst = buf.data() + (b * seq + t) * H;
+        const float *wv = w_word + static_cast<size_t>(id) * H;
+        const float *pv = w_pos + static_cast<size_t>(t) * H;
+        for (int64_t c = 0; c < H; ++c) dst[c] = wv[c] + pv[c] + w_typ[c];
+      }
+    s->enc.add_mask = cmask;
+    std::vector<float> h = s->enc.run(buf);
+    app::pool_rows(h.data(), cam.data(), batch, out);
+    return 0;
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return 1;
+  }
+}
+
+void nebw_ref_session_close(void *handle) { delete static_cast<RefSession *>(handle); }
+
 // npue::hostconv::gemm_nt (runtime/include/common/conv_host.hpp:150-181):
 // C[M,N] = A[M,K] . B[K,N] + bias, fp32.
 int nebw_ref_gemm_nt(const float *A, int64_t M, const float *B, int64_t K,
