@@ -15,7 +15,8 @@
  *     README.md:2111-2140).
  *   - Pointers named *_dev / documented "device" are CUDA device pointers;
  *     "host" pointers are ordinary memory.  `stream` is a cudaStream_t passed
- *     as void* (NULL = the device handle's own stream).
+ *     as void*: NULL means the device handle's own stream, so a caller that
+ *     wants the legacy default stream passes cudaStreamLegacy ((void*)0x1).
  *   - One nebw_dev per GPU.  Calls on different nebw_dev handles may run
  *     concurrently from different host threads; calls on one handle must not
  *     overlap.  Staged weights are immutable after staging.

@@ -22,7 +22,8 @@
 //   warp 1      allocates TMEM, issues tcgen05.mma (M=128, N=BN, K=16) from
 //               one thread, commits each stage back to the producer and each
 //               finished tile to the epilogue
-//   warps 2-5   epilogue: tcgen05.ld the accumulator (one row per thread),
+//   warps 2-9   epilogue: tcgen05.ld the accumulator (one row per thread,
+//               two warps per 32-lane quarter, half the columns each),
 //               bias / activation / residual in fp32, store
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
@@ -59,7 +60,7 @@ struct GemmArgs {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // 2 control warps + 8 epilogue warps
 
 template <int BN>
 struct GemmShape {
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+      mbar_init(&tempty[a], 8);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -285,8 +286,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Two warps per TMEM lane quarter (a warp may only read lanes
+    // [32*(warp%4), +32)); each takes half of the tile's columns.  TMEM loads
+    // are double-buffered: chunk c+1 is in flight while chunk c is stored.
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / 32;
+    const int quarter = warp & 3;
+    const int col_half = ((warp - 2) >> 2) * kHalf;
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -298,18 +305,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int mb = tile / n_blocks, nb = tile % n_blocks;
       const int row = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_wait_ld();
-        const int col0 = nb * BN + c;
-        if (row < M && col0 < p.N) epi_store32<EPI>(p, row, col0, r);
+                             static_cast<uint32_t>(acc * BN + col_half);
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(t_row, ra);
+      tmem_wait_ld_regs(ra);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, nxt);
+        if (c + 1 == kChunks) {
+          // every TMEM read of this tile has completed: hand the buffer back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        const int col0 = nb * BN + col_half + c * 32;
+        if (row < M && col0 < p.N) epi_store32<EPI>(p, row, col0, cur);
+        if (c + 1 < kChunks) tmem_wait_ld_regs(nxt);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
 

@@ -9,11 +9,11 @@
 //   per layer L:
 //     gemm QKV     qkv = bf16(a . Wqkv + b)
 //     attention    ctx = softmax(Q K^T) V           (per sequence, per head)
-//     gemm AO      x   = (ctx . Wao + b) + x        (fp32 residual, in place)
-//     layernorm    x   = LN1(x);  a = bf16(x)
+//     gemm AO      y   = ctx . Wao + b               (fp32)
+//     layernorm    x   = LN1(y + x);  a = bf16(x)   (add_into + layer_norm)
 //     gemm UP      h   = bf16(gelu(a . Wup + b))
-//     gemm DOWN    x   = (h . Wdn + b) + x
-//     layernorm    x   = LN2(x);  a = bf16(x)
+//     gemm DOWN    y   = h . Wdn + b
+//     layernorm    x   = LN2(y + x);  a = bf16(x)
 //   pool_l2        out = normalise(pool(x))
 //
 // Nothing in a pass needs the host to know T: every kernel bounds itself by
@@ -601,7 +601,7 @@ struct nebw_model {
   std::map<std::string, bool> staged;  // container name -> set
   // workspace (capacity rows_cap = B * S of the largest call so far)
   int64_t rows_cap = 0, batch_cap = 0, ids_cap = 0;
-  float *x = nullptr;
+  float *x = nullptr, *y = nullptr;  // residual stream, sublayer output
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
   float *out = nullptr;
@@ -618,6 +618,7 @@ namespace {
 
 void free_workspace(nebw_model *m) {
   cudaFree(m->x);
+  cudaFree(m->y);
   cudaFree(m->a);
   cudaFree(m->qkv);
   cudaFree(m->ctx);
@@ -627,7 +628,7 @@ void free_workspace(nebw_model *m) {
   cudaFree(m->len);
   cudaFree(m->off);
   cudaFree(m->out);
-  m->x = nullptr;
+  m->x = m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
   m->ids = m->len_in = m->len = m->off = nullptr;
   m->out = nullptr;
@@ -650,6 +651,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   };
   int rc = 0;
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->x), R * H * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->y), R * H * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->a), R * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->qkv), R * 3 * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ctx), R * H * 2);
@@ -756,12 +758,12 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(H);
     a.bias = w.b_ao;
-    a.resid = m->x;
-    a.out = m->x;
+    a.resid = nullptr;
+    a.out = m->y;
     if ((rc = prof_mark(m, NEBW_K_GEMM_AO, st))) return rc;
-    if ((rc = launch_gemm(d, w.ao, m->map_ctx, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.ao, m->map_ctx, nebw::kEpiF32, a, st))) return rc;
     if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
-    if ((rc = launch_layernorm(m->x, nullptr, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
+    if ((rc = launch_layernorm(m->x, m->y, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
                                m->a, st)))
       return rc;
     // FFN up + bias + GELU -> bf16
@@ -776,12 +778,12 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(F);
     a.bias = w.b_dn;
-    a.resid = m->x;
-    a.out = m->x;
+    a.resid = nullptr;
+    a.out = m->y;
     if ((rc = prof_mark(m, NEBW_K_GEMM_DOWN, st))) return rc;
-    if ((rc = launch_gemm(d, w.dn, m->map_h, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.dn, m->map_h, nebw::kEpiF32, a, st))) return rc;
     if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
-    if ((rc = launch_layernorm(m->x, nullptr, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
+    if ((rc = launch_layernorm(m->x, m->y, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
                                L + 1 < c.num_layers ? m->a : nullptr, st)))
       return rc;
   }

@@ -119,23 +119,39 @@ def _addr(x):
     raise TypeError(f"cannot take the address of {type(x)}")
 
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream's handle
+
+
 def _stream(s):
+    """cudaStream_t for the C ABI.  None -> the library's own stream (NULL);
+    a torch stream -> its handle, with torch's legacy default stream (handle
+    0) passed as cudaStreamLegacy so that it is not read as NULL."""
     if s is None:
         return None
-    if isinstance(s, int):
-        return s
-    return s.cuda_stream  # torch.cuda.Stream
+    h = s if isinstance(s, int) else s.cuda_stream
+    return h if h != 0 else CUDA_STREAM_LEGACY
 
 
 class Device:
     """One GPU (nebw_dev)."""
 
-    def __init__(self, index: int = 0):
+    def __init__(self, index: int = 0, torch_stream: bool = False):
+        """torch_stream: op calls that name no stream run on torch's current
+        stream (so they are ordered with the torch ops that made their
+        buffers) instead of on the handle's own stream."""
         h = C.c_void_p()
         _check(lib().nebw_open(index, C.byref(h)))
         self.h = h
         self.index = index
-        self._weights = {}
+        self.torch_stream = torch_stream
+
+    def _s(self, stream):
+        if stream is not None:
+            return _stream(stream)
+        if self.torch_stream:
+            import torch
+            return _stream(torch.cuda.current_stream())
+        return None
 
     def close(self):
         if self.h:
@@ -149,6 +165,9 @@ class Device:
             pass
 
     def sync(self):
+        if self.torch_stream:
+            import torch
+            torch.cuda.current_stream().synchronize()
         _check(lib().nebw_sync(self.h))
 
     def info(self):
@@ -173,32 +192,32 @@ class Device:
     def gemm(self, weight, A, M, K, N, C_out, bias=None, residual=None, act=ACT_NONE,
              c_dtype=BF16, stream=None):
         _check(lib().nebw_gemm(self.h, weight, _addr(A), M, K, N, _addr(bias), _addr(residual),
-                               act, _addr(C_out), c_dtype, _stream(stream)))
+                               act, _addr(C_out), c_dtype, self._s(stream)))
 
     def layernorm(self, x, gamma, beta, rows, H, y=None, a_bf16=None, eps=1e-12, stream=None):
         _check(lib().nebw_layernorm(self.h, _addr(x), _addr(y), _addr(gamma), _addr(beta), eps,
-                                    rows, H, _addr(a_bf16), _stream(stream)))
+                                    rows, H, _addr(a_bf16), self._s(stream)))
 
     def attention(self, qkv, seq_off, seq_len, B, max_len, heads, head_dim, ctx, stream=None):
         _check(lib().nebw_attention(self.h, _addr(qkv), _addr(seq_off), _addr(seq_len), B,
-                                    max_len, heads, head_dim, _addr(ctx), _stream(stream)))
+                                    max_len, heads, head_dim, _addr(ctx), self._s(stream)))
 
     def pack_offsets(self, len_in, B, S, len_out, seq_off, stream=None):
         _check(lib().nebw_pack_offsets(self.h, _addr(len_in), B, S, _addr(len_out),
-                                       _addr(seq_off), _stream(stream)))
+                                       _addr(seq_off), self._s(stream)))
 
     def embed_ln(self, ids, seq_off, seq_len, B, S, word, vocab, pos, typ, gamma, beta, H, x,
                  a_bf16=None, eps=1e-12, stream=None):
         _check(lib().nebw_embed_ln(self.h, _addr(ids), _addr(seq_off), _addr(seq_len), B, S,
                                    _addr(word), vocab, _addr(pos), _addr(typ), _addr(gamma),
-                                   _addr(beta), eps, H, _addr(x), _addr(a_bf16), _stream(stream)))
+                                   _addr(beta), eps, H, _addr(x), _addr(a_bf16), self._s(stream)))
 
     def pool_l2(self, h, seq_off, seq_len, B, H, pooling, out, l2=True, stream=None):
         _check(lib().nebw_pool_l2(self.h, _addr(h), _addr(seq_off), _addr(seq_len), B, H,
-                                  pooling, int(l2), _addr(out), _stream(stream)))
+                                  pooling, int(l2), _addr(out), self._s(stream)))
 
     def narrow_bf16(self, x, n, y, stream=None):
-        _check(lib().nebw_narrow_bf16(self.h, _addr(x), n, _addr(y), _stream(stream)))
+        _check(lib().nebw_narrow_bf16(self.h, _addr(x), n, _addr(y), self._s(stream)))
 
 
 class Model:

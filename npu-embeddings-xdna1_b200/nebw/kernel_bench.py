@@ -129,7 +129,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=2)
     a = ap.parse_args(argv)
-    dev = nebw.Device(0)
+    dev = nebw.Device(0, torch_stream=True)
     if a.op == "gemm":
         r = bench_gemm(dev, a.M, a.K, a.N, a.epi, a.iters, a.copies)
     elif a.op == "attention":

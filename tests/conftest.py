@@ -40,7 +40,7 @@ def ref_oracle():
 def device():
     import nebw
 
-    dev = nebw.Device(0)
+    dev = nebw.Device(0, torch_stream=True)
     yield dev
     dev.close()
 
