@@ -214,6 +214,21 @@ int nebw_model_profile(nebw_model *m, int enable);
 int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K_COUNT],
                                double ms[NEBW_K_COUNT]);
 
+/* nebw_encode_device without any allocation at call time.  This entry point
+ * has no counterpart in the reference.  It is for callers that cannot
+ * allocate device memory when a request arrives: a serving process that
+ * claims its whole GPU-memory budget at start-up, or a program sharing the
+ * GPU under a fixed partition.  (nebw_encode_device may cudaMalloc a larger
+ * workspace the first time it sees a larger batch.)  All intermediates live
+ * in one static 64 MiB device array that every GPU loading the library holds
+ * until exit; a batch whose B * S padded rows do not fit it is refused with
+ * NEBW_EINVAL (for bge-large, 2520 rows fit).  The first call on a device
+ * looks the array's address up and should come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race, so the
+ * caller serialises them.  Arguments and results as nebw_encode_device. */
+int nebw_encode_device_static(nebw_model *m, const int32_t *ids_dev, const int32_t *lens_dev,
+                              int32_t B, int32_t S, float *out_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1032,3 +1032,118 @@ extern "C" int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K
   m->ev_used = 0;
   return NEBW_OK;
 }
+
+// ---------------------------------------------------------------------------
+// The encoder pass without any allocation at call time.
+//
+// For callers that cannot allocate device memory when a request arrives --
+// a serving process that sizes and claims all of its GPU memory at start-up
+// and must then run within that budget, or a host program that shares the
+// GPU under a fixed partition and may not grow it -- nebw_encode_device
+// is unsuitable as-is, because the model grows its activation workspace with
+// cudaMalloc the first time it sees a larger batch.  This variant keeps every
+// intermediate of the pass (residual stream, sublayer output, bf16 operands,
+// Q|K|V, attention context, FFN activations, packed lengths and offsets) in
+// one file-scope __device__ array of kStaticScratchBytes, which each GPU that
+// loads this library holds from module load until the process exits.
+//
+// The array's name in host code is only a host-side stand-in, never a
+// device address, so the kernels are handed the address cudaGetSymbolAddress
+// returns for it: looked up once per device, on that device's first call of
+// nebw_encode_device_static, with the device current.  That first call
+// therefore does the set-up and should come before any stream capture.
+//
+// Every call shares the one array.  Nothing in it needs clearing between
+// calls: every element the pass reads for a real token is written earlier in
+// the same pass, and rows past the token count are computed into and
+// discarded.  Calls whose work overlaps on the GPU (different streams, or
+// different models on one device) race on the array and must be serialised
+// by the caller.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = 64ull << 20;  // 64 MiB per GPU
+__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxStaticDevices = 64;
+std::mutex g_static_mu;
+void *g_static_ptr[kMaxStaticDevices] = {};
+
+int static_scratch_address(int device, void **out) {
+  NEBW_REQUIRE(device >= 0 && device < kMaxStaticDevices, "device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_ptr[device]) {
+    void *p = nullptr;
+    NEBW_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));  // the caller made `device` current
+    g_static_ptr[device] = p;
+  }
+  *out = g_static_ptr[device];
+  return NEBW_OK;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+// Bytes of static scratch one pass over `rows` padded rows of `batch`
+// sequences needs, in the carve order used below.
+size_t static_scratch_need(const nebw_config &c, int64_t rows, int64_t batch) {
+  const size_t R = static_cast<size_t>(rows), H = c.hidden, F = c.intermediate;
+  return align256(R * H * 4) + align256(R * H * 4) + align256(R * H * 2) +
+         align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * F * 2) +
+         align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4);
+}
+
+}  // namespace
+
+extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, const int32_t *lens,
+                                         int32_t B, int32_t S, float *out, void *stream) {
+  NEBW_REQUIRE(m && ids && lens && out, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  if (int rc = model_ready(m)) return rc;
+  NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
+  NEBW_REQUIRE(S > 0 && S <= m->cfg.max_seq_len, "seq %d refused: 1..max_seq_len (%d)", S,
+               m->cfg.max_seq_len);
+  const int64_t rows = static_cast<int64_t>(B) * S;
+  const size_t need = static_scratch_need(m->cfg, rows, B);
+  NEBW_REQUIRE(need <= kStaticScratchBytes,
+               "batch %d x seq %d needs %zu bytes of scratch for this model; the static scratch "
+               "of nebw_encode_device_static holds %zu bytes (use nebw_encode_device)",
+               B, S, need, kStaticScratchBytes);
+  void *base = nullptr;
+  if (int rc = static_scratch_address(m->dev->device, &base)) return rc;
+
+  // A view of the model whose workspace is the static scratch; the real
+  // model's own workspace is neither used nor grown.
+  nebw_model v;
+  v.dev = m->dev;
+  v.cfg = m->cfg;
+  v.word = m->word;
+  v.pos = m->pos;
+  v.typ = m->typ;
+  v.emb_g = m->emb_g;
+  v.emb_b = m->emb_b;
+  v.layers = m->layers;
+  v.staged = m->staged;
+  const size_t H = m->cfg.hidden, F = m->cfg.intermediate, R = static_cast<size_t>(rows);
+  unsigned char *p = static_cast<unsigned char *>(base);
+  auto carve = [&p](size_t bytes) {
+    unsigned char *q = p;
+    p += align256(bytes);
+    return q;
+  };
+  v.x = reinterpret_cast<float *>(carve(R * H * 4));
+  v.y = reinterpret_cast<float *>(carve(R * H * 4));
+  v.a = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
+  v.qkv = reinterpret_cast<__nv_bfloat16 *>(carve(R * 3 * H * 2));
+  v.ctx = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
+  v.h = reinterpret_cast<__nv_bfloat16 *>(carve(R * F * 2));
+  v.len = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
+  v.off = reinterpret_cast<int *>(carve((static_cast<size_t>(B) + 1) * 4));
+  v.rows_cap = rows;
+  v.batch_cap = B;
+  int rc;
+  if ((rc = make_tmap_kmajor(&v.map_a, v.a, rows, H, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_kmajor(&v.map_ctx, v.ctx, rows, H, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_kmajor(&v.map_h, v.h, rows, F, nebw::kGemmBM))) return rc;
+  return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));
+}

@@ -90,6 +90,7 @@ def lib() -> C.CDLL:
         "nebw_encode": ([vp, vp, vp, i32, i32, vp], C.c_int),
         "nebw_encode_device": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
         "nebw_encode_launch_count": ([vp], C.c_int),
+        "nebw_encode_device_static": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
         "nebw_model_profile": ([vp, C.c_int], C.c_int),
         "nebw_model_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
     }

@@ -1,0 +1,82 @@
+"""The no-allocation encoder entry point, nebw_encode_device_static.
+
+It exists for callers that cannot allocate device memory when a request
+arrives (a serving process that claims its whole GPU-memory budget at
+start-up, or a program sharing the GPU under a fixed partition): it runs the
+same pass as nebw_encode_device with every intermediate in one static 64 MiB
+device array instead of the model's cudaMalloc'd workspace.
+
+This file is collected last on purpose, and it must pass both alone in a
+fresh process and after every other test.  Device buffers here come from
+torch; the entry point is called through the C ABI with ctypes.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _call(fn, *args):
+    import nebw
+    rc = fn(*args)
+    if rc != 0:
+        raise nebw.NebwError(rc, nebw.lib().nebw_last_error().decode())
+
+
+def test_static_entry_matches_allocating_entry_twice(device):
+    import torch
+
+    import nebw
+    from nebw import synth
+
+    cfg = synth.CONFIGS["minilm"]
+    w = synth.config_weights(cfg, layers=3)
+    ids, _mask, lens = synth.config_batch(cfg)
+    B, S = ids.shape
+    model = nebw.Model.from_weights(device, w, max_seq_len=S)
+    lib = nebw.lib()
+    stream = C.c_void_p(nebw._stream(torch.cuda.current_stream()))
+    ids_d = torch.from_numpy(ids).cuda()
+    lens_d = torch.from_numpy(lens).cuda()
+    want = torch.empty((B, w.hidden), dtype=torch.float32, device="cuda")
+    _call(lib.nebw_encode_device, model.h, ids_d.data_ptr(), lens_d.data_ptr(), B, S,
+          want.data_ptr(), stream)
+    device.sync()
+    want_h = want.cpu().numpy()
+    # two calls in a row: the second sees the first call's leftovers in the
+    # shared static array, and a different batch order
+    for order in (np.arange(B), np.random.default_rng(1).permutation(B)):
+        ids_o = torch.from_numpy(np.ascontiguousarray(ids[order])).cuda()
+        lens_o = torch.from_numpy(np.ascontiguousarray(lens[order])).cuda()
+        got = torch.full((B, w.hidden), float("nan"), dtype=torch.float32, device="cuda")
+        _call(lib.nebw_encode_device_static, model.h, ids_o.data_ptr(), lens_o.data_ptr(), B, S,
+              got.data_ptr(), stream)
+        device.sync()
+        got_h = got.cpu().numpy()
+        assert np.isfinite(got_h).all()
+        # the tolerance the encoder parity tests use
+        cos = (got_h * want_h[order]).sum(1) / (
+            np.linalg.norm(got_h, axis=1) * np.linalg.norm(want_h[order], axis=1))
+        assert cos.min() >= 0.9999 and np.abs(got_h - want_h[order]).max() <= 2e-3
+    model.close()
+
+
+def test_static_entry_refuses_oversized_batch(device):
+    import torch
+
+    import nebw
+    from nebw import synth
+
+    w = synth.make_weights(synth.BGE_LARGE, seed=3, cls_pool=True, layers=1)
+    model = nebw.Model.from_weights(device, w, max_seq_len=512)
+    B, S = 8, 512  # 4096 padded rows of bge-large width: more than 64 MiB of scratch
+    ids_d = torch.full((B, S), 1000, dtype=torch.int32, device="cuda")
+    lens_d = torch.full((B,), S, dtype=torch.int32, device="cuda")
+    out = torch.empty((B, w.hidden), dtype=torch.float32, device="cuda")
+    with pytest.raises(nebw.NebwError, match="static scratch"):
+        _call(nebw.lib().nebw_encode_device_static, model.h, ids_d.data_ptr(), lens_d.data_ptr(),
+              B, S, out.data_ptr(), None)
+    model.close()
