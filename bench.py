@@ -48,6 +48,7 @@ sys.path.insert(0, str(PKG))
 sys.path.insert(0, str(REPO))
 
 from nebw import synth  # noqa: E402
+from nebw.shard import gather_to_root, plan_shards, unpermute  # noqa: E402
 
 METRIC = "embeddings/sec at bge-large seq512"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -72,23 +73,6 @@ def seq_flops(a: synth.Arch, lens) -> np.ndarray:
     lens = np.asarray(lens, np.float64)
     return gemm_flops_per_token(a) * lens + a.layers * 4.0 * lens ** 2 * a.hidden
 
-
-def plan_shards(lens, n: int):
-    """Length-balanced shard plan: sequences in decreasing FLOPs order, each
-    to the rank with the least work so far (ties to the lowest rank).
-    Returns n sorted index arrays that partition range(len(lens))."""
-    lens = np.asarray(lens)
-    if n == 1:
-        return [np.arange(len(lens))]
-    cost = 1.0 * lens + lens.astype(np.float64) ** 2 / 2048.0  # any monotone FLOPs proxy
-    order = np.argsort(-cost, kind="stable")
-    load = np.zeros(n)
-    owner = np.empty(len(lens), np.int64)
-    for i in order:
-        r = int(np.argmin(load))
-        owner[i] = r
-        load[r] += cost[i]
-    return [np.nonzero(owner == r)[0] for r in range(n)]
 
 
 def load_peaks():
@@ -294,13 +278,12 @@ def gpu_arm(args, cfg):
     lens_d = lens_h.cuda()
     out_d = torch.zeros((max_b, H), dtype=torch.float32, device="cuda")
     gather_d = torch.zeros((world * max_b, H), dtype=torch.float32, device="cuda") if rank == 0 else None
-    gather_list = list(gather_d.chunk(world)) if rank == 0 else None
     out_h = torch.empty((world * max_b if world > 1 else b_r, H), dtype=torch.float32).pin_memory()
 
     def step():
         model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
         if world > 1:
-            dist.gather(out_d, gather_list, dst=0)
+            gather_to_root(out_d, gather_d, world, rank, dist)
 
     def barrier():
         if world > 1:
@@ -342,17 +325,13 @@ def gpu_arm(args, cfg):
         ids_d.copy_(ids_h, non_blocking=True)
         lens_d.copy_(lens_h, non_blocking=True)
         model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
-        dist.gather(out_d, gather_list, dst=0)
+        gather_to_root(out_d, gather_d, world, rank, dist)
         if rank == 0:
             out_h.copy_(gather_d, non_blocking=True)
         stream.synchronize()
         if rank != 0:
             return None
-        full = np.empty((B, H), np.float32)
-        g = out_h.numpy()
-        for r, idx in enumerate(shards):
-            full[idx] = g[r * max_b:r * max_b + len(idx)]
-        return full
+        return unpermute(out_h.numpy(), shards, max_b)
 
     for _ in range(max(1, args.warmup)):
         res = step_e2e()

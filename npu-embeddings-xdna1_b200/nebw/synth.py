@@ -195,8 +195,8 @@ def make_tokens(batch: int, seq: int, lengths: np.ndarray, seed: int):
     pos = np.arange(seq)[None, :]
     lens = np.asarray(lengths, np.int32)[:, None]
     mask = (pos < lens).astype(np.int32)
-    ids[:, 0] = CLS_ID
     ids[np.arange(batch), lens[:, 0] - 1] = SEP_ID
+    ids[:, 0] = CLS_ID  # a length-1 row is [CLS] alone
     ids[mask == 0] = PAD_ID
     return ids, mask
 

@@ -1,0 +1,88 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+    python tests/golden/make_golden.py            (needs oracle/_ref built)
+
+Each fixture is the output of the reference's OWN host-CPU encoder path --
+runtime/src/encoders/bert_encoder.cpp + pool.cpp + model.cpp compiled from the
+reference tree (oracle/Makefile `ref`) and driven through
+EmbedService::chunk's call sequence (oracle/ref_driver.cpp) -- on seeded
+synthetic weights and tokens of a benchmark configuration.  The weights are
+not stored: they are regenerated from the recorded seed by nebw.synth, and a
+fingerprint of them is stored so a drift in the generator is caught.
+
+Fixtures (rows sampled from each configuration's synthetic batch; the
+shortest and longest rows are always included):
+  minilm_c1.npz      all-MiniLM-L6-v2 arch, the full 32 x 128 batch, mean pool
+  bge_small_c2.npz   bge-small arch, 6 rows at seq 512, CLS pool
+  bge_base_c3.npz    bge-base arch, 3 rows at seq 512, CLS pool
+  bge_large_c4.npz   bge-large arch, 3 rows at seq 512, CLS pool
+"""
+
+from __future__ import annotations
+
+import hashlib
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO / "npu-embeddings-xdna1_b200"))
+sys.path.insert(0, str(REPO))
+
+from nebw import synth  # noqa: E402
+
+FIXTURES = {
+    "minilm_c1": ("minilm", None),
+    "bge_small_c2": ("bge-small", 6),
+    "bge_base_c3": ("bge-base", 3),
+    "bge_large_c4": ("bge-large", 3),
+}
+
+
+def weights_fingerprint(w) -> str:
+    h = hashlib.sha256()
+    for name, arr in w.tensors():
+        a = np.ascontiguousarray(arr)
+        h.update(name.encode())
+        h.update(a.reshape(-1)[:64].tobytes())
+        h.update(a.reshape(-1)[-64:].tobytes())
+    return h.hexdigest()
+
+
+def sample_rows(lens, n):
+    if n is None:
+        return np.arange(len(lens))
+    pick = {int(np.argmin(lens)), int(np.argmax(lens)), 0, len(lens) - 1}
+    extra = np.random.default_rng(7).permutation(len(lens))
+    for i in extra:
+        if len(pick) >= n:
+            break
+        pick.add(int(i))
+    return np.array(sorted(pick)[:n]) if len(pick) > n else np.array(sorted(pick))
+
+
+def main():
+    from oracle.oracle import RefOracle
+    ref = RefOracle()
+    for name, (key, n) in FIXTURES.items():
+        cfg = synth.CONFIGS[key]
+        w = synth.config_weights(cfg)
+        ids, mask, lens = synth.config_batch(cfg)
+        rows = sample_rows(lens, n)
+        t0 = time.time()
+        out = ref.encode(w, ids[rows], mask[rows])
+        print(f"{name}: {len(rows)} rows in {time.time() - t0:.1f} s")
+        np.savez_compressed(
+            HERE / f"{name}.npz", config=key, rows=rows.astype(np.int32),
+            ids=ids[rows], mask=mask[rows], lens=lens[rows].astype(np.int32), embeddings=out,
+            weight_seed=20261201 + cfg.index, token_seed=20261301 + cfg.index,
+            weights_fingerprint=weights_fingerprint(w),
+            provenance="reference host-CPU path (bert_encoder.cpp/pool.cpp/model.cpp, -O2 "
+                       "-march=x86-64-v3) via oracle/ref_driver.cpp")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,108 @@
+"""Pinning the oracle (CPU, no GPU).
+
+The C restatement (oracle/bert_oracle.c) is checked two ways:
+  * against the reference's own host path compiled from its tree
+    (oracle/_ref), op by op and end to end, bit for bit -- where that build
+    exists;
+  * against the committed golden fixtures (tests/golden/*.npz), which that
+    compiled reference produced (tests/golden/make_golden.py) -- always.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+GOLDEN = REPO / "tests" / "golden"
+
+
+def load_golden(name):
+    return dict(np.load(GOLDEN / f"{name}.npz"))
+
+
+def test_port_ops_bit_exact_vs_reference(port_oracle, ref_oracle):
+    rng = np.random.default_rng(0)
+    for M, K, N in ((37, 64, 40), (9, 384, 1152), (1, 8, 8)):
+        A = rng.standard_normal((M, K)).astype(np.float32)
+        B = rng.standard_normal((K, N)).astype(np.float32)
+        b = rng.standard_normal(N).astype(np.float32)
+        np.testing.assert_array_equal(port_oracle.gemm_nt(A, B, b), ref_oracle.gemm_nt(A, B, b))
+    v = np.concatenate([np.linspace(-12, 12, 8192, dtype=np.float32),
+                        rng.standard_normal(4096).astype(np.float32) * 3])
+    np.testing.assert_array_equal(port_oracle.gelu8(v), ref_oracle.gelu8(v))
+    e = np.linspace(-120, 0, 16384, dtype=np.float32)
+    np.testing.assert_array_equal(port_oracle.exp2(e), ref_oracle.exp2(e))
+    x = rng.standard_normal(10000).astype(np.float32) * 1e3
+    x[:4] = [0.0, -0.0, 65504.0, 3.3895314e38]
+    np.testing.assert_array_equal(port_oracle.to_bf16(x), ref_oracle.to_bf16(x))
+
+
+@pytest.mark.parametrize("cls", [0, 1])
+def test_port_pool_bit_exact_vs_reference(port_oracle, ref_oracle, cls):
+    rng = np.random.default_rng(cls)
+    S, H = 64, 384
+    h = rng.standard_normal((5, S, H)).astype(np.float32)
+    am = (np.arange(S)[None, :] < np.array([[1], [7], [64], [33], [2]])).astype(np.float32)
+    np.testing.assert_array_equal(port_oracle.pool_rows(h, am, S, cls),
+                                  ref_oracle.pool_rows(h, am, S, cls))
+
+
+def test_pool_refuses_masked_cls(port_oracle, ref_oracle):
+    h = np.zeros((1, 8, 16), np.float32)
+    am = np.zeros((1, 8), np.float32)
+    for o in (port_oracle, ref_oracle):
+        with pytest.raises(RuntimeError, match="CLS"):
+            o.pool_rows(h, am, 8, 1)
+
+
+def test_port_encode_bit_exact_vs_reference(port_oracle, ref_oracle):
+    from nebw import synth
+    cfg = synth.CONFIGS["minilm"]
+    w = synth.config_weights(cfg, layers=2)
+    ids, mask, _ = synth.config_batch(cfg)
+    a, ha = port_oracle.encode(w, ids[:5], mask[:5], hidden=True)
+    b, hb = ref_oracle.encode(w, ids[:5], mask[:5], hidden=True)
+    np.testing.assert_array_equal(ha, hb)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_golden_weights_regenerate():
+    """The generator still makes the weights the fixtures were made with."""
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    from make_golden import weights_fingerprint
+
+    from nebw import synth
+    g = load_golden("minilm_c1")
+    w = synth.config_weights(synth.CONFIGS[str(g["config"])])
+    assert weights_fingerprint(w) == str(g["weights_fingerprint"])
+    ids, mask, lens = synth.config_batch(synth.CONFIGS[str(g["config"])])
+    np.testing.assert_array_equal(ids[g["rows"]], g["ids"])
+    np.testing.assert_array_equal(mask[g["rows"]], g["mask"])
+
+
+def test_port_matches_golden_minilm(port_oracle):
+    from nebw import synth
+    g = load_golden("minilm_c1")
+    w = synth.config_weights(synth.CONFIGS["minilm"])
+    got = port_oracle.encode(w, g["ids"], g["mask"])
+    np.testing.assert_array_equal(got, g["embeddings"])
+
+
+def test_port_matches_golden_bge_small_row(port_oracle):
+    from nebw import synth
+    g = load_golden("bge_small_c2")
+    w = synth.config_weights(synth.CONFIGS["bge-small"])
+    r = int(np.argmin(g["lens"]))
+    got = port_oracle.encode(w, g["ids"][r:r + 1], g["mask"][r:r + 1])
+    np.testing.assert_array_equal(got, g["embeddings"][r:r + 1])
+
+
+def test_golden_fixtures_are_sane():
+    for name in ("minilm_c1", "bge_small_c2", "bge_base_c3", "bge_large_c4"):
+        g = load_golden(name)
+        e = g["embeddings"]
+        assert np.isfinite(e).all()
+        np.testing.assert_allclose(np.linalg.norm(e, axis=1), 1.0, rtol=1e-5)
+        assert (g["mask"].sum(1) == g["lens"]).all()
+        assert (g["ids"][:, 0] == 101).all()
