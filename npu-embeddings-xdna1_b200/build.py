@@ -46,6 +46,24 @@ def build_lib(force: bool = False, verbose: bool = False) -> Path:
     return out
 
 
+def build_host_tool(verbose: bool = False) -> Path:
+    """host/nebw_embed: the C++ host side (GpuBertEncoder) as a file-in,
+    file-out tool, linked against libnebw.so with an rpath to this dir."""
+    out = PKG / "host" / "nebw_embed"
+    srcs = [PKG / "host" / "nebw_embed.cpp", PKG / "host" / "gpu_bert_encoder.hpp",
+            REPO / "include" / "nebw.h", PKG / "libnebw.so"]
+    if out.exists() and out.stat().st_mtime >= max(s.stat().st_mtime for s in srcs):
+        return out
+    cxx = shutil.which("g++") or "g++"
+    cmd = [cxx, "-std=c++17", "-O2", "-Wall", "-I", str(REPO / "include"), "-o", str(out),
+           str(PKG / "host" / "nebw_embed.cpp"), "-L", str(PKG), "-lnebw",
+           "-Wl,-rpath,$ORIGIN/.."]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return out
+
+
 def build_oracle(verbose: bool = False):
     make = shutil.which("make")
     if not make:
@@ -59,6 +77,7 @@ def build_oracle(verbose: bool = False):
 
 def main(argv):
     build_lib(force="--force" in argv, verbose=True)
+    build_host_tool(verbose=True)
     if "--lib" not in argv:
         build_oracle(verbose=True)
 

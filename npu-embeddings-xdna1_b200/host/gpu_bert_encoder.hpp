@@ -1,0 +1,110 @@
+// GpuBertEncoder -- the reference runtime's encoder interface over libnebw.
+//
+// Header-only C++17 host side of the drop-in.  It mirrors the shape of the
+// reference's encoder and the call EmbedService::chunk makes on it
+// (runtime/src/server/embed_service.cpp:29-64: token ids and the 1/0
+// attention mask as the tokenizer emits them, padded to the sequence length;
+// pooled, L2-normalised [batch, hidden] fp32 out), and the reference's error
+// convention: every failure is a std::runtime_error whose text names the
+// cause (nebw_last_error()).
+//
+// Behaviour matched to the reference beyond the arithmetic:
+//   * a row whose mask is all zero is the reference's "empty sequence":
+//     mean pooling returns the zero vector (pool_rows divides a zero sum by
+//     max(0, 1e-9) and L2-normalises with the 1e-24 floor), CLS pooling
+//     throws "CLS pooling on a sequence whose first token is masked"
+//     (runtime/include/common/app_state.hpp:345-347);
+//   * a mask that is not a prefix of ones cannot come from the reference's
+//     tokenizers (wordpiece.cpp:354-378) and is refused rather than answered
+//     for a different input.
+//
+// Link with -lnebw (libnebw.so) and include this header with include/ on
+// the include path.
+#pragma once
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "nebw.h"
+
+namespace nebw {
+
+inline void check(int rc) {
+  if (rc != NEBW_OK) throw std::runtime_error(std::string("nebw: ") + nebw_last_error());
+}
+
+class GpuBertEncoder {
+ public:
+  // Open GPU `device` and stage every tensor of the `.npue` container at
+  // `npue_path` (the reference's npue::File + set_model_shape + stage_all).
+  GpuBertEncoder(const std::string &npue_path, int device = 0) {
+    check(nebw_open(device, &dev_));
+    const int rc = nebw_model_load_npue(dev_, npue_path.c_str(), &model_);
+    if (rc != NEBW_OK) {
+      const std::string msg = nebw_last_error();
+      nebw_close(dev_);
+      throw std::runtime_error("nebw: " + msg);
+    }
+    check(nebw_model_get_config(model_, &cfg_));
+  }
+  ~GpuBertEncoder() {
+    nebw_model_destroy(model_);
+    nebw_close(dev_);
+  }
+  GpuBertEncoder(const GpuBertEncoder &) = delete;
+  GpuBertEncoder &operator=(const GpuBertEncoder &) = delete;
+
+  int64_t hidden() const { return cfg_.hidden; }
+  int64_t max_seq() const { return cfg_.max_seq_len; }
+  bool cls_pooling() const { return cfg_.pooling == NEBW_POOL_CLS; }
+
+  // ids, attention_mask: [batch, seq] row-major.  Returns [batch, hidden].
+  std::vector<float> encode(const std::vector<int32_t> &ids,
+                            const std::vector<int32_t> &attention_mask, int64_t batch,
+                            int64_t seq) {
+    if (batch < 0 || seq <= 0 || ids.size() != static_cast<size_t>(batch * seq) ||
+        attention_mask.size() != ids.size())
+      throw std::runtime_error("nebw: ids/mask must both hold batch * seq values");
+    std::vector<float> out(static_cast<size_t>(batch) * cfg_.hidden, 0.f);
+    if (batch == 0) return out;
+    // Lengths from the mask; all-zero rows are set aside (see the header).
+    std::vector<int32_t> lens, keep_ids;
+    std::vector<int64_t> keep;
+    for (int64_t b = 0; b < batch; ++b) {
+      int32_t len = 0;
+      while (len < seq && attention_mask[b * seq + len] != 0) ++len;
+      for (int64_t s = len; s < seq; ++s)
+        if (attention_mask[b * seq + s] != 0)
+          throw std::runtime_error("nebw: attention mask of row " + std::to_string(b) +
+                                   " is not a prefix of ones");
+      if (len == 0) {
+        if (cls_pooling())
+          throw std::runtime_error("CLS pooling on a sequence whose first token is masked");
+        continue;  // mean pooling of an empty row: the zero vector
+      }
+      keep.push_back(b);
+      lens.push_back(len);
+      keep_ids.insert(keep_ids.end(), ids.begin() + b * seq, ids.begin() + (b + 1) * seq);
+    }
+    if (keep.empty()) return out;
+    std::vector<float> got(keep.size() * cfg_.hidden);
+    check(nebw_encode(model_, keep_ids.data(), lens.data(), static_cast<int32_t>(keep.size()),
+                      static_cast<int32_t>(seq), got.data()));
+    for (size_t i = 0; i < keep.size(); ++i)
+      std::copy(got.begin() + i * cfg_.hidden, got.begin() + (i + 1) * cfg_.hidden,
+                out.begin() + keep[i] * cfg_.hidden);
+    return out;
+  }
+
+  nebw_model *model() { return model_; }
+  nebw_dev *device() { return dev_; }
+
+ private:
+  nebw_dev *dev_ = nullptr;
+  nebw_model *model_ = nullptr;
+  nebw_config cfg_{};
+};
+
+}  // namespace nebw
