@@ -335,4 +335,211 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// The same GEMM on CTA pairs (tcgen05 cta_group::2): tiles of 256 x BN per
+// pair.  Each CTA of a pair loads its 128 rows of A and its BN/2 rows of W;
+// the pair leader issues M=256 UMMAs that read both CTAs' shared memory and
+// accumulate rows 0-127 in the leader's TMEM and rows 128-255 in the peer's.
+// Per FLOP, each SM moves half the operand bytes of the single-CTA tile, and
+// the smaller per-CTA stage allows a deeper ring (6 or 8 stages).
+//
+// Synchronisation, per stage s and accumulator buffer a:
+//   full[s]   leader only: the leader's producer arrives with the pair's
+//             transaction bytes; both CTAs' TMA loads complete on it
+//   empty[s]  both CTAs: the leader's MMA commit, multicast to the pair
+//   tfull[a]  both CTAs: the leader's commit after a tile's last k-block
+//   tempty[a] leader only: one arrival per epilogue warp of both CTAs (16)
+// No TMA load uses multicast; the only multicast is tcgen05.commit's.
+// ---------------------------------------------------------------------------
+
+template <int BN>
+struct GemmPairShape {
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static constexpr int kHalfN = BN / 2;                  // W rows loaded per CTA
+  static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
+  static constexpr int kBBytes = kHalfN * kGemmBK * 2;   // 16 or 8 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (192 * 1024) / kStageBytes;  // 6 or 8
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+};
+
+template <int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmW, const GemmArgs p) {
+  using S = GemmPairShape<BN>;
+  constexpr int kStages = S::kStages;
+  constexpr int kPairM = 2 * kGemmBM;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sW = smem + kStages * S::kABytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *tfull = empty + kStages;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+  const bool leader = rank == 0;
+
+  int M = p.M;
+  if (p.M_dev) M = min(M, __ldg(p.M_dev));
+  const int m_blocks = (M + kPairM - 1) / kPairM;
+  const int n_blocks = (p.N + BN - 1) / BN;
+  const int num_tiles = m_blocks * n_blocks;
+  const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 16);  // 8 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int mb = tile / n_blocks, nb = tile % n_blocks;
+        const int a_row = mb * kPairM + static_cast<int>(rank) * kGemmBM;
+        const int w_row = nb * BN + static_cast<int>(rank) * S::kHalfN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+          const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sA + stage * S::kABytes, &tmA, bar, kb * kGemmBK, a_row);
+          tma_load_2d_pair(sW + stage * S::kBBytes, &tmW, bar, kb * kGemmBK, w_row);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Tail: wait until the leader's MMAs have released every stage, so all
+      // loads this CTA issued have landed and all multicast commits aimed at
+      // this CTA's empty barriers have arrived before it may exit.
+      for (int i = 0; i < kStages && ok; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) break;
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kPairM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued_any = false, ok = true;
+      int local = 0;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
+          const uint32_t w0 = smem_u32(sW + stage * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(a0 + k * 32),
+                           sdesc_kmajor_sw128(w0 + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit_pair(&tfull[acc], 0x3);
+      }
+      if (issued_any) {
+        umma_commit_pair(drain, 0x1);
+        mbar_wait(drain, 0, p.err);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9 of both CTAs) ----------------
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / 32;
+    const int quarter = warp & 3;
+    const int col_half = ((warp - 2) >> 2) * kHalf;
+    const int row_in_tile = static_cast<int>(rank) * kGemmBM + quarter * 32 + lane;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, p.err))) break;
+      tc_fence_after();
+      const int mb = tile / n_blocks, nb = tile % n_blocks;
+      const int row = mb * kPairM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + col_half);
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(t_row, ra);
+      tmem_wait_ld_regs(ra);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, nxt);
+        if (c + 1 == kChunks) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&tempty[acc]), 0));
+        }
+        const int col0 = nb * BN + col_half + c * 32;
+        if (row < M && col0 < p.N) epi_store32<EPI>(p, row, col0, cur);
+        if (c + 1 < kChunks) tmem_wait_ld_regs(nxt);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its pair may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::kTmemCols);
+  }
+}
+
 }  // namespace nebw

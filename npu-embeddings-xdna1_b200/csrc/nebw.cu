@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -131,7 +132,7 @@ int make_tmap_kmajor(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K,
 struct Weight {
   __nv_bfloat16 *ptr = nullptr;  // [N, K] bf16
   int64_t K = 0, N = 0;
-  CUtensorMap map128, map256;    // box rows 128 / 256
+  CUtensorMap map64, map128, map256;  // box rows 64 / 128 / 256
 };
 
 struct nebw_dev {
@@ -142,6 +143,9 @@ struct nebw_dev {
   int *d_err = nullptr;
   std::map<uint64_t, Weight> weights;
   uint64_t next_handle = 1;
+  // CTA pairs the GPU can hold at once for the 2-CTA GEMM (0: use the
+  // single-CTA kernel); NEBW_GEMM_CTAS=1 in the environment forces 0.
+  int gemm_pairs = 0;
 };
 
 namespace {
@@ -154,6 +158,14 @@ int use_dev(nebw_dev *d) {
 
 cudaStream_t pick_stream(nebw_dev *d, void *stream) {
   return stream ? static_cast<cudaStream_t>(stream) : d->stream;
+}
+
+template <int BN, int EPI>
+int set_pair_attr() {
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_tc_pair_kernel<BN, EPI>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::GemmPairShape<BN>::kSmemBytes));
+  return NEBW_OK;
 }
 
 template <int BN, int EPI>
@@ -176,7 +188,39 @@ int set_all_gemm_attrs() {
   rc |= set_gemm_attr<256, nebw::kEpiBf16Erf>();
   rc |= set_gemm_attr<256, nebw::kEpiF32>();
   rc |= set_gemm_attr<256, nebw::kEpiF32Resid>();
+  rc |= set_pair_attr<128, nebw::kEpiBf16>();
+  rc |= set_pair_attr<128, nebw::kEpiBf16Gelu8>();
+  rc |= set_pair_attr<128, nebw::kEpiBf16Erf>();
+  rc |= set_pair_attr<128, nebw::kEpiF32>();
+  rc |= set_pair_attr<128, nebw::kEpiF32Resid>();
+  rc |= set_pair_attr<256, nebw::kEpiBf16>();
+  rc |= set_pair_attr<256, nebw::kEpiBf16Gelu8>();
+  rc |= set_pair_attr<256, nebw::kEpiBf16Erf>();
+  rc |= set_pair_attr<256, nebw::kEpiF32>();
+  rc |= set_pair_attr<256, nebw::kEpiF32Resid>();
   return rc ? NEBW_ECUDA : NEBW_OK;
+}
+
+// How many 2-CTA clusters of the pair GEMM fit on the GPU at once.
+int query_gemm_pairs(int *pairs) {
+  *pairs = 0;
+  const char *force = std::getenv("NEBW_GEMM_CTAS");
+  if (force && std::atoi(force) == 1) return NEBW_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(nebw::kGemmThreads);
+  cfg.dynamicSmemBytes = nebw::GemmPairShape<256>::kSmemBytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  NEBW_CUDA(cudaOccupancyMaxActiveClusters(&n, nebw::gemm_tc_pair_kernel<256, nebw::kEpiBf16>, &cfg));
+  *pairs = n;
+  return NEBW_OK;
 }
 
 // ---- launchers shared by the op entry points and the encoder pass ----------
@@ -213,9 +257,38 @@ int launch_gemm_bn(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensorMa
 // every tile full; other N % 8 == 0 widths run a masked last tile).
 int gemm_bn_for(int64_t N) { return N % 256 == 0 ? 256 : 128; }
 
+template <int BN>
+int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensorMap &mW,
+                     const GemmArgs &a, cudaStream_t st) {
+  const int64_t tiles = ((static_cast<int64_t>(a.M) + 2 * nebw::kGemmBM - 1) / (2 * nebw::kGemmBM)) *
+                        ((a.N + BN - 1) / BN);
+  const int pairs = static_cast<int>(std::min<int64_t>(tiles, d->gemm_pairs));
+  if (pairs <= 0) return NEBW_OK;
+  const dim3 g(2 * pairs), b(nebw::kGemmThreads);
+  const size_t smem = nebw::GemmPairShape<BN>::kSmemBytes;
+  switch (epi) {
+    case nebw::kEpiBf16: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiBf16Gelu8: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Gelu8><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiBf16Erf: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Erf><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiF32: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiF32Resid: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32Resid><<<g, b, smem, st>>>(mA, mW, a); break;
+    default: return set_error(NEBW_EINVAL, "unknown GEMM epilogue %d", epi);
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+// 2-CTA tiles (256 x BN per pair) when the GPU can place CTA pairs, else the
+// single-CTA kernel (128 x BN).  The A tensor map's box is 128 rows either
+// way; W's box is BN/2 rows for pairs and BN rows for single CTAs.
 int launch_gemm(nebw_dev *d, const Weight &w, const CUtensorMap &mA128, int epi,
                 const GemmArgs &a, cudaStream_t st) {
-  if (gemm_bn_for(a.N) == 256) return launch_gemm_bn<256>(d, epi, mA128, w.map256, a, st);
+  const bool wide = gemm_bn_for(a.N) == 256;
+  if (d->gemm_pairs > 0) {
+    if (wide) return launch_gemm_pair<256>(d, epi, mA128, w.map128, a, st);
+    return launch_gemm_pair<128>(d, epi, mA128, w.map64, a, st);
+  }
+  if (wide) return launch_gemm_bn<256>(d, epi, mA128, w.map256, a, st);
   return launch_gemm_bn<128>(d, epi, mA128, w.map128, a, st);
 }
 
@@ -341,6 +414,7 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
   NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
   if (int rc = set_all_gemm_attrs()) return rc;
+  if (int rc = query_gemm_pairs(&d->gemm_pairs)) return rc;
   if (int rc = load_tensor_map_encoder()) return rc;
   *out = d.release();
   return NEBW_OK;
@@ -446,6 +520,10 @@ int stage_weight(nebw_dev *d, const void *host_kn, int dtype, int64_t K, int64_t
   w->K = K;
   w->N = N;
   if (int rc = make_tmap_kmajor(&w->map128, dst, N, K, 128)) {
+    cudaFree(dst);
+    return rc;
+  }
+  if (int rc = make_tmap_kmajor(&w->map64, dst, N, K, 64)) {
     cudaFree(dst);
     return rc;
   }
