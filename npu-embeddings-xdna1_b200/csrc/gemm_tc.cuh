@@ -359,25 +359,79 @@ struct GemmPairShape {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = kHalfN * kGemmBK * 2;   // 16 or 8 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (192 * 1024) / kStageBytes;  // 6 or 8
+  static constexpr int kStages = (160 * 1024) / kStageBytes;  // 5 or 6
   static constexpr int kTmemCols = 2 * BN;
+  // epilogue staging: per epilogue warp two 32 x 32 fp32 (or bf16) chunks
+  static constexpr int kChunkBytes = 32 * 32 * 4;
+  static constexpr int kStagingBytes = 8 * 2 * kChunkBytes;  // 64 KB
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+  static constexpr int kSmemBytes =
+      1024 + kStages * kStageBytes + kStagingBytes + kBarBytes;
 };
+
+// Write 32 accumulator columns of this thread's row, after bias and the
+// activation, into a 32-row chunk staged in shared memory in the swizzled
+// layout of the output tensor map's 32 x 32 box: fp32 rows are 128 bytes
+// (128-byte swizzle: 16-byte piece p of row r sits at p ^ (r % 8)), bf16
+// rows are 64 bytes (64-byte swizzle: p ^ ((r / 2) % 4)).  Either way a
+// warp's 32 row-writes of one piece land in all 32 banks, four deep.
+template <int EPI>
+__device__ __forceinline__ void epi_stage32(const GemmArgs &p, int col0, const uint32_t (&r)[32],
+                                            uint8_t *chunk, int lane) {
+  const int ncols = min(32, p.N - col0);
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  if (p.bias) {
+    const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i * 4 < ncols) {
+        const float4 b = __ldg(b4 + i);
+        v[4 * i + 0] += b.x;
+        v[4 * i + 1] += b.y;
+        v[4 * i + 2] += b.z;
+        v[4 * i + 3] += b.w;
+      }
+    }
+  }
+  if constexpr (EPI == kEpiF32) {
+    uint8_t *row = chunk + lane * 128;
+    const int sw = lane & 7;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4 *>(row + ((q ^ sw) << 4)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      pk[i] = pack_bf16x2(epi_act<EPI>(v[2 * i]), epi_act<EPI>(v[2 * i + 1]));
+    uint8_t *row = chunk + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(row + ((q ^ sw) << 4)) =
+          make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  }
+}
 
 template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmW, const GemmArgs p) {
+                        const __grid_constant__ CUtensorMap tmW,
+                        const __grid_constant__ CUtensorMap tmC, const GemmArgs p) {
   using S = GemmPairShape<BN>;
   constexpr int kStages = S::kStages;
   constexpr int kPairM = 2 * kGemmBM;
+  constexpr bool kTmaStore = EPI != kEpiF32Resid;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sW = smem + kStages * S::kABytes;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+  uint8_t *staging = smem + kStages * S::kStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(staging + S::kStagingBytes);
   uint64_t *empty = full + kStages;
   uint64_t *tfull = empty + kStages;
   uint64_t *tempty = tfull + 2;
@@ -503,7 +557,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     constexpr int kChunks = kHalf / 32;
     const int quarter = warp & 3;
     const int col_half = ((warp - 2) >> 2) * kHalf;
-    const int row_in_tile = static_cast<int>(rank) * kGemmBM + quarter * 32 + lane;
+    const int row_base = static_cast<int>(rank) * kGemmBM + quarter * 32;  // this warp's 32 rows
+    uint8_t *my_staging = staging + (warp - 2) * 2 * S::kChunkBytes;
+    int nstore = 0;  // bulk stores this warp has issued (lane 0)
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
       const int acc = local & 1;
@@ -511,7 +567,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, p.err))) break;
       tc_fence_after();
       const int mb = tile / n_blocks, nb = tile % n_blocks;
-      const int row = mb * kPairM + row_in_tile;
+      const int row0 = mb * kPairM + row_base;
+      const int row = row0 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col_half);
       uint32_t ra[32], rb[32];
@@ -528,10 +585,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&tempty[acc]), 0));
         }
         const int col0 = nb * BN + col_half + c * 32;
-        if (row < M && col0 < p.N) epi_store32<EPI>(p, row, col0, cur);
+        if constexpr (kTmaStore) {
+          if (row0 < M && col0 < p.N) {  // warp-uniform
+            uint8_t *chunk = my_staging + (nstore & 1) * S::kChunkBytes;
+            if (lane == 0) bulk_wait_group_read<1>();  // the store that last read `chunk` is done
+            __syncwarp();
+            epi_stage32<EPI>(p, col0, cur, chunk, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, chunk, col0, row0);
+              bulk_commit_group();
+            }
+            ++nstore;
+          }
+        } else {
+          if (row < M && col0 < p.N) epi_store32<EPI>(p, row, col0, cur);
+        }
         if (c + 1 < kChunks) tmem_wait_ld_regs(nxt);
       }
     }
+    if (kTmaStore && lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();

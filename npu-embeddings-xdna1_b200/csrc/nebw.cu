@@ -123,6 +123,29 @@ int make_tmap_kmajor(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K,
   return NEBW_OK;
 }
 
+// A 2-D row-major output tensor map [rows, N] with a 32 x 32 box (the GEMM
+// epilogue's TMA store chunk): fp32 rows of the box are 128 bytes (128-byte
+// swizzle), bf16 rows 64 bytes (64-byte swizzle).
+int make_tmap_out(CUtensorMap *map, const void *ptr, int64_t rows, int64_t N, bool bf16) {
+  if (int rc = load_tensor_map_encoder()) return rc;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return set_error(NEBW_EINVAL, "GEMM output address is not 16-byte aligned");
+  const int esz = bf16 ? 2 : 4;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * esz};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                              2, const_cast<void *>(ptr), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NEBW_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d) for [%lld, %lld]",
+                     static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(N));
+  return NEBW_OK;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -259,6 +282,7 @@ int gemm_bn_for(int64_t N) { return N % 256 == 0 ? 256 : 128; }
 
 template <int BN>
 int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensorMap &mW,
+                     const CUtensorMap &mC,
                      const GemmArgs &a, cudaStream_t st) {
   const int64_t tiles = ((static_cast<int64_t>(a.M) + 2 * nebw::kGemmBM - 1) / (2 * nebw::kGemmBM)) *
                         ((a.N + BN - 1) / BN);
@@ -267,11 +291,11 @@ int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensor
   const dim3 g(2 * pairs), b(nebw::kGemmThreads);
   const size_t smem = nebw::GemmPairShape<BN>::kSmemBytes;
   switch (epi) {
-    case nebw::kEpiBf16: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16><<<g, b, smem, st>>>(mA, mW, a); break;
-    case nebw::kEpiBf16Gelu8: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Gelu8><<<g, b, smem, st>>>(mA, mW, a); break;
-    case nebw::kEpiBf16Erf: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Erf><<<g, b, smem, st>>>(mA, mW, a); break;
-    case nebw::kEpiF32: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32><<<g, b, smem, st>>>(mA, mW, a); break;
-    case nebw::kEpiF32Resid: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32Resid><<<g, b, smem, st>>>(mA, mW, a); break;
+    case nebw::kEpiBf16: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiBf16Gelu8: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Gelu8><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiBf16Erf: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Erf><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiF32: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiF32Resid: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32Resid><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     default: return set_error(NEBW_EINVAL, "unknown GEMM epilogue %d", epi);
   }
   NEBW_CUDA(cudaGetLastError());
@@ -281,12 +305,12 @@ int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensor
 // 2-CTA tiles (256 x BN per pair) when the GPU can place CTA pairs, else the
 // single-CTA kernel (128 x BN).  The A tensor map's box is 128 rows either
 // way; W's box is BN/2 rows for pairs and BN rows for single CTAs.
-int launch_gemm(nebw_dev *d, const Weight &w, const CUtensorMap &mA128, int epi,
-                const GemmArgs &a, cudaStream_t st) {
+int launch_gemm(nebw_dev *d, const Weight &w, const CUtensorMap &mA128, const CUtensorMap &mC,
+                int epi, const GemmArgs &a, cudaStream_t st) {
   const bool wide = gemm_bn_for(a.N) == 256;
   if (d->gemm_pairs > 0) {
-    if (wide) return launch_gemm_pair<256>(d, epi, mA128, w.map128, a, st);
-    return launch_gemm_pair<128>(d, epi, mA128, w.map64, a, st);
+    if (wide) return launch_gemm_pair<256>(d, epi, mA128, w.map128, mC, a, st);
+    return launch_gemm_pair<128>(d, epi, mA128, w.map64, mC, a, st);
   }
   if (wide) return launch_gemm_bn<256>(d, epi, mA128, w.map256, a, st);
   return launch_gemm_bn<128>(d, epi, mA128, w.map128, a, st);
@@ -586,8 +610,9 @@ extern "C" int nebw_gemm(nebw_dev *d, uint64_t weight, const void *A, int64_t M,
                    (!bias || reinterpret_cast<uintptr_t>(bias) % 16 == 0),
                "GEMM output, residual and bias must be 16-byte aligned");
   if (M == 0) return NEBW_OK;
-  CUtensorMap mA;
+  CUtensorMap mA, mC;
   if (int rc = make_tmap_kmajor(&mA, A, M, K, nebw::kGemmBM)) return rc;
+  if (int rc = make_tmap_out(&mC, C, M, N, c_dtype == NEBW_BF16)) return rc;
   GemmArgs a{};
   a.M = static_cast<int>(M);
   a.M_dev = nullptr;
@@ -597,7 +622,7 @@ extern "C" int nebw_gemm(nebw_dev *d, uint64_t weight, const void *A, int64_t M,
   a.resid = residual;
   a.out = C;
   a.err = d->d_err;
-  return launch_gemm(d, w, mA, pick_epi(act, c_dtype, residual != nullptr), a,
+  return launch_gemm(d, w, mA, mC, pick_epi(act, c_dtype, residual != nullptr), a,
                      pick_stream(d, stream));
 }
 
@@ -683,7 +708,8 @@ struct nebw_model {
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
   float *out = nullptr;
-  CUtensorMap map_a, map_ctx, map_h;
+  CUtensorMap map_a, map_ctx, map_h;          // GEMM A operands (TMA loads)
+  CUtensorMap out_qkv, out_y, out_h;          // GEMM outputs (TMA stores)
   // per-kernel timing: one event before each launch (tagged with the kernel
   // kind) and one after the last; interval i belongs to marks[i].kind
   bool prof = false;
@@ -749,6 +775,9 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   if ((rc = make_tmap_kmajor(&m->map_a, m->a, R, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_ctx, m->ctx, R, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_h, m->h, R, F, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_out(&m->out_qkv, m->qkv, R, 3 * H, true))) return rc;
+  if ((rc = make_tmap_out(&m->out_y, m->y, R, H, false))) return rc;
+  if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
   return NEBW_OK;
 }
 
@@ -827,7 +856,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->qkv;
     if ((rc = prof_mark(m, NEBW_K_GEMM_QKV, st))) return rc;
-    if ((rc = launch_gemm(d, w.qkv, m->map_a, nebw::kEpiBf16, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv, nebw::kEpiBf16, a, st))) return rc;
     // attention
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if ((rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st)))
@@ -839,7 +868,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->y;
     if ((rc = prof_mark(m, NEBW_K_GEMM_AO, st))) return rc;
-    if ((rc = launch_gemm(d, w.ao, m->map_ctx, nebw::kEpiF32, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.ao, m->map_ctx, m->out_y, nebw::kEpiF32, a, st))) return rc;
     if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
     if ((rc = launch_layernorm(m->x, m->y, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
                                m->a, st)))
@@ -851,7 +880,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->h;
     if ((rc = prof_mark(m, NEBW_K_GEMM_UP, st))) return rc;
-    if ((rc = launch_gemm(d, w.up, m->map_a, up_epi, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.up, m->map_a, m->out_h, up_epi, a, st))) return rc;
     // FFN down + bias + residual (fp32, in place)
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(F);
@@ -859,7 +888,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->y;
     if ((rc = prof_mark(m, NEBW_K_GEMM_DOWN, st))) return rc;
-    if ((rc = launch_gemm(d, w.dn, m->map_h, nebw::kEpiF32, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.dn, m->map_h, m->out_y, nebw::kEpiF32, a, st))) return rc;
     if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
     if ((rc = launch_layernorm(m->x, m->y, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
                                L + 1 < c.num_layers ? m->a : nullptr, st)))
@@ -1223,5 +1252,8 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   if ((rc = make_tmap_kmajor(&v.map_a, v.a, rows, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_ctx, v.ctx, rows, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_h, v.h, rows, F, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_out(&v.out_qkv, v.qkv, rows, 3 * H, true))) return rc;
+  if ((rc = make_tmap_out(&v.out_y, v.y, rows, H, false))) return rc;
+  if ((rc = make_tmap_out(&v.out_h, v.h, rows, F, true))) return rc;
   return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));
 }

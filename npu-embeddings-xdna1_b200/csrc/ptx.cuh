@@ -294,6 +294,41 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t *bar, uint16_t cta_mas
       : "memory");
 }
 
+// ---- TMA stores ---------------------------------------------------------------
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA) before a bulk store reads them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2-D tiled bulk-tensor store shared -> global; elements outside the tensor
+// are not written.  c0 * sizeof(elem) must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int32_t c0,
+                                             int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N committed bulk groups still have to READ their
+// shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Wait until every committed bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // ---- misc -------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
