@@ -92,6 +92,42 @@ __device__ __forceinline__ float gelu8(float v) {
   return fmaxf(v, 0.0f) + pl;
 }
 
+// gelu8 on two values at once with sm_100's packed fp32 arithmetic
+// (fma.rn.f32x2 / add.rn.f32x2): each lane is the same IEEE operation as the
+// scalar form above, so the results are bit-identical at half the FMA-pipe
+// instructions.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpk2(uint64_t r, float &a, float &b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma_x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ void gelu8_x2(float &a, float &b) {
+  const uint64_t u = pk2(fminf(fabsf(a), 4.0f), fminf(fabsf(b), 4.0f));
+  uint64_t pl = fma_x2(pk2(-7.2340282171e-05f, -7.2340282171e-05f), u,
+                       pk2(1.8179518005e-03f, 1.8179518005e-03f));
+  pl = fma_x2(pl, u, pk2(-1.7707383379e-02f, -1.7707383379e-02f));
+  pl = fma_x2(pl, u, pk2(8.4577147641e-02f, 8.4577147641e-02f));
+  pl = fma_x2(pl, u, pk2(-1.9228671834e-01f, -1.9228671834e-01f));
+  pl = fma_x2(pl, u, pk2(9.8431124458e-02f, 9.8431124458e-02f));
+  pl = fma_x2(pl, u, pk2(3.6137852062e-01f, 3.6137852062e-01f));
+  pl = fma_x2(pl, u, pk2(-4.9454128936e-01f, -4.9454128936e-01f));
+  pl = fma_x2(pl, u, pk2(-1.3007010117e-04f, -1.3007010117e-04f));
+  unpk2(add_x2(pk2(fmaxf(a, 0.0f), fmaxf(b, 0.0f)), pl), a, b);
+}
+
 // Exact-erf GELU, 0.5 x (1 + erf(x / sqrt 2)), through CUDA's erff.
 __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
@@ -388,10 +424,8 @@ __device__ __forceinline__ void epi_stage32(const GemmArgs &p, int col0, const u
     for (int i = 0; i < 8; ++i) {
       if (i * 4 < ncols) {
         const float4 b = __ldg(b4 + i);
-        v[4 * i + 0] += b.x;
-        v[4 * i + 1] += b.y;
-        v[4 * i + 2] += b.z;
-        v[4 * i + 3] += b.w;
+        unpk2(add_x2(pk2(v[4 * i + 0], v[4 * i + 1]), pk2(b.x, b.y)), v[4 * i + 0], v[4 * i + 1]);
+        unpk2(add_x2(pk2(v[4 * i + 2], v[4 * i + 3]), pk2(b.z, b.w)), v[4 * i + 2], v[4 * i + 3]);
       }
     }
   }
@@ -404,9 +438,17 @@ __device__ __forceinline__ void epi_stage32(const GemmArgs &p, int col0, const u
           make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else {
     uint32_t pk[16];
+    if constexpr (EPI == kEpiBf16Gelu8) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      pk[i] = pack_bf16x2(epi_act<EPI>(v[2 * i]), epi_act<EPI>(v[2 * i + 1]));
+      for (int i = 0; i < 16; ++i) {
+        gelu8_x2(v[2 * i], v[2 * i + 1]);
+        pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        pk[i] = pack_bf16x2(epi_act<EPI>(v[2 * i]), epi_act<EPI>(v[2 * i + 1]));
+    }
     uint8_t *row = chunk + lane * 64;
     const int sw = (lane >> 1) & 3;
 #pragma unroll
