@@ -269,7 +269,7 @@ def gpu_arm(args, cfg):
 
     dev = nebw.Device(local)
     model = nebw.Model.from_weights(dev, w, max_seq_len=S)
-    launches_per_step = model.launch_count()
+    launches_per_step = model.launch_count(S)
     stream = torch.cuda.current_stream()
 
     ids_h = torch.from_numpy(np.ascontiguousarray(ids[mine])).pin_memory()

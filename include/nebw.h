@@ -110,11 +110,14 @@ int nebw_layernorm(nebw_dev *dev, float *x, const float *y, const float *gamma,
 
 /* Fused masked attention over packed sequences.  Replaces qk / softmax_cpu /
  * av and attention_npu (bert_encoder.cpp:481-530, :995-1181).
- *   qkv_bf16 [T, 3H] device (Q|K|V per row, Q pre-scaled by 1/sqrt(d))
+ *   qkv_bf16 [rows, 3H] device (Q|K|V per row, Q pre-scaled by 1/sqrt(d));
+ *   rows = the buffer's row count (>= every seq_off[b] + seq_len[b])
  *   seq_off [B+1], seq_len [B] int32 device: sequence b owns packed rows
  *   [seq_off[b], seq_off[b] + seq_len[b])
- *   ctx_bf16 [T, H] device.  head_dim in {32, 64}; max_len bounds seq_len. */
-int nebw_attention(nebw_dev *dev, const void *qkv_bf16, const int32_t *seq_off,
+ *   ctx_bf16 [rows, H] device.  head_dim in {32, 64}; max_len bounds
+ *   seq_len.  head_dim 64 with max_len <= 512 runs on tcgen05 (S and P.V on
+ *   the 5th-generation tensor cores); head_dim 32 on mma.sync. */
+int nebw_attention(nebw_dev *dev, const void *qkv_bf16, int64_t rows, const int32_t *seq_off,
                    const int32_t *seq_len, int32_t B, int32_t max_len, int32_t heads,
                    int32_t head_dim, void *ctx_bf16, void *stream);
 
@@ -196,8 +199,9 @@ int nebw_encode_device(nebw_model *m, const int32_t *ids_dev, const int32_t *len
                        int32_t B, int32_t S, float *out_dev, void *stream);
 
 /* Number of kernel launches one nebw_encode_device call makes for a model
- * (for launch accounting). */
-int nebw_encode_launch_count(const nebw_model *m);
+ * at padded sequence length `seq` (<= 0: the model's max_seq_len), for
+ * launch accounting. */
+int nebw_encode_launch_count(const nebw_model *m, int32_t seq);
 
 /* ---- per-kernel timing (the reference's BertEncoder::Timings,
  * bert_encoder.hpp:67-87, measured on the device) ------------------------

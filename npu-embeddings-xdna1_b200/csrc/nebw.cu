@@ -37,6 +37,7 @@
 
 #include "../../include/nebw.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "gemm_tc.cuh"
 #include "npue_file.h"
 #include "ptx.cuh"
@@ -389,6 +390,47 @@ int launch_attention(const __nv_bfloat16 *qkv, const int *off, const int *len, i
   return NEBW_OK;
 }
 
+template <int LP>
+void launch_attention_tc_lp(const CUtensorMap &map, const int *off, const int *len, const int *list,
+                            const int *count, int B, int heads, int H, __nv_bfloat16 *ctx, int *err,
+                            cudaStream_t st) {
+  const dim3 grid(LP / 128, heads, B);
+  nebw::attention_tc_kernel<LP><<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape<LP>::kSmemBytes,
+                                  st>>>(map, off, len, list, count, H, ctx, err);
+}
+
+// tcgen05 attention for head_dim 64.  With `lists`/`counts` (the length
+// buckets attn_bucket_kernel made), one launch per bucket up to max_len;
+// without, one launch sized for max_len over every sequence.
+int launch_attention_tc(const CUtensorMap &map, const int *off, const int *len, const int *lists,
+                        const int *counts, int B, int max_len, int heads, __nv_bfloat16 *ctx,
+                        int *err, cudaStream_t st) {
+  NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0 &&
+                   max_len <= 512,
+               "attention grid refused (B %d, heads %d, max_len %d <= 512)", B, heads, max_len);
+  const int H = heads * nebw::kAttnTcD;
+  if (lists) {
+    launch_attention_tc_lp<128>(map, off, len, lists, counts, B, heads, H, ctx, err, st);
+    if (max_len > 128)
+      launch_attention_tc_lp<256>(map, off, len, lists + B, counts + 1, B, heads, H, ctx, err, st);
+    if (max_len > 256)
+      launch_attention_tc_lp<512>(map, off, len, lists + 2 * B, counts + 2, B, heads, H, ctx, err, st);
+  } else if (max_len <= 128) {
+    launch_attention_tc_lp<128>(map, off, len, nullptr, nullptr, B, heads, H, ctx, err, st);
+  } else if (max_len <= 256) {
+    launch_attention_tc_lp<256>(map, off, len, nullptr, nullptr, B, heads, H, ctx, err, st);
+  } else {
+    launch_attention_tc_lp<512>(map, off, len, nullptr, nullptr, B, heads, H, ctx, err, st);
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+int attention_launches(int head_dim, int max_len) {
+  if (head_dim != 64) return 1;
+  return max_len <= 128 ? 1 : (max_len <= 256 ? 2 : 3);
+}
+
 int launch_pool(const float *h, const int *off, const int *len, int B, int H, int pooling, int l2,
                 float *out, cudaStream_t st) {
   NEBW_REQUIRE(H > 0 && H <= 16 * nebw::kPoolThreads, "pool width %d refused (<= 4096)", H);
@@ -438,6 +480,12 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
   NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
   if (int rc = set_all_gemm_attrs()) return rc;
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::AttnTcShape<128>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::AttnTcShape<256>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::AttnTcShape<512>::kSmemBytes));
   if (int rc = query_gemm_pairs(&d->gemm_pairs)) return rc;
   if (int rc = load_tensor_map_encoder()) return rc;
   *out = d.release();
@@ -636,11 +684,19 @@ extern "C" int nebw_layernorm(nebw_dev *d, float *x, const float *y, const float
                           static_cast<__nv_bfloat16 *>(a_bf16), pick_stream(d, stream));
 }
 
-extern "C" int nebw_attention(nebw_dev *d, const void *qkv, const int32_t *off, const int32_t *len,
-                              int32_t B, int32_t max_len, int32_t heads, int32_t hd, void *ctx,
-                              void *stream) {
+extern "C" int nebw_attention(nebw_dev *d, const void *qkv, int64_t rows, const int32_t *off,
+                              const int32_t *len, int32_t B, int32_t max_len, int32_t heads,
+                              int32_t hd, void *ctx, void *stream) {
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(qkv && off && len && ctx, "null attention operand");
+  NEBW_REQUIRE(rows > 0 && rows < (1ll << 31), "rows %lld refused", static_cast<long long>(rows));
+  if (hd == nebw::kAttnTcD && max_len <= 512) {
+    CUtensorMap map;
+    if (int rc = make_tmap_kmajor(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 128))
+      return rc;
+    return launch_attention_tc(map, off, len, nullptr, nullptr, B, max_len, heads,
+                               static_cast<__nv_bfloat16 *>(ctx), d->d_err, pick_stream(d, stream));
+  }
   return launch_attention(static_cast<const __nv_bfloat16 *>(qkv), off, len, B, max_len, heads, hd,
                           static_cast<__nv_bfloat16 *>(ctx), pick_stream(d, stream));
 }
@@ -707,6 +763,8 @@ struct nebw_model {
   float *x = nullptr, *y = nullptr;  // residual stream, sublayer output
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
+  int *att_lists = nullptr, *att_counts = nullptr;  // length buckets [3][B], [3]
+  CUtensorMap map_qkv_att;  // Q|K|V rows as 64 x 128 TMA tiles for attention
   float *out = nullptr;
   CUtensorMap map_a, map_ctx, map_h;          // GEMM A operands (TMA loads)
   CUtensorMap out_qkv, out_y, out_h;          // GEMM outputs (TMA stores)
@@ -731,10 +789,13 @@ void free_workspace(nebw_model *m) {
   cudaFree(m->len_in);
   cudaFree(m->len);
   cudaFree(m->off);
+  cudaFree(m->att_lists);
+  cudaFree(m->att_counts);
   cudaFree(m->out);
   m->x = m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
   m->ids = m->len_in = m->len = m->off = nullptr;
+  m->att_lists = m->att_counts = nullptr;
   m->out = nullptr;
   m->rows_cap = m->batch_cap = m->ids_cap = 0;
 }
@@ -764,6 +825,8 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len_in), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->off), (Bc + 1) * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_lists), 3 * Bc * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_counts), 4 * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->out), Bc * H * 4);
   if (rc) {
     free_workspace(m);
@@ -778,6 +841,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   if ((rc = make_tmap_out(&m->out_qkv, m->qkv, R, 3 * H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_y, m->y, R, H, false))) return rc;
   if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
+  if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
   return NEBW_OK;
 }
 
@@ -837,6 +901,11 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   int rc;
   if ((rc = prof_mark(m, NEBW_K_PACK, st))) return rc;
   if ((rc = launch_pack(len_in, B, S, m->len, m->off, d->d_err, st))) return rc;
+  const bool tc_attention = c.head_dim == nebw::kAttnTcD && S <= 512;
+  if (tc_attention) {
+    nebw::attn_bucket_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_lists, m->att_counts);
+    NEBW_CUDA(cudaGetLastError());
+  }
   if ((rc = prof_mark(m, NEBW_K_EMBED_LN, st))) return rc;
   if ((rc = launch_embed_ln(ids, B, S, m->off, m->len, m->word, c.vocab_size, m->pos, m->typ,
                             m->emb_g, m->emb_b, c.layer_norm_eps, c.hidden, m->x, m->a, d->d_err,
@@ -859,7 +928,12 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv, nebw::kEpiBf16, a, st))) return rc;
     // attention
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
-    if ((rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st)))
+    if (tc_attention)
+      rc = launch_attention_tc(m->map_qkv_att, m->off, m->len, m->att_lists, m->att_counts, B, S,
+                               c.num_heads, m->ctx, d->d_err, st);
+    else
+      rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st);
+    if (rc)
       return rc;
     // attention-out + bias + residual (fp32, in place)
     a.N = static_cast<int>(H);
@@ -1107,9 +1181,11 @@ extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *len
   return nebw_sync(d);
 }
 
-extern "C" int nebw_encode_launch_count(const nebw_model *m) {
+extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
-  return 3 + 7 * m->cfg.num_layers;
+  const int S = seq > 0 ? seq : m->cfg.max_seq_len;
+  const bool tc = m->cfg.head_dim == nebw::kAttnTcD && S <= 512;
+  return 3 + (tc ? 1 : 0) + m->cfg.num_layers * (6 + attention_launches(tc ? 64 : 0, S));
 }
 
 extern "C" int nebw_model_profile(nebw_model *m, int enable) {
@@ -1197,7 +1273,8 @@ size_t static_scratch_need(const nebw_config &c, int64_t rows, int64_t batch) {
   const size_t R = static_cast<size_t>(rows), H = c.hidden, F = c.intermediate;
   return align256(R * H * 4) + align256(R * H * 4) + align256(R * H * 2) +
          align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * F * 2) +
-         align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4);
+         align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4) +
+         align256(3 * static_cast<size_t>(batch) * 4) + align256(4 * 4);
 }
 
 }  // namespace
@@ -1246,6 +1323,8 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   v.h = reinterpret_cast<__nv_bfloat16 *>(carve(R * F * 2));
   v.len = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
   v.off = reinterpret_cast<int *>(carve((static_cast<size_t>(B) + 1) * 4));
+  v.att_lists = reinterpret_cast<int *>(carve(3 * static_cast<size_t>(B) * 4));
+  v.att_counts = reinterpret_cast<int *>(carve(4 * 4));
   v.rows_cap = rows;
   v.batch_cap = B;
   int rc;
@@ -1255,5 +1334,6 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   if ((rc = make_tmap_out(&v.out_qkv, v.qkv, rows, 3 * H, true))) return rc;
   if ((rc = make_tmap_out(&v.out_y, v.y, rows, H, false))) return rc;
   if ((rc = make_tmap_out(&v.out_h, v.h, rows, F, true))) return rc;
+  if ((rc = make_tmap_kmajor(&v.map_qkv_att, v.qkv, rows, 3 * H, 128))) return rc;
   return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));
 }

@@ -76,7 +76,7 @@ def lib() -> C.CDLL:
         "nebw_release_weight": ([vp, C.c_uint64], C.c_int),
         "nebw_gemm": ([vp, C.c_uint64, vp, i64, i64, i64, vp, vp, C.c_int, vp, C.c_int, vp], C.c_int),
         "nebw_layernorm": ([vp, vp, vp, vp, vp, C.c_float, i64, i64, vp, vp], C.c_int),
-        "nebw_attention": ([vp, vp, vp, vp, i32, i32, i32, i32, vp, vp], C.c_int),
+        "nebw_attention": ([vp, vp, i64, vp, vp, i32, i32, i32, i32, vp, vp], C.c_int),
         "nebw_pack_offsets": ([vp, vp, i32, i32, vp, vp, vp], C.c_int),
         "nebw_embed_ln": ([vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, vp, vp, C.c_float, i32, vp,
                            vp, vp], C.c_int),
@@ -89,7 +89,7 @@ def lib() -> C.CDLL:
         "nebw_model_get_config": ([vp, C.POINTER(Config)], C.c_int),
         "nebw_encode": ([vp, vp, vp, i32, i32, vp], C.c_int),
         "nebw_encode_device": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
-        "nebw_encode_launch_count": ([vp], C.c_int),
+        "nebw_encode_launch_count": ([vp, i32], C.c_int),
         "nebw_encode_device_static": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
         "nebw_model_profile": ([vp, C.c_int], C.c_int),
         "nebw_model_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
@@ -199,8 +199,8 @@ class Device:
         _check(lib().nebw_layernorm(self.h, _addr(x), _addr(y), _addr(gamma), _addr(beta), eps,
                                     rows, H, _addr(a_bf16), self._s(stream)))
 
-    def attention(self, qkv, seq_off, seq_len, B, max_len, heads, head_dim, ctx, stream=None):
-        _check(lib().nebw_attention(self.h, _addr(qkv), _addr(seq_off), _addr(seq_len), B,
+    def attention(self, qkv, rows, seq_off, seq_len, B, max_len, heads, head_dim, ctx, stream=None):
+        _check(lib().nebw_attention(self.h, _addr(qkv), rows, _addr(seq_off), _addr(seq_len), B,
                                     max_len, heads, head_dim, _addr(ctx), self._s(stream)))
 
     def pack_offsets(self, len_in, B, S, len_out, seq_off, stream=None):
@@ -278,8 +278,8 @@ class Model:
     def hidden(self) -> int:
         return self.cfg.hidden
 
-    def launch_count(self) -> int:
-        return lib().nebw_encode_launch_count(self.h)
+    def launch_count(self, seq: int = 0) -> int:
+        return lib().nebw_encode_launch_count(self.h, seq)
 
     KERNEL_KINDS = ("pack", "embed_ln", "gemm_qkv", "attention", "gemm_ao", "layernorm",
                     "gemm_up", "gemm_down", "pool")

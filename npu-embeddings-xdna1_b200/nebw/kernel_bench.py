@@ -69,7 +69,7 @@ def bench_attention(dev, B, L, heads, hd, iters, copies):
     len_d = torch.from_numpy(lens).cuda()
 
     def run(i):
-        dev.attention(qkv[i % copies], off_d, len_d, B, L, heads, hd, ctx,
+        dev.attention(qkv[i % copies], T, off_d, len_d, B, L, heads, hd, ctx,
                       stream=torch.cuda.current_stream())
 
     for i in range(3):

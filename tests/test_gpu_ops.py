@@ -168,8 +168,8 @@ def test_attention_matches_float64(device, D, heads):
     H = D * heads
     qkv = bf16_bits(rng.standard_normal((T, 3 * H), np.float32) * 0.5)
     ctx = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
-    device.attention(dev_tensor(qkv), dev_tensor(off), dev_tensor(lens), len(lens), 512, heads, D,
-                     ctx)
+    device.attention(dev_tensor(qkv), T, dev_tensor(off), dev_tensor(lens), len(lens), 512, heads,
+                     D, ctx)
     device.sync()
     got = bits_to_f32(host_bits(ctx)).astype(np.float64)
     q = bits_to_f32(qkv).astype(np.float64)
