@@ -71,6 +71,14 @@ int nebw_copy_h2d(nebw_dev *dev, void *dst_dev, const void *src_host, size_t byt
 int nebw_copy_d2h(nebw_dev *dev, void *dst_host, const void *src_dev, size_t bytes);
 int nebw_device_info(nebw_dev *dev, int *sm_count, int *cc_major, int *cc_minor);
 
+/* Which attention kernel a device handle uses for head_dim 64 (no
+ * counterpart in the reference, which has one host path):
+ * NEBW_ATTN_MMA -- flash attention on mma.sync (the default);
+ * NEBW_ATTN_TCGEN05 -- S and P.V on tcgen05 UMMA with TMEM accumulators.
+ * Both give results within the same parity tolerance. */
+enum { NEBW_ATTN_MMA = 0, NEBW_ATTN_TCGEN05 = 1 };
+int nebw_set_attention_kernel(nebw_dev *dev, int kind);
+
 /* ---- weights -------------------------------------------------------------
  * Replaces npu::Design::stage(arg, data, bytes) (design.hpp:199-263,
  * design.cpp:394) for a GEMM operand.  `host_kn` is the container's operand

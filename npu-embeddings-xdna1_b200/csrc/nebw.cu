@@ -170,6 +170,9 @@ struct nebw_dev {
   // CTA pairs the GPU can hold at once for the 2-CTA GEMM (0: use the
   // single-CTA kernel); NEBW_GEMM_CTAS=1 in the environment forces 0.
   int gemm_pairs = 0;
+  // attention kernel for head_dim 64: NEBW_ATTN_MMA (mma.sync flash) or
+  // NEBW_ATTN_TCGEN05 (UMMA/TMEM); see nebw_set_attention_kernel
+  int attn_kind = NEBW_ATTN_MMA;
 };
 
 namespace {
@@ -553,6 +556,14 @@ extern "C" int nebw_device_info(nebw_dev *d, int *sm, int *maj, int *min) {
   return NEBW_OK;
 }
 
+extern "C" int nebw_set_attention_kernel(nebw_dev *d, int kind) {
+  NEBW_REQUIRE(d != nullptr, "null device handle");
+  NEBW_REQUIRE(kind == NEBW_ATTN_MMA || kind == NEBW_ATTN_TCGEN05, "attention kernel %d refused",
+               kind);
+  d->attn_kind = kind;
+  return NEBW_OK;
+}
+
 // ---------------------------------------------------------------------------
 // C ABI: weights
 // ---------------------------------------------------------------------------
@@ -690,7 +701,7 @@ extern "C" int nebw_attention(nebw_dev *d, const void *qkv, int64_t rows, const 
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(qkv && off && len && ctx, "null attention operand");
   NEBW_REQUIRE(rows > 0 && rows < (1ll << 31), "rows %lld refused", static_cast<long long>(rows));
-  if (hd == nebw::kAttnTcD && max_len <= 512) {
+  if (d->attn_kind == NEBW_ATTN_TCGEN05 && hd == nebw::kAttnTcD && max_len <= 512) {
     CUtensorMap map;
     if (int rc = make_tmap_kmajor(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 128))
       return rc;
@@ -901,7 +912,8 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   int rc;
   if ((rc = prof_mark(m, NEBW_K_PACK, st))) return rc;
   if ((rc = launch_pack(len_in, B, S, m->len, m->off, d->d_err, st))) return rc;
-  const bool tc_attention = c.head_dim == nebw::kAttnTcD && S <= 512;
+  const bool tc_attention =
+      d->attn_kind == NEBW_ATTN_TCGEN05 && c.head_dim == nebw::kAttnTcD && S <= 512;
   if (tc_attention) {
     nebw::attn_bucket_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_lists, m->att_counts);
     NEBW_CUDA(cudaGetLastError());
@@ -1184,7 +1196,8 @@ extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *len
 extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
   const int S = seq > 0 ? seq : m->cfg.max_seq_len;
-  const bool tc = m->cfg.head_dim == nebw::kAttnTcD && S <= 512;
+  const bool tc =
+      m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD && S <= 512;
   return 3 + (tc ? 1 : 0) + m->cfg.num_layers * (6 + attention_launches(tc ? 64 : 0, S));
 }
 

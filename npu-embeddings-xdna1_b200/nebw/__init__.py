@@ -91,6 +91,7 @@ def lib() -> C.CDLL:
         "nebw_encode_device": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
         "nebw_encode_launch_count": ([vp, i32], C.c_int),
         "nebw_encode_device_static": ([vp, vp, vp, i32, i32, vp, vp], C.c_int),
+        "nebw_set_attention_kernel": ([vp, C.c_int], C.c_int),
         "nebw_model_profile": ([vp, C.c_int], C.c_int),
         "nebw_model_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
     }
@@ -170,6 +171,11 @@ class Device:
             import torch
             torch.cuda.current_stream().synchronize()
         _check(lib().nebw_sync(self.h))
+
+    ATTN_MMA, ATTN_TCGEN05 = 0, 1
+
+    def set_attention_kernel(self, kind: int):
+        _check(lib().nebw_set_attention_kernel(self.h, kind))
 
     def info(self):
         sm, ma, mi = C.c_int(), C.c_int(), C.c_int()

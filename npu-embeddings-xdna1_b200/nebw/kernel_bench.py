@@ -128,8 +128,10 @@ def main(argv=None):
     ap.add_argument("--epi", default="bf16", choices=["bf16", "gelu8", "erf", "f32", "resid"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=2)
+    ap.add_argument("--attn-kind", type=int, default=0, help="0 mma.sync, 1 tcgen05")
     a = ap.parse_args(argv)
     dev = nebw.Device(0, torch_stream=True)
+    dev.set_attention_kernel(a.attn_kind)
     if a.op == "gemm":
         r = bench_gemm(dev, a.M, a.K, a.N, a.epi, a.iters, a.copies)
     elif a.op == "attention":

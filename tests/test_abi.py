@@ -37,7 +37,7 @@ def test_null_arguments_refused_without_touching_a_device():
     assert L.nebw_model_get_config(None, None) == 1
     assert "null" in L.nebw_last_error().decode()
     assert L.nebw_model_profile(None, 1) == 1
-    assert L.nebw_encode_launch_count(None) == -1
+    assert L.nebw_encode_launch_count(None, 0) == -1
 
 
 def test_oracle_is_not_on_the_product_path():

@@ -160,17 +160,22 @@ def _packed(lens):
     return off, int(off[-1])
 
 
-@pytest.mark.parametrize("D,heads", [(32, 12), (64, 16)])
-def test_attention_matches_float64(device, D, heads):
-    rng = np.random.default_rng(D)
-    lens = np.array([1, 8, 63, 64, 65, 130, 512, 200], np.int32)
+@pytest.mark.parametrize("D,heads,kind", [(32, 12, 0), (64, 16, 0), (64, 16, 1), (64, 12, 1)])
+def test_attention_matches_float64(device, D, heads, kind):
+    """kind 0: mma.sync flash kernel; kind 1: tcgen05 kernel (head_dim 64)."""
+    rng = np.random.default_rng(D + kind)
+    lens = np.array([1, 8, 63, 64, 65, 127, 128, 129, 130, 512, 200, 257], np.int32)
     off, T = _packed(lens)
     H = D * heads
     qkv = bf16_bits(rng.standard_normal((T, 3 * H), np.float32) * 0.5)
     ctx = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
-    device.attention(dev_tensor(qkv), T, dev_tensor(off), dev_tensor(lens), len(lens), 512, heads,
-                     D, ctx)
-    device.sync()
+    device.set_attention_kernel(kind)
+    try:
+        device.attention(dev_tensor(qkv), T, dev_tensor(off), dev_tensor(lens), len(lens), 512,
+                         heads, D, ctx)
+        device.sync()
+    finally:
+        device.set_attention_kernel(0)
     got = bits_to_f32(host_bits(ctx)).astype(np.float64)
     q = bits_to_f32(qkv).astype(np.float64)
     for b, L in enumerate(lens):
