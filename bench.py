@@ -268,6 +268,7 @@ def gpu_arm(args, cfg):
     T_r = int(lens[mine].sum())
 
     dev = nebw.Device(local)
+    dev.set_attention_kernel(dev.ATTN_TCGEN05 if args.attention == "tcgen05" else dev.ATTN_MMA)
     model = nebw.Model.from_weights(dev, w, max_seq_len=S)
     launches_per_step = model.launch_count(S)
     stream = torch.cuda.current_stream()
@@ -468,6 +469,8 @@ def main():
     ap.add_argument("--impl", choices=["nebw", "reference"], default="nebw")
     ap.add_argument("--config", default="bge-large", choices=sorted(synth.CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attention", choices=["mma", "tcgen05"], default="mma",
+                    help="attention kernel for head_dim 64")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

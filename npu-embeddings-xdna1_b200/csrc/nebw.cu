@@ -393,45 +393,25 @@ int launch_attention(const __nv_bfloat16 *qkv, const int *off, const int *len, i
   return NEBW_OK;
 }
 
-template <int LP>
-void launch_attention_tc_lp(const CUtensorMap &map, const int *off, const int *len, const int *list,
-                            const int *count, int B, int heads, int H, __nv_bfloat16 *ctx, int *err,
-                            cudaStream_t st) {
-  const dim3 grid(LP / 128, heads, B);
-  nebw::attention_tc_kernel<LP><<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape<LP>::kSmemBytes,
-                                  st>>>(map, off, len, list, count, H, ctx, err);
-}
-
-// tcgen05 attention for head_dim 64.  With `lists`/`counts` (the length
-// buckets attn_bucket_kernel made), one launch per bucket up to max_len;
-// without, one launch sized for max_len over every sequence.
-int launch_attention_tc(const CUtensorMap &map, const int *off, const int *len, const int *lists,
-                        const int *counts, int B, int max_len, int heads, __nv_bfloat16 *ctx,
-                        int *err, cudaStream_t st) {
-  NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0 &&
-                   max_len <= 512,
-               "attention grid refused (B %d, heads %d, max_len %d <= 512)", B, heads, max_len);
+// tcgen05 attention for head_dim 64: one launch over (128-query tiles,
+// heads, sequences), in the longest-first order `order` gives (or request
+// order when it is null).
+int launch_attention_tc(const CUtensorMap &map, const int *off, const int *len, const int *order,
+                        int B, int max_len, int heads, __nv_bfloat16 *ctx, int *err,
+                        cudaStream_t st) {
+  NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0,
+               "attention grid refused (B %d, heads %d, max_len %d)", B, heads, max_len);
   const int H = heads * nebw::kAttnTcD;
-  if (lists) {
-    launch_attention_tc_lp<128>(map, off, len, lists, counts, B, heads, H, ctx, err, st);
-    if (max_len > 128)
-      launch_attention_tc_lp<256>(map, off, len, lists + B, counts + 1, B, heads, H, ctx, err, st);
-    if (max_len > 256)
-      launch_attention_tc_lp<512>(map, off, len, lists + 2 * B, counts + 2, B, heads, H, ctx, err, st);
-  } else if (max_len <= 128) {
-    launch_attention_tc_lp<128>(map, off, len, nullptr, nullptr, B, heads, H, ctx, err, st);
-  } else if (max_len <= 256) {
-    launch_attention_tc_lp<256>(map, off, len, nullptr, nullptr, B, heads, H, ctx, err, st);
-  } else {
-    launch_attention_tc_lp<512>(map, off, len, nullptr, nullptr, B, heads, H, ctx, err, st);
-  }
+  const dim3 grid((max_len + 127) / 128, heads, B);
+  nebw::attention_tc_kernel<<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape::kSmemBytes, st>>>(
+      map, off, len, order, H, ctx, err);
   NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }
 
 int attention_launches(int head_dim, int max_len) {
-  if (head_dim != 64) return 1;
-  return max_len <= 128 ? 1 : (max_len <= 256 ? 2 : 3);
+  (void)max_len;
+  return head_dim == 64 ? 1 : 1;
 }
 
 int launch_pool(const float *h, const int *off, const int *len, int B, int H, int pooling, int l2,
@@ -483,12 +463,8 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
   NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
   if (int rc = set_all_gemm_attrs()) return rc;
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::AttnTcShape<128>::kSmemBytes));
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::AttnTcShape<256>::kSmemBytes));
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::AttnTcShape<512>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::AttnTcShape::kSmemBytes));
   if (int rc = query_gemm_pairs(&d->gemm_pairs)) return rc;
   if (int rc = load_tensor_map_encoder()) return rc;
   *out = d.release();
@@ -701,11 +677,11 @@ extern "C" int nebw_attention(nebw_dev *d, const void *qkv, int64_t rows, const 
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(qkv && off && len && ctx, "null attention operand");
   NEBW_REQUIRE(rows > 0 && rows < (1ll << 31), "rows %lld refused", static_cast<long long>(rows));
-  if (d->attn_kind == NEBW_ATTN_TCGEN05 && hd == nebw::kAttnTcD && max_len <= 512) {
+  if (d->attn_kind == NEBW_ATTN_TCGEN05 && hd == nebw::kAttnTcD) {
     CUtensorMap map;
     if (int rc = make_tmap_kmajor(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 128))
       return rc;
-    return launch_attention_tc(map, off, len, nullptr, nullptr, B, max_len, heads,
+    return launch_attention_tc(map, off, len, nullptr, B, max_len, heads,
                                static_cast<__nv_bfloat16 *>(ctx), d->d_err, pick_stream(d, stream));
   }
   return launch_attention(static_cast<const __nv_bfloat16 *>(qkv), off, len, B, max_len, heads, hd,
@@ -774,7 +750,7 @@ struct nebw_model {
   float *x = nullptr, *y = nullptr;  // residual stream, sublayer output
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
-  int *att_lists = nullptr, *att_counts = nullptr;  // length buckets [3][B], [3]
+  int *att_order = nullptr;  // sequences, longest length class first [B]
   CUtensorMap map_qkv_att;  // Q|K|V rows as 64 x 128 TMA tiles for attention
   float *out = nullptr;
   CUtensorMap map_a, map_ctx, map_h;          // GEMM A operands (TMA loads)
@@ -800,13 +776,12 @@ void free_workspace(nebw_model *m) {
   cudaFree(m->len_in);
   cudaFree(m->len);
   cudaFree(m->off);
-  cudaFree(m->att_lists);
-  cudaFree(m->att_counts);
+  cudaFree(m->att_order);
   cudaFree(m->out);
   m->x = m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
   m->ids = m->len_in = m->len = m->off = nullptr;
-  m->att_lists = m->att_counts = nullptr;
+  m->att_order = nullptr;
   m->out = nullptr;
   m->rows_cap = m->batch_cap = m->ids_cap = 0;
 }
@@ -836,8 +811,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len_in), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->off), (Bc + 1) * 4);
-  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_lists), 3 * Bc * 4);
-  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_counts), 4 * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_order), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->out), Bc * H * 4);
   if (rc) {
     free_workspace(m);
@@ -913,9 +887,9 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   if ((rc = prof_mark(m, NEBW_K_PACK, st))) return rc;
   if ((rc = launch_pack(len_in, B, S, m->len, m->off, d->d_err, st))) return rc;
   const bool tc_attention =
-      d->attn_kind == NEBW_ATTN_TCGEN05 && c.head_dim == nebw::kAttnTcD && S <= 512;
+      d->attn_kind == NEBW_ATTN_TCGEN05 && c.head_dim == nebw::kAttnTcD;
   if (tc_attention) {
-    nebw::attn_bucket_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_lists, m->att_counts);
+    nebw::attn_order_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_order);
     NEBW_CUDA(cudaGetLastError());
   }
   if ((rc = prof_mark(m, NEBW_K_EMBED_LN, st))) return rc;
@@ -941,7 +915,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     // attention
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if (tc_attention)
-      rc = launch_attention_tc(m->map_qkv_att, m->off, m->len, m->att_lists, m->att_counts, B, S,
+      rc = launch_attention_tc(m->map_qkv_att, m->off, m->len, m->att_order, B, S,
                                c.num_heads, m->ctx, d->d_err, st);
     else
       rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st);
@@ -1197,7 +1171,7 @@ extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
   const int S = seq > 0 ? seq : m->cfg.max_seq_len;
   const bool tc =
-      m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD && S <= 512;
+      m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD;
   return 3 + (tc ? 1 : 0) + m->cfg.num_layers * (6 + attention_launches(tc ? 64 : 0, S));
 }
 
@@ -1287,7 +1261,7 @@ size_t static_scratch_need(const nebw_config &c, int64_t rows, int64_t batch) {
   return align256(R * H * 4) + align256(R * H * 4) + align256(R * H * 2) +
          align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * F * 2) +
          align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4) +
-         align256(3 * static_cast<size_t>(batch) * 4) + align256(4 * 4);
+         align256(static_cast<size_t>(batch) * 4);
 }
 
 }  // namespace
@@ -1336,8 +1310,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   v.h = reinterpret_cast<__nv_bfloat16 *>(carve(R * F * 2));
   v.len = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
   v.off = reinterpret_cast<int *>(carve((static_cast<size_t>(B) + 1) * 4));
-  v.att_lists = reinterpret_cast<int *>(carve(3 * static_cast<size_t>(B) * 4));
-  v.att_counts = reinterpret_cast<int *>(carve(4 * 4));
+  v.att_order = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
   v.rows_cap = rows;
   v.batch_cap = B;
   int rc;

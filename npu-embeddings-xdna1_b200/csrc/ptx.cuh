@@ -205,6 +205,17 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
          (static_cast<uint64_t>(2) << 61);
 }
 
+// Descriptor for an MN-major operand tile in the 128-byte-swizzled layout a
+// TMA load of [K rows x 64 MN-elements] produces: each K-row is 64 contiguous
+// bf16 (128 B), eight K-rows form a 1024-byte atom, atoms follow each other
+// along K (stride-dimension byte offset 1024).  MN extent 64 is one atom, so
+// the leading-dimension offset is not used.  Advancing K by 16 is +2048 B.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
 // Instruction descriptor for tcgen05.mma kind::f16 with bf16 A and B, fp32
 // D, both operands K-major, dense:
 //   bits 4-5 D format (1 = f32); 7-9 A format (1 = bf16); 10-12 B format
