@@ -1,8 +1,9 @@
 // Fused masked attention on the 5th-generation tensor cores (head_dim 64).
 //
-// One CTA per (128-query tile, head, sequence), flash-style over key blocks
-// of 128 with an online softmax, warp-specialised so that loads, tensor-core
-// products and the softmax of different key blocks overlap:
+// Persistent CTAs over (sequence, 128-query tile, head) work items,
+// flash-style over key blocks of 128 with an online softmax, warp-specialised
+// so that loads, tensor-core products and the softmax of different key
+// blocks (and of consecutive items) overlap:
 //
 //   warp 0      TMA: the Q tile once, then K_j and V_j blocks of the packed
 //               Q|K|V rows (128-byte swizzled) through a 2-stage ring
@@ -59,18 +60,34 @@ __device__ __forceinline__ T *smem_at(uint8_t *base, int off) {
   return reinterpret_cast<T *>(base + off);
 }
 
+// One unit of attention work: query tile `qt` of sequence `b` (all heads).
+// Encoded as (b << 8) | qt in the work list attn_work_kernel builds.
+struct AttnItem {
+  int b, qt;
+};
+
+__device__ __forceinline__ AttnItem attn_item(const int *items, int item, int qtiles) {
+  if (items) {
+    const int e = __ldg(items + item);
+    return {e >> 8, e & 255};
+  }
+  return {item / qtiles, item % qtiles};
+}
+
+// Persistent: each CTA walks work indices w = blockIdx.x, +gridDim.x, ...
+// over n_items x heads (w -> item w / heads, head w % heads), keeping the
+// load / product / softmax pipeline running across items.  With `items`
+// null, the items are every (b, qt < qtiles) and tiles past a sequence's
+// length are skipped.
 __global__ void __launch_bounds__(kAttnTcThreads, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const int *__restrict__ seq_off,
-                        const int *__restrict__ seq_len, const int *__restrict__ order, int H,
-                        __nv_bfloat16 *__restrict__ ctx, int *err) {
+                        const int *__restrict__ seq_len, const int *__restrict__ items,
+                        const int *__restrict__ items_count, int n_items_host, int qtiles,
+                        int heads, __nv_bfloat16 *__restrict__ ctx, int *err) {
   using S = AttnTcShape;
-  const int b = order ? __ldg(order + blockIdx.z) : blockIdx.z;
-  const int h = blockIdx.y;
-  const int L = __ldg(seq_len + b);
-  const int q0 = blockIdx.x * 128;
-  if (q0 >= L) return;
-  const int base = __ldg(seq_off + b);
-  const int nk = (L + 127) >> 7;
+  const int H = heads * kAttnTcD;
+  const int n_items = items_count ? __ldg(items_count) : n_items_host;
+  const int n_work = n_items * heads;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   if (reinterpret_cast<uintptr_t>(smem) & 1023) {  // swizzled tiles need 1 KB alignment
@@ -78,19 +95,20 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     return;
   }
   uint64_t *bars = smem_at<uint64_t>(smem, S::kBars);
-  uint64_t *q_full = bars + 0;
-  uint64_t *kv_full = bars + 1;   // [2]
-  uint64_t *kv_empty = bars + 3;  // [2]
-  uint64_t *s_full = bars + 5, *s_free = bars + 6;
-  uint64_t *p_full = bars + 7;
-  uint64_t *o_full = bars + 8, *o_free = bars + 9;
-  uint64_t *drain = bars + 10;
+  uint64_t *q_full = bars + 0, *q_free = bars + 1;
+  uint64_t *kv_full = bars + 2;   // [2]
+  uint64_t *kv_empty = bars + 4;  // [2]
+  uint64_t *s_full = bars + 6, *s_free = bars + 7;
+  uint64_t *p_full = bars + 8;
+  uint64_t *o_full = bars + 9, *o_free = bars + 10;
+  uint64_t *drain = bars + 11;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQKV);
     mbar_init(q_full, 1);
+    mbar_init(q_free, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(kv_full + s, 1);
       mbar_init(kv_empty + s, 1);
@@ -117,34 +135,43 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, 16384);
-      tma_load_2d(smem + S::kQ, &tmQKV, q_full, h * kAttnTcD, base + q0);
-      int j = 0;
-      for (; j < nk && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(kv_empty + s, ph ^ 1u, err)) {
+      int g = 0, t = 0;
+      for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+        const AttnItem it = attn_item(items, w / heads, qtiles);
+        const int h = w % heads;
+        const int L = __ldg(seq_len + it.b), q0 = it.qt * 128;
+        if (q0 >= L) continue;
+        const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
+        if (t > 0 && !mbar_wait(q_free, (t - 1) & 1, err)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(kv_full + s, 2 * 16384);
-        tma_load_2d(smem + S::kK0 + s * S::kStage, &tmQKV, kv_full + s, H + h * kAttnTcD,
-                    base + j * 128);
-        tma_load_2d(smem + S::kV0 + s * S::kStage, &tmQKV, kv_full + s, 2 * H + h * kAttnTcD,
-                    base + j * 128);
+        mbar_arrive_expect_tx(q_full, 16384);
+        tma_load_2d(smem + S::kQ, &tmQKV, q_full, h * kAttnTcD, base + q0);
+        ++t;
+        for (int j = 0; j < nk; ++j, ++g) {
+          const int s = g & 1;
+          if (!mbar_wait(kv_empty + s, ((g >> 1) & 1) ^ 1u, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(kv_full + s, 2 * 16384);
+          tma_load_2d(smem + S::kK0 + s * S::kStage, &tmQKV, kv_full + s, H + h * kAttnTcD,
+                      base + j * 128);
+          tma_load_2d(smem + S::kV0 + s * S::kStage, &tmQKV, kv_full + s, 2 * H + h * kAttnTcD,
+                      base + j * 128);
+        }
       }
       if (ok) {
         // every load issued has been consumed (so it landed) before exit
-        for (int t = 0; t < 2; ++t, ++j) {
-          const int s = j & 1;
-          if (!mbar_wait(kv_empty + s, ((j >> 1) & 1) ^ 1u, err)) break;
-        }
+        for (int k = 0; k < 2; ++k, ++g)
+          if (!mbar_wait(kv_empty + (g & 1), ((g >> 1) & 1) ^ 1u, err)) break;
+        if (t > 0) mbar_wait(q_free, (t - 1) & 1, err);
       } else {
-        // error path: at least let the loads in flight land
-        for (int t = j - 1; t >= 0 && t >= j - 2; --t)
-          mbar_wait(kv_full + (t & 1), (t >> 1) & 1, err);
+        for (int k = g - 1; k >= 0 && k >= g - 2; --k)
+          mbar_wait(kv_full + (k & 1), (k >> 1) & 1, err);
+        if (t > 0) mbar_wait(q_full, (t - 1) & 1, err);
       }
-      mbar_wait(q_full, 0, err);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -152,30 +179,43 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       constexpr uint32_t idS = idesc_bf16_f32(128, 128);
       constexpr uint32_t idO = idesc_bf16_f32(128, kAttnTcD) | (1u << 16);  // B (V) MN-major
       const uint32_t qa = smem_u32(smem + S::kQ), pa = smem_u32(smem + S::kP);
-      bool ok = mbar_wait(q_full, 0, err), issued = false;
-      for (int j = 0; j < nk && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        ok = mbar_wait(kv_full + s, ph, err) && (j == 0 || mbar_wait(s_free, (j - 1) & 1, err));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t ka = smem_u32(smem + S::kK0 + s * S::kStage);
+      bool ok = true, issued = false;
+      int g = 0, t = 0;
+      for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+        const AttnItem it = attn_item(items, w / heads, qtiles);
+        const int L = __ldg(seq_len + it.b);
+        if (it.qt * 128 >= L) continue;
+        const int nk = (L + 127) >> 7;
+        if (!mbar_wait(q_full, t & 1, err)) {
+          ok = false;
+          break;
+        }
+        ++t;
+        for (int j = 0; j < nk; ++j, ++g) {
+          const int s = g & 1;
+          ok = mbar_wait(kv_full + s, (g >> 1) & 1, err) &&
+               (g == 0 || mbar_wait(s_free, (g - 1) & 1, err));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t ka = smem_u32(smem + S::kK0 + s * S::kStage);
 #pragma unroll
-        for (int k = 0; k < kAttnTcD / 16; ++k)
-          umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS,
-                    k > 0 ? 1u : 0u);
-        umma_commit(s_full);
-        issued = true;
-        ok = mbar_wait(p_full, j & 1, err) && (j == 0 || mbar_wait(o_free, (j - 1) & 1, err));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t va = smem_u32(smem + S::kV0 + s * S::kStage);
+          for (int k = 0; k < kAttnTcD / 16; ++k)
+            umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS,
+                      k > 0 ? 1u : 0u);
+          umma_commit(s_full);
+          if (j == nk - 1) umma_commit(q_free);  // this item's Q is no longer read
+          issued = true;
+          ok = mbar_wait(p_full, g & 1, err) && (g == 0 || mbar_wait(o_free, (g - 1) & 1, err));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t va = smem_u32(smem + S::kV0 + s * S::kStage);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
-                    sdesc_mnmajor_sw128(va + ks * 2048), idO, ks > 0 ? 1u : 0u);
-        umma_commit(o_full);
-        umma_commit(kv_empty + s);
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
+                      sdesc_mnmajor_sw128(va + ks * 2048), idO, ks > 0 ? 1u : 0u);
+          umma_commit(o_full);
+          umma_commit(kv_empty + s);
+        }
       }
       if (issued) {
         umma_commit(drain);
@@ -188,103 +228,116 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     const int r = (warp & 3) * 32 + lane;  // TMEM lane = query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint8_t *prow = smem + S::kP + r * 128;
-    float o[kAttnTcD];
-#pragma unroll
-    for (int i = 0; i < kAttnTcD; ++i) o[i] = 0.f;
-    float m_prev = -INFINITY, m_prev2 = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nk && ok; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, err))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int kbase = j * 128;
-      const bool partial = kbase + 128 > L;
-      // pass 1: row max of this key block
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
-        tmem_wait_ld_regs(v);
-        if (partial) {
+    int g = 0;
+    for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+      const AttnItem it = attn_item(items, w / heads, qtiles);
+      const int h = w % heads;
+      const int L = __ldg(seq_len + it.b), q0 = it.qt * 128;
+      if (q0 >= L) continue;
+      const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
+      float o[kAttnTcD];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (kbase + c * 32 + i < L) mx = fmaxf(mx, __uint_as_float(v[i]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
-        }
-      }
-      const float m_new = fmaxf(m_prev, mx);
-      // fold in the previous block's P V (its products used m_prev)
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, err))) {
+      for (int i = 0; i < kAttnTcD; ++i) o[i] = 0.f;
+      float m_prev = -INFINITY, m_prev2 = -INFINITY, l = 0.f;
+      for (int j = 0; j < nk; ++j, ++g) {
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full, g & 1, err))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t va[32], vb[32];
-        tmem_ld_32x32b_x32(tO + lane_off, va);
-        tmem_ld_32x32b_x32(tO + lane_off + 32, vb);
-        tmem_wait_ld_regs(va);
-        tmem_wait_ld_regs(vb);
-        const float sc = exp2f((m_prev2 - m_prev) * kLog2e);
+        const int kbase = j * 128;
+        const bool partial = kbase + 128 > L;
+        // pass 1: row max of this key block
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
+          tmem_wait_ld_regs(v);
+          if (partial) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          o[i] = fmaf(o[i], sc, __uint_as_float(va[i]));
-          o[32 + i] = fmaf(o[32 + i], sc, __uint_as_float(vb[i]));
+            for (int i = 0; i < 32; ++i)
+              if (kbase + c * 32 + i < L) mx = fmaxf(mx, __uint_as_float(v[i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+          }
+        }
+        const float m_new = fmaxf(m_prev, mx);
+        // fold in the previous block's P V (its products used m_prev)
+        if (j > 0) {
+          if (!__all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t va[32], vb[32];
+          tmem_ld_32x32b_x32(tO + lane_off, va);
+          tmem_ld_32x32b_x32(tO + lane_off + 32, vb);
+          tmem_wait_ld_regs(va);
+          tmem_wait_ld_regs(vb);
+          const float sc = exp2f((m_prev2 - m_prev) * kLog2e);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            o[i] = fmaf(o[i], sc, __uint_as_float(va[i]));
+            o[32 + i] = fmaf(o[32 + i], sc, __uint_as_float(vb[i]));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free);
+        }
+        // pass 2: p, running sum, P (bf16) into the shared A tile
+        const float m2 = m_new * kLog2e;
+        l *= exp2f((m_prev - m_new) * kLog2e);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
+          tmem_wait_ld_regs(v);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int kj = kbase + c * 32 + 2 * i;
+            float p0 = exp2f(fmaf(__uint_as_float(v[2 * i]), kLog2e, -m2));
+            float p1 = exp2f(fmaf(__uint_as_float(v[2 * i + 1]), kLog2e, -m2));
+            if (partial) {
+              p0 = kj < L ? p0 : 0.f;
+              p1 = kj + 1 < L ? p1 : 0.f;
+            }
+            l += p0 + p1;
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          uint8_t *blk = prow + (c >> 1) * 16384;
+          const int p0 = (c & 1) * 4;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4 *>(blk + (((p0 + q) ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
         tc_fence_before();
+        fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(o_free);
-      }
-      // pass 2: p, running sum, P (bf16) into the shared A tile
-      const float m2 = m_new * kLog2e;
-      l *= exp2f((m_prev - m_new) * kLog2e);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
-        tmem_wait_ld_regs(v);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int kj = kbase + c * 32 + 2 * i;
-          float p0 = exp2f(fmaf(__uint_as_float(v[2 * i]), kLog2e, -m2));
-          float p1 = exp2f(fmaf(__uint_as_float(v[2 * i + 1]), kLog2e, -m2));
-          if (partial) {
-            p0 = kj < L ? p0 : 0.f;
-            p1 = kj + 1 < L ? p1 : 0.f;
-          }
-          l += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
+        if (lane == 0) {
+          mbar_arrive(s_free);  // S read: the next QK^T may overwrite it
+          mbar_arrive(p_full);  // P written: O_j = P_j V_j may start
         }
-        uint8_t *blk = prow + (c >> 1) * 16384;
-        const int p0 = (c & 1) * 4;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4 *>(blk + (((p0 + q) ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        m_prev2 = m_prev;
+        m_prev = m_new;
       }
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);  // S read: the next QK^T may overwrite it
-        mbar_arrive(p_full);  // P written: O_j = P_j V_j may start
+      if (!ok || !__all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, err))) {
+        ok = false;
+        break;
       }
-      m_prev2 = m_prev;
-      m_prev = m_new;
-    }
-    if (ok && __all_sync(0xffffffffu, mbar_wait(o_full, (nk - 1) & 1, err))) {
       tc_fence_after();
       uint32_t va[32], vb[32];
       tmem_ld_32x32b_x32(tO + lane_off, va);
       tmem_ld_32x32b_x32(tO + lane_off + 32, vb);
       tmem_wait_ld_regs(va);
       tmem_wait_ld_regs(vb);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);  // the next item's first P V may overwrite O
       const float sc = exp2f((m_prev2 - m_prev) * kLog2e);
       const float inv = 1.0f / l;
 #pragma unroll
@@ -313,30 +366,35 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   }
 }
 
-// Launch order for the attention grid: the sequences sorted into length
-// classes, longest class first (L > 256, then > 128, then the rest), so the
-// heaviest CTAs start first and the tail of the launch is short work.
-// One CTA, B <= 65535.
+// The attention work list: one item per (sequence, 128-query tile), longest
+// length class first (L > 256, then > 128, then the rest) so that the
+// heaviest items start first and the tail of the persistent loop is short
+// work; items[k] = (b << 8) | qt, count[0] = the number of items.
+// One CTA, B <= 65535, L <= 32767.
 __global__ void __launch_bounds__(1024)
-    attn_order_kernel(const int *__restrict__ seq_len, int B, int *__restrict__ order) {
+    attn_work_kernel(const int *__restrict__ seq_len, int B, int *__restrict__ items,
+                     int *__restrict__ count) {
   __shared__ int cnt[3], start[3];
   if (threadIdx.x < 3) cnt[threadIdx.x] = 0;
   __syncthreads();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int L = seq_len[b];
-    atomicAdd(&cnt[L > 256 ? 0 : (L > 128 ? 1 : 2)], 1);
+    atomicAdd(&cnt[L > 256 ? 0 : (L > 128 ? 1 : 2)], (L + 127) >> 7);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     start[0] = 0;
     start[1] = cnt[0];
     start[2] = cnt[0] + cnt[1];
+    count[0] = cnt[0] + cnt[1] + cnt[2];
   }
   __syncthreads();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int L = seq_len[b];
     const int k = L > 256 ? 0 : (L > 128 ? 1 : 2);
-    order[atomicAdd(&start[k], 1)] = b;
+    const int nq = (L + 127) >> 7;
+    const int at = atomicAdd(&start[k], nq);
+    for (int q = 0; q < nq; ++q) items[at + q] = (b << 8) | q;
   }
 }
 

@@ -393,18 +393,22 @@ int launch_attention(const __nv_bfloat16 *qkv, const int *off, const int *len, i
   return NEBW_OK;
 }
 
-// tcgen05 attention for head_dim 64: one launch over (128-query tiles,
-// heads, sequences), in the longest-first order `order` gives (or request
-// order when it is null).
-int launch_attention_tc(const CUtensorMap &map, const int *off, const int *len, const int *order,
-                        int B, int max_len, int heads, __nv_bfloat16 *ctx, int *err,
-                        cudaStream_t st) {
-  NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0,
+// tcgen05 attention for head_dim 64: a persistent launch (two CTAs per SM)
+// over the work items -- the device-built, longest-first list `items` with
+// its count `items_count`, or, when `items` is null, every (sequence,
+// 128-query tile < max_len) pair.
+int launch_attention_tc(nebw_dev *d, const CUtensorMap &map, const int *off, const int *len,
+                        const int *items, const int *items_count, int B, int max_len, int heads,
+                        __nv_bfloat16 *ctx, cudaStream_t st) {
+  NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0 &&
+                   max_len <= 32767,
                "attention grid refused (B %d, heads %d, max_len %d)", B, heads, max_len);
-  const int H = heads * nebw::kAttnTcD;
-  const dim3 grid((max_len + 127) / 128, heads, B);
+  const int qtiles = (max_len + 127) / 128;
+  const int64_t n_items = static_cast<int64_t>(B) * qtiles;
+  NEBW_REQUIRE(n_items * heads < (1ll << 31), "attention work too large");
+  const dim3 grid(2 * d->sm_count);
   nebw::attention_tc_kernel<<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape::kSmemBytes, st>>>(
-      map, off, len, order, H, ctx, err);
+      map, off, len, items, items_count, static_cast<int>(n_items), qtiles, heads, ctx, d->d_err);
   NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }
@@ -681,8 +685,8 @@ extern "C" int nebw_attention(nebw_dev *d, const void *qkv, int64_t rows, const 
     CUtensorMap map;
     if (int rc = make_tmap_kmajor(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 128))
       return rc;
-    return launch_attention_tc(map, off, len, nullptr, B, max_len, heads,
-                               static_cast<__nv_bfloat16 *>(ctx), d->d_err, pick_stream(d, stream));
+    return launch_attention_tc(d, map, off, len, nullptr, nullptr, B, max_len, heads,
+                               static_cast<__nv_bfloat16 *>(ctx), pick_stream(d, stream));
   }
   return launch_attention(static_cast<const __nv_bfloat16 *>(qkv), off, len, B, max_len, heads, hd,
                           static_cast<__nv_bfloat16 *>(ctx), pick_stream(d, stream));
@@ -750,7 +754,7 @@ struct nebw_model {
   float *x = nullptr, *y = nullptr;  // residual stream, sublayer output
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
-  int *att_order = nullptr;  // sequences, longest length class first [B]
+  int *att_items = nullptr;  // attention work list (longest first) [B * S/128 + 1]
   CUtensorMap map_qkv_att;  // Q|K|V rows as 64 x 128 TMA tiles for attention
   float *out = nullptr;
   CUtensorMap map_a, map_ctx, map_h;          // GEMM A operands (TMA loads)
@@ -776,12 +780,12 @@ void free_workspace(nebw_model *m) {
   cudaFree(m->len_in);
   cudaFree(m->len);
   cudaFree(m->off);
-  cudaFree(m->att_order);
+  cudaFree(m->att_items);
   cudaFree(m->out);
   m->x = m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
   m->ids = m->len_in = m->len = m->off = nullptr;
-  m->att_order = nullptr;
+  m->att_items = nullptr;
   m->out = nullptr;
   m->rows_cap = m->batch_cap = m->ids_cap = 0;
 }
@@ -811,7 +815,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len_in), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->off), (Bc + 1) * 4);
-  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_order), Bc * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_items), (R / 128 + Bc + 1) * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->out), Bc * H * 4);
   if (rc) {
     free_workspace(m);
@@ -889,7 +893,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   const bool tc_attention =
       d->attn_kind == NEBW_ATTN_TCGEN05 && c.head_dim == nebw::kAttnTcD;
   if (tc_attention) {
-    nebw::attn_order_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_order);
+    nebw::attn_work_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_items + 1, m->att_items);
     NEBW_CUDA(cudaGetLastError());
   }
   if ((rc = prof_mark(m, NEBW_K_EMBED_LN, st))) return rc;
@@ -915,8 +919,8 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     // attention
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if (tc_attention)
-      rc = launch_attention_tc(m->map_qkv_att, m->off, m->len, m->att_order, B, S,
-                               c.num_heads, m->ctx, d->d_err, st);
+      rc = launch_attention_tc(d, m->map_qkv_att, m->off, m->len, m->att_items + 1, m->att_items, B, S,
+                               c.num_heads, m->ctx, st);
     else
       rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st);
     if (rc)
@@ -1261,7 +1265,7 @@ size_t static_scratch_need(const nebw_config &c, int64_t rows, int64_t batch) {
   return align256(R * H * 4) + align256(R * H * 4) + align256(R * H * 2) +
          align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * F * 2) +
          align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4) +
-         align256(static_cast<size_t>(batch) * 4);
+         align256((R / 128 + static_cast<size_t>(batch) + 1) * 4);
 }
 
 }  // namespace
@@ -1310,7 +1314,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   v.h = reinterpret_cast<__nv_bfloat16 *>(carve(R * F * 2));
   v.len = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
   v.off = reinterpret_cast<int *>(carve((static_cast<size_t>(B) + 1) * 4));
-  v.att_order = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
+  v.att_items = reinterpret_cast<int *>(carve((R / 128 + static_cast<size_t>(B) + 1) * 4));
   v.rows_cap = rows;
   v.batch_cap = B;
   int rc;
