@@ -20,7 +20,7 @@ import numpy as np
 
 PKG_DIR = Path(__file__).resolve().parent.parent          # npu-embeddings-xdna1_b200/
 REPO_DIR = PKG_DIR.parent
-LIB_PATH = PKG_DIR / "libnebw.so"
+LIB_PATH = Path(os.environ["NEBW_LIB"]) if os.environ.get("NEBW_LIB") else PKG_DIR / "libnebw.so"
 HEADER_PATH = REPO_DIR / "include" / "nebw.h"
 
 F32, BF16 = 0, 1
