@@ -389,8 +389,9 @@ def gpu_arm(args, cfg):
         att_fl = 4.0 * L2_s * Hf * L
         kernels["attention"]["tflops"] = att_fl / (pms["attention"] / steps / 1e3) / 1e12
         kernels["attention"]["frac_of_peak"] = kernels["attention"]["tflops"] / peak_t
-        # read x and y (fp32), write x (fp32) and the bf16 copy: 14 B/element, 2 per layer
-        ln_bytes = T_s * Hf * (4 + 4 + 4 + 2) * 2 * L
+        # read x (fp32) and y (bf16), write x (fp32) and the bf16 copy: 12 B/element,
+        # 2 per layer
+        ln_bytes = T_s * Hf * (4 + 2 + 4 + 2) * 2 * L
         kernels["layernorm"]["gbs"] = ln_bytes / (pms["layernorm"] / steps / 1e3) / 1e9
         kernels["layernorm"]["frac_of_peak"] = kernels["layernorm"]["gbs"] / peaks["hbm_gbs"]
         # the dominant kernel: the FFN-up GEMM (T x 1024 -> 4096, bias + gelu8, bf16 out)
@@ -469,7 +470,7 @@ def main():
     ap.add_argument("--impl", choices=["nebw", "reference"], default="nebw")
     ap.add_argument("--config", default="bge-large", choices=sorted(synth.CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--attention", choices=["mma", "tcgen05"], default="mma",
+    ap.add_argument("--attention", choices=["mma", "tcgen05"], default="tcgen05",
                     help="attention kernel for head_dim 64")
     args = ap.parse_args()
     if args.warmup < 3:

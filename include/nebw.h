@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NEBW_ABI_VERSION 1
+#define NEBW_ABI_VERSION 2
 
 typedef enum nebw_status {
   NEBW_OK = 0,
@@ -73,9 +73,11 @@ int nebw_device_info(nebw_dev *dev, int *sm_count, int *cc_major, int *cc_minor)
 
 /* Which attention kernel a device handle uses for head_dim 64 (no
  * counterpart in the reference, which has one host path):
- * NEBW_ATTN_MMA -- flash attention on mma.sync (the default);
- * NEBW_ATTN_TCGEN05 -- S and P.V on tcgen05 UMMA with TMEM accumulators.
- * Both give results within the same parity tolerance. */
+ * NEBW_ATTN_TCGEN05 -- S and P.V on tcgen05 UMMA with TMEM accumulators,
+ *   persistent CTAs over a longest-first work list (the default);
+ * NEBW_ATTN_MMA -- flash attention on mma.sync.
+ * Both give results within the same parity tolerance; head_dim 32 always
+ * runs on mma.sync. */
 enum { NEBW_ATTN_MMA = 0, NEBW_ATTN_TCGEN05 = 1 };
 int nebw_set_attention_kernel(nebw_dev *dev, int kind);
 
@@ -109,10 +111,11 @@ int nebw_gemm(nebw_dev *dev, uint64_t weight, const void *A, int64_t M, int64_t 
 /* LayerNorm over rows of width H, in place: x = LN(x + y) (y may be NULL).
  * Replaces layer_norm / layer_norm_cpu / add_norm_bf16
  * (bert_encoder.cpp:370-463, :1304-1361; kernels/layernorm{,_rne}.cc):
- * two-pass fp32, biased variance, eps inside the square root.  If a_bf16 is
- * not NULL the normalised rows are also written as bf16 RNE (the next
- * GEMM's A).  H % 128 == 0, H <= 2048. */
-int nebw_layernorm(nebw_dev *dev, float *x, const float *y, const float *gamma,
+ * two-pass fp32, biased variance, eps inside the square root.  y is fp32
+ * (y_dtype NEBW_F32) or a bf16 GEMM output (NEBW_BF16), widened exactly;
+ * x is fp32.  If a_bf16 is not NULL the normalised rows are also written as
+ * bf16 RNE (the next GEMM's A).  H % 128 == 0, H <= 2048. */
+int nebw_layernorm(nebw_dev *dev, float *x, const void *y, int y_dtype, const float *gamma,
                    const float *beta, float eps, int64_t rows, int64_t H, void *a_bf16,
                    void *stream);
 

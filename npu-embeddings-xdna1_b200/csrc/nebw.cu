@@ -9,11 +9,15 @@
 //   per layer L:
 //     gemm QKV     qkv = bf16(a . Wqkv + b)
 //     attention    ctx = softmax(Q K^T) V           (per sequence, per head)
-//     gemm AO      y   = ctx . Wao + b               (fp32)
+//     gemm AO      y   = bf16(ctx . Wao + b)
 //     layernorm    x   = LN1(y + x);  a = bf16(x)   (add_into + layer_norm)
 //     gemm UP      h   = bf16(gelu(a . Wup + b))
-//     gemm DOWN    y   = h . Wdn + b
+//     gemm DOWN    y   = bf16(h . Wdn + b)
 //     layernorm    x   = LN2(y + x);  a = bf16(x)
+//
+// Every GEMM output is narrowed to bf16 RNE as the reference's array path
+// does (kernels/narrow_f32_bf16.cc:50-90, run on each GEMM C tile); the
+// residual stream x and the LayerNorm arithmetic stay fp32.
 //   pool_l2        out = normalise(pool(x))
 //
 // Nothing in a pass needs the host to know T: every kernel bounds itself by
@@ -172,7 +176,7 @@ struct nebw_dev {
   int gemm_pairs = 0;
   // attention kernel for head_dim 64: NEBW_ATTN_MMA (mma.sync flash) or
   // NEBW_ATTN_TCGEN05 (UMMA/TMEM); see nebw_set_attention_kernel
-  int attn_kind = NEBW_ATTN_MMA;
+  int attn_kind = NEBW_ATTN_TCGEN05;
 };
 
 namespace {
@@ -321,14 +325,19 @@ int launch_gemm(nebw_dev *d, const Weight &w, const CUtensorMap &mA128, const CU
 }
 
 template <int NV>
-void launch_ln_nv(float *x, const float *y, const float *g, const float *b, float eps, int rows,
-                  const int *rows_dev, __nv_bfloat16 *a, cudaStream_t st) {
+void launch_ln_nv(float *x, const void *y, bool y_bf16, const float *g, const float *b, float eps,
+                  int rows, const int *rows_dev, __nv_bfloat16 *a, cudaStream_t st) {
   const int grid = (rows + nebw::kRowWarps - 1) / nebw::kRowWarps;
-  nebw::layernorm_kernel<NV><<<grid, nebw::kRowWarps * 32, 0, st>>>(x, y, g, b, eps, rows, rows_dev, a);
+  if (y_bf16)
+    nebw::layernorm_kernel<NV, __nv_bfloat16><<<grid, nebw::kRowWarps * 32, 0, st>>>(
+        x, static_cast<const __nv_bfloat16 *>(y), g, b, eps, rows, rows_dev, a);
+  else
+    nebw::layernorm_kernel<NV, float><<<grid, nebw::kRowWarps * 32, 0, st>>>(
+        x, static_cast<const float *>(y), g, b, eps, rows, rows_dev, a);
 }
 
-int launch_layernorm(float *x, const float *y, const float *g, const float *b, float eps,
-                     int64_t rows, int64_t H, const int *rows_dev, __nv_bfloat16 *a,
+int launch_layernorm(float *x, const void *y, bool y_bf16, const float *g, const float *b,
+                     float eps, int64_t rows, int64_t H, const int *rows_dev, __nv_bfloat16 *a,
                      cudaStream_t st) {
   NEBW_REQUIRE(H % 128 == 0 && H >= 128 && H <= 2048,
                "LayerNorm width %lld refused: a multiple of 128 up to 2048 is required",
@@ -337,7 +346,7 @@ int launch_layernorm(float *x, const float *y, const float *g, const float *b, f
   const int r = static_cast<int>(rows);
   switch (H / 128) {
 #define NEBW_LN_CASE(n) \
-  case n: launch_ln_nv<n>(x, y, g, b, eps, r, rows_dev, a, st); break;
+  case n: launch_ln_nv<n>(x, y, y_bf16, g, b, eps, r, rows_dev, a, st); break;
     NEBW_LN_CASE(1) NEBW_LN_CASE(2) NEBW_LN_CASE(3) NEBW_LN_CASE(4) NEBW_LN_CASE(5)
     NEBW_LN_CASE(6) NEBW_LN_CASE(7) NEBW_LN_CASE(8) NEBW_LN_CASE(9) NEBW_LN_CASE(10)
     NEBW_LN_CASE(11) NEBW_LN_CASE(12) NEBW_LN_CASE(13) NEBW_LN_CASE(14) NEBW_LN_CASE(15)
@@ -665,13 +674,14 @@ extern "C" int nebw_gemm(nebw_dev *d, uint64_t weight, const void *A, int64_t M,
                      pick_stream(d, stream));
 }
 
-extern "C" int nebw_layernorm(nebw_dev *d, float *x, const float *y, const float *gamma,
-                              const float *beta, float eps, int64_t rows, int64_t H, void *a_bf16,
-                              void *stream) {
+extern "C" int nebw_layernorm(nebw_dev *d, float *x, const void *y, int y_dtype,
+                              const float *gamma, const float *beta, float eps, int64_t rows,
+                              int64_t H, void *a_bf16, void *stream) {
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(x && gamma && beta, "null LayerNorm operand");
+  NEBW_REQUIRE(y_dtype == NEBW_F32 || y_dtype == NEBW_BF16, "y dtype %d refused", y_dtype);
   NEBW_REQUIRE(rows >= 0 && rows < (1ll << 31) / 2, "rows %lld refused", static_cast<long long>(rows));
-  return launch_layernorm(x, y, gamma, beta, eps, rows, H, nullptr,
+  return launch_layernorm(x, y, y_dtype == NEBW_BF16, gamma, beta, eps, rows, H, nullptr,
                           static_cast<__nv_bfloat16 *>(a_bf16), pick_stream(d, stream));
 }
 
@@ -751,7 +761,8 @@ struct nebw_model {
   std::map<std::string, bool> staged;  // container name -> set
   // workspace (capacity rows_cap = B * S of the largest call so far)
   int64_t rows_cap = 0, batch_cap = 0, ids_cap = 0;
-  float *x = nullptr, *y = nullptr;  // residual stream, sublayer output
+  float *x = nullptr;                 // residual stream (fp32)
+  __nv_bfloat16 *y = nullptr;         // sublayer output: AO / FFN-down GEMM, RNE bf16
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
   int *att_items = nullptr;  // attention work list (longest first) [B * S/128 + 1]
@@ -782,7 +793,8 @@ void free_workspace(nebw_model *m) {
   cudaFree(m->off);
   cudaFree(m->att_items);
   cudaFree(m->out);
-  m->x = m->y = nullptr;
+  m->x = nullptr;
+  m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
   m->ids = m->len_in = m->len = m->off = nullptr;
   m->att_items = nullptr;
@@ -806,7 +818,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   };
   int rc = 0;
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->x), R * H * 4);
-  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->y), R * H * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->y), R * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->a), R * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->qkv), R * 3 * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ctx), R * H * 2);
@@ -828,7 +840,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   if ((rc = make_tmap_kmajor(&m->map_ctx, m->ctx, R, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_h, m->h, R, F, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_out(&m->out_qkv, m->qkv, R, 3 * H, true))) return rc;
-  if ((rc = make_tmap_out(&m->out_y, m->y, R, H, false))) return rc;
+  if ((rc = make_tmap_out(&m->out_y, m->y, R, H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
   return NEBW_OK;
@@ -932,9 +944,9 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->y;
     if ((rc = prof_mark(m, NEBW_K_GEMM_AO, st))) return rc;
-    if ((rc = launch_gemm(d, w.ao, m->map_ctx, m->out_y, nebw::kEpiF32, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.ao, m->map_ctx, m->out_y, nebw::kEpiBf16, a, st))) return rc;
     if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
-    if ((rc = launch_layernorm(m->x, m->y, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
+    if ((rc = launch_layernorm(m->x, m->y, true, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
                                m->a, st)))
       return rc;
     // FFN up + bias + GELU -> bf16
@@ -952,9 +964,9 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->y;
     if ((rc = prof_mark(m, NEBW_K_GEMM_DOWN, st))) return rc;
-    if ((rc = launch_gemm(d, w.dn, m->map_h, m->out_y, nebw::kEpiF32, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.dn, m->map_h, m->out_y, nebw::kEpiBf16, a, st))) return rc;
     if ((rc = prof_mark(m, NEBW_K_LN, st))) return rc;
-    if ((rc = launch_layernorm(m->x, m->y, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
+    if ((rc = launch_layernorm(m->x, m->y, true, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H, T_dev,
                                L + 1 < c.num_layers ? m->a : nullptr, st)))
       return rc;
   }
@@ -1307,7 +1319,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
     return q;
   };
   v.x = reinterpret_cast<float *>(carve(R * H * 4));
-  v.y = reinterpret_cast<float *>(carve(R * H * 4));
+  v.y = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
   v.a = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
   v.qkv = reinterpret_cast<__nv_bfloat16 *>(carve(R * 3 * H * 2));
   v.ctx = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
@@ -1322,7 +1334,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   if ((rc = make_tmap_kmajor(&v.map_ctx, v.ctx, rows, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_h, v.h, rows, F, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_out(&v.out_qkv, v.qkv, rows, 3 * H, true))) return rc;
-  if ((rc = make_tmap_out(&v.out_y, v.y, rows, H, false))) return rc;
+  if ((rc = make_tmap_out(&v.out_y, v.y, rows, H, true))) return rc;
   if ((rc = make_tmap_out(&v.out_h, v.h, rows, F, true))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_qkv_att, v.qkv, rows, 3 * H, 128))) return rc;
   return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));

@@ -101,10 +101,21 @@ __device__ __forceinline__ void ln_row_regs(float4 (&v)[NV], const float *__rest
   }
 }
 
+// Four consecutive elements of a GEMM output row, widened to fp32.
+__device__ __forceinline__ float4 load4(const float *p) {
+  return *reinterpret_cast<const float4 *>(p);
+}
+__device__ __forceinline__ float4 load4(const __nv_bfloat16 *p) {
+  const uint2 u = *reinterpret_cast<const uint2 *>(p);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
 // x[r] = LN(x[r] (+ y[r])) for r < T; also a[r] = bf16(x[r]) when a != null.
-template <int NV>
+// y is the GEMM output (fp32, or bf16 after the RNE narrow); x stays fp32.
+template <int NV, typename YT>
 __global__ void __launch_bounds__(kRowWarps * 32)
-    layernorm_kernel(float *__restrict__ x, const float *__restrict__ y,
+    layernorm_kernel(float *__restrict__ x, const YT *__restrict__ y,
                      const float *__restrict__ g, const float *__restrict__ bta, float eps,
                      int rows, const int *__restrict__ rows_dev, __nv_bfloat16 *__restrict__ a) {
   const int H = NV * 128;
@@ -120,7 +131,7 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     const int c = (i * 32 + lane) * 4;
     v[i] = *reinterpret_cast<const float4 *>(xr + c);
     if (y) {
-      const float4 w = *reinterpret_cast<const float4 *>(y + static_cast<int64_t>(row) * H + c);
+      const float4 w = load4(y + static_cast<int64_t>(row) * H + c);
       v[i].x = w.x + v[i].x;
       v[i].y = w.y + v[i].y;
       v[i].z = w.z + v[i].z;

@@ -75,7 +75,7 @@ def lib() -> C.CDLL:
         "nebw_stage_weight": ([vp, vp, C.c_int, i64, i64, C.POINTER(C.c_uint64)], C.c_int),
         "nebw_release_weight": ([vp, C.c_uint64], C.c_int),
         "nebw_gemm": ([vp, C.c_uint64, vp, i64, i64, i64, vp, vp, C.c_int, vp, C.c_int, vp], C.c_int),
-        "nebw_layernorm": ([vp, vp, vp, vp, vp, C.c_float, i64, i64, vp, vp], C.c_int),
+        "nebw_layernorm": ([vp, vp, vp, C.c_int, vp, vp, C.c_float, i64, i64, vp, vp], C.c_int),
         "nebw_attention": ([vp, vp, i64, vp, vp, i32, i32, i32, i32, vp, vp], C.c_int),
         "nebw_pack_offsets": ([vp, vp, i32, i32, vp, vp, vp], C.c_int),
         "nebw_embed_ln": ([vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, vp, vp, C.c_float, i32, vp,
@@ -201,9 +201,13 @@ class Device:
         _check(lib().nebw_gemm(self.h, weight, _addr(A), M, K, N, _addr(bias), _addr(residual),
                                act, _addr(C_out), c_dtype, self._s(stream)))
 
-    def layernorm(self, x, gamma, beta, rows, H, y=None, a_bf16=None, eps=1e-12, stream=None):
-        _check(lib().nebw_layernorm(self.h, _addr(x), _addr(y), _addr(gamma), _addr(beta), eps,
-                                    rows, H, _addr(a_bf16), self._s(stream)))
+    def layernorm(self, x, gamma, beta, rows, H, y=None, a_bf16=None, eps=1e-12, stream=None,
+                  y_dtype=None):
+        """x = LN(x + y) in place; y_dtype defaults to y's own (torch bf16 -> BF16, else F32)."""
+        if y_dtype is None:
+            y_dtype = BF16 if str(getattr(y, "dtype", "")) == "torch.bfloat16" else F32
+        _check(lib().nebw_layernorm(self.h, _addr(x), _addr(y), y_dtype, _addr(gamma),
+                                    _addr(beta), eps, rows, H, _addr(a_bf16), self._s(stream)))
 
     def attention(self, qkv, rows, seq_off, seq_len, B, max_len, heads, head_dim, ctx, stream=None):
         _check(lib().nebw_attention(self.h, _addr(qkv), rows, _addr(seq_off), _addr(seq_len), B,

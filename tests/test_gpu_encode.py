@@ -85,23 +85,24 @@ def test_bge_base_geometry_vs_oracle(device, port_oracle):
     m.close()
 
 
-def test_tcgen05_attention_encoder_vs_oracle(device, port_oracle):
-    """The whole pass with the tcgen05 attention kernel and its length
-    buckets (<=128, <=256, <=512 all present)."""
+@pytest.mark.parametrize("kind", [0, 1])
+def test_attention_kind_encoder_vs_oracle(device, port_oracle, kind):
+    """The whole pass with each attention kernel (0 mma.sync, 1 tcgen05, the
+    default) over 128-key block boundaries (<=128, <=256, <=512 all present)."""
     import nebw
     from nebw import synth
     w = synth.make_weights(synth.BGE_BASE, seed=19, cls_pool=True, layers=2)
     lens = np.array([512, 300, 8, 129, 128, 1, 256, 257], np.int32)
     ids, mask = synth.make_tokens(len(lens), 512, lens, seed=20)
-    device.set_attention_kernel(1)
+    device.set_attention_kernel(kind)
     try:
         m = nebw.Model.from_weights(device, w, max_seq_len=512)
         got = m.encode(ids, lens)
         m.close()
     finally:
-        device.set_attention_kernel(0)
+        device.set_attention_kernel(device.ATTN_TCGEN05)
     want = port_oracle.encode(w, ids, mask)
-    check(got, want, "tcgen05 attention")
+    check(got, want, f"attention kind {kind}")
 
 
 def test_npue_container_roundtrip(device, port_oracle, minilm, tmp_path):

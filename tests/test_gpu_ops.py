@@ -130,6 +130,31 @@ def test_layernorm(device, port_oracle, H):
     np.testing.assert_array_equal(host_bits(a_d), port_oracle.to_bf16(got))
 
 
+@pytest.mark.parametrize("y_bf16", [False, True])
+def test_add_layernorm(device, port_oracle, y_bf16):
+    """x = LN(x + y): y as an fp32 or a bf16 GEMM output, widened exactly."""
+    rng = np.random.default_rng(11 + y_bf16)
+    rows, H = 777, 1024
+    x = rng.standard_normal((rows, H)).astype(np.float32)
+    y = (rng.standard_normal((rows, H)) * 2).astype(np.float32)
+    g = rng.standard_normal(H).astype(np.float32)
+    b = rng.standard_normal(H).astype(np.float32)
+    if y_bf16:
+        y_d = torch.from_numpy(y).to(torch.bfloat16).cuda()
+        y_host = y_d.float().cpu().numpy()
+    else:
+        y_d = dev_tensor(y)
+        y_host = y
+    x_d = dev_tensor(x)
+    a_d = torch.empty((rows, H), dtype=torch.bfloat16, device="cuda")
+    device.layernorm(x_d, dev_tensor(g), dev_tensor(b), rows, H, y=y_d, a_bf16=a_d)
+    device.sync()
+    got = x_d.cpu().numpy()
+    want = port_oracle.layer_norm(y_host + x, g, b)
+    assert np.abs(got - want).max() <= 2e-5 * np.abs(want).max()
+    np.testing.assert_array_equal(host_bits(a_d), port_oracle.to_bf16(got))
+
+
 def test_pack_offsets_bit_exact(device):
     rng = np.random.default_rng(3)
     for B in (1, 7, 1024, 5000):
@@ -175,7 +200,7 @@ def test_attention_matches_float64(device, D, heads, kind):
                          heads, D, ctx)
         device.sync()
     finally:
-        device.set_attention_kernel(0)
+        device.set_attention_kernel(device.ATTN_TCGEN05)
     got = bits_to_f32(host_bits(ctx)).astype(np.float64)
     q = bits_to_f32(qkv).astype(np.float64)
     for b, L in enumerate(lens):
