@@ -1,21 +1,33 @@
 // Fused masked attention on the 5th-generation tensor cores (head_dim 64).
 //
 // Persistent CTAs over (sequence, 128-query tile, head) work items,
-// flash-style over key blocks of 128 with an online softmax, warp-specialised
-// so that loads, tensor-core products and the softmax of different key
-// blocks (and of consecutive items) overlap:
+// flash-style over key blocks of up to 128 with an online softmax,
+// warp-specialised so that loads, tensor-core products and the softmax of
+// different key blocks (and of consecutive items) overlap:
 //
-//   warp 0      TMA: the Q tile once, then K_j and V_j blocks of the packed
-//               Q|K|V rows (128-byte swizzled) through a 2-stage ring
-//   warp 1      tcgen05.mma from one thread:
-//                 S   = Q K_j^T   (M=128, N=128, K=16 x 4) -> TMEM [0, 128)
-//                 O_j = P_j V_j   (M=128, N=64, K=16 x 8; V read MN-major,
-//                                  no transpose)     -> TMEM [128, 192)
-//   warps 2-5   one query row per thread (its TMEM lane): row max of S_j,
-//               p = exp2((s - m) log2 e) with keys >= L set to 0, running
-//               sum, P_j as bf16 into shared memory (swizzled K-major, the
-//               A layout); then O_acc = O_acc * exp2(m_prev - m) + O_j in
-//               registers; at the end ctx = O_acc / sum as bf16
+//   warp 0      TMA: the Q tile once per item, then K_j and V_j of the packed
+//               Q|K|V rows (128-byte swizzled) through separate 2-stage
+//               rings, so K_j+2 can land while V_j is still being read
+//   warp 1      tcgen05.mma from one thread, software-pipelined inside an
+//               item so that the softmax of key block j can start before
+//               P_j-1 V_j-1 runs (an item's last P V is issued as soon as its
+//               P is written):
+//                 S_j  = Q K_j^T  (M=128, N = the block's valid keys rounded
+//                                  up to 16, K=16 x 4)     -> TMEM [0, 128)
+//                 O_j-1 = P_j-1 V_j-1 (M=128, N=64, K = 16 x that block's
+//                                  N/16; V read MN-major)  -> TMEM [128, 192)
+//   warps 2-5   one query row per thread (its TMEM lane); a warp whose 32
+//               rows all lie past the sequence only keeps the barrier
+//               protocol.  Row max over the valid keys of S_j, p =
+//               2^(s log2 e - m log2 e) on the SFU (packed fp32 FMAs for the
+//               argument and the running sum), P_j as bf16 into shared memory
+//               (swizzled K-major, the UMMA A layout); then O_acc = O_acc *
+//               2^(m_prev - m) + O_j in registers; at the end
+//               ctx = O_acc / sum as bf16
+//
+// Only the valid keys of a block are multiplied and exponentiated (in
+// 16-key groups), so short sequences -- most of an embedding batch -- cost
+// what their length needs rather than a full 128 x 128 tile.
 //
 // 112 KB of shared memory and 256 TMEM columns per CTA, so two CTAs share
 // an SM and one's softmax overlaps the other's loads and products.  Q is
@@ -47,10 +59,9 @@ constexpr int kAttnTcTmemCols = 256;  // S [0,128), O [128,192)
 
 struct AttnTcShape {
   static constexpr int kQ = 0;                      // 16 KB
-  static constexpr int kK0 = 16384;                 // K stage 0, 16 KB
-  static constexpr int kV0 = kK0 + 16384;           // V stage 0
-  static constexpr int kStage = 32768;              // K + V per stage
-  static constexpr int kP = kK0 + 2 * kStage;       // P, 32 KB (2 K-blocks of 64 keys)
+  static constexpr int kK0 = 16384;                 // K stages 0, 1: 16 KB each
+  static constexpr int kV0 = kK0 + 2 * 16384;       // V stages 0, 1: 16 KB each
+  static constexpr int kP = kV0 + 2 * 16384;        // P, 32 KB (2 K-blocks of 64 keys)
   static constexpr int kBars = kP + 32768;          // barriers
   static constexpr int kSmemBytes = kBars + 256;    // 114,944 B: two CTAs per SM
 };
@@ -72,6 +83,12 @@ __device__ __forceinline__ AttnItem attn_item(const int *items, int item, int qt
     return {e >> 8, e & 255};
   }
   return {item / qtiles, item % qtiles};
+}
+
+// Valid keys of key block j of a sequence of length L, rounded up to 16 (the
+// UMMA N granularity at M = 128 and the K step of P V).
+__device__ __forceinline__ int attn_block_cols(int L, int j) {
+  return (min(128, L - j * 128) + 15) & ~15;
 }
 
 // Persistent: each CTA walks work indices w = blockIdx.x, +gridDim.x, ...
@@ -96,13 +113,15 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   }
   uint64_t *bars = smem_at<uint64_t>(smem, S::kBars);
   uint64_t *q_full = bars + 0, *q_free = bars + 1;
-  uint64_t *kv_full = bars + 2;   // [2]
-  uint64_t *kv_empty = bars + 4;  // [2]
-  uint64_t *s_full = bars + 6, *s_free = bars + 7;
-  uint64_t *p_full = bars + 8;
-  uint64_t *o_full = bars + 9, *o_free = bars + 10;
-  uint64_t *drain = bars + 11;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+  uint64_t *k_full = bars + 2;    // [2]
+  uint64_t *k_empty = bars + 4;   // [2]
+  uint64_t *v_full = bars + 6;    // [2]
+  uint64_t *v_empty = bars + 8;   // [2]
+  uint64_t *s_full = bars + 10, *s_free = bars + 11;
+  uint64_t *p_full = bars + 12;
+  uint64_t *o_full = bars + 13, *o_free = bars + 14;
+  uint64_t *drain = bars + 15;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -110,8 +129,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     mbar_init(q_full, 1);
     mbar_init(q_free, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 4);
@@ -135,7 +156,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       bool ok = true;
-      int g = 0, t = 0;
+      int gk = 0, gv = 0, t = 0;  // K, V and Q loads issued
       for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
         const AttnItem it = attn_item(items, w / heads, qtiles);
         const int h = w % heads;
@@ -149,38 +170,68 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         mbar_arrive_expect_tx(q_full, 16384);
         tma_load_2d(smem + S::kQ, &tmQKV, q_full, h * kAttnTcD, base + q0);
         ++t;
-        for (int j = 0; j < nk; ++j, ++g) {
-          const int s = g & 1;
-          if (!mbar_wait(kv_empty + s, ((g >> 1) & 1) ^ 1u, err)) {
+        for (int j = 0; j < nk; ++j) {
+          const int s = gk & 1;
+          const uint32_t ph = ((gk >> 1) & 1) ^ 1u;
+          if (!mbar_wait(k_empty + s, ph, err)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(kv_full + s, 2 * 16384);
-          tma_load_2d(smem + S::kK0 + s * S::kStage, &tmQKV, kv_full + s, H + h * kAttnTcD,
+          mbar_arrive_expect_tx(k_full + s, 16384);
+          tma_load_2d(smem + S::kK0 + s * 16384, &tmQKV, k_full + s, H + h * kAttnTcD,
                       base + j * 128);
-          tma_load_2d(smem + S::kV0 + s * S::kStage, &tmQKV, kv_full + s, 2 * H + h * kAttnTcD,
+          ++gk;
+          if (!mbar_wait(v_empty + s, ph, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(v_full + s, 16384);
+          tma_load_2d(smem + S::kV0 + s * 16384, &tmQKV, v_full + s, 2 * H + h * kAttnTcD,
                       base + j * 128);
+          ++gv;
         }
       }
       if (ok) {
         // every load issued has been consumed (so it landed) before exit
-        for (int k = 0; k < 2; ++k, ++g)
-          if (!mbar_wait(kv_empty + (g & 1), ((g >> 1) & 1) ^ 1u, err)) break;
+        for (int k = 0; k < 2; ++k, ++gk) {
+          const uint32_t ph = ((gk >> 1) & 1) ^ 1u;
+          if (!mbar_wait(k_empty + (gk & 1), ph, err) || !mbar_wait(v_empty + (gk & 1), ph, err))
+            break;
+        }
         if (t > 0) mbar_wait(q_free, (t - 1) & 1, err);
       } else {
-        for (int k = g - 1; k >= 0 && k >= g - 2; --k)
-          mbar_wait(kv_full + (k & 1), (k >> 1) & 1, err);
+        // wait (bounded) for the copies still in flight to land
+        for (int k = gk - 1; k >= 0 && k >= gk - 2; --k)
+          mbar_wait(k_full + (k & 1), (k >> 1) & 1, err);
+        for (int k = gv - 1; k >= 0 && k >= gv - 2; --k)
+          mbar_wait(v_full + (k & 1), (k >> 1) & 1, err);
         if (t > 0) mbar_wait(q_full, (t - 1) & 1, err);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16_f32(128, 128);
       constexpr uint32_t idO = idesc_bf16_f32(128, kAttnTcD) | (1u << 16);  // B (V) MN-major
       const uint32_t qa = smem_u32(smem + S::kQ), pa = smem_u32(smem + S::kP);
       bool ok = true, issued = false;
       int g = 0, t = 0;
+      int pend_g = -1, pend_cols = 0;  // the P V still to issue (block pend_g)
+      // O_pg = P_pg V_pg over the block's `cols` keys
+      auto issue_pv = [&](int pg, int cols) -> bool {
+        const int s = pg & 1;
+        if (!mbar_wait(v_full + s, (pg >> 1) & 1, err) || !mbar_wait(p_full, pg & 1, err) ||
+            (pg > 0 && !mbar_wait(o_free, (pg - 1) & 1, err)))
+          return false;
+        tc_fence_after();
+        const uint32_t va = smem_u32(smem + S::kV0 + s * 16384);
+#pragma unroll 1
+        for (int ks = 0; ks < cols / 16; ++ks)
+          umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
+                    sdesc_mnmajor_sw128(va + ks * 2048), idO, ks > 0 ? 1u : 0u);
+        umma_commit(o_full);
+        umma_commit(v_empty + s);
+        return true;
+      };
       for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
         const AttnItem it = attn_item(items, w / heads, qtiles);
         const int L = __ldg(seq_len + it.b);
@@ -193,29 +244,29 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         ++t;
         for (int j = 0; j < nk; ++j, ++g) {
           const int s = g & 1;
-          ok = mbar_wait(kv_full + s, (g >> 1) & 1, err) &&
+          const int cols = attn_block_cols(L, j);
+          ok = mbar_wait(k_full + s, (g >> 1) & 1, err) &&
                (g == 0 || mbar_wait(s_free, (g - 1) & 1, err));
           if (!ok) break;
           tc_fence_after();
-          const uint32_t ka = smem_u32(smem + S::kK0 + s * S::kStage);
+          const uint32_t ka = smem_u32(smem + S::kK0 + s * 16384);
+          const uint32_t idS = idesc_bf16_f32(128, cols);
 #pragma unroll
           for (int k = 0; k < kAttnTcD / 16; ++k)
             umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS,
                       k > 0 ? 1u : 0u);
           umma_commit(s_full);
+          umma_commit(k_empty + s);
           if (j == nk - 1) umma_commit(q_free);  // this item's Q is no longer read
           issued = true;
-          ok = mbar_wait(p_full, g & 1, err) && (g == 0 || mbar_wait(o_free, (g - 1) & 1, err));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t va = smem_u32(smem + S::kV0 + s * S::kStage);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
-                      sdesc_mnmajor_sw128(va + ks * 2048), idO, ks > 0 ? 1u : 0u);
-          umma_commit(o_full);
-          umma_commit(kv_empty + s);
+          if (pend_g >= 0 && !(ok = issue_pv(pend_g, pend_cols))) break;
+          pend_g = g;
+          pend_cols = cols;
         }
+        // the item's last P V goes out now rather than behind the next
+        // item's loads: the softmax warps wait for it to write ctx
+        if (ok && !(ok = issue_pv(pend_g, pend_cols))) break;
+        pend_g = -1;
       }
       if (issued) {
         umma_commit(drain);
@@ -225,9 +276,11 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   } else {
     // ---------------- softmax and output (warps 2..5) ----------------
     constexpr float kLog2e = 1.4426950408889634f;
-    const int r = (warp & 3) * 32 + lane;  // TMEM lane = query row within the tile
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int w4 = warp & 3;
+    const int r = w4 * 32 + lane;  // TMEM lane = query row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>(w4 * 32) << 16;
     uint8_t *prow = smem + S::kP + r * 128;
+    const uint64_t log2e2 = pk2(kLog2e, kLog2e);
     bool ok = true;
     int g = 0;
     for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
@@ -236,6 +289,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       const int L = __ldg(seq_len + it.b), q0 = it.qt * 128;
       if (q0 >= L) continue;
       const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
+      // warp-uniform: does any of this warp's 32 query rows belong to the sequence?
+      const bool active = q0 + w4 * 32 < L;
       float o[kAttnTcD];
 #pragma unroll
       for (int i = 0; i < kAttnTcD; ++i) o[i] = 0.f;
@@ -246,25 +301,30 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           break;
         }
         tc_fence_after();
-        const int kbase = j * 128;
-        const bool partial = kbase + 128 > L;
-        // pass 1: row max of this key block
-        float mx = -INFINITY;
+        const int n = min(128, L - j * 128);  // valid keys of this block
+        const int nch = (n + 31) >> 5;        // 32-key chunks holding them
+        const int tail = n & 31;              // valid keys of a partial last chunk
+        float m_new = m_prev;
+        if (active) {
+          // pass 1: row max over the valid keys
+          float mx = -INFINITY;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
-          tmem_wait_ld_regs(v);
-          if (partial) {
+          for (int c = 0; c < nch; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
+            tmem_wait_ld_regs(v);
+            if (tail && c == nch - 1) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (kbase + c * 32 + i < L) mx = fmaxf(mx, __uint_as_float(v[i]));
-          } else {
+              for (int i = 0; i < 32; ++i)
+                if (i < tail) mx = fmaxf(mx, __uint_as_float(v[i]));
+            } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+              for (int i = 0; i < 32; i += 2)
+                mx = fmaxf(mx, fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
+            }
           }
+          m_new = fmaxf(m_prev, mx);
         }
-        const float m_new = fmaxf(m_prev, mx);
         // fold in the previous block's P V (its products used m_prev)
         if (j > 0) {
           if (!__all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, err))) {
@@ -272,48 +332,57 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
             break;
           }
           tc_fence_after();
-          uint32_t va[32], vb[32];
-          tmem_ld_32x32b_x32(tO + lane_off, va);
-          tmem_ld_32x32b_x32(tO + lane_off + 32, vb);
-          tmem_wait_ld_regs(va);
-          tmem_wait_ld_regs(vb);
-          const float sc = exp2f((m_prev2 - m_prev) * kLog2e);
+          if (active) {
+            const float sc = ex2_approx((m_prev2 - m_prev) * kLog2e);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            o[i] = fmaf(o[i], sc, __uint_as_float(va[i]));
-            o[32 + i] = fmaf(o[32 + i], sc, __uint_as_float(vb[i]));
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t va[32];
+              tmem_ld_32x32b_x32(tO + lane_off + hh * 32, va);
+              tmem_wait_ld_regs(va);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[hh * 32 + i] = fmaf(o[hh * 32 + i], sc, __uint_as_float(va[i]));
+            }
           }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(o_free);
         }
-        // pass 2: p, running sum, P (bf16) into the shared A tile
-        const float m2 = m_new * kLog2e;
-        l *= exp2f((m_prev - m_new) * kLog2e);
+        if (active) {
+          // pass 2: p, running sum, P (bf16) into the shared A tile
+          const float m2 = m_new * kLog2e;
+          const uint64_t negm2 = pk2(-m2, -m2);
+          l *= ex2_approx((m_prev - m_new) * kLog2e);
+          uint64_t acc = pk2(0.f, 0.f);
+          // 16 keys at a time: TMEM columns -> p -> two swizzled 16-byte P chunks
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
-          tmem_wait_ld_regs(v);
-          uint32_t pk[16];
+          for (int c = 0; c < (n + 15) >> 4; ++c) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(tS + lane_off + c * 16, v);
+            tmem_wait_ld_regs(v);
+            const int valid = n - c * 16;  // >= 16: the whole group
+            uint32_t pk[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int kj = kbase + c * 32 + 2 * i;
-            float p0 = exp2f(fmaf(__uint_as_float(v[2 * i]), kLog2e, -m2));
-            float p1 = exp2f(fmaf(__uint_as_float(v[2 * i + 1]), kLog2e, -m2));
-            if (partial) {
-              p0 = kj < L ? p0 : 0.f;
-              p1 = kj + 1 < L ? p1 : 0.f;
+            for (int i = 0; i < 8; ++i) {
+              float x0, x1;
+              unpk2(fma_x2(pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), log2e2,
+                           negm2),
+                    x0, x1);
+              float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+              p0 = 2 * i < valid ? p0 : 0.f;
+              p1 = 2 * i + 1 < valid ? p1 : 0.f;
+              acc = add_x2(acc, pk2(p0, p1));
+              pk[i] = pack_bf16x2(p0, p1);
             }
-            l += p0 + p1;
-            pk[i] = pack_bf16x2(p0, p1);
+            uint8_t *blk = prow + (c >> 2) * 16384;
+            const int q0c = (c & 3) * 2;
+            *reinterpret_cast<uint4 *>(blk + ((q0c ^ (r & 7)) << 4)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4 *>(blk + (((q0c + 1) ^ (r & 7)) << 4)) =
+                make_uint4(pk[4], pk[5], pk[6], pk[7]);
           }
-          uint8_t *blk = prow + (c >> 1) * 16384;
-          const int p0 = (c & 1) * 4;
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4 *>(blk + (((p0 + q) ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          float a0, a1;
+          unpk2(acc, a0, a1);
+          l += a0 + a1;
         }
         tc_fence_before();
         fence_proxy_async_smem();
@@ -330,22 +399,23 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         break;
       }
       tc_fence_after();
-      uint32_t va[32], vb[32];
-      tmem_ld_32x32b_x32(tO + lane_off, va);
-      tmem_ld_32x32b_x32(tO + lane_off + 32, vb);
-      tmem_wait_ld_regs(va);
-      tmem_wait_ld_regs(vb);
+      if (active) {
+        const float sc = ex2_approx((m_prev2 - m_prev) * kLog2e);
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t va[32];
+          tmem_ld_32x32b_x32(tO + lane_off + hh * 32, va);
+          tmem_wait_ld_regs(va);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[hh * 32 + i] = fmaf(o[hh * 32 + i], sc, __uint_as_float(va[i])) * inv;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free);  // the next item's first P V may overwrite O
-      const float sc = exp2f((m_prev2 - m_prev) * kLog2e);
-      const float inv = 1.0f / l;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        o[i] = fmaf(o[i], sc, __uint_as_float(va[i])) * inv;
-        o[32 + i] = fmaf(o[32 + i], sc, __uint_as_float(vb[i])) * inv;
-      }
-      if (q0 + r < L) {
+      if (active && q0 + r < L) {
         uint4 *dst = reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + r) * H +
                                                h * kAttnTcD);
 #pragma unroll

@@ -93,27 +93,8 @@ __device__ __forceinline__ float gelu8(float v) {
 }
 
 // gelu8 on two values at once with sm_100's packed fp32 arithmetic
-// (fma.rn.f32x2 / add.rn.f32x2): each lane is the same IEEE operation as the
-// scalar form above, so the results are bit-identical at half the FMA-pipe
-// instructions.
-__device__ __forceinline__ uint64_t pk2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void unpk2(uint64_t r, float &a, float &b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t fma_x2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t add_x2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
+// (fma_x2 / add_x2): each lane is the same IEEE operation as the scalar form
+// above, so the results are bit-identical at half the FMA-pipe instructions.
 __device__ __forceinline__ void gelu8_x2(float &a, float &b) {
   const uint64_t u = pk2(fminf(fabsf(a), 4.0f), fminf(fabsf(b), 4.0f));
   uint64_t pl = fma_x2(pk2(-7.2340282171e-05f, -7.2340282171e-05f), u,

@@ -3,6 +3,7 @@
     python -m nebw.kernel_bench gemm --M 16384 --K 1024 --N 4096 --epi gelu8
     python -m nebw.kernel_bench attention --B 64 --len 512 --heads 16 --hd 64
     python -m nebw.kernel_bench layernorm --M 131072 --H 1024
+    python -m nebw.kernel_bench encoder --config bge-large --layers 1
 
 (run with npu-embeddings-xdna1_b200/ on sys.path).  Each case runs a few
 warm-up launches and then times --iters launches with CUDA events on the
@@ -113,10 +114,49 @@ def bench_layernorm(dev, M, H, iters, copies):
     return {"kernel": "layernorm", "M": M, "H": H, "ms": ms, "gbs": by / ms / 1e6}
 
 
+def bench_encoder(dev, config, layers, iters):
+    """Whole passes of a benchmark configuration's batch through a model of
+    `layers` layers (the production launch sequence, attention work list
+    included), with per-kernel device times from the model's profiler."""
+    import torch
+    import nebw
+    from nebw import synth
+    cfg = synth.CONFIGS[config]
+    ids, _, lens = synth.config_batch(cfg)
+    m = nebw.Model.from_weights(dev, synth.config_weights(cfg, layers=layers), max_seq_len=cfg.seq)
+    ids_d = torch.from_numpy(ids).cuda()
+    lens_d = torch.from_numpy(lens.astype(np.int32)).cuda()
+    out = torch.empty(cfg.batch, m.hidden, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def run():
+        m.encode_into(ids_d, lens_d, out, cfg.batch, cfg.seq, stream=st)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    m.profile(True)
+    m.profile_collect()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    per = {k: round(ms / iters, 4) for k, (n, ms) in m.profile_collect().items() if n}
+    m.profile(False)
+    m.close()
+    return {"kernel": "encoder", "config": config, "layers": layers,
+            "ms": e0.elapsed_time(e1) / iters, "kernels_ms": per}
+
+
 def main(argv=None):
     import nebw
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attention", "layernorm"])
+    ap.add_argument("op", choices=["gemm", "attention", "layernorm", "encoder"])
+    ap.add_argument("--config", default="bge-large")
+    ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--M", type=int, default=16384)
     ap.add_argument("--K", type=int, default=1024)
     ap.add_argument("--N", type=int, default=4096)
@@ -128,7 +168,7 @@ def main(argv=None):
     ap.add_argument("--epi", default="bf16", choices=["bf16", "gelu8", "erf", "f32", "resid"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=2)
-    ap.add_argument("--attn-kind", type=int, default=0, help="0 mma.sync, 1 tcgen05")
+    ap.add_argument("--attn-kind", type=int, default=1, help="0 mma.sync, 1 tcgen05")
     a = ap.parse_args(argv)
     dev = nebw.Device(0, torch_stream=True)
     dev.set_attention_kernel(a.attn_kind)
@@ -136,8 +176,10 @@ def main(argv=None):
         r = bench_gemm(dev, a.M, a.K, a.N, a.epi, a.iters, a.copies)
     elif a.op == "attention":
         r = bench_attention(dev, a.B, a.len, a.heads, a.hd, a.iters, a.copies)
-    else:
+    elif a.op == "layernorm":
         r = bench_layernorm(dev, a.M, a.H, a.iters, a.copies)
+    else:
+        r = bench_encoder(dev, a.config, a.layers, a.iters)
     print(json.dumps(r), flush=True)
     dev.close()
 
