@@ -1274,7 +1274,7 @@ size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 // sequences needs, in the carve order used below.
 size_t static_scratch_need(const nebw_config &c, int64_t rows, int64_t batch) {
   const size_t R = static_cast<size_t>(rows), H = c.hidden, F = c.intermediate;
-  return align256(R * H * 4) + align256(R * H * 4) + align256(R * H * 2) +
+  return align256(R * H * 4) + align256(R * H * 2) + align256(R * H * 2) +
          align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * F * 2) +
          align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4) +
          align256((R / 128 + static_cast<size_t>(batch) + 1) * 4);
