@@ -186,3 +186,48 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
         w.add(p + "ln2.weight", model.ln2_g[i], "F32", "layernorm", [H])
         w.add(p + "ln2.bias", model.ln2_b[i], "F32", "layernorm", [H])
     return w.write(path)
+
+
+def write_vit_container(path, model, source_repo: str = "synthetic/random-init"):
+    """Write a ViT (arch vit_patch16_prenorm_gelu) container in the host
+    layout: GEMM operands F32 row-major [K, N], everything else F32.  Config
+    keys are the ones read_geometry() requires (runtime/include/vit/
+    geometry.hpp), tensor names the ones VitEncoder::stage_all() reads
+    (runtime/src/vit/encoder.cpp:125-189)."""
+    a = model.arch
+    H, F, L = a.hidden, a.ffn, model.layers
+    pd = a.channels * a.patch_size ** 2
+    config = {
+        "arch": "vit_patch16_prenorm_gelu",
+        "source_repo": source_repo,
+        "source_sha256": model.fingerprint(),
+        "num_layers": L, "num_heads": a.heads, "hidden": H, "head_dim": a.head_dim,
+        "intermediate": F, "num_labels": a.num_labels,
+        "image_size": a.image_size, "crop_size": a.image_size, "patch_size": a.patch_size,
+        "num_channels": a.channels, "patch_dim": pd, "n_patches": a.n_patches,
+        "max_seq_len": a.n_pos, "resample": 3, "image_resize": "square",
+        "image_mean": [0.5] * a.channels, "image_std": [0.5] * a.channels,
+        "layer_norm_eps": a.ln_eps, "attention_scale": 1.0 / float(np.sqrt(a.head_dim)),
+        "qkv_scale_folded": True,
+        "gemm_layout": "host",
+        "a_dtype": "f32",
+    }
+    w = ContainerWriter(config)
+    shapes = {"frontend.patch_embed": [pd, H], "frontend.patch_embed.bias": [H],
+              "frontend.cls_token": [H], "frontend.position_embeddings": [a.n_pos, H],
+              "layernorm.weight": [H], "layernorm.bias": [H]}
+    for name, arr in model.tensors():
+        if name in shapes:
+            shape = shapes[name]
+        else:
+            kind = name.split(".", 2)[2]
+            shape = {"qkv": [H, 3 * H], "qkv.bias": [3 * H], "attn_out": [H, H],
+                     "attn_out.bias": [H], "ffn_up": [H, F], "ffn_up.bias": [F],
+                     "ffn_down": [F, H], "ffn_down.bias": [H]}.get(kind, [H])
+        role = "gemm_b_host" if len(shape) == 2 and name != "frontend.position_embeddings" else \
+            ("embedding" if name.startswith("frontend.") else
+             ("layernorm" if ".ln" in name or name.startswith("layernorm") else "bias"))
+        w.add(name, arr, "F32", role, shape)
+    w.add("classifier.weight", model.head_w, "F32", "gemm_b_host", [H, a.num_labels])
+    w.add("classifier.bias", model.head_b, "F32", "bias", [a.num_labels])
+    return w.write(path)

@@ -229,3 +229,174 @@ def mask_to_lengths(mask: np.ndarray) -> np.ndarray:
         raise ValueError("attention mask is not a prefix of ones in every row; "
                          "the packed device path cannot represent it")
     return lens
+
+
+# ---------------------------------------------------------------------------
+# ViT (arch vit_patch16_prenorm_gelu): benchmark configuration 5
+# ---------------------------------------------------------------------------
+#
+#   weights   patch embedding, CLS token, position table and every GEMM
+#             weight N(0, 0.02); biases N(0, 0.02); LayerNorm gamma = 1,
+#             beta = 0; 1/sqrt(head_dim) folded into the Q columns and Q bias
+#             (the container's qkv_scale_folded); a random 1000-label head so
+#             the container is complete (the head is not on the hot path).
+#   images    [n, 3, S, S] fp32 uniform in [-1, 1] (normalised pixels), fed
+#             to the reference's im2col order (runtime/src/vit/image.cpp:
+#             732-755).
+
+
+@dataclass(frozen=True)
+class VitArch:
+    name: str
+    layers: int
+    hidden: int
+    heads: int
+    ffn: int
+    image_size: int = 224
+    patch_size: int = 16
+    channels: int = 3
+    num_labels: int = 1000
+    ln_eps: float = 1e-12
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+    @property
+    def n_patches(self) -> int:
+        return (self.image_size // self.patch_size) ** 2
+
+    @property
+    def n_pos(self) -> int:
+        return self.n_patches + 1
+
+
+@dataclass(frozen=True)
+class VitConfig:
+    key: str
+    arch: VitArch
+    batch: int
+    index: int
+
+
+VIT_BASE = VitArch("vit-base-patch16-224", 12, 768, 12, 3072)
+VIT_CONFIGS = {"vit-base": VitConfig("vit-base", VIT_BASE, 2048, 4)}
+
+
+@dataclass
+class VitWeights:
+    arch: VitArch
+    layers: int
+    patch_w: np.ndarray          # [C*P*P, H]
+    patch_b: np.ndarray
+    cls: np.ndarray              # [H]
+    pos: np.ndarray              # [n_pos, H]
+    lnf_g: np.ndarray
+    lnf_b: np.ndarray
+    head_w: np.ndarray           # [H, num_labels]
+    head_b: np.ndarray
+    w_qkv: list = field(default_factory=list)
+    b_qkv: list = field(default_factory=list)
+    w_ao: list = field(default_factory=list)
+    b_ao: list = field(default_factory=list)
+    ln1_g: list = field(default_factory=list)
+    ln1_b: list = field(default_factory=list)
+    w_up: list = field(default_factory=list)
+    b_up: list = field(default_factory=list)
+    w_dn: list = field(default_factory=list)
+    b_dn: list = field(default_factory=list)
+    ln2_g: list = field(default_factory=list)
+    ln2_b: list = field(default_factory=list)
+    seed: int = 0
+
+    hidden = property(lambda self: self.arch.hidden)
+    heads = property(lambda self: self.arch.heads)
+    head_dim = property(lambda self: self.arch.head_dim)
+    ffn = property(lambda self: self.arch.ffn)
+
+    def fingerprint(self) -> str:
+        h = hashlib.sha256()
+        a = self.arch
+        h.update(f"vit,{self.layers},{a.hidden},{a.heads},{a.ffn},{a.image_size},{self.seed}".encode())
+        h.update(self.patch_w[:4].tobytes())
+        h.update(self.w_qkv[0][:4].tobytes())
+        return h.hexdigest()
+
+    def tensors(self):
+        """(name, array) in the ViT container's naming (runtime/src/vit/
+        encoder.cpp:125-139, :176-207)."""
+        yield "frontend.patch_embed", self.patch_w
+        yield "frontend.patch_embed.bias", self.patch_b
+        yield "frontend.cls_token", self.cls
+        yield "frontend.position_embeddings", self.pos
+        for i in range(self.layers):
+            p = f"layer.{i}."
+            yield p + "qkv", self.w_qkv[i]
+            yield p + "qkv.bias", self.b_qkv[i]
+            yield p + "attn_out", self.w_ao[i]
+            yield p + "attn_out.bias", self.b_ao[i]
+            yield p + "ffn_up", self.w_up[i]
+            yield p + "ffn_up.bias", self.b_up[i]
+            yield p + "ffn_down", self.w_dn[i]
+            yield p + "ffn_down.bias", self.b_dn[i]
+            yield p + "ln1.weight", self.ln1_g[i]
+            yield p + "ln1.bias", self.ln1_b[i]
+            yield p + "ln2.weight", self.ln2_g[i]
+            yield p + "ln2.bias", self.ln2_b[i]
+        yield "layernorm.weight", self.lnf_g
+        yield "layernorm.bias", self.lnf_b
+
+
+def make_vit_weights(arch: VitArch, seed: int, layers: int | None = None) -> VitWeights:
+    """Random-init weights of a ViT architecture (optionally truncated)."""
+    rng = np.random.default_rng(seed)
+    H, F = arch.hidden, arch.ffn
+    pd = arch.channels * arch.patch_size ** 2
+    if pd != H:
+        raise ValueError(f"patch_dim {pd} != hidden {H}: the patch embedding rides the "
+                         "attention-out GEMM shape in this architecture")
+    L = arch.layers if layers is None else layers
+    scale = np.float32(1.0 / np.sqrt(arch.head_dim))
+
+    def normal(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+
+    m = VitWeights(arch=arch, layers=L, patch_w=normal(pd, H), patch_b=normal(H), cls=normal(H),
+                   pos=normal(arch.n_pos, H), lnf_g=np.ones(H, np.float32),
+                   lnf_b=np.zeros(H, np.float32), head_w=normal(H, arch.num_labels),
+                   head_b=normal(arch.num_labels), seed=seed)
+    for _ in range(L):
+        wqkv = normal(H, 3 * H)
+        bqkv = normal(3 * H)
+        wqkv[:, :H] *= scale          # qkv_scale_folded
+        bqkv[:H] *= scale
+        m.w_qkv.append(wqkv)
+        m.b_qkv.append(bqkv)
+        m.w_ao.append(normal(H, H))
+        m.b_ao.append(normal(H))
+        m.ln1_g.append(np.ones(H, np.float32))
+        m.ln1_b.append(np.zeros(H, np.float32))
+        m.w_up.append(normal(H, F))
+        m.b_up.append(normal(F))
+        m.w_dn.append(normal(F, H))
+        m.b_dn.append(normal(H))
+        m.ln2_g.append(np.ones(H, np.float32))
+        m.ln2_b.append(np.zeros(H, np.float32))
+    return m
+
+
+def make_images(n: int, arch: VitArch, seed: int) -> np.ndarray:
+    """[n, C, S, S] fp32 uniform in [-1, 1]."""
+    rng = np.random.default_rng(seed)
+    shape = (n, arch.channels, arch.image_size, arch.image_size)
+    return rng.uniform(-1.0, 1.0, size=shape).astype(np.float32)
+
+
+def vit_config_weights(cfg: VitConfig, layers: int | None = None,
+                       seed: int | None = None) -> VitWeights:
+    return make_vit_weights(cfg.arch, 20261201 + cfg.index if seed is None else seed, layers)
+
+
+def vit_config_images(cfg: VitConfig, n: int | None = None, seed: int | None = None) -> np.ndarray:
+    return make_images(cfg.batch if n is None else n, cfg.arch,
+                       20261301 + cfg.index if seed is None else seed)

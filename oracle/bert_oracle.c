@@ -397,3 +397,172 @@ int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
   free(x); free(res); free(qkv); free(ctx); free(tmp); free(up); free(amask); free(cam);
   return rc;
 }
+
+/* ======================================================================== *
+ * ViT (arch vit_patch16_prenorm_gelu): VitEncoder::run, host path
+ * (runtime/src/vit/encoder.cpp:222-431) with the whisper host ops it calls
+ * (runtime/src/whisper/npu_ops.cpp:449-620) and the im2col of
+ * runtime/src/vit/image.cpp:732-755.
+ * ======================================================================== */
+
+/* im2col_patches (image.cpp:732-755): patch row p*n + q, column
+ * (c*P + i)*P + j  <-  chw[(c*S + p*P + i)*S + q*P + j]. */
+void nebw_oracle_vit_im2col(const float *chw, int32_t channels, int32_t image,
+                            int32_t patch, float *out) {
+  const int64_t n = image / patch, pd = (int64_t)channels * patch * patch;
+  for (int64_t p = 0; p < n; ++p)
+    for (int64_t q = 0; q < n; ++q) {
+      float *dst = out + (p * n + q) * pd;
+      for (int64_t c = 0; c < channels; ++c)
+        for (int64_t i = 0; i < patch; ++i)
+          for (int64_t j = 0; j < patch; ++j)
+            dst[(c * patch + i) * patch + j] =
+                chw[(c * image + p * patch + i) * image + q * patch + j];
+    }
+}
+
+/* layernorm_rows (npu_ops.cpp:449-468): mean and variance summed in double
+ * in row order; y = ((x - mean) * is) * gamma + beta with is =
+ * 1/sqrt(var + eps) in float (the reference build contracts the last
+ * multiply-add into one fused operation). */
+static void ln_row_vit(float *row, int64_t d, const float *g, const float *b,
+                       float eps) {
+  double sm = 0.0;
+  for (int64_t j = 0; j < d; ++j) sm += row[j];
+  const float mean = (float)(sm / (double)d);
+  double sv = 0.0;
+  for (int64_t j = 0; j < d; ++j) {
+    const double dd = (double)row[j] - (double)mean;
+    sv = fma(dd, dd, sv);
+  }
+  const float var = (float)(sv / (double)d);
+  const float is = 1.0f / sqrtf(var + eps);
+  for (int64_t j = 0; j < d; ++j) row[j] = fmaf((row[j] - mean) * is, g[j], b[j]);
+}
+
+typedef struct {
+  const float *src;
+  float *dst;
+  int64_t d;
+  const float *g, *b;
+  float eps;
+} ln_vit_ctx;
+
+static void ln_vit_rows(void *p, int64_t lo, int64_t hi) {
+  const ln_vit_ctx *c = (const ln_vit_ctx *)p;
+  for (int64_t r = lo; r < hi; ++r) {
+    float *row = c->dst + r * c->d;
+    if (c->src != c->dst) memcpy(row, c->src + r * c->d, (size_t)c->d * sizeof(float));
+    ln_row_vit(row, c->d, c->g, c->b, c->eps);
+  }
+}
+
+/* whisper attention, no softmax operator (npu_ops.cpp:478-600): per (query
+ * i, head h) scores q.k (eight-lane fused partial sums, hsum256) times the
+ * scale, softmax with the row max subtracted and std::exp, sum in key order,
+ * inverse sum; ctx = sum_j (p_j * inv) * v_j with fused multiply-adds. */
+typedef struct {
+  const float *qkv;
+  float *ctx;
+  int64_t n_pos, H, heads, hd;
+  float scale;
+} vit_attn_ctx;
+
+static void vit_attn_pairs(void *p, int64_t lo, int64_t hi) {
+  const vit_attn_ctx *a = (const vit_attn_ctx *)p;
+  const int64_t S = a->n_pos, H = a->H, hd = a->hd, nv = hd / 8;
+  float *sc = (float *)malloc((size_t)S * sizeof(float));
+  for (int64_t pr = lo; pr < hi; ++pr) {
+    const int64_t img = pr / (S * a->heads), rem = pr % (S * a->heads);
+    const int64_t i = rem / a->heads, h = rem % a->heads;
+    const float *base = a->qkv + img * S * 3 * H;
+    const float *q = base + i * 3 * H + h * hd;
+    for (int64_t j = 0; j < S; ++j) {
+      const float *k = base + j * 3 * H + H + h * hd;
+      float s[8];
+      for (int l = 0; l < 8; ++l) s[l] = q[l] * k[l];
+      for (int64_t v = 1; v < nv; ++v)
+        for (int l = 0; l < 8; ++l) s[l] = fmaf(q[8 * v + l], k[8 * v + l], s[l]);
+      sc[j] = hsum8(s) * a->scale;
+    }
+    float mx = sc[0];
+    for (int64_t j = 1; j < S; ++j) mx = sc[j] > mx ? sc[j] : mx;
+    float sum = 0.f;
+    for (int64_t j = 0; j < S; ++j) {
+      sc[j] = expf(sc[j] - mx);
+      sum += sc[j];
+    }
+    const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+    float *o = a->ctx + (img * S + i) * H + h * hd;
+    for (int64_t d = 0; d < hd; ++d) o[d] = 0.0f;
+    for (int64_t j = 0; j < S; ++j) {
+      const float w = sc[j] * inv;
+      const float *v = base + j * 3 * H + 2 * H + h * hd;
+      for (int64_t d = 0; d < hd; ++d) o[d] = fmaf(w, v[d], o[d]);
+    }
+  }
+  free(sc);
+}
+
+/* VitEncoder::run (encoder.cpp:222-431), image by image:
+ *   patches = im2col(image); pe = gemm(patches, patch_embed) + bias
+ *   x[0] = cls + pos[0]; x[1+p] = pe[p] + pos[1+p]
+ *   per layer: x += attn_out(attention(qkv(LN1(x))))
+ *              x += ffn_down(gelu_erf(ffn_up(LN2(x))))
+ *   x = LN_final(x); the CLS row is x[0]. */
+int nebw_oracle_vit_encode(const nebw_oracle_vit *m, const float *images, int32_t n_images,
+                           int32_t threads, float *cls_out, float *hidden_out) {
+  const int64_t H = m->hidden, F = m->ffn, P = m->patch_size, C = m->channels;
+  const int64_t side = m->image_size / P, np = side * side, S = np + 1, pd = C * P * P;
+  if (m->image_size % P || pd != H)
+    return fail("ViT geometry refused: image_size % patch and channels*patch^2 == hidden");
+  if (H % 8 || m->head_dim % 8 || m->head_dim * m->heads != H)
+    return fail("ViT head geometry refused (multiples of 8, heads*head_dim == hidden)");
+  const int64_t rows = (int64_t)n_images * S;
+  float *x = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *nrm = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *qkv = (float *)malloc((size_t)rows * 3 * H * sizeof(float));
+  float *ctx = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *tmp = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *up = (float *)malloc((size_t)rows * F * sizeof(float));
+  float *pat = (float *)malloc((size_t)np * pd * sizeof(float));
+  float *pe = (float *)malloc((size_t)np * H * sizeof(float));
+  if (!x || !nrm || !qkv || !ctx || !tmp || !up || !pat || !pe) {
+    free(x); free(nrm); free(qkv); free(ctx); free(tmp); free(up); free(pat); free(pe);
+    return fail("out of host memory");
+  }
+  for (int64_t img = 0; img < n_images; ++img) {
+    nebw_oracle_vit_im2col(images + img * C * m->image_size * m->image_size, (int32_t)C,
+                           m->image_size, (int32_t)P, pat);
+    nebw_oracle_gemm_nt(pat, np, m->patch_w, pd, H, m->patch_b, pe, threads);
+    float *xi = x + img * S * H;
+    for (int64_t c = 0; c < H; ++c) xi[c] = m->cls[c];
+    memcpy(xi + H, pe, (size_t)np * H * sizeof(float));
+    for (int64_t t = 0; t < S; ++t)
+      for (int64_t c = 0; c < H; ++c) xi[t * H + c] += m->pos[t * H + c];
+  }
+  for (int32_t L = 0; L < m->layers; ++L) {
+    ln_vit_ctx lc = {x, nrm, H, m->ln1_g[L], m->ln1_b[L], m->ln_eps};
+    parallel_for(rows, threads, ln_vit_rows, &lc);
+    nebw_oracle_gemm_nt(nrm, rows, m->w_qkv[L], H, 3 * H, m->b_qkv[L], qkv, threads);
+    vit_attn_ctx ac = {qkv, ctx, S, H, m->heads, m->head_dim, m->attn_scale};
+    parallel_for(rows * m->heads, threads, vit_attn_pairs, &ac);
+    nebw_oracle_gemm_nt(ctx, rows, m->w_ao[L], H, H, m->b_ao[L], tmp, threads);
+    for (int64_t i = 0; i < rows * H; ++i) x[i] += tmp[i];
+    lc.g = m->ln2_g[L];
+    lc.b = m->ln2_b[L];
+    parallel_for(rows, threads, ln_vit_rows, &lc);
+    nebw_oracle_gemm_nt(nrm, rows, m->w_up[L], H, F, m->b_up[L], up, threads);
+    act_ctx gc = {up, 1};
+    parallel_for(rows * F, threads, act_range, &gc);
+    nebw_oracle_gemm_nt(up, rows, m->w_dn[L], F, H, m->b_dn[L], tmp, threads);
+    for (int64_t i = 0; i < rows * H; ++i) x[i] += tmp[i];
+  }
+  ln_vit_ctx lf = {x, x, H, m->lnf_g, m->lnf_b, m->ln_eps};
+  parallel_for(rows, threads, ln_vit_rows, &lf);
+  for (int64_t img = 0; img < n_images; ++img)
+    memcpy(cls_out + img * H, x + img * S * H, (size_t)H * sizeof(float));
+  if (hidden_out) memcpy(hidden_out, x, (size_t)rows * H * sizeof(float));
+  free(x); free(nrm); free(qkv); free(ctx); free(tmp); free(up); free(pat); free(pe);
+  return 0;
+}

@@ -65,6 +65,30 @@ int nebw_oracle_pool_rows(const float *h, const float *am, int64_t take,
                           float *out);
 const char *nebw_oracle_last_error(void);
 
+/* ViT (arch vit_patch16_prenorm_gelu): pre-LN encoder over image patches. */
+typedef struct nebw_oracle_vit {
+  int32_t layers, hidden, heads, head_dim, ffn;
+  int32_t image_size, patch_size, channels;  /* hidden == channels*patch^2 */
+  float ln_eps;
+  float attn_scale;  /* 1 when 1/sqrt(head_dim) is folded into the Q operand */
+  const float *patch_w, *patch_b;            /* [C*P*P, H], [H]          */
+  const float *cls, *pos;                    /* [H], [n_patches + 1, H]  */
+  const float *lnf_g, *lnf_b;                /* final LayerNorm          */
+  const float *const *w_qkv, *const *b_qkv;
+  const float *const *w_ao, *const *b_ao;
+  const float *const *ln1_g, *const *ln1_b;
+  const float *const *w_up, *const *b_up;
+  const float *const *w_dn, *const *b_dn;
+  const float *const *ln2_g, *const *ln2_b;
+} nebw_oracle_vit;
+
+/* images [n, C, S, S] fp32 (normalised pixels) -> cls_out [n, H] (the CLS
+ * row after the final LayerNorm); hidden_out [n, n_pos, H] or NULL. */
+int nebw_oracle_vit_encode(const nebw_oracle_vit *m, const float *images, int32_t n_images,
+                           int32_t threads, float *cls_out, float *hidden_out);
+void nebw_oracle_vit_im2col(const float *chw, int32_t channels, int32_t image,
+                            int32_t patch, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,7 +1,7 @@
 """TEST INFRASTRUCTURE ONLY -- Python front of the parity oracle.
 
-Two CPU implementations of the reference's host-CPU BERT path, both behind
-ctypes:
+Two CPU implementations of the reference's host-CPU BERT and ViT paths, both
+behind ctypes:
 
   PortOracle  oracle/libnebw_oracle.so -- the plain-C restatement
               (oracle/bert_oracle.c).  Travels with the repository, so it is
@@ -46,6 +46,15 @@ class _Model(C.Structure):
                                          "w_up", "b_up", "w_dn", "b_dn", "ln2_g", "ln2_b")]
 
 
+class _Vit(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("layers", "hidden", "heads", "head_dim", "ffn",
+                                          "image_size", "patch_size", "channels")] + [
+        ("ln_eps", C.c_float), ("attn_scale", C.c_float)] + [
+        (n, _f32p) for n in ("patch_w", "patch_b", "cls", "pos", "lnf_g", "lnf_b")] + [
+        (n, C.POINTER(_f32p)) for n in ("w_qkv", "b_qkv", "w_ao", "b_ao", "ln1_g", "ln1_b",
+                                         "w_up", "b_up", "w_dn", "b_dn", "ln2_g", "ln2_b")]
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -74,6 +83,48 @@ class PortOracle:
         L.nebw_oracle_pool_rows.argtypes = [_f32p, _f32p, C.c_int64, C.c_int64, C.c_int64,
                                             C.c_int32, C.c_int32, _f32p]
         L.nebw_oracle_pool_rows.restype = C.c_int
+        L.nebw_oracle_vit_encode.argtypes = [C.POINTER(_Vit), _f32p, C.c_int32, C.c_int32, _f32p,
+                                             _f32p]
+        L.nebw_oracle_vit_encode.restype = C.c_int
+        L.nebw_oracle_vit_im2col.argtypes = [_f32p, C.c_int32, C.c_int32, C.c_int32, _f32p]
+
+    def vit_encode(self, w, images, threads: int | None = None, hidden: bool = False):
+        """ViT host path: images [n, C, S, S] -> CLS rows [n, H] (after the
+        final LayerNorm); with hidden=True also every row [n, n_pos, H]."""
+        a = w.arch
+        images = np.ascontiguousarray(images, np.float32)
+        n = images.shape[0]
+        keep = []
+
+        def arr(lst):
+            v = (_f32p * len(lst))(*[_ptr(np.ascontiguousarray(x, np.float32)) for x in lst])
+            keep.append(v)
+            return v
+
+        m = _Vit(layers=w.layers, hidden=a.hidden, heads=a.heads, head_dim=a.head_dim, ffn=a.ffn,
+                 image_size=a.image_size, patch_size=a.patch_size, channels=a.channels,
+                 ln_eps=a.ln_eps, attn_scale=1.0,
+                 patch_w=_ptr(w.patch_w), patch_b=_ptr(w.patch_b), cls=_ptr(w.cls),
+                 pos=_ptr(w.pos), lnf_g=_ptr(w.lnf_g), lnf_b=_ptr(w.lnf_b),
+                 w_qkv=arr(w.w_qkv), b_qkv=arr(w.b_qkv), w_ao=arr(w.w_ao), b_ao=arr(w.b_ao),
+                 ln1_g=arr(w.ln1_g), ln1_b=arr(w.ln1_b), w_up=arr(w.w_up), b_up=arr(w.b_up),
+                 w_dn=arr(w.w_dn), b_dn=arr(w.b_dn), ln2_g=arr(w.ln2_g), ln2_b=arr(w.ln2_b))
+        out = np.zeros((n, a.hidden), np.float32)
+        hid = np.zeros((n, a.n_pos, a.hidden), np.float32) if hidden else None
+        rc = self.lib.nebw_oracle_vit_encode(C.byref(m), _ptr(images), n,
+                                             threads or host_threads(), _ptr(out),
+                                             _ptr(hid) if hidden else None)
+        del keep
+        if rc:
+            raise RuntimeError(self.lib.nebw_oracle_last_error().decode())
+        return (out, hid) if hidden else out
+
+    def vit_im2col(self, image, patch):
+        image = np.ascontiguousarray(image, np.float32)
+        c, s = image.shape[0], image.shape[1]
+        out = np.zeros(((s // patch) ** 2, c * patch * patch), np.float32)
+        self.lib.nebw_oracle_vit_im2col(_ptr(image), c, s, patch, _ptr(out))
+        return out
 
     def _struct(self, w):
         keep = []
@@ -180,6 +231,34 @@ class RefOracle:
                                            C.c_int32]
         L.nebw_ref_session_run.restype = C.c_int
         L.nebw_ref_session_close.argtypes = [C.c_void_p]
+        L.nebw_ref_vit_encode.argtypes = [C.c_char_p, _f32p, C.c_int32, C.c_int32, _f32p, _f32p,
+                                          C.c_char_p, C.c_int32]
+        L.nebw_ref_vit_encode.restype = C.c_int
+
+    def vit_encode_container(self, path, images, hidden_size, n_pos=None, threads=None,
+                             hidden=False):
+        images = np.ascontiguousarray(images, np.float32)
+        n = images.shape[0]
+        out = np.zeros((n, hidden_size), np.float32)
+        hid = np.zeros((n, n_pos, hidden_size), np.float32) if hidden else None
+        err = C.create_string_buffer(4096)
+        rc = self.lib.nebw_ref_vit_encode(str(path).encode(), _ptr(images), n,
+                                          threads or host_threads(), _ptr(out),
+                                          _ptr(hid) if hidden else None, err, 4096)
+        if rc:
+            raise RuntimeError(err.value.decode())
+        return (out, hid) if hidden else out
+
+    def vit_encode(self, w, images, threads=None, hidden=False, workdir=None):
+        """Write `w` as a host-layout ViT container, then run the reference."""
+        import sys
+        sys.path.insert(0, str(HERE.parent / "npu-embeddings-xdna1_b200"))
+        from nebw.npue import write_vit_container  # noqa: E402
+        with tempfile.TemporaryDirectory(dir=workdir) as td:
+            path = Path(td) / "oracle_vit.npue"
+            write_vit_container(path, w)
+            return self.vit_encode_container(path, images, w.arch.hidden, w.arch.n_pos,
+                                             threads, hidden)
 
     def encode_container(self, path, seq, ids, mask, threads=None, hidden=False, hidden_size=None):
         ids = np.ascontiguousarray(ids, np.int32)

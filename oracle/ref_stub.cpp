@@ -1,8 +1,9 @@
 // TEST INFRASTRUCTURE ONLY -- part of the parity oracle, never shipped.
 //
 // Host-side stand-ins for the reference's XRT device layer, so that the
-// reference's own host-CPU encoder (runtime/src/encoders/bert_encoder.cpp,
-// compiled from the reference tree where it lies) links without XRT.
+// reference's own host-CPU encoders (runtime/src/encoders/bert_encoder.cpp and
+// runtime/src/vit/encoder.cpp, compiled from the reference tree where they
+// lie) link without XRT.
 //
 // The oracle runs the reference with `--npu-ops` empty, which is its default
 // (runtime/include/common/npu_ops_flag.hpp:96-103): every GEMM goes to
@@ -11,12 +12,13 @@
 // name: reaching one means the oracle is not running the host path and its
 // answer must not be trusted.
 //
-// Symbols provided (the set the linker reports missing when bert_encoder.cpp,
-// pool.cpp, model.cpp, json_min.cpp and tokenizers/*.cpp are linked alone):
+// Symbols provided (the set the linker reports missing when the sources in
+// oracle/Makefile's REF_SRCS are linked alone):
 //   npu::Device::{Device,~Device}                    runtime/include/runtime/device.hpp:29-38
 //   npu::Design::{Design,~Design,stage,bind,...}     runtime/include/runtime/design.hpp:199-263
-//   npue::whisper::NpuAttention::run                 runtime/include/whisper/attention_npu.hpp:162
 //   npue::gemma_rope_tables                          runtime/include/encoders/gemma_kernels.hpp:88
+// (npue::whisper::NpuAttention::run comes from the reference's own
+// whisper/attention_npu.cpp, linked for the ViT path; it is not reached.)
 
 #include <stdexcept>
 #include <string>
@@ -24,7 +26,6 @@
 #include "encoders/gemma_kernels.hpp"
 #include "runtime/design.hpp"
 #include "runtime/device.hpp"
-#include "whisper/attention_npu.hpp"
 
 namespace {
 [[noreturn]] void unreachable(const char *what) {
@@ -43,6 +44,9 @@ Device::~Device() {}
 struct Design::Impl {};
 Design::Design(Device &dev, const std::string &dir) : dev_(&dev) {
   info_.name = dir;  // used only as a cache-key label by host_b.hpp
+  // NpuGemm::alloc_buffers (runtime/src/whisper/npu_ops.cpp:29-32) reads the
+  // A and C entries of buffer_bytes; a host-layout run never uses the sizes.
+  info_.buffer_bytes.assign(3, 0);
 }
 Design::~Design() {}
 
@@ -50,7 +54,11 @@ void Design::run(const std::vector<const void *> &, void *) { unreachable("Desig
 void Design::dispatch_only() { unreachable("Design::dispatch_only"); }
 void Design::bind_instr(size_t) { unreachable("Design::bind_instr"); }
 size_t Design::stage(size_t, const void *, size_t) { unreachable("Design::stage"); }
-size_t Design::stage_alloc(size_t, size_t) { unreachable("Design::stage_alloc"); }
+// VitEncoder::stage_all -> NpuGemm::alloc_buffers (runtime/src/whisper/
+// npu_ops.cpp:29-32) reserves the design's A and C slots even on a
+// host-layout container, whose GEMMs never touch them; the slot numbers are
+// returned and never used.
+size_t Design::stage_alloc(size_t arg, size_t) { return arg; }
 // The one method that does not throw: BertEncoder::run() takes the FFN-down
 // A-slot address unconditionally when it builds its FusedNext/FusedNextBf16
 // descriptors (bert_encoder.cpp:1529-1541) and only writes through it when
@@ -72,13 +80,6 @@ void Design::sync_slot_from_device(size_t, size_t, size_t) {
 }  // namespace npu
 
 namespace npue {
-namespace whisper {
-void NpuAttention::run(const float *, int64_t, const float *, int64_t, int64_t,
-                       int64_t, int64_t, float, float *) {
-  unreachable("NpuAttention::run");
-}
-}  // namespace whisper
-
 void gemma_rope_tables(int64_t, int64_t, double, float *, float *) {
   unreachable("gemma_rope_tables");
 }

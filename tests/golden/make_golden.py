@@ -16,6 +16,14 @@ shortest and longest rows are always included):
   bge_small_c2.npz   bge-small arch, 6 rows at seq 512, CLS pool
   bge_base_c3.npz    bge-base arch, 3 rows at seq 512, CLS pool
   bge_large_c4.npz   bge-large arch, 3 rows at seq 512, CLS pool
+  vit_base_c5.npz    vit-base-patch16-224 arch, the first 3 images of the
+                     configuration's batch, the CLS row after the final
+                     LayerNorm -- the reference's VitEncoder::run
+                     (runtime/src/vit/encoder.cpp) via oracle/ref_vit_driver.cpp.
+                     The images are regenerated from the recorded seed (their
+                     SHA-256 is stored), not stored.
+
+    python tests/golden/make_golden.py vit_base_c5     (one fixture)
 """
 
 from __future__ import annotations
@@ -64,10 +72,35 @@ def sample_rows(lens, n):
     return np.array(sorted(pick)[:n]) if len(pick) > n else np.array(sorted(pick))
 
 
+VIT_FIXTURES = {"vit_base_c5": ("vit-base", 3)}
+
+
+def make_vit(ref, name, key, n):
+    cfg = synth.VIT_CONFIGS[key]
+    w = synth.vit_config_weights(cfg)
+    images = synth.vit_config_images(cfg, n=n)
+    t0 = time.time()
+    out = ref.vit_encode(w, images)
+    print(f"{name}: {n} images in {time.time() - t0:.1f} s")
+    np.savez_compressed(
+        HERE / f"{name}.npz", config=key, n_images=np.int32(n),
+        image_seed=20261301 + cfg.index, image_sha256=hashlib.sha256(images.tobytes()).hexdigest(),
+        embeddings=out, weight_seed=20261201 + cfg.index,
+        weights_fingerprint=weights_fingerprint(w),
+        provenance="reference host-CPU ViT path (vit/encoder.cpp, whisper/npu_ops.cpp, -O2 "
+                   "-march=x86-64-v3) via oracle/ref_vit_driver.cpp")
+
+
 def main():
     from oracle.oracle import RefOracle
     ref = RefOracle()
+    only = set(sys.argv[1:])
+    for name, (key, n) in VIT_FIXTURES.items():
+        if not only or name in only:
+            make_vit(ref, name, key, n)
     for name, (key, n) in FIXTURES.items():
+        if only and name not in only:
+            continue
         cfg = synth.CONFIGS[key]
         w = synth.config_weights(cfg)
         ids, mask, lens = synth.config_batch(cfg)

@@ -106,3 +106,55 @@ def test_golden_fixtures_are_sane():
         np.testing.assert_allclose(np.linalg.norm(e, axis=1), 1.0, rtol=1e-5)
         assert (g["mask"].sum(1) == g["lens"]).all()
         assert (g["ids"][:, 0] == 101).all()
+
+
+# ---- ViT (benchmark configuration 5) ---------------------------------------
+
+def _small_vit():
+    from nebw import synth
+    arch = synth.VitArch("vit-test", 2, 768, 12, 3072, image_size=32)
+    return arch, synth.make_vit_weights(arch, 7), synth.make_images(3, arch, 8)
+
+
+def test_port_vit_bit_exact_vs_reference(port_oracle, ref_oracle):
+    """The C restatement of VitEncoder::run against the reference's own
+    vit/encoder.cpp + whisper/npu_ops.cpp host path: every row, bit for bit."""
+    _, w, imgs = _small_vit()
+    a, ha = port_oracle.vit_encode(w, imgs, hidden=True)
+    b, hb = ref_oracle.vit_encode(w, imgs, hidden=True)
+    np.testing.assert_array_equal(ha, hb)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_vit_im2col_order(port_oracle):
+    """Patch row p*n+q holds channel-major (c, i, j) pixels
+    (runtime/src/vit/image.cpp:732-755), checked against numpy's reshape."""
+    from nebw import synth
+    img = synth.make_images(1, synth.VIT_BASE, 3)[0]
+    P, n = 16, 224 // 16
+    want = img.reshape(3, n, P, n, P).transpose(1, 3, 0, 2, 4).reshape(n * n, 3 * P * P)
+    np.testing.assert_array_equal(port_oracle.vit_im2col(img, P), want)
+
+
+def test_vit_golden_inputs_regenerate():
+    import hashlib
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    from make_golden import weights_fingerprint
+
+    from nebw import synth
+    g = load_golden("vit_base_c5")
+    cfg = synth.VIT_CONFIGS[str(g["config"])]
+    assert weights_fingerprint(synth.vit_config_weights(cfg)) == str(g["weights_fingerprint"])
+    imgs = synth.vit_config_images(cfg, n=int(g["n_images"]))
+    assert hashlib.sha256(imgs.tobytes()).hexdigest() == str(g["image_sha256"])
+    assert np.isfinite(g["embeddings"]).all()
+
+
+def test_port_matches_golden_vit(port_oracle):
+    from nebw import synth
+    g = load_golden("vit_base_c5")
+    cfg = synth.VIT_CONFIGS["vit-base"]
+    got = port_oracle.vit_encode(synth.vit_config_weights(cfg),
+                                 synth.vit_config_images(cfg, n=1))
+    np.testing.assert_array_equal(got, g["embeddings"][:1])
