@@ -462,19 +462,284 @@ def gpu_arm(args, cfg):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# configuration 5: vit-base-patch16-224 (a secondary workload, --config vit-base)
+# ---------------------------------------------------------------------------
+
+METRIC_VIT = "images/sec at vit-base-patch16-224 (CLS row)"
+
+
+def vit_flops_per_image(a: synth.VitArch) -> float:
+    """Patch GEMM + L x (the four GEMMs over n_pos rows + QK^T and PV)."""
+    H, F, S = a.hidden, a.ffn, a.n_pos
+    return (2.0 * a.n_patches * a.channels * a.patch_size ** 2 * H
+            + a.layers * (2.0 * S * (4 * H * H + 2 * H * F) + 4.0 * S * S * H))
+
+
+def vit_cpu_setup(cfg, w, workdir):
+    """(runner, kind, threads): runner(images) -> CLS rows."""
+    from oracle.oracle import REF_LIB, PortOracle, RefOracle, host_threads
+    threads = host_threads()
+    if REF_LIB.exists():
+        from nebw.npue import write_vit_container
+        path = Path(workdir) / "bench_ref_vit.npue"
+        write_vit_container(path, w)
+        sess = RefOracle().vit_session(path, threads)
+        return (lambda imgs: sess.run(imgs, w.hidden)), "reference", threads
+    port = PortOracle()
+    return (lambda imgs: port.vit_encode(w, imgs, threads=threads)), "port", threads
+
+
+def vit_cpu_baseline(cfg, w, images, budget_s=15.0):
+    with tempfile.TemporaryDirectory() as td:
+        run, kind, threads = vit_cpu_setup(cfg, w, td)
+        t0 = time.perf_counter()
+        run(images[:1])
+        t1 = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        run(images[1:2])
+        per = time.perf_counter() - t0
+        n = int(max(1, min(16, budget_s // max(per, 1e-3))))
+        t0 = time.perf_counter()
+        run(images[2:2 + n])
+        el = time.perf_counter() - t0 + per
+    return {"value": (n + 1) / el, "unit": "images/s", "cores": threads, "kind": kind,
+            "sample": f"{n + 1} images of the {cfg.batch}-image batch, {el:.1f} s timed after a "
+                      f"{t1:.1f} s warm-up (one image at a time, as VitEncoder::run takes them)",
+            "full_batch_s_extrapolated": cfg.batch * el / (n + 1)}
+
+
+def vit_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    w = synth.vit_config_weights(cfg)
+    per_step = 2
+    images = synth.vit_config_images(cfg, n=per_step * (args.warmup + args.steps))
+    with tempfile.TemporaryDirectory() as td:
+        run, kind, threads = vit_cpu_setup(cfg, w, td)
+        for i in range(args.warmup):
+            run(images[i * per_step:(i + 1) * per_step])
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            j = args.warmup + i
+            run(images[j * per_step:(j + 1) * per_step])
+        el = time.perf_counter() - t0
+    value = args.steps * per_step / el
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC_VIT, "value": value, "unit": "images/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg.key}: batch {cfg.batch} images 3x224x224",
+                   "global_batch": cfg.batch, "parallelism": "host threads",
+                   "step": f"{per_step} images of the batch per step (bounded sample)"},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind,
+                         "sample": f"{args.warmup} warm + {args.steps} timed steps of "
+                                   f"{per_step} images"},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+def vit_arm(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    import nebw
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    arch = cfg.arch
+    B, H = cfg.batch, arch.hidden
+    w = synth.vit_config_weights(cfg)
+    images = synth.vit_config_images(cfg)
+    # every image costs the same: contiguous equal shards, gathered in order
+    per = -(-B // world)
+    lo, hi = min(B, rank * per), min(B, (rank + 1) * per)
+    n_r = hi - lo
+    dev = nebw.Device(local)
+    dev.set_attention_kernel(dev.ATTN_TCGEN05 if args.attention == "tcgen05" else dev.ATTN_MMA)
+    model = nebw.VitModel.from_weights(dev, w)
+    launches_per_step = model.launch_count()
+    stream = torch.cuda.current_stream()
+    img_h = torch.from_numpy(np.ascontiguousarray(images[lo:hi])).pin_memory()
+    img_d = img_h.cuda()
+    out_d = torch.zeros((per, H), dtype=torch.float32, device="cuda")
+    gather_d = torch.zeros((world * per, H), dtype=torch.float32, device="cuda") if rank == 0 else None
+    out_h = torch.empty((world * per, H), dtype=torch.float32).pin_memory()
+
+    def step():
+        model.encode_into(img_d, out_d, n_r, stream=stream)
+        if world > 1:
+            gather_to_root(out_d, gather_d, world, rank, dist)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.6)
+    model.profile(True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    if sampler:
+        sampler.stop()
+    model.profile(False)
+    prof = model.profile_collect()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    def step_e2e():
+        if world == 1:
+            model.encode_into(img_h, out_h, n_r, host=True)   # nebw_vit_encode: H2D, pass, D2H
+            return out_h[:n_r].numpy()
+        img_d.copy_(img_h, non_blocking=True)
+        model.encode_into(img_d, out_d, n_r, stream=stream)
+        gather_to_root(out_d, gather_d, world, rank, dist)
+        if rank == 0:
+            out_h.copy_(gather_d, non_blocking=True)
+        stream.synchronize()
+        return out_h.numpy()[:B] if rank == 0 else None
+
+    for _ in range(max(1, args.warmup)):
+        res = step_e2e()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        res = step_e2e()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t.item())
+    prof_t = torch.tensor([[prof[k][1] for k in model.KERNEL_KINDS]], dtype=torch.float64,
+                          device="cuda")
+    if world > 1:
+        all_prof = [torch.zeros_like(prof_t) for _ in range(world)]
+        dist.all_gather(all_prof, prof_t)
+    else:
+        all_prof = [prof_t]
+    ok = bool(np.isfinite(res).all()) if rank == 0 else True
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = vit_cpu_baseline(cfg, w, images)
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        slow = int(np.argmax([p.sum().item() for p in all_prof]))
+        pms = dict(zip(model.KERNEL_KINDS, all_prof[slow][0].tolist()))
+        steps = args.steps
+        R = float(n_r * arch.n_pos)
+        Hf, F, L = float(H), float(arch.ffn), arch.layers
+        gemm_fl = {"gemm_qkv": 2 * R * Hf * 3 * Hf * L, "gemm_ao": 2 * R * Hf * Hf * L,
+                   "gemm_up": 2 * R * Hf * F * L, "gemm_down": 2 * R * F * Hf * L}
+        total_ms = sum(pms.values()) / steps
+        kernels = {k: {"ms_per_step": pms[k] / steps,
+                       "share": pms[k] / steps / total_ms if total_ms else None}
+                   for k in model.KERNEL_KINDS}
+        for k, fl in gemm_fl.items():
+            kernels[k]["tflops"] = fl / (pms[k] / steps / 1e3) / 1e12
+            kernels[k]["frac_of_peak"] = kernels[k]["tflops"] / peak_t
+        att_fl = 4.0 * n_r * arch.n_pos ** 2 * Hf * L
+        kernels["attention"]["tflops"] = att_fl / (pms["attention"] / steps / 1e3) / 1e12
+        kernels["attention"]["frac_of_peak"] = kernels["attention"]["tflops"] / peak_t
+        ln_bytes = R * Hf * (4 + 2) * 2 * L  # pre-LN: read x fp32, write the bf16 operand
+        kernels["layernorm"]["gbs"] = ln_bytes / (pms["layernorm"] / steps / 1e3) / 1e9
+        kernels["layernorm"]["frac_of_peak"] = kernels["layernorm"]["gbs"] / peaks["hbm_gbs"]
+        up_ms = pms["gemm_up"] / (L * steps)
+        up_flops = 2.0 * R * Hf * F
+        gemm_ms = sum(pms[k] for k in gemm_fl) / steps
+        per_img = vit_flops_per_image(arch)
+        line = {
+            "metric": METRIC_VIT, "value": B * steps / (ms_max / 1e3), "unit": "images/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{cfg.key}: {arch.name} architecture ({arch.layers}L, hidden "
+                                   f"{H}, {arch.heads} heads, FFN {arch.ffn}, pre-LN, 16x16 patch "
+                                   f"embedding, {arch.n_pos} positions), random-init N(0,0.02); "
+                                   f"batch {B} images 3x224x224 fp32 uniform [-1,1]; CLS row",
+                       "global_batch": B, "seq_len": arch.n_pos,
+                       "parallelism": f"dp{world} (equal image shards, NCCL gather to rank 0)"
+                       if world > 1 else "single GPU",
+                       "l2": "no flush: every step streams 1.2 GB of images and GBs of "
+                             "activations, far above the 126 MB L2"},
+            "e2e": {"value": B * steps / e2e_s, "unit": "images/s",
+                    "h2d_bytes_per_step": int(n_r * arch.channels * arch.image_size ** 2 * 4),
+                    "d2h_bytes_per_step": int(B * H * 4),
+                    "timer": "wall clock, synchronous per step, max over ranks"},
+            "gpu_launches": int(launches_per_step * steps * world),
+            "roofline": {"kernel": "gemm_tc<256, gelu-erf> FFN-up (R x 768 -> 3072)",
+                         "bound": "tensor", "achieved": up_flops / (up_ms / 1e3) / 1e12,
+                         "peak": peak_t, "unit": "TFLOP/s",
+                         "frac": up_flops / (up_ms / 1e3) / 1e12 / peak_t,
+                         "peak_source": f"{peak_src} bf16 dense, sustained",
+                         "traffic": None, "flops_per_launch": up_flops, "ms_per_launch": up_ms},
+            "roofline_gemm_family": {"achieved": sum(gemm_fl.values()) / (gemm_ms / 1e3) / 1e12,
+                                     "peak": peak_t, "unit": "TFLOP/s",
+                                     "frac": sum(gemm_fl.values()) / (gemm_ms / 1e3) / 1e12 / peak_t},
+            "end_to_end_frac": {"tflops": B * per_img / (ms_max / steps / 1e3) / 1e12,
+                                "frac": B * per_img / (ms_max / steps / 1e3) / 1e12 / (peak_t * world)},
+            "kernels": kernels,
+            "outputs_finite": ok,
+        }
+        if sampler:
+            line["clocks"] = sampler.summary()
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+    model.close()
+    dev.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["nebw", "reference"], default="nebw")
-    ap.add_argument("--config", default="bge-large", choices=sorted(synth.CONFIGS))
+    ap.add_argument("--config", default="bge-large",
+                    choices=sorted(synth.CONFIGS) + sorted(synth.VIT_CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attention", choices=["mma", "tcgen05"], default="tcgen05",
                     help="attention kernel for head_dim 64")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.config in synth.VIT_CONFIGS:
+        cfg = synth.VIT_CONFIGS[args.config]
+        return vit_reference_arm(args, cfg) if args.impl == "reference" else vit_arm(args, cfg)
     cfg = synth.CONFIGS[args.config]
     if args.impl == "reference":
         return reference_arm(args, cfg)

@@ -244,6 +244,61 @@ int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K_COUNT],
 int nebw_encode_device_static(nebw_model *m, const int32_t *ids_dev, const int32_t *lens_dev,
                               int32_t B, int32_t S, float *out_dev, void *stream);
 
+/* ---- ViT encoder (container arch "vit_patch16_prenorm_gelu") --------------
+ * Replaces npue::vit::VitEncoder (runtime/include/vit/encoder.hpp:87-289):
+ * its stage_all() (runtime/src/vit/encoder.cpp:23-189) becomes
+ * nebw_vit_create + nebw_vit_set_tensor or nebw_vit_load_npue, and its run()
+ * (:222-431) becomes nebw_vit_encode / nebw_vit_encode_device, which also
+ * take over the image -> patch step im2col_patches
+ * (runtime/src/vit/image.cpp:732-755).  Schedule (pre-LN):
+ *   patches = im2col(image); x = [cls; patches . W_patch + b] + pos
+ *   per layer: x += attn_out(attention(qkv(LN1(x))))
+ *              x += ffn_down(gelu_erf(ffn_up(LN2(x))))
+ *   out = LN_final(x[CLS row])            (the reference's run() returns every
+ *                                          row; the head reads the CLS row)
+ * Q's 1/sqrt(head_dim) must already be folded into the qkv operand, as
+ * containers with qkv_scale_folded (the packer's default) have it.  Every
+ * image is one unmasked sequence of (image_size/patch_size)^2 + 1 rows.
+ * GEMM operands bf16 (RNE), fp32 accumulation and residual stream, exact-erf
+ * GELU in the FFN-up epilogue, attention on the same kernels as the BERT
+ * pass, LayerNorm fp32 two-pass. */
+typedef struct nebw_vit_config {
+  int32_t num_layers, hidden, num_heads, head_dim, intermediate;
+  int32_t image_size, patch_size, num_channels;  /* hidden == channels * patch^2 */
+  float layer_norm_eps;
+} nebw_vit_config;
+
+typedef struct nebw_vit nebw_vit;
+
+int nebw_vit_create(nebw_dev *dev, const nebw_vit_config *cfg, nebw_vit **out);
+/* Tensor names of the ViT container (encoder.cpp:125-139): frontend.patch_embed
+ * [C*P*P, hidden] (+ .bias), frontend.cls_token [hidden],
+ * frontend.position_embeddings [n_pos, hidden], layer.{i}.{qkv, attn_out,
+ * ffn_up, ffn_down}[.bias], layer.{i}.{ln1,ln2}.{weight,bias},
+ * layernorm.{weight,bias}.  GEMM operands [K, N] F32 or BF16; the rest F32. */
+int nebw_vit_set_tensor(nebw_vit *m, const char *name, const void *host, int dtype, int64_t rows,
+                        int64_t cols);
+/* A gemm_layout "host" container; its classifier head is not loaded (the
+ * reference runs the head on the host, encoder.cpp:433-444). */
+int nebw_vit_load_npue(nebw_dev *dev, const char *path, nebw_vit **out);
+int nebw_vit_get_config(const nebw_vit *m, nebw_vit_config *cfg);
+int nebw_vit_destroy(nebw_vit *m);
+/* images [n, C, S, S] fp32 (normalised pixels, 16-byte aligned) -> out [n,
+ * hidden] fp32, the CLS row after the final LayerNorm.  Device buffers,
+ * asynchronous on `stream` (NULL: the device's stream). */
+int nebw_vit_encode_device(nebw_vit *m, const float *images_dev, int32_t n, float *out_dev,
+                           void *stream);
+/* The same with host buffers: copies in, the pass, copies out, synchronous. */
+int nebw_vit_encode(nebw_vit *m, const float *images_host, int32_t n, float *out_host);
+/* Kernel launches one nebw_vit_encode_device makes. */
+int nebw_vit_launch_count(const nebw_vit *m);
+/* Per-kernel device time, as nebw_model_profile: im2col under NEBW_K_PACK,
+ * the patch GEMM and the row assembly under NEBW_K_EMBED_LN, the pre-LN
+ * LayerNorms under NEBW_K_LN, the final CLS-row LayerNorm under NEBW_K_POOL. */
+int nebw_vit_profile(nebw_vit *m, int enable);
+int nebw_vit_profile_collect(nebw_vit *m, int64_t launches[NEBW_K_COUNT],
+                             double ms[NEBW_K_COUNT]);
+
 #ifdef __cplusplus
 }
 #endif

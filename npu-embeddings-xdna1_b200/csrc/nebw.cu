@@ -1339,3 +1339,9 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   if ((rc = make_tmap_kmajor(&v.map_qkv_att, v.qkv, rows, 3 * H, 128))) return rc;
   return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));
 }
+
+// ---------------------------------------------------------------------------
+// The ViT encoder: same translation unit (it uses the helpers above).
+// ---------------------------------------------------------------------------
+
+#include "vit.cuh"

@@ -268,4 +268,8 @@ int64_t NpueFile::config_int(const std::string &key) const {
   return std::stoll(config_string(key));
 }
 
+double NpueFile::config_double(const std::string &key) const {
+  return std::stod(config_string(key));
+}
+
 }  // namespace nebw

@@ -50,6 +50,7 @@ class NpueFile {
   bool has(const std::string &name) const { return tensors_.count(name) != 0; }
   // config values, as the reference reads them (model.cpp:366-380)
   int64_t config_int(const std::string &key) const;
+  double config_double(const std::string &key) const;
   std::string config_string(const std::string &key) const;
   bool has_config(const std::string &key) const { return config_.find(key) != nullptr; }
   uint32_t arch() const { return arch_; }

@@ -91,7 +91,7 @@ __device__ __forceinline__ void ln_row_regs(float4 (&v)[NV], const float *__rest
     y.y = fmaf((v[i].y - mean) * is, gg.y, bb.y);
     y.z = fmaf((v[i].z - mean) * is, gg.z, bb.z);
     y.w = fmaf((v[i].w - mean) * is, gg.w, bb.w);
-    *reinterpret_cast<float4 *>(xo + c) = y;
+    if (xo) *reinterpret_cast<float4 *>(xo + c) = y;
     if (ao) {
       uint2 pk;
       pk.x = pack_bf16x2(y.x, y.y);

@@ -41,6 +41,12 @@ class Config(C.Structure):
         ("layer_norm_eps", C.c_float)]
 
 
+class VitConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "num_layers", "hidden", "num_heads", "head_dim", "intermediate", "image_size",
+        "patch_size", "num_channels")] + [("layer_norm_eps", C.c_float)]
+
+
 _lib = None
 
 
@@ -94,6 +100,16 @@ def lib() -> C.CDLL:
         "nebw_set_attention_kernel": ([vp, C.c_int], C.c_int),
         "nebw_model_profile": ([vp, C.c_int], C.c_int),
         "nebw_model_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
+        "nebw_vit_create": ([vp, C.POINTER(VitConfig), C.POINTER(vp)], C.c_int),
+        "nebw_vit_set_tensor": ([vp, C.c_char_p, vp, C.c_int, i64, i64], C.c_int),
+        "nebw_vit_load_npue": ([vp, C.c_char_p, C.POINTER(vp)], C.c_int),
+        "nebw_vit_get_config": ([vp, C.POINTER(VitConfig)], C.c_int),
+        "nebw_vit_destroy": ([vp], C.c_int),
+        "nebw_vit_encode_device": ([vp, vp, i32, vp, vp], C.c_int),
+        "nebw_vit_encode": ([vp, vp, i32, vp], C.c_int),
+        "nebw_vit_launch_count": ([vp], C.c_int),
+        "nebw_vit_profile": ([vp, C.c_int], C.c_int),
+        "nebw_vit_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -321,3 +337,90 @@ class Model:
         else:
             _check(lib().nebw_encode_device(self.h, _addr(ids), _addr(lens), B, S, _addr(out),
                                             _stream(stream)))
+
+
+class VitModel:
+    """A staged ViT encoder (container arch vit_patch16_prenorm_gelu) on one
+    device: images [n, C, S, S] fp32 -> the CLS row after the final
+    LayerNorm, [n, hidden] fp32."""
+
+    KERNEL_KINDS = Model.KERNEL_KINDS
+
+    def __init__(self, dev: Device, handle):
+        self.dev = dev
+        self.h = handle
+        cfg = VitConfig()
+        _check(lib().nebw_vit_get_config(self.h, C.byref(cfg)))
+        self.cfg = cfg
+
+    @classmethod
+    def from_weights(cls, dev: Device, w):
+        """Stage a nebw.synth.VitWeights on `dev`."""
+        a = w.arch
+        cfg = VitConfig(num_layers=w.layers, hidden=a.hidden, num_heads=a.heads,
+                        head_dim=a.head_dim, intermediate=a.ffn, image_size=a.image_size,
+                        patch_size=a.patch_size, num_channels=a.channels,
+                        layer_norm_eps=a.ln_eps)
+        h = C.c_void_p()
+        _check(lib().nebw_vit_create(dev.h, C.byref(cfg), C.byref(h)))
+        m = cls(dev, h)
+        try:
+            for name, arr in w.tensors():
+                x = np.ascontiguousarray(arr, np.float32)
+                rows, cols = (x.shape[0], x.shape[1]) if x.ndim == 2 else (1, x.shape[0])
+                _check(lib().nebw_vit_set_tensor(m.h, name.encode(), x.ctypes.data, F32, rows,
+                                                 cols))
+        except Exception:
+            m.close()
+            raise
+        return m
+
+    @classmethod
+    def from_npue(cls, dev: Device, path):
+        h = C.c_void_p()
+        _check(lib().nebw_vit_load_npue(dev.h, str(path).encode(), C.byref(h)))
+        return cls(dev, h)
+
+    def close(self):
+        if self.h:
+            lib().nebw_vit_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def hidden(self) -> int:
+        return self.cfg.hidden
+
+    def launch_count(self) -> int:
+        return lib().nebw_vit_launch_count(self.h)
+
+    def profile(self, enable: bool = True):
+        _check(lib().nebw_vit_profile(self.h, int(enable)))
+
+    def profile_collect(self) -> dict:
+        n = len(self.KERNEL_KINDS)
+        launches = (C.c_int64 * n)()
+        ms = (C.c_double * n)()
+        _check(lib().nebw_vit_profile_collect(self.h, launches, ms))
+        return {k: (int(launches[i]), float(ms[i])) for i, k in enumerate(self.KERNEL_KINDS)}
+
+    def encode(self, images: np.ndarray) -> np.ndarray:
+        """Host in, host out."""
+        images = np.ascontiguousarray(images, np.float32)
+        out = np.empty((images.shape[0], self.hidden), np.float32)
+        _check(lib().nebw_vit_encode(self.h, images.ctypes.data, images.shape[0],
+                                     out.ctypes.data))
+        return out
+
+    def encode_into(self, images, out, n: int, host=False, stream=None):
+        """Host or device buffers by address; the device form is asynchronous."""
+        if host:
+            _check(lib().nebw_vit_encode(self.h, _addr(images), n, _addr(out)))
+        else:
+            _check(lib().nebw_vit_encode_device(self.h, _addr(images), n, _addr(out),
+                                                _stream(stream)))

@@ -234,6 +234,16 @@ class RefOracle:
         L.nebw_ref_vit_encode.argtypes = [C.c_char_p, _f32p, C.c_int32, C.c_int32, _f32p, _f32p,
                                           C.c_char_p, C.c_int32]
         L.nebw_ref_vit_encode.restype = C.c_int
+        L.nebw_ref_vit_session_open.argtypes = [C.c_char_p, C.c_int32, C.c_char_p, C.c_int32]
+        L.nebw_ref_vit_session_open.restype = C.c_void_p
+        L.nebw_ref_vit_session_run.argtypes = [C.c_void_p, _f32p, C.c_int32, _f32p, C.c_char_p,
+                                               C.c_int32]
+        L.nebw_ref_vit_session_run.restype = C.c_int
+        L.nebw_ref_vit_session_close.argtypes = [C.c_void_p]
+
+    def vit_session(self, path, threads=None):
+        """A persistent reference ViT encoder over a container (for timing)."""
+        return _RefVitSession(self.lib, path, threads or host_threads())
 
     def vit_encode_container(self, path, images, hidden_size, n_pos=None, threads=None,
                              hidden=False):
@@ -353,3 +363,29 @@ class _RefSession:
         if self.h:
             self.lib.nebw_ref_session_close(self.h)
             self.h = None
+
+
+class _RefVitSession:
+    def __init__(self, lib, path, threads):
+        self.lib = lib
+        err = C.create_string_buffer(4096)
+        self.h = lib.nebw_ref_vit_session_open(str(path).encode(), threads, err, 4096)
+        if not self.h:
+            raise RuntimeError(err.value.decode())
+
+    def run(self, images, hidden_size):
+        images = np.ascontiguousarray(images, np.float32)
+        out = np.zeros((images.shape[0], hidden_size), np.float32)
+        err = C.create_string_buffer(4096)
+        if self.lib.nebw_ref_vit_session_run(self.h, _ptr(images), images.shape[0], _ptr(out),
+                                             err, 4096):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def close(self):
+        if self.h:
+            self.lib.nebw_ref_vit_session_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

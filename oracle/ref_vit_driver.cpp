@@ -86,4 +86,53 @@ int nebw_ref_vit_encode(const char *npue_path, const float *images, int32_t n_im
   }
 }
 
+// A persistent reference ViT encoder over one container, for timing:
+// open() stages it once (VitEncoder::stage_all), run() is the reference's
+// steady-state per-image cost (im2col + VitEncoder::run).
+struct RefVitSession {
+  npue::File f;
+  npue::vit::Geometry g;
+  app::Pool pool;
+  npu::Device dev;
+  npu::Design design;
+  npue::vit::VitEncoder enc;
+  RefVitSession(const char *path, int threads)
+      : f(path), g(npue::vit::read_geometry(f, path)), pool(threads > 0 ? threads : 1),
+        design(dev, "oracle-host"), enc(f, design, pool, g) {
+    npue::vit::EncoderStreams st;
+    st.rows = g.n_pos;
+    enc.set_streams(st);
+    enc.stage_all();
+  }
+};
+
+void *nebw_ref_vit_session_open(const char *npue_path, int32_t threads, char *err,
+                                int32_t errlen) {
+  try {
+    return new RefVitSession(npue_path, threads);
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return nullptr;
+  }
+}
+
+int nebw_ref_vit_session_run(void *handle, const float *images, int32_t n_images, float *cls_out,
+                             char *err, int32_t errlen) {
+  try {
+    auto *s = static_cast<RefVitSession *>(handle);
+    const int64_t img_elems = s->g.num_channels * s->g.image_size * s->g.image_size;
+    for (int64_t i = 0; i < n_images; ++i) {
+      const std::vector<float> x = s->enc.run(patches_of(images + i * img_elems, s->g));
+      std::memcpy(cls_out + i * s->g.d_model, x.data(),
+                  static_cast<size_t>(s->g.d_model) * sizeof(float));
+    }
+    return 0;
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return 1;
+  }
+}
+
+void nebw_ref_vit_session_close(void *handle) { delete static_cast<RefVitSession *>(handle); }
+
 }  // extern "C"
