@@ -669,7 +669,9 @@ def vit_arm(args, cfg):
         att_fl = 4.0 * n_r * arch.n_pos ** 2 * Hf * L
         kernels["attention"]["tflops"] = att_fl / (pms["attention"] / steps / 1e3) / 1e12
         kernels["attention"]["frac_of_peak"] = kernels["attention"]["tflops"] / peak_t
-        ln_bytes = R * Hf * (4 + 2) * 2 * L  # pre-LN: read x fp32, write the bf16 operand
+        # the first LN1 reads x and writes the bf16 operand (6 B/element); every
+        # later site reads x and y, writes x and the operand (12 B/element)
+        ln_bytes = R * Hf * (6 + 12 * (2 * L - 1))
         kernels["layernorm"]["gbs"] = ln_bytes / (pms["layernorm"] / steps / 1e3) / 1e9
         kernels["layernorm"]["frac_of_peak"] = kernels["layernorm"]["gbs"] / peaks["hbm_gbs"]
         up_ms = pms["gemm_up"] / (L * steps)

@@ -259,7 +259,9 @@ int nebw_encode_device_static(nebw_model *m, const int32_t *ids_dev, const int32
  * Q's 1/sqrt(head_dim) must already be folded into the qkv operand, as
  * containers with qkv_scale_folded (the packer's default) have it.  Every
  * image is one unmasked sequence of (image_size/patch_size)^2 + 1 rows.
- * GEMM operands bf16 (RNE), fp32 accumulation and residual stream, exact-erf
+ * GEMM operands bf16 (RNE), fp32 accumulation, every GEMM output narrowed
+ * to bf16 RNE (as the reference's array path narrows each C tile), the
+ * residual add fused into the next LayerNorm, fp32 residual stream, exact-erf
  * GELU in the FFN-up epilogue, attention on the same kernels as the BERT
  * pass, LayerNorm fp32 two-pass. */
 typedef struct nebw_vit_config {
@@ -293,8 +295,9 @@ int nebw_vit_encode(nebw_vit *m, const float *images_host, int32_t n, float *out
 /* Kernel launches one nebw_vit_encode_device makes. */
 int nebw_vit_launch_count(const nebw_vit *m);
 /* Per-kernel device time, as nebw_model_profile: im2col under NEBW_K_PACK,
- * the patch GEMM and the row assembly under NEBW_K_EMBED_LN, the pre-LN
- * LayerNorms under NEBW_K_LN, the final CLS-row LayerNorm under NEBW_K_POOL. */
+ * the patch GEMM and the row assembly under NEBW_K_EMBED_LN, the LayerNorm
+ * sites (each fused with the residual add before it) under NEBW_K_LN, the
+ * last residual add with the final CLS-row LayerNorm under NEBW_K_POOL. */
 int nebw_vit_profile(nebw_vit *m, int enable);
 int nebw_vit_profile_collect(nebw_vit *m, int64_t launches[NEBW_K_COUNT],
                              double ms[NEBW_K_COUNT]);

@@ -9,18 +9,22 @@
 //   vit_im2col      patches = bf16(im2col(image))         (image.cpp:732-755)
 //   gemm PATCH      pe = patches . W_patch + b            (fp32)
 //   vit_assemble    x = [cls; pe] + pos                   (encoder.cpp:267-281)
+//   ln_rows         a = bf16(LN1_0(x))                    (x unchanged: pre-LN)
 //   per layer L:
-//     ln_rows       a = bf16(LN1(x))                      (x unchanged: pre-LN)
 //     gemm QKV      qkv = bf16(a . Wqkv + b)
 //     attention     ctx = softmax(Q K^T) V               (per image, per head)
-//     gemm AO       x = (ctx . Wao + b) + x               (fp32, in place)
-//     ln_rows       a = bf16(LN2(x))
+//     gemm AO       y = bf16(ctx . Wao + b)
+//     ln_rows       x += y;  a = bf16(LN2(x))
 //     gemm UP       h = bf16(gelu_erf(a . Wup + b))
-//     gemm DOWN     x = (h . Wdn + b) + x                 (fp32, in place)
-//   ln_rows         out = LN_final(x[CLS rows])           (fp32)
+//     gemm DOWN     y = bf16(h . Wdn + b)
+//     ln_rows       x += y;  a = bf16(LN1_L+1(x))          (last layer: the
+//                   final LayerNorm of the CLS rows only, out = LN(x + y), fp32)
 //
-// The residual adds keep the reference's rounding order: the GEMM's
-// (acc + bias) first, then + x (encoder.cpp:395-399, :408-411).
+// The residual adds keep the reference's order -- the GEMM's (acc + bias)
+// first, then + x (encoder.cpp:395-399, :408-411) -- with the sublayer output
+// narrowed to bf16 RNE in between, as the reference's array path narrows
+// every GEMM C tile (kernels/narrow_f32_bf16.cc:50-90); the residual stream
+// and the LayerNorm arithmetic stay fp32.
 
 #include "vitops.cuh"
 
@@ -41,6 +45,7 @@ struct nebw_vit {
   // workspace for img_cap images (rows_cap = img_cap * n_pos)
   int64_t img_cap = 0;
   float *x = nullptr;                                      // residual stream fp32 [R, H]
+  __nv_bfloat16 *y = nullptr;                              // sublayer output bf16 [R, H]
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *len = nullptr, *off = nullptr, *att_items = nullptr;
   float *images = nullptr, *out = nullptr;                 // staging for nebw_vit_encode
@@ -48,7 +53,7 @@ struct nebw_vit {
   // qkv buffer and the patch GEMM's fp32 output in the h buffer, both dead
   // at that point of the pass
   CUtensorMap map_a, map_ctx, map_h, map_patches;
-  CUtensorMap out_qkv, out_h, out_x, out_pe, map_qkv_att;
+  CUtensorMap out_qkv, out_h, out_y, out_pe, map_qkv_att;
   bool prof = false;
   std::vector<std::pair<cudaEvent_t, int>> marks;
   std::vector<cudaEvent_t> ev_pool;
@@ -58,13 +63,14 @@ struct nebw_vit {
 namespace {
 
 void vit_free_workspace(nebw_vit *m) {
-  for (void *p : {static_cast<void *>(m->x), static_cast<void *>(m->a),
+  for (void *p : {static_cast<void *>(m->x), static_cast<void *>(m->y), static_cast<void *>(m->a),
                   static_cast<void *>(m->qkv), static_cast<void *>(m->ctx),
                   static_cast<void *>(m->h), static_cast<void *>(m->len),
                   static_cast<void *>(m->off), static_cast<void *>(m->att_items),
                   static_cast<void *>(m->images), static_cast<void *>(m->out)})
     cudaFree(p);
   m->x = nullptr;
+  m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
   m->len = m->off = m->att_items = nullptr;
   m->images = m->out = nullptr;
@@ -88,6 +94,7 @@ int vit_ensure_workspace(nebw_vit *m, int64_t n) {
   };
   int rc = 0;
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->x), R * H * 4);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->y), R * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->a), R * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->qkv), R * 3 * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ctx), R * H * 2);
@@ -108,7 +115,7 @@ int vit_ensure_workspace(nebw_vit *m, int64_t n) {
   if ((rc = make_tmap_kmajor(&m->map_patches, m->qkv, NP, m->patch_dim, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_out(&m->out_qkv, m->qkv, R, 3 * H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
-  if ((rc = make_tmap_out(&m->out_x, m->x, R, H, false))) return rc;
+  if ((rc = make_tmap_out(&m->out_y, m->y, R, H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_pe, m->h, NP, H, false))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
   return NEBW_OK;
@@ -149,23 +156,26 @@ int vit_mark(nebw_vit *m, int kind, cudaStream_t st) {
 }
 
 template <int NV>
-void launch_ln_rows_nv(const float *x, int64_t stride, int rows, const float *g, const float *b,
-                       float eps, float *out_f32, __nv_bfloat16 *out_a, cudaStream_t st) {
+void launch_ln_rows_nv(float *x, const __nv_bfloat16 *y, int64_t stride, int rows,
+                       const float *g, const float *b, float eps, int write_x, float *out_f32,
+                       __nv_bfloat16 *out_a, cudaStream_t st) {
   const int grid = (rows + nebw::kRowWarps - 1) / nebw::kRowWarps;
-  nebw::ln_rows_kernel<NV><<<grid, nebw::kRowWarps * 32, 0, st>>>(x, stride, rows, g, b, eps,
-                                                                   out_f32, out_a);
+  nebw::ln_rows_kernel<NV><<<grid, nebw::kRowWarps * 32, 0, st>>>(x, y, stride, rows, g, b, eps,
+                                                                   write_x, out_f32, out_a);
 }
 
-int launch_ln_rows(const float *x, int64_t stride, int64_t rows, int64_t H, const float *g,
-                   const float *b, float eps, float *out_f32, __nv_bfloat16 *out_a,
-                   cudaStream_t st) {
+// ln_rows_kernel: v = x (+ y), optionally written back to x; LN(v) to
+// out_f32 and/or out_a.
+int launch_ln_rows(float *x, const __nv_bfloat16 *y, int64_t stride, int64_t rows, int64_t H,
+                   const float *g, const float *b, float eps, bool write_x, float *out_f32,
+                   __nv_bfloat16 *out_a, cudaStream_t st) {
   NEBW_REQUIRE(H % 128 == 0 && H >= 128 && H <= 2048, "LayerNorm width %lld refused",
                static_cast<long long>(H));
   if (rows <= 0) return NEBW_OK;
   const int r = static_cast<int>(rows);
   switch (H / 128) {
 #define NEBW_LNR_CASE(n) \
-  case n: launch_ln_rows_nv<n>(x, stride, r, g, b, eps, out_f32, out_a, st); break;
+  case n: launch_ln_rows_nv<n>(x, y, stride, r, g, b, eps, write_x, out_f32, out_a, st); break;
     NEBW_LNR_CASE(1) NEBW_LNR_CASE(2) NEBW_LNR_CASE(3) NEBW_LNR_CASE(4) NEBW_LNR_CASE(5)
     NEBW_LNR_CASE(6) NEBW_LNR_CASE(7) NEBW_LNR_CASE(8) NEBW_LNR_CASE(9) NEBW_LNR_CASE(10)
     NEBW_LNR_CASE(11) NEBW_LNR_CASE(12) NEBW_LNR_CASE(13) NEBW_LNR_CASE(14) NEBW_LNR_CASE(15)
@@ -229,12 +239,15 @@ int vit_encode_device(nebw_vit *m, const float *images, int n, float *out, cudaS
     }
   }
   a.M = static_cast<int>(R);
+  // LN1 of layer 0; every later LayerNorm site is fused with the residual add
+  // before it
+  if ((rc = vit_mark(m, NEBW_K_LN, st))) return rc;
+  if ((rc = launch_ln_rows(m->x, nullptr, 1, R, H, m->layers[0].ln1_g, m->layers[0].ln1_b,
+                           c.layer_norm_eps, false, nullptr, m->a, st)))
+    return rc;
   for (int L = 0; L < c.num_layers; ++L) {
     const VitLayerW &w = m->layers[L];
     // x += attn_out(attention(qkv(LN1(x))))
-    if ((rc = vit_mark(m, NEBW_K_LN, st))) return rc;
-    if ((rc = launch_ln_rows(m->x, 1, R, H, w.ln1_g, w.ln1_b, c.layer_norm_eps, nullptr, m->a, st)))
-      return rc;
     a.N = static_cast<int>(3 * H);
     a.K = static_cast<int>(H);
     a.bias = w.b_qkv;
@@ -253,34 +266,40 @@ int vit_encode_device(nebw_vit *m, const float *images, int n, float *out, cudaS
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(H);
     a.bias = w.b_ao;
-    a.resid = m->x;
-    a.out = m->x;
+    a.out = m->y;
     if ((rc = vit_mark(m, NEBW_K_GEMM_AO, st))) return rc;
-    if ((rc = launch_gemm(d, w.ao, m->map_ctx, m->out_x, nebw::kEpiF32Resid, a, st))) return rc;
-    // x += ffn_down(gelu_erf(ffn_up(LN2(x))))
+    if ((rc = launch_gemm(d, w.ao, m->map_ctx, m->out_y, nebw::kEpiBf16, a, st))) return rc;
     if ((rc = vit_mark(m, NEBW_K_LN, st))) return rc;
-    if ((rc = launch_ln_rows(m->x, 1, R, H, w.ln2_g, w.ln2_b, c.layer_norm_eps, nullptr, m->a, st)))
+    if ((rc = launch_ln_rows(m->x, m->y, 1, R, H, w.ln2_g, w.ln2_b, c.layer_norm_eps, true,
+                             nullptr, m->a, st)))
       return rc;
+    // x += ffn_down(gelu_erf(ffn_up(LN2(x))))
     a.N = static_cast<int>(F);
     a.K = static_cast<int>(H);
     a.bias = w.b_up;
-    a.resid = nullptr;
     a.out = m->h;
     if ((rc = vit_mark(m, NEBW_K_GEMM_UP, st))) return rc;
     if ((rc = launch_gemm(d, w.up, m->map_a, m->out_h, nebw::kEpiBf16Erf, a, st))) return rc;
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(F);
     a.bias = w.b_dn;
-    a.resid = m->x;
-    a.out = m->x;
+    a.out = m->y;
     if ((rc = vit_mark(m, NEBW_K_GEMM_DOWN, st))) return rc;
-    if ((rc = launch_gemm(d, w.dn, m->map_h, m->out_x, nebw::kEpiF32Resid, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.dn, m->map_h, m->out_y, nebw::kEpiBf16, a, st))) return rc;
+    if (L + 1 < c.num_layers) {
+      if ((rc = vit_mark(m, NEBW_K_LN, st))) return rc;
+      if ((rc = launch_ln_rows(m->x, m->y, 1, R, H, m->layers[L + 1].ln1_g,
+                               m->layers[L + 1].ln1_b, c.layer_norm_eps, true, nullptr, m->a,
+                               st)))
+        return rc;
+    } else {
+      // the last residual add and the final LayerNorm, CLS rows only
+      if ((rc = vit_mark(m, NEBW_K_POOL, st))) return rc;
+      if ((rc = launch_ln_rows(m->x, m->y, m->n_pos, n, H, m->lnf_g, m->lnf_b, c.layer_norm_eps,
+                               false, out, nullptr, st)))
+        return rc;
+    }
   }
-  // the final LayerNorm of the CLS rows
-  if ((rc = vit_mark(m, NEBW_K_POOL, st))) return rc;
-  if ((rc = launch_ln_rows(m->x, m->n_pos, n, H, m->lnf_g, m->lnf_b, c.layer_norm_eps, out,
-                           nullptr, st)))
-    return rc;
   return vit_mark(m, -1, st);
 }
 
@@ -495,8 +514,7 @@ extern "C" int nebw_vit_encode(nebw_vit *m, const float *images, int32_t n, floa
 extern "C" int nebw_vit_launch_count(const nebw_vit *m) {
   if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
   const bool tc = vit_tc_attention(m);
-  return 4 + (tc ? 1 : 0) + m->cfg.num_layers * (6 + attention_launches(tc ? 64 : 0, m->n_pos)) +
-         1;
+  return 5 + (tc ? 1 : 0) + m->cfg.num_layers * (6 + attention_launches(tc ? 64 : 0, m->n_pos));
 }
 
 extern "C" int nebw_vit_profile(nebw_vit *m, int enable) {

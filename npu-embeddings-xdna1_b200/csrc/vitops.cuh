@@ -1,7 +1,7 @@
 // Memory-bound kernels of the ViT encoder pass (arch vit_patch16_prenorm_gelu):
-// the image -> patch-row step, the CLS/position assembly, the pre-LN
-// LayerNorm that leaves the residual stream untouched, and the uniform
-// sequence table the attention kernels read.
+// the image -> patch-row step, the CLS/position assembly, the residual add
+// fused with the pre-LN LayerNorm that follows it, and the uniform sequence
+// table the attention kernels read.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -63,24 +63,41 @@ __global__ void __launch_bounds__(256)
   *reinterpret_cast<float4 *>(x + r * H + col) = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
-// LayerNorm of rows r = 0..rows-1 read at x + r * stride_rows * H, written
-// out of place: out_f32[r] (fp32, may be null) and/or out_a[r] (bf16 RNE,
-// may be null).  The pre-LN sites (the GEMM operand of each sublayer) leave
-// the residual stream as it is; the final LayerNorm reads only the CLS rows
-// (stride n_pos).  Warp per row, two-pass fp32 as layernorm_kernel.
+// LayerNorm of rows r = 0..rows-1 of the residual stream, read at
+// x + r * stride_rows * H, with the sublayer output y (bf16, same row layout;
+// may be null) added first:
+//   v = x[r] (+ y[r]);  if write_x: x[r] = v
+//   out_f32[r] = LN(v) (may be null);  out_a[r] = bf16(LN(v)) (may be null)
+// This is the pre-LN schedule's residual add (x += sublayer, encoder.cpp:
+// 395-399, :408-411) fused with the next LayerNorm site, which reads the
+// updated stream; the final LayerNorm reads only the CLS rows (stride n_pos)
+// and writes nothing back.  Warp per row, two-pass fp32 as layernorm_kernel.
 template <int NV>
 __global__ void __launch_bounds__(kRowWarps * 32)
-    ln_rows_kernel(const float *__restrict__ x, int64_t stride_rows, int rows,
-                   const float *__restrict__ g, const float *__restrict__ bta, float eps,
+    ln_rows_kernel(float *__restrict__ x, const __nv_bfloat16 *__restrict__ y,
+                   int64_t stride_rows, int rows, const float *__restrict__ g,
+                   const float *__restrict__ bta, float eps, int write_x,
                    float *__restrict__ out_f32, __nv_bfloat16 *__restrict__ out_a) {
   const int H = NV * 128;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const float *xr = x + static_cast<int64_t>(row) * stride_rows * H;
+  const int64_t at = static_cast<int64_t>(row) * stride_rows * H;
+  float *xr = x + at;
   float4 v[NV];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) v[i] = *reinterpret_cast<const float4 *>(xr + (i * 32 + lane) * 4);
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    v[i] = *reinterpret_cast<const float4 *>(xr + c);
+    if (y) {
+      const float4 w = load4(y + at + c);
+      v[i].x = v[i].x + w.x;
+      v[i].y = v[i].y + w.y;
+      v[i].z = v[i].z + w.z;
+      v[i].w = v[i].w + w.w;
+      if (write_x) *reinterpret_cast<float4 *>(xr + c) = v[i];
+    }
+  }
   ln_row_regs<NV>(v, g, bta, eps, H, lane,
                   out_f32 ? out_f32 + static_cast<int64_t>(row) * H : nullptr,
                   out_a ? out_a + static_cast<int64_t>(row) * H : nullptr);
