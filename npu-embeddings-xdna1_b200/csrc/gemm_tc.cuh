@@ -630,6 +630,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int col_half = ((warp - 2) >> 2) * kHalf;
     const int row_base = static_cast<int>(rank) * kGemmBM + quarter * 32;  // this warp's 32 rows
     uint8_t *my_staging = staging + (warp - 2) * 2 * S::kChunkBytes;
+    // a warp's 8 KB of staging holds two fp32 or four bf16 32 x 32 chunks:
+    // that many stores may still be reading it while the next is written
+    constexpr bool kF32Out = EPI == kEpiF32 || EPI == kEpiF32Resid;
+    constexpr int kOutChunk = kF32Out ? S::kChunkBytes : S::kChunkBytes / 2;
+    constexpr int kSlots = 2 * S::kChunkBytes / kOutChunk;
     int nstore = 0;  // bulk stores this warp has issued (lane 0)
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
@@ -658,8 +663,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const int col0 = nb * BN + col_half + c * 32;
         if constexpr (kTmaStore) {
           if (row0 < M && col0 < p.N) {  // warp-uniform
-            uint8_t *chunk = my_staging + (nstore & 1) * S::kChunkBytes;
-            if (lane == 0) bulk_wait_group_read<1>();  // the store that last read `chunk` is done
+            uint8_t *chunk = my_staging + (nstore % kSlots) * kOutChunk;
+            // the store that last read `chunk` is done
+            if (lane == 0) bulk_wait_group_read<kSlots - 1>();
             __syncwarp();
             epi_stage32<EPI>(p, col0, cur, chunk, lane);
             fence_proxy_async_smem();
