@@ -5,9 +5,10 @@
 // warp-specialised so that loads, tensor-core products and the softmax of
 // different key blocks (and of consecutive items) overlap:
 //
-//   warp 0      TMA: the Q tile once per item, then K_j and V_j of the packed
-//               Q|K|V rows (128-byte swizzled) through separate 2-stage
-//               rings, so K_j+2 can land while V_j is still being read
+//   warp 0      TMA: the Q tile once per item through a 2-slot ring (the
+//               next item's Q lands while this one runs), then K_j and V_j
+//               of the packed Q|K|V rows (128-byte swizzled) in issue order
+//               through a 3-slot ring
 //   warp 1      tcgen05.mma from one thread, software-pipelined inside an
 //               item so that the softmax of key block j can start before
 //               P_j-1 V_j-1 runs (an item's last P V is issued as soon as its
@@ -58,10 +59,11 @@ constexpr int kAttnTcD = 64;
 constexpr int kAttnTcTmemCols = 256;  // S [0,128), O [128,192)
 
 struct AttnTcShape {
-  static constexpr int kQ = 0;                      // 16 KB
-  static constexpr int kK0 = 16384;                 // K stages 0, 1: 16 KB each
-  static constexpr int kV0 = kK0 + 2 * 16384;       // V stages 0, 1: 16 KB each
-  static constexpr int kP = kV0 + 2 * 16384;        // P, 32 KB (2 K-blocks of 64 keys)
+  static constexpr int kTile = 16384;               // one 128 x 64 bf16 tile
+  static constexpr int kQSlots = 2, kKvSlots = 3;
+  static constexpr int kQ0 = 0;                     // Q ring: 2 slots
+  static constexpr int kKv0 = kQSlots * kTile;      // K/V ring: 3 slots, K_j V_j K_j+1 ...
+  static constexpr int kP = kKv0 + kKvSlots * kTile;  // P, 32 KB (2 K-blocks of 64 keys)
   static constexpr int kBars = kP + 32768;          // barriers
   static constexpr int kSmemBytes = kBars + 256;    // 114,944 B: two CTAs per SM
 };
@@ -112,11 +114,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     return;
   }
   uint64_t *bars = smem_at<uint64_t>(smem, S::kBars);
-  uint64_t *q_full = bars + 0, *q_free = bars + 1;
-  uint64_t *k_full = bars + 2;    // [2]
-  uint64_t *k_empty = bars + 4;   // [2]
-  uint64_t *v_full = bars + 6;    // [2]
-  uint64_t *v_empty = bars + 8;   // [2]
+  uint64_t *q_full = bars + 0;    // [2]
+  uint64_t *q_empty = bars + 2;   // [2]
+  uint64_t *kv_full = bars + 4;   // [3]
+  uint64_t *kv_empty = bars + 7;  // [3]
   uint64_t *s_full = bars + 10, *s_free = bars + 11;
   uint64_t *p_full = bars + 12;
   uint64_t *o_full = bars + 13, *o_free = bars + 14;
@@ -126,13 +127,13 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQKV);
-    mbar_init(q_full, 1);
-    mbar_init(q_free, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full + s, 1);
-      mbar_init(k_empty + s, 1);
-      mbar_init(v_full + s, 1);
-      mbar_init(v_empty + s, 1);
+    for (int s = 0; s < S::kQSlots; ++s) {
+      mbar_init(q_full + s, 1);
+      mbar_init(q_empty + s, 1);
+    }
+    for (int s = 0; s < S::kKvSlots; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 4);
@@ -154,82 +155,77 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // Q through a 2-slot ring (the next item's Q lands while this item
+    // runs), K_j and V_j in issue order through a 3-slot ring; a slot is
+    // reloaded once the MMA that read it has completed (its empty barrier).
     if (lane == 0) {
       bool ok = true;
-      int gk = 0, gv = 0, t = 0;  // K, V and Q loads issued
+      int t = 0, g = 0;  // Q loads and K/V loads issued
       for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
         const AttnItem it = attn_item(items, w / heads, qtiles);
         const int h = w % heads;
         const int L = __ldg(seq_len + it.b), q0 = it.qt * 128;
         if (q0 >= L) continue;
         const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
-        if (t > 0 && !mbar_wait(q_free, (t - 1) & 1, err)) {
-          ok = false;
-          break;
+        {
+          const int qs = t % S::kQSlots;
+          if (!mbar_wait(q_empty + qs, ((t / S::kQSlots) & 1) ^ 1u, err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(q_full + qs, S::kTile);
+          tma_load_2d(smem + S::kQ0 + qs * S::kTile, &tmQKV, q_full + qs, h * kAttnTcD, base + q0);
+          ++t;
         }
-        mbar_arrive_expect_tx(q_full, 16384);
-        tma_load_2d(smem + S::kQ, &tmQKV, q_full, h * kAttnTcD, base + q0);
-        ++t;
-        for (int j = 0; j < nk; ++j) {
-          const int s = gk & 1;
-          const uint32_t ph = ((gk >> 1) & 1) ^ 1u;
-          if (!mbar_wait(k_empty + s, ph, err)) {
-            ok = false;
-            break;
+        for (int j = 0; j < nk && ok; ++j) {
+          for (int kv = 0; kv < 2; ++kv, ++g) {  // K_j, then V_j
+            const int ss = g % S::kKvSlots;
+            if (!mbar_wait(kv_empty + ss, ((g / S::kKvSlots) & 1) ^ 1u, err)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(kv_full + ss, S::kTile);
+            tma_load_2d(smem + S::kKv0 + ss * S::kTile, &tmQKV, kv_full + ss,
+                        (1 + kv) * H + h * kAttnTcD, base + j * 128);
           }
-          mbar_arrive_expect_tx(k_full + s, 16384);
-          tma_load_2d(smem + S::kK0 + s * 16384, &tmQKV, k_full + s, H + h * kAttnTcD,
-                      base + j * 128);
-          ++gk;
-          if (!mbar_wait(v_empty + s, ph, err)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(v_full + s, 16384);
-          tma_load_2d(smem + S::kV0 + s * 16384, &tmQKV, v_full + s, 2 * H + h * kAttnTcD,
-                      base + j * 128);
-          ++gv;
         }
       }
       if (ok) {
         // every load issued has been consumed (so it landed) before exit
-        for (int k = 0; k < 2; ++k, ++gk) {
-          const uint32_t ph = ((gk >> 1) & 1) ^ 1u;
-          if (!mbar_wait(k_empty + (gk & 1), ph, err) || !mbar_wait(v_empty + (gk & 1), ph, err))
-            break;
-        }
-        if (t > 0) mbar_wait(q_free, (t - 1) & 1, err);
+        for (int k = 0; k < S::kKvSlots; ++k, ++g)
+          if (!mbar_wait(kv_empty + g % S::kKvSlots, ((g / S::kKvSlots) & 1) ^ 1u, err)) break;
+        for (int k = 0; k < S::kQSlots; ++k, ++t)
+          if (!mbar_wait(q_empty + t % S::kQSlots, ((t / S::kQSlots) & 1) ^ 1u, err)) break;
       } else {
         // wait (bounded) for the copies still in flight to land
-        for (int k = gk - 1; k >= 0 && k >= gk - 2; --k)
-          mbar_wait(k_full + (k & 1), (k >> 1) & 1, err);
-        for (int k = gv - 1; k >= 0 && k >= gv - 2; --k)
-          mbar_wait(v_full + (k & 1), (k >> 1) & 1, err);
-        if (t > 0) mbar_wait(q_full, (t - 1) & 1, err);
+        for (int k = g - 1; k >= 0 && k >= g - S::kKvSlots; --k)
+          mbar_wait(kv_full + k % S::kKvSlots, (k / S::kKvSlots) & 1, err);
+        for (int k = t - 1; k >= 0 && k >= t - S::kQSlots; --k)
+          mbar_wait(q_full + k % S::kQSlots, (k / S::kQSlots) & 1, err);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idO = idesc_bf16_f32(128, kAttnTcD) | (1u << 16);  // B (V) MN-major
-      const uint32_t qa = smem_u32(smem + S::kQ), pa = smem_u32(smem + S::kP);
+      const uint32_t pa = smem_u32(smem + S::kP);
       bool ok = true, issued = false;
-      int g = 0, t = 0;
-      int pend_g = -1, pend_cols = 0;  // the P V still to issue (block pend_g)
-      // O_pg = P_pg V_pg over the block's `cols` keys
-      auto issue_pv = [&](int pg, int cols) -> bool {
-        const int s = pg & 1;
-        if (!mbar_wait(v_full + s, (pg >> 1) & 1, err) || !mbar_wait(p_full, pg & 1, err) ||
-            (pg > 0 && !mbar_wait(o_free, (pg - 1) & 1, err)))
+      int gb = 0, t = 0, g = 0;  // key blocks, Q slots and K/V slots consumed
+      int pend_b = -1, pend_cols = 0, pend_v = 0;  // the P V still to issue
+      // O_b = P_b V_b over the block's `cols` keys, V in K/V sequence slot vq
+      auto issue_pv = [&](int b, int cols, int vq) -> bool {
+        const int vs = vq % S::kKvSlots;
+        if (!mbar_wait(kv_full + vs, (vq / S::kKvSlots) & 1, err) ||
+            !mbar_wait(p_full, b & 1, err) || (b > 0 && !mbar_wait(o_free, (b - 1) & 1, err)))
           return false;
         tc_fence_after();
-        const uint32_t va = smem_u32(smem + S::kV0 + s * 16384);
+        const uint32_t va = smem_u32(smem + S::kKv0 + vs * S::kTile);
 #pragma unroll 1
         for (int ks = 0; ks < cols / 16; ++ks)
           umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
                     sdesc_mnmajor_sw128(va + ks * 2048), idO, ks > 0 ? 1u : 0u);
         umma_commit(o_full);
-        umma_commit(v_empty + s);
+        umma_commit(kv_empty + vs);
         return true;
       };
       for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
@@ -237,36 +233,39 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         const int L = __ldg(seq_len + it.b);
         if (it.qt * 128 >= L) continue;
         const int nk = (L + 127) >> 7;
-        if (!mbar_wait(q_full, t & 1, err)) {
+        const int qs = t % S::kQSlots;
+        if (!mbar_wait(q_full + qs, (t / S::kQSlots) & 1, err)) {
           ok = false;
           break;
         }
         ++t;
-        for (int j = 0; j < nk; ++j, ++g) {
-          const int s = g & 1;
+        const uint32_t qa = smem_u32(smem + S::kQ0 + qs * S::kTile);
+        for (int j = 0; j < nk; ++j, ++gb, g += 2) {
+          const int ks = g % S::kKvSlots;  // K_j at sequence g, V_j at g + 1
           const int cols = attn_block_cols(L, j);
-          ok = mbar_wait(k_full + s, (g >> 1) & 1, err) &&
-               (g == 0 || mbar_wait(s_free, (g - 1) & 1, err));
+          ok = mbar_wait(kv_full + ks, (g / S::kKvSlots) & 1, err) &&
+               (gb == 0 || mbar_wait(s_free, (gb - 1) & 1, err));
           if (!ok) break;
           tc_fence_after();
-          const uint32_t ka = smem_u32(smem + S::kK0 + s * 16384);
+          const uint32_t ka = smem_u32(smem + S::kKv0 + ks * S::kTile);
           const uint32_t idS = idesc_bf16_f32(128, cols);
 #pragma unroll
           for (int k = 0; k < kAttnTcD / 16; ++k)
             umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS,
                       k > 0 ? 1u : 0u);
           umma_commit(s_full);
-          umma_commit(k_empty + s);
-          if (j == nk - 1) umma_commit(q_free);  // this item's Q is no longer read
+          umma_commit(kv_empty + ks);
+          if (j == nk - 1) umma_commit(q_empty + qs);  // this item's Q is no longer read
           issued = true;
-          if (pend_g >= 0 && !(ok = issue_pv(pend_g, pend_cols))) break;
-          pend_g = g;
+          if (pend_b >= 0 && !(ok = issue_pv(pend_b, pend_cols, pend_v))) break;
+          pend_b = gb;
           pend_cols = cols;
+          pend_v = g + 1;
         }
         // the item's last P V goes out now rather than behind the next
         // item's loads: the softmax warps wait for it to write ctx
-        if (ok && !(ok = issue_pv(pend_g, pend_cols))) break;
-        pend_g = -1;
+        if (ok && !(ok = issue_pv(pend_b, pend_cols, pend_v))) break;
+        pend_b = -1;
       }
       if (issued) {
         umma_commit(drain);
@@ -302,27 +301,35 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         }
         tc_fence_after();
         const int n = min(128, L - j * 128);  // valid keys of this block
-        const int nch = (n + 31) >> 5;        // 32-key chunks holding them
-        const int tail = n & 31;              // valid keys of a partial last chunk
         float m_new = m_prev;
         if (active) {
-          // pass 1: row max over the valid keys
-          float mx = -INFINITY;
-#pragma unroll 1
-          for (int c = 0; c < nch; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tS + lane_off + c * 32, v);
-            tmem_wait_ld_regs(v);
-            if (tail && c == nch - 1) {
+          // pass 1: row max over the valid keys.  16-key groups, the next
+          // group's TMEM load in flight while this one is reduced, eight
+          // independent running maxima (short dependency chains)
+          float m8[8];
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < tail) mx = fmaxf(mx, __uint_as_float(v[i]));
-            } else {
+          for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+          {
+            const int ng = (n + 15) >> 4;
+            uint32_t va[16], vb[16];
+            tmem_ld_32x32b_x16(tS + lane_off, va);
+            tmem_wait_ld_regs(va);
 #pragma unroll
-              for (int i = 0; i < 32; i += 2)
-                mx = fmaxf(mx, fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
+            for (int c = 0; c < 8; ++c) {
+              if (c < ng) {
+                uint32_t(&cur)[16] = (c & 1) ? vb : va;
+                uint32_t(&nxt)[16] = (c & 1) ? va : vb;
+                if (c + 1 < ng) tmem_ld_32x32b_x16(tS + lane_off + (c + 1) * 16, nxt);
+                const int vc = n - c * 16;  // valid keys from this group's first column
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  m8[i & 7] = fmaxf(m8[i & 7], i < vc ? __uint_as_float(cur[i]) : -INFINITY);
+                if (c + 1 < ng) tmem_wait_ld_regs(nxt);
+              }
             }
           }
+          const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
           m_new = fmaxf(m_prev, mx);
         }
         // fold in the previous block's P V (its products used m_prev)
@@ -352,34 +359,48 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           const float m2 = m_new * kLog2e;
           const uint64_t negm2 = pk2(-m2, -m2);
           l *= ex2_approx((m_prev - m_new) * kLog2e);
-          uint64_t acc = pk2(0.f, 0.f);
-          // 16 keys at a time: TMEM columns -> p -> two swizzled 16-byte P chunks
-#pragma unroll 1
-          for (int c = 0; c < (n + 15) >> 4; ++c) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(tS + lane_off + c * 16, v);
-            tmem_wait_ld_regs(v);
-            const int valid = n - c * 16;  // >= 16: the whole group
-            uint32_t pk[8];
+          // 16 keys at a time: TMEM columns -> p -> two swizzled 16-byte P
+          // chunks, the next group's TMEM load in flight meanwhile; four
+          // independent packed partial sums
+          uint64_t acc4[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float x0, x1;
-              unpk2(fma_x2(pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), log2e2,
-                           negm2),
-                    x0, x1);
-              float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-              p0 = 2 * i < valid ? p0 : 0.f;
-              p1 = 2 * i + 1 < valid ? p1 : 0.f;
-              acc = add_x2(acc, pk2(p0, p1));
-              pk[i] = pack_bf16x2(p0, p1);
+          for (int i = 0; i < 4; ++i) acc4[i] = pk2(0.f, 0.f);
+          {
+            const int ng = (n + 15) >> 4;
+            uint32_t va[16], vb[16];
+            tmem_ld_32x32b_x16(tS + lane_off, va);
+            tmem_wait_ld_regs(va);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              if (c < ng) {
+                uint32_t(&cur)[16] = (c & 1) ? vb : va;
+                uint32_t(&nxt)[16] = (c & 1) ? va : vb;
+                if (c + 1 < ng) tmem_ld_32x32b_x16(tS + lane_off + (c + 1) * 16, nxt);
+                const int valid = n - c * 16;  // >= 16: the whole group
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float x0, x1;
+                  unpk2(fma_x2(pk2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])),
+                               log2e2, negm2),
+                        x0, x1);
+                  float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+                  p0 = 2 * i < valid ? p0 : 0.f;
+                  p1 = 2 * i + 1 < valid ? p1 : 0.f;
+                  acc4[i & 3] = add_x2(acc4[i & 3], pk2(p0, p1));
+                  pk[i] = pack_bf16x2(p0, p1);
+                }
+                uint8_t *blk = prow + (c >> 2) * 16384;
+                const int q0c = (c & 3) * 2;
+                *reinterpret_cast<uint4 *>(blk + ((q0c ^ (r & 7)) << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4 *>(blk + (((q0c + 1) ^ (r & 7)) << 4)) =
+                    make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                if (c + 1 < ng) tmem_wait_ld_regs(nxt);
+              }
             }
-            uint8_t *blk = prow + (c >> 2) * 16384;
-            const int q0c = (c & 3) * 2;
-            *reinterpret_cast<uint4 *>(blk + ((q0c ^ (r & 7)) << 4)) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            *reinterpret_cast<uint4 *>(blk + (((q0c + 1) ^ (r & 7)) << 4)) =
-                make_uint4(pk[4], pk[5], pk[6], pk[7]);
           }
+          const uint64_t acc = add_x2(add_x2(acc4[0], acc4[1]), add_x2(acc4[2], acc4[3]));
           float a0, a1;
           unpk2(acc, a0, a1);
           l += a0 + a1;
