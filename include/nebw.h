@@ -186,9 +186,17 @@ typedef struct nebw_config {
 int nebw_model_create(nebw_dev *dev, const nebw_config *cfg, nebw_model **out);
 int nebw_model_set_tensor(nebw_model *m, const char *name, const void *host, int dtype,
                           int64_t rows, int64_t cols);
-/* Stage every tensor of a `.npue` container (gemm_layout "host": F32 [K,N]
- * operands) -- the reference's npue::File + set_model_shape + stage_all
- * (runtime/src/model.cpp:214-380). */
+/* A GEMM operand ("layer.{i}.{qkv,attn_out,ffn_up,ffn_down}") already in the
+ * device layout: bf16 bits, row-major [N, K] (K-major), as the packer's
+ * gemm_layout "tma_bf16" containers store it -- uploaded as is, no
+ * re-tiling.  Replaces the pre-tiled operand staging of Design::stage
+ * (runtime/src/design.cpp:394) for the array's block-panel layout. */
+int nebw_model_set_gemm_nk(nebw_model *m, const char *name, const uint16_t *host_bf16_nk,
+                           int64_t n_rows, int64_t k_cols);
+/* Stage every tensor of a `.npue` container -- the reference's npue::File +
+ * set_model_shape + stage_all (runtime/src/model.cpp:214-380).  gemm_layout
+ * "host" (F32 [K,N] operands, the reference packer's --dtype f32) or
+ * "tma_bf16" (bf16 [N,K] operands, nebw.pack). */
 int nebw_model_load_npue(nebw_dev *dev, const char *path, nebw_model **out);
 int nebw_model_destroy(nebw_model *m);
 int nebw_model_get_config(const nebw_model *m, nebw_config *cfg);

@@ -606,6 +606,39 @@ int stage_weight(nebw_dev *d, const void *host_kn, int dtype, int64_t K, int64_t
   return NEBW_OK;
 }
 
+// An operand already in the device layout (bf16 [N, K], K-major): one upload
+// and the tensor maps.
+int stage_weight_nk(nebw_dev *d, const uint16_t *host_nk, int64_t K, int64_t N, Weight *w) {
+  NEBW_REQUIRE(host_nk != nullptr, "null weight data");
+  NEBW_REQUIRE(K >= 64 && N >= 8 && K % 8 == 0 && N % 8 == 0 && K < (1 << 30) && N < (1 << 30),
+               "weight [N=%lld, K=%lld] refused: K >= 64, K %% 8 == 0, N %% 8 == 0",
+               static_cast<long long>(N), static_cast<long long>(K));
+  __nv_bfloat16 *dst = nullptr;
+  if (cudaMalloc(&dst, static_cast<size_t>(K) * N * 2) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(NEBW_ENOMEM, "cudaMalloc for a [%lld, %lld] weight failed",
+                     static_cast<long long>(N), static_cast<long long>(K));
+  }
+  cudaError_t e = cudaMemcpyAsync(dst, host_nk, static_cast<size_t>(K) * N * 2,
+                                  cudaMemcpyHostToDevice, d->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+  if (e != cudaSuccess) {
+    cudaFree(dst);
+    return set_error(NEBW_ECUDA, "weight upload failed: %s", cudaGetErrorString(e));
+  }
+  w->ptr = dst;
+  w->K = K;
+  w->N = N;
+  for (auto mp : {std::make_pair(&w->map64, 64), std::make_pair(&w->map128, 128),
+                  std::make_pair(&w->map256, 256)})
+    if (int rc = make_tmap_kmajor(mp.first, dst, N, K, mp.second)) {
+      cudaFree(dst);
+      w->ptr = nullptr;
+      return rc;
+    }
+  return NEBW_OK;
+}
+
 }  // namespace
 
 extern "C" int nebw_stage_weight(nebw_dev *d, const void *host_kn, int dtype, int64_t K, int64_t N,
@@ -1076,6 +1109,41 @@ extern "C" int nebw_model_set_tensor(nebw_model *m, const char *name, const void
   return rc;
 }
 
+extern "C" int nebw_model_set_gemm_nk(nebw_model *m, const char *name, const uint16_t *host,
+                                      int64_t n_rows, int64_t k_cols) {
+  NEBW_REQUIRE(m && name && host, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  const nebw_config &c = m->cfg;
+  const std::string n(name);
+  const int64_t H = c.hidden, F = c.intermediate;
+  NEBW_REQUIRE(n.rfind("layer.", 0) == 0, "'%s' is not a GEMM operand", name);
+  const size_t dot = n.find('.', 6);
+  NEBW_REQUIRE(dot != std::string::npos, "malformed tensor name '%s'", name);
+  const int L = std::atoi(n.substr(6, dot - 6).c_str());
+  NEBW_REQUIRE(L >= 0 && L < c.num_layers, "tensor '%s' names a layer outside [0, %d)", name,
+               c.num_layers);
+  const std::string leaf = n.substr(dot + 1);
+  LayerW &w = m->layers[L];
+  Weight *dst = nullptr;
+  int64_t K = 0, N = 0;
+  if (leaf == "qkv") dst = &w.qkv, K = H, N = 3 * H;
+  else if (leaf == "attn_out") dst = &w.ao, K = H, N = H;
+  else if (leaf == "ffn_up") dst = &w.up, K = H, N = F;
+  else if (leaf == "ffn_down") dst = &w.dn, K = F, N = H;
+  else return set_error(NEBW_EINVAL, "'%s' is not a GEMM operand", name);
+  if (n_rows != N || k_cols != K)
+    return set_error(NEBW_EINVAL, "GEMM operand '%s' is [%lld, %lld] (N, K), expected [%lld, %lld]",
+                     name, static_cast<long long>(n_rows), static_cast<long long>(k_cols),
+                     static_cast<long long>(N), static_cast<long long>(K));
+  if (dst->ptr) {
+    cudaFree(dst->ptr);
+    dst->ptr = nullptr;
+  }
+  if (int rc = stage_weight_nk(m->dev, host, K, N, dst)) return rc;
+  m->staged[n] = true;
+  return NEBW_OK;
+}
+
 extern "C" int nebw_model_destroy(nebw_model *m) {
   if (!m) return NEBW_OK;
   cudaSetDevice(m->dev->device);
@@ -1111,11 +1179,14 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
                        "bert_abs_gelu_postln is implemented", arch.c_str());
     std::string layout = "pretiled_bf16";
     if (f.has_config("gemm_layout")) layout = f.config_string("gemm_layout");
-    if (layout != "host")
+    if (layout != "host" && layout != "tma_bf16")
       return set_error(NEBW_EINVAL,
-                       "container gemm_layout '%s' refused: this library stages the plain "
-                       "row-major [K, N] operands of a gemm_layout \"host\" container and "
-                       "re-tiles them itself", layout.c_str());
+                       "container gemm_layout '%s' refused: this library reads the row-major "
+                       "[K, N] operands of a gemm_layout \"host\" container (re-tiling them "
+                       "itself) or the bf16 [N, K] operands of a \"tma_bf16\" container "
+                       "(nebw.pack); the array's block panels are not a B200 layout",
+                       layout.c_str());
+    const bool nk_layout = layout == "tma_bf16";
     nebw_config c{};
     c.num_layers = static_cast<int32_t>(f.config_int("num_layers"));
     c.hidden = static_cast<int32_t>(f.config_int("hidden"));
@@ -1145,7 +1216,18 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
       const int64_t r = t.shape.size() >= 1 ? t.shape[0] : 1;
       const int64_t cc = t.shape.size() >= 2 ? t.shape[1] : 1;
       const int dt = t.dtype == "F32" ? NEBW_F32 : NEBW_BF16;
-      int rc = nebw_model_set_tensor(m, n.c_str(), t.data, dt, r, cc);
+      const bool gemm_operand = t.shape.size() == 2 && n.rfind("layer.", 0) == 0;
+      int rc;
+      if (nk_layout && gemm_operand) {
+        if (t.dtype != "BF16") {
+          nebw_model_destroy(m);
+          return set_error(NEBW_EINVAL, "tma_bf16 container: GEMM operand '%s' is %s, BF16 "
+                           "expected", n.c_str(), t.dtype.c_str());
+        }
+        rc = nebw_model_set_gemm_nk(m, n.c_str(), reinterpret_cast<const uint16_t *>(t.data), r, cc);
+      } else {
+        rc = nebw_model_set_tensor(m, n.c_str(), t.data, dt, r, cc);
+      }
       if (rc) {
         const std::string msg = g_last_error;
         nebw_model_destroy(m);
