@@ -138,3 +138,19 @@ def test_deterministic_and_batch_independent(device, minilm):
     for r in (0, 5, 31):
         np.testing.assert_array_equal(full[r:r + 1], m.encode(ids[r:r + 1], lens[r:r + 1]))
     m.close()
+
+
+def test_encode_refusals(device):
+    """Shapes outside what the model was staged for fail by name."""
+    import nebw
+    from nebw import synth
+    w = synth.make_weights(synth.MINILM, seed=3, cls_pool=False, layers=1)
+    m = nebw.Model.from_weights(device, w, max_seq_len=64)
+    ids, _ = synth.make_tokens(2, 128, np.array([10, 20]), seed=4)
+    with pytest.raises(nebw.NebwError, match="seq"):
+        m.encode(ids, np.array([10, 20], np.int32))            # S = 128 > max_seq_len 64
+    with pytest.raises(nebw.NebwError, match="empty"):
+        m.encode(ids[:0, :64], np.zeros(0, np.int32))          # no rows
+    ok = m.encode(ids[:, :64], np.array([10, 20], np.int32))   # the same rows, S = 64
+    m.close()
+    assert np.isfinite(ok).all()
