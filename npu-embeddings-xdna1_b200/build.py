@@ -47,17 +47,19 @@ def build_lib(force: bool = False, verbose: bool = False) -> Path:
 
 
 def build_host_tool(verbose: bool = False) -> Path:
-    """host/nebw_embed: the C++ host side (GpuBertEncoder) as a file-in,
-    file-out tool, linked against libnebw.so with an rpath to this dir."""
+    """host/nebw_embed: the C++ host side (GpuBertEncoder, the WordPiece
+    tokenizer) as a file-in, file-out tool, linked against libnebw.so with an
+    rpath to this dir."""
     out = PKG / "host" / "nebw_embed"
     srcs = [PKG / "host" / "nebw_embed.cpp", PKG / "host" / "gpu_bert_encoder.hpp",
-            REPO / "include" / "nebw.h", PKG / "libnebw.so"]
+            PKG / "host" / "wordpiece.cpp", PKG / "host" / "wordpiece.hpp",
+            PKG / "host" / "bert_unicode.inc", REPO / "include" / "nebw.h", PKG / "libnebw.so"]
     if out.exists() and out.stat().st_mtime >= max(s.stat().st_mtime for s in srcs):
         return out
     cxx = shutil.which("g++") or "g++"
     cmd = [cxx, "-std=c++17", "-O2", "-Wall", "-I", str(REPO / "include"), "-o", str(out),
-           str(PKG / "host" / "nebw_embed.cpp"), "-L", str(PKG), "-lnebw",
-           "-Wl,-rpath,$ORIGIN/.."]
+           str(PKG / "host" / "nebw_embed.cpp"), str(PKG / "host" / "wordpiece.cpp"),
+           "-L", str(PKG), "-lnebw", "-Wl,-rpath,$ORIGIN/.."]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

@@ -1,21 +1,30 @@
-// nebw_embed -- file in, file out, through the C++ host side of the library.
+// nebw_embed -- the embedding CLI path of the reference (`npuembeddings embed`,
+// runtime/include/runtime/run_execute.hpp:150-258, embed_service.cpp:29-64)
+// with the encoder on a B200, through the C++ host side of the library.
 //
 //   nebw_embed <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [device]
+//       token ids and the 1/0 attention mask as raw little-endian int32
+//       [n, seq] (as a tokenizer emits them, padded to seq) -> raw fp32
+//       [n, hidden] pooled embeddings
+//   nebw_embed --text <model.npue> <texts.txt> <seq> <out.f32> [device] [--vocab v.txt]
+//       one text per line, WordPiece-tokenized on the host (wordpiece.hpp)
+//       with the vocabulary the container carries (tokenizer.vocab) or
+//       --vocab, then encoded on the GPU
+//   nebw_embed --tokenize <model.npue|vocab.txt> <texts.txt> <seq> <ids.i32> <mask.i32>
+//       the tokenizer alone (no GPU): the ids and mask files of the first form
 //
-// ids.i32 / mask.i32: raw little-endian int32 [n, seq] (token ids and the 1/0
-// attention mask as a tokenizer emits them, padded to seq); out.f32: raw
-// fp32 [n, hidden] pooled embeddings.  The batch path of the reference's
-// `npuembeddings embed` after tokenisation (runtime/include/runtime/
-// run_execute.hpp:150-258, embed_service.cpp:29-64), with the encoder on a
-// B200.  Exit status 0 on success, 1 with the cause on stderr otherwise.
+// Exit status 0 on success, 1 with the cause on stderr otherwise.
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <fstream>
 #include <stdexcept>
 #include <string>
 #include <vector>
 
+#include "../csrc/npue_file.h"
 #include "gpu_bert_encoder.hpp"
+#include "wordpiece.hpp"
 
 namespace {
 std::vector<int32_t> read_i32(const std::string &path) {
@@ -28,15 +37,96 @@ std::vector<int32_t> read_i32(const std::string &path) {
   f.read(reinterpret_cast<char *>(v.data()), n);
   return v;
 }
+
+template <typename T>
+void write_raw(const std::string &path, const std::vector<T> &v) {
+  std::ofstream o(path, std::ios::binary);
+  o.write(reinterpret_cast<const char *>(v.data()), static_cast<std::streamsize>(v.size() * sizeof(T)));
+  if (!o) throw std::runtime_error("cannot write " + path);
+}
+
+std::vector<std::string> read_lines(const std::string &path) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) throw std::runtime_error("cannot open " + path);
+  std::vector<std::string> out;
+  std::string line;
+  while (std::getline(f, line)) {
+    if (!line.empty() && line.back() == '\r') line.pop_back();
+    out.push_back(line);
+  }
+  return out;
+}
+
+bool ends_with(const std::string &s, const char *suffix) {
+  const size_t n = std::strlen(suffix);
+  return s.size() >= n && s.compare(s.size() - n, n, suffix) == 0;
+}
+
+// The vocabulary a container carries (the packer's tokenizer.vocab), or a
+// vocab.txt file.
+nebw::WordPiece load_vocab(const std::string &path) {
+  if (!ends_with(path, ".npue")) return nebw::WordPiece::from_vocab_file(path);
+  nebw::NpueFile f(path);
+  if (!f.has("tokenizer.vocab"))
+    throw std::runtime_error(path + " carries no tokenizer.vocab; pass --vocab vocab.txt");
+  const auto &t = f.tensor("tokenizer.vocab");
+  return nebw::WordPiece::from_vocab_bytes(reinterpret_cast<const char *>(t.data), t.nbytes);
+}
+
+void tokenize_all(const nebw::WordPiece &wp, const std::vector<std::string> &texts, int seq,
+                  std::vector<int32_t> &ids, std::vector<int32_t> &mask) {
+  ids.clear();
+  mask.clear();
+  for (const auto &t : texts) {
+    const nebw::Tokens e = wp.encode(t, seq);
+    ids.insert(ids.end(), e.ids.begin(), e.ids.end());
+    mask.insert(mask.end(), e.mask.begin(), e.mask.end());
+  }
+}
+
+int usage(const char *argv0) {
+  std::fprintf(stderr,
+               "usage: %s <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [device]\n"
+               "       %s --text <model.npue> <texts.txt> <seq> <out.f32> [device] [--vocab v.txt]\n"
+               "       %s --tokenize <model.npue|vocab.txt> <texts.txt> <seq> <ids.i32> <mask.i32>\n",
+               argv0, argv0, argv0);
+  return 2;
+}
 }  // namespace
 
 int main(int argc, char **argv) {
-  if (argc < 6) {
-    std::fprintf(stderr, "usage: %s <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [device]\n",
-                 argv[0]);
-    return 2;
-  }
   try {
+    if (argc >= 2 && std::strcmp(argv[1], "--tokenize") == 0) {
+      if (argc != 7) return usage(argv[0]);
+      const nebw::WordPiece wp = load_vocab(argv[2]);
+      std::vector<int32_t> ids, mask;
+      tokenize_all(wp, read_lines(argv[3]), std::atoi(argv[4]), ids, mask);
+      write_raw(argv[5], ids);
+      write_raw(argv[6], mask);
+      return 0;
+    }
+    if (argc >= 2 && std::strcmp(argv[1], "--text") == 0) {
+      if (argc < 6) return usage(argv[0]);
+      std::string vocab = argv[2];
+      int device = 0;
+      for (int i = 6; i < argc; ++i) {
+        if (std::strcmp(argv[i], "--vocab") == 0 && i + 1 < argc) vocab = argv[++i];
+        else device = std::atoi(argv[i]);
+      }
+      const int seq = std::atoi(argv[4]);
+      const nebw::WordPiece wp = load_vocab(vocab);
+      const std::vector<std::string> texts = read_lines(argv[3]);
+      std::vector<int32_t> ids, mask;
+      tokenize_all(wp, texts, seq, ids, mask);
+      nebw::GpuBertEncoder enc(argv[2], device);
+      const std::vector<float> out =
+          enc.encode(ids, mask, static_cast<int64_t>(texts.size()), seq);
+      write_raw(argv[5], out);
+      std::printf("%zu texts -> %zu embeddings of %lld dims -> %s\n", texts.size(), texts.size(),
+                  static_cast<long long>(enc.hidden()), argv[5]);
+      return 0;
+    }
+    if (argc < 6) return usage(argv[0]);
     const int64_t seq = std::atoll(argv[4]);
     const int device = argc > 6 ? std::atoi(argv[6]) : 0;
     const std::vector<int32_t> ids = read_i32(argv[2]), mask = read_i32(argv[3]);
@@ -45,10 +135,7 @@ int main(int argc, char **argv) {
     const int64_t n = static_cast<int64_t>(ids.size()) / seq;
     nebw::GpuBertEncoder enc(argv[1], device);
     const std::vector<float> out = enc.encode(ids, mask, n, seq);
-    std::ofstream o(argv[5], std::ios::binary);
-    o.write(reinterpret_cast<const char *>(out.data()),
-            static_cast<std::streamsize>(out.size() * sizeof(float)));
-    if (!o) throw std::runtime_error(std::string("cannot write ") + argv[5]);
+    write_raw(argv[5], out);
     std::printf("%lld embeddings of %lld dims -> %s\n", static_cast<long long>(n),
                 static_cast<long long>(enc.hidden()), argv[5]);
     return 0;

@@ -35,6 +35,7 @@
 #include "runtime/device.hpp"
 #include "runtime/model.hpp"
 #include "runtime/pool.hpp"
+#include "tokenizers/wordpiece.hpp"
 
 namespace {
 void set_err(char *err, int32_t errlen, const char *msg) {
@@ -220,6 +221,25 @@ int nebw_ref_pool_rows(const float *h, const float *am, int64_t take,
     return 0;
   } catch (const std::exception &e) {
     set_err(err, errlen, e.what());
+    return 1;
+  }
+}
+
+// The reference's WordPiece (runtime/src/tokenizers/wordpiece.cpp) on one
+// text: ids and the 1/0 mask padded to max_len, as EmbedService::chunk gets
+// them.  Returns 0, or 1 with `err` set.
+int nebw_ref_wordpiece(const char *vocab_path, const char *text, int32_t max_len, int32_t *ids,
+                       int32_t *mask, char *err, int32_t errlen) {
+  try {
+    const npue::WordPiece wp = npue::WordPiece::from_vocab_file(vocab_path);
+    const npue::Encoded e = wp.encode(text, max_len);
+    for (int32_t i = 0; i < max_len; ++i) {
+      ids[i] = e.input_ids[static_cast<size_t>(i)];
+      mask[i] = e.attention_mask[static_cast<size_t>(i)];
+    }
+    return 0;
+  } catch (const std::exception &ex) {
+    set_err(err, errlen, ex.what());
     return 1;
   }
 }
