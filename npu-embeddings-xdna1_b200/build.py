@@ -21,8 +21,9 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 REPO = PKG.parent
 SOURCES = ["csrc/nebw.cu", "csrc/npue_file.cpp"]
-DEPS = SOURCES + ["csrc/gemm_tc.cuh", "csrc/attention.cuh", "csrc/rowops.cuh", "csrc/ptx.cuh",
-                  "csrc/npue_file.h", "../include/nebw.h"]
+# every header the library includes: a change to any of them rebuilds it
+DEPS = SOURCES + sorted(str(p.relative_to(PKG)) for p in (PKG / "csrc").glob("*.cuh")) + [
+    "csrc/npue_file.h", "../include/nebw.h"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
               "-Xcompiler", "-fPIC", "-shared"]
 

@@ -15,16 +15,19 @@
 //               P is written):
 //                 S_j  = Q K_j^T  (M=128, N = the block's valid keys rounded
 //                                  up to 16, K=16 x 4)     -> TMEM [0, 128)
-//                 O_j-1 = P_j-1 V_j-1 (M=128, N=64, K = 16 x that block's
+//                 O += P_j-1 V_j-1 (M=128, N=64, K = 16 x that block's
 //                                  N/16; V read MN-major)  -> TMEM [128, 192)
 //   warps 2-5   one query row per thread (its TMEM lane); a warp whose 32
 //               rows all lie past the sequence only keeps the barrier
-//               protocol.  Row max over the valid keys of S_j, p =
-//               2^(s log2 e - m log2 e) on the SFU (packed fp32 FMAs for the
-//               argument and the running sum), P_j as bf16 into shared memory
-//               (swizzled K-major, the UMMA A layout); then O_acc = O_acc *
-//               2^(m_prev - m) + O_j in registers; at the end
-//               ctx = O_acc / sum as bf16
+//               protocol.  S_j is read from TMEM once, into registers; row
+//               max over its valid keys; p = 2^(s log2 e - m log2 e) on the
+//               SFU (packed fp32 FMAs for the argument and the running sum),
+//               P_j as bf16 into shared memory (swizzled K-major, the UMMA A
+//               layout).  O accumulates in TMEM; the max m that p is taken
+//               against is raised (and O and the sum rescaled in place) only
+//               when a row's max grows past it by more than a factor 2^8,
+//               so p <= 2^8 and O is rarely touched before the end, where
+//               ctx = O / sum as bf16
 //
 // Only the valid keys of a block are multiplied and exponentiated (in
 // 16-key groups), so short sequences -- most of an embedding batch -- cost
@@ -120,9 +123,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   uint64_t *kv_empty = bars + 7;  // [3]
   uint64_t *s_full = bars + 10, *s_free = bars + 11;
   uint64_t *p_full = bars + 12;
-  uint64_t *o_full = bars + 13, *o_free = bars + 14;
-  uint64_t *drain = bars + 15;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+  uint64_t *o_full = bars + 13;
+  uint64_t *drain = bars + 14;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 15);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -139,7 +142,6 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     mbar_init(s_free, 4);
     mbar_init(p_full, 4);
     mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -212,18 +214,20 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       bool ok = true, issued = false;
       int gb = 0, t = 0, g = 0;  // key blocks, Q slots and K/V slots consumed
       int pend_b = -1, pend_cols = 0, pend_v = 0;  // the P V still to issue
-      // O_b = P_b V_b over the block's `cols` keys, V in K/V sequence slot vq
-      auto issue_pv = [&](int b, int cols, int vq) -> bool {
+      bool pend_first = false;
+      // O (+)= P_b V_b over the block's `cols` keys, V in K/V sequence slot
+      // vq; an item's first block overwrites O.  The softmax warps' reads of
+      // O (rescale, the previous item's output) precede their p_full arrive.
+      auto issue_pv = [&](int b, int cols, int vq, bool first) -> bool {
         const int vs = vq % S::kKvSlots;
-        if (!mbar_wait(kv_full + vs, (vq / S::kKvSlots) & 1, err) ||
-            !mbar_wait(p_full, b & 1, err) || (b > 0 && !mbar_wait(o_free, (b - 1) & 1, err)))
+        if (!mbar_wait(kv_full + vs, (vq / S::kKvSlots) & 1, err) || !mbar_wait(p_full, b & 1, err))
           return false;
         tc_fence_after();
         const uint32_t va = smem_u32(smem + S::kKv0 + vs * S::kTile);
 #pragma unroll 1
         for (int ks = 0; ks < cols / 16; ++ks)
           umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
-                    sdesc_mnmajor_sw128(va + ks * 2048), idO, ks > 0 ? 1u : 0u);
+                    sdesc_mnmajor_sw128(va + ks * 2048), idO, (!first || ks > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(kv_empty + vs);
         return true;
@@ -257,14 +261,15 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           umma_commit(kv_empty + ks);
           if (j == nk - 1) umma_commit(q_empty + qs);  // this item's Q is no longer read
           issued = true;
-          if (pend_b >= 0 && !(ok = issue_pv(pend_b, pend_cols, pend_v))) break;
+          if (pend_b >= 0 && !(ok = issue_pv(pend_b, pend_cols, pend_v, pend_first))) break;
           pend_b = gb;
           pend_cols = cols;
           pend_v = g + 1;
+          pend_first = j == 0;
         }
         // the item's last P V goes out now rather than behind the next
         // item's loads: the softmax warps wait for it to write ctx
-        if (ok && !(ok = issue_pv(pend_b, pend_cols, pend_v))) break;
+        if (ok && !(ok = issue_pv(pend_b, pend_cols, pend_v, pend_first))) break;
         pend_b = -1;
       }
       if (issued) {
@@ -274,7 +279,14 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     }
   } else {
     // ---------------- softmax and output (warps 2..5) ----------------
+    // S_j is read from TMEM once, into registers (and S released at once, so
+    // QK^T of the next block runs during this block's exponentials).  The
+    // probabilities are taken against m_used, a running row max that is
+    // only raised when the block's max exceeds it by more than 2^8 (in
+    // base 2); then O in TMEM and the running sum are rescaled.  So
+    // p <= 2^8, and after the first block O is rarely touched until the end.
     constexpr float kLog2e = 1.4426950408889634f;
+    constexpr float kRescaleLog2 = 8.0f;
     const int w4 = warp & 3;
     const int r = w4 * 32 + lane;  // TMEM lane = query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(w4 * 32) << 16;
@@ -290,10 +302,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
       // warp-uniform: does any of this warp's 32 query rows belong to the sequence?
       const bool active = q0 + w4 * 32 < L;
-      float o[kAttnTcD];
-#pragma unroll
-      for (int i = 0; i < kAttnTcD; ++i) o[i] = 0.f;
-      float m_prev = -INFINITY, m_prev2 = -INFINITY, l = 0.f;
+      float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < nk; ++j, ++g) {
         if (!__all_sync(0xffffffffu, mbar_wait(s_full, g & 1, err))) {
           ok = false;
@@ -301,119 +310,106 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         }
         tc_fence_after();
         const int n = min(128, L - j * 128);  // valid keys of this block
-        float m_new = m_prev;
+        const int ng = (n + 15) >> 4;         // 16-key groups holding them
+        uint32_t s[8][16];
         if (active) {
-          // pass 1: row max over the valid keys.  16-key groups, the next
-          // group's TMEM load in flight while this one is reduced, eight
-          // independent running maxima (short dependency chains)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c < ng) tmem_ld_32x32b_x16(tS + lane_off + c * 16, s[c]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c < ng) pin_regs(s[c]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);  // S is in registers: the next QK^T may overwrite it
+        float m_new = m_used;
+        if (active) {
+          // row max over the valid keys, eight independent running maxima
           float m8[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-          {
-            const int ng = (n + 15) >> 4;
-            uint32_t va[16], vb[16];
-            tmem_ld_32x32b_x16(tS + lane_off, va);
-            tmem_wait_ld_regs(va);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              if (c < ng) {
-                uint32_t(&cur)[16] = (c & 1) ? vb : va;
-                uint32_t(&nxt)[16] = (c & 1) ? va : vb;
-                if (c + 1 < ng) tmem_ld_32x32b_x16(tS + lane_off + (c + 1) * 16, nxt);
-                const int vc = n - c * 16;  // valid keys from this group's first column
+          for (int c = 0; c < 8; ++c) {
+            if (c < ng) {
+              const int vc = n - c * 16;  // valid keys from this group's first column
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                  m8[i & 7] = fmaxf(m8[i & 7], i < vc ? __uint_as_float(cur[i]) : -INFINITY);
-                if (c + 1 < ng) tmem_wait_ld_regs(nxt);
-              }
+              for (int i = 0; i < 16; ++i)
+                m8[i & 7] = fmaxf(m8[i & 7], i < vc ? __uint_as_float(s[c][i]) : -INFINITY);
             }
           }
           const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                                  fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-          m_new = fmaxf(m_prev, mx);
+          m_new = fmaxf(m_used, mx);
         }
-        // fold in the previous block's P V (its products used m_prev)
+        const bool grow = __any_sync(0xffffffffu, active && (m_new - m_used) * kLog2e > kRescaleLog2);
         if (j > 0) {
+          // P_j-1 V_j-1 has completed: the P tile is free and O is current
           if (!__all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, err))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (active) {
-            const float sc = ex2_approx((m_prev2 - m_prev) * kLog2e);
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint32_t va[32];
-              tmem_ld_32x32b_x32(tO + lane_off + hh * 32, va);
+        }
+        if (grow) {  // warp-uniform; every lane of the warp moves to its own new max
+          const float sc = ex2_approx((m_used - m_new) * kLog2e);
+          if (j > 0) {
+            // 16 columns at a time: S_j is still held in 128 registers
+#pragma unroll 1
+            for (int q = 0; q < kAttnTcD / 16; ++q) {
+              uint32_t va[16];
+              tmem_ld_32x32b_x16(tO + lane_off + q * 16, va);
               tmem_wait_ld_regs(va);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) o[hh * 32 + i] = fmaf(o[hh * 32 + i], sc, __uint_as_float(va[i]));
+              for (int i = 0; i < 16; ++i) va[i] = __float_as_uint(__uint_as_float(va[i]) * sc);
+              tmem_st_32x32b_x16(tO + lane_off + q * 16, va);
             }
+            tmem_wait_st();
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(o_free);
+          l *= sc;
+          m_used = m_new;
         }
         if (active) {
-          // pass 2: p, running sum, P (bf16) into the shared A tile
-          const float m2 = m_new * kLog2e;
+          // p, running sum, P (bf16) into the shared A tile, 8 keys at a
+          // time as one swizzled 16-byte chunk; two packed partial sums
+          const float m2 = m_used * kLog2e;
           const uint64_t negm2 = pk2(-m2, -m2);
-          l *= ex2_approx((m_prev - m_new) * kLog2e);
-          // 16 keys at a time: TMEM columns -> p -> two swizzled 16-byte P
-          // chunks, the next group's TMEM load in flight meanwhile; four
-          // independent packed partial sums
-          uint64_t acc4[4];
+          uint64_t acc2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc4[i] = pk2(0.f, 0.f);
-          {
-            const int ng = (n + 15) >> 4;
-            uint32_t va[16], vb[16];
-            tmem_ld_32x32b_x16(tS + lane_off, va);
-            tmem_wait_ld_regs(va);
+          for (int c = 0; c < 8; ++c) {
+            if (c < ng) {
+              uint8_t *blk = prow + (c >> 2) * 16384;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              if (c < ng) {
-                uint32_t(&cur)[16] = (c & 1) ? vb : va;
-                uint32_t(&nxt)[16] = (c & 1) ? va : vb;
-                if (c + 1 < ng) tmem_ld_32x32b_x16(tS + lane_off + (c + 1) * 16, nxt);
-                const int valid = n - c * 16;  // >= 16: the whole group
-                uint32_t pk[8];
+              for (int hf = 0; hf < 2; ++hf) {
+                const int valid = n - c * 16 - hf * 8;  // valid keys from this chunk's first
+                uint32_t pk[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < 4; ++i) {
+                  const int k = hf * 8 + 2 * i;
                   float x0, x1;
-                  unpk2(fma_x2(pk2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])),
+                  unpk2(fma_x2(pk2(__uint_as_float(s[c][k]), __uint_as_float(s[c][k + 1])),
                                log2e2, negm2),
                         x0, x1);
                   float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
                   p0 = 2 * i < valid ? p0 : 0.f;
                   p1 = 2 * i + 1 < valid ? p1 : 0.f;
-                  acc4[i & 3] = add_x2(acc4[i & 3], pk2(p0, p1));
+                  acc2[i & 1] = add_x2(acc2[i & 1], pk2(p0, p1));
                   pk[i] = pack_bf16x2(p0, p1);
                 }
-                uint8_t *blk = prow + (c >> 2) * 16384;
-                const int q0c = (c & 3) * 2;
-                *reinterpret_cast<uint4 *>(blk + ((q0c ^ (r & 7)) << 4)) =
+                *reinterpret_cast<uint4 *>(blk + ((((c & 3) * 2 + hf) ^ (r & 7)) << 4)) =
                     make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                *reinterpret_cast<uint4 *>(blk + (((q0c + 1) ^ (r & 7)) << 4)) =
-                    make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                if (c + 1 < ng) tmem_wait_ld_regs(nxt);
               }
             }
           }
-          const uint64_t acc = add_x2(add_x2(acc4[0], acc4[1]), add_x2(acc4[2], acc4[3]));
           float a0, a1;
-          unpk2(acc, a0, a1);
+          unpk2(add_x2(acc2[0], acc2[1]), a0, a1);
           l += a0 + a1;
         }
         tc_fence_before();
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(s_free);  // S read: the next QK^T may overwrite it
-          mbar_arrive(p_full);  // P written: O_j = P_j V_j may start
-        }
-        m_prev2 = m_prev;
-        m_prev = m_new;
+        if (lane == 0) mbar_arrive(p_full);  // P written (and O rescaled): P_j V_j may start
       }
       if (!ok || !__all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, err))) {
         ok = false;
@@ -421,31 +417,30 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       }
       tc_fence_after();
       if (active) {
-        const float sc = ex2_approx((m_prev2 - m_prev) * kLog2e);
         const float inv = 1.0f / l;
+        uint4 *dst = reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + r) * H +
+                                               h * kAttnTcD);
+        const bool row = q0 + r < L;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t va[32];
           tmem_ld_32x32b_x32(tO + lane_off + hh * 32, va);
           tmem_wait_ld_regs(va);
+          float o[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            o[hh * 32 + i] = fmaf(o[hh * 32 + i], sc, __uint_as_float(va[i])) * inv;
+          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(va[i]) * inv;
+          if (row) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[hh * 4 + i] = make_uint4(pack_bf16x2(o[8 * i], o[8 * i + 1]),
+                                           pack_bf16x2(o[8 * i + 2], o[8 * i + 3]),
+                                           pack_bf16x2(o[8 * i + 4], o[8 * i + 5]),
+                                           pack_bf16x2(o[8 * i + 6], o[8 * i + 7]));
+          }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);  // the next item's first P V may overwrite O
-      if (active && q0 + r < L) {
-        uint4 *dst = reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + r) * H +
-                                               h * kAttnTcD);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_uint4(pack_bf16x2(o[8 * i], o[8 * i + 1]),
-                              pack_bf16x2(o[8 * i + 2], o[8 * i + 3]),
-                              pack_bf16x2(o[8 * i + 4], o[8 * i + 5]),
-                              pack_bf16x2(o[8 * i + 6], o[8 * i + 7]));
-      }
+      // O reads are complete before this warp's next p_full arrive (the
+      // fence there orders them before the next item's first P V)
     }
   }
 
