@@ -208,74 +208,88 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idO = idesc_bf16_f32(128, kAttnTcD) | (1u << 16);  // B (V) MN-major
-      const uint32_t pa = smem_u32(smem + S::kP);
-      bool ok = true, issued = false;
-      int gb = 0, t = 0, g = 0;  // key blocks, Q slots and K/V slots consumed
-      int pend_b = -1, pend_cols = 0, pend_v = 0;  // the P V still to issue
-      bool pend_first = false;
-      // O (+)= P_b V_b over the block's `cols` keys, V in K/V sequence slot
-      // vq; an item's first block overwrites O.  The softmax warps' reads of
-      // O (rescale, the previous item's output) precede their p_full arrive.
-      auto issue_pv = [&](int b, int cols, int vq, bool first) -> bool {
-        const int vs = vq % S::kKvSlots;
-        if (!mbar_wait(kv_full + vs, (vq / S::kKvSlots) & 1, err) || !mbar_wait(p_full, b & 1, err))
-          return false;
-        tc_fence_after();
-        const uint32_t va = smem_u32(smem + S::kKv0 + vs * S::kTile);
-#pragma unroll 1
-        for (int ks = 0; ks < cols / 16; ++ks)
-          umma_bf16(tO, sdesc_kmajor_sw128(pa + (ks >> 2) * 16384 + (ks & 3) * 32),
-                    sdesc_mnmajor_sw128(va + ks * 2048), idO, (!first || ks > 0) ? 1u : 0u);
+    // The whole warp walks the schedule and waits (so that the loop state
+    // and the descriptors are warp-uniform); one elected lane issues the
+    // tcgen05 instructions.
+    constexpr uint32_t idO = idesc_bf16_f32(128, kAttnTcD) | (1u << 16);  // B (V) MN-major
+    const uint32_t pa = smem_u32(smem + S::kP);
+    const bool leader = elect_one_sync();
+    auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
+    };
+    bool ok = true, issued = false;
+    int gb = 0, t = 0, g = 0;  // key blocks, Q slots and K/V slots consumed
+    int pend_b = -1, pend_cols = 0, pend_v = 0;  // the P V still to issue
+    bool pend_first = false;
+    // O (+)= P_b V_b over the block's `cols` keys, V in K/V sequence slot
+    // vq; an item's first block overwrites O.  The softmax warps' reads of
+    // O (rescale, the previous item's output) precede their p_full arrive.
+    auto issue_pv = [&](int b, int cols, int vq, bool first) -> bool {
+      const int vs = vq % S::kKvSlots;
+      if (!wait_all(kv_full + vs, (vq / S::kKvSlots) & 1) || !wait_all(p_full, b & 1)) return false;
+      tc_fence_after();
+      const uint64_t da = sdesc_kmajor_sw128(pa);
+      const uint64_t db = sdesc_mnmajor_sw128(smem_u32(smem + S::kKv0 + vs * S::kTile));
+      if (leader) {
+        // descriptor start addresses advance in 16-byte units: P by 32 B per
+        // 16 keys (1024 per 64-key half), V by 2048 B per 16 keys
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          if (ks < cols / 16)
+            umma_bf16(tO, da + (ks >> 2) * 1024 + (ks & 3) * 2, db + ks * 128, idO,
+                      (!first || ks > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(kv_empty + vs);
-        return true;
-      };
-      for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
-        const AttnItem it = attn_item(items, w / heads, qtiles);
-        const int L = __ldg(seq_len + it.b);
-        if (it.qt * 128 >= L) continue;
-        const int nk = (L + 127) >> 7;
-        const int qs = t % S::kQSlots;
-        if (!mbar_wait(q_full + qs, (t / S::kQSlots) & 1, err)) {
-          ok = false;
-          break;
-        }
-        ++t;
-        const uint32_t qa = smem_u32(smem + S::kQ0 + qs * S::kTile);
-        for (int j = 0; j < nk; ++j, ++gb, g += 2) {
-          const int ks = g % S::kKvSlots;  // K_j at sequence g, V_j at g + 1
-          const int cols = attn_block_cols(L, j);
-          ok = mbar_wait(kv_full + ks, (g / S::kKvSlots) & 1, err) &&
-               (gb == 0 || mbar_wait(s_free, (gb - 1) & 1, err));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t ka = smem_u32(smem + S::kKv0 + ks * S::kTile);
-          const uint32_t idS = idesc_bf16_f32(128, cols);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+      const AttnItem it = attn_item(items, w / heads, qtiles);
+      const int L = __ldg(seq_len + it.b);
+      if (it.qt * 128 >= L) continue;
+      const int nk = (L + 127) >> 7;
+      const int qs = t % S::kQSlots;
+      if (!wait_all(q_full + qs, (t / S::kQSlots) & 1)) {
+        ok = false;
+        break;
+      }
+      ++t;
+      const uint64_t dq = sdesc_kmajor_sw128(smem_u32(smem + S::kQ0 + qs * S::kTile));
+      for (int j = 0; j < nk; ++j, ++gb, g += 2) {
+        const int ks = g % S::kKvSlots;  // K_j at sequence g, V_j at g + 1
+        const int cols = attn_block_cols(L, j);
+        ok = wait_all(kv_full + ks, (g / S::kKvSlots) & 1) &&
+             (gb == 0 || wait_all(s_free, (gb - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t dk = sdesc_kmajor_sw128(smem_u32(smem + S::kKv0 + ks * S::kTile));
+        const uint32_t idS = idesc_bf16_f32(128, cols);
+        if (leader) {
 #pragma unroll
-          for (int k = 0; k < kAttnTcD / 16; ++k)
-            umma_bf16(tS, sdesc_kmajor_sw128(qa + k * 32), sdesc_kmajor_sw128(ka + k * 32), idS,
-                      k > 0 ? 1u : 0u);
+          for (int k = 0; k < kAttnTcD / 16; ++k)  // +32 B per 16 elements of K
+            umma_bf16(tS, dq + k * 2, dk + k * 2, idS, k > 0 ? 1u : 0u);
           umma_commit(s_full);
           umma_commit(kv_empty + ks);
           if (j == nk - 1) umma_commit(q_empty + qs);  // this item's Q is no longer read
-          issued = true;
-          if (pend_b >= 0 && !(ok = issue_pv(pend_b, pend_cols, pend_v, pend_first))) break;
-          pend_b = gb;
-          pend_cols = cols;
-          pend_v = g + 1;
-          pend_first = j == 0;
         }
-        // the item's last P V goes out now rather than behind the next
-        // item's loads: the softmax warps wait for it to write ctx
-        if (ok && !(ok = issue_pv(pend_b, pend_cols, pend_v, pend_first))) break;
-        pend_b = -1;
+        __syncwarp();
+        issued = true;
+        if (pend_b >= 0 && !(ok = issue_pv(pend_b, pend_cols, pend_v, pend_first))) break;
+        pend_b = gb;
+        pend_cols = cols;
+        pend_v = g + 1;
+        pend_first = j == 0;
       }
-      if (issued) {
-        umma_commit(drain);
-        mbar_wait(drain, 0, err);
-      }
+      // the item's last P V goes out now rather than behind the next
+      // item's loads: the softmax warps wait for it to write ctx
+      if (ok && !(ok = issue_pv(pend_b, pend_cols, pend_v, pend_first))) break;
+      pend_b = -1;
+    }
+    if (issued) {
+      if (leader) umma_commit(drain);
+      __syncwarp();
+      wait_all(drain, 0);
     }
   } else {
     // ---------------- softmax and output (warps 2..5) ----------------
@@ -310,38 +324,49 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         }
         tc_fence_after();
         const int n = min(128, L - j * 128);  // valid keys of this block
-        const int ng = (n + 15) >> 4;         // 16-key groups holding them
+        const int nf = n >> 4;                // whole 16-key groups
+        const int vl = n & 15;                // valid keys of a partial last group (0: none)
+        // s[c]: whole group c; a partial last group (then nf <= 7) in s[7]
         uint32_t s[8][16];
         if (active) {
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            if (c < ng) tmem_ld_32x32b_x16(tS + lane_off + c * 16, s[c]);
+            if (c < nf) tmem_ld_32x32b_x16(tS + lane_off + c * 16, s[c]);
+          if (vl) tmem_ld_32x32b_x16(tS + lane_off + nf * 16, s[7]);
           tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            if (c < ng) pin_regs(s[c]);
+            if (c < nf) pin_regs(s[c]);
+          if (vl) pin_regs(s[7]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free);  // S is in registers: the next QK^T may overwrite it
         float m_new = m_used;
         if (active) {
-          // row max over the valid keys, eight independent running maxima
-          float m8[8];
+          // keys of the partial group past the valid ones -> -inf, so that
+          // they neither raise the max nor (2^-inf = 0) add to P
+          if (vl) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            if (c < ng) {
-              const int vc = n - c * 16;  // valid keys from this group's first column
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                m8[i & 7] = fmaxf(m8[i & 7], i < vc ? __uint_as_float(s[c][i]) : -INFINITY);
-            }
+            for (int i = 0; i < 16; ++i) s[7][i] = i < vl ? s[7][i] : 0xff800000u;
           }
-          const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                 fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-          m_new = fmaxf(m_used, mx);
+          // row max, four independent chains of three-input maxima
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c < nf) {
+#pragma unroll
+              for (int i = 0; i < 16; i += 2)
+                m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], __uint_as_float(s[c][i]),
+                                         __uint_as_float(s[c][i + 1]));
+            }
+          if (vl) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 2)
+              m4[(i >> 1) & 3] =
+                  fmax3(m4[(i >> 1) & 3], __uint_as_float(s[7][i]), __uint_as_float(s[7][i + 1]));
+          }
+          m_new = fmax3(m_used, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         }
         const bool grow = __any_sync(0xffffffffu, active && (m_new - m_used) * kLog2e > kRescaleLog2);
         if (j > 0) {
@@ -376,32 +401,30 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           const float m2 = m_used * kLog2e;
           const uint64_t negm2 = pk2(-m2, -m2);
           uint64_t acc2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
+          // the 16 keys of group c
+          auto exp_group = [&](const uint32_t(&v)[16], int c) {
+            uint8_t *blk = prow + (c >> 2) * 16384;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            if (c < ng) {
-              uint8_t *blk = prow + (c >> 2) * 16384;
+            for (int hf = 0; hf < 2; ++hf) {
+              uint32_t pk[4];
 #pragma unroll
-              for (int hf = 0; hf < 2; ++hf) {
-                const int valid = n - c * 16 - hf * 8;  // valid keys from this chunk's first
-                uint32_t pk[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const int k = hf * 8 + 2 * i;
-                  float x0, x1;
-                  unpk2(fma_x2(pk2(__uint_as_float(s[c][k]), __uint_as_float(s[c][k + 1])),
-                               log2e2, negm2),
-                        x0, x1);
-                  float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-                  p0 = 2 * i < valid ? p0 : 0.f;
-                  p1 = 2 * i + 1 < valid ? p1 : 0.f;
-                  acc2[i & 1] = add_x2(acc2[i & 1], pk2(p0, p1));
-                  pk[i] = pack_bf16x2(p0, p1);
-                }
-                *reinterpret_cast<uint4 *>(blk + ((((c & 3) * 2 + hf) ^ (r & 7)) << 4)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              for (int i = 0; i < 4; ++i) {
+                const int k = hf * 8 + 2 * i;
+                float x0, x1;
+                unpk2(fma_x2(pk2(__uint_as_float(v[k]), __uint_as_float(v[k + 1])), log2e2, negm2),
+                      x0, x1);
+                const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);  // 0 past the valid keys
+                acc2[i & 1] = add_x2(acc2[i & 1], pk2(p0, p1));
+                pk[i] = pack_bf16x2(p0, p1);
               }
+              *reinterpret_cast<uint4 *>(blk + ((((c & 3) * 2 + hf) ^ (r & 7)) << 4)) =
+                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-          }
+          };
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c < nf) exp_group(s[c], c);
+          if (vl) exp_group(s[7], nf);
           float a0, a1;
           unpk2(add_x2(acc2[0], acc2[1]), a0, a1);
           l += a0 + a1;

@@ -39,6 +39,18 @@ __device__ __forceinline__ void record_err(int *err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// True in exactly one active lane of the warp (PTX elect.sync): the lane
+// that issues for a warp which walks a schedule together.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ---- mbarrier -------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
@@ -307,6 +319,13 @@ __device__ __forceinline__ uint64_t add_x2(uint64_t a, uint64_t b) {
 __device__ __forceinline__ uint64_t mul_x2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max.f32).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
 
