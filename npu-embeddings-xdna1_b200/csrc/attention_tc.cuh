@@ -27,7 +27,8 @@
 //               against is raised (and O and the sum rescaled in place) only
 //               when a row's max grows past it by more than a factor 2^8,
 //               so p <= 2^8 and O is rarely touched before the end, where
-//               ctx = O / sum as bf16
+//               ctx = O / sum as bf16, staged through shared memory into
+//               whole 128-byte row slices per store
 //
 // Only the valid keys of a block are multiplied and exponentiated (in
 // 16-key groups), so short sequences -- most of an embedding batch -- cost
@@ -440,27 +441,35 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       }
       tc_fence_after();
       if (active) {
+        // ctx rows = O / sum as bf16, staged through this warp's own 32
+        // rows of the first P block (free: the last P V has completed) so
+        // that each global store writes four whole 128-byte row slices
         const float inv = 1.0f / l;
-        uint4 *dst = reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + r) * H +
-                                               h * kAttnTcD);
-        const bool row = q0 + r < L;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t va[32];
-          tmem_ld_32x32b_x32(tO + lane_off + hh * 32, va);
+#pragma unroll 1
+        for (int q = 0; q < kAttnTcD / 16; ++q) {
+          uint32_t va[16];
+          tmem_ld_32x32b_x16(tO + lane_off + q * 16, va);
           tmem_wait_ld_regs(va);
-          float o[32];
+          uint32_t pk[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(va[i]) * inv;
-          if (row) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[hh * 4 + i] = make_uint4(pack_bf16x2(o[8 * i], o[8 * i + 1]),
-                                           pack_bf16x2(o[8 * i + 2], o[8 * i + 3]),
-                                           pack_bf16x2(o[8 * i + 4], o[8 * i + 5]),
-                                           pack_bf16x2(o[8 * i + 6], o[8 * i + 7]));
-          }
+          for (int i = 0; i < 8; ++i)
+            pk[i] = pack_bf16x2(__uint_as_float(va[2 * i]) * inv, __uint_as_float(va[2 * i + 1]) * inv);
+          *reinterpret_cast<uint4 *>(prow + (((2 * q) ^ (r & 7)) << 4)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4 *>(prow + (((2 * q + 1) ^ (r & 7)) << 4)) =
+              make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
+        __syncwarp();
+        const int ch = lane & 7;  // 16-byte chunk of a row slice
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = w4 * 32 + 4 * i + (lane >> 3);  // query row within the tile
+          if (q0 + rr < L)
+            *reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + rr) * H +
+                                       h * kAttnTcD + ch * 8) =
+                *reinterpret_cast<const uint4 *>(smem + S::kP + rr * 128 + ((ch ^ (rr & 7)) << 4));
+        }
+        __syncwarp();
       }
       // O reads are complete before this warp's next p_full arrive (the
       // fence there orders them before the next item's first P V)
