@@ -322,6 +322,13 @@ __device__ __forceinline__ uint64_t mul_x2(uint64_t a, uint64_t b) {
   return d;
 }
 
+// 1/x on the SFU (PTX rcp.approx.ftz.f32: about 1 ulp; 1/inf = 0).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // max(a, b, c) in one instruction (sm_100 three-input max.f32).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
