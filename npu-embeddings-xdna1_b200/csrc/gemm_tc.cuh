@@ -584,8 +584,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader only) ----------------
-    if (leader && lane == 0) {
+    // The whole warp walks the schedule and waits (so that the loop state
+    // and the descriptors are warp-uniform); one elected lane issues.
+    if (leader) {
       constexpr uint32_t idesc = idesc_bf16_f32(kPairM, BN);
+      const bool elect = elect_one_sync();
+      auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
+      };
       int stage = 0;
       uint32_t phase = 0;
       bool issued_any = false, ok = true;
@@ -593,34 +599,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        if (!wait_all(&tempty[acc], acc_phase ^ 1u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.err)) {
+          if (!wait_all(&full[stage], phase)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
-          const uint32_t w0 = smem_u32(sW + stage * S::kBBytes);
+          const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + stage * S::kABytes));
+          const uint64_t dw = sdesc_kmajor_sw128(smem_u32(sW + stage * S::kBBytes));
+          if (elect) {
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(a0 + k * 32),
-                           sdesc_kmajor_sw128(w0 + k * 32), idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < kGemmBK / 16; ++k)  // +32 B per 16 elements of K
+              umma_bf16_pair(d_tmem, da + k * 2, dw + k * 2, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_commit_pair(&empty[stage], 0x3);
           }
+          __syncwarp();
           issued_any = true;
-          umma_commit_pair(&empty[stage], 0x3);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) umma_commit_pair(&tfull[acc], 0x3);
+        if (ok && elect) umma_commit_pair(&tfull[acc], 0x3);
+        __syncwarp();
       }
       if (issued_any) {
-        umma_commit_pair(drain, 0x1);
-        mbar_wait(drain, 0, p.err);
+        if (elect) umma_commit_pair(drain, 0x1);
+        __syncwarp();
+        wait_all(drain, 0);
       }
     }
   } else {
