@@ -305,8 +305,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp walks the schedule and waits (so that the loop state
+    // and the descriptors are warp-uniform); one elected lane issues.
+    {
       constexpr uint32_t idesc = idesc_bf16_f32(kGemmBM, BN);
+      const bool elect = elect_one_sync();
+      auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
+      };
       int stage = 0;
       uint32_t phase = 0;
       bool issued_any = false, ok = true;
@@ -314,35 +320,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        if (!wait_all(&tempty[acc], acc_phase ^ 1u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.err)) {
+          if (!wait_all(&full[stage], phase)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
-          const uint32_t w0 = smem_u32(sW + stage * S::kBBytes);
+          const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + stage * S::kABytes));
+          const uint64_t dw = sdesc_kmajor_sw128(smem_u32(sW + stage * S::kBBytes));
+          if (elect) {
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_bf16(d_tmem, sdesc_kmajor_sw128(a0 + k * 32), sdesc_kmajor_sw128(w0 + k * 32),
-                      idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < kGemmBK / 16; ++k)  // +32 B per 16 elements of K
+              umma_bf16(d_tmem, da + k * 2, dw + k * 2, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_commit(&empty[stage]);  // stage reusable once these MMAs retire
           }
+          __syncwarp();
           issued_any = true;
-          umma_commit(&empty[stage]);  // stage reusable once these MMAs retire
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok && elect) umma_commit(&tfull[acc]);
+        __syncwarp();
       }
-      // Drain: all MMAs this thread issued have retired before TMEM is freed.
+      // Drain: all MMAs this warp issued have retired before TMEM is freed.
       if (issued_any) {
-        umma_commit(drain);
-        mbar_wait(drain, 0, p.err);
+        if (elect) umma_commit(drain);
+        __syncwarp();
+        wait_all(drain, 0);
       }
     }
   } else {

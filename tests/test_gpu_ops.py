@@ -279,3 +279,75 @@ def test_embed_refuses_bad_token(device):
                     z(S, H), z(2, H), dev_tensor(np.ones(H, np.float32)), z(H), H, x)
     with pytest.raises(nebw.NebwError, match="token id"):
         device.sync()
+
+
+_SINGLE_CTA_CHILD = r"""
+import sys
+import numpy as np
+import torch
+import nebw
+
+inp = np.load(sys.argv[1])
+dev = nebw.Device(0, torch_stream=True)
+res = {}
+for key in sorted({k.rsplit('_', 1)[0] for k in inp.files}):
+    A, W, b = inp[key + '_A'], inp[key + '_W'], inp[key + '_b']
+    M, K = A.shape
+    N = W.shape[1]
+    h = dev.stage_weight(W)
+    a = torch.from_numpy(A.view(np.int16).copy()).cuda().view(torch.bfloat16)
+    bd = torch.from_numpy(b).cuda()
+    for act, cd in ((0, 0), (0, 1), (1, 1), (2, 1)):
+        c = torch.empty((M, N), dtype=torch.float32 if cd == 0 else torch.bfloat16, device='cuda')
+        dev.gemm(h, a, M, K, N, c, bias=bd, act=act, c_dtype=cd)
+        dev.sync()
+        res[f'{key}_{act}_{cd}'] = c.float().cpu().numpy()
+    dev.release_weight(h)
+dev.close()
+np.savez(sys.argv[2], **res)
+"""
+
+
+def test_gemm_single_cta_kernel_matches_pairs(device, tmp_path):
+    """The single-CTA GEMM (128-row tiles; the path for GPUs that cannot
+    place CTA pairs, forced here with NEBW_GEMM_CTAS=1 in a child process)
+    against the CTA-pair path of this process, every epilogue: fp32 outputs
+    within fp32 accumulation-order noise, bf16 outputs within one bf16 ulp."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    rng = np.random.default_rng(23)
+    shapes = [(37, 200, 24), (300, 384, 1152), (513, 1024, 4096)]
+    inputs = {}
+    for M, K, N in shapes:
+        key = f"{M}x{K}x{N}"
+        inputs[key + "_A"] = bf16_bits(rng.standard_normal((M, K), np.float32))
+        inputs[key + "_W"] = rng.standard_normal((K, N), np.float32) * 0.05
+        inputs[key + "_b"] = rng.standard_normal(N).astype(np.float32)
+    np.savez(tmp_path / "in.npz", **inputs)
+    repo = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, NEBW_GEMM_CTAS="1",
+               PYTHONPATH=os.pathsep.join([str(repo / "npu-embeddings-xdna1_b200"), str(repo)]))
+    subprocess.run([sys.executable, "-c", _SINGLE_CTA_CHILD, str(tmp_path / "in.npz"),
+                    str(tmp_path / "out.npz")], env=env, check=True, timeout=300)
+    single = np.load(tmp_path / "out.npz")
+    for M, K, N in shapes:
+        key = f"{M}x{K}x{N}"
+        h = device.stage_weight(inputs[key + "_W"])
+        a = dev_tensor(inputs[key + "_A"])
+        bd = dev_tensor(inputs[key + "_b"])
+        for act, cd in ((0, 0), (0, 1), (1, 1), (2, 1)):
+            c = torch.empty((M, N), dtype=torch.float32 if cd == 0 else torch.bfloat16,
+                            device="cuda")
+            device.gemm(h, a, M, K, N, c, bias=bd, act=act, c_dtype=cd)
+            device.sync()
+            got = c.float().cpu().numpy().astype(np.float64)
+            ref = single[f"{key}_{act}_{cd}"].astype(np.float64)
+            assert np.isfinite(ref).all()
+            if cd == 0:
+                assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max() + 1e-6, (key, act)
+            else:
+                assert np.all(np.abs(got - ref) <= np.abs(ref) * 2.0 ** -7 + 1e-6), (key, act)
+        device.release_weight(h)
