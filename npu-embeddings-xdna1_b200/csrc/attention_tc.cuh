@@ -1,22 +1,24 @@
 // Fused masked attention on the 5th-generation tensor cores (head_dim 64).
 //
 // Persistent CTAs over (sequence, 128-query tile, head) work items,
-// flash-style over key blocks of up to 128 with an online softmax,
+// flash-style over key blocks of up to 64 with an online softmax,
 // warp-specialised so that loads, tensor-core products and the softmax of
 // different key blocks (and of consecutive items) overlap:
 //
 //   warp 0      TMA: the Q tile once per item through a 2-slot ring (the
 //               next item's Q lands while this one runs), then K_j and V_j
-//               of the packed Q|K|V rows (128-byte swizzled) in issue order
-//               through a 3-slot ring
-//   warp 1      tcgen05.mma from one thread, software-pipelined inside an
+//               (64-key tiles) of the packed Q|K|V rows (128-byte swizzled)
+//               in issue order through a 3-slot ring
+//   warp 1      tcgen05.mma from one elected lane (the whole warp walks the
+//               schedule, so loop state and descriptors stay warp-uniform),
+//               software-pipelined inside an
 //               item so that the softmax of key block j can start before
 //               P_j-1 V_j-1 runs (an item's last P V is issued as soon as its
 //               P is written):
 //                 S_j  = Q K_j^T  (M=128, N = the block's valid keys rounded
-//                                  up to 16, K=16 x 4)     -> TMEM [0, 128)
+//                                  up to 16, K=16 x 4)     -> TMEM [0, 64)
 //                 O += P_j-1 V_j-1 (M=128, N=64, K = 16 x that block's
-//                                  N/16; V read MN-major)  -> TMEM [128, 192)
+//                                  N/16; V read MN-major)  -> TMEM [64, 128)
 //   warps 2-5   one query row per thread (its TMEM lane); a warp whose 32
 //               rows all lie past the sequence only keeps the barrier
 //               protocol.  S_j is read from TMEM once, into registers; row
@@ -34,8 +36,10 @@
 // 16-key groups), so short sequences -- most of an embedding batch -- cost
 // what their length needs rather than a full 128 x 128 tile.
 //
-// 112 KB of shared memory and 256 TMEM columns per CTA, so two CTAs share
-// an SM and one's softmax overlaps the other's loads and products.  Q is
+// 72 KB of shared memory, 128 TMEM columns and at most 112 registers per
+// thread per CTA, so three CTAs share an SM (three softmax warps per SM
+// sub-partition) and one's softmax overlaps the others' waits on loads and
+// products; the 64-key block is what makes the third CTA fit.  Q is
 // pre-scaled by 1/sqrt(64) (the packer's fold, tools/pack/pack_npue.py:
 // 2742-2750); no scale is applied here.
 //
@@ -60,16 +64,18 @@ namespace nebw {
 
 constexpr int kAttnTcThreads = 192;  // TMA warp, MMA warp, 4 softmax warps
 constexpr int kAttnTcD = 64;
-constexpr int kAttnTcTmemCols = 256;  // S [0,128), O [128,192)
+constexpr int kAttnTcKeys = 64;       // keys per block
+constexpr int kAttnTcTmemCols = 128;  // S [0,64), O [64,128)
 
 struct AttnTcShape {
-  static constexpr int kTile = 16384;               // one 128 x 64 bf16 tile
+  static constexpr int kTile = 16384;               // one 128 x 64 bf16 Q tile
+  static constexpr int kKvTile = 8192;              // one 64 x 64 bf16 K or V tile
   static constexpr int kQSlots = 2, kKvSlots = 3;
   static constexpr int kQ0 = 0;                     // Q ring: 2 slots
   static constexpr int kKv0 = kQSlots * kTile;      // K/V ring: 3 slots, K_j V_j K_j+1 ...
-  static constexpr int kP = kKv0 + kKvSlots * kTile;  // P, 32 KB (2 K-blocks of 64 keys)
-  static constexpr int kBars = kP + 32768;          // barriers
-  static constexpr int kSmemBytes = kBars + 256;    // 114,944 B: two CTAs per SM
+  static constexpr int kP = kKv0 + kKvSlots * kKvTile;  // P, 16 KB (128 rows x 64 keys)
+  static constexpr int kBars = kP + 16384;          // barriers
+  static constexpr int kSmemBytes = kBars + 256;    // 73,984 B: three CTAs per SM
 };
 
 template <typename T>
@@ -94,7 +100,7 @@ __device__ __forceinline__ AttnItem attn_item(const int *items, int item, int qt
 // Valid keys of key block j of a sequence of length L, rounded up to 16 (the
 // UMMA N granularity at M = 128 and the K step of P V).
 __device__ __forceinline__ int attn_block_cols(int L, int j) {
-  return (min(128, L - j * 128) + 15) & ~15;
+  return (min(kAttnTcKeys, L - j * kAttnTcKeys) + 15) & ~15;
 }
 
 // Persistent: each CTA walks work indices w = blockIdx.x, +gridDim.x, ...
@@ -102,8 +108,9 @@ __device__ __forceinline__ int attn_block_cols(int L, int j) {
 // load / product / softmax pipeline running across items.  With `items`
 // null, the items are every (b, qt < qtiles) and tiles past a sequence's
 // length are skipped.
-__global__ void __launch_bounds__(kAttnTcThreads, 2)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const int *__restrict__ seq_off,
+__global__ void __launch_bounds__(kAttnTcThreads, 3)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV,
+                        const __grid_constant__ CUtensorMap tmKV, const int *__restrict__ seq_off,
                         const int *__restrict__ seq_len, const int *__restrict__ items,
                         const int *__restrict__ items_count, int n_items_host, int qtiles,
                         int heads, __nv_bfloat16 *__restrict__ ctx, int *err) {
@@ -131,6 +138,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQKV);
+    tma_prefetch_desc(&tmKV);
     for (int s = 0; s < S::kQSlots; ++s) {
       mbar_init(q_full + s, 1);
       mbar_init(q_empty + s, 1);
@@ -154,7 +162,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tS = tmem, tO = tmem + kAttnTcKeys;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -169,7 +177,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
         const int h = w % heads;
         const int L = __ldg(seq_len + it.b), q0 = it.qt * 128;
         if (q0 >= L) continue;
-        const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
+        const int base = __ldg(seq_off + it.b), nk = (L + kAttnTcKeys - 1) / kAttnTcKeys;
         {
           const int qs = t % S::kQSlots;
           if (!mbar_wait(q_empty + qs, ((t / S::kQSlots) & 1) ^ 1u, err)) {
@@ -187,9 +195,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(kv_full + ss, S::kTile);
-            tma_load_2d(smem + S::kKv0 + ss * S::kTile, &tmQKV, kv_full + ss,
-                        (1 + kv) * H + h * kAttnTcD, base + j * 128);
+            mbar_arrive_expect_tx(kv_full + ss, S::kKvTile);
+            tma_load_2d(smem + S::kKv0 + ss * S::kKvTile, &tmKV, kv_full + ss,
+                        (1 + kv) * H + h * kAttnTcD, base + j * kAttnTcKeys);
           }
         }
       }
@@ -230,15 +238,14 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       if (!wait_all(kv_full + vs, (vq / S::kKvSlots) & 1) || !wait_all(p_full, b & 1)) return false;
       tc_fence_after();
       const uint64_t da = sdesc_kmajor_sw128(pa);
-      const uint64_t db = sdesc_mnmajor_sw128(smem_u32(smem + S::kKv0 + vs * S::kTile));
+      const uint64_t db = sdesc_mnmajor_sw128(smem_u32(smem + S::kKv0 + vs * S::kKvTile));
       if (leader) {
         // descriptor start addresses advance in 16-byte units: P by 32 B per
-        // 16 keys (1024 per 64-key half), V by 2048 B per 16 keys
+        // 16 keys, V by 2048 B per 16 keys
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
+        for (int ks = 0; ks < kAttnTcKeys / 16; ++ks)
           if (ks < cols / 16)
-            umma_bf16(tO, da + (ks >> 2) * 1024 + (ks & 3) * 2, db + ks * 128, idO,
-                      (!first || ks > 0) ? 1u : 0u);
+            umma_bf16(tO, da + ks * 2, db + ks * 128, idO, (!first || ks > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(kv_empty + vs);
       }
@@ -249,7 +256,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       const AttnItem it = attn_item(items, w / heads, qtiles);
       const int L = __ldg(seq_len + it.b);
       if (it.qt * 128 >= L) continue;
-      const int nk = (L + 127) >> 7;
+      const int nk = (L + kAttnTcKeys - 1) / kAttnTcKeys;
       const int qs = t % S::kQSlots;
       if (!wait_all(q_full + qs, (t / S::kQSlots) & 1)) {
         ok = false;
@@ -264,7 +271,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
              (gb == 0 || wait_all(s_free, (gb - 1) & 1));
         if (!ok) break;
         tc_fence_after();
-        const uint64_t dk = sdesc_kmajor_sw128(smem_u32(smem + S::kKv0 + ks * S::kTile));
+        const uint64_t dk = sdesc_kmajor_sw128(smem_u32(smem + S::kKv0 + ks * S::kKvTile));
         const uint32_t idS = idesc_bf16_f32(128, cols);
         if (leader) {
 #pragma unroll
@@ -314,7 +321,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
       const int h = w % heads;
       const int L = __ldg(seq_len + it.b), q0 = it.qt * 128;
       if (q0 >= L) continue;
-      const int base = __ldg(seq_off + it.b), nk = (L + 127) >> 7;
+      const int base = __ldg(seq_off + it.b), nk = (L + kAttnTcKeys - 1) / kAttnTcKeys;
       // warp-uniform: does any of this warp's 32 query rows belong to the sequence?
       const bool active = q0 + w4 * 32 < L;
       float m_used = -INFINITY, l = 0.f;
@@ -324,21 +331,22 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           break;
         }
         tc_fence_after();
-        const int n = min(128, L - j * 128);  // valid keys of this block
+        const int n = min(kAttnTcKeys, L - j * kAttnTcKeys);  // valid keys of this block
         const int nf = n >> 4;                // whole 16-key groups
         const int vl = n & 15;                // valid keys of a partial last group (0: none)
-        // s[c]: whole group c; a partial last group (then nf <= 7) in s[7]
-        uint32_t s[8][16];
+        constexpr int kG = kAttnTcKeys / 16;  // groups per block
+        // s[c]: whole group c; a partial last group (then nf <= kG - 1) in s[kG - 1]
+        uint32_t s[kG][16];
         if (active) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
+          for (int c = 0; c < kG; ++c)
             if (c < nf) tmem_ld_32x32b_x16(tS + lane_off + c * 16, s[c]);
-          if (vl) tmem_ld_32x32b_x16(tS + lane_off + nf * 16, s[7]);
+          if (vl) tmem_ld_32x32b_x16(tS + lane_off + nf * 16, s[kG - 1]);
           tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
+          for (int c = 0; c < kG; ++c)
             if (c < nf) pin_regs(s[c]);
-          if (vl) pin_regs(s[7]);
+          if (vl) pin_regs(s[kG - 1]);
         }
         tc_fence_before();
         __syncwarp();
@@ -349,12 +357,12 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           // they neither raise the max nor (2^-inf = 0) add to P
           if (vl) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) s[7][i] = i < vl ? s[7][i] : 0xff800000u;
+            for (int i = 0; i < 16; ++i) s[kG - 1][i] = i < vl ? s[kG - 1][i] : 0xff800000u;
           }
           // row max, four independent chains of three-input maxima
           float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
+          for (int c = 0; c < kG; ++c)
             if (c < nf) {
 #pragma unroll
               for (int i = 0; i < 16; i += 2)
@@ -364,8 +372,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           if (vl) {
 #pragma unroll
             for (int i = 0; i < 16; i += 2)
-              m4[(i >> 1) & 3] =
-                  fmax3(m4[(i >> 1) & 3], __uint_as_float(s[7][i]), __uint_as_float(s[7][i + 1]));
+              m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], __uint_as_float(s[kG - 1][i]),
+                                       __uint_as_float(s[kG - 1][i + 1]));
           }
           m_new = fmax3(m_used, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         }
@@ -404,7 +412,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
           uint64_t acc2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
           // the 16 keys of group c
           auto exp_group = [&](const uint32_t(&v)[16], int c) {
-            uint8_t *blk = prow + (c >> 2) * 16384;
+            uint8_t *blk = prow;
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               uint32_t pk[4];
@@ -423,9 +431,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, 2)
             }
           };
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
+          for (int c = 0; c < kG; ++c)
             if (c < nf) exp_group(s[c], c);
-          if (vl) exp_group(s[7], nf);
+          if (vl) exp_group(s[kG - 1], nf);
           float a0, a1;
           unpk2(add_x2(acc2[0], acc2[1]), a0, a1);
           l += a0 + a1;

@@ -402,11 +402,12 @@ int launch_attention(const __nv_bfloat16 *qkv, const int *off, const int *len, i
   return NEBW_OK;
 }
 
-// tcgen05 attention for head_dim 64: a persistent launch (two CTAs per SM)
+// tcgen05 attention for head_dim 64: a persistent launch (three CTAs per SM)
 // over the work items -- the device-built, longest-first list `items` with
 // its count `items_count`, or, when `items` is null, every (sequence,
 // 128-query tile < max_len) pair.
-int launch_attention_tc(nebw_dev *d, const CUtensorMap &map, const int *off, const int *len,
+int launch_attention_tc(nebw_dev *d, const CUtensorMap &map, const CUtensorMap &map_kv,
+                        const int *off, const int *len,
                         const int *items, const int *items_count, int B, int max_len, int heads,
                         __nv_bfloat16 *ctx, cudaStream_t st) {
   NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0 &&
@@ -415,9 +416,9 @@ int launch_attention_tc(nebw_dev *d, const CUtensorMap &map, const int *off, con
   const int qtiles = (max_len + 127) / 128;
   const int64_t n_items = static_cast<int64_t>(B) * qtiles;
   NEBW_REQUIRE(n_items * heads < (1ll << 31), "attention work too large");
-  const dim3 grid(2 * d->sm_count);
+  const dim3 grid(3 * d->sm_count);
   nebw::attention_tc_kernel<<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape::kSmemBytes, st>>>(
-      map, off, len, items, items_count, static_cast<int>(n_items), qtiles, heads, ctx, d->d_err);
+      map, map_kv, off, len, items, items_count, static_cast<int>(n_items), qtiles, heads, ctx, d->d_err);
   NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }
@@ -478,6 +479,8 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   if (int rc = set_all_gemm_attrs()) return rc;
   NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  nebw::AttnTcShape::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared));
   if (int rc = query_gemm_pairs(&d->gemm_pairs)) return rc;
   if (int rc = load_tensor_map_encoder()) return rc;
   *out = d.release();
@@ -725,10 +728,12 @@ extern "C" int nebw_attention(nebw_dev *d, const void *qkv, int64_t rows, const 
   NEBW_REQUIRE(qkv && off && len && ctx, "null attention operand");
   NEBW_REQUIRE(rows > 0 && rows < (1ll << 31), "rows %lld refused", static_cast<long long>(rows));
   if (d->attn_kind == NEBW_ATTN_TCGEN05 && hd == nebw::kAttnTcD) {
-    CUtensorMap map;
+    CUtensorMap map, map_kv;
     if (int rc = make_tmap_kmajor(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 128))
       return rc;
-    return launch_attention_tc(d, map, off, len, nullptr, nullptr, B, max_len, heads,
+    if (int rc = make_tmap_kmajor(&map_kv, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 64))
+      return rc;
+    return launch_attention_tc(d, map, map_kv, off, len, nullptr, nullptr, B, max_len, heads,
                                static_cast<__nv_bfloat16 *>(ctx), pick_stream(d, stream));
   }
   return launch_attention(static_cast<const __nv_bfloat16 *>(qkv), off, len, B, max_len, heads, hd,
@@ -799,7 +804,7 @@ struct nebw_model {
   __nv_bfloat16 *a = nullptr, *qkv = nullptr, *ctx = nullptr, *h = nullptr;
   int *ids = nullptr, *len_in = nullptr, *len = nullptr, *off = nullptr;
   int *att_items = nullptr;  // attention work list (longest first) [B * S/128 + 1]
-  CUtensorMap map_qkv_att;  // Q|K|V rows as 64 x 128 TMA tiles for attention
+  CUtensorMap map_qkv_att, map_kv_att;  // Q|K|V rows as 64 x 128 / 64 x 64 TMA tiles
   float *out = nullptr;
   CUtensorMap map_a, map_ctx, map_h;          // GEMM A operands (TMA loads)
   CUtensorMap out_qkv, out_y, out_h;          // GEMM outputs (TMA stores)
@@ -876,6 +881,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   if ((rc = make_tmap_out(&m->out_y, m->y, R, H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
+  if ((rc = make_tmap_kmajor(&m->map_kv_att, m->qkv, R, 3 * H, 64))) return rc;
   return NEBW_OK;
 }
 
@@ -964,7 +970,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     // attention
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if (tc_attention)
-      rc = launch_attention_tc(d, m->map_qkv_att, m->off, m->len, m->att_items + 1, m->att_items, B, S,
+      rc = launch_attention_tc(d, m->map_qkv_att, m->map_kv_att, m->off, m->len, m->att_items + 1, m->att_items, B, S,
                                c.num_heads, m->ctx, st);
     else
       rc = launch_attention(m->qkv, m->off, m->len, B, S, c.num_heads, c.head_dim, m->ctx, st);
@@ -1419,6 +1425,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   if ((rc = make_tmap_out(&v.out_y, v.y, rows, H, true))) return rc;
   if ((rc = make_tmap_out(&v.out_h, v.h, rows, F, true))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_qkv_att, v.qkv, rows, 3 * H, 128))) return rc;
+  if ((rc = make_tmap_kmajor(&v.map_kv_att, v.qkv, rows, 3 * H, 64))) return rc;
   return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));
 }
 

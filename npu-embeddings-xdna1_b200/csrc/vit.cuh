@@ -53,7 +53,7 @@ struct nebw_vit {
   // qkv buffer and the patch GEMM's fp32 output in the h buffer, both dead
   // at that point of the pass
   CUtensorMap map_a, map_ctx, map_h, map_patches;
-  CUtensorMap out_qkv, out_h, out_y, out_pe, map_qkv_att;
+  CUtensorMap out_qkv, out_h, out_y, out_pe, map_qkv_att, map_kv_att;
   bool prof = false;
   std::vector<std::pair<cudaEvent_t, int>> marks;
   std::vector<cudaEvent_t> ev_pool;
@@ -118,6 +118,7 @@ int vit_ensure_workspace(nebw_vit *m, int64_t n) {
   if ((rc = make_tmap_out(&m->out_y, m->y, R, H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_pe, m->h, NP, H, false))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
+  if ((rc = make_tmap_kmajor(&m->map_kv_att, m->qkv, R, 3 * H, 64))) return rc;
   return NEBW_OK;
 }
 
@@ -257,7 +258,7 @@ int vit_encode_device(nebw_vit *m, const float *images, int n, float *out, cudaS
     if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv, nebw::kEpiBf16, a, st))) return rc;
     if ((rc = vit_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if (tc)
-      rc = launch_attention_tc(d, m->map_qkv_att, m->off, m->len, m->att_items + 1, m->att_items,
+      rc = launch_attention_tc(d, m->map_qkv_att, m->map_kv_att, m->off, m->len, m->att_items + 1, m->att_items,
                                n, m->n_pos, c.num_heads, m->ctx, st);
     else
       rc = launch_attention(m->qkv, m->off, m->len, n, m->n_pos, c.num_heads, c.head_dim, m->ctx,
