@@ -450,8 +450,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
       tc_fence_after();
       if (active) {
         // ctx rows = O / sum as bf16, staged through this warp's own 32
-        // rows of the first P block (free: the last P V has completed) so
-        // that each global store writes four whole 128-byte row slices
+        // rows of the P tile (free: the last P V has completed) so that
+        // each global store writes four whole 128-byte row slices
         const float inv = 1.0f / l;
 #pragma unroll 1
         for (int q = 0; q < kAttnTcD / 16; ++q) {

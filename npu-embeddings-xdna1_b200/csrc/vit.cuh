@@ -54,6 +54,10 @@ struct nebw_vit {
   // at that point of the pass
   CUtensorMap map_a, map_ctx, map_h, map_patches;
   CUtensorMap out_qkv, out_h, out_y, out_pe, map_qkv_att, map_kv_att;
+  // nebw_vit_encode: the stream its host->device chunk copies run on, and
+  // one "chunk landed" event per chunk
+  cudaStream_t copy_st = nullptr;
+  std::vector<cudaEvent_t> chunk_ev;
   bool prof = false;
   std::vector<std::pair<cudaEvent_t, int>> marks;
   std::vector<cudaEvent_t> ev_pool;
@@ -408,6 +412,8 @@ extern "C" int nebw_vit_destroy(nebw_vit *m) {
   cudaStreamSynchronize(m->dev->stream);
   vit_free_workspace(m);
   for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
+  for (cudaEvent_t e : m->chunk_ev) cudaEventDestroy(e);
+  if (m->copy_st) cudaStreamDestroy(m->copy_st);
   cudaFree(m->patch.ptr);
   for (float *p : {m->patch_b, m->cls, m->pos, m->lnf_g, m->lnf_b}) cudaFree(p);
   for (auto &w : m->layers) {
@@ -495,6 +501,15 @@ extern "C" int nebw_vit_encode_device(nebw_vit *m, const float *images, int32_t 
   return vit_encode_device(m, images, n, out, pick_stream(m->dev, stream));
 }
 
+// Host buffers: the batch is split into up to kVitChunks chunks whose
+// host->device copies run on a second stream, so that chunk i + 1 crosses
+// PCIe while the encoder runs on chunk i (only the first chunk's copy is
+// exposed); the pass over each chunk is the device pass above.  With
+// pageable host memory the copies are synchronous and nothing overlaps,
+// with the same results.
+constexpr int kVitChunks = 8;
+constexpr int kVitMinChunk = 256;  // images; smaller batches go in one piece
+
 extern "C" int nebw_vit_encode(nebw_vit *m, const float *images, int32_t n, float *out) {
   NEBW_REQUIRE(m && images && out, "null argument");
   if (int rc = use_dev(m->dev)) return rc;
@@ -503,10 +518,34 @@ extern "C" int nebw_vit_encode(nebw_vit *m, const float *images, int32_t n, floa
   if (int rc = vit_ensure_workspace(m, n)) return rc;
   const nebw_vit_config &c = m->cfg;
   cudaStream_t st = m->dev->stream;
-  const size_t img_bytes =
-      static_cast<size_t>(n) * c.num_channels * c.image_size * c.image_size * 4;
-  NEBW_CUDA(cudaMemcpyAsync(m->images, images, img_bytes, cudaMemcpyHostToDevice, st));
-  if (int rc = vit_encode_device(m, m->images, n, m->out, st)) return rc;
+  if (!m->copy_st) NEBW_CUDA(cudaStreamCreateWithFlags(&m->copy_st, cudaStreamNonBlocking));
+  while (static_cast<int>(m->chunk_ev.size()) < kVitChunks) {
+    cudaEvent_t e;
+    NEBW_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    m->chunk_ev.push_back(e);
+  }
+  const size_t per_img = static_cast<size_t>(c.num_channels) * c.image_size * c.image_size;
+  const int chunk = n < 2 * kVitMinChunk
+                        ? n
+                        : std::max(kVitMinChunk, (n + kVitChunks - 1) / kVitChunks);
+  const int nchunks = (n + chunk - 1) / chunk;
+  // the copies may start once the previous call's work on the stream is done
+  NEBW_CUDA(cudaEventRecord(m->chunk_ev[0], st));
+  NEBW_CUDA(cudaStreamWaitEvent(m->copy_st, m->chunk_ev[0], 0));
+  for (int i = 0; i < nchunks; ++i) {
+    const int i0 = i * chunk, cnt = std::min(chunk, n - i0);
+    NEBW_CUDA(cudaMemcpyAsync(m->images + i0 * per_img, images + i0 * per_img,
+                              static_cast<size_t>(cnt) * per_img * 4, cudaMemcpyHostToDevice,
+                              m->copy_st));
+    NEBW_CUDA(cudaEventRecord(m->chunk_ev[i], m->copy_st));
+  }
+  for (int i = 0; i < nchunks; ++i) {
+    const int i0 = i * chunk, cnt = std::min(chunk, n - i0);
+    NEBW_CUDA(cudaStreamWaitEvent(st, m->chunk_ev[i], 0));
+    if (int rc = vit_encode_device(m, m->images + i0 * per_img, cnt,
+                                   m->out + static_cast<size_t>(i0) * c.hidden, st))
+      return rc;
+  }
   NEBW_CUDA(cudaMemcpyAsync(out, m->out, static_cast<size_t>(n) * c.hidden * 4,
                             cudaMemcpyDeviceToHost, st));
   return nebw_sync(m->dev);

@@ -88,6 +88,30 @@ def test_vit_rows_independent_and_deterministic(device, small_vit):
     np.testing.assert_array_equal(full, again)
 
 
+def test_vit_host_path_chunks_match_device_path(device, small_vit):
+    """nebw_vit_encode splits a batch of >= 512 images into chunks whose
+    host->device copies overlap the pass over the previous chunk: the CLS
+    rows are the same bits as one device pass over the whole batch (600
+    images -> chunks of 256, 256, 88)."""
+    import torch
+    import nebw
+    from nebw import synth
+    arch, w = small_vit
+    imgs = synth.make_images(600, arch, 33)
+    m = nebw.VitModel.from_weights(device, w)
+    host = m.encode(imgs)
+    d_img = torch.from_numpy(imgs).cuda()
+    d_out = torch.empty((600, m.hidden), dtype=torch.float32, device="cuda")
+    m.encode_into(d_img, d_out, 600)
+    device.sync()
+    dev_rows = d_out.cpu().numpy()
+    again = m.encode(imgs)
+    m.close()
+    assert np.isfinite(host).all()
+    np.testing.assert_array_equal(host, dev_rows)
+    np.testing.assert_array_equal(host, again)
+
+
 def test_vit_npue_roundtrip(device, small_vit, tmp_path):
     """A host-layout ViT container loads into the same model as its weights."""
     import nebw
