@@ -676,6 +676,18 @@ def vit_arm(args, cfg):
         kernels["layernorm"]["frac_of_peak"] = kernels["layernorm"]["gbs"] / peaks["hbm_gbs"]
         up_ms = pms["gemm_up"] / (L * steps)
         up_flops = 2.0 * R * Hf * F
+        up_traffic = None
+        if PROFILE_TRAFFIC.exists():
+            tr = json.loads(PROFILE_TRAFFIC.read_text()).get("vit_gemm_up")
+            if tr:  # one ncu capture at M = m rows, scaled to M = R as for bge-large
+                sc = R / tr["m"]
+                up_traffic = (tr["weight_bytes"] + (tr["dram_read"] - tr["weight_bytes"]) * sc
+                              + tr["dram_write"] * sc)
+        # the profiler's kinds under their ViT names: im2col is timed as the
+        # packing step, the patch GEMM + [cls; pe] + pos + LN1 of layer 0 as
+        # the embedding step
+        kernels["im2col"] = kernels.pop("pack")
+        kernels["patch_embed_ln"] = kernels.pop("embed_ln")
         gemm_ms = sum(pms[k] for k in gemm_fl) / steps
         per_img = vit_flops_per_image(arch)
         line = {
@@ -702,7 +714,8 @@ def vit_arm(args, cfg):
                          "peak": peak_t, "unit": "TFLOP/s",
                          "frac": up_flops / (up_ms / 1e3) / 1e12 / peak_t,
                          "peak_source": f"{peak_src} bf16 dense, sustained",
-                         "traffic": None, "flops_per_launch": up_flops, "ms_per_launch": up_ms},
+                         "traffic": up_traffic, "algorithmic_bytes": R * Hf * 2 + Hf * F * 2 + R * F * 2,
+                         "flops_per_launch": up_flops, "ms_per_launch": up_ms},
             "roofline_gemm_family": {"achieved": sum(gemm_fl.values()) / (gemm_ms / 1e3) / 1e12,
                                      "peak": peak_t, "unit": "TFLOP/s",
                                      "frac": sum(gemm_fl.values()) / (gemm_ms / 1e3) / 1e12 / peak_t},
