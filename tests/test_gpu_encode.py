@@ -88,11 +88,13 @@ def test_bge_base_geometry_vs_oracle(device, port_oracle):
 @pytest.mark.parametrize("kind", [0, 1])
 def test_attention_kind_encoder_vs_oracle(device, port_oracle, kind):
     """The whole pass with each attention kernel (0 mma.sync, 1 tcgen05, the
-    default) over 128-key block boundaries (<=128, <=256, <=512 all present)."""
+    default) across key-block and query-tile boundaries: lengths on, just
+    under and just over multiples of 64 (the tcgen05 kernel's key block) and
+    128 (its query tile), partial 16-key groups, 1 and 512."""
     import nebw
     from nebw import synth
     w = synth.make_weights(synth.BGE_BASE, seed=19, cls_pool=True, layers=2)
-    lens = np.array([512, 300, 8, 129, 128, 1, 256, 257], np.int32)
+    lens = np.array([512, 300, 8, 129, 128, 1, 256, 257, 63, 64, 65, 200, 17], np.int32)
     ids, mask = synth.make_tokens(len(lens), 512, lens, seed=20)
     device.set_attention_kernel(kind)
     try:
