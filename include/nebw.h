@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NEBW_ABI_VERSION 2
+#define NEBW_ABI_VERSION 3
 
 typedef enum nebw_status {
   NEBW_OK = 0,
@@ -47,6 +47,10 @@ typedef enum nebw_status {
 
 enum { NEBW_F32 = 0, NEBW_BF16 = 1 };
 enum { NEBW_ACT_NONE = 0, NEBW_ACT_GELU8 = 1, NEBW_ACT_GELU_ERF = 2 };
+/* The activation of a gated FFN's gate half (GatedAct, app_state.hpp:109):
+ * SiLU ("silu", nomic_bert_rope_swiglu) or exact-erf GELU ("gelu",
+ * gte_new_rope_geglu). */
+enum { NEBW_GATE_SILU = 0, NEBW_GATE_GELU_ERF = 1 };
 enum { NEBW_POOL_MEAN = 0, NEBW_POOL_CLS = 1 };
 
 typedef struct nebw_dev nebw_dev;
@@ -177,6 +181,20 @@ typedef struct nebw_config {
   int32_t activation;      /* NEBW_ACT_GELU8 (the reference BERT host
                               path) or NEBW_ACT_GELU_ERF                 */
   float layer_norm_eps;    /* the reference BERT host path uses 1e-12    */
+  /* The gated / rotary families (set_model_shape, app_state.hpp:440-560):
+   * arch nomic_bert_rope_swiglu and gte_new_rope_geglu.  Zero for BERT. */
+  int32_t gated_ffn;       /* 1: ffn_up is [hidden, 2*intermediate] = [up | gate]
+                              along N and the FFN is up * act(gate)
+                              (swiglu_cpu, bert_encoder.cpp:582-627)      */
+  int32_t gated_act;       /* NEBW_GATE_SILU / NEBW_GATE_GELU_ERF         */
+  int32_t rope;            /* 1: rotary positions on Q and K (rotate-half,
+                              position 0 at each sequence's first token;
+                              apply_rope_qkv, bert_encoder.cpp:926-993); a
+                              position table, if set, is added as the
+                              reference adds its zero placeholder         */
+  int32_t reserved0;
+  double rope_theta;       /* inv_freq_j = theta^(-2j / head_dim) unless
+                              nebw_model_set_rope_freq gives the set      */
 } nebw_config;
 
 /* Model = npue::BertEncoder's staged state (stage_all,
@@ -193,10 +211,17 @@ int nebw_model_set_tensor(nebw_model *m, const char *name, const void *host, int
  * (runtime/src/design.cpp:394) for the array's block-panel layout. */
 int nebw_model_set_gemm_nk(nebw_model *m, const char *name, const uint16_t *host_bf16_nk,
                            int64_t n_rows, int64_t k_cols);
+/* The rotary frequency set as data (gte_new_rope_geglu's rope_inv_freq):
+ * n = head_dim / 2 values, angle(s, j) = s * inv_freq[j] in double, as
+ * apply_rope_qkv builds its tables (bert_encoder.cpp:929-945). */
+int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, int32_t n);
 /* Stage every tensor of a `.npue` container -- the reference's npue::File +
  * set_model_shape + stage_all (runtime/src/model.cpp:214-380).  gemm_layout
  * "host" (F32 [K,N] operands, the reference packer's --dtype f32) or
- * "tma_bf16" (bf16 [N,K] operands, nebw.pack). */
+ * "tma_bf16" (bf16 [N,K] operands, nebw.pack).  Architectures
+ * bert_abs_gelu_postln, nomic_bert_rope_swiglu and gte_new_rope_geglu, with
+ * set_model_shape's refusals for the latter two (position encoding, gating,
+ * the order of the fused FFN-up halves, the gate's activation). */
 int nebw_model_load_npue(nebw_dev *dev, const char *path, nebw_model **out);
 int nebw_model_destroy(nebw_model *m);
 int nebw_model_get_config(const nebw_model *m, nebw_config *cfg);

@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
@@ -42,6 +43,7 @@
 #include "../../include/nebw.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "gated.cuh"
 #include "gemm_tc.cuh"
 #include "npue_file.h"
 #include "ptx.cuh"
@@ -109,12 +111,14 @@ int load_tensor_map_encoder() {
 
 // A 2-D bf16 K-major tensor map [rows, K] with a {64, box_rows} box and
 // 128-byte swizzle (the GEMM's A and W operand tiles).
-int make_tmap_kmajor(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int box_rows) {
+// `stride` is the row pitch in elements (0: K).
+int make_tmap_kmajor(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int box_rows,
+                     int64_t stride = 0) {
   if (int rc = load_tensor_map_encoder()) return rc;
   if (reinterpret_cast<uintptr_t>(ptr) % 16)
     return set_error(NEBW_EINVAL, "GEMM operand address is not 16-byte aligned");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride ? stride : K) * 2};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(nebw::kGemmBK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr),
@@ -795,6 +799,10 @@ struct nebw_model {
   nebw_dev *dev = nullptr;
   nebw_config cfg{};
   float *word = nullptr, *pos = nullptr, *typ = nullptr, *emb_g = nullptr, *emb_b = nullptr;
+  // rotary tables [max_seq_len, head_dim] fp32 (cfg.rope), built on first use
+  // from rope_freq (nebw_model_set_rope_freq) or cfg.rope_theta
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  std::vector<double> rope_freq;
   std::vector<LayerW> layers;
   std::map<std::string, bool> staged;  // container name -> set
   // workspace (capacity rows_cap = B * S of the largest call so far)
@@ -846,6 +854,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   NEBW_CUDA(cudaStreamSynchronize(m->dev->stream));
   free_workspace(m);
   const int64_t H = m->cfg.hidden, F = m->cfg.intermediate;
+  const int64_t FW = m->cfg.gated_ffn ? 2 * F : F;  // FFN-up output width
   const int64_t R = std::max(rows, m->rows_cap), Bc = std::max(B, m->batch_cap);
   auto alloc = [&](void **p, size_t bytes) -> int {
     if (cudaMalloc(p, bytes) != cudaSuccess) {
@@ -860,7 +869,7 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->a), R * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->qkv), R * 3 * H * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ctx), R * H * 2);
-  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->h), R * F * 2);
+  rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->h), R * FW * 2);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ids), R * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len_in), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len), Bc * 4);
@@ -876,10 +885,11 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   m->ids_cap = R;
   if ((rc = make_tmap_kmajor(&m->map_a, m->a, R, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_ctx, m->ctx, R, H, nebw::kGemmBM))) return rc;
-  if ((rc = make_tmap_kmajor(&m->map_h, m->h, R, F, nebw::kGemmBM))) return rc;
+  // FFN-down reads the first F columns of each FW-wide row of h
+  if ((rc = make_tmap_kmajor(&m->map_h, m->h, R, F, nebw::kGemmBM, FW))) return rc;
   if ((rc = make_tmap_out(&m->out_qkv, m->qkv, R, 3 * H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_y, m->y, R, H, true))) return rc;
-  if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
+  if ((rc = make_tmap_out(&m->out_h, m->h, R, FW, true))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
   if ((rc = make_tmap_kmajor(&m->map_kv_att, m->qkv, R, 3 * H, 64))) return rc;
   return NEBW_OK;
@@ -894,8 +904,9 @@ int upload_f32(nebw_dev *d, float **dst, const void *src, int dtype, int64_t n) 
 }
 
 std::vector<std::string> required_names(const nebw_config &c) {
-  std::vector<std::string> v = {"embeddings.word", "embeddings.position", "embeddings.token_type",
+  std::vector<std::string> v = {"embeddings.word", "embeddings.token_type",
                                 "embeddings.ln.weight", "embeddings.ln.bias"};
+  if (!c.rope) v.push_back("embeddings.position");  // rotary models need no table
   for (int L = 0; L < c.num_layers; ++L) {
     const std::string p = "layer." + std::to_string(L) + ".";
     for (const char *s : {"qkv", "qkv.bias", "attn_out", "attn_out.bias", "ln1.weight", "ln1.bias",
@@ -910,6 +921,74 @@ int model_ready(const nebw_model *m) {
   for (const auto &n : required_names(m->cfg))
     if (!m->staged.count(n))
       return set_error(NEBW_ESTATE, "model tensor '%s' has not been staged", n.c_str());
+  return NEBW_OK;
+}
+
+// Rotary models: the cos / sin tables [max_seq_len, head_dim] as
+// apply_rope_qkv builds them (bert_encoder.cpp:929-952): angle = s *
+// inv_freq[j] in double, cos and sin rounded to fp32, the same value in
+// columns j and j + head_dim/2; inv_freq from the container's data or
+// theta^(-2j / head_dim) (gemma_rope_tables, gemma_kernels.cpp:114-136).
+// A rotary model without a position table gets a zero one (the reference's
+// containers carry a zero placeholder that its embedding adds).
+int prepare_rope(nebw_model *m) {
+  const nebw_config &c = m->cfg;
+  if (!c.rope) return NEBW_OK;
+  const int64_t H = c.hidden, S = c.max_seq_len, hd = c.head_dim, half = hd / 2;
+  if (!m->pos) {
+    NEBW_CUDA(cudaMalloc(&m->pos, S * H * 4));
+    NEBW_CUDA(cudaMemset(m->pos, 0, S * H * 4));
+  }
+  if (m->rope_cos) return NEBW_OK;
+  std::vector<double> inv(static_cast<size_t>(half));
+  if (!m->rope_freq.empty()) {
+    inv = m->rope_freq;
+  } else {
+    NEBW_REQUIRE(c.rope_theta > 0.0, "rotary model without rope_theta or a frequency set");
+    for (int64_t j = 0; j < half; ++j)
+      inv[static_cast<size_t>(j)] =
+          1.0 / std::pow(c.rope_theta, 2.0 * static_cast<double>(j) / static_cast<double>(hd));
+  }
+  std::vector<float> cs(static_cast<size_t>(S * hd)), sn(static_cast<size_t>(S * hd));
+  for (int64_t s = 0; s < S; ++s)
+    for (int64_t j = 0; j < half; ++j) {
+      const double ang = static_cast<double>(s) * inv[static_cast<size_t>(j)];
+      const float cv = static_cast<float>(std::cos(ang)), sv = static_cast<float>(std::sin(ang));
+      cs[s * hd + j] = cs[s * hd + half + j] = cv;
+      sn[s * hd + j] = sn[s * hd + half + j] = sv;
+    }
+  float *dc = nullptr, *ds = nullptr;
+  NEBW_CUDA(cudaMalloc(&dc, cs.size() * 4));
+  NEBW_CUDA(cudaMalloc(&ds, sn.size() * 4));
+  NEBW_CUDA(cudaMemcpy(dc, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  NEBW_CUDA(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  m->rope_cos = dc;
+  m->rope_sin = ds;
+  return NEBW_OK;
+}
+
+int launch_rope(const nebw_model *m, int B, int S, cudaStream_t st) {
+  const nebw_config &c = m->cfg;
+  const dim3 grid((S + nebw::kRowWarps - 1) / nebw::kRowWarps, B);
+  if (c.head_dim == 64)
+    nebw::rope_qk_kernel<64><<<grid, nebw::kRowWarps * 32, 0, st>>>(
+        m->qkv, m->off, m->len, c.hidden, m->rope_cos, m->rope_sin);
+  else
+    nebw::rope_qk_kernel<32><<<grid, nebw::kRowWarps * 32, 0, st>>>(
+        m->qkv, m->off, m->len, c.hidden, m->rope_cos, m->rope_sin);
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+int launch_glu(const nebw_model *m, int rows, const int *rows_dev, cudaStream_t st) {
+  const int64_t F = m->cfg.intermediate;
+  const int64_t threads = static_cast<int64_t>(rows) * (F / 8);
+  const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+  if (m->cfg.gated_act == NEBW_GATE_SILU)
+    nebw::glu_kernel<0><<<grid, 256, 0, st>>>(m->h, rows, rows_dev, static_cast<int>(F));
+  else
+    nebw::glu_kernel<1><<<grid, 256, 0, st>>>(m->h, rows, rows_dev, static_cast<int>(F));
+  NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }
 
@@ -934,6 +1013,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
   NEBW_REQUIRE(S > 0 && S <= c.max_seq_len, "seq %d refused: 1..max_seq_len (%d)", S,
                c.max_seq_len);
+  if (int rc = prepare_rope(m)) return rc;
   if (int rc = ensure_workspace(m, B, S)) return rc;
   const int64_t H = c.hidden, F = c.intermediate;
   const int rows = static_cast<int>(static_cast<int64_t>(B) * S);
@@ -967,8 +1047,9 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.out = m->qkv;
     if ((rc = prof_mark(m, NEBW_K_GEMM_QKV, st))) return rc;
     if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv, nebw::kEpiBf16, a, st))) return rc;
-    // attention
+    // attention (rotary positions on Q and K first, timed with it)
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
+    if (c.rope && (rc = launch_rope(m, B, S, st))) return rc;
     if (tc_attention)
       rc = launch_attention_tc(d, m->map_qkv_att, m->map_kv_att, m->off, m->len, m->att_items + 1, m->att_items, B, S,
                                c.num_heads, m->ctx, st);
@@ -988,14 +1069,19 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     if ((rc = launch_layernorm(m->x, m->y, true, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H, T_dev,
                                m->a, st)))
       return rc;
-    // FFN up + bias + GELU -> bf16
-    a.N = static_cast<int>(F);
+    // FFN up + bias + GELU -> bf16; gated: up | gate (2F wide, plain
+    // narrow), then h = up * act(gate) over the first F columns (timed with
+    // the GEMM, as the fused activation of the plain FFN is)
+    a.N = static_cast<int>(c.gated_ffn ? 2 * F : F);
     a.K = static_cast<int>(H);
     a.bias = w.b_up;
     a.resid = nullptr;
     a.out = m->h;
     if ((rc = prof_mark(m, NEBW_K_GEMM_UP, st))) return rc;
-    if ((rc = launch_gemm(d, w.up, m->map_a, m->out_h, up_epi, a, st))) return rc;
+    if ((rc = launch_gemm(d, w.up, m->map_a, m->out_h, c.gated_ffn ? nebw::kEpiBf16 : up_epi, a,
+                          st)))
+      return rc;
+    if (c.gated_ffn && (rc = launch_glu(m, rows, T_dev, st))) return rc;
     // FFN down + bias + residual (fp32, in place)
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(F);
@@ -1033,6 +1119,11 @@ extern "C" int nebw_model_create(nebw_dev *d, const nebw_config *cfg, nebw_model
                c.pooling);
   NEBW_REQUIRE(c.activation == NEBW_ACT_GELU8 || c.activation == NEBW_ACT_GELU_ERF,
                "activation %d refused", c.activation);
+  NEBW_REQUIRE(c.gated_ffn == 0 || c.gated_ffn == 1, "gated_ffn %d refused: 0 or 1", c.gated_ffn);
+  NEBW_REQUIRE(!c.gated_ffn || c.gated_act == NEBW_GATE_SILU || c.gated_act == NEBW_GATE_GELU_ERF,
+               "gated activation %d refused", c.gated_act);
+  NEBW_REQUIRE(c.rope == 0 || c.rope == 1, "rope %d refused: 0 or 1", c.rope);
+  NEBW_REQUIRE(!c.rope || c.rope_theta >= 0.0, "negative rope_theta refused");
   std::unique_ptr<nebw_model> m(new nebw_model());
   m->dev = d;
   m->cfg = c;
@@ -1099,8 +1190,8 @@ extern "C" int nebw_model_set_tensor(nebw_model *m, const char *name, const void
     else if (leaf == "qkv.bias") rc = vec(&w.b_qkv, 3 * H);
     else if (leaf == "attn_out") rc = gemm_w(&w.ao, H, H);
     else if (leaf == "attn_out.bias") rc = vec(&w.b_ao, H);
-    else if (leaf == "ffn_up") rc = gemm_w(&w.up, H, F);
-    else if (leaf == "ffn_up.bias") rc = vec(&w.b_up, F);
+    else if (leaf == "ffn_up") rc = gemm_w(&w.up, H, c.gated_ffn ? 2 * F : F);
+    else if (leaf == "ffn_up.bias") rc = vec(&w.b_up, c.gated_ffn ? 2 * F : F);
     else if (leaf == "ffn_down") rc = gemm_w(&w.dn, F, H);
     else if (leaf == "ffn_down.bias") rc = vec(&w.b_dn, H);
     else if (leaf == "ln1.weight") rc = vec(&w.ln1_g, H);
@@ -1156,13 +1247,31 @@ extern "C" int nebw_model_destroy(nebw_model *m) {
   cudaStreamSynchronize(m->dev->stream);
   free_workspace(m);
   for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
-  for (float *p : {m->word, m->pos, m->typ, m->emb_g, m->emb_b}) cudaFree(p);
+  for (float *p : {m->word, m->pos, m->typ, m->emb_g, m->emb_b, m->rope_cos, m->rope_sin})
+    cudaFree(p);
   for (auto &w : m->layers) {
     for (Weight *x : {&w.qkv, &w.ao, &w.up, &w.dn}) cudaFree(x->ptr);
     for (float *p : {w.b_qkv, w.b_ao, w.b_up, w.b_dn, w.ln1_g, w.ln1_b, w.ln2_g, w.ln2_b})
       cudaFree(p);
   }
   delete m;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, int32_t n) {
+  NEBW_REQUIRE(m && inv_freq, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  NEBW_REQUIRE(m->cfg.rope, "the model is not rotary (config.rope is 0)");
+  NEBW_REQUIRE(n == m->cfg.head_dim / 2, "%d rotary frequencies given, head_dim / 2 = %d expected",
+               n, m->cfg.head_dim / 2);
+  for (int32_t j = 0; j < n; ++j)
+    NEBW_REQUIRE(std::isfinite(inv_freq[j]) && inv_freq[j] >= 0.0,
+                 "rotary frequency %d is %g", j, inv_freq[j]);
+  NEBW_CUDA(cudaStreamSynchronize(m->dev->stream));
+  m->rope_freq.assign(inv_freq, inv_freq + n);
+  cudaFree(m->rope_cos);
+  cudaFree(m->rope_sin);
+  m->rope_cos = m->rope_sin = nullptr;  // rebuilt on the next pass
   return NEBW_OK;
 }
 
@@ -1179,10 +1288,12 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
   try {
     nebw::NpueFile f(path);
     const std::string arch = f.config_string("arch");
-    if (arch != "bert_abs_gelu_postln")
+    if (arch != "bert_abs_gelu_postln" && arch != "nomic_bert_rope_swiglu" &&
+        arch != "gte_new_rope_geglu")
       return set_error(NEBW_EINVAL,
-                       "container architecture '%s' has no encoder in this library; only "
-                       "bert_abs_gelu_postln is implemented", arch.c_str());
+                       "container architecture '%s' has no encoder in this library; "
+                       "bert_abs_gelu_postln, nomic_bert_rope_swiglu and gte_new_rope_geglu "
+                       "are implemented", arch.c_str());
     std::string layout = "pretiled_bf16";
     if (f.has_config("gemm_layout")) layout = f.config_string("gemm_layout");
     if (layout != "host" && layout != "tma_bf16")
@@ -1210,9 +1321,83 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
     c.l2_normalize = f.has_config("l2_normalize") ? f.config_string("l2_normalize") == "true" : 1;
     c.activation = NEBW_ACT_GELU8;  // what the reference's BERT host path runs (gelu_cpu)
     c.layer_norm_eps = 1e-12f;      // hard-coded by layer_norm_cpu (bert_encoder.cpp:438)
+    // The rotary / gated families, with set_model_shape's refusals
+    // (app_state.hpp:440-560): position encoding and gating asserted, the
+    // order of the fused FFN-up halves and the gate's activation read.
+    std::vector<double> inv_freq;
+    if (arch != "bert_abs_gelu_postln") {
+      const std::string pet = f.config_string("position_embedding_type");
+      if (pet != "rope")
+        return set_error(NEBW_EINVAL, "container arch is %s but position_embedding_type is '%s', "
+                         "expected 'rope'", arch.c_str(), pet.c_str());
+      if (!f.has_config("gated_ffn") || f.config_string("gated_ffn") != "true")
+        return set_error(NEBW_EINVAL, "container arch is %s but gated_ffn is not true: refusing a "
+                         "plain FFN over a fused up|gate weight", arch.c_str());
+      c.gated_ffn = 1;
+      c.rope = 1;
+      if (arch == "nomic_bert_rope_swiglu") {
+        const std::string halves = f.config_string("swiglu_halves");
+        if (halves != "fc11_up|fc12_gate")
+          return set_error(NEBW_EINVAL, "unrecognised swiglu_halves ordering '%s' (expected "
+                           "'fc11_up|fc12_gate')", halves.c_str());
+        c.rope_theta = f.config_double("rope_theta");
+        if (!(c.rope_theta > 0.0))
+          return set_error(NEBW_EINVAL, "nomic_bert_rope_swiglu container has a non-positive "
+                           "rope_theta");
+      } else {
+        const std::string halves = f.config_string("glu_halves");
+        if (halves.rfind("up_first|gate_second", 0) != 0)
+          return set_error(NEBW_EINVAL, "unrecognised glu_halves ordering '%s' (expected it to "
+                           "begin 'up_first|gate_second')", halves.c_str());
+        if (!f.has_config("rope_inv_freq"))
+          return set_error(NEBW_EINVAL, "gte_new_rope_geglu container carries no rope_inv_freq "
+                           "(the frequency set is data, not derivable from rope_theta)");
+        // a JSON array of numbers held as a string, as the packer writes it
+        const std::string raw = f.config_string("rope_inv_freq");
+        const char *q = raw.c_str();
+        while (*q && *q != '[') ++q;
+        if (*q == '[') ++q;
+        while (*q) {
+          while (*q == ' ' || *q == ',' || *q == '\n' || *q == '\t') ++q;
+          if (*q == ']' || !*q) break;
+          char *end = nullptr;
+          const double v = std::strtod(q, &end);
+          if (end == q)
+            return set_error(NEBW_EINVAL, "rope_inv_freq is not a JSON array of numbers");
+          inv_freq.push_back(static_cast<double>(static_cast<float>(v)));  // held as float
+          q = end;
+        }
+        if (static_cast<int>(inv_freq.size()) != c.head_dim / 2)
+          return set_error(NEBW_EINVAL, "rope_inv_freq holds %zu values, head_dim / 2 = %d "
+                           "expected", inv_freq.size(), c.head_dim / 2);
+      }
+      // the gate's activation is data: "silu" or "gelu" (exact erf); absent
+      // means silu on a nomic container and is refused on a gte one
+      std::string act = "silu";
+      if (f.has_config("activation")) act = f.config_string("activation");
+      else if (arch == "gte_new_rope_geglu")
+        return set_error(NEBW_EINVAL, "gte_new_rope_geglu container carries no 'activation' key");
+      if (act == "silu") c.gated_act = NEBW_GATE_SILU;
+      else if (act == "gelu") c.gated_act = NEBW_GATE_GELU_ERF;
+      else
+        return set_error(NEBW_EINVAL, "unknown gated-FFN activation '%s' (silu or gelu)",
+                         act.c_str());
+    }
     nebw_model *m = nullptr;
     if (int rc = nebw_model_create(d, &c, &m)) return rc;
-    for (const auto &n : required_names(c)) {
+    if (!inv_freq.empty()) {
+      if (int rc = nebw_model_set_rope_freq(m, inv_freq.data(),
+                                            static_cast<int32_t>(inv_freq.size()))) {
+        const std::string msg = g_last_error;
+        nebw_model_destroy(m);
+        return set_error(rc, "%s", msg.c_str());
+      }
+    }
+    std::vector<std::string> names = required_names(c);
+    // a rotary container's zero position placeholder is staged as the
+    // reference's embedding adds it (absent, a zero table is used)
+    if (c.rope && f.has("embeddings.position")) names.push_back("embeddings.position");
+    for (const auto &n : names) {
       const auto &t = f.tensor(n);
       if (t.dtype != "F32" && t.dtype != "BF16") {
         nebw_model_destroy(m);
@@ -1276,7 +1461,9 @@ extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   const int S = seq > 0 ? seq : m->cfg.max_seq_len;
   const bool tc =
       m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD;
-  return 3 + (tc ? 1 : 0) + m->cfg.num_layers * (6 + attention_launches(tc ? 64 : 0, S));
+  const int per_layer = 6 + attention_launches(tc ? 64 : 0, S) + (m->cfg.rope ? 1 : 0) +
+                        (m->cfg.gated_ffn ? 1 : 0);
+  return 3 + (tc ? 1 : 0) + m->cfg.num_layers * per_layer;
 }
 
 extern "C" int nebw_model_profile(nebw_model *m, int enable) {
@@ -1361,9 +1548,10 @@ size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 // Bytes of static scratch one pass over `rows` padded rows of `batch`
 // sequences needs, in the carve order used below.
 size_t static_scratch_need(const nebw_config &c, int64_t rows, int64_t batch) {
-  const size_t R = static_cast<size_t>(rows), H = c.hidden, F = c.intermediate;
+  const size_t R = static_cast<size_t>(rows), H = c.hidden,
+               FW = static_cast<size_t>(c.intermediate) * (c.gated_ffn ? 2 : 1);
   return align256(R * H * 4) + align256(R * H * 2) + align256(R * H * 2) +
-         align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * F * 2) +
+         align256(R * 3 * H * 2) + align256(R * H * 2) + align256(R * FW * 2) +
          align256(static_cast<size_t>(batch) * 4) + align256((static_cast<size_t>(batch) + 1) * 4) +
          align256((R / 128 + static_cast<size_t>(batch) + 1) * 4);
 }
@@ -1378,6 +1566,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
   NEBW_REQUIRE(S > 0 && S <= m->cfg.max_seq_len, "seq %d refused: 1..max_seq_len (%d)", S,
                m->cfg.max_seq_len);
+  if (int rc = prepare_rope(m)) return rc;
   const int64_t rows = static_cast<int64_t>(B) * S;
   const size_t need = static_scratch_need(m->cfg, rows, B);
   NEBW_REQUIRE(need <= kStaticScratchBytes,
@@ -1397,9 +1586,12 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   v.typ = m->typ;
   v.emb_g = m->emb_g;
   v.emb_b = m->emb_b;
+  v.rope_cos = m->rope_cos;
+  v.rope_sin = m->rope_sin;
   v.layers = m->layers;
   v.staged = m->staged;
   const size_t H = m->cfg.hidden, F = m->cfg.intermediate, R = static_cast<size_t>(rows);
+  const size_t FW = m->cfg.gated_ffn ? 2 * F : F;
   unsigned char *p = static_cast<unsigned char *>(base);
   auto carve = [&p](size_t bytes) {
     unsigned char *q = p;
@@ -1411,7 +1603,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   v.a = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
   v.qkv = reinterpret_cast<__nv_bfloat16 *>(carve(R * 3 * H * 2));
   v.ctx = reinterpret_cast<__nv_bfloat16 *>(carve(R * H * 2));
-  v.h = reinterpret_cast<__nv_bfloat16 *>(carve(R * F * 2));
+  v.h = reinterpret_cast<__nv_bfloat16 *>(carve(R * FW * 2));
   v.len = reinterpret_cast<int *>(carve(static_cast<size_t>(B) * 4));
   v.off = reinterpret_cast<int *>(carve((static_cast<size_t>(B) + 1) * 4));
   v.att_items = reinterpret_cast<int *>(carve((R / 128 + static_cast<size_t>(B) + 1) * 4));
@@ -1420,10 +1612,10 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   int rc;
   if ((rc = make_tmap_kmajor(&v.map_a, v.a, rows, H, nebw::kGemmBM))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_ctx, v.ctx, rows, H, nebw::kGemmBM))) return rc;
-  if ((rc = make_tmap_kmajor(&v.map_h, v.h, rows, F, nebw::kGemmBM))) return rc;
+  if ((rc = make_tmap_kmajor(&v.map_h, v.h, rows, F, nebw::kGemmBM, FW))) return rc;
   if ((rc = make_tmap_out(&v.out_qkv, v.qkv, rows, 3 * H, true))) return rc;
   if ((rc = make_tmap_out(&v.out_y, v.y, rows, H, true))) return rc;
-  if ((rc = make_tmap_out(&v.out_h, v.h, rows, F, true))) return rc;
+  if ((rc = make_tmap_out(&v.out_h, v.h, rows, FW, true))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_qkv_att, v.qkv, rows, 3 * H, 128))) return rc;
   if ((rc = make_tmap_kmajor(&v.map_kv_att, v.qkv, rows, 3 * H, 64))) return rc;
   return encode_device(&v, ids, lens, B, S, out, pick_stream(m->dev, stream));

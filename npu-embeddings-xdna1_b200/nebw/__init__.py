@@ -25,6 +25,7 @@ HEADER_PATH = REPO_DIR / "include" / "nebw.h"
 
 F32, BF16 = 0, 1
 ACT_NONE, ACT_GELU8, ACT_GELU_ERF = 0, 1, 2
+GATE_SILU, GATE_GELU_ERF = 0, 1
 POOL_MEAN, POOL_CLS = 0, 1
 
 
@@ -38,7 +39,8 @@ class Config(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "num_layers", "hidden", "num_heads", "head_dim", "intermediate", "vocab_size",
         "max_seq_len", "type_vocab_size", "pooling", "l2_normalize", "activation")] + [
-        ("layer_norm_eps", C.c_float)]
+        ("layer_norm_eps", C.c_float)] + [(n, C.c_int32) for n in (
+        "gated_ffn", "gated_act", "rope", "reserved0")] + [("rope_theta", C.c_double)]
 
 
 class VitConfig(C.Structure):
@@ -89,6 +91,7 @@ def lib() -> C.CDLL:
         "nebw_pool_l2": ([vp, vp, vp, vp, i32, i32, C.c_int, C.c_int, vp, vp], C.c_int),
         "nebw_narrow_bf16": ([vp, vp, i64, vp, vp], C.c_int),
         "nebw_model_create": ([vp, C.POINTER(Config), C.POINTER(vp)], C.c_int),
+        "nebw_model_set_rope_freq": ([vp, C.POINTER(C.c_double), C.c_int32], C.c_int),
         "nebw_model_set_tensor": ([vp, C.c_char_p, vp, C.c_int, i64, i64], C.c_int),
         "nebw_model_load_npue": ([vp, C.c_char_p, C.POINTER(vp)], C.c_int),
         "nebw_model_set_gemm_nk": ([vp, C.c_char_p, vp, i64, i64], C.c_int),
@@ -261,16 +264,25 @@ class Model:
     @classmethod
     def from_weights(cls, dev: Device, w, max_seq_len: int = 512, activation: int = ACT_GELU8):
         """Stage a nebw.synth.BertWeights (container layout) on `dev`."""
+        gated = getattr(w, "gated", "")
         cfg = Config(num_layers=w.layers, hidden=w.hidden, num_heads=w.heads,
                      head_dim=w.head_dim, intermediate=w.ffn, vocab_size=w.vocab,
                      max_seq_len=max_seq_len, type_vocab_size=w.typ.shape[0],
                      pooling=POOL_CLS if w.cls_pool else POOL_MEAN, l2_normalize=1,
                      activation=ACT_GELU_ERF if getattr(w, "gelu_erf", False) else activation,
-                     layer_norm_eps=1e-12)
+                     layer_norm_eps=1e-12, gated_ffn=int(bool(gated)),
+                     gated_act=GATE_GELU_ERF if gated == "geglu" else GATE_SILU,
+                     rope=int(getattr(w, "rope", False)),
+                     rope_theta=float(getattr(w, "rope_theta", 0.0)))
         h = C.c_void_p()
         _check(lib().nebw_model_create(dev.h, C.byref(cfg), C.byref(h)))
         m = cls(dev, h)
         try:
+            freq = getattr(w, "rope_inv_freq", ())
+            if len(freq):  # held as float32, as the reference reads them
+                f = np.ascontiguousarray(np.asarray(freq, np.float32).astype(np.float64))
+                _check(lib().nebw_model_set_rope_freq(
+                    m.h, f.ctypes.data_as(C.POINTER(C.c_double)), len(f)))
             for name, arr in w.tensors():
                 a = np.ascontiguousarray(arr, np.float32)
                 rows, cols = (a.shape[0], a.shape[1]) if a.ndim == 2 else (1, a.shape[0])
