@@ -60,8 +60,16 @@ PROFILE_TRAFFIC = REPO / "profiles" / "traffic.json"
 # ---------------------------------------------------------------------------
 
 def gemm_flops_per_token(a: synth.Arch) -> float:
+    """QKV + attention-out + FFN-up (2F wide for the gated families) + FFN-down."""
     H, F = a.hidden, a.ffn
-    return 2.0 * a.layers * (3 * H * H + H * H + H * F + F * H)
+    FW = 2 * F if a.gated else F
+    return 2.0 * a.layers * (3 * H * H + H * H + H * FW + F * H)
+
+
+def metric_for(cfg) -> str:
+    """The headline metric (bge-large) or the same metric named for another
+    configuration."""
+    return METRIC if cfg.key == "bge-large" else f"embeddings/sec at {cfg.key} seq{cfg.seq}"
 
 
 def attn_flops(a: synth.Arch, lens) -> float:
@@ -218,7 +226,7 @@ def reference_arm(args, cfg):
         el = time.perf_counter() - t0
     value = args.steps * per_step / el
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "embeddings/s",
+        "impl": "reference", "metric": metric_for(cfg), "value": value, "unit": "embeddings/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * el / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -373,8 +381,9 @@ def gpu_arm(args, cfg):
         T_s, L2_s = all_tok[slow].tolist()
         steps = args.steps
         Hf, F, L = float(H), float(arch.ffn), arch.layers
+        FW = 2.0 * F if arch.gated else F  # FFN-up width ([up | gate] for the gated families)
         gemm_fl = {"gemm_qkv": 2 * T_s * Hf * 3 * Hf * L, "gemm_ao": 2 * T_s * Hf * Hf * L,
-                   "gemm_up": 2 * T_s * Hf * F * L, "gemm_down": 2 * T_s * F * Hf * L}
+                   "gemm_up": 2 * T_s * Hf * FW * L, "gemm_down": 2 * T_s * F * Hf * L}
         gemm_ms = sum(pms[k] for k in gemm_fl) / steps
         gemm_tflops = sum(gemm_fl.values()) / (gemm_ms / 1e3) / 1e12
         peak_t = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
@@ -396,10 +405,10 @@ def gpu_arm(args, cfg):
         kernels["layernorm"]["frac_of_peak"] = kernels["layernorm"]["gbs"] / peaks["hbm_gbs"]
         # the dominant kernel: the FFN-up GEMM (T x 1024 -> 4096, bias + gelu8, bf16 out)
         up_ms = pms["gemm_up"] / (L * steps)
-        up_flops = 2.0 * T_s * Hf * F
-        up_bytes = T_s * Hf * 2 + Hf * F * 2 + T_s * F * 2  # A + W + C, algorithmic
+        up_flops = 2.0 * T_s * Hf * FW
+        up_bytes = T_s * Hf * 2 + Hf * FW * 2 + T_s * FW * 2  # A + W + C, algorithmic
         traffic = None
-        if PROFILE_TRAFFIC.exists():
+        if PROFILE_TRAFFIC.exists() and cfg.key == "bge-large":
             # one ncu capture of this kernel at M = m_cap, scaled to M = T: the
             # activation and output bytes grow with M, the weight bytes do not
             tr = json.loads(PROFILE_TRAFFIC.read_text())["gemm_up"]
@@ -411,14 +420,17 @@ def gpu_arm(args, cfg):
         e2e = B * steps / e2e_s
         all_flops = float(seq_flops(arch, lens).sum())
         line = {
-            "metric": METRIC, "value": value, "unit": "embeddings/s", "n_gpus": world,
+            "metric": metric_for(cfg), "value": value, "unit": "embeddings/s", "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": ms_max / steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": f"{cfg.key}: {arch.name} architecture ({arch.layers}L, hidden "
-                                   f"{arch.hidden}, {arch.heads} heads, FFN {arch.ffn}), random-init "
-                                   f"N(0,0.02); batch {B} x seq {S}, lengths {cfg.lengths} "
-                                   f"clipped [8,{S}]; CLS pooling + L2",
+                                   f"{arch.hidden}, {arch.heads} heads, FFN {arch.ffn}"
+                                   + (f", {arch.gated} over a {2 * arch.ffn}-wide FFN-up, rotary "
+                                      "positions" if arch.gated else "")
+                                   + f"), random-init N(0,0.02); batch {B} x seq {S}, lengths "
+                                   f"{cfg.lengths} clipped [8,{S}]; "
+                                   f"{'CLS' if cfg.cls_pool else 'mean'} pooling + L2",
                        "global_batch": B, "seq_len": S, "real_tokens": int(lens.sum()),
                        "parallelism": f"dp{world} (length-balanced shards, NCCL gather to rank 0)"
                        if world > 1 else "single GPU",
@@ -429,7 +441,10 @@ def gpu_arm(args, cfg):
                     "d2h_bytes_per_step": int(B * H * 4) if world == 1 else int(world * max_b * H * 4),
                     "timer": "wall clock, synchronous per step, max over ranks"},
             "gpu_launches": int(launches_per_step * steps * world),
-            "roofline": {"kernel": "gemm_tc<256, gelu8> FFN-up (T x 1024 -> 4096), the largest share",
+            "roofline": {"kernel": (f"gemm_tc<256, bf16> FFN-up (T x {H} -> {int(FW)}) + the "
+                                    f"{arch.gated} kernel" if arch.gated else
+                                    f"gemm_tc<256, gelu8> FFN-up (T x {H} -> {int(F)})")
+                                   + ", the largest share",
                          "bound": "tensor", "achieved": up_flops / (up_ms / 1e3) / 1e12,
                          "peak": peak_t, "unit": "TFLOP/s",
                          "frac": up_flops / (up_ms / 1e3) / 1e12 / peak_t,

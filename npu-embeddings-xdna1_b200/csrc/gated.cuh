@@ -29,9 +29,9 @@ namespace nebw {
 // cos[s, j] == cos[s, j + HD/2] (the reference's duplicated halves).  Lane
 // work items are two adjacent d of one head of Q or K, so that a half-warp
 // reads 64 contiguous bytes of each half.  The rotation is
-//   o1 = x1 c - x2 s,  o2 = x2 c + x1 s
-// with separately rounded products, as the reference's AVX2 form evaluates
-// it (no fused multiply-add).
+//   o1 = fma(-x2, s, x1 c),  o2 = fma(x1, s, x2 c)
+// the order in which the reference's own build (g++ -O2 -march=x86-64-v3)
+// evaluates its AVX2 form: the second product of each line fused.
 template <int HD>
 __global__ void __launch_bounds__(kRowWarps * 32)
     rope_qk_kernel(__nv_bfloat16 *__restrict__ qkv, const int *__restrict__ seq_off,
@@ -55,10 +55,10 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     const float2 x1 = __bfloat1622float2(a), x2 = __bfloat1622float2(z);
     const float c0 = __ldg(cs + d), c1 = __ldg(cs + d + 1);
     const float s0 = __ldg(sn + d), s1 = __ldg(sn + d + 1);
-    const float o1a = __fsub_rn(__fmul_rn(x1.x, c0), __fmul_rn(x2.x, s0));
-    const float o1b = __fsub_rn(__fmul_rn(x1.y, c1), __fmul_rn(x2.y, s1));
-    const float o2a = __fadd_rn(__fmul_rn(x2.x, c0), __fmul_rn(x1.x, s0));
-    const float o2b = __fadd_rn(__fmul_rn(x2.y, c1), __fmul_rn(x1.y, s1));
+    const float o1a = __fmaf_rn(-x2.x, s0, __fmul_rn(x1.x, c0));
+    const float o1b = __fmaf_rn(-x2.y, s1, __fmul_rn(x1.y, c1));
+    const float o2a = __fmaf_rn(x1.x, s0, __fmul_rn(x2.x, c0));
+    const float o2b = __fmaf_rn(x1.y, s1, __fmul_rn(x2.y, c1));
     *reinterpret_cast<__nv_bfloat162 *>(v + d) = __floats2bfloat162_rn(o1a, o1b);
     *reinterpret_cast<__nv_bfloat162 *>(v + d + kHalf) = __floats2bfloat162_rn(o2a, o2b);
   }

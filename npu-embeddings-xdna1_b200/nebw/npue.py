@@ -32,6 +32,8 @@ VERSION = 1
 HEADER = struct.Struct("<4sIII QQQQ 16s")
 ALIGN = 4096
 ARCH_BERT = 0
+ARCH_NOMIC = 2   # nomic_bert_rope_swiglu
+ARCH_GTE = 3     # gte_new_rope_geglu
 FLAG_PRETILED = 1
 
 DTYPES = {
@@ -134,7 +136,8 @@ class ContainerReader:
         return False
 
 
-def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synthetic/random-init"):
+def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synthetic/random-init",
+                         config_overrides: dict | None = None):
     """Write a BERT (arch 0) container in the host layout the reference's CPU
     path reads: GEMM operands F32 row-major [K, N] (`gemm_b_host`), biases and
     LayerNorm F32, embeddings F32.  Tensor names and config keys follow the
@@ -142,8 +145,12 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
     config keys are the ones set_model_shape() requires
     (runtime/include/common/app_state.hpp:380-631)."""
     H, F, L = model.hidden, model.ffn, model.layers
+    gated = getattr(model, "gated", "")
+    FW = 2 * F if gated else F
+    arch_name = {"": "bert_abs_gelu_postln", "swiglu": "nomic_bert_rope_swiglu",
+                 "geglu": "gte_new_rope_geglu"}[gated]
     config = {
-        "arch": "bert_abs_gelu_postln",
+        "arch": arch_name,
         "source_repo": source_repo,
         "source_sha256": model.fingerprint(),
         "num_layers": L, "num_heads": model.heads, "hidden": H,
@@ -165,7 +172,30 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
             "position_embeddings_presliced_to": int(max_seq_len),
         },
     }
-    w = ContainerWriter(config)
+    header_arch = ARCH_BERT
+    if gated:
+        # the keys set_model_shape reads for the gated / rotary families
+        # (app_state.hpp:440-560): a zero position placeholder, the fused
+        # FFN-up halves' order, the gate's activation, the rotary frequencies
+        config["position_embedding_type"] = "rope"
+        config["gated_ffn"] = True
+        if gated == "swiglu":
+            header_arch = ARCH_NOMIC
+            config["swiglu_halves"] = "fc11_up|fc12_gate"
+            config["activation"] = "silu"
+            config["rope_theta"] = float(model.rope_theta)
+        else:
+            header_arch = ARCH_GTE
+            config["glu_halves"] = "up_first|gate_second (gate half gets the activation)"
+            config["activation"] = "gelu"
+            config["rope_inv_freq"] = json.dumps([float(np.float32(v)) for v in model.rope_inv_freq])
+    # config_overrides: keys to replace (None: drop), for malformed-container tests
+    for k, v in (config_overrides or {}).items():
+        if v is None:
+            config.pop(k, None)
+        else:
+            config[k] = v
+    w = ContainerWriter(config, arch=header_arch)
     w.add("embeddings.word", model.word, "F32", "embedding", [model.vocab, H])
     w.add("embeddings.position", model.pos[:max_seq_len], "F32", "embedding", [max_seq_len, H])
     w.add("embeddings.token_type", model.typ, "F32", "embedding", [model.typ.shape[0], H])
@@ -179,8 +209,8 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
         w.add(p + "attn_out.bias", model.b_ao[i], "F32", "bias", [H])
         w.add(p + "ln1.weight", model.ln1_g[i], "F32", "layernorm", [H])
         w.add(p + "ln1.bias", model.ln1_b[i], "F32", "layernorm", [H])
-        w.add(p + "ffn_up", model.w_up[i], "F32", "gemm_b_host", [H, F])
-        w.add(p + "ffn_up.bias", model.b_up[i], "F32", "bias", [F])
+        w.add(p + "ffn_up", model.w_up[i], "F32", "gemm_b_host", [H, FW])
+        w.add(p + "ffn_up.bias", model.b_up[i], "F32", "bias", [FW])
         w.add(p + "ffn_down", model.w_dn[i], "F32", "gemm_b_host", [F, H])
         w.add(p + "ffn_down.bias", model.b_dn[i], "F32", "bias", [H])
         w.add(p + "ln2.weight", model.ln2_g[i], "F32", "layernorm", [H])

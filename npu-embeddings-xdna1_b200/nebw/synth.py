@@ -43,6 +43,13 @@ class Arch:
     heads: int
     ffn: int
     max_pos: int = 512
+    # the gated / rotary families (container arch nomic_bert_rope_swiglu,
+    # gte_new_rope_geglu): "" (BERT), "swiglu" or "geglu"; rotary positions
+    # from rope_theta, or from an explicit frequency set
+    gated: str = ""
+    rope: bool = False
+    rope_theta: float = 0.0
+    rope_inv_freq: tuple = ()
 
     @property
     def head_dim(self) -> int:
@@ -64,6 +71,14 @@ MINILM = Arch("all-MiniLM-L6-v2", 6, 384, 12, 1536)
 BGE_SMALL = Arch("bge-small-en-v1.5", 12, 384, 12, 1536)
 BGE_BASE = Arch("bge-base-en-v1.5", 12, 768, 12, 3072)
 BGE_LARGE = Arch("bge-large-en-v1.5", 24, 1024, 16, 4096)
+# nomic-embed-text-v1.5's shape: post-LN, no biases, SwiGLU, RoPE theta 1000
+NOMIC_BASE = Arch("nomic-embed-text-v1.5", 12, 768, 12, 3072, gated="swiglu", rope=True,
+                  rope_theta=1000.0)
+# gte-base-en-v1.5's shape: GeGLU (exact erf), real biases, RoPE with the
+# scaled frequency set inv_freq_i = 160000^(-i/32) / 8^(1/32) as data
+GTE_BASE = Arch("gte-base-en-v1.5", 12, 768, 12, 3072, gated="geglu", rope=True,
+                rope_inv_freq=tuple(float(160000.0 ** (-i / 32) / 8.0 ** (1 / 32))
+                                    for i in range(32)))
 
 CONFIGS = {
     "minilm": Config("minilm", MINILM, 32, 128, "uniform:8:128", False, 0),
@@ -71,6 +86,12 @@ CONFIGS = {
     "bge-base": Config("bge-base", BGE_BASE, 512, 512, "full", True, 2),
     "bge-large": Config("bge-large", BGE_LARGE, 1024, 512,
                         f"lognormal:96:{LOGNORMAL_SIGMA}", True, 3),
+    # the gated / rotary families on bge-large's length distribution (mean
+    # pooling, as both models are used)
+    "nomic-base": Config("nomic-base", NOMIC_BASE, 1024, 512,
+                         f"lognormal:96:{LOGNORMAL_SIGMA}", False, 6),
+    "gte-base": Config("gte-base", GTE_BASE, 1024, 512,
+                       f"lognormal:96:{LOGNORMAL_SIGMA}", False, 7),
 }
 
 
@@ -101,10 +122,19 @@ class BertWeights:
     ln2_b: list = field(default_factory=list)
     gelu_erf: bool = False
     seed: int = 0
+    gated: str = ""
+    rope: bool = False
+    rope_theta: float = 0.0
+    rope_inv_freq: tuple = ()
 
     @property
     def head_dim(self) -> int:
         return self.hidden // self.heads
+
+    @property
+    def up_width(self) -> int:
+        """Columns of ffn_up: 2F ([up | gate]) for the gated families."""
+        return 2 * self.ffn if self.gated else self.ffn
 
     def fingerprint(self) -> str:
         h = hashlib.sha256()
@@ -147,26 +177,38 @@ def make_weights(arch: Arch, seed: int, cls_pool: bool, layers: int | None = Non
     def normal(*shape):
         return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
 
+    # nomic has no biases (zero placeholders in its container); the rotary
+    # families carry a zero position table (the reference packer's
+    # placeholder, which its embedding adds)
+    no_bias = arch.gated == "swiglu"
+
+    def bias(n):
+        return np.zeros(n, np.float32) if no_bias else normal(n)
+
     m = BertWeights(
         layers=L, hidden=H, heads=arch.heads, ffn=F, vocab=vocab, cls_pool=cls_pool,
-        word=normal(vocab, H), pos=normal(arch.max_pos, H), typ=normal(TYPE_VOCAB, H),
+        word=normal(vocab, H),
+        pos=np.zeros((arch.max_pos, H), np.float32) if arch.rope else normal(arch.max_pos, H),
+        typ=normal(TYPE_VOCAB, H),
         emb_ln_g=np.ones(H, np.float32), emb_ln_b=np.zeros(H, np.float32),
-        gelu_erf=gelu_erf, seed=seed)
+        gelu_erf=gelu_erf, seed=seed, gated=arch.gated, rope=arch.rope,
+        rope_theta=arch.rope_theta, rope_inv_freq=arch.rope_inv_freq)
+    FW = 2 * F if arch.gated else F
     for _ in range(L):
         wqkv = normal(H, 3 * H)
-        bqkv = normal(3 * H)
-        wqkv[:, :H] *= scale          # the packer's Q-scale fold
+        bqkv = bias(3 * H)
+        wqkv[:, :H] *= scale          # the packer's Q-scale fold (exact before RoPE: linear)
         bqkv[:H] *= scale
         m.w_qkv.append(wqkv)
         m.b_qkv.append(bqkv)
         m.w_ao.append(normal(H, H))
-        m.b_ao.append(normal(H))
+        m.b_ao.append(bias(H))
         m.ln1_g.append(np.ones(H, np.float32))
         m.ln1_b.append(np.zeros(H, np.float32))
-        m.w_up.append(normal(H, F))
-        m.b_up.append(normal(F))
+        m.w_up.append(normal(H, FW))
+        m.b_up.append(bias(FW))
         m.w_dn.append(normal(F, H))
-        m.b_dn.append(normal(H))
+        m.b_dn.append(bias(H))
         m.ln2_g.append(np.ones(H, np.float32))
         m.ln2_b.append(np.zeros(H, np.float32))
     return m

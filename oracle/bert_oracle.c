@@ -326,6 +326,70 @@ void nebw_oracle_to_bf16(const float *x, uint16_t *out, int64_t n) {
   for (int64_t i = 0; i < n; ++i) out[i] = to_bf16_ref(x[i]);
 }
 
+/* swiglu_cpu (bert_encoder.cpp:582-627), the AVX2 form every width that is
+ * a multiple of 8 takes: SiLU = x / (1 + exp2(max(-x * log2e, -120))) with
+ * the reference's exp2 polynomial, or the exact erf GELU in double; out[j] =
+ * up[j] * act(gate[j]) over rows of [up | gate]. */
+typedef struct {
+  const float *in;
+  float *out;
+  int64_t F;
+  int32_t gated;
+} glu_ctx;
+
+static void glu_rows(void *p, int64_t lo, int64_t hi) {
+  const glu_ctx *c = (const glu_ctx *)p;
+  for (int64_t r = lo; r < hi; ++r) {
+    const float *up = c->in + r * 2 * c->F, *gate = up + c->F;
+    float *dst = c->out + r * c->F;
+    for (int64_t j = 0; j < c->F; ++j) {
+      const float xv = gate[j];
+      float act;
+      if (c->gated == 2) {
+        act = gelu_erf_ref(xv);
+      } else {
+        float a = (0.0f - xv) * 1.4426950408889634f;
+        if (a < -120.0f) a = -120.0f;
+        act = xv / (1.0f + exp2_ref(a));
+      }
+      dst[j] = up[j] * act;
+    }
+  }
+}
+
+/* apply_rope_qkv (bert_encoder.cpp:926-993): tables cos/sin [S, d] from
+ * angle s * inv_freq[j] in double rounded to float, the same value in
+ * columns j and j + d/2; each head of Q and K rotated pairwise.  The
+ * reference's AVX2 rotation, as its own build (g++ -O2 -march=x86-64-v3)
+ * compiles it, fuses the second product of each line into the sum:
+ *   o1 = fma(-x2, s, x1 c),  o2 = fma(x1, s, x2 c)
+ * (measured: an intrinsic form of that shape, built with those flags, gives
+ * exactly these values; pinned against oracle/_ref by the tests). */
+typedef struct {
+  float *qkv;
+  const float *cs, *sn;
+  int64_t S, H, heads, hd;
+} rope_ctx;
+
+static void rope_rows(void *p, int64_t lo, int64_t hi) {
+  const rope_ctx *c = (const rope_ctx *)p;
+  const int64_t half = c->hd / 2;
+  for (int64_t row = lo; row < hi; ++row) {
+    const int64_t s = row % c->S;
+    const float *cs = c->cs + s * c->hd, *sn = c->sn + s * c->hd;
+    float *base = c->qkv + row * 3 * c->H;
+    for (int64_t h = 0; h < c->heads; ++h)
+      for (int qk = 0; qk < 2; ++qk) {
+        float *v = base + qk * c->H + h * c->hd;
+        for (int64_t d = 0; d < half; ++d) {
+          const float x1 = v[d], x2 = v[d + half];
+          v[d] = fmaf(-x2, sn[d], x1 * cs[d]);
+          v[d + half] = fmaf(x1, sn[d], x2 * cs[d]);
+        }
+      }
+  }
+}
+
 /* ---- the encoder: BertEncoder::run (bert_encoder.cpp:1419-1598) ----------
  * host_ln/host_sm/host_gelu, no --npu-ops:
  *   x = LN(emb)
@@ -347,11 +411,29 @@ int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
   float *qkv = (float *)malloc((size_t)rows * 3 * H * sizeof(float));
   float *ctx = (float *)malloc((size_t)rows * H * sizeof(float));
   float *tmp = (float *)malloc((size_t)rows * H * sizeof(float));
-  float *up = (float *)malloc((size_t)rows * F * sizeof(float));
+  const int64_t FW = m->gated ? 2 * F : F;
+  float *up = (float *)malloc((size_t)rows * FW * sizeof(float));
+  float *gl = m->gated ? (float *)malloc((size_t)rows * F * sizeof(float)) : NULL;
+  float *rcs = NULL, *rsn = NULL;
+  if (m->rope_inv_freq) {
+    const int64_t hd = m->head_dim, half = hd / 2;
+    rcs = (float *)malloc((size_t)S * hd * sizeof(float));
+    rsn = (float *)malloc((size_t)S * hd * sizeof(float));
+    if (rcs && rsn)
+      for (int64_t s = 0; s < S; ++s)
+        for (int64_t j = 0; j < half; ++j) {
+          const double ang = (double)s * m->rope_inv_freq[j];
+          const float cv = (float)cos(ang), sv = (float)sin(ang);
+          rcs[s * hd + j] = rcs[s * hd + half + j] = cv;
+          rsn[s * hd + j] = rsn[s * hd + half + j] = sv;
+        }
+  }
   float *amask = (float *)malloc((size_t)rows * sizeof(float));
   float *cam = (float *)malloc((size_t)rows * sizeof(float));
-  if (!x || !res || !qkv || !ctx || !tmp || !up || !amask || !cam) {
+  if (!x || !res || !qkv || !ctx || !tmp || !up || !amask || !cam ||
+      (m->gated && !gl) || (m->rope_inv_freq && (!rcs || !rsn))) {
     free(x); free(res); free(qkv); free(ctx); free(tmp); free(up); free(amask); free(cam);
+    free(gl); free(rcs); free(rsn);
     return fail("out of host memory");
   }
 
@@ -374,6 +456,10 @@ int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
   for (int32_t L = 0; L < m->layers; ++L) {
     memcpy(res, x, (size_t)rows * H * sizeof(float));
     nebw_oracle_gemm_nt(x, rows, m->w_qkv[L], H, 3 * H, m->b_qkv[L], qkv, threads);
+    if (m->rope_inv_freq) {
+      rope_ctx rc = {qkv, rcs, rsn, S, H, m->heads, m->head_dim};
+      parallel_for(rows, threads, rope_rows, &rc);
+    }
     attn_ctx ac = {qkv, amask, ctx, S, H, m->heads, m->head_dim};
     parallel_for(B * m->heads, threads, attn_pairs, &ac);
     nebw_oracle_gemm_nt(ctx, rows, m->w_ao[L], H, H, m->b_ao[L], tmp, threads);
@@ -382,10 +468,15 @@ int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
     lc.b = m->ln1_b[L];
     parallel_for(rows, threads, ln_rows, &lc);
     memcpy(res, x, (size_t)rows * H * sizeof(float));
-    nebw_oracle_gemm_nt(x, rows, m->w_up[L], H, F, m->b_up[L], up, threads);
-    act_ctx gc = {up, m->gelu_erf};
-    parallel_for(rows * F, threads, act_range, &gc);
-    nebw_oracle_gemm_nt(up, rows, m->w_dn[L], F, H, m->b_dn[L], tmp, threads);
+    nebw_oracle_gemm_nt(x, rows, m->w_up[L], H, FW, m->b_up[L], up, threads);
+    if (m->gated) {
+      glu_ctx gg = {up, gl, F, m->gated};
+      parallel_for(rows, threads, glu_rows, &gg);
+    } else {
+      act_ctx gc = {up, m->gelu_erf};
+      parallel_for(rows * F, threads, act_range, &gc);
+    }
+    nebw_oracle_gemm_nt(m->gated ? gl : up, rows, m->w_dn[L], F, H, m->b_dn[L], tmp, threads);
     for (int64_t i = 0; i < rows * H; ++i) x[i] = tmp[i] + res[i];
     lc.g = m->ln2_g[L];
     lc.b = m->ln2_b[L];
@@ -395,6 +486,7 @@ int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
   if (hidden_out) memcpy(hidden_out, x, (size_t)rows * H * sizeof(float));
   const int rc = nebw_oracle_pool_rows(x, cam, B, S, H, m->cls_pool, m->l2_normalize, out);
   free(x); free(res); free(qkv); free(ctx); free(tmp); free(up); free(amask); free(cam);
+  free(gl); free(rcs); free(rsn);
   return rc;
 }
 

@@ -39,6 +39,14 @@ typedef struct nebw_oracle_model {
   const float *const *w_up, *const *b_up;     /* [H, F],  [F]  */
   const float *const *w_dn, *const *b_dn;     /* [F, H],  [H]  */
   const float *const *ln2_g, *const *ln2_b;   /* [H]           */
+  /* The gated / rotary families (arch nomic_bert_rope_swiglu,
+   * gte_new_rope_geglu): gated 0 = plain FFN, 1 = up * SiLU(gate), 2 = up *
+   * erf-GELU(gate) over a w_up of [H, 2F] = [up | gate] (swiglu_cpu,
+   * bert_encoder.cpp:582-627); rope_inv_freq non-NULL: head_dim/2 rotary
+   * frequencies applied to Q and K after the QKV GEMM (apply_rope_qkv,
+   * bert_encoder.cpp:926-993). */
+  int32_t gated;
+  const double *rope_inv_freq;
 } nebw_oracle_model;
 
 /* Encode `batch` padded sequences of `seq` token ids.

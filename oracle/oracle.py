@@ -43,7 +43,21 @@ class _Model(C.Structure):
         ("ln_eps", C.c_float)] + [
         (n, _f32p) for n in ("word", "pos", "typ", "emb_ln_g", "emb_ln_b")] + [
         (n, C.POINTER(_f32p)) for n in ("w_qkv", "b_qkv", "w_ao", "b_ao", "ln1_g", "ln1_b",
-                                         "w_up", "b_up", "w_dn", "b_dn", "ln2_g", "ln2_b")]
+                                         "w_up", "b_up", "w_dn", "b_dn", "ln2_g", "ln2_b")] + [
+        ("gated", C.c_int32), ("rope_inv_freq", C.POINTER(C.c_double))]
+
+
+def rope_inv_freq(w) -> np.ndarray | None:
+    """The rotary frequencies the reference uses for a model: its float
+    list widened to double (gte, app_state.hpp:516-521), or theta^(-2j/d) in
+    double (nomic, gemma_rope_tables); None for BERT."""
+    if not getattr(w, "rope", False):
+        return None
+    if len(getattr(w, "rope_inv_freq", ())):
+        return np.asarray(w.rope_inv_freq, np.float32).astype(np.float64)
+    d = w.head_dim
+    return np.array([1.0 / np.power(float(w.rope_theta), 2.0 * j / d) for j in range(d // 2)],
+                    np.float64)
 
 
 class _Vit(C.Structure):
@@ -141,7 +155,13 @@ class PortOracle:
                    emb_ln_g=_ptr(w.emb_ln_g), emb_ln_b=_ptr(w.emb_ln_b),
                    w_qkv=arr(w.w_qkv), b_qkv=arr(w.b_qkv), w_ao=arr(w.w_ao), b_ao=arr(w.b_ao),
                    ln1_g=arr(w.ln1_g), ln1_b=arr(w.ln1_b), w_up=arr(w.w_up), b_up=arr(w.b_up),
-                   w_dn=arr(w.w_dn), b_dn=arr(w.b_dn), ln2_g=arr(w.ln2_g), ln2_b=arr(w.ln2_b))
+                   w_dn=arr(w.w_dn), b_dn=arr(w.b_dn), ln2_g=arr(w.ln2_g), ln2_b=arr(w.ln2_b),
+                   gated={"": 0, "swiglu": 1, "geglu": 2}[getattr(w, "gated", "")])
+        freq = rope_inv_freq(w)
+        if freq is not None:
+            freq = np.ascontiguousarray(freq)
+            keep.append(freq)
+            m.rope_inv_freq = freq.ctypes.data_as(C.POINTER(C.c_double))
         return m, keep
 
     def encode(self, w, ids, mask, threads: int | None = None, hidden: bool = False):

@@ -16,14 +16,15 @@
 // oracle/Makefile's REF_SRCS are linked alone):
 //   npu::Device::{Device,~Device}                    runtime/include/runtime/device.hpp:29-38
 //   npu::Design::{Design,~Design,stage,bind,...}     runtime/include/runtime/design.hpp:199-263
-//   npue::gemma_rope_tables                          runtime/include/encoders/gemma_kernels.hpp:88
+// (npue::gemma_rope_tables, which the rotary host path of
+// nomic_bert_rope_swiglu calls, comes from the reference's own
+// encoders/gemma_kernels.cpp, linked alongside.)
 // (npue::whisper::NpuAttention::run comes from the reference's own
 // whisper/attention_npu.cpp, linked for the ViT path; it is not reached.)
 
 #include <stdexcept>
 #include <string>
 
-#include "encoders/gemma_kernels.hpp"
 #include "runtime/design.hpp"
 #include "runtime/device.hpp"
 
@@ -79,8 +80,4 @@ void Design::sync_slot_from_device(size_t, size_t, size_t) {
 
 }  // namespace npu
 
-namespace npue {
-void gemma_rope_tables(int64_t, int64_t, double, float *, float *) {
-  unreachable("gemma_rope_tables");
-}
-}  // namespace npue
+

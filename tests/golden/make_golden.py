@@ -16,6 +16,12 @@ shortest and longest rows are always included):
   bge_small_c2.npz   bge-small arch, 6 rows at seq 512, CLS pool
   bge_base_c3.npz    bge-base arch, 3 rows at seq 512, CLS pool
   bge_large_c4.npz   bge-large arch, 3 rows at seq 512, CLS pool
+  nomic_c6.npz       nomic-embed-text-v1.5 shape (container arch
+                     nomic_bert_rope_swiglu: RoPE theta 1000, SwiGLU, no
+                     biases), 3 rows at seq 512, mean pool
+  gte_c7.npz         gte-base-en-v1.5 shape (container arch
+                     gte_new_rope_geglu: RoPE frequencies as data, erf GeGLU),
+                     3 rows at seq 512, mean pool
   vit_base_c5.npz    vit-base-patch16-224 arch, the first 3 images of the
                      configuration's batch, the CLS row after the final
                      LayerNorm -- the reference's VitEncoder::run
@@ -47,6 +53,8 @@ FIXTURES = {
     "bge_small_c2": ("bge-small", 6),
     "bge_base_c3": ("bge-base", 3),
     "bge_large_c4": ("bge-large", 3),
+    "nomic_c6": ("nomic-base", 3),
+    "gte_c7": ("gte-base", 3),
 }
 
 

@@ -156,3 +156,81 @@ def test_encode_refusals(device):
     ok = m.encode(ids[:, :64], np.array([10, 20], np.int32))   # the same rows, S = 64
     m.close()
     assert np.isfinite(ok).all()
+
+
+GATED = ["nomic-base", "gte-base"]
+
+
+@pytest.mark.parametrize("key", GATED)
+def test_gated_rope_vs_oracle(device, port_oracle, key, tmp_path):
+    """The rotary / gated families (nomic_bert_rope_swiglu: RoPE from theta,
+    SwiGLU, no biases; gte_new_rope_geglu: RoPE frequencies as data, erf
+    GeGLU, biases) against the oracle -- staged from weights and loaded from
+    a container the reference reads -- with lengths across the 64-key and
+    128-query attention boundaries, so that every rotary position 0..511
+    of the table is used."""
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    cfg = synth.CONFIGS[key]
+    w = synth.config_weights(cfg, layers=2)
+    lens = np.array([512, 1, 63, 64, 65, 129, 200, 17], np.int32)
+    ids, mask = synth.make_tokens(len(lens), 512, lens, seed=43)
+    want = port_oracle.encode(w, ids, mask)
+    m = nebw.Model.from_weights(device, w, max_seq_len=512)
+    check(m.encode(ids, lens), want, f"{key} from weights")
+    m.close()
+    path = tmp_path / f"{key}.npue"
+    write_bert_container(path, w, max_seq_len=512)
+    m = nebw.Model.from_npue(device, path)
+    assert m.cfg.gated_ffn == 1 and m.cfg.rope == 1
+    check(m.encode(ids, lens), want, f"{key} from container")
+    m.close()
+
+
+@pytest.mark.parametrize("name,key", [("nomic_c6", "nomic-base"), ("gte_c7", "gte-base")])
+def test_gated_full_depth_matches_reference_golden(device, name, key):
+    """Full 12-layer models at seq 512 against the rows the reference's own
+    host path produced (tests/golden/)."""
+    from pathlib import Path
+    import nebw
+    from nebw import synth
+    g = np.load(Path(__file__).parent / "golden" / f"{name}.npz")
+    w = synth.config_weights(synth.CONFIGS[key])
+    m = nebw.Model.from_weights(device, w, max_seq_len=512)
+    check(m.encode(g["ids"], g["lens"]), g["embeddings"], f"{key} golden")
+    m.close()
+
+
+@pytest.mark.parametrize("override,needle", [
+    ({"swiglu_halves": "fc12_gate|fc11_up"}, "swiglu_halves"),
+    ({"position_embedding_type": "absolute"}, "position_embedding_type"),
+    ({"gated_ffn": False}, "gated_ffn"),
+    ({"activation": "relu"}, "activation"),
+    ({"rope_theta": 0.0}, "rope_theta"),
+])
+def test_gated_container_refusals(device, override, needle, tmp_path):
+    """A rotary / gated container that is malformed in one key is refused
+    with that key named, as the reference's set_model_shape refuses it."""
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    w = synth.config_weights(synth.CONFIGS["nomic-base"], layers=1)
+    path = tmp_path / "bad.npue"
+    write_bert_container(path, w, max_seq_len=64, config_overrides=override)
+    with pytest.raises(nebw.NebwError, match=needle):
+        nebw.Model.from_npue(device, path)
+
+
+def test_gte_container_refuses_missing_freq_or_activation(device, tmp_path):
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    w = synth.config_weights(synth.CONFIGS["gte-base"], layers=1)
+    for override, needle in (({"rope_inv_freq": None}, "rope_inv_freq"),
+                             ({"activation": None}, "activation"),
+                             ({"rope_inv_freq": "[1.0, 0.5]"}, "rope_inv_freq")):
+        path = tmp_path / "bad_gte.npue"
+        write_bert_container(path, w, max_seq_len=64, config_overrides=override)
+        with pytest.raises(nebw.NebwError, match=needle):
+            nebw.Model.from_npue(device, path)

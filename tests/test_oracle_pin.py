@@ -158,3 +158,37 @@ def test_port_matches_golden_vit(port_oracle):
     got = port_oracle.vit_encode(synth.vit_config_weights(cfg),
                                  synth.vit_config_images(cfg, n=1))
     np.testing.assert_array_equal(got, g["embeddings"][:1])
+
+
+@pytest.mark.parametrize("key", ["nomic-base", "gte-base"])
+def test_port_gated_rope_bit_exact_vs_reference(port_oracle, ref_oracle, key):
+    """The rotary / gated families (nomic: RoPE theta, SwiGLU, no biases;
+    gte: RoPE frequency data, erf GeGLU): the restatement against the
+    reference's own host path on the same 2-layer container, every hidden
+    row and the pooled output, bit for bit."""
+    from nebw import synth
+    cfg = synth.CONFIGS[key]
+    w = synth.config_weights(cfg, layers=2)
+    lens = np.array([64, 1, 33, 63, 17], np.int32)
+    ids, mask = synth.make_tokens(len(lens), 64, lens, seed=41)
+    a, ha = port_oracle.encode(w, ids, mask, hidden=True)
+    b, hb = ref_oracle.encode(w, ids, mask, hidden=True)
+    np.testing.assert_array_equal(ha, hb)
+    np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("name,key", [("nomic_c6", "nomic-base"), ("gte_c7", "gte-base")])
+def test_port_matches_golden_gated(port_oracle, name, key):
+    """The restatement reproduces the reference's golden rows of the full
+    12-layer models (shortest row of each fixture), bit for bit."""
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    from make_golden import weights_fingerprint
+
+    from nebw import synth
+    g = load_golden(name)
+    w = synth.config_weights(synth.CONFIGS[key])
+    assert weights_fingerprint(w) == str(g["weights_fingerprint"])
+    r = int(np.argmin(g["lens"]))
+    got = port_oracle.encode(w, g["ids"][r:r + 1], g["mask"][r:r + 1])
+    np.testing.assert_array_equal(got, g["embeddings"][r:r + 1])
