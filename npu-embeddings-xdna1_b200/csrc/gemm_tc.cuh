@@ -46,6 +46,11 @@ enum GemmEpi : int {
   kEpiBf16Erf = 2,    // out bf16 = erf-gelu(acc + bias)
   kEpiF32 = 3,        // out f32  = acc + bias
   kEpiF32Resid = 4,   // out f32  = (acc + bias) + resid   (resid may alias out)
+  // Gated FFN-up over a weight whose N columns are interleaved in groups of
+  // 64 = [32 up | 32 gate] (the same 32 output columns): out bf16 [M, N/2],
+  // out[:, 32g + i] = (up + bias) * act(gate + bias).  CTA-pair kernel only.
+  kEpiBf16SwiGLU = 5,  // act = SiLU
+  kEpiBf16GeGLU = 6,   // act = erf GELU
 };
 
 struct GemmArgs {
@@ -155,6 +160,14 @@ __device__ __forceinline__ void gelu_erf_x2(float &a, float &b) {
   unpk2(sp, s0, s1);
   const uint64_t aq = mul_x2(ax, pk2(rcp_approx(s0), rcp_approx(s1)));  // 2 |x| q
   unpk2(fma_x2(aq, pk2(-0.5f, -0.5f), pk2(fmaxf(a, 0.0f), fmaxf(b, 0.0f))), a, b);
+}
+
+// SiLU on the SFU: x / (1 + 2^(-x log2 e)), the exponent floored at -120 as
+// swiglu_cpu floors it (bert_encoder.cpp:582-627); ex2.approx and a fast
+// divide, far below the bf16 rounding of the gated product.
+__device__ __forceinline__ float silu_fast(float x) {
+  const float a = fmaxf(-x * 1.4426950408889634f, -120.0f);
+  return __fdividef(x, 1.0f + ex2_approx(a));
 }
 
 template <int EPI>
@@ -497,6 +510,46 @@ __device__ __forceinline__ void epi_stage32(const GemmArgs &p, int col0, const u
   }
 }
 
+// Gated epilogue: the up chunk (GEMM columns col0 .. col0+31) and the gate
+// chunk (col0+32 .. col0+63) of this thread's row -> 32 bf16 outputs
+// up * act(gate), biases added first, staged as one bf16 32 x 32 chunk in
+// the output map's 64-byte swizzle.
+template <int EPI>
+__device__ __forceinline__ void epi_stage_glu(const GemmArgs &p, int col0,
+                                              const uint32_t (&ru)[32],
+                                              const uint32_t (&rg)[32], uint8_t *chunk,
+                                              int lane) {
+  uint32_t pk[16];
+  const float4 *bu = p.bias ? reinterpret_cast<const float4 *>(p.bias + col0) : nullptr;
+  const float4 *bg = p.bias ? reinterpret_cast<const float4 *>(p.bias + col0 + 32) : nullptr;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float u[4] = {__uint_as_float(ru[4 * q]), __uint_as_float(ru[4 * q + 1]),
+                  __uint_as_float(ru[4 * q + 2]), __uint_as_float(ru[4 * q + 3])};
+    float g[4] = {__uint_as_float(rg[4 * q]), __uint_as_float(rg[4 * q + 1]),
+                  __uint_as_float(rg[4 * q + 2]), __uint_as_float(rg[4 * q + 3])};
+    if (bu) {
+      const float4 b1 = __ldg(bu + q), b2 = __ldg(bg + q);
+      u[0] += b1.x; u[1] += b1.y; u[2] += b1.z; u[3] += b1.w;
+      g[0] += b2.x; g[1] += b2.y; g[2] += b2.z; g[3] += b2.w;
+    }
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (EPI == kEpiBf16SwiGLU) o[i] = u[i] * silu_fast(g[i]);
+      else o[i] = u[i] * gelu_erf(g[i]);
+    }
+    pk[2 * q] = pack_bf16x2(o[0], o[1]);
+    pk[2 * q + 1] = pack_bf16x2(o[2], o[3]);
+  }
+  uint8_t *row = chunk + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4 *>(row + ((q ^ sw) << 4)) =
+        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+}
+
 template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -667,6 +720,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col_half);
       uint32_t ra[32], rb[32];
+      if constexpr (EPI == kEpiBf16SwiGLU || EPI == kEpiBf16GeGLU) {
+        // chunk pairs: 2k = up, 2k + 1 = gate of the same 32 output columns
+#pragma unroll
+        for (int c = 0; c < kChunks; c += 2) {
+          tmem_ld_32x32b_x32(t_row + c * 32, ra);
+          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, rb);
+          tmem_wait_ld_regs(ra);
+          tmem_wait_ld_regs(rb);
+          if (c + 2 == kChunks) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&tempty[acc]), 0));
+          }
+          const int col0 = nb * BN + col_half + c * 32;  // GEMM column of the up chunk
+          if (row0 < M && col0 < p.N) {  // warp-uniform
+            uint8_t *chunk = my_staging + (nstore % kSlots) * kOutChunk;
+            if (lane == 0) bulk_wait_group_read<kSlots - 1>();
+            __syncwarp();
+            epi_stage_glu<EPI>(p, col0, ra, rb, chunk, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, chunk, col0 / 2, row0);  // output column (col0 / 64) * 32
+              bulk_commit_group();
+            }
+            ++nstore;
+          }
+        }
+        continue;
+      }
       tmem_ld_32x32b_x32(t_row, ra);
       tmem_wait_ld_regs(ra);
 #pragma unroll

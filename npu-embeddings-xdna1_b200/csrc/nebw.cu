@@ -232,6 +232,10 @@ int set_all_gemm_attrs() {
   rc |= set_pair_attr<256, nebw::kEpiBf16Gelu8>();
   rc |= set_pair_attr<256, nebw::kEpiBf16Erf>();
   rc |= set_pair_attr<256, nebw::kEpiF32>();
+  rc |= set_pair_attr<128, nebw::kEpiBf16SwiGLU>();
+  rc |= set_pair_attr<128, nebw::kEpiBf16GeGLU>();
+  rc |= set_pair_attr<256, nebw::kEpiBf16SwiGLU>();
+  rc |= set_pair_attr<256, nebw::kEpiBf16GeGLU>();
   rc |= set_pair_attr<256, nebw::kEpiF32Resid>();
   return rc ? NEBW_ECUDA : NEBW_OK;
 }
@@ -308,6 +312,8 @@ int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensor
     case nebw::kEpiBf16Erf: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Erf><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     case nebw::kEpiF32: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     case nebw::kEpiF32Resid: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32Resid><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiBf16SwiGLU: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16SwiGLU><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiBf16GeGLU: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16GeGLU><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     default: return set_error(NEBW_EINVAL, "unknown GEMM epilogue %d", epi);
   }
   NEBW_CUDA(cudaGetLastError());
@@ -803,6 +809,10 @@ struct nebw_model {
   // from rope_freq (nebw_model_set_rope_freq) or cfg.rope_theta
   float *rope_cos = nullptr, *rope_sin = nullptr;
   std::vector<double> rope_freq;
+  // gated FFN with the GLU fused into the FFN-up GEMM's epilogue (CTA pairs
+  // available): ffn_up's columns are staged interleaved in groups of 64 =
+  // [32 up | 32 gate] and the GEMM writes h [rows, F] directly
+  bool glu_fused = false;
   std::vector<LayerW> layers;
   std::map<std::string, bool> staged;  // container name -> set
   // workspace (capacity rows_cap = B * S of the largest call so far)
@@ -854,7 +864,8 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   NEBW_CUDA(cudaStreamSynchronize(m->dev->stream));
   free_workspace(m);
   const int64_t H = m->cfg.hidden, F = m->cfg.intermediate;
-  const int64_t FW = m->cfg.gated_ffn ? 2 * F : F;  // FFN-up output width
+  // FFN-up output width: [up | gate] when the GLU is a separate pass
+  const int64_t FW = m->cfg.gated_ffn && !m->glu_fused ? 2 * F : F;
   const int64_t R = std::max(rows, m->rows_cap), Bc = std::max(B, m->batch_cap);
   auto alloc = [&](void **p, size_t bytes) -> int {
     if (cudaMalloc(p, bytes) != cudaSuccess) {
@@ -901,6 +912,34 @@ int upload_f32(nebw_dev *d, float **dst, const void *src, int dtype, int64_t n) 
   NEBW_CUDA(cudaMemcpyAsync(*dst, src, n * 4, cudaMemcpyHostToDevice, d->stream));
   NEBW_CUDA(cudaStreamSynchronize(d->stream));
   return NEBW_OK;
+}
+
+// Column n of the interleaved gated FFN-up operand (groups of 64 = [32 up |
+// 32 gate] of the same 32 output columns) takes column glu_src(n) of the
+// container's [up | gate] halves.
+int64_t glu_src(int64_t n, int64_t F) {
+  const int64_t g = n / 64, i = n % 64;
+  return i < 32 ? g * 32 + i : F + g * 32 + (i - 32);
+}
+
+// A host [rows, cols] array of `esize`-byte elements with its columns
+// (by_rows false) or rows (by_rows true) reordered by glu_src.
+std::vector<unsigned char> glu_interleave(const void *src, int64_t rows, int64_t cols,
+                                          size_t esize, int64_t F, bool by_rows) {
+  std::vector<unsigned char> out(static_cast<size_t>(rows * cols) * esize);
+  const unsigned char *in = static_cast<const unsigned char *>(src);
+  if (by_rows) {
+    for (int64_t r = 0; r < rows; ++r)
+      std::memcpy(&out[static_cast<size_t>(r * cols) * esize],
+                  in + static_cast<size_t>(glu_src(r, F) * cols) * esize,
+                  static_cast<size_t>(cols) * esize);
+  } else {
+    for (int64_t r = 0; r < rows; ++r)
+      for (int64_t n = 0; n < cols; ++n)
+        std::memcpy(&out[static_cast<size_t>(r * cols + n) * esize],
+                    in + static_cast<size_t>(r * cols + glu_src(n, F)) * esize, esize);
+  }
+  return out;
 }
 
 std::vector<std::string> required_names(const nebw_config &c) {
@@ -1078,10 +1117,12 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->h;
     if ((rc = prof_mark(m, NEBW_K_GEMM_UP, st))) return rc;
-    if ((rc = launch_gemm(d, w.up, m->map_a, m->out_h, c.gated_ffn ? nebw::kEpiBf16 : up_epi, a,
-                          st)))
-      return rc;
-    if (c.gated_ffn && (rc = launch_glu(m, rows, T_dev, st))) return rc;
+    const int epi = !c.gated_ffn ? up_epi
+                    : m->glu_fused ? (c.gated_act == NEBW_GATE_SILU ? nebw::kEpiBf16SwiGLU
+                                                                    : nebw::kEpiBf16GeGLU)
+                                   : nebw::kEpiBf16;
+    if ((rc = launch_gemm(d, w.up, m->map_a, m->out_h, epi, a, st))) return rc;
+    if (c.gated_ffn && !m->glu_fused && (rc = launch_glu(m, rows, T_dev, st))) return rc;
     // FFN down + bias + residual (fp32, in place)
     a.N = static_cast<int>(H);
     a.K = static_cast<int>(F);
@@ -1127,6 +1168,7 @@ extern "C" int nebw_model_create(nebw_dev *d, const nebw_config *cfg, nebw_model
   std::unique_ptr<nebw_model> m(new nebw_model());
   m->dev = d;
   m->cfg = c;
+  m->glu_fused = c.gated_ffn && d->gemm_pairs > 0;
   m->layers.resize(c.num_layers);
   *out = m.release();
   return NEBW_OK;
@@ -1190,7 +1232,28 @@ extern "C" int nebw_model_set_tensor(nebw_model *m, const char *name, const void
     else if (leaf == "qkv.bias") rc = vec(&w.b_qkv, 3 * H);
     else if (leaf == "attn_out") rc = gemm_w(&w.ao, H, H);
     else if (leaf == "attn_out.bias") rc = vec(&w.b_ao, H);
-    else if (leaf == "ffn_up") rc = gemm_w(&w.up, H, c.gated_ffn ? 2 * F : F);
+    else if (leaf == "ffn_up" && m->glu_fused) {
+      // interleaved [32 up | 32 gate] column groups for the fused GLU epilogue
+      if (!(rc = expect(H, 2 * F))) {
+        const auto inter =
+            glu_interleave(host, H, 2 * F, dtype == NEBW_F32 ? 4 : 2, F, /*by_rows=*/false);
+        if (w.up.ptr) {
+          cudaFree(w.up.ptr);
+          w.up.ptr = nullptr;
+        }
+        rc = stage_weight(m->dev, inter.data(), dtype, H, 2 * F, &w.up);
+      }
+    } else if (leaf == "ffn_up.bias" && m->glu_fused) {
+      if (rows * cols != 2 * F)
+        rc = set_error(NEBW_EINVAL, "tensor '%s' must hold %lld values", name,
+                       static_cast<long long>(2 * F));
+      else if (dtype != NEBW_F32)
+        rc = set_error(NEBW_EINVAL, "this tensor must be F32 (as the container stores it)");
+      else {
+        const auto inter = glu_interleave(host, 1, 2 * F, 4, F, false);
+        rc = upload_f32(m->dev, &w.b_up, inter.data(), dtype, 2 * F);
+      }
+    } else if (leaf == "ffn_up") rc = gemm_w(&w.up, H, c.gated_ffn ? 2 * F : F);
     else if (leaf == "ffn_up.bias") rc = vec(&w.b_up, c.gated_ffn ? 2 * F : F);
     else if (leaf == "ffn_down") rc = gemm_w(&w.dn, F, H);
     else if (leaf == "ffn_down.bias") rc = vec(&w.b_dn, H);
@@ -1225,9 +1288,14 @@ extern "C" int nebw_model_set_gemm_nk(nebw_model *m, const char *name, const uin
   int64_t K = 0, N = 0;
   if (leaf == "qkv") dst = &w.qkv, K = H, N = 3 * H;
   else if (leaf == "attn_out") dst = &w.ao, K = H, N = H;
-  else if (leaf == "ffn_up") dst = &w.up, K = H, N = F;
+  else if (leaf == "ffn_up") dst = &w.up, K = H, N = c.gated_ffn ? 2 * F : F;
   else if (leaf == "ffn_down") dst = &w.dn, K = F, N = H;
   else return set_error(NEBW_EINVAL, "'%s' is not a GEMM operand", name);
+  std::vector<unsigned char> inter;
+  if (leaf == "ffn_up" && m->glu_fused && n_rows == N && k_cols == K) {
+    inter = glu_interleave(host, N, K, 2, F, /*by_rows=*/true);  // [N, K]: reorder rows
+    host = reinterpret_cast<const uint16_t *>(inter.data());
+  }
   if (n_rows != N || k_cols != K)
     return set_error(NEBW_EINVAL, "GEMM operand '%s' is [%lld, %lld] (N, K), expected [%lld, %lld]",
                      name, static_cast<long long>(n_rows), static_cast<long long>(k_cols),
@@ -1462,7 +1530,7 @@ extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   const bool tc =
       m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD;
   const int per_layer = 6 + attention_launches(tc ? 64 : 0, S) + (m->cfg.rope ? 1 : 0) +
-                        (m->cfg.gated_ffn ? 1 : 0);
+                        (m->cfg.gated_ffn && !m->glu_fused ? 1 : 0);
   return 3 + (tc ? 1 : 0) + m->cfg.num_layers * per_layer;
 }
 
@@ -1588,10 +1656,11 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   v.emb_b = m->emb_b;
   v.rope_cos = m->rope_cos;
   v.rope_sin = m->rope_sin;
+  v.glu_fused = m->glu_fused;
   v.layers = m->layers;
   v.staged = m->staged;
   const size_t H = m->cfg.hidden, F = m->cfg.intermediate, R = static_cast<size_t>(rows);
-  const size_t FW = m->cfg.gated_ffn ? 2 * F : F;
+  const size_t FW = m->cfg.gated_ffn && !m->glu_fused ? 2 * F : F;
   unsigned char *p = static_cast<unsigned char *>(base);
   auto carve = [&p](size_t bytes) {
     unsigned char *q = p;

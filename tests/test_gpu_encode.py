@@ -234,3 +234,43 @@ def test_gte_container_refuses_missing_freq_or_activation(device, tmp_path):
         write_bert_container(path, w, max_seq_len=64, config_overrides=override)
         with pytest.raises(nebw.NebwError, match=needle):
             nebw.Model.from_npue(device, path)
+
+
+_GATED_SINGLE_CTA_CHILD = r"""
+import sys
+import numpy as np
+import nebw
+from nebw import synth
+
+key, out = sys.argv[1], sys.argv[2]
+w = synth.config_weights(synth.CONFIGS[key], layers=2)
+lens = np.array([512, 1, 63, 64, 65, 129, 200, 17], np.int32)
+ids, mask = synth.make_tokens(len(lens), 512, lens, seed=43)
+dev = nebw.Device(0)
+m = nebw.Model.from_weights(dev, w, max_seq_len=512)
+np.save(out, m.encode(ids, lens))
+m.close()
+dev.close()
+"""
+
+
+@pytest.mark.parametrize("key", GATED)
+def test_gated_single_cta_path_vs_oracle(port_oracle, key, tmp_path):
+    """Without CTA pairs (forced with NEBW_GEMM_CTAS=1 in a child process)
+    the gated FFN runs unfused: FFN-up writes [up | gate] and a separate pass
+    forms up * act(gate).  That path against the oracle."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    from nebw import synth
+    repo = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, NEBW_GEMM_CTAS="1",
+               PYTHONPATH=os.pathsep.join([str(repo / "npu-embeddings-xdna1_b200"), str(repo)]))
+    out = tmp_path / "single.npy"
+    subprocess.run([sys.executable, "-c", _GATED_SINGLE_CTA_CHILD, key, str(out)], env=env,
+                   check=True, timeout=600)
+    w = synth.config_weights(synth.CONFIGS[key], layers=2)
+    lens = np.array([512, 1, 63, 64, 65, 129, 200, 17], np.int32)
+    ids, mask = synth.make_tokens(len(lens), 512, lens, seed=43)
+    check(np.load(out), port_oracle.encode(w, ids, mask), f"{key} single-CTA path")
