@@ -73,3 +73,34 @@ def test_reader_roundtrip_and_refusals(tmp_path):
     (tmp_path / "v2.npue").write_bytes(bytes(bad))
     with pytest.raises(ValueError, match="version"):
         ContainerReader(tmp_path / "v2.npue")
+
+
+@pytest.mark.parametrize("key,arch,act", [("nomic-base", "nomic_bert_rope_swiglu", "silu"),
+                                          ("gte-base", "gte_new_rope_geglu", "gelu")])
+def test_gated_rotary_container_keys(tmp_path, key, arch, act):
+    """The gated / rotary containers carry the keys the reference's
+    set_model_shape reads (app_state.hpp:440-560): arch, rope position
+    encoding, gated_ffn, the FFN-up halves' order, the gate activation, and
+    theta (nomic) or the frequency list as a JSON string (gte); ffn_up is
+    [hidden, 2 * intermediate]."""
+    import json
+    from nebw import synth
+    from nebw.npue import ContainerReader, write_bert_container
+    w = synth.config_weights(synth.CONFIGS[key], layers=1)
+    path = tmp_path / "g.npue"
+    write_bert_container(path, w, max_seq_len=64)
+    with ContainerReader(path) as r:
+        c = r.config
+        assert c["arch"] == arch and c["position_embedding_type"] == "rope"
+        assert c["gated_ffn"] is True and c["activation"] == act
+        assert r.entries["layer.0.ffn_up"]["logical_shape"] == [w.hidden, 2 * w.ffn]
+        assert r.entries["layer.0.ffn_up.bias"]["logical_shape"] == [2 * w.ffn]
+        if key == "nomic-base":
+            assert c["swiglu_halves"] == "fc11_up|fc12_gate" and c["rope_theta"] == 1000.0
+            assert not np.any(r.tensor("layer.0.qkv.bias"))  # nomic has no biases
+        else:
+            assert c["glu_halves"].startswith("up_first|gate_second")
+            freq = json.loads(c["rope_inv_freq"])
+            assert len(freq) == w.head_dim // 2
+            np.testing.assert_array_equal(np.float32(freq), np.float32(w.rope_inv_freq))
+        assert not np.any(r.tensor("embeddings.position"))  # the zero placeholder
