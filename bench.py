@@ -441,8 +441,8 @@ def gpu_arm(args, cfg):
                     "d2h_bytes_per_step": int(B * H * 4) if world == 1 else int(world * max_b * H * 4),
                     "timer": "wall clock, synchronous per step, max over ranks"},
             "gpu_launches": int(launches_per_step * steps * world),
-            "roofline": {"kernel": (f"gemm_tc<256, bf16> FFN-up (T x {H} -> {int(FW)}) + the "
-                                    f"{arch.gated} kernel" if arch.gated else
+            "roofline": {"kernel": (f"gemm_tc<256, {arch.gated}> FFN-up (T x {H} -> {int(FW)}, "
+                                    f"{arch.gated} epilogue -> {int(F)})" if arch.gated else
                                     f"gemm_tc<256, gelu8> FFN-up (T x {H} -> {int(F)})")
                                    + ", the largest share",
                          "bound": "tensor", "achieved": up_flops / (up_ms / 1e3) / 1e12,

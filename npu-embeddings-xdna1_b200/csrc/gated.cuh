@@ -64,6 +64,16 @@ __global__ void __launch_bounds__(kRowWarps * 32)
   }
 }
 
+// Position of every packed row in its sequence (pos[seq_off[b] + s] = s),
+// grid (ceil(S / 256), B): the rotary QKV epilogue's per-row input.
+__global__ void __launch_bounds__(256)
+    row_pos_kernel(const int *__restrict__ seq_off, const int *__restrict__ seq_len,
+                   int *__restrict__ pos) {
+  const int b = blockIdx.y;
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < __ldg(seq_len + b)) pos[__ldg(seq_off + b) + s] = s;
+}
+
 // SiLU as swiglu_cpu computes it: x / (1 + 2^max(-x log2 e, -120)).
 __device__ __forceinline__ float silu_ref(float x) {
   const float a = fmaxf(__fmul_rn(-x, 1.4426950408889634f), -120.0f);

@@ -51,6 +51,10 @@ enum GemmEpi : int {
   // out[:, 32g + i] = (up + bias) * act(gate + bias).  CTA-pair kernel only.
   kEpiBf16SwiGLU = 5,  // act = SiLU
   kEpiBf16GeGLU = 6,   // act = erf GELU
+  // QKV with rotary positions: columns < rope_cols (Q and K) rotated per
+  // head_dim-64 head by the row's position (row_pos) before the narrow, V
+  // columns plain.  CTA-pair kernel only.
+  kEpiBf16Rope = 7,
 };
 
 struct GemmArgs {
@@ -61,6 +65,11 @@ struct GemmArgs {
   const float *resid;  // [M, N] fp32 for kEpiF32Resid
   void *out;           // [M, N], bf16 or fp32 by epilogue
   int *err;            // device error word
+  // kEpiBf16Rope: position of each packed row in its sequence, the cos / sin
+  // tables [rope_rows, 64], the rotated column count (2 * hidden)
+  const int *row_pos;
+  const float *rope_cos, *rope_sin;
+  int rope_rows, rope_cols;
 };
 
 constexpr int kGemmBM = 128;
@@ -550,6 +559,57 @@ __device__ __forceinline__ void epi_stage_glu(const GemmArgs &p, int col0,
         make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
 }
 
+// Rotary epilogue for one head of Q or K: chunk x1 (dims 0..31, GEMM
+// columns col0 ..) and x2 (dims 32..63, col0 + 32 ..) of this thread's row,
+// biases added, rotated by the row's position (o1 = fma(-x2, s, x1 c), o2 =
+// fma(x1, s, x2 c), the reference build's evaluation order), narrowed and
+// staged as two bf16 32 x 32 chunks.  The position is clamped to the table,
+// so a row past the live count reads a valid entry (its output is never
+// used).
+__device__ __forceinline__ void epi_stage_rope(const GemmArgs &p, int col0, int row, int live_rows,
+                                               const uint32_t (&r1)[32], const uint32_t (&r2)[32],
+                                               uint8_t *chunk1, uint8_t *chunk2, int lane) {
+  int pos = row < live_rows ? __ldg(p.row_pos + row) : 0;
+  pos = min(max(pos, 0), p.rope_rows - 1);
+  const float4 *cs = reinterpret_cast<const float4 *>(p.rope_cos + static_cast<int64_t>(pos) * 64);
+  const float4 *sn = reinterpret_cast<const float4 *>(p.rope_sin + static_cast<int64_t>(pos) * 64);
+  const float4 *b1 = p.bias ? reinterpret_cast<const float4 *>(p.bias + col0) : nullptr;
+  const float4 *b2 = p.bias ? reinterpret_cast<const float4 *>(p.bias + col0 + 32) : nullptr;
+  uint32_t pk1[16], pk2a[16];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 c = __ldg(cs + q), sv = __ldg(sn + q);
+    float x1[4] = {__uint_as_float(r1[4 * q]), __uint_as_float(r1[4 * q + 1]),
+                   __uint_as_float(r1[4 * q + 2]), __uint_as_float(r1[4 * q + 3])};
+    float x2[4] = {__uint_as_float(r2[4 * q]), __uint_as_float(r2[4 * q + 1]),
+                   __uint_as_float(r2[4 * q + 2]), __uint_as_float(r2[4 * q + 3])};
+    if (b1) {
+      const float4 u = __ldg(b1 + q), w = __ldg(b2 + q);
+      x1[0] += u.x; x1[1] += u.y; x1[2] += u.z; x1[3] += u.w;
+      x2[0] += w.x; x2[1] += w.y; x2[2] += w.z; x2[3] += w.w;
+    }
+    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+    float o1[4], o2[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o1[i] = __fmaf_rn(-x2[i], ss[i], __fmul_rn(x1[i], cc[i]));
+      o2[i] = __fmaf_rn(x1[i], ss[i], __fmul_rn(x2[i], cc[i]));
+    }
+    pk1[2 * q] = pack_bf16x2(o1[0], o1[1]);
+    pk1[2 * q + 1] = pack_bf16x2(o1[2], o1[3]);
+    pk2a[2 * q] = pack_bf16x2(o2[0], o2[1]);
+    pk2a[2 * q + 1] = pack_bf16x2(o2[2], o2[3]);
+  }
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    *reinterpret_cast<uint4 *>(chunk1 + lane * 64 + ((q ^ sw) << 4)) =
+        make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
+    *reinterpret_cast<uint4 *>(chunk2 + lane * 64 + ((q ^ sw) << 4)) =
+        make_uint4(pk2a[4 * q], pk2a[4 * q + 1], pk2a[4 * q + 2], pk2a[4 * q + 3]);
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -746,6 +806,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
               bulk_commit_group();
             }
             ++nstore;
+          }
+        }
+        continue;
+      }
+      if constexpr (EPI == kEpiBf16Rope) {
+        // chunk pairs: the two halves (dims 0..31, 32..63) of one head
+#pragma unroll
+        for (int c = 0; c < kChunks; c += 2) {
+          tmem_ld_32x32b_x32(t_row + c * 32, ra);
+          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, rb);
+          tmem_wait_ld_regs(ra);
+          tmem_wait_ld_regs(rb);
+          if (c + 2 == kChunks) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&tempty[acc]), 0));
+          }
+          const int col0 = nb * BN + col_half + c * 32;
+          if (row0 < M && col0 < p.N) {  // warp-uniform
+            uint8_t *c1 = my_staging + (nstore % kSlots) * kOutChunk;
+            uint8_t *c2 = my_staging + ((nstore + 1) % kSlots) * kOutChunk;
+            if (lane == 0) bulk_wait_group_read<kSlots - 2>();  // both slots free
+            __syncwarp();
+            if (col0 < p.rope_cols) {
+              epi_stage_rope(p, col0, row, M, ra, rb, c1, c2, lane);
+            } else {
+              epi_stage32<kEpiBf16>(p, col0, ra, c1, lane);
+              epi_stage32<kEpiBf16>(p, col0 + 32, rb, c2, lane);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, c1, col0, row0);
+              bulk_commit_group();
+              tma_store_2d(&tmC, c2, col0 + 32, row0);
+              bulk_commit_group();
+            }
+            nstore += 2;
           }
         }
         continue;

@@ -236,6 +236,8 @@ int set_all_gemm_attrs() {
   rc |= set_pair_attr<128, nebw::kEpiBf16GeGLU>();
   rc |= set_pair_attr<256, nebw::kEpiBf16SwiGLU>();
   rc |= set_pair_attr<256, nebw::kEpiBf16GeGLU>();
+  rc |= set_pair_attr<128, nebw::kEpiBf16Rope>();
+  rc |= set_pair_attr<256, nebw::kEpiBf16Rope>();
   rc |= set_pair_attr<256, nebw::kEpiF32Resid>();
   return rc ? NEBW_ECUDA : NEBW_OK;
 }
@@ -314,6 +316,7 @@ int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensor
     case nebw::kEpiF32Resid: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiF32Resid><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     case nebw::kEpiBf16SwiGLU: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16SwiGLU><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     case nebw::kEpiBf16GeGLU: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16GeGLU><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiBf16Rope: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Rope><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     default: return set_error(NEBW_EINVAL, "unknown GEMM epilogue %d", epi);
   }
   NEBW_CUDA(cudaGetLastError());
@@ -813,6 +816,9 @@ struct nebw_model {
   // available): ffn_up's columns are staged interleaved in groups of 64 =
   // [32 up | 32 gate] and the GEMM writes h [rows, F] directly
   bool glu_fused = false;
+  // rotary positions applied in the QKV GEMM's epilogue (CTA pairs,
+  // head_dim 64): the position of each packed row, [rows_cap] ints
+  int *row_pos = nullptr;
   std::vector<LayerW> layers;
   std::map<std::string, bool> staged;  // container name -> set
   // workspace (capacity rows_cap = B * S of the largest call so far)
@@ -849,6 +855,8 @@ void free_workspace(nebw_model *m) {
   cudaFree(m->off);
   cudaFree(m->att_items);
   cudaFree(m->out);
+  cudaFree(m->row_pos);
+  m->row_pos = nullptr;
   m->x = nullptr;
   m->y = nullptr;
   m->a = m->qkv = m->ctx = m->h = nullptr;
@@ -887,6 +895,8 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->off), (Bc + 1) * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->att_items), (R / 128 + Bc + 1) * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->out), Bc * H * 4);
+  if (m->cfg.rope && m->cfg.head_dim == 64 && m->dev->gemm_pairs > 0)
+    rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->row_pos), R * 4);
   if (rc) {
     free_workspace(m);
     return rc;
@@ -1072,6 +1082,14 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
                             st)))
     return rc;
   const int up_epi = c.activation == NEBW_ACT_GELU_ERF ? nebw::kEpiBf16Erf : nebw::kEpiBf16Gelu8;
+  // rotary in the QKV epilogue when the model's workspace holds the row
+  // positions (the static-scratch view does not: it takes the separate pass)
+  const bool rope_fused = c.rope && m->row_pos != nullptr;
+  if (rope_fused) {
+    const dim3 pg((S + 255) / 256, B);
+    nebw::row_pos_kernel<<<pg, 256, 0, st>>>(m->off, m->len, m->row_pos);
+    NEBW_CUDA(cudaGetLastError());
+  }
   for (int L = 0; L < c.num_layers; ++L) {
     const LayerW &w = m->layers[L];
     GemmArgs a{};
@@ -1085,10 +1103,22 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
     a.resid = nullptr;
     a.out = m->qkv;
     if ((rc = prof_mark(m, NEBW_K_GEMM_QKV, st))) return rc;
-    if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv, nebw::kEpiBf16, a, st))) return rc;
-    // attention (rotary positions on Q and K first, timed with it)
+    if (rope_fused) {  // rotary positions applied in the epilogue
+      a.row_pos = m->row_pos;
+      a.rope_cos = m->rope_cos;
+      a.rope_sin = m->rope_sin;
+      a.rope_rows = c.max_seq_len;
+      a.rope_cols = static_cast<int>(2 * H);
+    }
+    if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv,
+                          rope_fused ? nebw::kEpiBf16Rope : nebw::kEpiBf16, a, st)))
+      return rc;
+    a.row_pos = nullptr;
+    a.rope_cos = a.rope_sin = nullptr;
+    a.rope_rows = a.rope_cols = 0;
+    // attention (rotary positions on Q and K first when not fused, timed with it)
     if ((rc = prof_mark(m, NEBW_K_ATTENTION, st))) return rc;
-    if (c.rope && (rc = launch_rope(m, B, S, st))) return rc;
+    if (c.rope && !rope_fused && (rc = launch_rope(m, B, S, st))) return rc;
     if (tc_attention)
       rc = launch_attention_tc(d, m->map_qkv_att, m->map_kv_att, m->off, m->len, m->att_items + 1, m->att_items, B, S,
                                c.num_heads, m->ctx, st);
@@ -1529,9 +1559,11 @@ extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   const int S = seq > 0 ? seq : m->cfg.max_seq_len;
   const bool tc =
       m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD;
-  const int per_layer = 6 + attention_launches(tc ? 64 : 0, S) + (m->cfg.rope ? 1 : 0) +
+  const bool rope_fused = m->cfg.rope && m->cfg.head_dim == 64 && m->dev->gemm_pairs > 0;
+  const int per_layer = 6 + attention_launches(tc ? 64 : 0, S) +
+                        (m->cfg.rope && !rope_fused ? 1 : 0) +
                         (m->cfg.gated_ffn && !m->glu_fused ? 1 : 0);
-  return 3 + (tc ? 1 : 0) + m->cfg.num_layers * per_layer;
+  return 3 + (tc ? 1 : 0) + (rope_fused ? 1 : 0) + m->cfg.num_layers * per_layer;
 }
 
 extern "C" int nebw_model_profile(nebw_model *m, int enable) {
