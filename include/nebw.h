@@ -126,7 +126,9 @@ int nebw_layernorm(nebw_dev *dev, float *x, const void *y, int y_dtype, const fl
 /* Fused masked attention over packed sequences.  Replaces qk / softmax_cpu /
  * av and attention_npu (bert_encoder.cpp:481-530, :995-1181).
  *   qkv_bf16 [rows, 3H] device (Q|K|V per row, Q pre-scaled by 1/sqrt(d));
- *   rows = the buffer's row count (>= every seq_off[b] + seq_len[b])
+ *   rows = the buffer's row count (>= every seq_off[b] + seq_len[b]); the
+ *   rows past a sequence up to its next 16-row boundary (and below rows)
+ *   must hold finite values: head_dim 64 multiplies them by exactly zero
  *   seq_off [B+1], seq_len [B] int32 device: sequence b owns packed rows
  *   [seq_off[b], seq_off[b] + seq_len[b])
  *   ctx_bf16 [rows, H] device.  head_dim in {32, 64}; max_len bounds

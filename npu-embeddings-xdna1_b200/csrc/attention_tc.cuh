@@ -495,11 +495,43 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
 // The attention work list: one item per (sequence, 128-query tile), longest
 // length class first (L > 256, then > 128, then the rest) so that the
 // heaviest items start first and the tail of the persistent loop is short
-// work; items[k] = (b << 8) | qt, count[0] = the number of items.
-// One CTA, B <= 65535, L <= 32767.
+// work; items[k] = (b << 8) | qt, count[0] = the number of items.  Built by
+// block 0; B <= 65535, L <= 32767.
+//
+// Blocks past the first (when T_dev is set) zero the rows [T, min(rows,
+// T256 + kAttnTcKeys)) of the Q|K|V buffer and of the QKV GEMM's A operand,
+// T = *T_dev the packed row count and T256 = T rounded up to the CTA-pair
+// GEMM's 256 rows.  The last sequence's partial 16-key group multiplies V
+// rows past T by P = 0, which contributes 0 only if those rows are finite,
+// and the QKV GEMM computes the rows [T, T256) from the A rows there; the
+// buffers can hold any bits past T (another model's or a larger batch's
+// leftovers).  Nothing else in a pass writes A past T and the GEMM writes
+// finite rows from zero ones, so one clear per pass keeps them finite.
+constexpr int kAttnTailBlocks = 16;
+
 __global__ void __launch_bounds__(1024)
     attn_work_kernel(const int *__restrict__ seq_len, int B, int *__restrict__ items,
-                     int *__restrict__ count) {
+                     int *__restrict__ count, const int *__restrict__ T_dev, int64_t rows,
+                     __nv_bfloat16 *__restrict__ qkv, int qkv_cols, __nv_bfloat16 *__restrict__ a,
+                     int a_cols) {
+  if (blockIdx.x > 0) {
+    if (!T_dev) return;
+    const int64_t T = __ldg(T_dev);
+    const int64_t end = min(rows, ((T + 255) & ~int64_t{255}) + kAttnTcKeys);
+    if (T >= end) return;
+    const int64_t q8 = qkv_cols / 8, a8 = a_cols / 8, per_row = q8 + a8;
+    const int64_t n = (end - T) * per_row;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x - 1) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x - 1) * blockDim.x) {
+      const int64_t r = T + i / per_row, c = i % per_row;
+      if (c < q8)
+        reinterpret_cast<uint4 *>(qkv + r * qkv_cols)[c] = z;
+      else
+        reinterpret_cast<uint4 *>(a + r * a_cols)[c - q8] = z;
+    }
+    return;
+  }
   __shared__ int cnt[3], start[3];
   if (threadIdx.x < 3) cnt[threadIdx.x] = 0;
   __syncthreads();

@@ -978,9 +978,12 @@ int model_ready(const nebw_model *m) {
 // inv_freq[j] in double, cos and sin rounded to fp32, the same value in
 // columns j and j + head_dim/2; inv_freq from the container's data or
 // theta^(-2j / head_dim) (gemma_rope_tables, gemma_kernels.cpp:114-136).
-// A rotary model without a position table gets a zero one (the reference's
-// containers carry a zero placeholder that its embedding adds).
-int prepare_rope(nebw_model *m) {
+// A rotary model gets a zero position table at creation (the reference's
+// containers carry a zero placeholder that its embedding adds; a staged
+// table overwrites it).  Built when the model is created (theta known) or
+// its frequency set is given, never during a pass -- the static-scratch
+// entry point allocates nothing.
+int build_rope(nebw_model *m) {
   const nebw_config &c = m->cfg;
   if (!c.rope) return NEBW_OK;
   const int64_t H = c.hidden, S = c.max_seq_len, hd = c.head_dim, half = hd / 2;
@@ -989,11 +992,11 @@ int prepare_rope(nebw_model *m) {
     NEBW_CUDA(cudaMemset(m->pos, 0, S * H * 4));
   }
   if (m->rope_cos) return NEBW_OK;
+  if (m->rope_freq.empty() && !(c.rope_theta > 0.0)) return NEBW_OK;  // set later
   std::vector<double> inv(static_cast<size_t>(half));
   if (!m->rope_freq.empty()) {
     inv = m->rope_freq;
   } else {
-    NEBW_REQUIRE(c.rope_theta > 0.0, "rotary model without rope_theta or a frequency set");
     for (int64_t j = 0; j < half; ++j)
       inv[static_cast<size_t>(j)] =
           1.0 / std::pow(c.rope_theta, 2.0 * static_cast<double>(j) / static_cast<double>(hd));
@@ -1013,6 +1016,15 @@ int prepare_rope(nebw_model *m) {
   NEBW_CUDA(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
   m->rope_cos = dc;
   m->rope_sin = ds;
+  return NEBW_OK;
+}
+
+// A pass over a rotary model needs its tables (built at creation or by
+// nebw_model_set_rope_freq).
+int rope_ready(const nebw_model *m) {
+  NEBW_REQUIRE(!m->cfg.rope || (m->rope_cos && m->pos),
+               "rotary model without its frequency set: give rope_theta at creation or call "
+               "nebw_model_set_rope_freq");
   return NEBW_OK;
 }
 
@@ -1062,7 +1074,7 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
   NEBW_REQUIRE(S > 0 && S <= c.max_seq_len, "seq %d refused: 1..max_seq_len (%d)", S,
                c.max_seq_len);
-  if (int rc = prepare_rope(m)) return rc;
+  if (int rc = rope_ready(m)) return rc;
   if (int rc = ensure_workspace(m, B, S)) return rc;
   const int64_t H = c.hidden, F = c.intermediate;
   const int rows = static_cast<int>(static_cast<int64_t>(B) * S);
@@ -1073,7 +1085,12 @@ int encode_device(nebw_model *m, const int *ids, const int *len_in, int B, int S
   const bool tc_attention =
       d->attn_kind == NEBW_ATTN_TCGEN05 && c.head_dim == nebw::kAttnTcD;
   if (tc_attention) {
-    nebw::attn_work_kernel<<<1, 1024, 0, st>>>(m->len, B, m->att_items + 1, m->att_items);
+    // with the work list, zero the Q|K|V and A rows just past the packed
+    // rows, up to the workspace's extent (the attention's last partial key
+    // group reads V there)
+    nebw::attn_work_kernel<<<1 + nebw::kAttnTailBlocks, 1024, 0, st>>>(
+        m->len, B, m->att_items + 1, m->att_items, T_dev, m->rows_cap, m->qkv,
+        static_cast<int>(3 * H), m->a, static_cast<int>(H));
     NEBW_CUDA(cudaGetLastError());
   }
   if ((rc = prof_mark(m, NEBW_K_EMBED_LN, st))) return rc;
@@ -1200,6 +1217,11 @@ extern "C" int nebw_model_create(nebw_dev *d, const nebw_config *cfg, nebw_model
   m->cfg = c;
   m->glu_fused = c.gated_ffn && d->gemm_pairs > 0;
   m->layers.resize(c.num_layers);
+  if (int rc = build_rope(m.get())) {
+    const std::string msg = g_last_error;
+    nebw_model_destroy(m.release());
+    return set_error(rc, "%s", msg.c_str());
+  }
   *out = m.release();
   return NEBW_OK;
 }
@@ -1369,8 +1391,8 @@ extern "C" int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, i
   m->rope_freq.assign(inv_freq, inv_freq + n);
   cudaFree(m->rope_cos);
   cudaFree(m->rope_sin);
-  m->rope_cos = m->rope_sin = nullptr;  // rebuilt on the next pass
-  return NEBW_OK;
+  m->rope_cos = m->rope_sin = nullptr;
+  return build_rope(m);
 }
 
 extern "C" int nebw_model_get_config(const nebw_model *m, nebw_config *cfg) {
@@ -1666,7 +1688,7 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   NEBW_REQUIRE(B > 0 && B <= 65535, "batch %d refused: 1..65535", B);
   NEBW_REQUIRE(S > 0 && S <= m->cfg.max_seq_len, "seq %d refused: 1..max_seq_len (%d)", S,
                m->cfg.max_seq_len);
-  if (int rc = prepare_rope(m)) return rc;
+  if (int rc = rope_ready(m)) return rc;
   const int64_t rows = static_cast<int64_t>(B) * S;
   const size_t need = static_scratch_need(m->cfg, rows, B);
   NEBW_REQUIRE(need <= kStaticScratchBytes,

@@ -239,7 +239,11 @@ int vit_encode_device(nebw_vit *m, const float *images, int n, float *out, cudaS
     nebw::uniform_seqs_kernel<<<(n + 1 + 255) / 256, 256, 0, st>>>(n, m->n_pos, m->len, m->off);
     NEBW_CUDA(cudaGetLastError());
     if (tc) {
-      nebw::attn_work_kernel<<<1, 1024, 0, st>>>(m->len, n, m->att_items + 1, m->att_items);
+      // with the work list, zero the Q|K|V and A rows just past this batch's
+      // rows (inside the workspace's maps when an earlier batch was larger)
+      nebw::attn_work_kernel<<<1 + nebw::kAttnTailBlocks, 1024, 0, st>>>(
+          m->len, n, m->att_items + 1, m->att_items, m->off + n, m->img_cap * m->n_pos, m->qkv,
+          static_cast<int>(3 * H), m->a, static_cast<int>(H));
       NEBW_CUDA(cudaGetLastError());
     }
   }

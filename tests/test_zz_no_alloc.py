@@ -80,3 +80,47 @@ def test_static_entry_refuses_oversized_batch(device):
         _call(nebw.lib().nebw_encode_device_static, model.h, ids_d.data_ptr(), lens_d.data_ptr(),
               B, S, out.data_ptr(), None)
     model.close()
+
+
+@pytest.mark.parametrize("key", ["nomic-base", "gte-base"])
+def test_static_entry_rotary_models(device, key):
+    """The rotary / gated families through the static entry point: their
+    rotary tables are built when the model is created (or its frequency set
+    is given), so the pass itself still allocates nothing; two calls in a
+    row against the allocating entry point."""
+    import torch
+
+    import nebw
+    from nebw import synth
+
+    w = synth.config_weights(synth.CONFIGS[key], layers=2)
+    lens = np.array([64, 1, 33, 63, 17, 40], np.int32)
+    S = 64
+    ids, _mask = synth.make_tokens(len(lens), S, lens, seed=47)
+    B = len(lens)
+    model = nebw.Model.from_weights(device, w, max_seq_len=S)
+    try:
+        lib = nebw.lib()
+        stream = C.c_void_p(nebw._stream(torch.cuda.current_stream()))
+        ids_d = torch.from_numpy(ids).cuda()
+        lens_d = torch.from_numpy(lens).cuda()
+        want = torch.empty((B, w.hidden), dtype=torch.float32, device="cuda")
+        _call(lib.nebw_encode_device, model.h, ids_d.data_ptr(), lens_d.data_ptr(), B, S,
+              want.data_ptr(), stream)
+        device.sync()
+        want_h = want.cpu().numpy()
+        assert np.isfinite(want_h).all()
+        # the scratch holds the earlier tests' leftovers (another layout): the
+        # rows past the packed ones must not reach the output
+        for _ in range(2):
+            got = torch.full((B, w.hidden), float("nan"), dtype=torch.float32, device="cuda")
+            _call(lib.nebw_encode_device_static, model.h, ids_d.data_ptr(), lens_d.data_ptr(),
+                  B, S, got.data_ptr(), stream)
+            device.sync()
+            got_h = got.cpu().numpy()
+            assert np.isfinite(got_h).all()
+            cos = (got_h * want_h).sum(1) / (
+                np.linalg.norm(got_h, axis=1) * np.linalg.norm(want_h, axis=1))
+            assert cos.min() >= 0.9999 and np.abs(got_h - want_h).max() <= 2e-3
+    finally:
+        model.close()
