@@ -223,8 +223,17 @@ int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, int32_t n);
  * "tma_bf16" (bf16 [N,K] operands, nebw.pack).  Architectures
  * bert_abs_gelu_postln, nomic_bert_rope_swiglu and gte_new_rope_geglu, with
  * set_model_shape's refusals for the latter two (position encoding, gating,
- * the order of the fused FFN-up halves, the gate's activation). */
+ * the order of the fused FFN-up halves, the gate's activation).  A tma_bf16
+ * GEMM operand whose layout_hash is not nebw_tma_layout_hash() is refused,
+ * as the reference refuses a design whose b_layout_hash differs from the
+ * model's (runtime/src/runtime.cpp:190-222).  The container is checked before
+ * the device is used, so refusals need no GPU. */
 int nebw_model_load_npue(nebw_dev *dev, const char *path, nebw_model **out);
+/* The layout hash this library reads tma_bf16 GEMM operands in: sha256 (hex)
+ * of the canonical JSON {"dtype":"BF16","kind":"dense","order":"n,k"}
+ * (tools/lib/npue.py:777-785's scheme).  No reference counterpart as a
+ * function: the reference reads it from a design's design.json. */
+const char *nebw_tma_layout_hash(void);
 int nebw_model_destroy(nebw_model *m);
 int nebw_model_get_config(const nebw_model *m, nebw_config *cfg);
 

@@ -1401,8 +1401,20 @@ extern "C" int nebw_model_get_config(const nebw_model *m, nebw_config *cfg) {
   return NEBW_OK;
 }
 
+namespace {
+// The layout this library reads a tma_bf16 container's GEMM operands in:
+// sha256 of the canonical descriptor {"dtype":"BF16","kind":"dense",
+// "order":"n,k"} (dense row-major [N, K] bf16; TMA applies the swizzle as it
+// loads).  The packer writes the same hash beside each operand.
+constexpr char kTmaLayoutHash[] =
+    "11a82b85f370c9a7fa302e55afdde7415734be70c40e25d543c57a860f15ae3a";
+}  // namespace
+
+extern "C" const char *nebw_tma_layout_hash(void) { return kTmaLayoutHash; }
+
+// The container is read and checked before the device is touched (the model
+// is created last), so a refused container is refused on any host.
 extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **out) {
-  if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(path && out, "null argument");
   *out = nullptr;
   try {
@@ -1503,6 +1515,23 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
         return set_error(NEBW_EINVAL, "unknown gated-FFN activation '%s' (silu or gelu)",
                          act.c_str());
     }
+    std::vector<std::string> names = required_names(c);
+    // a tma_bf16 operand laid out for another reader is refused by its
+    // layout hash, as the reference's runtime refuses a design whose
+    // b_layout_hash differs from the model's (runtime/src/runtime.cpp:190-222)
+    if (nk_layout)
+      for (const auto &n : names) {
+        const auto &t = f.tensor(n);
+        if (!(t.shape.size() == 2 && n.rfind("layer.", 0) == 0)) continue;
+        if (t.layout_hash != kTmaLayoutHash)
+          return set_error(NEBW_EINVAL,
+                           "tma_bf16 container: GEMM operand '%s' has layout_hash %s; this "
+                           "library reads %.16s... (dense [N, K] BF16): repack it with nebw.pack",
+                           n.c_str(),
+                           t.layout_hash.empty() ? "(none)"
+                                                 : ("'" + t.layout_hash.substr(0, 16) + "...'").c_str(),
+                           kTmaLayoutHash);
+      }
     nebw_model *m = nullptr;
     if (int rc = nebw_model_create(d, &c, &m)) return rc;
     if (!inv_freq.empty()) {
@@ -1513,7 +1542,6 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
         return set_error(rc, "%s", msg.c_str());
       }
     }
-    std::vector<std::string> names = required_names(c);
     // a rotary container's zero position placeholder is staged as the
     // reference's embedding adds it (absent, a zero table is used)
     if (c.rope && f.has("embeddings.position")) names.push_back("embeddings.position");

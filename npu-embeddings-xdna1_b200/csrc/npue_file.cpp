@@ -228,6 +228,12 @@ NpueFile::NpueFile(const std::string &path) : path_(path) {
       t.name = n->str;
       t.role = r ? r->str : "";
       t.dtype = d->str;
+      const Json *lh = e.find("layout_hash");
+      if (lh) {
+        if (lh->kind != Json::String)
+          throw std::runtime_error(path + ": tensor " + t.name + " has a non-string layout_hash");
+        t.layout_hash = lh->str;
+      }
       for (const Json &x : sh->arr) t.shape.push_back(static_cast<int64_t>(x.num));
       t.offset = static_cast<uint64_t>(o->num);
       t.nbytes = static_cast<uint64_t>(nb->num);

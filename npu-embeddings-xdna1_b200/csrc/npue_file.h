@@ -34,6 +34,7 @@ struct Json {
 
 struct NpueTensor {
   std::string name, role, dtype;
+  std::string layout_hash;  // sha256 of the layout descriptor; empty when the entry has none
   std::vector<int64_t> shape;
   uint64_t offset = 0, nbytes = 0;
   const uint8_t *data = nullptr;

@@ -20,6 +20,7 @@ this writer produces byte-identical files to the reference writer.
 
 from __future__ import annotations
 
+import hashlib
 import json
 import mmap
 import struct
@@ -47,6 +48,24 @@ DTYPES = {
 }
 
 
+def tma_b_layout() -> dict:
+    """The byte layout of a tma_bf16 container's GEMM operands: dense
+    row-major [N, K] bf16, each output column's K weights contiguous -- the
+    B operand the library's tcgen05 GEMM tiles with TMA as it loads (the
+    swizzle is applied by the load, not stored).  Built here only, so that the
+    packer and the tests describe it with one dict."""
+    return {"kind": "dense", "order": "n,k", "dtype": "BF16"}
+
+
+def layout_hash(layout: dict) -> str:
+    """sha256 of the descriptor's canonical JSON (sorted keys, no spaces),
+    the scheme of the reference's `layout_hash` (tools/lib/npue.py:777-785):
+    the loader compares one string and refuses a mismatch rather than read
+    bytes laid out for another kernel."""
+    canonical = json.dumps(layout, sort_keys=True, separators=(",", ":"))
+    return hashlib.sha256(canonical.encode("utf-8")).hexdigest()
+
+
 def _pad(n: int) -> int:
     return (-n) % ALIGN
 
@@ -62,7 +81,7 @@ class ContainerWriter:
         self._arrays: list[np.ndarray] = []
         self._cursor = 0
 
-    def add(self, name: str, array, dtype: str, role: str, shape) -> dict:
+    def add(self, name: str, array, dtype: str, role: str, shape, layout: dict | None = None) -> dict:
         arr = np.ascontiguousarray(array, dtype=DTYPES[dtype])
         nbytes = arr.nbytes
         entry = {
@@ -74,6 +93,9 @@ class ContainerWriter:
             "offset": self._cursor,
             "nbytes": nbytes,
         }
+        if layout is not None:  # a laid-out operand carries its descriptor and hash
+            entry["layout"] = dict(layout)
+            entry["layout_hash"] = layout_hash(layout)
         self._entries.append(entry)
         self._arrays.append(arr)
         self._cursor += nbytes + _pad(nbytes)

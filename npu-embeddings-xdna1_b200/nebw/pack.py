@@ -40,7 +40,7 @@ from pathlib import Path
 
 import numpy as np
 
-from .npue import ContainerWriter
+from .npue import ContainerWriter, tma_b_layout
 
 SAFETENSORS_DTYPES = {"F32": np.dtype("<f4"), "F16": np.dtype("<f2"), "BF16": np.dtype("<u2"),
                       "F64": np.dtype("<f8")}
@@ -167,7 +167,8 @@ def pack_bert(model_dir, out, layout: str = "tma_bf16", max_seq: int | None = No
         if host:
             w.add(name, kn.reshape(-1), "F32", "gemm_b_host", [K, N])
         else:
-            w.add(name, to_bf16_bits(kn.T).reshape(-1), "BF16", "gemm_b_tma", [N, K])
+            w.add(name, to_bf16_bits(kn.T).reshape(-1), "BF16", "gemm_b_tma", [N, K],
+                  layout=tma_b_layout())
 
     w.add("embeddings.word", src["embeddings.word_embeddings.weight"], "F32", "embedding",
           [cfg["vocab_size"], hidden])
