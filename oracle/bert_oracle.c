@@ -499,6 +499,97 @@ int nebw_oracle_encode(const nebw_oracle_model *m, const int32_t *ids,
 
 /* im2col_patches (image.cpp:732-755): patch row p*n + q, column
  * (c*P + i)*P + j  <-  chw[(c*S + p*P + i)*S + q*P + j]. */
+/* ---- int8 datapath: the array path of a --dtype i8 container --------------
+ * Each GEMM input is quantised per row to int8 with the SmoothQuant divisor
+ * folded in, the array multiplies int8 x int8 into int32, and the host
+ * dequantises C with the row scale, the column scale and the bias.  The int32
+ * product is exact, so these steps pin bit-exactly.  Only an int32 C (the
+ * designs' c_elem_bytes 4) is restated, and N % 8 == 0 (every BERT width),
+ * the widths on which the reference's AVX2 bodies cover whole rows. */
+
+/* app::quantise_a_int8 (host_kernels.hpp:263-315), one row:
+ *   mx = max_j |x_j * ias_j|, sc = mx > 0 ? mx / 127 : 1,
+ *   q_j = rne(clamp((x_j * ias_j) * (1 / sc), -127, 127)). */
+static void quant_row(const float *x, int64_t K, const float *ias, int8_t *q, float *scale) {
+  float mx = 0.0f;
+  for (int64_t j = 0; j < K; ++j) {
+    const float a = fabsf(x[j] * ias[j]);
+    if (a > mx) mx = a;
+  }
+  const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+  *scale = sc;
+  const float inv = 1.0f / sc;
+  for (int64_t j = 0; j < K; ++j) {
+    const float t = fminf(fmaxf((x[j] * ias[j]) * inv, -127.0f), 127.0f);
+    q[j] = (int8_t)nearbyintf(t);
+  }
+}
+
+void nebw_oracle_quantise_rows(const float *a, int64_t rows, int64_t K, const float *ias,
+                               int8_t *q, float *scale) {
+  for (int64_t r = 0; r < rows; ++r) quant_row(a + r * K, K, ias, q + r * K, scale + r);
+}
+
+typedef struct {
+  const int8_t *A, *B;
+  int32_t *C;
+  int64_t K, N;
+} gemm_i8_ctx;
+
+static void gemm_i8_rows(void *p, int64_t lo, int64_t hi) {
+  const gemm_i8_ctx *c = (const gemm_i8_ctx *)p;
+  for (int64_t m = lo; m < hi; ++m) {
+    int32_t *row = c->C + m * c->N;
+    for (int64_t n = 0; n < c->N; ++n) row[n] = 0;
+    for (int64_t k = 0; k < c->K; ++k) {
+      const int32_t a = c->A[m * c->K + k];
+      const int8_t *b = c->B + k * c->N;
+      for (int64_t n = 0; n < c->N; ++n) row[n] += a * (int32_t)b[n];
+    }
+  }
+}
+
+/* The array's int8 GEMM: C[M, N] = A[M, K] . B[K, N] in int32 (exact). */
+void nebw_oracle_gemm_i8(const int8_t *A, int64_t M, const int8_t *B, int64_t K, int64_t N,
+                         int32_t *C, int32_t threads) {
+  gemm_i8_ctx c = {A, B, C, K, N};
+  parallel_for(M, threads, gemm_i8_rows, &c);
+}
+
+/* app::dequantise_c, int32 C (host_kernels.hpp:575-613): y = fma(float(c) *
+ * sa[row], ws[col], bias[col]) -- the float conversion rounds to nearest even,
+ * the product rounds, the multiply-add rounds once. */
+static inline float dequant_one(int32_t c, float sa, float ws, float b) {
+  return fmaf((float)c * sa, ws, b);
+}
+
+int nebw_oracle_dequantise(const int32_t *C, int64_t rows, int64_t N, const float *sa,
+                           const float *ws, const float *bias, float *out) {
+  if (N % 8) return fail("dequantise: N must be a multiple of 8");
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t j = 0; j < N; ++j)
+      out[r * N + j] = dequant_one(C[r * N + j], sa[r], ws[j], bias[j]);
+  return 0;
+}
+
+/* app::dequant_act_quant with the BERT FFN's GELU (host_kernels.hpp:404-526;
+ * the act of bert_encoder.cpp:821-829): per row, dequantise as above, gelu8,
+ * then quantise for the next GEMM with its divisor ias_next. */
+int nebw_oracle_dequant_gelu_quant(const int32_t *C, int64_t rows, int64_t N, const float *sa,
+                                   const float *ws, const float *bias, const float *ias_next,
+                                   int8_t *q, float *sa_next) {
+  if (N % 8) return fail("dequant_gelu_quant: N must be a multiple of 8");
+  float *v = (float *)malloc((size_t)N * sizeof(float));
+  if (!v) return fail("dequant_gelu_quant: out of memory");
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t j = 0; j < N; ++j)
+      v[j] = gelu8_ref(dequant_one(C[r * N + j], sa[r], ws[j], bias[j]));
+    quant_row(v, N, ias_next, q + r * N, sa_next + r);
+  }
+  free(v);
+  return 0;
+}
+
 void nebw_oracle_vit_im2col(const float *chw, int32_t channels, int32_t image,
                             int32_t patch, float *out) {
   const int64_t n = image / patch, pd = (int64_t)channels * patch * patch;

@@ -73,6 +73,21 @@ int nebw_oracle_pool_rows(const float *h, const float *am, int64_t take,
                           float *out);
 const char *nebw_oracle_last_error(void);
 
+/* The int8 datapath of a --dtype i8 container (the array's quantised
+ * operands): per-row quantisation with the SmoothQuant divisor (ias =
+ * 1/asmooth), the exact int32 GEMM, dequantisation, and the FFN-up epilogue
+ * that dequantises, applies gelu8 and quantises for FFN-down.  int32 C only;
+ * N % 8 == 0. */
+void nebw_oracle_quantise_rows(const float *a, int64_t rows, int64_t K, const float *ias,
+                               int8_t *q, float *scale);
+void nebw_oracle_gemm_i8(const int8_t *A, int64_t M, const int8_t *B, int64_t K, int64_t N,
+                         int32_t *C, int32_t threads);
+int nebw_oracle_dequantise(const int32_t *C, int64_t rows, int64_t N, const float *sa,
+                           const float *ws, const float *bias, float *out);
+int nebw_oracle_dequant_gelu_quant(const int32_t *C, int64_t rows, int64_t N, const float *sa,
+                                   const float *ws, const float *bias, const float *ias_next,
+                                   int8_t *q, float *sa_next);
+
 /* ViT (arch vit_patch16_prenorm_gelu): pre-LN encoder over image patches. */
 typedef struct nebw_oracle_vit {
   int32_t layers, hidden, heads, head_dim, ffn;

@@ -76,14 +76,77 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-class PortOracle:
+_i8p = C.POINTER(C.c_int8)
+
+
+class _Int8Steps:
+    """The int8 datapath's host steps, bound by symbol name: the port's
+    restatement and the reference's own templates share one signature
+    (quantise, dequantise, dequantise + gelu8 + quantise)."""
+
+    _quantise = _dequantise = _dequant_gelu_quant = ""
+
+    def _bind_int8(self):
+        L = self.lib
+        q = getattr(L, self._quantise)
+        q.argtypes = [_f32p, C.c_int64, C.c_int64, _f32p, _i8p, _f32p]
+        d = getattr(L, self._dequantise)
+        d.argtypes = [_i32p, C.c_int64, C.c_int64, _f32p, _f32p, _f32p, _f32p]
+        d.restype = C.c_int
+        g = getattr(L, self._dequant_gelu_quant)
+        g.argtypes = [_i32p, C.c_int64, C.c_int64, _f32p, _f32p, _f32p, _f32p, _i8p, _f32p]
+        g.restype = C.c_int
+
+    def quantise_rows(self, a, ias):
+        a = np.ascontiguousarray(a, np.float32)
+        ias = np.ascontiguousarray(ias, np.float32)
+        rows, K = a.shape
+        q = np.zeros((rows, K), np.int8)
+        sc = np.zeros(rows, np.float32)
+        getattr(self.lib, self._quantise)(_ptr(a), rows, K, _ptr(ias), _ptr(q, _i8p), _ptr(sc))
+        return q, sc
+
+    def dequantise(self, c, sa, ws, bias):
+        c = np.ascontiguousarray(c, np.int32)
+        sa, ws, bias = (np.ascontiguousarray(v, np.float32) for v in (sa, ws, bias))
+        rows, N = c.shape
+        out = np.zeros((rows, N), np.float32)
+        rc = getattr(self.lib, self._dequantise)(_ptr(c, _i32p), rows, N, _ptr(sa), _ptr(ws),
+                                                  _ptr(bias), _ptr(out))
+        if rc:
+            raise RuntimeError(f"{self._dequantise} failed ({rc})")
+        return out
+
+    def dequant_gelu_quant(self, c, sa, ws, bias, ias_next):
+        c = np.ascontiguousarray(c, np.int32)
+        sa, ws, bias, ias_next = (np.ascontiguousarray(v, np.float32)
+                                  for v in (sa, ws, bias, ias_next))
+        rows, N = c.shape
+        q = np.zeros((rows, N), np.int8)
+        sn = np.zeros(rows, np.float32)
+        rc = getattr(self.lib, self._dequant_gelu_quant)(
+            _ptr(c, _i32p), rows, N, _ptr(sa), _ptr(ws), _ptr(bias), _ptr(ias_next),
+            _ptr(q, _i8p), _ptr(sn))
+        if rc:
+            raise RuntimeError(f"{self._dequant_gelu_quant} failed ({rc})")
+        return q, sn
+
+
+class PortOracle(_Int8Steps):
     """The C restatement, fed from in-memory weights."""
+
+    _quantise = "nebw_oracle_quantise_rows"
+    _dequantise = "nebw_oracle_dequantise"
+    _dequant_gelu_quant = "nebw_oracle_dequant_gelu_quant"
 
     def __init__(self, lib_path: Path = PORT_LIB):
         if not Path(lib_path).exists():
             raise FileNotFoundError(f"{lib_path} is not built (make -C oracle port)")
         self.lib = C.CDLL(str(lib_path))
         L = self.lib
+        self._bind_int8()
+        L.nebw_oracle_gemm_i8.argtypes = [_i8p, C.c_int64, _i8p, C.c_int64, C.c_int64, _i32p,
+                                          C.c_int32]
         L.nebw_oracle_encode.argtypes = [C.POINTER(_Model), _i32p, _i32p, C.c_int32, C.c_int32,
                                          C.c_int32, _f32p, _f32p]
         L.nebw_oracle_encode.restype = C.c_int
@@ -189,6 +252,17 @@ class PortOracle:
         self.lib.nebw_oracle_gemm_nt(_ptr(A), M, _ptr(B), K, N, _ptr(bias), _ptr(Cm), threads)
         return Cm
 
+    def gemm_i8(self, A, B, threads=1):
+        """int8 [M, K] . int8 [K, N] -> int32 [M, N], exact."""
+        A = np.ascontiguousarray(A, np.int8)
+        B = np.ascontiguousarray(B, np.int8)
+        M, K = A.shape
+        N = B.shape[1]
+        Cm = np.zeros((M, N), np.int32)
+        self.lib.nebw_oracle_gemm_i8(_ptr(A, _i8p), M, _ptr(B, _i8p), K, N, _ptr(Cm, _i32p),
+                                     threads)
+        return Cm
+
     def gelu8(self, x):
         y = np.array(x, np.float32, copy=True)
         self.lib.nebw_oracle_gelu8(_ptr(y), y.size)
@@ -225,14 +299,19 @@ class PortOracle:
         return out
 
 
-class RefOracle:
+class RefOracle(_Int8Steps):
     """The reference's own host path, compiled from its tree."""
+
+    _quantise = "nebw_ref_quantise_a_int8"
+    _dequantise = "nebw_ref_dequantise_c"
+    _dequant_gelu_quant = "nebw_ref_dequant_gelu_quant"
 
     def __init__(self, lib_path: Path = REF_LIB):
         if not Path(lib_path).exists():
             raise FileNotFoundError(f"{lib_path} is not built (make -C oracle ref)")
         self.lib = C.CDLL(str(lib_path))
         L = self.lib
+        self._bind_int8()
         L.nebw_ref_encode.argtypes = [C.c_char_p, C.c_int32, _i32p, _i32p, C.c_int32, C.c_int32,
                                       _f32p, _f32p, C.c_char_p, C.c_int32]
         L.nebw_ref_encode.restype = C.c_int

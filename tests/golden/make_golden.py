@@ -28,6 +28,11 @@ shortest and longest rows are always included):
                      (runtime/src/vit/encoder.cpp) via oracle/ref_vit_driver.cpp.
                      The images are regenerated from the recorded seed (their
                      SHA-256 is stored), not stored.
+  int8_steps.npz     the int8 datapath's host steps (host_kernels.hpp:
+                     quantise_a_int8, dequantise_c with an int32 C,
+                     dequant_act_quant with gelu8) on int8_step_inputs(), via
+                     oracle/ref_i8_driver.cpp; the inputs are regenerated
+                     (their SHA-256 is stored), the outputs stored.
 
     python tests/golden/make_golden.py vit_base_c5     (one fixture)
 """
@@ -83,6 +88,67 @@ def sample_rows(lens, n):
 VIT_FIXTURES = {"vit_base_c5": ("vit-base", 3)}
 
 
+INT8_SEED = 20261401
+
+
+def int8_step_inputs(seed: int = INT8_SEED) -> dict:
+    """Seeded inputs for the int8 steps: activation rows with per-column
+    SmoothQuant divisors (an all-zero row, a row of exact rounding ties, a
+    row with one outlier), int32 accumulators from a real int8 product plus a
+    row of values large enough to round when widened to float, and the row /
+    column scales and biases of a dequantisation.  N and K are multiples of 8
+    except for the `tail` rows (K = 37), which exercise the scalar tail."""
+    rng = np.random.default_rng(seed)
+    rows, K, N = 16, 512, 512
+    a = (rng.standard_normal((rows, K)) * rng.lognormal(0.0, 1.0, K)).astype(np.float32)
+    a[0] = 0.0
+    a[1] = 0.0
+    a[1, 0] = 127.0
+    a[1, 1:9] = [0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 126.5, -126.5]
+    a[2, 7] = 4.0e3
+    ias = (1.0 / rng.lognormal(0.0, 0.5, K)).astype(np.float32)
+    ias[:9] = 1.0
+    aq = rng.integers(-127, 128, (rows, 1024), dtype=np.int8)
+    wq = rng.integers(-127, 128, (1024, N), dtype=np.int8)
+    c = (aq.astype(np.int64) @ wq.astype(np.int64)).astype(np.int32)
+    c[3] = rng.integers(-(2**31 - 1), 2**31 - 1, N, dtype=np.int64).astype(np.int32)
+    sa = (rng.lognormal(-4.0, 0.5, rows)).astype(np.float32)
+    ws = (rng.lognormal(-6.0, 0.5, N)).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    ias_next = (1.0 / rng.lognormal(0.0, 0.5, N)).astype(np.float32)
+    tail = (rng.standard_normal((5, 37)) * 3).astype(np.float32)
+    tail_ias = (1.0 / rng.lognormal(0.0, 0.5, 37)).astype(np.float32)
+    return dict(a=a, ias=ias, c=c, sa=sa, ws=ws, bias=bias, ias_next=ias_next, tail=tail,
+                tail_ias=tail_ias)
+
+
+def int8_inputs_sha256(inp: dict) -> str:
+    h = hashlib.sha256()
+    for k in sorted(inp):
+        h.update(k.encode())
+        h.update(np.ascontiguousarray(inp[k]).tobytes())
+    return h.hexdigest()
+
+
+def int8_step_outputs(o, inp: dict) -> dict:
+    """The four int8 steps of `o` (a PortOracle or RefOracle) on `inp`."""
+    q, sc = o.quantise_rows(inp["a"], inp["ias"])
+    tq, tsc = o.quantise_rows(inp["tail"], inp["tail_ias"])
+    y = o.dequantise(inp["c"], inp["sa"], inp["ws"], inp["bias"])
+    gq, gsn = o.dequant_gelu_quant(inp["c"], inp["sa"], inp["ws"], inp["bias"], inp["ias_next"])
+    return dict(q=q, scale=sc, tail_q=tq, tail_scale=tsc, dequant=y, gelu_q=gq, gelu_scale=gsn)
+
+
+def make_int8(ref):
+    inp = int8_step_inputs()
+    out = int8_step_outputs(ref, inp)
+    np.savez_compressed(
+        HERE / "int8_steps.npz", seed=np.int64(INT8_SEED), inputs_sha256=int8_inputs_sha256(inp),
+        provenance="reference host_kernels.hpp int8 steps (-O2 -march=x86-64-v3) via "
+                   "oracle/ref_i8_driver.cpp", **out)
+    print("int8_steps: written")
+
+
 def make_vit(ref, name, key, n):
     cfg = synth.VIT_CONFIGS[key]
     w = synth.vit_config_weights(cfg)
@@ -103,6 +169,8 @@ def main():
     from oracle.oracle import RefOracle
     ref = RefOracle()
     only = set(sys.argv[1:])
+    if not only or "int8_steps" in only:
+        make_int8(ref)
     for name, (key, n) in VIT_FIXTURES.items():
         if not only or name in only:
             make_vit(ref, name, key, n)

@@ -192,3 +192,67 @@ def test_port_matches_golden_gated(port_oracle, name, key):
     r = int(np.argmin(g["lens"]))
     got = port_oracle.encode(w, g["ids"][r:r + 1], g["mask"][r:r + 1])
     np.testing.assert_array_equal(got, g["embeddings"][r:r + 1])
+
+
+# ---- the int8 datapath's host steps --------------------------------------
+
+def _int8_golden_module():
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import make_golden
+    return make_golden
+
+
+def _bits_equal(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape and a.dtype == b.dtype
+    if a.dtype == np.float32:
+        a, b = a.view(np.uint32), b.view(np.uint32)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_port_int8_steps_bit_exact_vs_reference(port_oracle, ref_oracle):
+    """quantise_a_int8, dequantise_c (int32 C) and dequant_act_quant (gelu8)
+    of host_kernels.hpp, compiled from the reference tree, against the C
+    restatement: bit for bit, on seeded inputs with rounding ties, a zero
+    row, a scalar tail and int32 values that round when widened."""
+    mg = _int8_golden_module()
+    for seed in (mg.INT8_SEED, 7, 8):
+        inp = mg.int8_step_inputs(seed)
+        got = mg.int8_step_outputs(port_oracle, inp)
+        want = mg.int8_step_outputs(ref_oracle, inp)
+        for k in want:
+            _bits_equal(got[k], want[k])
+
+
+def test_port_int8_matches_golden(port_oracle):
+    mg = _int8_golden_module()
+    g = load_golden("int8_steps")
+    inp = mg.int8_step_inputs(int(g["seed"]))
+    assert mg.int8_inputs_sha256(inp) == str(g["inputs_sha256"])
+    got = mg.int8_step_outputs(port_oracle, inp)
+    for k, v in got.items():
+        _bits_equal(v, g[k])
+    # the crafted row: 127 sets the scale to 1, ties round to even
+    np.testing.assert_array_equal(got["q"][1, :9], [127, 0, 2, 2, 0, -2, -2, 126, -126])
+    assert got["scale"][0] == 1.0 and not got["q"][0].any()  # an all-zero row
+
+
+def test_port_int8_quantise_invariants(port_oracle):
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((64, 384)).astype(np.float32) * 10
+    ias = (1.0 / rng.lognormal(0.0, 0.5, 384)).astype(np.float32)
+    q, sc = port_oracle.quantise_rows(a, ias)
+    assert np.abs(q.astype(np.int32)).max() <= 127
+    assert (np.abs(q.astype(np.int32)).max(axis=1) == 127).all()
+    # each value is within half a step of its quantised value
+    assert (np.abs(q * sc[:, None] - a * ias) <= 0.5 * sc[:, None] * (1 + 1e-6)).all()
+
+
+def test_port_gemm_i8_exact(port_oracle):
+    rng = np.random.default_rng(6)
+    for M, K, N in ((7, 64, 40), (33, 1024, 96)):
+        A = rng.integers(-127, 128, (M, K), dtype=np.int8)
+        B = rng.integers(-127, 128, (K, N), dtype=np.int8)
+        want = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.int32)
+        np.testing.assert_array_equal(port_oracle.gemm_i8(A, B, threads=2), want)
