@@ -220,7 +220,9 @@ int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, int32_t n);
 /* Stage every tensor of a `.npue` container -- the reference's npue::File +
  * set_model_shape + stage_all (runtime/src/model.cpp:214-380).  gemm_layout
  * "host" (F32 [K,N] operands, the reference packer's --dtype f32) or
- * "tma_bf16" (bf16 [N,K] operands, nebw.pack).  Architectures
+ * "tma_bf16" (bf16 [N,K] operands, nebw.pack) or "pretiled_bf16" (the
+ * reference's default block panels, a_dtype bf16, or int8 panels with
+ * .wscale and .asmooth, a_dtype i8: see nebw_npue_gemm_kn).  Architectures
  * bert_abs_gelu_postln, nomic_bert_rope_swiglu and gte_new_rope_geglu, with
  * set_model_shape's refusals for the latter two (position encoding, gating,
  * the order of the fused FFN-up halves, the gate's activation).  A tma_bf16
@@ -229,6 +231,14 @@ int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, int32_t n);
  * model's (runtime/src/runtime.cpp:190-222).  The container is checked before
  * the device is used, so refusals need no GPU. */
 int nebw_model_load_npue(nebw_dev *dev, const char *path, nebw_model **out);
+/* One GEMM operand of a pre-tiled container (gemm_layout "pretiled_bf16",
+ * block_panel BF16 or I8) as fp32 row-major [K, N], I8 dequantised per
+ * column by its .wscale -- the reference's host_b_kn (runtime/include/common/
+ * host_b.hpp:74-224).  Host only: no device is used.  nebw_model_load_npue
+ * stages such operands this way, an int8 one further divided row by row by
+ * its .asmooth (the activation's SmoothQuant divisor, moved onto the
+ * weights). */
+int nebw_npue_gemm_kn(const char *path, const char *name, float *out_kn, int64_t K, int64_t N);
 /* The layout hash this library reads tma_bf16 GEMM operands in: sha256 (hex)
  * of the canonical JSON {"dtype":"BF16","kind":"dense","order":"n,k"}
  * (tools/lib/npue.py:777-785's scheme).  No reference counterpart as a

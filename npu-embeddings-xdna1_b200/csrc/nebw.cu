@@ -1412,6 +1412,93 @@ constexpr char kTmaLayoutHash[] =
 
 extern "C" const char *nebw_tma_layout_hash(void) { return kTmaLayoutHash; }
 
+namespace {
+// A block_panel GEMM operand -- the reference's pre-tiled array layout, BF16
+// or I8 -- back to fp32 row-major [K, N], I8 dequantised per column by the
+// operand's `.wscale`, as the reference's host_b_kn (runtime/include/common/
+// host_b.hpp:74-224) reads it.  The flat panel runs over the axes (kb, nb,
+// ri, ci, si, ti), ti fastest, with k = kb*tile_k + ri*mac_s + si and
+// n = nb*tile_n + ci*mac_t + ti.
+int panel_to_kn(const nebw::NpueFile &f, const std::string &name, std::vector<float> &out) {
+  const nebw::NpueTensor &t = f.tensor(name);
+  NEBW_REQUIRE(t.shape.size() == 2, "'%s' is not a 2-D GEMM operand", name.c_str());
+  const int64_t K = t.shape[0], N = t.shape[1];
+  NEBW_REQUIRE(t.padded_shape.empty() ||
+                   (t.padded_shape.size() == 2 && t.padded_shape[0] == K && t.padded_shape[1] == N),
+               "'%s': logical and padded shapes differ; repack it", name.c_str());
+  NEBW_REQUIRE(t.layout_kind == "block_panel" && t.layout_order == "k,n,kt,nt" &&
+                   t.layout_inner == "s,t",
+               "'%s': layout '%s' (order '%s', inner '%s') refused: block_panel k,n,kt,nt / s,t is "
+               "the pre-tiled layout this library reads", name.c_str(), t.layout_kind.c_str(),
+               t.layout_order.c_str(), t.layout_inner.c_str());
+  const int64_t tk = t.tile_k, tn = t.tile_n, s = t.mac_s, tt = t.mac_t;
+  NEBW_REQUIRE(tk > 0 && tn > 0 && s > 0 && tt > 0 && K % tk == 0 && N % tn == 0 && tk % s == 0 &&
+                   tn % tt == 0,
+               "'%s': [%lld, %lld] does not tile into (%lld, %lld) with mac (%lld, %lld)",
+               name.c_str(), static_cast<long long>(K), static_cast<long long>(N),
+               static_cast<long long>(tk), static_cast<long long>(tn), static_cast<long long>(s),
+               static_cast<long long>(tt));
+  const bool i8 = t.dtype == "I8";
+  NEBW_REQUIRE((i8 || t.dtype == "BF16") && t.layout_dtype == t.dtype,
+               "'%s': a %s panel described as %s; BF16 or I8 panels are read", name.c_str(),
+               t.dtype.c_str(), t.layout_dtype.c_str());
+  NEBW_REQUIRE(t.nbytes == static_cast<uint64_t>(K * N * (i8 ? 1 : 2)),
+               "'%s': %llu bytes for a [%lld, %lld] %s panel", name.c_str(),
+               static_cast<unsigned long long>(t.nbytes), static_cast<long long>(K),
+               static_cast<long long>(N), t.dtype.c_str());
+  std::vector<float> ws;
+  if (i8) {
+    const std::string wn = name + ".wscale";
+    NEBW_REQUIRE(f.has(wn), "int8 operand '%s' has no %s", name.c_str(), wn.c_str());
+    const nebw::NpueTensor &w = f.tensor(wn);
+    NEBW_REQUIRE(w.dtype == "F32" && w.nbytes == static_cast<uint64_t>(N) * 4,
+                 "%s must be F32 [%lld]", wn.c_str(), static_cast<long long>(N));
+    ws.resize(static_cast<size_t>(N));
+    std::memcpy(ws.data(), w.data, static_cast<size_t>(N) * 4);
+  }
+  out.assign(static_cast<size_t>(K * N), 0.0f);
+  const int64_t R0 = tk / s, C0 = tn / tt;
+  int64_t idx = 0;
+  for (int64_t kb = 0; kb < K / tk; ++kb)
+    for (int64_t nb = 0; nb < N / tn; ++nb)
+      for (int64_t ri = 0; ri < R0; ++ri)
+        for (int64_t ci = 0; ci < C0; ++ci)
+          for (int64_t si = 0; si < s; ++si) {
+            float *row = out.data() + (kb * tk + ri * s + si) * N + nb * tn + ci * tt;
+            for (int64_t ti = 0; ti < tt; ++ti, ++idx) {
+              if (i8) {
+                const int8_t q = reinterpret_cast<const int8_t *>(t.data)[idx];
+                row[ti] = static_cast<float>(q) * ws[static_cast<size_t>(nb * tn + ci * tt + ti)];
+              } else {
+                uint16_t h;
+                std::memcpy(&h, t.data + 2 * idx, 2);
+                const uint32_t bits = static_cast<uint32_t>(h) << 16;
+                std::memcpy(&row[ti], &bits, 4);
+              }
+            }
+          }
+  return NEBW_OK;
+}
+}  // namespace
+
+extern "C" int nebw_npue_gemm_kn(const char *path, const char *name, float *out, int64_t K,
+                                 int64_t N) {
+  NEBW_REQUIRE(path && name && out, "null argument");
+  try {
+    nebw::NpueFile f(path);
+    const nebw::NpueTensor &t = f.tensor(name);
+    NEBW_REQUIRE(t.shape.size() == 2 && t.shape[0] == K && t.shape[1] == N,
+                 "'%s' is not [%lld, %lld]", name, static_cast<long long>(K),
+                 static_cast<long long>(N));
+    std::vector<float> kn;
+    if (int rc = panel_to_kn(f, name, kn)) return rc;
+    std::memcpy(out, kn.data(), kn.size() * 4);
+    return NEBW_OK;
+  } catch (const std::exception &e) {
+    return set_error(NEBW_EIO, "%s", e.what());
+  }
+}
+
 // The container is read and checked before the device is touched (the model
 // is created last), so a refused container is refused on any host.
 extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **out) {
@@ -1428,14 +1515,21 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
                        "are implemented", arch.c_str());
     std::string layout = "pretiled_bf16";
     if (f.has_config("gemm_layout")) layout = f.config_string("gemm_layout");
-    if (layout != "host" && layout != "tma_bf16")
+    if (layout != "host" && layout != "tma_bf16" && layout != "pretiled_bf16")
       return set_error(NEBW_EINVAL,
-                       "container gemm_layout '%s' refused: this library reads the row-major "
-                       "[K, N] operands of a gemm_layout \"host\" container (re-tiling them "
-                       "itself) or the bf16 [N, K] operands of a \"tma_bf16\" container "
-                       "(nebw.pack); the array's block panels are not a B200 layout",
+                       "container gemm_layout '%s' refused: this library reads \"host\" (F32 "
+                       "[K, N]), \"tma_bf16\" (bf16 [N, K], nebw.pack) and the reference's "
+                       "pre-tiled block panels (\"pretiled_bf16\", a_dtype bf16 or i8)",
                        layout.c_str());
     const bool nk_layout = layout == "tma_bf16";
+    const bool panels = layout == "pretiled_bf16";
+    // a pre-tiled container's operand type: bf16 panels, or int8 panels with
+    // per-column .wscale and the activation's SmoothQuant divisor .asmooth
+    std::string a_dtype = "bf16";
+    if (panels && f.has_config("a_dtype")) a_dtype = f.config_string("a_dtype");
+    if (panels && a_dtype != "bf16" && a_dtype != "i8")
+      return set_error(NEBW_EINVAL, "pre-tiled container with a_dtype '%s' refused: bf16 or i8 "
+                       "(int4 panels are not read)", a_dtype.c_str());
     nebw_config c{};
     c.num_layers = static_cast<int32_t>(f.config_int("num_layers"));
     c.hidden = static_cast<int32_t>(f.config_int("hidden"));
@@ -1547,7 +1641,8 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
     if (c.rope && f.has("embeddings.position")) names.push_back("embeddings.position");
     for (const auto &n : names) {
       const auto &t = f.tensor(n);
-      if (t.dtype != "F32" && t.dtype != "BF16") {
+      const bool gemm_operand = t.shape.size() == 2 && n.rfind("layer.", 0) == 0;
+      if (t.dtype != "F32" && t.dtype != "BF16" && !(panels && gemm_operand && t.dtype == "I8")) {
         nebw_model_destroy(m);
         return set_error(NEBW_EINVAL, "tensor '%s' has dtype %s; F32 or BF16 expected",
                          n.c_str(), t.dtype.c_str());
@@ -1555,9 +1650,29 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
       const int64_t r = t.shape.size() >= 1 ? t.shape[0] : 1;
       const int64_t cc = t.shape.size() >= 2 ? t.shape[1] : 1;
       const int dt = t.dtype == "F32" ? NEBW_F32 : NEBW_BF16;
-      const bool gemm_operand = t.shape.size() == 2 && n.rfind("layer.", 0) == 0;
       int rc;
-      if (nk_layout && gemm_operand) {
+      if (panels && gemm_operand) {
+        // untiled on the host and staged as F32 [K, N]; for int8 the
+        // dequantised weights take the activation's divisor as well:
+        // (a / asmooth) . W == a . (W / asmooth[k]), the reference's host
+        // product (host_gemm, bert_encoder.cpp:714-739) moved onto W
+        std::vector<float> kn;
+        rc = panel_to_kn(f, n, kn);
+        if (!rc && a_dtype == "i8") {
+          const std::string an = n + ".asmooth";
+          if (!f.has(an) || f.tensor(an).dtype != "F32" ||
+              f.tensor(an).nbytes != static_cast<uint64_t>(r) * 4) {
+            nebw_model_destroy(m);
+            return set_error(NEBW_EINVAL, "int8 operand '%s' has no F32 [%lld] %s", n.c_str(),
+                             static_cast<long long>(r), an.c_str());
+          }
+          std::vector<float> as(static_cast<size_t>(r));
+          std::memcpy(as.data(), f.tensor(an).data, as.size() * 4);
+          for (int64_t k = 0; k < r; ++k)
+            for (int64_t j = 0; j < cc; ++j) kn[static_cast<size_t>(k * cc + j)] /= as[static_cast<size_t>(k)];
+        }
+        if (!rc) rc = nebw_model_set_tensor(m, n.c_str(), kn.data(), NEBW_F32, r, cc);
+      } else if (nk_layout && gemm_operand) {
         if (t.dtype != "BF16") {
           nebw_model_destroy(m);
           return set_error(NEBW_EINVAL, "tma_bf16 container: GEMM operand '%s' is %s, BF16 "

@@ -234,6 +234,26 @@ NpueFile::NpueFile(const std::string &path) : path_(path) {
           throw std::runtime_error(path + ": tensor " + t.name + " has a non-string layout_hash");
         t.layout_hash = lh->str;
       }
+      if (const Json *lj = e.find("layout"); lj && lj->kind == Json::Object) {
+        auto str = [&](const char *k) {
+          const Json *v = lj->find(k);
+          return v && v->kind == Json::String ? v->str : std::string();
+        };
+        auto num = [&](const char *k) {
+          const Json *v = lj->find(k);
+          return v && v->kind == Json::Number ? static_cast<int64_t>(v->num) : int64_t{0};
+        };
+        t.layout_kind = str("kind");
+        t.layout_order = str("order");
+        t.layout_inner = str("inner");
+        t.layout_dtype = str("dtype");
+        t.tile_k = num("tile_k");
+        t.tile_n = num("tile_n");
+        t.mac_s = num("mac_s");
+        t.mac_t = num("mac_t");
+      }
+      if (const Json *ps = e.find("padded_shape"); ps && ps->kind == Json::Array)
+        for (const Json &x : ps->arr) t.padded_shape.push_back(static_cast<int64_t>(x.num));
       for (const Json &x : sh->arr) t.shape.push_back(static_cast<int64_t>(x.num));
       t.offset = static_cast<uint64_t>(o->num);
       t.nbytes = static_cast<uint64_t>(nb->num);

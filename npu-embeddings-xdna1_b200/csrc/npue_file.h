@@ -35,6 +35,11 @@ struct Json {
 struct NpueTensor {
   std::string name, role, dtype;
   std::string layout_hash;  // sha256 of the layout descriptor; empty when the entry has none
+  // the entry's layout descriptor (kind empty when it has none): a block
+  // panel's tile and sub-tile sizes, axis order and element type
+  std::string layout_kind, layout_order, layout_inner, layout_dtype;
+  int64_t tile_k = 0, tile_n = 0, mac_s = 0, mac_t = 0;
+  std::vector<int64_t> padded_shape;
   std::vector<int64_t> shape;
   uint64_t offset = 0, nbytes = 0;
   const uint8_t *data = nullptr;

@@ -95,6 +95,7 @@ def lib() -> C.CDLL:
         "nebw_model_set_tensor": ([vp, C.c_char_p, vp, C.c_int, i64, i64], C.c_int),
         "nebw_model_load_npue": ([vp, C.c_char_p, C.POINTER(vp)], C.c_int),
         "nebw_tma_layout_hash": ([], C.c_char_p),
+        "nebw_npue_gemm_kn": ([C.c_char_p, C.c_char_p, vp, i64, i64], C.c_int),
         "nebw_model_set_gemm_nk": ([vp, C.c_char_p, vp, i64, i64], C.c_int),
         "nebw_model_destroy": ([vp], C.c_int),
         "nebw_model_get_config": ([vp, C.POINTER(Config)], C.c_int),

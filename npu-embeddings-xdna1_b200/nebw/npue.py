@@ -66,6 +66,44 @@ def layout_hash(layout: dict) -> str:
     return hashlib.sha256(canonical.encode("utf-8")).hexdigest()
 
 
+def untile_block_panel(flat, K: int, N: int, layout: dict) -> np.ndarray:
+    """A `block_panel` GEMM operand (the reference's pre-tiled array layout)
+    back to row-major [K, N].  The flat panel runs over the axes (kb, nb, ri,
+    ci, si, ti), ti fastest, of sizes (K/tile_k, N/tile_n, tile_k/mac_s,
+    tile_n/mac_t, mac_s, mac_t), with k = kb*tile_k + ri*mac_s + si and
+    n = nb*tile_n + ci*mac_t + ti (runtime/include/common/host_b.hpp:22-30).
+    Only order "k,n,kt,nt" with inner "s,t" is defined there."""
+    _check_panel(K, N, layout)
+    tk, tn, s, t = (int(layout[k]) for k in ("tile_k", "tile_n", "mac_s", "mac_t"))
+    x = np.asarray(flat).reshape(K // tk, N // tn, tk // s, tn // t, s, t)
+    return np.ascontiguousarray(x.transpose(0, 2, 4, 1, 3, 5).reshape(K, N))
+
+
+def tile_block_panel(kn, layout: dict) -> np.ndarray:
+    """Row-major [K, N] to the flat `block_panel` order (untile_block_panel's
+    inverse)."""
+    K, N = kn.shape
+    _check_panel(K, N, layout)
+    tk, tn, s, t = (int(layout[k]) for k in ("tile_k", "tile_n", "mac_s", "mac_t"))
+    x = np.asarray(kn).reshape(K // tk, tk // s, s, N // tn, tn // t, t)
+    return np.ascontiguousarray(x.transpose(0, 3, 1, 4, 2, 5).reshape(-1))
+
+
+def block_panel_layout(tile_k: int, tile_n: int, mac_s: int, mac_t: int, dtype: str) -> dict:
+    """The descriptor of a block-panel operand, with the reference's keys."""
+    return {"kind": "block_panel", "tile_k": tile_k, "tile_n": tile_n, "order": "k,n,kt,nt",
+            "inner": "s,t", "mac_s": mac_s, "mac_t": mac_t, "dtype": dtype}
+
+
+def _check_panel(K: int, N: int, layout: dict):
+    if layout.get("kind") != "block_panel" or layout.get("order") != "k,n,kt,nt" or \
+            layout.get("inner") != "s,t":
+        raise ValueError(f"layout {layout!r}: only block_panel k,n,kt,nt / s,t is defined")
+    tk, tn, s, t = (int(layout[k]) for k in ("tile_k", "tile_n", "mac_s", "mac_t"))
+    if K % tk or N % tn or tk % s or tn % t:
+        raise ValueError(f"[{K}, {N}] does not tile into ({tk}, {tn}) with mac ({s}, {t})")
+
+
 def _pad(n: int) -> int:
     return (-n) % ALIGN
 
@@ -158,14 +196,46 @@ class ContainerReader:
         return False
 
 
+def _bf16_bits(x) -> np.ndarray:
+    """fp32 -> bf16 bits, round to nearest even."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def quantise_int8_columns(kn, asmooth):
+    """Weight side of the int8 datapath, as this writer produces it: W' =
+    diag(asmooth) W, per-column wscale = max_k |W'| / 127 (1 for a zero
+    column), q = round-half-even(W' / wscale) clamped to +-127.  Returns
+    (q int8 [K, N], wscale f32 [N])."""
+    wp = np.asarray(kn, np.float32) * np.asarray(asmooth, np.float32)[:, None]
+    mx = np.abs(wp).max(axis=0)
+    ws = np.where(mx > 0, mx / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(wp / ws[None, :]), -127, 127).astype(np.int8)
+    return q, ws
+
+
 def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synthetic/random-init",
-                         config_overrides: dict | None = None):
+                         config_overrides: dict | None = None, gemm_layout: str = "host",
+                         a_dtype: str = "bf16", tile=(64, 32), mac=(8, 8), smooth_seed: int = 0):
     """Write a BERT (arch 0) container in the host layout the reference's CPU
     path reads: GEMM operands F32 row-major [K, N] (`gemm_b_host`), biases and
     LayerNorm F32, embeddings F32.  Tensor names and config keys follow the
     reference packer's BERT branch (tools/pack/pack_npue.py:2640-2790); the
     config keys are the ones set_model_shape() requires
-    (runtime/include/common/app_state.hpp:380-631)."""
+    (runtime/include/common/app_state.hpp:380-631).
+
+    gemm_layout "pretiled_bf16" writes the reference's pre-tiled form instead:
+    each GEMM operand a `block_panel` of `tile` = (tile_k, tile_n) tiles in
+    `mac` = (mac_s, mac_t) sub-tiles with its layout descriptor and
+    layout_hash, as bf16 (a_dtype "bf16") or as int8 (a_dtype "i8") with its
+    per-column `.wscale` and the activation's SmoothQuant divisor `.asmooth`
+    (seeded positive factors, not calibrated: any factors describe the same
+    model, W' = diag(asmooth) W against A / asmooth)."""
+    if gemm_layout not in ("host", "pretiled_bf16") or a_dtype not in ("bf16", "i8"):
+        raise ValueError(f"gemm_layout {gemm_layout!r} / a_dtype {a_dtype!r}")
+    pretiled = gemm_layout == "pretiled_bf16"
+    i8 = pretiled and a_dtype == "i8"
+    srng = np.random.default_rng(smooth_seed)
     H, F, L = model.hidden, model.ffn, model.layers
     gated = getattr(model, "gated", "")
     FW = 2 * F if gated else F
@@ -183,17 +253,20 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
         "pooling": "cls" if model.cls_pool else "mean",
         "l2_normalize": True,
         "activation": "gelu_erf_exact",
-        "gemm_layout": "host",
-        "a_dtype": "f32",
+        "gemm_layout": gemm_layout,
+        "a_dtype": a_dtype if pretiled else "f32",
         "fusions": {
             "qkv_fused": True,
             "transposed_to_kn": True,
             "qk_scale_folded_into_q": True,
-            "gemm_operands_bf16": False,
+            "gemm_operands_bf16": pretiled and not i8,
             "biases_and_layernorm_fp32": True,
             "position_embeddings_presliced_to": int(max_seq_len),
         },
     }
+    if pretiled:
+        config.update(tile_k=int(tile[0]), tile_n=int(tile[1]), mac_s=int(mac[0]),
+                      mac_t=int(mac[1]))
     header_arch = ARCH_BERT
     if gated:
         # the keys set_model_shape reads for the gated / rotary families
@@ -218,6 +291,24 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
         else:
             config[k] = v
     w = ContainerWriter(config, arch=header_arch)
+
+    def gemm(name, kn):
+        K, N = kn.shape
+        if not pretiled:
+            w.add(name, kn, "F32", "gemm_b_host", [K, N])
+            return
+        layout = block_panel_layout(int(tile[0]), int(tile[1]), int(mac[0]), int(mac[1]),
+                                    "I8" if i8 else "BF16")
+        if not i8:
+            w.add(name, tile_block_panel(_bf16_bits(kn), layout), "BF16", "gemm_b", [K, N],
+                  layout=layout)
+            return
+        asm = srng.lognormal(0.0, 0.5, K).astype(np.float32)
+        q, ws = quantise_int8_columns(kn, asm)
+        w.add(name, tile_block_panel(q, layout), "I8", "gemm_b", [K, N], layout=layout)
+        w.add(name + ".wscale", ws, "F32", "quant_scale", [N])
+        w.add(name + ".asmooth", asm, "F32", "quant_smooth", [K])
+
     w.add("embeddings.word", model.word, "F32", "embedding", [model.vocab, H])
     w.add("embeddings.position", model.pos[:max_seq_len], "F32", "embedding", [max_seq_len, H])
     w.add("embeddings.token_type", model.typ, "F32", "embedding", [model.typ.shape[0], H])
@@ -225,15 +316,15 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
     w.add("embeddings.ln.bias", model.emb_ln_b, "F32", "layernorm", [H])
     for i in range(L):
         p = f"layer.{i}."
-        w.add(p + "qkv", model.w_qkv[i], "F32", "gemm_b_host", [H, 3 * H])
+        gemm(p + "qkv", model.w_qkv[i])
         w.add(p + "qkv.bias", model.b_qkv[i], "F32", "bias", [3 * H])
-        w.add(p + "attn_out", model.w_ao[i], "F32", "gemm_b_host", [H, H])
+        gemm(p + "attn_out", model.w_ao[i])
         w.add(p + "attn_out.bias", model.b_ao[i], "F32", "bias", [H])
         w.add(p + "ln1.weight", model.ln1_g[i], "F32", "layernorm", [H])
         w.add(p + "ln1.bias", model.ln1_b[i], "F32", "layernorm", [H])
-        w.add(p + "ffn_up", model.w_up[i], "F32", "gemm_b_host", [H, FW])
+        gemm(p + "ffn_up", model.w_up[i])
         w.add(p + "ffn_up.bias", model.b_up[i], "F32", "bias", [FW])
-        w.add(p + "ffn_down", model.w_dn[i], "F32", "gemm_b_host", [F, H])
+        gemm(p + "ffn_down", model.w_dn[i])
         w.add(p + "ffn_down.bias", model.b_dn[i], "F32", "bias", [H])
         w.add(p + "ln2.weight", model.ln2_g[i], "F32", "layernorm", [H])
         w.add(p + "ln2.bias", model.ln2_b[i], "F32", "layernorm", [H])

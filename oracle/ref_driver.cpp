@@ -12,9 +12,11 @@
 //
 // with the encoder set up the way setup_encoder() does for an all-host run:
 // set_model_shape (app_state.hpp:380), set_design_seq (:637), host_ln /
-// host_sm / host_gelu true, stage_all() (bert_encoder.cpp:41-172) on a
-// `gemm_layout:"host"` container so every GEMM is hostconv::gemm_nt over the
-// container's F32 [K,N] operand.
+// host_sm / host_gelu true, stage_all() (bert_encoder.cpp:41-172), so every
+// GEMM is hostconv::gemm_nt over the operand as fp32 [K,N]: a
+// `gemm_layout:"host"` container's F32 operand, or a pre-tiled container's
+// panel untiled by host_b.hpp (int8 dequantised by .wscale, A divided by
+// .asmooth), the stand-in design describing that container's operands.
 //
 // It also exposes a few of the reference's inline host kernels one by one
 // (gemm_nt, gelu8, to_bf16, exp2_avx2, pool_rows) so the CPU restatement in
@@ -37,11 +39,33 @@
 #include "runtime/pool.hpp"
 #include "tokenizers/wordpiece.hpp"
 
+extern std::string nebw_oracle_b_layout_hash;  // oracle/ref_stub.cpp
+extern size_t nebw_oracle_a_elem_bytes;
+
 namespace {
 void set_err(char *err, int32_t errlen, const char *msg) {
   if (!err || errlen <= 0) return;
   std::strncpy(err, msg, static_cast<size_t>(errlen) - 1);
   err[errlen - 1] = '\0';
+}
+
+// The stand-in design matches the container, as a design set exported for it
+// would: the operands' layout hash, and int8 operands for a_dtype "i8".
+void describe_design(const npue::File &f) {
+  std::string layout, a_dtype;
+  try {
+    layout = f.config_string("gemm_layout");
+  } catch (const std::exception &) {
+  }
+  try {
+    a_dtype = f.config_string("a_dtype");
+  } catch (const std::exception &) {
+  }
+  nebw_oracle_b_layout_hash.clear();
+  nebw_oracle_a_elem_bytes = 2;
+  if (layout == "host") return;
+  nebw_oracle_b_layout_hash = f.info("layer.0.qkv").layout_hash;
+  if (a_dtype == "i8") nebw_oracle_a_elem_bytes = 1;
 }
 }  // namespace
 
@@ -58,6 +82,7 @@ int nebw_ref_encode(const char *npue_path, int32_t seq, const int32_t *ids,
                     float *out, float *hidden_out, char *err, int32_t errlen) {
   try {
     npue::File f(npue_path);
+    describe_design(f);
     app::set_model_shape(f);
     app::set_design_seq(seq);
     app::Pool pool(threads > 0 ? threads : 1);
@@ -122,6 +147,7 @@ void *nebw_ref_session_open(const char *npue_path, int32_t seq, int32_t threads,
     // geometry globals first: the encoder's constructor and stage_all read them
     {
       npue::File probe(npue_path);
+      describe_design(probe);
       app::set_model_shape(probe);
       app::set_design_seq(seq);
     }

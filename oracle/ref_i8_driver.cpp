@@ -6,6 +6,9 @@
 //   quantise_a_int8    :263-315  A -> int8 per row, SmoothQuant divisor folded
 //   dequantise_c       :529-614  int32 C -> fp32 with row/column scales + bias
 //   dequant_act_quant  :404-526  the FFN-up epilogue: dequantise, act, quantise
+// and the reference's reader of pre-tiled GEMM operands,
+//   npue::hostb::host_b_kn (runtime/include/common/host_b.hpp:74-224)
+// over a container opened with npue::File (runtime/src/model.cpp).
 // Rows run serially (the templates' par_rows argument); the act given to
 // dequant_act_quant applies the reference's gelu8 (host_kernels.hpp:325-352),
 // the BERT FFN's activation.  The buffers handed to the reference are
@@ -20,6 +23,8 @@
 #include <exception>
 
 #include "common/host_kernels.hpp"
+#include "runtime/model.hpp"
+#include "common/host_b.hpp"
 
 namespace {
 
@@ -74,6 +79,20 @@ int nebw_ref_dequant_gelu_quant(const int32_t *c, int64_t rows, int64_t N, const
   try {
     app::dequant_act_quant(ca.p, 4, rows, N, N, gelu, sa, ws, bias, ias_next, q, sa_next,
                            serial_rows);
+    return 0;
+  } catch (const std::exception &) {
+    return 1;
+  }
+}
+
+// `name` of the container at `path` as fp32 [K, N] (BF16 widened, I8
+// dequantised by .wscale); returns 0, or 1 when the reference refuses.
+int nebw_ref_host_b_kn(const char *path, const char *name, float *out, int64_t K, int64_t N) {
+  try {
+    npue::File f(path);
+    const std::vector<float> kn = npue::hostb::host_b_kn(f, name);
+    if (static_cast<int64_t>(kn.size()) != K * N) return 2;
+    std::memcpy(out, kn.data(), kn.size() * 4);
     return 0;
   } catch (const std::exception &) {
     return 1;

@@ -42,9 +42,24 @@ struct Device::Impl {};
 Device::Device() {}
 Device::~Device() {}
 
+}  // namespace npu
+
+// What the stand-in design reports for a pre-tiled container (gemm_layout
+// "pretiled_bf16"), set by the drivers before an encoder is built: the
+// operands' layout_hash, so that stage_all's design/model layout check
+// (bert_encoder.cpp:41-150) passes as it does with a matching design set,
+// and the operand width, 1 for an int8 container, which is what makes
+// stage_all load .wscale / .asmooth and the host GEMM divide A by .asmooth.
+std::string nebw_oracle_b_layout_hash;
+size_t nebw_oracle_a_elem_bytes = 2;
+
+namespace npu {
+
 struct Design::Impl {};
 Design::Design(Device &dev, const std::string &dir) : dev_(&dev) {
   info_.name = dir;  // used only as a cache-key label by host_b.hpp
+  info_.b_layout_hash = nebw_oracle_b_layout_hash;
+  info_.a_elem_bytes = nebw_oracle_a_elem_bytes;
   // NpuGemm::alloc_buffers (runtime/src/whisper/npu_ops.cpp:29-32) reads the
   // A and C entries of buffer_bytes; a host-layout run never uses the sizes.
   info_.buffer_bytes.assign(3, 0);
@@ -54,7 +69,14 @@ Design::~Design() {}
 void Design::run(const std::vector<const void *> &, void *) { unreachable("Design::run"); }
 void Design::dispatch_only() { unreachable("Design::dispatch_only"); }
 void Design::bind_instr(size_t) { unreachable("Design::bind_instr"); }
-size_t Design::stage(size_t, const void *, size_t) { unreachable("Design::stage"); }
+// Staging a pre-tiled weight panel uploads nothing here: the host GEMM reads
+// the operand from the container (host_b.hpp) by the slot it was recorded
+// under, so a fresh slot number per call is all stage_all needs.  A host-
+// layout container never stages.
+size_t Design::stage(size_t, const void *, size_t) {
+  static size_t staged = size_t{1} << 32;  // apart from host_layout's slot numbers
+  return ++staged;
+}
 // VitEncoder::stage_all -> NpuGemm::alloc_buffers (runtime/src/whisper/
 // npu_ops.cpp:29-32) reserves the design's A and C slots even on a
 // host-layout container, whose GEMMs never touch them; the slot numbers are

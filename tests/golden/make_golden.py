@@ -28,6 +28,12 @@ shortest and longest rows are always included):
                      (runtime/src/vit/encoder.cpp) via oracle/ref_vit_driver.cpp.
                      The images are regenerated from the recorded seed (their
                      SHA-256 is stored), not stored.
+  pretiled_bf16_c1.npz, pretiled_i8_c1.npz
+                     MiniLM's configuration written by nebw.npue in the
+                     reference's pre-tiled form (block panels, bf16, or int8
+                     with .wscale / .asmooth), 8 rows through the reference's
+                     host path on that container (host_b.hpp untiles it);
+                     the container is regenerated (its SHA-256 is stored).
   int8_steps.npz     the int8 datapath's host steps (host_kernels.hpp:
                      quantise_a_int8, dequantise_c with an int32 C,
                      dequant_act_quant with gelu8) on int8_step_inputs(), via
@@ -149,6 +155,40 @@ def make_int8(ref):
     print("int8_steps: written")
 
 
+PRETILED = {"pretiled_bf16_c1": ("minilm", "bf16"), "pretiled_i8_c1": ("minilm", "i8")}
+PRETILED_TILE, PRETILED_MAC, PRETILED_SMOOTH_SEED = (64, 64), (8, 8), 20261501
+
+
+def write_pretiled(path, key: str, a_dtype: str) -> str:
+    """The configuration's seeded weights as a pre-tiled container at `path`;
+    returns its SHA-256."""
+    from nebw.npue import write_bert_container
+    cfg = synth.CONFIGS[key]
+    write_bert_container(path, synth.config_weights(cfg), max_seq_len=cfg.seq,
+                         gemm_layout="pretiled_bf16", a_dtype=a_dtype, tile=PRETILED_TILE,
+                         mac=PRETILED_MAC, smooth_seed=PRETILED_SMOOTH_SEED)
+    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
+
+
+def make_pretiled(ref, name, key, a_dtype):
+    import tempfile
+    cfg = synth.CONFIGS[key]
+    ids, mask, lens = synth.config_batch(cfg)
+    rows = sample_rows(lens, 8)
+    with tempfile.TemporaryDirectory(dir=HERE) as td:
+        path = Path(td) / "c.npue"
+        digest = write_pretiled(path, key, a_dtype)
+        out = ref.encode_container(path, cfg.seq, ids[rows], mask[rows], hidden_size=cfg.arch.hidden)
+    np.savez_compressed(
+        HERE / f"{name}.npz", config=key, a_dtype=a_dtype, container_sha256=digest,
+        rows=rows.astype(np.int32), ids=ids[rows], mask=mask[rows],
+        lens=lens[rows].astype(np.int32), embeddings=out,
+        provenance="reference host-CPU path on a pre-tiled container (host_b.hpp untile, "
+                   "int8 dequantised by .wscale with A divided by .asmooth) via "
+                   "oracle/ref_driver.cpp")
+    print(f"{name}: {len(rows)} rows")
+
+
 def make_vit(ref, name, key, n):
     cfg = synth.VIT_CONFIGS[key]
     w = synth.vit_config_weights(cfg)
@@ -171,6 +211,9 @@ def main():
     only = set(sys.argv[1:])
     if not only or "int8_steps" in only:
         make_int8(ref)
+    for name, (key, a_dtype) in PRETILED.items():
+        if not only or name in only:
+            make_pretiled(ref, name, key, a_dtype)
     for name, (key, n) in VIT_FIXTURES.items():
         if not only or name in only:
             make_vit(ref, name, key, n)

@@ -112,21 +112,45 @@ def describe(path) -> dict:
         return {"config": r.config, "tensors": tensors, "order": list(r.entries)}
 
 
-def main():
-    ref = Path("/root/reference")
-    sys.path.insert(0, str(ref / "tools" / "pack"))
-    sys.path.insert(0, str(ref / "tools" / "lib"))
+REFERENCE = Path("/root/reference")
+
+
+def reference_pack(workdir, dtype: str, extra=()) -> Path:
+    """Pack synthetic_checkpoint() into workdir with the reference's own
+    packer (tools/pack/pack_npue.py main()) at --dtype `dtype`.  Its ONNX
+    reads -- the packer's `load` and, for int8, the calibration oracle's
+    (reference/encoder.py, reference/onnx_io.py) -- are replaced by the
+    checkpoint's own tensors, and `model_digest` by the SHA-256 of
+    model.safetensors.  Returns the container's path."""
+    for sub in ("tools/pack", "tools/lib", "reference"):
+        if str(REFERENCE / sub) not in sys.path:
+            sys.path.insert(0, str(REFERENCE / sub))
     import pack_npue as P  # the reference's packer
-    with tempfile.TemporaryDirectory() as td:
-        d = Path(td) / "tiny-bert"
-        src = synthetic_checkpoint(d)
-        digest = hashlib.sha256((d / "model.safetensors").read_bytes()).hexdigest()
-        P.load = lambda path, **kw: (src, {})
-        P.model_digest = lambda path: digest
-        out = Path(td) / "ref.npue"
-        sys.argv = ["pack_npue.py", "--model-dir", str(d), "--out", str(out), "--dtype", "f32",
-                    "--max-seq", str(MAX_SEQ)]
+    d = Path(workdir) / "tiny-bert"
+    src = synthetic_checkpoint(d)
+    digest = hashlib.sha256((d / "model.safetensors").read_bytes()).hexdigest()
+    fake = lambda path, **kw: (src, {})  # noqa: E731
+    P.load = fake
+    P.model_digest = lambda path: digest
+    if dtype == "i8":
+        import encoder
+        import onnx_io
+        onnx_io.load = fake
+        encoder.load = fake
+    out = Path(workdir) / f"ref_{dtype}.npue"
+    argv = sys.argv
+    sys.argv = ["pack_npue.py", "--model-dir", str(d), "--out", str(out), "--dtype", dtype,
+                "--max-seq", str(MAX_SEQ), *extra]
+    try:
         P.main()
+    finally:
+        sys.argv = argv
+    return out
+
+
+def main():
+    with tempfile.TemporaryDirectory() as td:
+        out = reference_pack(td, "f32")
         desc = describe(out)
     desc["provenance"] = ("reference tools/pack/pack_npue.py main(), --dtype f32 --max-seq "
                           f"{MAX_SEQ}, on synthetic_checkpoint(seed {SEED}); its ONNX reads "

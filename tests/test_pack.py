@@ -160,3 +160,143 @@ def test_pack_refuses_other_models(tmp_path):
     (d / "config.json").write_text(json.dumps(cfg))
     with pytest.raises(SystemExit, match="model_type"):
         pack_bert(d, tmp_path / "x.npue")
+
+
+# ---- the reference's pre-tiled containers (block panels, bf16 / int8) ----
+
+def test_block_panel_order_and_round_trip():
+    """untile_block_panel against the axis order written out element by
+    element: flat index over (kb, nb, ri, ci, si, ti), ti fastest, k = kb*tk
+    + ri*s + si, n = nb*tn + ci*t + ti."""
+    from nebw.npue import block_panel_layout, tile_block_panel, untile_block_panel
+    K, N = 32, 48
+    lay = block_panel_layout(16, 24, 4, 8, "I8")
+    flat = np.arange(K * N, dtype=np.int32)
+    want = np.empty((K, N), np.int32)
+    f = 0
+    for kb in range(K // 16):
+        for nb in range(N // 24):
+            for ri in range(16 // 4):
+                for ci in range(24 // 8):
+                    for si in range(4):
+                        for ti in range(8):
+                            want[kb * 16 + ri * 4 + si, nb * 24 + ci * 8 + ti] = flat[f]
+                            f += 1
+    np.testing.assert_array_equal(untile_block_panel(flat, K, N, lay), want)
+    np.testing.assert_array_equal(tile_block_panel(want, lay), flat)
+    with pytest.raises(ValueError, match="does not tile"):
+        untile_block_panel(flat, K, N, block_panel_layout(16, 20, 4, 8, "I8"))
+
+
+def _gemm_kn(lib, path, name, K, N):
+    out = np.zeros((K, N), np.float32)
+    rc = lib.nebw_npue_gemm_kn(str(path).encode(), name.encode(), out.ctypes.data, K, N)
+    return rc, out
+
+
+def _assert_reader_matches_reference(path, ref_oracle):
+    import ctypes as C
+
+    import nebw
+    from nebw.npue import ContainerReader
+    lib = nebw.lib()
+    f = ref_oracle.lib.nebw_ref_host_b_kn
+    f.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_int64, C.c_int64]
+    n = 0
+    with ContainerReader(path) as r:
+        ops = [(k, e["logical_shape"]) for k, e in r.entries.items() if e["role"] == "gemm_b"]
+    for name, (K, N) in ops:
+        rc, mine = _gemm_kn(lib, path, name, K, N)
+        assert rc == 0, lib.nebw_last_error().decode()
+        theirs = np.zeros((K, N), np.float32)
+        assert f(str(path).encode(), name.encode(), theirs.ctypes.data, K, N) == 0
+        np.testing.assert_array_equal(mine.view(np.uint32), theirs.view(np.uint32), err_msg=name)
+        n += 1
+    assert n > 0
+
+
+@pytest.mark.parametrize("a_dtype", ["bf16", "i8"])
+def test_pretiled_reader_bit_exact_vs_reference_on_our_containers(tmp_path, ref_oracle, a_dtype):
+    """nebw_npue_gemm_kn (the library's reader) against the reference's
+    host_b_kn, compiled from its tree, on containers nebw.npue writes."""
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    w = synth.config_weights(synth.CONFIGS["minilm"], layers=2)
+    path = tmp_path / f"{a_dtype}.npue"
+    write_bert_container(path, w, max_seq_len=64, gemm_layout="pretiled_bf16", a_dtype=a_dtype,
+                         tile=(64, 48), smooth_seed=1)
+    _assert_reader_matches_reference(path, ref_oracle)
+
+
+@pytest.mark.parametrize("dtype,extra", [("bf16", ("--tile-n", "32")), ("i8", ("--tile-n", "32"))])
+def test_pretiled_reader_bit_exact_on_reference_packed_containers(tmp_path, ref_oracle, dtype,
+                                                                  extra):
+    """Containers made by the reference's own packer (--dtype bf16, and --dtype
+    i8 with its SmoothQuant calibration) read bit-identically by the library
+    and by the reference's host_b_kn."""
+    from conftest import has_reference
+    if not has_reference():
+        pytest.skip("the reference tree is not here")
+    from make_pack_golden import reference_pack
+    path = reference_pack(tmp_path, dtype, extra)
+    from nebw.npue import ContainerReader
+    with ContainerReader(path) as r:
+        assert r.config["gemm_layout"] == "pretiled_bf16" and r.config["a_dtype"] == dtype
+    _assert_reader_matches_reference(path, ref_oracle)
+
+
+def test_pretiled_golden_containers_regenerate():
+    """The containers behind tests/golden/pretiled_*.npz come back byte for
+    byte from nebw.npue, so the GPU test reads what the reference read."""
+    import make_golden
+    for name, (key, a_dtype) in make_golden.PRETILED.items():
+        g = np.load(GOLDEN / f"{name}.npz")
+        with __import__("tempfile").TemporaryDirectory(dir=GOLDEN) as td:
+            digest = make_golden.write_pretiled(f"{td}/c.npue", key, a_dtype)
+        assert digest == str(g["container_sha256"]), name
+
+
+def test_gemm_kn_refusals(tmp_path):
+    """The reader refuses, by name, what it cannot read: an axis order it does
+    not define, tiles that do not divide the operand, an int8 operand without
+    its .wscale."""
+    import nebw
+    from nebw.npue import ContainerWriter, block_panel_layout, tile_block_panel
+    lib = nebw.lib()
+    K, N = 64, 64
+    q = np.arange(K * N, dtype=np.int64).reshape(K, N).astype(np.int8)
+
+    def one(layout, with_ws=True):
+        w = ContainerWriter({"arch": "bert_abs_gelu_postln"})
+        w.add("layer.0.qkv", tile_block_panel(q, block_panel_layout(32, 32, 8, 8, "I8")), "I8",
+              "gemm_b", [K, N], layout=layout)
+        if with_ws:
+            w.add("layer.0.qkv.wscale", np.ones(N, np.float32), "F32", "quant_scale", [N])
+        path = tmp_path / "c.npue"
+        w.write(path)
+        rc, _ = _gemm_kn(lib, path, "layer.0.qkv", K, N)
+        return rc, lib.nebw_last_error().decode()
+
+    good = block_panel_layout(32, 32, 8, 8, "I8")
+    assert one(good)[0] == 0
+    rc, msg = one(dict(good, order="n,k,nt,kt"))
+    assert rc != 0 and "refused" in msg
+    rc, msg = one(dict(good, tile_n=48))
+    assert rc != 0 and "does not tile" in msg
+    rc, msg = one(good, with_ws=False)
+    assert rc != 0 and ".wscale" in msg
+
+
+def test_loader_refuses_int4_containers_without_a_gpu(tmp_path):
+    import ctypes as C
+
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    w = synth.config_weights(synth.CONFIGS["minilm"], layers=1)
+    path = tmp_path / "i4.npue"
+    write_bert_container(path, w, max_seq_len=64, gemm_layout="pretiled_bf16", a_dtype="i8",
+                         config_overrides={"a_dtype": "i4"})
+    h = C.c_void_p()
+    assert nebw.lib().nebw_model_load_npue(None, str(path).encode(), C.byref(h)) == 1
+    assert "a_dtype 'i4'" in nebw.lib().nebw_last_error().decode()
