@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <cctype>
 #include <cmath>
 #include <cstdarg>
 #include <cstdlib>
@@ -1527,6 +1528,8 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
     // per-column .wscale and the activation's SmoothQuant divisor .asmooth
     std::string a_dtype = "bf16";
     if (panels && f.has_config("a_dtype")) a_dtype = f.config_string("a_dtype");
+    for (char &ch : a_dtype) ch = static_cast<char>(std::tolower(static_cast<unsigned char>(ch)));
+    // (the BERT packer writes "bf16" / "i8", the ViT packer "BF16" / "I8")
     if (panels && a_dtype != "bf16" && a_dtype != "i8")
       return set_error(NEBW_EINVAL, "pre-tiled container with a_dtype '%s' refused: bf16 or i8 "
                        "(int4 panels are not read)", a_dtype.c_str());

@@ -447,11 +447,19 @@ extern "C" int nebw_vit_load_npue(nebw_dev *d, const char *path, nebw_vit **out)
                        arch.c_str());
     std::string layout = "pretiled_bf16";
     if (f.has_config("gemm_layout")) layout = f.config_string("gemm_layout");
-    if (layout != "host")
+    if (layout != "host" && layout != "pretiled_bf16")
       return set_error(NEBW_EINVAL,
-                       "container gemm_layout '%s' refused: this library stages the plain "
-                       "row-major [K, N] operands of a gemm_layout \"host\" container and "
-                       "re-tiles them itself", layout.c_str());
+                       "container gemm_layout '%s' refused: this library reads \"host\" (F32 "
+                       "[K, N]) and the reference's pre-tiled block panels (\"pretiled_bf16\", "
+                       "a_dtype bf16 or i8)", layout.c_str());
+    const bool panels = layout == "pretiled_bf16";
+    std::string a_dtype = "bf16";
+    if (panels && f.has_config("a_dtype")) a_dtype = f.config_string("a_dtype");
+    for (char &ch : a_dtype) ch = static_cast<char>(std::tolower(static_cast<unsigned char>(ch)));
+    // (the BERT packer writes "bf16" / "i8", the ViT packer "BF16" / "I8")
+    if (panels && a_dtype != "bf16" && a_dtype != "i8")
+      return set_error(NEBW_EINVAL, "pre-tiled container with a_dtype '%s' refused: bf16 or i8 "
+                       "(int4 panels are not read)", a_dtype.c_str());
     if (f.has_config("qkv_scale_folded") && f.config_string("qkv_scale_folded") == "false")
       return set_error(NEBW_EINVAL,
                        "container has qkv_scale_folded false: this library expects "
@@ -476,7 +484,8 @@ extern "C" int nebw_vit_load_npue(nebw_dev *d, const char *path, nebw_vit **out)
     if (int rc = nebw_vit_create(d, &c, &m)) return rc;
     for (const auto &n : vit_required_names(c)) {
       const auto &t = f.tensor(n);
-      if (t.dtype != "F32" && t.dtype != "BF16") {
+      const bool gemm_operand = t.shape.size() == 2 && !t.layout_kind.empty();
+      if (t.dtype != "F32" && t.dtype != "BF16" && !(panels && gemm_operand && t.dtype == "I8")) {
         nebw_vit_destroy(m);
         return set_error(NEBW_EINVAL, "tensor '%s' has dtype %s; F32 or BF16 expected",
                          n.c_str(), t.dtype.c_str());
@@ -484,7 +493,34 @@ extern "C" int nebw_vit_load_npue(nebw_dev *d, const char *path, nebw_vit **out)
       const int64_t r = t.shape.size() >= 1 ? t.shape[0] : 1;
       const int64_t cc = t.shape.size() >= 2 ? t.shape[1] : 1;
       const int dt = t.dtype == "F32" ? NEBW_F32 : NEBW_BF16;
-      int rc = nebw_vit_set_tensor(m, n.c_str(), t.data, dt, r, cc);
+      int rc;
+      if (panels && gemm_operand) {
+        // untiled on the host and staged as F32 [K, N]; an int8 operand's
+        // optional .asmooth becomes a per-row factor 1/asmooth (1 where it is
+        // not positive), as NpuGemm::run_host scales A (runtime/src/whisper/
+        // npu_ops.cpp:96-116, 158-190), moved onto W
+        std::vector<float> kn;
+        rc = panel_to_kn(f, n, kn);
+        const std::string an = n + ".asmooth";
+        if (!rc && a_dtype == "i8" && f.has(an)) {
+          const auto &at = f.tensor(an);
+          if (at.dtype != "F32" || at.nbytes != static_cast<uint64_t>(r) * 4) {
+            nebw_vit_destroy(m);
+            return set_error(NEBW_EINVAL, "%s must be F32 [%lld]", an.c_str(),
+                             static_cast<long long>(r));
+          }
+          std::vector<float> as(static_cast<size_t>(r));
+          std::memcpy(as.data(), at.data, as.size() * 4);
+          for (int64_t k = 0; k < r; ++k) {
+            const float inv = as[static_cast<size_t>(k)] > 0.f ? 1.0f / as[static_cast<size_t>(k)]
+                                                                : 1.0f;
+            for (int64_t j = 0; j < cc; ++j) kn[static_cast<size_t>(k * cc + j)] *= inv;
+          }
+        }
+        if (!rc) rc = nebw_vit_set_tensor(m, n.c_str(), kn.data(), NEBW_F32, r, cc);
+      } else {
+        rc = nebw_vit_set_tensor(m, n.c_str(), t.data, dt, r, cc);
+      }
       if (rc) {
         const std::string msg = g_last_error;
         nebw_vit_destroy(m);

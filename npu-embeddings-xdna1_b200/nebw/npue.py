@@ -214,6 +214,27 @@ def quantise_int8_columns(kn, asmooth):
     return q, ws
 
 
+def _add_gemm_operand(w, name, kn, pretiled: bool, i8: bool, tile, mac, srng):
+    """One GEMM operand [K, N]: F32 row-major (host layout), or a block panel
+    of bf16, or of int8 with its .wscale and a seeded .asmooth."""
+    kn = np.asarray(kn, np.float32)
+    K, N = kn.shape
+    if not pretiled:
+        w.add(name, kn, "F32", "gemm_b_host", [K, N])
+        return
+    layout = block_panel_layout(int(tile[0]), int(tile[1]), int(mac[0]), int(mac[1]),
+                                "I8" if i8 else "BF16")
+    if not i8:
+        w.add(name, tile_block_panel(_bf16_bits(kn), layout), "BF16", "gemm_b", [K, N],
+              layout=layout)
+        return
+    asm = srng.lognormal(0.0, 0.5, K).astype(np.float32)
+    q, ws = quantise_int8_columns(kn, asm)
+    w.add(name, tile_block_panel(q, layout), "I8", "gemm_b", [K, N], layout=layout)
+    w.add(name + ".wscale", ws, "F32", "quant_scale", [N])
+    w.add(name + ".asmooth", asm, "F32", "quant_smooth", [K])
+
+
 def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synthetic/random-init",
                          config_overrides: dict | None = None, gemm_layout: str = "host",
                          a_dtype: str = "bf16", tile=(64, 32), mac=(8, 8), smooth_seed: int = 0):
@@ -293,21 +314,7 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
     w = ContainerWriter(config, arch=header_arch)
 
     def gemm(name, kn):
-        K, N = kn.shape
-        if not pretiled:
-            w.add(name, kn, "F32", "gemm_b_host", [K, N])
-            return
-        layout = block_panel_layout(int(tile[0]), int(tile[1]), int(mac[0]), int(mac[1]),
-                                    "I8" if i8 else "BF16")
-        if not i8:
-            w.add(name, tile_block_panel(_bf16_bits(kn), layout), "BF16", "gemm_b", [K, N],
-                  layout=layout)
-            return
-        asm = srng.lognormal(0.0, 0.5, K).astype(np.float32)
-        q, ws = quantise_int8_columns(kn, asm)
-        w.add(name, tile_block_panel(q, layout), "I8", "gemm_b", [K, N], layout=layout)
-        w.add(name + ".wscale", ws, "F32", "quant_scale", [N])
-        w.add(name + ".asmooth", asm, "F32", "quant_smooth", [K])
+        _add_gemm_operand(w, name, kn, pretiled, i8, tile, mac, srng)
 
     w.add("embeddings.word", model.word, "F32", "embedding", [model.vocab, H])
     w.add("embeddings.position", model.pos[:max_seq_len], "F32", "embedding", [max_seq_len, H])
@@ -331,12 +338,22 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
     return w.write(path)
 
 
-def write_vit_container(path, model, source_repo: str = "synthetic/random-init"):
+def write_vit_container(path, model, source_repo: str = "synthetic/random-init",
+                        gemm_layout: str = "host", a_dtype: str = "bf16", tile=(64, 64),
+                        mac=(8, 8), smooth_seed: int = 0):
     """Write a ViT (arch vit_patch16_prenorm_gelu) container in the host
     layout: GEMM operands F32 row-major [K, N], everything else F32.  Config
     keys are the ones read_geometry() requires (runtime/include/vit/
     geometry.hpp), tensor names the ones VitEncoder::stage_all() reads
-    (runtime/src/vit/encoder.cpp:125-189)."""
+    (runtime/src/vit/encoder.cpp:125-189).  gemm_layout "pretiled_bf16"
+    writes the encoder's GEMM operands (patch embedding and the four per
+    layer) as block panels instead, as write_bert_container does; the
+    classifier head stays F32."""
+    if gemm_layout not in ("host", "pretiled_bf16") or a_dtype not in ("bf16", "i8"):
+        raise ValueError(f"gemm_layout {gemm_layout!r} / a_dtype {a_dtype!r}")
+    pretiled = gemm_layout == "pretiled_bf16"
+    i8 = pretiled and a_dtype == "i8"
+    srng = np.random.default_rng(smooth_seed)
     a = model.arch
     H, F, L = a.hidden, a.ffn, model.layers
     pd = a.channels * a.patch_size ** 2
@@ -352,9 +369,14 @@ def write_vit_container(path, model, source_repo: str = "synthetic/random-init")
         "image_mean": [0.5] * a.channels, "image_std": [0.5] * a.channels,
         "layer_norm_eps": a.ln_eps, "attention_scale": 1.0 / float(np.sqrt(a.head_dim)),
         "qkv_scale_folded": True,
-        "gemm_layout": "host",
-        "a_dtype": "f32",
+        "gemm_layout": gemm_layout,
+        # the ViT packer spells the operand type in capitals
+        # (tools/pack/packers/vit.py:113, 554, 637), and its encoder compares so
+        "a_dtype": ("I8" if i8 else "BF16") if pretiled else "f32",
     }
+    if pretiled:
+        config.update(tile_k=int(tile[0]), tile_n=int(tile[1]), mac_s=int(mac[0]),
+                      mac_t=int(mac[1]))
     w = ContainerWriter(config)
     shapes = {"frontend.patch_embed": [pd, H], "frontend.patch_embed.bias": [H],
               "frontend.cls_token": [H], "frontend.position_embeddings": [a.n_pos, H],
@@ -367,9 +389,12 @@ def write_vit_container(path, model, source_repo: str = "synthetic/random-init")
             shape = {"qkv": [H, 3 * H], "qkv.bias": [3 * H], "attn_out": [H, H],
                      "attn_out.bias": [H], "ffn_up": [H, F], "ffn_up.bias": [F],
                      "ffn_down": [F, H], "ffn_down.bias": [H]}.get(kind, [H])
-        role = "gemm_b_host" if len(shape) == 2 and name != "frontend.position_embeddings" else \
-            ("embedding" if name.startswith("frontend.") else
-             ("layernorm" if ".ln" in name or name.startswith("layernorm") else "bias"))
+        if len(shape) == 2 and name != "frontend.position_embeddings":
+            _add_gemm_operand(w, name, np.asarray(arr, np.float32).reshape(shape), pretiled, i8,
+                              tile, mac, srng)
+            continue
+        role = "embedding" if name.startswith("frontend.") else \
+            ("layernorm" if ".ln" in name or name.startswith("layernorm") else "bias")
         w.add(name, arr, "F32", role, shape)
     w.add("classifier.weight", model.head_w, "F32", "gemm_b_host", [H, a.num_labels])
     w.add("classifier.bias", model.head_b, "F32", "bias", [a.num_labels])

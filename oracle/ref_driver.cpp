@@ -39,8 +39,7 @@
 #include "runtime/pool.hpp"
 #include "tokenizers/wordpiece.hpp"
 
-extern std::string nebw_oracle_b_layout_hash;  // oracle/ref_stub.cpp
-extern size_t nebw_oracle_a_elem_bytes;
+void nebw_oracle_describe_design(const npue::File &f);  // oracle/ref_stub.cpp
 
 namespace {
 void set_err(char *err, int32_t errlen, const char *msg) {
@@ -49,24 +48,6 @@ void set_err(char *err, int32_t errlen, const char *msg) {
   err[errlen - 1] = '\0';
 }
 
-// The stand-in design matches the container, as a design set exported for it
-// would: the operands' layout hash, and int8 operands for a_dtype "i8".
-void describe_design(const npue::File &f) {
-  std::string layout, a_dtype;
-  try {
-    layout = f.config_string("gemm_layout");
-  } catch (const std::exception &) {
-  }
-  try {
-    a_dtype = f.config_string("a_dtype");
-  } catch (const std::exception &) {
-  }
-  nebw_oracle_b_layout_hash.clear();
-  nebw_oracle_a_elem_bytes = 2;
-  if (layout == "host") return;
-  nebw_oracle_b_layout_hash = f.info("layer.0.qkv").layout_hash;
-  if (a_dtype == "i8") nebw_oracle_a_elem_bytes = 1;
-}
 }  // namespace
 
 extern "C" {
@@ -82,7 +63,7 @@ int nebw_ref_encode(const char *npue_path, int32_t seq, const int32_t *ids,
                     float *out, float *hidden_out, char *err, int32_t errlen) {
   try {
     npue::File f(npue_path);
-    describe_design(f);
+    nebw_oracle_describe_design(f);
     app::set_model_shape(f);
     app::set_design_seq(seq);
     app::Pool pool(threads > 0 ? threads : 1);
@@ -147,7 +128,7 @@ void *nebw_ref_session_open(const char *npue_path, int32_t seq, int32_t threads,
     // geometry globals first: the encoder's constructor and stage_all read them
     {
       npue::File probe(npue_path);
-      describe_design(probe);
+      nebw_oracle_describe_design(probe);
       app::set_model_shape(probe);
       app::set_design_seq(seq);
     }

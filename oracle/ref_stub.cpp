@@ -27,6 +27,7 @@
 
 #include "runtime/design.hpp"
 #include "runtime/device.hpp"
+#include "runtime/model.hpp"
 
 namespace {
 [[noreturn]] void unreachable(const char *what) {
@@ -52,6 +53,26 @@ Device::~Device() {}
 // stage_all load .wscale / .asmooth and the host GEMM divide A by .asmooth.
 std::string nebw_oracle_b_layout_hash;
 size_t nebw_oracle_a_elem_bytes = 2;
+
+// The stand-in design matches the container, as a design set exported for it
+// would: the operands' layout hash, and int8 operands for a_dtype "i8".
+// Called by the drivers before they build an encoder.
+void nebw_oracle_describe_design(const npue::File &f) {
+  std::string layout, a_dtype;
+  try {
+    layout = f.config_string("gemm_layout");
+  } catch (const std::exception &) {
+  }
+  try {
+    a_dtype = f.config_string("a_dtype");
+  } catch (const std::exception &) {
+  }
+  nebw_oracle_b_layout_hash.clear();
+  nebw_oracle_a_elem_bytes = 2;
+  if (layout == "host") return;
+  nebw_oracle_b_layout_hash = f.info("layer.0.qkv").layout_hash;
+  if (a_dtype == "i8" || a_dtype == "I8") nebw_oracle_a_elem_bytes = 1;  // BERT / ViT packers
+}
 
 namespace npu {
 

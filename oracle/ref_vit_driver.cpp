@@ -29,6 +29,8 @@
 #include "vit/encoder.hpp"
 #include "vit/geometry.hpp"
 
+void nebw_oracle_describe_design(const npue::File &f);  // oracle/ref_stub.cpp
+
 namespace {
 void set_err(char *err, int32_t errlen, const char *msg) {
   if (!err || errlen <= 0) return;
@@ -63,6 +65,7 @@ int nebw_ref_vit_encode(const char *npue_path, const float *images, int32_t n_im
                         int32_t errlen) {
   try {
     npue::File f(npue_path);
+    nebw_oracle_describe_design(f);
     const npue::vit::Geometry g = npue::vit::read_geometry(f, npue_path);
     app::Pool pool(threads > 0 ? threads : 1);
     npu::Device dev;
@@ -97,7 +100,8 @@ struct RefVitSession {
   npu::Design design;
   npue::vit::VitEncoder enc;
   RefVitSession(const char *path, int threads)
-      : f(path), g(npue::vit::read_geometry(f, path)), pool(threads > 0 ? threads : 1),
+      : f(path), g((nebw_oracle_describe_design(f), npue::vit::read_geometry(f, path))),
+        pool(threads > 0 ? threads : 1),
         design(dev, "oracle-host"), enc(f, design, pool, g) {
     npue::vit::EncoderStreams st;
     st.rows = g.n_pos;

@@ -34,6 +34,11 @@ shortest and longest rows are always included):
                      with .wscale / .asmooth), 8 rows through the reference's
                      host path on that container (host_b.hpp untiles it);
                      the container is regenerated (its SHA-256 is stored).
+  vit_pretiled_bf16_c5.npz, vit_pretiled_i8_c5.npz
+                     vit-base written by nebw.npue with pre-tiled encoder
+                     operands (bf16, or int8 with .wscale / .asmooth), the
+                     CLS rows of 2 images through the reference's ViT host
+                     path on that container; container SHA-256 stored.
   int8_steps.npz     the int8 datapath's host steps (host_kernels.hpp:
                      quantise_a_int8, dequantise_c with an int32 C,
                      dequant_act_quant with gelu8) on int8_step_inputs(), via
@@ -189,6 +194,39 @@ def make_pretiled(ref, name, key, a_dtype):
     print(f"{name}: {len(rows)} rows")
 
 
+VIT_PRETILED = {"vit_pretiled_bf16_c5": ("vit-base", "bf16"),
+                "vit_pretiled_i8_c5": ("vit-base", "i8")}
+
+
+def write_vit_pretiled(path, key: str, a_dtype: str) -> str:
+    from nebw.npue import write_vit_container
+    cfg = synth.VIT_CONFIGS[key]
+    write_vit_container(path, synth.vit_config_weights(cfg), gemm_layout="pretiled_bf16",
+                        a_dtype=a_dtype, tile=PRETILED_TILE, mac=PRETILED_MAC,
+                        smooth_seed=PRETILED_SMOOTH_SEED)
+    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
+
+
+def make_vit_pretiled(ref, name, key, a_dtype, n=2):
+    import tempfile
+    cfg = synth.VIT_CONFIGS[key]
+    w = synth.vit_config_weights(cfg)
+    images = synth.vit_config_images(cfg, n=n)
+    with tempfile.TemporaryDirectory(dir=HERE) as td:
+        path = Path(td) / "v.npue"
+        digest = write_vit_pretiled(path, key, a_dtype)
+        out = ref.vit_encode_container(path, images, hidden_size=w.arch.hidden,
+                                       n_pos=w.arch.n_pos)
+    np.savez_compressed(
+        HERE / f"{name}.npz", config=key, a_dtype=a_dtype, container_sha256=digest,
+        n_images=np.int32(n), image_sha256=hashlib.sha256(images.tobytes()).hexdigest(),
+        embeddings=out,
+        provenance="reference host-CPU ViT path on a pre-tiled container (host_b.hpp untile, "
+                   "int8 dequantised by .wscale with A scaled by 1/asmooth) via "
+                   "oracle/ref_vit_driver.cpp")
+    print(f"{name}: {n} images")
+
+
 def make_vit(ref, name, key, n):
     cfg = synth.VIT_CONFIGS[key]
     w = synth.vit_config_weights(cfg)
@@ -214,6 +252,9 @@ def main():
     for name, (key, a_dtype) in PRETILED.items():
         if not only or name in only:
             make_pretiled(ref, name, key, a_dtype)
+    for name, (key, a_dtype) in VIT_PRETILED.items():
+        if not only or name in only:
+            make_vit_pretiled(ref, name, key, a_dtype)
     for name, (key, n) in VIT_FIXTURES.items():
         if not only or name in only:
             make_vit(ref, name, key, n)

@@ -137,3 +137,30 @@ def test_vit_refuses_bad_geometry(device):
     h = C.c_void_p()
     rc = nebw.lib().nebw_vit_create(device.h, C.byref(cfg), C.byref(h))
     assert rc != 0 and b"patch" in nebw.lib().nebw_last_error()
+
+
+@pytest.mark.parametrize("name", ["vit_pretiled_bf16_c5", "vit_pretiled_i8_c5"])
+def test_vit_pretiled_containers_match_reference_golden(device, tmp_path, name):
+    """vit-base with pre-tiled encoder operands (the reference packer's
+    default form: bf16 block panels, or int8 with .wscale / .asmooth),
+    regenerated byte for byte, loaded by nebw_vit_load_npue and encoded on
+    the B200, against the reference's ViT host path on the same container."""
+    import hashlib
+    import sys
+
+    import nebw
+    from nebw import synth
+    sys.path.insert(0, str(REPO / "tests" / "golden"))
+    import make_golden
+    g = dict(np.load(REPO / "tests" / "golden" / f"{name}.npz"))
+    key, a_dtype = make_golden.VIT_PRETILED[name]
+    path = tmp_path / "v.npue"
+    assert make_golden.write_vit_pretiled(path, key, a_dtype) == str(g["container_sha256"])
+    images = synth.vit_config_images(synth.VIT_CONFIGS[key], n=int(g["n_images"]))
+    assert hashlib.sha256(images.tobytes()).hexdigest() == str(g["image_sha256"])
+    m = nebw.VitModel.from_npue(device, path)
+    try:
+        got = m.encode(images)
+    finally:
+        m.close()
+    check(got, g["embeddings"], name)

@@ -249,10 +249,13 @@ def test_pretiled_golden_containers_regenerate():
     """The containers behind tests/golden/pretiled_*.npz come back byte for
     byte from nebw.npue, so the GPU test reads what the reference read."""
     import make_golden
-    for name, (key, a_dtype) in make_golden.PRETILED.items():
+    cases = [(n, make_golden.write_pretiled, k, a) for n, (k, a) in make_golden.PRETILED.items()]
+    cases += [(n, make_golden.write_vit_pretiled, k, a)
+              for n, (k, a) in make_golden.VIT_PRETILED.items()]
+    for name, write, key, a_dtype in cases:
         g = np.load(GOLDEN / f"{name}.npz")
         with __import__("tempfile").TemporaryDirectory(dir=GOLDEN) as td:
-            digest = make_golden.write_pretiled(f"{td}/c.npue", key, a_dtype)
+            digest = write(f"{td}/c.npue", key, a_dtype)
         assert digest == str(g["container_sha256"]), name
 
 
