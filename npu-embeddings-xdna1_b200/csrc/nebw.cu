@@ -1671,8 +1671,18 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
           }
           std::vector<float> as(static_cast<size_t>(r));
           std::memcpy(as.data(), f.tensor(an).data, as.size() * 4);
-          for (int64_t k = 0; k < r; ++k)
-            for (int64_t j = 0; j < cc; ++j) kn[static_cast<size_t>(k * cc + j)] /= as[static_cast<size_t>(k)];
+          for (int64_t k = 0; k < r; ++k) {
+            const float a = as[static_cast<size_t>(k)];
+            if (!(a > 0.0f) || !std::isfinite(a)) {
+              // the reference would divide by it and carry inf / NaN into
+              // every row; refused by name instead
+              nebw_model_destroy(m);
+              return set_error(NEBW_EINVAL, "%s[%lld] = %g: SmoothQuant divisors must be "
+                               "positive and finite", an.c_str(), static_cast<long long>(k),
+                               static_cast<double>(a));
+            }
+            for (int64_t j = 0; j < cc; ++j) kn[static_cast<size_t>(k * cc + j)] /= a;
+          }
         }
         if (!rc) rc = nebw_model_set_tensor(m, n.c_str(), kn.data(), NEBW_F32, r, cc);
       } else if (nk_layout && gemm_operand) {
