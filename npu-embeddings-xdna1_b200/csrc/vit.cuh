@@ -435,8 +435,9 @@ extern "C" int nebw_vit_get_config(const nebw_vit *m, nebw_vit_config *cfg) {
   return NEBW_OK;
 }
 
+// The container is read and checked before the device is touched
+// (nebw_vit_create uses it), so a refused container is refused on any host.
 extern "C" int nebw_vit_load_npue(nebw_dev *d, const char *path, nebw_vit **out) {
-  if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(path && out, "null argument");
   *out = nullptr;
   try {

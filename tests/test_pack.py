@@ -303,3 +303,19 @@ def test_loader_refuses_int4_containers_without_a_gpu(tmp_path):
     h = C.c_void_p()
     assert nebw.lib().nebw_model_load_npue(None, str(path).encode(), C.byref(h)) == 1
     assert "a_dtype 'i4'" in nebw.lib().nebw_last_error().decode()
+
+
+def test_vit_loader_refuses_int4_containers_without_a_gpu(tmp_path):
+    import ctypes as C
+
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_vit_container
+    w = synth.vit_config_weights(synth.VIT_CONFIGS["vit-base"], layers=1)
+    path = tmp_path / "v.npue"
+    write_vit_container(path, w, gemm_layout="pretiled_bf16", a_dtype="bf16")
+    raw = path.read_bytes().replace(b'"a_dtype":"BF16"', b'"a_dtype":"I4__"', 1)
+    path.write_bytes(raw)
+    h = C.c_void_p()
+    assert nebw.lib().nebw_vit_load_npue(None, str(path).encode(), C.byref(h)) == 1
+    assert "a_dtype 'i4__'" in nebw.lib().nebw_last_error().decode()
