@@ -290,11 +290,18 @@ int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K_COUNT],
  * GPU under a fixed partition.  (nebw_encode_device may cudaMalloc a larger
  * workspace the first time it sees a larger batch.)  All intermediates live
  * in one static 64 MiB device array that every GPU loading the library holds
- * until exit; a batch whose B * S padded rows do not fit it is refused with
- * NEBW_EINVAL (for bge-large, 2520 rows fit).  The first call on a device
- * looks the array's address up and should come before any stream capture.
- * All calls share the array: calls that overlap on the GPU race, so the
- * caller serialises them.  Arguments and results as nebw_encode_device. */
+ * until exit.  A batch needs B * S * (16 * hidden + 2 * F) bytes of it (F the
+ * FFN width; 2F for a gated FFN without CTA pairs; plus 4 per row for a
+ * rotary head_dim-64 model), plus about 12 * B + B * S / 32 bytes and up to
+ * 2.5 KB of alignment; a batch that does not fit is refused with NEBW_EINVAL
+ * (bge-large: about 2730 padded rows fit; MiniLM: about 7280).  The first
+ * call on a device looks the array's address up and should come before any
+ * stream capture.  All calls share the array and it keeps the last call's
+ * contents (a pass clears what it reads before writing it): calls that
+ * overlap on the GPU race, so the caller serialises them.  The pass launches
+ * the same kernels as nebw_encode_device and returns the same bits; static
+ * calls record no per-kernel profiling events.  Arguments and results as
+ * nebw_encode_device. */
 int nebw_encode_device_static(nebw_model *m, const int32_t *ids_dev, const int32_t *lens_dev,
                               int32_t B, int32_t S, float *out_dev, void *stream);
 

@@ -1,11 +1,12 @@
-"""Single-kernel timing through the C ABI, for tuning and for profiler runs.
+"""Single-kernel timing through the C ABI, for tuning and for profiler runs
+(the commands behind the profiles/ summaries; not part of the library).
 
-    python -m nebw.kernel_bench gemm --M 16384 --K 1024 --N 4096 --epi gelu8
-    python -m nebw.kernel_bench attention --B 64 --len 512 --heads 16 --hd 64
-    python -m nebw.kernel_bench layernorm --M 131072 --H 1024
-    python -m nebw.kernel_bench encoder --config bge-large --layers 1
+    python kernel_bench.py gemm --M 16384 --K 1024 --N 4096 --epi gelu8
+    python kernel_bench.py attention --B 64 --len 512 --heads 16 --hd 64
+    python kernel_bench.py layernorm --M 131072 --H 1024
+    python kernel_bench.py encoder --config bge-large --layers 1
 
-(run with npu-embeddings-xdna1_b200/ on sys.path).  Each case runs a few
+Each case runs a few
 warm-up launches and then times --iters launches with CUDA events on the
 launching stream, printing one JSON line with the per-launch time and the
 achieved TFLOP/s or GB/s.  Operand buffers are sized so that, across the
@@ -16,8 +17,12 @@ from __future__ import annotations
 
 import argparse
 import json
+import sys
+from pathlib import Path
 
 import numpy as np
+
+sys.path.insert(0, str(Path(__file__).resolve().parent / "npu-embeddings-xdna1_b200"))
 
 
 def _bits(a):

@@ -72,7 +72,7 @@ def build_oracle(verbose: bool = False):
     if not make:
         raise FileNotFoundError("make not found")
     subprocess.run([make, "-s", "-C", str(REPO / "oracle"), "port"], check=True)
-    ref = Path(os.environ.get("NEBW_REFERENCE", "/root/reference"))
+    ref = Path(os.environ.get("NEBW_REFERENCE", str(REPO.parent / "reference")))
     if (ref / "runtime" / "src" / "encoders" / "bert_encoder.cpp").exists():
         subprocess.run([make, "-s", "-j8", "-C", str(REPO / "oracle"), "ref", f"REF={ref}"],
                        check=True)

@@ -1,9 +1,10 @@
-// BERT WordPiece for the host tools -- see wordpiece.hpp.
+// BERT WordPiece for the host tools: a pretokenizer over code points and a
+// vocabulary trie (see wordpiece.hpp for the pipeline).
 #include "wordpiece.hpp"
 
 #include <algorithm>
 #include <fstream>
-#include <sstream>
+#include <iterator>
 #include <stdexcept>
 
 namespace nebw {
@@ -18,259 +19,320 @@ struct FoldEntry {
 
 #include "bert_unicode.inc"
 
-bool in_ranges(uint32_t cp, const CpRange *r, int n) {
-  const CpRange *it =
-      std::upper_bound(r, r + n, cp, [](uint32_t v, const CpRange &x) { return v < x.lo; });
-  return it != r && cp <= (it - 1)->hi;
+// ---- Unicode classes (tables generated from unicodedata) -------------------
+
+bool in_table(char32_t cp, const CpRange *table, int n) {
+  int lo = 0, hi = n - 1;  // binary search over sorted, disjoint ranges
+  while (lo <= hi) {
+    const int mid = (lo + hi) / 2;
+    if (cp < table[mid].lo)
+      hi = mid - 1;
+    else if (cp > table[mid].hi)
+      lo = mid + 1;
+    else
+      return true;
+  }
+  return false;
 }
 
-bool is_cjk(uint32_t cp) {  // the Han blocks of BasicTokenizer._is_chinese_char
-  return (cp >= 0x4E00 && cp <= 0x9FFF) || (cp >= 0x3400 && cp <= 0x4DBF) ||
-         (cp >= 0x20000 && cp <= 0x2A6DF) || (cp >= 0x2A700 && cp <= 0x2B73F) ||
-         (cp >= 0x2B740 && cp <= 0x2B81F) || (cp >= 0x2B820 && cp <= 0x2CEAF) ||
-         (cp >= 0xF900 && cp <= 0xFAFF) || (cp >= 0x2F800 && cp <= 0x2FA1F);
+bool is_control(char32_t cp) { return in_table(cp, kControl, kControl_n); }
+bool is_space(char32_t cp) { return in_table(cp, kSpace, kSpace_n); }
+bool is_punct(char32_t cp) { return in_table(cp, kPunct, kPunct_n); }
+
+// The CJK ideograph blocks HuggingFace's BasicTokenizer isolates
+// (_is_chinese_char): the Unified Ideographs, Extensions A-E and the
+// Compatibility Ideographs (and Supplement).  Kana and Hangul are not among
+// them.
+bool is_han(char32_t cp) {
+  static constexpr CpRange kHan[] = {{0x3400, 0x4DBF},   {0x4E00, 0x9FFF},   {0xF900, 0xFAFF},
+                                     {0x20000, 0x2A6DF}, {0x2A700, 0x2B73F}, {0x2B740, 0x2B81F},
+                                     {0x2B820, 0x2CEAF}, {0x2F800, 0x2FA1F}};
+  return in_table(cp, kHan, static_cast<int>(std::size(kHan)));
 }
 
-// lower(), NFD, Mn marks dropped -- appended to `out`
-void fold(uint32_t cp, std::vector<uint32_t> &out) {
-  if (cp >= 0xAC00 && cp <= 0xD7A3) {  // Hangul syllable: L V (T) jamo
-    const uint32_t s = cp - 0xAC00;
-    out.push_back(0x1100 + s / 588);
-    out.push_back(0x1161 + (s % 588) / 28);
-    if (s % 28) out.push_back(0x11A7 + s % 28);
+// Lower case, canonical decomposition and removal of nonspacing marks, one
+// code point at a time, appended to `out`.
+void fold_into(char32_t cp, std::u32string &out) {
+  constexpr char32_t kSBase = 0xAC00, kLBase = 0x1100, kVBase = 0x1161, kTBase = 0x11A7;
+  constexpr char32_t kVCount = 21, kTCount = 28, kSCount = 19 * kVCount * kTCount;
+  if (cp >= kSBase && cp < kSBase + kSCount) {  // Hangul syllable -> L V (T) jamo
+    const char32_t s = cp - kSBase;
+    out += kLBase + s / (kVCount * kTCount);
+    out += kVBase + (s % (kVCount * kTCount)) / kTCount;
+    if (s % kTCount) out += kTBase + s % kTCount;
     return;
   }
-  const FoldEntry *it = std::lower_bound(
-      kFold, kFold + kFold_n, cp, [](const FoldEntry &e, uint32_t v) { return e.cp < v; });
-  if (it != kFold + kFold_n && it->cp == cp) {
-    for (uint32_t k = 0; k < it->len; ++k) out.push_back(kFoldData[it->off + k]);
-  } else {
-    out.push_back(cp);
+  int lo = 0, hi = kFold_n - 1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) / 2;
+    if (cp < kFold[mid].cp) {
+      hi = mid - 1;
+    } else if (cp > kFold[mid].cp) {
+      lo = mid + 1;
+    } else {
+      out.append(kFoldData + kFold[mid].off, kFoldData + kFold[mid].off + kFold[mid].len);
+      return;
+    }
   }
+  out += cp;
 }
 
-// Lenient UTF-8: a byte that does not start a well-formed sequence decodes
-// to U+FFFD on its own (the clean step then drops it).
-std::vector<uint32_t> decode(const std::string &s) {
-  std::vector<uint32_t> out;
-  out.reserve(s.size());
-  const size_t n = s.size();
-  for (size_t i = 0; i < n;) {
-    const unsigned char c = static_cast<unsigned char>(s[i]);
-    int len;
-    uint32_t cp;
-    if (c < 0x80) len = 1, cp = c;
-    else if ((c & 0xE0) == 0xC0) len = 2, cp = c & 0x1Fu;
-    else if ((c & 0xF0) == 0xE0) len = 3, cp = c & 0x0Fu;
-    else if ((c & 0xF8) == 0xF0) len = 4, cp = c & 0x07u;
-    else len = 0, cp = 0;
-    bool ok = len > 0 && i + len <= n;
-    for (int k = 1; ok && k < len; ++k) {
-      const unsigned char cc = static_cast<unsigned char>(s[i + k]);
-      ok = (cc & 0xC0) == 0x80;
-      cp = (cp << 6) | (cc & 0x3Fu);
+// ---- UTF-8 ------------------------------------------------------------------
+
+// Bytes of the sequence a lead byte starts (1-4), 0 for a byte that starts
+// none (a continuation byte, or 0xF8-0xFF).
+int lead_span(unsigned char b) {
+  if (b < 0x80) return 1;
+  if (b < 0xC0 || b >= 0xF8) return 0;
+  return b < 0xE0 ? 2 : (b < 0xF0 ? 3 : 4);
+}
+
+// Lenient decoding: a byte that does not start a complete sequence of
+// continuation bytes stands for U+FFFD on its own and decoding resumes at
+// the next byte.  (Overlong forms and surrogates are decoded as written.)
+std::u32string decode_utf8(const char *p, size_t n) {
+  std::u32string out;
+  out.reserve(n);
+  size_t i = 0;
+  while (i < n) {
+    const unsigned char b = static_cast<unsigned char>(p[i]);
+    const int span = lead_span(b);
+    bool whole = span > 0 && i + static_cast<size_t>(span) <= n;
+    char32_t cp = span > 1 ? b & (0x7Fu >> span) : b;
+    for (int k = 1; whole && k < span; ++k) {
+      const unsigned char c = static_cast<unsigned char>(p[i + static_cast<size_t>(k)]);
+      whole = (c >> 6) == 2;
+      cp = (cp << 6) | (c & 0x3Fu);
     }
-    if (!ok) {
-      out.push_back(0xFFFD);
-      ++i;
-      continue;
+    if (whole) {
+      out += cp;
+      i += static_cast<size_t>(span);
+    } else {
+      out += char32_t{0xFFFD};
+      i += 1;
     }
-    out.push_back(cp);
-    i += static_cast<size_t>(len);
   }
   return out;
 }
 
-void encode_utf8(uint32_t cp, std::string &s) {
+void append_utf8(char32_t cp, std::string &s) {
   if (cp < 0x80) {
-    s.push_back(static_cast<char>(cp));
-  } else if (cp < 0x800) {
-    s.push_back(static_cast<char>(0xC0 | (cp >> 6)));
-    s.push_back(static_cast<char>(0x80 | (cp & 0x3F)));
-  } else if (cp < 0x10000) {
-    s.push_back(static_cast<char>(0xE0 | (cp >> 12)));
-    s.push_back(static_cast<char>(0x80 | ((cp >> 6) & 0x3F)));
-    s.push_back(static_cast<char>(0x80 | (cp & 0x3F)));
-  } else {
-    s.push_back(static_cast<char>(0xF0 | (cp >> 18)));
-    s.push_back(static_cast<char>(0x80 | ((cp >> 12) & 0x3F)));
-    s.push_back(static_cast<char>(0x80 | ((cp >> 6) & 0x3F)));
-    s.push_back(static_cast<char>(0x80 | (cp & 0x3F)));
+    s += static_cast<char>(cp);
+    return;
   }
+  const int tail = cp < 0x800 ? 1 : (cp < 0x10000 ? 2 : 3);
+  static constexpr unsigned char kLead[4] = {0, 0xC0, 0xE0, 0xF0};
+  s += static_cast<char>(kLead[tail] | (cp >> (6 * tail)));
+  for (int k = tail - 1; k >= 0; --k) s += static_cast<char>(0x80 | ((cp >> (6 * k)) & 0x3F));
 }
 
-constexpr size_t kMaxPieceChars = 100;
+// ---- pretokenizer -------------------------------------------------------------
+
+constexpr size_t kMaxWordChars = 100;  // longer words are [UNK] whole
+
+// Code points in, words out: `emit` receives each folded, punctuation-split
+// word in order.
+template <typename Emit>
+void pretokenize(const std::u32string &text, Emit emit) {
+  std::u32string raw, folded, piece;
+  auto finish_raw = [&]() {
+    if (raw.empty()) return;
+    folded.clear();
+    for (char32_t cp : raw) fold_into(cp, folded);
+    raw.clear();
+    piece.clear();
+    for (char32_t cp : folded) {
+      if (!is_punct(cp)) {
+        piece += cp;
+        continue;
+      }
+      if (!piece.empty()) emit(piece);
+      piece.assign(1, cp);
+      emit(piece);
+      piece.clear();
+    }
+    if (!piece.empty()) emit(piece);
+  };
+  for (char32_t cp : text) {
+    if (cp == 0 || cp == 0xFFFD || is_control(cp)) continue;
+    if (is_space(cp)) {
+      finish_raw();
+    } else if (is_han(cp)) {
+      finish_raw();
+      raw.assign(1, cp);
+      finish_raw();
+    } else {
+      raw += cp;
+    }
+  }
+  finish_raw();
+}
 
 }  // namespace
 
+// ---- vocabulary --------------------------------------------------------------
+
 WordPiece WordPiece::from_vocab_file(const std::string &path) {
   std::ifstream f(path, std::ios::binary);
-  if (!f) throw std::runtime_error("tokenizer: cannot open " + path);
-  std::stringstream ss;
-  ss << f.rdbuf();
-  WordPiece t;
-  t.index(ss.str());
-  return t;
+  if (!f) throw std::runtime_error("WordPiece vocabulary file could not be opened: " + path);
+  std::string blob((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  return WordPiece(blob);
 }
 
 WordPiece WordPiece::from_vocab_bytes(const char *data, size_t bytes) {
-  WordPiece t;
-  t.index(std::string(data, bytes));
-  return t;
+  return WordPiece(std::string(data, bytes));
 }
 
-// One token per line, id = line number; a trailing '\r' is not part of it.
-void WordPiece::index(const std::string &blob) {
-  size_t at = 0;
-  while (at < blob.size()) {
-    size_t nl = blob.find('\n', at);
-    if (nl == std::string::npos) nl = blob.size();
-    std::string tok = blob.substr(at, nl - at);
-    if (!tok.empty() && tok.back() == '\r') tok.pop_back();
-    id_.emplace(tok, static_cast<int32_t>(tokens_.size()));
-    tokens_.push_back(std::move(tok));
-    at = nl + 1;
+int32_t WordPiece::child(int32_t node, char32_t cp) const {
+  const auto it = edges_.find((static_cast<uint64_t>(node) << 21) | cp);
+  return it == edges_.end() ? -1 : it->second;
+}
+
+int32_t WordPiece::add_child(int32_t node, char32_t cp) {
+  const uint64_t key = (static_cast<uint64_t>(node) << 21) | cp;
+  const auto it = edges_.find(key);
+  if (it != edges_.end()) return it->second;
+  const int32_t n = static_cast<int32_t>(node_token_.size());
+  node_token_.push_back(-1);
+  edges_.emplace(key, n);
+  return n;
+}
+
+// The blob holds one entry per '\n'-terminated line (a final line without
+// '\n' counts; one trailing '\r' is not part of an entry); entry k has id k,
+// and a repeated entry keeps its first id.
+WordPiece::WordPiece(const std::string &blob) {
+  for (size_t at = 0; at < blob.size();) {
+    size_t end = blob.find('\n', at);
+    if (end == std::string::npos) end = blob.size();
+    size_t stop = end;
+    if (stop > at && blob[stop - 1] == '\r') --stop;
+    vocab_.emplace_back(blob, at, stop - at);
+    ids_.emplace(vocab_.back(), static_cast<int32_t>(vocab_.size() - 1));
+    at = end + 1;
   }
-  if (tokens_.empty()) throw std::runtime_error("tokenizer: empty vocabulary");
-  auto need = [&](const char *t) {
-    auto it = id_.find(t);
-    if (it == id_.end()) throw std::runtime_error(std::string("tokenizer: vocabulary has no ") + t);
+  if (vocab_.empty()) throw std::runtime_error("WordPiece vocabulary is empty");
+  auto special = [&](const char *name) {
+    const auto it = ids_.find(name);
+    if (it == ids_.end())
+      throw std::runtime_error(std::string("WordPiece vocabulary lacks the special token ") + name);
     return it->second;
   };
-  cls_id = need("[CLS]");
-  sep_id = need("[SEP]");
-  pad_id = need("[PAD]");
-  unk_id = need("[UNK]");
-  for (const char *s : {"[CLS]", "[SEP]", "[PAD]", "[UNK]", "[MASK]"})
-    if (id_.count(s)) specials_.emplace_back(s);
-  std::stable_sort(specials_.begin(), specials_.end(),
-                   [](const std::string &a, const std::string &b) { return a.size() > b.size(); });
+  cls_id = special("[CLS]");
+  sep_id = special("[SEP]");
+  pad_id = special("[PAD]");
+  unk_id = special("[UNK]");
+  for (const char *name : {"[MASK]", "[CLS]", "[SEP]", "[PAD]", "[UNK]"}) {  // longest first
+    const auto it = ids_.find(name);
+    if (it != ids_.end()) specials_.emplace_back(name, it->second);
+  }
+
+  // The tries.  A word's pieces are canonical UTF-8 of their code points, so
+  // an entry whose bytes are not the canonical encoding of what they decode
+  // to can never match one and is left out.
+  node_token_ = {-1, -1};
+  auto insert = [&](int32_t root, const char *p, size_t n, int32_t id) {
+    const std::u32string cps = decode_utf8(p, n);
+    std::string back;
+    for (char32_t cp : cps) append_utf8(cp, back);
+    if (back.size() != n || back.compare(0, n, p, n) != 0) return;
+    int32_t node = root;
+    for (char32_t cp : cps) node = add_child(node, cp);
+    if (node_token_[static_cast<size_t>(node)] < 0) node_token_[static_cast<size_t>(node)] = id;
+  };
+  for (size_t id = 0; id < vocab_.size(); ++id) {
+    const std::string &e = vocab_[id];
+    insert(0, e.data(), e.size(), static_cast<int32_t>(id));
+    if (e.size() >= 2 && e[0] == '#' && e[1] == '#')
+      insert(1, e.data() + 2, e.size() - 2, static_cast<int32_t>(id));
+  }
 }
 
 int32_t WordPiece::id_of(const std::string &token) const {
-  auto it = id_.find(token);
-  return it == id_.end() ? unk_id : it->second;
+  const auto it = ids_.find(token);
+  return it == ids_.end() ? unk_id : it->second;
 }
 
-// Special tokens in the raw text are kept whole: the text is cut at the
-// earliest one (the longer one on a tie) and the parts around it tokenized.
-std::vector<std::string> WordPiece::tokenize(const std::string &text) const {
-  std::vector<std::string> out;
-  size_t from = 0;
-  while (true) {
-    size_t best = std::string::npos;
-    const std::string *which = nullptr;
-    for (const auto &s : specials_) {
-      const size_t p = text.find(s, from);
-      if (p != std::string::npos && (best == std::string::npos || p < best)) {
-        best = p;
-        which = &s;
-      }
-    }
-    if (!which) break;
-    auto head = tokenize_text(text.substr(from, best - from));
-    out.insert(out.end(), head.begin(), head.end());
-    out.push_back(*which);
-    from = best + which->size();
-  }
-  auto tail = tokenize_text(text.substr(from));
-  out.insert(out.end(), tail.begin(), tail.end());
-  return out;
-}
+// ---- tokenization ---------------------------------------------------------------
 
-void WordPiece::wordpiece(const std::vector<uint32_t> &piece,
-                          std::vector<std::string> &out) const {
-  if (piece.size() > kMaxPieceChars) {
-    out.push_back("[UNK]");
+// Greedy longest match: from each position the longest entry of the trie
+// (whole entries at the word's start, "##" continuations after it); a word
+// with a position where nothing matches is one [UNK].
+void WordPiece::word_ids(const std::u32string &word, std::vector<int32_t> &out) const {
+  if (word.size() > kMaxWordChars) {
+    out.push_back(unk_id);
     return;
   }
-  std::string flat;
-  std::vector<size_t> byte_at(piece.size() + 1);
-  for (size_t i = 0; i < piece.size(); ++i) {
-    byte_at[i] = flat.size();
-    encode_utf8(piece[i], flat);
-  }
-  byte_at[piece.size()] = flat.size();
-  std::vector<std::string> sub;
-  for (size_t start = 0; start < piece.size();) {
-    size_t end = piece.size();
-    std::string hit;
-    for (; end > start; --end) {
-      std::string s = flat.substr(byte_at[start], byte_at[end] - byte_at[start]);
-      if (start > 0) s.insert(0, "##");
-      if (id_.count(s)) {
-        hit = std::move(s);
-        break;
+  const size_t mark = out.size();
+  for (size_t start = 0; start < word.size();) {
+    int32_t node = start == 0 ? 0 : 1, hit = -1;
+    size_t hit_end = start;
+    for (size_t k = start; k < word.size(); ++k) {
+      node = child(node, word[k]);
+      if (node < 0) break;
+      if (node_token_[static_cast<size_t>(node)] >= 0) {
+        hit = node_token_[static_cast<size_t>(node)];
+        hit_end = k + 1;
       }
     }
-    if (hit.empty()) {
-      out.push_back("[UNK]");
+    if (hit < 0) {
+      out.resize(mark);
+      out.push_back(unk_id);
       return;
     }
-    sub.push_back(std::move(hit));
-    start = end;
+    out.push_back(hit);
+    start = hit_end;
   }
-  out.insert(out.end(), sub.begin(), sub.end());
 }
 
-std::vector<std::string> WordPiece::tokenize_text(const std::string &text) const {
-  std::vector<uint32_t> clean;
-  for (uint32_t cp : decode(text)) {
-    if (cp == 0 || cp == 0xFFFD || in_ranges(cp, kControl, kControl_n)) continue;
-    if (in_ranges(cp, kSpace, kSpace_n)) {
-      clean.push_back(' ');
-    } else if (is_cjk(cp)) {
-      clean.push_back(' ');
-      clean.push_back(cp);
-      clean.push_back(' ');
-    } else {
-      clean.push_back(cp);
-    }
-  }
-  std::vector<std::string> out;
-  std::vector<uint32_t> word, folded, piece;
-  auto flush = [&]() {
-    if (word.empty()) return;
-    folded.clear();
-    for (uint32_t cp : word) fold(cp, folded);
-    piece.clear();
-    for (uint32_t cp : folded) {
-      if (in_ranges(cp, kPunct, kPunct_n)) {
-        if (!piece.empty()) wordpiece(piece, out);
-        piece.assign(1, cp);
-        wordpiece(piece, out);
-        piece.clear();
-      } else {
-        piece.push_back(cp);
-      }
-    }
-    if (!piece.empty()) wordpiece(piece, out);
-    word.clear();
+// Special tokens written in the text stay whole: at each byte position the
+// longest special that starts there is taken, and the text between specials
+// is pretokenized.
+void WordPiece::piece_ids(const std::string &text, std::vector<int32_t> &out) const {
+  auto plain = [&](size_t from, size_t to) {
+    if (to <= from) return;
+    pretokenize(decode_utf8(text.data() + from, to - from),
+                [&](const std::u32string &w) { word_ids(w, out); });
   };
-  for (uint32_t cp : clean) {
-    if (cp == ' ')
-      flush();
-    else
-      word.push_back(cp);
+  size_t from = 0;
+  for (size_t i = 0; i < text.size(); ++i) {
+    if (text[i] != '[') continue;  // every special token starts with '['
+    for (const auto &s : specials_) {
+      if (text.compare(i, s.first.size(), s.first) != 0) continue;
+      plain(from, i);
+      out.push_back(s.second);
+      from = i + s.first.size();
+      i = from - 1;
+      break;
+    }
   }
-  flush();
+  plain(from, text.size());
+}
+
+std::vector<std::string> WordPiece::tokenize(const std::string &text) const {
+  std::vector<int32_t> ids;
+  piece_ids(text, ids);
+  std::vector<std::string> out;
+  out.reserve(ids.size());
+  for (int32_t id : ids) out.push_back(vocab_[static_cast<size_t>(id)]);
   return out;
 }
 
 Tokens WordPiece::encode(const std::string &text, int max_len) const {
-  if (max_len < 2) throw std::runtime_error("tokenizer: max_len below 2 cannot hold [CLS] [SEP]");
-  const std::vector<std::string> toks = tokenize(text);
-  const size_t take = std::min(toks.size(), static_cast<size_t>(max_len - 2));
+  if (max_len < 2)
+    throw std::runtime_error("WordPiece: a sequence length below 2 cannot hold [CLS] and [SEP]");
+  std::vector<int32_t> pieces;
+  piece_ids(text, pieces);
+  const size_t room = static_cast<size_t>(max_len) - 2, kept = std::min(pieces.size(), room);
   Tokens t;
-  t.ids.reserve(static_cast<size_t>(max_len));
-  t.ids.push_back(cls_id);
-  for (size_t i = 0; i < take; ++i) t.ids.push_back(id_of(toks[i]));
-  t.ids.push_back(sep_id);
-  t.n_tokens = static_cast<int32_t>(t.ids.size());
-  t.truncated = take < toks.size();
-  t.mask.assign(t.ids.size(), 1);
-  t.ids.resize(static_cast<size_t>(max_len), pad_id);
-  t.mask.resize(static_cast<size_t>(max_len), 0);
+  t.truncated = pieces.size() > room;
+  t.n_tokens = static_cast<int32_t>(kept + 2);
+  t.ids.assign(static_cast<size_t>(max_len), pad_id);
+  t.mask.assign(static_cast<size_t>(max_len), 0);
+  t.ids[0] = cls_id;
+  std::copy(pieces.begin(), pieces.begin() + static_cast<std::ptrdiff_t>(kept), t.ids.begin() + 1);
+  t.ids[kept + 1] = sep_id;
+  std::fill(t.mask.begin(), t.mask.begin() + static_cast<std::ptrdiff_t>(kept + 2), 1);
   return t;
 }
 

@@ -1,25 +1,28 @@
-// BERT WordPiece tokenizer for the host tools: text -> [CLS] ids [SEP] + pad,
-// the attention mask, as the runtime's tokenizer produces them for the
-// embedding models (npue::WordPiece, runtime/include/tokenizers/wordpiece.hpp,
-// runtime/src/tokenizers/wordpiece.cpp).  Same pipeline, in HuggingFace
-// BasicTokenizer order:
+// BERT WordPiece tokenizer for the host tools: text -> [CLS] ids [SEP] + pad
+// and the attention mask, with the output contract of the runtime's tokenizer
+// for the embedding models (npue::WordPiece, runtime/include/tokenizers/
+// wordpiece.hpp).  The algorithm is HuggingFace's BertTokenizer
+// (BasicTokenizer with do_lower_case and tokenize_chinese_chars, then
+// WordpieceTokenizer with max_input_chars_per_word = 100), written here as
+// two stages:
 //
-//   clean      drop U+0000, U+FFFD and control characters; whitespace -> ' '
-//   CJK        Han ideographs padded with spaces (one token each); Hiragana,
-//              Katakana and Hangul are not "CJK" in this sense
-//   split      on spaces
-//   fold       per code point: lower(), NFD, drop Mn marks (one table lookup;
-//              Hangul syllables decomposed arithmetically)
-//   punct      every punctuation code point its own token
-//   wordpiece  greedy longest match first, "##" continuations, a piece with
-//              no match (or longer than 100 code points) becomes [UNK]
-//   specials   [CLS] [SEP] [PAD] [UNK] [MASK] in the raw text stay single
-//              tokens
+//   Pretokenizer  UTF-8 -> code points -> words: U+0000, U+FFFD and control
+//                 characters dropped, whitespace separates words, each Han
+//                 ideograph is a word of its own, each code point of a word
+//                 is folded (lower case, canonical decomposition, nonspacing
+//                 marks removed; one table lookup, Hangul syllables
+//                 decomposed arithmetically), and every punctuation code
+//                 point splits off as a word of its own.
+//   PieceTrie     the vocabulary as two code-point tries -- whole entries,
+//                 and the "##" continuation entries without their prefix --
+//                 walked for the longest entry at each position of a word;
+//                 a word with a position nothing matches, or longer than 100
+//                 code points, becomes [UNK].
 //
-// encode(): [CLS] + the first max_len - 2 tokens + [SEP], then [PAD] up to
-// max_len; mask 1 on the real positions.  Invalid UTF-8 bytes decode to
-// U+FFFD and are dropped.  The Unicode tables (bert_unicode.inc) are
-// generated from Python's unicodedata by gen_unicode_tables.py.
+// Special tokens ([CLS] [SEP] [PAD] [UNK] [MASK], those the vocabulary has)
+// written in the raw text are kept whole.  The Unicode tables
+// (bert_unicode.inc) are generated from Python's unicodedata by
+// gen_unicode_tables.py.
 #pragma once
 
 #include <cstdint>
@@ -40,21 +43,29 @@ class WordPiece {
   static WordPiece from_vocab_file(const std::string &path);
   static WordPiece from_vocab_bytes(const char *data, size_t bytes);
 
+  // The pieces of `text` (no [CLS] / [SEP]), as vocabulary strings.
   std::vector<std::string> tokenize(const std::string &text) const;
+  // [CLS] + the first max_len - 2 pieces + [SEP], then [PAD] up to max_len.
   Tokens encode(const std::string &text, int max_len) const;
   int32_t id_of(const std::string &token) const;
-  size_t vocab_size() const { return tokens_.size(); }
+  size_t vocab_size() const { return vocab_.size(); }
 
   int32_t cls_id = -1, sep_id = -1, pad_id = -1, unk_id = -1;
 
  private:
-  void index(const std::string &blob);
-  std::vector<std::string> tokenize_text(const std::string &text) const;
-  void wordpiece(const std::vector<uint32_t> &piece, std::vector<std::string> &out) const;
+  explicit WordPiece(const std::string &blob);
+  void piece_ids(const std::string &text, std::vector<int32_t> &out) const;
+  void word_ids(const std::u32string &word, std::vector<int32_t> &out) const;
+  int32_t child(int32_t node, char32_t cp) const;
+  int32_t add_child(int32_t node, char32_t cp);
 
-  std::vector<std::string> tokens_;
-  std::unordered_map<std::string, int32_t> id_;
-  std::vector<std::string> specials_;  // longest first
+  std::vector<std::string> vocab_;                // id -> entry
+  std::unordered_map<std::string, int32_t> ids_;  // entry -> first id
+  // trie over code points: node 0 roots whole entries, node 1 the "##"
+  // continuations; edges keyed by (node << 21) | code point
+  std::unordered_map<uint64_t, int32_t> edges_;
+  std::vector<int32_t> node_token_;           // entry id ending at a node, or -1
+  std::vector<std::pair<std::string, int32_t>> specials_;  // longest first
 };
 
 }  // namespace nebw

@@ -1,3 +1,4 @@
+import os
 import sys
 from pathlib import Path
 
@@ -9,7 +10,9 @@ for p in (str(PKG), str(REPO)):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-REFERENCE = Path("/root/reference")
+# the reference tree (read-only; present only where the reference is checked
+# out): $NEBW_REFERENCE, else a checkout beside this repository
+REFERENCE = Path(os.environ.get("NEBW_REFERENCE", str(REPO.parent / "reference")))
 
 
 def pytest_configure(config):

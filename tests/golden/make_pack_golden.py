@@ -21,6 +21,7 @@ tests/test_pack.py packs the same checkpoint with nebw.pack and compares.
 from __future__ import annotations
 
 import hashlib
+import os
 import json
 import sys
 import tempfile
@@ -112,7 +113,8 @@ def describe(path) -> dict:
         return {"config": r.config, "tensors": tensors, "order": list(r.entries)}
 
 
-REFERENCE = Path("/root/reference")
+# the reference tree: $NEBW_REFERENCE, else a checkout beside this repository
+REFERENCE = Path(os.environ.get("NEBW_REFERENCE", str(REPO.parent / "reference")))
 
 
 def reference_pack(workdir, dtype: str, extra=()) -> Path:
