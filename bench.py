@@ -48,7 +48,6 @@ sys.path.insert(0, str(PKG))
 sys.path.insert(0, str(REPO))
 
 from nebw import synth  # noqa: E402
-from nebw.shard import gather_to_root, plan_shards, unpermute  # noqa: E402
 
 METRIC = "embeddings/sec at bge-large seq512"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -148,6 +147,74 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
+# ranks (N > 1): the data path is libnebw's own NCCL communicator
+# ---------------------------------------------------------------------------
+
+class Ranks:
+    """One process per GPU.  torch.distributed runs over gloo, on the host
+    only: barriers, the max of the per-rank timings, and handing rank 0's
+    communicator id to the others.  The sharded pass and the gather of the
+    embeddings go through libnebw (nebw_comm_init_rank,
+    nebw_encode_shard_gather / nebw_encode_sharded over NCCL)."""
+
+    def __init__(self, dev, world: int, rank: int):
+        import torch.distributed as dist
+
+        import nebw
+        self.world, self.rank, self.dist = world, rank, dist
+        self.comm = None
+        if world > 1:
+            from datetime import timedelta
+            dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+            box = [nebw.comm_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            self.comm = nebw.Comm.init_rank(dev, world, rank, box[0], timeout_s=120.0)
+
+    def barrier(self):
+        import torch
+        if self.comm is not None:
+            self.comm.sync(stream=torch.cuda.current_stream())
+        if self.world > 1:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, x: float) -> float:
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        if self.world > 1:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_gather(self, row):
+        import torch
+        t = torch.tensor([row], dtype=torch.float64)
+        if self.world == 1:
+            return [t]
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t)
+        return out
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+# ---------------------------------------------------------------------------
 # the CPU arms
 # ---------------------------------------------------------------------------
 
@@ -176,28 +243,45 @@ def pick_sample(lens, n):
     return np.array(sorted(idx))[:n]
 
 
-def run_cpu_baseline(cfg, w, ids, mask, lens, budget_s=15.0):
+CPU_METHOD = ("the reference's own host path (one lane, every host thread), one request of "
+              "p sequences at a time, each padded to the configuration's seq as the reference "
+              "pads every request; p = ceil(8 * threads / seq) so that its 8-row GEMM blocks "
+              "occupy every thread; one untimed request first, then the timed sequences; "
+              "sequences/s = timed sequences / their wall time")
+
+
+def cpu_per_request(cfg, threads: int) -> int:
+    """p: sequences per reference request -- enough 8-row GEMM blocks
+    (conv_host.hpp:154-160) to occupy every host thread."""
+    return int(max(1, min(cfg.batch, -(-threads * 8 // cfg.seq))))
+
+
+def cpu_host_facts(threads: int) -> dict:
+    return {"cores": threads, "nproc": os.cpu_count(), "cpu_model": cpu_model(),
+            "method": CPU_METHOD}
+
+
+def run_cpu_baseline(cfg, w, ids, mask, lens, n_timed: int = 8):
+    """The CPU baseline beside the GPU line: CPU_METHOD with n_timed >= 8
+    sequences spread over the batch (the longest and shortest included)."""
     with tempfile.TemporaryDirectory() as td:
         run, kind, threads = cpu_reference_setup(cfg, w, td)
-        first = pick_sample(lens, 1)
+        p = cpu_per_request(cfg, threads)
+        sample = pick_sample(lens, max(n_timed, p))
         t0 = time.perf_counter()
-        run(ids[first], mask[first])  # warm: builds the reference's weight cache
-        t1 = time.perf_counter() - t0
+        run(ids[sample[:p]], mask[sample[:p]])  # untimed: builds the reference's weight cache
+        t_warm = time.perf_counter() - t0
         t0 = time.perf_counter()
-        run(ids[first], mask[first])
-        per_seq = time.perf_counter() - t0
-        n = int(max(1, min(32, budget_s // max(per_seq, 1e-3))))
-        n = int(min(32, max(n, -(-threads * 8 // cfg.seq))))  # occupy every host thread
-        sample = pick_sample(lens, n)
-        t0 = time.perf_counter()
-        run(ids[sample], mask[sample])
-        el = time.perf_counter() - t0 + per_seq
-        n_total = len(sample) + 1
-    return {"value": n_total / el, "unit": "embeddings/s", "cores": threads, "kind": kind,
-            "sample": f"{n_total} sequences of the {cfg.batch}-row batch, each padded to "
-                      f"seq {cfg.seq} as the reference pads every request; "
-                      f"{el:.1f} s timed after a {t1:.1f} s warm-up",
-            "full_batch_s_extrapolated": cfg.batch * el / n_total}
+        for i in range(0, len(sample), p):
+            r = sample[i:i + p]
+            run(ids[r], mask[r])
+        el = time.perf_counter() - t0
+    return {"value": len(sample) / el, "unit": "embeddings/s", "kind": kind,
+            **cpu_host_facts(threads),
+            "sample": f"{len(sample)} sequences of the {cfg.batch}-row batch in requests of {p}, "
+                      f"each padded to seq {cfg.seq}; {el:.1f} s timed after a {t_warm:.1f} s "
+                      f"untimed request",
+            "full_batch_s_extrapolated": cfg.batch * el / len(sample)}
 
 
 def reference_arm(args, cfg):
@@ -208,9 +292,8 @@ def reference_arm(args, cfg):
     ids, mask, lens = synth.config_batch(cfg)
     with tempfile.TemporaryDirectory() as td:
         run, kind, threads = cpu_reference_setup(cfg, w, td)
-        # enough rows per step to occupy every host thread: the reference
-        # parallelises its GEMMs over 8-row blocks (conv_host.hpp:154-160)
-        per_step = int(max(1, min(cfg.batch, -(-threads * 8 // cfg.seq))))
+        # one reference request of p sequences per step (CPU_METHOD)
+        per_step = cpu_per_request(cfg, threads)
         order = pick_sample(lens, min(len(lens), per_step * (args.warmup + args.steps)))
 
         def rows(i):
@@ -234,9 +317,11 @@ def reference_arm(args, cfg):
                                f"{cfg.arch.layers}L/{cfg.arch.hidden}H, lengths {cfg.lengths}",
                    "global_batch": cfg.batch, "seq_len": cfg.seq, "parallelism": "host threads",
                    "step": f"{per_step} sequence(s) of the batch per step (bounded sample)"},
-        "cpu_baseline": {"value": value, "unit": "embeddings/s", "cores": threads, "kind": kind,
-                         "sample": f"{args.warmup} warm + {args.steps} timed steps of "
-                                   f"{per_step} sequence(s) of the batch, padded to {cfg.seq}"},
+        "cpu_baseline": {"value": value, "unit": "embeddings/s", "kind": kind,
+                         **cpu_host_facts(threads),
+                         "sample": f"{args.warmup} untimed + {args.steps} timed requests of "
+                                   f"{per_step} sequence(s) of the batch, padded to {cfg.seq} "
+                                   f"({args.steps * per_step} timed sequences)"},
         "e2e": {"value": value, "unit": "embeddings/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -250,7 +335,6 @@ def reference_arm(args, cfg):
 
 def gpu_arm(args, cfg):
     import torch
-    import torch.distributed as dist
 
     import nebw
 
@@ -260,113 +344,95 @@ def gpu_arm(args, cfg):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
 
     arch = cfg.arch
     w = synth.config_weights(cfg)
     ids, mask, lens = synth.config_batch(cfg)
     B, S, H = cfg.batch, cfg.seq, arch.hidden
-    shards = plan_shards(lens, world)
-    mine = shards[rank]
+    dev = nebw.Device(local)
+    ranks = Ranks(dev, world, rank)
+    owner, counts = nebw.shard_plan(lens, world)
+    mine = np.nonzero(owner == rank)[0]
     b_r = len(mine)
-    max_b = max(len(s) for s in shards)
     T_r = int(lens[mine].sum())
 
-    dev = nebw.Device(local)
     dev.set_attention_kernel(dev.ATTN_TCGEN05 if args.attention == "tcgen05" else dev.ATTN_MMA)
     model = nebw.Model.from_weights(dev, w, max_seq_len=S)
-    launches_per_step = model.launch_count(S)
+    launches_per_step = model.launch_count(S) + (1 if world > 1 and rank == 0 else 0)
     stream = torch.cuda.current_stream()
 
     ids_h = torch.from_numpy(np.ascontiguousarray(ids[mine])).pin_memory()
     lens_h = torch.from_numpy(np.ascontiguousarray(lens[mine])).pin_memory()
     ids_d = ids_h.cuda()
     lens_d = lens_h.cuda()
-    out_d = torch.zeros((max_b, H), dtype=torch.float32, device="cuda")
-    gather_d = torch.zeros((world * max_b, H), dtype=torch.float32, device="cuda") if rank == 0 else None
-    out_h = torch.empty((world * max_b if world > 1 else b_r, H), dtype=torch.float32).pin_memory()
+    out_d = torch.zeros((B if rank == 0 else b_r, H), dtype=torch.float32, device="cuda")
+    order_d = torch.from_numpy(nebw.shard_order(owner, world)).cuda() if rank == 0 else None
+    out_h = np.empty((B, H), np.float32)
 
     def step():
-        model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
-        if world > 1:
-            gather_to_root(out_d, gather_d, world, rank, dist)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        if world == 1:
+            model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
+        else:  # this rank's shard, then the gather to rank 0 in request order
+            ranks.comm.encode_shard_gather(model, ids_d, lens_d, b_r, S, counts, order_d,
+                                           out_d if rank == 0 else None, stream=stream)
 
     # ---- device-resident throughput --------------------------------------
     for _ in range(args.warmup):
         step()
-    barrier()
+    ranks.barrier()
     sampler = ClockSampler(range(world)) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.6)
     model.profile(True)
-    barrier()
+    ranks.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
-    barrier()
+    ranks.barrier()
     if sampler:
         sampler.stop()
     model.profile(False)
     prof = model.profile_collect()
     ms = e0.elapsed_time(e1)
     dev.sync()
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = ranks.max(ms)
 
     # ---- end to end through the public API with host buffers ------------
+    # N = 1: nebw_encode (H2D of ids and lengths, the pass, D2H); N > 1:
+    # nebw_encode_sharded (every rank is handed the whole batch, copies its
+    # shard in, encodes, gathers to rank 0, which copies [B, H] out)
     def step_e2e():
         if world == 1:
-            model.encode_into(ids_h, lens_h, out_h, b_r, S, host=True)  # nebw_encode: H2D, pass, D2H
-            return out_h.numpy()
-        ids_d.copy_(ids_h, non_blocking=True)
-        lens_d.copy_(lens_h, non_blocking=True)
-        model.encode_into(ids_d, lens_d, out_d, b_r, S, stream=stream)
-        gather_to_root(out_d, gather_d, world, rank, dist)
-        if rank == 0:
-            out_h.copy_(gather_d, non_blocking=True)
-        stream.synchronize()
-        if rank != 0:
-            return None
-        return unpermute(out_h.numpy(), shards, max_b)
+            model.encode_into(ids, lens, out_h, B, S, host=True)
+            return out_h
+        return ranks.comm.encode_sharded(model, ids, lens, out_h if rank == 0 else None)
 
     for _ in range(max(1, args.warmup)):
         res = step_e2e()
-    barrier()
+    ranks.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         res = step_e2e()
-    barrier()
-    e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_s = float(t.item())
+    ranks.barrier()
+    e2e_s = ranks.max(time.perf_counter() - t0)
+
+    # N > 1: rank 0 re-encodes a fixed subset of rows -- most of them owned
+    # by other ranks -- on its own GPU alone; rows are independent passes, so
+    # the gathered rows must match bit for bit
+    rows_match = None
+    if world > 1 and rank == 0:
+        sub = np.unique(np.concatenate([np.linspace(0, B - 1, 48).astype(int),
+                                        [int(np.argmax(lens)), int(np.argmin(lens))]]))
+        alone = model.encode(ids[sub], lens[sub])
+        rows_match = {"value": bool(np.array_equal(alone, res[sub])), "rows": int(len(sub)),
+                      "rows_on_other_ranks": int((owner[sub] != 0).sum())}
 
     # per-rank profile -> the slowest rank's numbers are the ones reported
-    prof_t = torch.tensor([[prof[k][1] for k in model.KERNEL_KINDS]], dtype=torch.float64,
-                          device="cuda")
-    tok_t = torch.tensor([float(T_r), float((lens[mine].astype(np.float64) ** 2).sum())],
-                         dtype=torch.float64, device="cuda")
-    if world > 1:
-        all_prof = [torch.zeros_like(prof_t) for _ in range(world)]
-        all_tok = [torch.zeros_like(tok_t) for _ in range(world)]
-        dist.all_gather(all_prof, prof_t)
-        dist.all_gather(all_tok, tok_t)
-    else:
-        all_prof, all_tok = [prof_t], [tok_t]
+    all_prof = ranks.all_gather([prof[k][1] for k in model.KERNEL_KINDS])
+    all_tok = ranks.all_gather([float(T_r), float((lens[mine].astype(np.float64) ** 2).sum())])
 
     ok = res is not None and bool(np.isfinite(res).all()) if rank == 0 else True
 
@@ -378,7 +444,7 @@ def gpu_arm(args, cfg):
         peaks, peak_src = load_peaks()
         slow = int(np.argmax([p.sum().item() for p in all_prof]))
         pms = dict(zip(model.KERNEL_KINDS, all_prof[slow][0].tolist()))
-        T_s, L2_s = all_tok[slow].tolist()
+        T_s, L2_s = all_tok[slow][0].tolist()
         steps = args.steps
         Hf, F, L = float(H), float(arch.ffn), arch.layers
         FW = 2.0 * F if arch.gated else F  # FFN-up width ([up | gate] for the gated families)
@@ -432,13 +498,14 @@ def gpu_arm(args, cfg):
                                    f"{cfg.lengths} clipped [8,{S}]; "
                                    f"{'CLS' if cfg.cls_pool else 'mean'} pooling + L2",
                        "global_batch": B, "seq_len": S, "real_tokens": int(lens.sum()),
-                       "parallelism": f"dp{world} (length-balanced shards, NCCL gather to rank 0)"
-                       if world > 1 else "single GPU",
+                       "parallelism": f"dp{world} (libnebw: length-balanced shards, "
+                                      "NCCL gather to rank 0)" if world > 1 else "single GPU",
                        "l2": "no flush: every step streams the 0.6 GB bf16 weights and GBs of "
                              "activations, far above the 126 MB L2"},
             "e2e": {"value": e2e, "unit": "embeddings/s",
                     "h2d_bytes_per_step": int(B * S * 4 + B * 4),
-                    "d2h_bytes_per_step": int(B * H * 4) if world == 1 else int(world * max_b * H * 4),
+                    "d2h_bytes_per_step": int(B * H * 4),
+                    "api": "nebw_encode" if world == 1 else "nebw_encode_sharded (every rank)",
                     "timer": "wall clock, synchronous per step, max over ranks"},
             "gpu_launches": int(launches_per_step * steps * world),
             "roofline": {"kernel": (f"gemm_tc<256, {arch.gated}> FFN-up (T x {H} -> {int(FW)}, "
@@ -463,6 +530,15 @@ def gpu_arm(args, cfg):
             "kernels": kernels,
             "outputs_finite": ok,
         }
+        if world > 1:
+            line["collective"] = {
+                "what": "gather of the pooled [b_r, H] fp32 rows to rank 0 (ncclSend / ncclRecv "
+                        "in one group) + a request-order scatter kernel on rank 0, inside "
+                        "nebw_encode_shard_gather",
+                "bytes_per_step": int(B * H * 4), "nranks": world,
+                "counts": [int(c) for c in counts]}
+            line["rows_match_single_gpu"] = rows_match["value"]
+            line["rows_match_detail"] = rows_match
         if sampler:
             line["clocks"] = sampler.summary()
         if cpu is not None:
@@ -470,10 +546,8 @@ def gpu_arm(args, cfg):
         print(json.dumps(line), flush=True)
 
     model.close()
+    ranks.close()
     dev.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
     return 0
 
 
@@ -518,7 +592,7 @@ def vit_cpu_baseline(cfg, w, images, budget_s=15.0):
         t0 = time.perf_counter()
         run(images[2:2 + n])
         el = time.perf_counter() - t0 + per
-    return {"value": (n + 1) / el, "unit": "images/s", "cores": threads, "kind": kind,
+    return {"value": (n + 1) / el, "unit": "images/s", "kind": kind, **cpu_host_facts(threads),
             "sample": f"{n + 1} images of the {cfg.batch}-image batch, {el:.1f} s timed after a "
                       f"{t1:.1f} s warm-up (one image at a time, as VitEncoder::run takes them)",
             "full_batch_s_extrapolated": cfg.batch * el / (n + 1)}
@@ -549,7 +623,7 @@ def vit_reference_arm(args, cfg):
         "config": {"workload": f"{cfg.key}: batch {cfg.batch} images 3x224x224",
                    "global_batch": cfg.batch, "parallelism": "host threads",
                    "step": f"{per_step} images of the batch per step (bounded sample)"},
-        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": value, "unit": "images/s", "kind": kind, **cpu_host_facts(threads),
                          "sample": f"{args.warmup} warm + {args.steps} timed steps of "
                                    f"{per_step} images"},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0,
@@ -560,7 +634,6 @@ def vit_reference_arm(args, cfg):
 
 def vit_arm(args, cfg):
     import torch
-    import torch.distributed as dist
 
     import nebw
 
@@ -570,63 +643,53 @@ def vit_arm(args, cfg):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
     arch = cfg.arch
     B, H = cfg.batch, arch.hidden
     w = synth.vit_config_weights(cfg)
     images = synth.vit_config_images(cfg)
     # every image costs the same: contiguous equal shards, gathered in order
     per = -(-B // world)
-    lo, hi = min(B, rank * per), min(B, (rank + 1) * per)
+    bounds = [(min(B, r * per), min(B, (r + 1) * per)) for r in range(world)]
+    counts = np.array([hi - lo for lo, hi in bounds], np.int32)
+    lo, hi = bounds[rank]
     n_r = hi - lo
     dev = nebw.Device(local)
+    ranks = Ranks(dev, world, rank)
     dev.set_attention_kernel(dev.ATTN_TCGEN05 if args.attention == "tcgen05" else dev.ATTN_MMA)
     model = nebw.VitModel.from_weights(dev, w)
     launches_per_step = model.launch_count()
     stream = torch.cuda.current_stream()
     img_h = torch.from_numpy(np.ascontiguousarray(images[lo:hi])).pin_memory()
     img_d = img_h.cuda()
-    out_d = torch.zeros((per, H), dtype=torch.float32, device="cuda")
-    gather_d = torch.zeros((world * per, H), dtype=torch.float32, device="cuda") if rank == 0 else None
-    out_h = torch.empty((world * per, H), dtype=torch.float32).pin_memory()
+    out_d = torch.zeros((max(n_r, 1), H), dtype=torch.float32, device="cuda")
+    gather_d = torch.zeros((B, H), dtype=torch.float32, device="cuda") if rank == 0 else None
+    out_h = torch.empty((B, H), dtype=torch.float32).pin_memory()
 
     def step():
         model.encode_into(img_d, out_d, n_r, stream=stream)
-        if world > 1:
-            gather_to_root(out_d, gather_d, world, rank, dist)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        if world > 1:  # libnebw's NCCL gather of the CLS rows, rank order = image order
+            ranks.comm.gather_rows(out_d, counts, H, gather_d, 0, stream=stream)
 
     for _ in range(args.warmup):
         step()
-    barrier()
+    ranks.barrier()
     sampler = ClockSampler(range(world)) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.6)
     model.profile(True)
-    barrier()
+    ranks.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
-    barrier()
+    ranks.barrier()
     if sampler:
         sampler.stop()
     model.profile(False)
     prof = model.profile_collect()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = ranks.max(e0.elapsed_time(e1))
 
     def step_e2e():
         if world == 1:
@@ -634,31 +697,21 @@ def vit_arm(args, cfg):
             return out_h[:n_r].numpy()
         img_d.copy_(img_h, non_blocking=True)
         model.encode_into(img_d, out_d, n_r, stream=stream)
-        gather_to_root(out_d, gather_d, world, rank, dist)
+        ranks.comm.gather_rows(out_d, counts, H, gather_d, 0, stream=stream)
         if rank == 0:
             out_h.copy_(gather_d, non_blocking=True)
-        stream.synchronize()
-        return out_h.numpy()[:B] if rank == 0 else None
+        ranks.comm.sync(stream=stream)
+        return out_h.numpy() if rank == 0 else None
 
     for _ in range(max(1, args.warmup)):
         res = step_e2e()
-    barrier()
+    ranks.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         res = step_e2e()
-    barrier()
-    e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_s = float(t.item())
-    prof_t = torch.tensor([[prof[k][1] for k in model.KERNEL_KINDS]], dtype=torch.float64,
-                          device="cuda")
-    if world > 1:
-        all_prof = [torch.zeros_like(prof_t) for _ in range(world)]
-        dist.all_gather(all_prof, prof_t)
-    else:
-        all_prof = [prof_t]
+    ranks.barrier()
+    e2e_s = ranks.max(time.perf_counter() - t0)
+    all_prof = ranks.all_gather([prof[k][1] for k in model.KERNEL_KINDS])
     ok = bool(np.isfinite(res).all()) if rank == 0 else True
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -715,8 +768,8 @@ def vit_arm(args, cfg):
                                    f"embedding, {arch.n_pos} positions), random-init N(0,0.02); "
                                    f"batch {B} images 3x224x224 fp32 uniform [-1,1]; CLS row",
                        "global_batch": B, "seq_len": arch.n_pos,
-                       "parallelism": f"dp{world} (equal image shards, NCCL gather to rank 0)"
-                       if world > 1 else "single GPU",
+                       "parallelism": f"dp{world} (equal image shards, libnebw NCCL gather "
+                                      "to rank 0)" if world > 1 else "single GPU",
                        "l2": "no flush: every step streams 1.2 GB of images and GBs of "
                              "activations, far above the 126 MB L2"},
             "e2e": {"value": B * steps / e2e_s, "unit": "images/s",
@@ -739,6 +792,12 @@ def vit_arm(args, cfg):
             "kernels": kernels,
             "outputs_finite": ok,
         }
+        if world > 1:
+            line["collective"] = {
+                "what": "gather of the [n_r, H] fp32 CLS rows to rank 0 (ncclSend / ncclRecv "
+                        "in one group, nebw_gather_rows)",
+                "bytes_per_step": int(B * H * 4), "nranks": world,
+                "counts": [int(c) for c in counts]}
         if sampler:
             line["clocks"] = sampler.summary()
         if cpu is not None:
@@ -746,10 +805,8 @@ def vit_arm(args, cfg):
         print(json.dumps(line), flush=True)
 
     model.close()
+    ranks.close()
     dev.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
     return 0
 
 

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NEBW_ABI_VERSION 3
+#define NEBW_ABI_VERSION 4
 
 typedef enum nebw_status {
   NEBW_OK = 0,
@@ -42,7 +42,10 @@ typedef enum nebw_status {
                         model with unstaged tensors)                         */
   NEBW_EDEVICE = 5,  /* a kernel reported an error (bad token id, bad
                         length, a bounded wait that timed out)              */
-  NEBW_EIO = 6       /* a container file could not be read or is malformed */
+  NEBW_EIO = 6,      /* a container file could not be read or is malformed */
+  NEBW_ECOMM = 7     /* NCCL is missing, or a collective failed or did not
+                        finish within the communicator's timeout (the
+                        communicator is then aborted)                      */
 } nebw_status;
 
 enum { NEBW_F32 = 0, NEBW_BF16 = 1 };
@@ -69,6 +72,15 @@ int nebw_close(nebw_dev *dev);
 /* Wait for the handle's stream, then report (and clear) any error a kernel
  * recorded since the last check. */
 int nebw_sync(nebw_dev *dev);
+/* Self-check of the kernels' bounded waits (no counterpart in the
+ * reference): one warp waits on an mbarrier that nothing arrives on, for
+ * limit_ns (1 us .. 1 s) of the GPU's global timer, with no copy or
+ * tensor-core product in flight.  *expired = 1 when the wait ran out as it
+ * should; the kernel then has recorded the wait-timeout code in the device
+ * error word, so the next nebw_sync returns NEBW_EDEVICE (and clears it).
+ * Every wait of the GEMM and attention kernels takes this path, bounded at
+ * 2 s, before unwinding.  Synchronous. */
+int nebw_check_bounded_wait(nebw_dev *dev, int64_t limit_ns, int32_t *expired);
 int nebw_alloc(nebw_dev *dev, size_t bytes, void **dptr);
 int nebw_free(nebw_dev *dev, void *dptr);
 int nebw_copy_h2d(nebw_dev *dev, void *dst_dev, const void *src_host, size_t bytes);
@@ -362,6 +374,85 @@ int nebw_vit_launch_count(const nebw_vit *m);
 int nebw_vit_profile(nebw_vit *m, int enable);
 int nebw_vit_profile_collect(nebw_vit *m, int64_t launches[NEBW_K_COUNT],
                              double ms[NEBW_K_COUNT]);
+
+/* ---- several GPUs: the batch sharded, the embeddings gathered -------------
+ * The reference has no multi-device code; its only concurrency is host
+ * threads sharing one NPU (the --pipeline lanes of EmbedService::embed,
+ * runtime/src/server/embed_service.cpp:66-108, run_setup.hpp:465-480).  Every
+ * sequence is an independent encoder pass (conv_host.hpp:154-158,
+ * bert_encoder.cpp:1001-1004), so a batch splits across GPUs with one weight
+ * replica per GPU (one nebw_model per GPU) and no exchange on the data path;
+ * the pooled [b_r, hidden] fp32 rows of every rank are gathered to rank 0
+ * over NCCL (NVLink / NVSwitch) and put back in request order there.
+ *
+ * NCCL (libnccl.so.2, or the file $NEBW_NCCL_LIB names) is loaded on first
+ * use, or the copy the process already holds is used; without it these calls
+ * return NEBW_ECOMM.  A process that also uses another NCCL (PyTorch's)
+ * loads that one before the first call here.  Communicators are non-blocking and every wait on one is
+ * bounded by its timeout_s: on expiry (a rank that never joins, a peer that
+ * died) the communicator is aborted, the call returns NEBW_ECOMM, and later
+ * calls on it return NEBW_ESTATE.  Collective calls must be made by every
+ * rank in the same order. */
+#define NEBW_COMM_ID_BYTES 128
+typedef struct nebw_comm nebw_comm;
+
+/* A fresh communicator id: made by one rank and handed to the others over
+ * the host (a socket, a file, a key-value store). */
+int nebw_comm_unique_id(uint8_t id[NEBW_COMM_ID_BYTES]);
+/* Join communicator `id` as `rank` of `nranks` (one process per GPU).
+ * Collective. */
+int nebw_comm_init_rank(nebw_dev *dev, int32_t nranks, int32_t rank,
+                        const uint8_t id[NEBW_COMM_ID_BYTES], double timeout_s,
+                        nebw_comm **out);
+/* One process driving n GPUs: comms[i] is rank i, on devs[i]. */
+int nebw_comm_init_all(int32_t n, nebw_dev *const *devs, double timeout_s, nebw_comm **comms);
+/* Flush and free (bounded by the timeout; an aborted communicator is only
+ * freed). */
+int nebw_comm_destroy(nebw_comm *c);
+int nebw_comm_size(const nebw_comm *c, int32_t *nranks, int32_t *rank);
+/* Wait (bounded) for `stream` to drain -- the collectives enqueued on it
+ * included -- then report device errors as nebw_sync does. */
+int nebw_comm_sync(nebw_comm *c, void *stream);
+
+/* The shard plan, host only and deterministic (every rank computes the same
+ * plan from the same lengths): sequences in decreasing cost l + l^2 / 2048
+ * (the GEMMs grow with l, attention with l^2), each to the rank with the
+ * least cost so far.  owner[B] gets each sequence's rank, counts[nranks]
+ * the sequences per rank; a rank's shard is its sequences in ascending
+ * order. */
+int nebw_shard_plan(const int32_t *lens, int32_t B, int32_t nranks, int32_t *owner,
+                    int32_t *counts);
+/* order[k] = the request index of row k of the rank-major gather (each
+ * rank's sequences ascending). */
+int nebw_shard_order(const int32_t *owner, int32_t B, int32_t nranks, int32_t *order);
+/* Gather counts[r] rows of H fp32 from every rank r (rows_dev, device) to
+ * rank `root`'s out_dev [sum(counts), H] in rank order.  Asynchronous on
+ * `stream`; collective. */
+int nebw_gather_rows(nebw_comm *c, const float *rows_dev, const int32_t *counts, int32_t H,
+                     float *out_dev, int32_t root, void *stream);
+
+/* The sharded encoder pass with the shard already on this rank's GPU: encode
+ * this rank's b_r sequences (ids_dev [b_r, S], lens_dev [b_r]), gather the
+ * pooled rows to rank 0, and there write out_dev [B, hidden] (B =
+ * sum(counts)) in request order through order_dev [B] (nebw_shard_order;
+ * NULL keeps rank order).  Asynchronous on `stream`; nebw_comm_sync waits.
+ * Collective. */
+int nebw_encode_shard_gather(nebw_model *m, nebw_comm *c, const int32_t *ids_dev,
+                             const int32_t *lens_dev, int32_t b_r, int32_t S,
+                             const int32_t *counts, const int32_t *order_dev, float *out_dev,
+                             void *stream);
+/* The sharded pass with host buffers, as nebw_encode: every rank passes the
+ * whole batch (ids [B, S], lens [B]) and encodes its share of the plan; rank
+ * 0 receives [B, hidden] in request order in `out` (other ranks may pass
+ * NULL).  Synchronous; collective. */
+int nebw_encode_sharded(nebw_model *m, nebw_comm *c, const int32_t *ids, const int32_t *lens,
+                        int32_t B, int32_t S, float *out);
+/* One process, n GPUs: models[i] on comms[i] (nebw_comm_init_all), one host
+ * thread per GPU running nebw_encode_sharded; `out` [B, hidden] in request
+ * order.  Synchronous.  (The reference's lane-parallel EmbedService::embed,
+ * embed_service.cpp:66-108, over GPUs instead of one NPU.) */
+int nebw_encode_multi(int32_t n, nebw_model *const *models, nebw_comm *const *comms,
+                      const int32_t *ids, const int32_t *lens, int32_t B, int32_t S, float *out);
 
 #ifdef __cplusplus
 }

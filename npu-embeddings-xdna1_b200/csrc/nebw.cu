@@ -524,6 +524,27 @@ extern "C" int nebw_sync(nebw_dev *d) {
   return NEBW_OK;
 }
 
+extern "C" int nebw_check_bounded_wait(nebw_dev *d, int64_t limit_ns, int32_t *expired) {
+  NEBW_REQUIRE(expired != nullptr, "null output");
+  NEBW_REQUIRE(limit_ns >= 1000 && limit_ns <= 1000000000ll,
+               "wait limit %lld ns refused: 1 us .. 1 s", static_cast<long long>(limit_ns));
+  if (int rc = use_dev(d)) return rc;
+  int *out = nullptr;
+  NEBW_CUDA(cudaMalloc(&out, sizeof(int)));
+  NEBW_CUDA(cudaMemsetAsync(out, 0xff, sizeof(int), d->stream));
+  nebw::wait_probe_kernel<<<1, 32, 0, d->stream>>>(static_cast<uint64_t>(limit_ns), d->d_err, out);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+  int v = -1;
+  if (e == cudaSuccess) e = cudaMemcpy(&v, out, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(out);
+  if (e != cudaSuccess)
+    return set_error(NEBW_ECUDA, "bounded-wait check: %s", cudaGetErrorString(e));
+  NEBW_REQUIRE(v == 0 || v == 1, "bounded-wait check: the probe wrote no result");
+  *expired = v;
+  return NEBW_OK;
+}
+
 extern "C" int nebw_alloc(nebw_dev *d, size_t bytes, void **p) {
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(p != nullptr, "null output pointer");
@@ -1923,3 +1944,9 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
 // ---------------------------------------------------------------------------
 
 #include "vit.cuh"
+
+// ---------------------------------------------------------------------------
+// Several GPUs: the sharded pass and the NCCL gather.
+// ---------------------------------------------------------------------------
+
+#include "multi.cuh"

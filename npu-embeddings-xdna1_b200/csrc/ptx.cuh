@@ -85,8 +85,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Wait until the phase with parity `parity` of `bar` has completed, for at
-// most kWaitTimeoutNs.  Returns false (and records kDevWaitTimeout) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+// most `limit_ns` of %globaltimer.  Returns false (and records
+// kDevWaitTimeout) on timeout.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, int *err,
+                                              uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -94,11 +96,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(a, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_err(err, kDevWaitTimeout);
       return false;
     }
   }
+}
+
+// The library's waits: bounded by kWaitTimeoutNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+  return mbar_wait_for(bar, parity, err, kWaitTimeoutNs);
+}
+
+// Self-check of the bounded wait: one warp waits on an mbarrier that nothing
+// arrives on (its phase 0 never completes), for `limit_ns`.  No copy or
+// tensor-core product is in flight.  out[0] = 1 if the wait ran out (and
+// kDevWaitTimeout was recorded in *err), 0 if it completed.
+__global__ void wait_probe_kernel(uint64_t limit_ns, int *err, int *out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool done = mbar_wait_for(&bar, 0, err, limit_ns);
+  if (threadIdx.x == 0) out[0] = done ? 0 : 1;
 }
 
 // ---- TMA ------------------------------------------------------------------

@@ -116,6 +116,19 @@ def lib() -> C.CDLL:
         "nebw_vit_launch_count": ([vp], C.c_int),
         "nebw_vit_profile": ([vp, C.c_int], C.c_int),
         "nebw_vit_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
+        "nebw_check_bounded_wait": ([vp, i64, C.POINTER(i32)], C.c_int),
+        "nebw_comm_unique_id": ([vp], C.c_int),
+        "nebw_comm_init_rank": ([vp, i32, i32, vp, C.c_double, C.POINTER(vp)], C.c_int),
+        "nebw_comm_init_all": ([i32, C.POINTER(vp), C.c_double, C.POINTER(vp)], C.c_int),
+        "nebw_comm_destroy": ([vp], C.c_int),
+        "nebw_comm_size": ([vp, C.POINTER(i32), C.POINTER(i32)], C.c_int),
+        "nebw_comm_sync": ([vp, vp], C.c_int),
+        "nebw_shard_plan": ([vp, i32, i32, vp, vp], C.c_int),
+        "nebw_shard_order": ([vp, i32, i32, vp], C.c_int),
+        "nebw_gather_rows": ([vp, vp, vp, i32, vp, i32, vp], C.c_int),
+        "nebw_encode_shard_gather": ([vp, vp, vp, vp, i32, i32, vp, vp, vp, vp], C.c_int),
+        "nebw_encode_sharded": ([vp, vp, vp, vp, i32, i32, vp], C.c_int),
+        "nebw_encode_multi": ([i32, C.POINTER(vp), C.POINTER(vp), vp, vp, i32, i32, vp], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -198,6 +211,12 @@ class Device:
 
     def set_attention_kernel(self, kind: int):
         _check(lib().nebw_set_attention_kernel(self.h, kind))
+
+    def check_bounded_wait(self, limit_ns: int) -> bool:
+        """True if the probe's wait ran out (nebw_check_bounded_wait)."""
+        e = C.c_int32()
+        _check(lib().nebw_check_bounded_wait(self.h, limit_ns, C.byref(e)))
+        return bool(e.value)
 
     def info(self):
         sm, ma, mi = C.c_int(), C.c_int(), C.c_int()
@@ -439,3 +458,118 @@ class VitModel:
         else:
             _check(lib().nebw_vit_encode_device(self.h, _addr(images), n, _addr(out),
                                                 _stream(stream)))
+
+
+# ---------------------------------------------------------------------------
+# several GPUs (nebw_comm): the batch sharded, the embeddings gathered
+# ---------------------------------------------------------------------------
+
+COMM_ID_BYTES = 128
+
+
+def shard_plan(lens, nranks: int):
+    """(owner [B], counts [nranks]) of the library's length-balanced plan."""
+    lens = np.ascontiguousarray(lens, np.int32)
+    owner = np.empty(len(lens), np.int32)
+    counts = np.empty(nranks, np.int32)
+    _check(lib().nebw_shard_plan(lens.ctypes.data, len(lens), nranks, owner.ctypes.data,
+                                 counts.ctypes.data))
+    return owner, counts
+
+
+def shard_order(owner, nranks: int) -> np.ndarray:
+    """order[k] = request index of row k of the rank-major gather."""
+    owner = np.ascontiguousarray(owner, np.int32)
+    order = np.empty(len(owner), np.int32)
+    _check(lib().nebw_shard_order(owner.ctypes.data, len(owner), nranks, order.ctypes.data))
+    return order
+
+
+def comm_unique_id() -> bytes:
+    buf = (C.c_uint8 * COMM_ID_BYTES)()
+    _check(lib().nebw_comm_unique_id(buf))
+    return bytes(buf)
+
+
+class Comm:
+    """A rank of an NCCL communicator on one Device (nebw_comm)."""
+
+    def __init__(self, dev: Device, handle):
+        self.dev = dev
+        self.h = handle
+        n, r = C.c_int32(), C.c_int32()
+        _check(lib().nebw_comm_size(self.h, C.byref(n), C.byref(r)))
+        self.nranks, self.rank = n.value, r.value
+
+    @classmethod
+    def init_rank(cls, dev: Device, nranks: int, rank: int, uid: bytes, timeout_s: float = 60.0):
+        if len(uid) != COMM_ID_BYTES:
+            raise ValueError("a communicator id is 128 bytes")
+        buf = (C.c_uint8 * COMM_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        _check(lib().nebw_comm_init_rank(dev.h, nranks, rank, buf, timeout_s, C.byref(h)))
+        return cls(dev, h)
+
+    @classmethod
+    def init_all(cls, devs, timeout_s: float = 60.0):
+        n = len(devs)
+        dh = (C.c_void_p * n)(*[d.h.value for d in devs])
+        out = (C.c_void_p * n)()
+        _check(lib().nebw_comm_init_all(n, dh, timeout_s, out))
+        return [cls(d, C.c_void_p(out[i])) for i, d in enumerate(devs)]
+
+    def close(self):
+        if self.h:
+            rc = lib().nebw_comm_destroy(self.h)
+            self.h = None
+            _check(rc)
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().nebw_comm_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+    def sync(self, stream=None):
+        _check(lib().nebw_comm_sync(self.h, _stream(stream)))
+
+    def gather_rows(self, rows, counts, H: int, out=None, root: int = 0, stream=None):
+        counts = np.ascontiguousarray(counts, np.int32)
+        _check(lib().nebw_gather_rows(self.h, _addr(rows), counts.ctypes.data, H, _addr(out), root,
+                                      _stream(stream)))
+
+    def encode_shard_gather(self, model: Model, ids, lens, b_r: int, S: int, counts, order=None,
+                            out=None, stream=None):
+        """Device-resident sharded pass (asynchronous; sync() waits)."""
+        counts = np.ascontiguousarray(counts, np.int32)
+        _check(lib().nebw_encode_shard_gather(model.h, self.h, _addr(ids), _addr(lens), b_r, S,
+                                              counts.ctypes.data, _addr(order), _addr(out),
+                                              _stream(stream)))
+
+    def encode_sharded(self, model: Model, ids: np.ndarray, lens: np.ndarray, out=None):
+        """Host buffers, synchronous; rank 0 gets [B, hidden] in request
+        order (returned), the other ranks None."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        lens = np.ascontiguousarray(lens, np.int32)
+        B, S = ids.shape
+        if self.rank == 0 and out is None:
+            out = np.empty((B, model.hidden), np.float32)
+        _check(lib().nebw_encode_sharded(model.h, self.h, ids.ctypes.data, lens.ctypes.data, B, S,
+                                         _addr(out) if self.rank == 0 else None))
+        return out if self.rank == 0 else None
+
+
+def encode_multi(models, comms, ids: np.ndarray, lens: np.ndarray) -> np.ndarray:
+    """One process, n GPUs (Comm.init_all): [B, hidden] in request order."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    lens = np.ascontiguousarray(lens, np.int32)
+    B, S = ids.shape
+    n = len(models)
+    out = np.empty((B, models[0].hidden), np.float32)
+    mh = (C.c_void_p * n)(*[m.h.value for m in models])
+    ch = (C.c_void_p * n)(*[c.h.value for c in comms])
+    _check(lib().nebw_encode_multi(n, mh, ch, ids.ctypes.data, lens.ctypes.data, B, S,
+                                   out.ctypes.data))
+    return out

@@ -10,6 +10,14 @@ for p in (str(PKG), str(REPO)):
     if p not in sys.path:
         sys.path.insert(0, p)
 
+# PyTorch (device buffers, streams and gloo ranks in the tests) loads its own
+# NCCL with libtorch; it is imported first so that libnebw's communicator
+# calls use that copy (the dynamic loader shares one libnccl.so.2 per process)
+try:
+    import torch  # noqa: F401
+except ImportError:
+    pass
+
 # the reference tree (read-only; present only where the reference is checked
 # out): $NEBW_REFERENCE, else a checkout beside this repository
 REFERENCE = Path(os.environ.get("NEBW_REFERENCE", str(REPO.parent / "reference")))

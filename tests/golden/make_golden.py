@@ -10,19 +10,21 @@ synthetic weights and tokens of a benchmark configuration.  The weights are
 not stored: they are regenerated from the recorded seed by nebw.synth, and a
 fingerprint of them is stored so a drift in the generator is caught.
 
-Fixtures (rows sampled from each configuration's synthetic batch; the
-shortest and longest rows are always included):
+Fixtures (rows sampled from each configuration's synthetic batch: the
+shortest and longest rows, the first and last row index, and rows spread
+evenly over the sorted lengths, so the tail of a skewed length distribution
+is sampled as well as its median):
   minilm_c1.npz      all-MiniLM-L6-v2 arch, the full 32 x 128 batch, mean pool
-  bge_small_c2.npz   bge-small arch, 6 rows at seq 512, CLS pool
-  bge_base_c3.npz    bge-base arch, 3 rows at seq 512, CLS pool
-  bge_large_c4.npz   bge-large arch, 3 rows at seq 512, CLS pool
+  bge_small_c2.npz   bge-small arch, 32 rows at seq 512, CLS pool
+  bge_base_c3.npz    bge-base arch, 32 rows at seq 512, CLS pool
+  bge_large_c4.npz   bge-large arch, 32 rows at seq 512, CLS pool
   nomic_c6.npz       nomic-embed-text-v1.5 shape (container arch
                      nomic_bert_rope_swiglu: RoPE theta 1000, SwiGLU, no
-                     biases), 3 rows at seq 512, mean pool
+                     biases), 16 rows at seq 512, mean pool
   gte_c7.npz         gte-base-en-v1.5 shape (container arch
                      gte_new_rope_geglu: RoPE frequencies as data, erf GeGLU),
-                     3 rows at seq 512, mean pool
-  vit_base_c5.npz    vit-base-patch16-224 arch, the first 3 images of the
+                     16 rows at seq 512, mean pool
+  vit_base_c5.npz    vit-base-patch16-224 arch, the first 16 images of the
                      configuration's batch, the CLS row after the final
                      LayerNorm -- the reference's VitEncoder::run
                      (runtime/src/vit/encoder.cpp) via oracle/ref_vit_driver.cpp.
@@ -66,11 +68,11 @@ from nebw import synth  # noqa: E402
 
 FIXTURES = {
     "minilm_c1": ("minilm", None),
-    "bge_small_c2": ("bge-small", 6),
-    "bge_base_c3": ("bge-base", 3),
-    "bge_large_c4": ("bge-large", 3),
-    "nomic_c6": ("nomic-base", 3),
-    "gte_c7": ("gte-base", 3),
+    "bge_small_c2": ("bge-small", 32),
+    "bge_base_c3": ("bge-base", 32),
+    "bge_large_c4": ("bge-large", 32),
+    "nomic_c6": ("nomic-base", 16),
+    "gte_c7": ("gte-base", 16),
 }
 
 
@@ -85,18 +87,27 @@ def weights_fingerprint(w) -> str:
 
 
 def sample_rows(lens, n):
+    """n row indices: the shortest and longest rows, row 0 and row B-1, then
+    rows at evenly spaced positions of the length-sorted order (a stable
+    sort, so the pick is deterministic), topped up from a seeded
+    permutation if equal picks collide."""
     if n is None:
         return np.arange(len(lens))
+    lens = np.asarray(lens)
     pick = {int(np.argmin(lens)), int(np.argmax(lens)), 0, len(lens) - 1}
-    extra = np.random.default_rng(7).permutation(len(lens))
-    for i in extra:
+    by_len = np.argsort(lens, kind="stable")
+    for q in np.linspace(0, len(lens) - 1, n):
+        if len(pick) >= n:
+            break
+        pick.add(int(by_len[int(round(q))]))
+    for i in np.random.default_rng(7).permutation(len(lens)):
         if len(pick) >= n:
             break
         pick.add(int(i))
-    return np.array(sorted(pick)[:n]) if len(pick) > n else np.array(sorted(pick))
+    return np.array(sorted(pick))
 
 
-VIT_FIXTURES = {"vit_base_c5": ("vit-base", 3)}
+VIT_FIXTURES = {"vit_base_c5": ("vit-base", 16)}
 
 
 INT8_SEED = 20261401

@@ -180,6 +180,30 @@ def test_pack_offsets_refuses_bad_length(device):
     device.sync()  # the error word was cleared
 
 
+def test_bounded_wait_runs_out_and_reports(device):
+    """The kernels' bounded mbarrier wait, made to run out: a probe waits 1 ms
+    on a barrier nothing arrives on (no copy or product in flight), returns,
+    records the wait-timeout code, and the next sync reports it by name; the
+    context stays usable (a second probe and an op still run)."""
+    import nebw
+    device.sync()
+    assert device.check_bounded_wait(1_000_000)
+    with pytest.raises(nebw.NebwError, match="bounded device wait timed out") as e:
+        device.sync()
+    assert e.value.code == 5  # NEBW_EDEVICE
+    device.sync()  # cleared
+    assert device.check_bounded_wait(10_000)
+    with pytest.raises(nebw.NebwError, match="timed out"):
+        device.sync()
+    x = torch.ones(256, device="cuda")
+    y = torch.empty(256, dtype=torch.bfloat16, device="cuda")
+    device.narrow_bf16(x, 256, y)
+    device.sync()
+    assert bool((y.float() == 1).all())
+    with pytest.raises(nebw.NebwError, match="refused"):
+        device.check_bounded_wait(10)
+
+
 def _packed(lens):
     off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     return off, int(off[-1])

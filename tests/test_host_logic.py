@@ -1,5 +1,7 @@
-"""Host-side logic (CPU, no GPU): synthetic inputs, mask handling, the shard
-plan, and the multi-rank gather -- the last with real gloo ranks."""
+"""Host-side logic (CPU, no GPU): synthetic inputs, mask handling, the
+library's shard plan and gather order (nebw_shard_plan / nebw_shard_order
+through the C ABI), and the multi-rank gather -- the last with real gloo
+ranks."""
 
 import os
 import socket
@@ -7,7 +9,7 @@ import socket
 import numpy as np
 import pytest
 
-from nebw import shard, synth
+from nebw import synth
 
 
 def test_token_layout():
@@ -46,30 +48,67 @@ def test_mask_to_lengths_refuses_holes():
         synth.mask_to_lengths(np.array([[1, 0, 1, 0]], np.int32))
 
 
+def _greedy_plan(lens, n):
+    """Independent restatement of the plan the library documents: sequences
+    in decreasing cost l + l^2/2048 (stable), each to the least-loaded rank
+    (lowest on ties)."""
+    lens = np.asarray(lens, np.float64)
+    cost = lens + lens ** 2 / 2048.0
+    load = np.zeros(n)
+    owner = np.empty(len(lens), np.int64)
+    for i in np.argsort(-cost, kind="stable"):
+        r = int(np.argmin(load))
+        owner[i] = r
+        load[r] += cost[i]
+    return owner, cost
+
+
 @pytest.mark.parametrize("n", [1, 2, 3, 4, 8])
-def test_plan_shards_partitions_and_balances(n):
+def test_shard_plan_partitions_and_balances(n):
+    """nebw_shard_plan (C ABI, host only) against the restatement above, on
+    the bge-large batch: the same owners, every sequence once, balanced."""
+    import nebw
     _, _, lens = synth.config_batch(synth.CONFIGS["bge-large"])
-    parts = shard.plan_shards(lens, n)
-    allidx = np.sort(np.concatenate(parts))
-    np.testing.assert_array_equal(allidx, np.arange(len(lens)))
-    assert all((np.diff(p) > 0).all() for p in parts)
-    cost = shard.shard_cost(lens)
-    loads = np.array([cost[p].sum() for p in parts])
+    owner, counts = nebw.shard_plan(lens, n)
+    want, cost = _greedy_plan(lens, n)
+    np.testing.assert_array_equal(owner, want)
+    np.testing.assert_array_equal(counts, np.bincount(want, minlength=n))
+    loads = np.array([cost[owner == r].sum() for r in range(n)])
     assert loads.max() / loads.mean() < 1.01  # greedy LPT on 1024 items balances tightly
-    again = shard.plan_shards(lens, n)  # deterministic: every rank computes the same plan
-    assert all(np.array_equal(a, b) for a, b in zip(parts, again))
+    again, _ = nebw.shard_plan(lens, n)  # deterministic: every rank computes the same plan
+    np.testing.assert_array_equal(owner, again)
 
 
-def test_unpermute_restores_request_order():
+def test_shard_order_restores_request_order():
+    """nebw_shard_order: row k of the rank-major gather is request
+    order[k]; scattering by it restores request order, bit for bit."""
+    import nebw
     lens = np.array([5, 300, 7, 512, 64, 9, 100], np.int32)
-    parts = shard.plan_shards(lens, 3)
-    max_b = max(len(p) for p in parts)
+    owner, counts = nebw.shard_plan(lens, 3)
+    order = nebw.shard_order(owner, 3)
     H = 4
     rows = np.arange(len(lens) * H, dtype=np.float32).reshape(len(lens), H)
-    gathered = np.full((3 * max_b, H), np.nan, np.float32)
-    for r, p in enumerate(parts):
-        gathered[r * max_b:r * max_b + len(p)] = rows[p]
-    np.testing.assert_array_equal(shard.unpermute(gathered, parts, max_b), rows)
+    gathered = np.concatenate([rows[owner == r] for r in range(3)])  # rank-major, ascending
+    out = np.full_like(rows, np.nan)
+    out[order] = gathered
+    np.testing.assert_array_equal(out, rows)
+    np.testing.assert_array_equal(np.sort(order), np.arange(len(lens)))
+
+
+def test_shard_plan_refusals():
+    import nebw
+    with pytest.raises(nebw.NebwError, match="ranks refused"):
+        nebw.shard_plan(np.array([3, 4], np.int32), 0)
+    with pytest.raises(nebw.NebwError, match="outside"):
+        nebw.shard_order(np.array([0, 2], np.int32), 2)
+
+
+def test_comm_unique_id_needs_no_gpu():
+    """A communicator id is made on the host (NCCL's bootstrap), 128 bytes,
+    fresh each time."""
+    import nebw
+    a, b = nebw.comm_unique_id(), nebw.comm_unique_id()
+    assert len(a) == len(b) == nebw.COMM_ID_BYTES and a != b
 
 
 def _free_port():
@@ -81,7 +120,9 @@ def _free_port():
 
 
 def _rank_main(rank, world, port, outdir):
-    """One gloo rank: encode its shard with the CPU oracle, gather to rank 0."""
+    """One gloo rank: the library's plan picks its shard, the CPU oracle
+    encodes it, gloo gathers the padded blocks to rank 0, which compacts them
+    by the plan's counts and scatters them by the library's order."""
     import sys
     from pathlib import Path
     repo = Path(__file__).resolve().parent.parent
@@ -90,7 +131,7 @@ def _rank_main(rank, world, port, outdir):
     import torch
     import torch.distributed as dist
 
-    from nebw import shard as sh
+    import nebw
     from nebw import synth as sy
     from oracle.oracle import PortOracle
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -100,16 +141,18 @@ def _rank_main(rank, world, port, outdir):
     lens = np.array([3, 40, 17, 64, 9, 33, 1, 50, 8], np.int32)
     ids, mask = sy.make_tokens(len(lens), 64, lens, seed=5)
     ids = np.minimum(ids, 1999)
-    parts = sh.plan_shards(lens, world)
-    mine = parts[rank]
-    max_b = max(len(p) for p in parts)
+    owner, counts = nebw.shard_plan(lens, world)
+    mine = np.nonzero(owner == rank)[0]
+    max_b = int(counts.max())
     emb = PortOracle().encode(w, ids[mine], mask[mine], threads=1)
     local = torch.zeros((max_b, w.hidden), dtype=torch.float32)
     local[:len(mine)] = torch.from_numpy(emb)
-    buf = torch.zeros((world * max_b, w.hidden), dtype=torch.float32) if rank == 0 else None
-    sh.gather_to_root(local, buf, world, rank, dist)
+    blocks = [torch.zeros_like(local) for _ in range(world)] if rank == 0 else None
+    dist.gather(local, blocks, dst=0)
     if rank == 0:
-        full = sh.unpermute(buf.numpy(), parts, max_b)
+        gathered = np.concatenate([blocks[r][:counts[r]].numpy() for r in range(world)])
+        full = np.empty_like(gathered)
+        full[nebw.shard_order(owner, world)] = gathered
         np.save(os.path.join(outdir, "gathered.npy"), full)
         np.save(os.path.join(outdir, "single.npy"),
                 PortOracle().encode(w, ids, mask, threads=1))
@@ -118,8 +161,9 @@ def _rank_main(rank, world, port, outdir):
 
 
 def test_gloo_two_rank_gather_matches_single_process(tmp_path):
-    """Sharded encode + gather + restore on 2 gloo ranks is bit-identical to
-    one process encoding the whole batch (rows are independent)."""
+    """Sharded encode + gather + restore on 2 gloo ranks, with the library's
+    plan and order, is bit-identical to one process encoding the whole batch
+    (rows are independent)."""
     import torch.multiprocessing as mp
     port = _free_port()
     mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True,
