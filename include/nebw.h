@@ -87,13 +87,13 @@ int nebw_copy_h2d(nebw_dev *dev, void *dst_dev, const void *src_host, size_t byt
 int nebw_copy_d2h(nebw_dev *dev, void *dst_host, const void *src_dev, size_t bytes);
 int nebw_device_info(nebw_dev *dev, int *sm_count, int *cc_major, int *cc_minor);
 
-/* Which attention kernel a device handle uses for head_dim 64 (no
+/* Which attention kernel a device handle uses (no
  * counterpart in the reference, which has one host path):
  * NEBW_ATTN_TCGEN05 -- S and P.V on tcgen05 UMMA with TMEM accumulators,
  *   persistent CTAs over a longest-first work list (the default);
  * NEBW_ATTN_MMA -- flash attention on mma.sync.
- * Both give results within the same parity tolerance; head_dim 32 always
- * runs on mma.sync. */
+ * Both give results within the same parity tolerance, at head_dim 64 and
+ * 32; other head_dims are refused. */
 enum { NEBW_ATTN_MMA = 0, NEBW_ATTN_TCGEN05 = 1 };
 int nebw_set_attention_kernel(nebw_dev *dev, int kind);
 
@@ -144,8 +144,8 @@ int nebw_layernorm(nebw_dev *dev, float *x, const void *y, int y_dtype, const fl
  *   seq_off [B+1], seq_len [B] int32 device: sequence b owns packed rows
  *   [seq_off[b], seq_off[b] + seq_len[b])
  *   ctx_bf16 [rows, H] device.  head_dim in {32, 64}; max_len bounds
- *   seq_len.  head_dim 64 with max_len <= 512 runs on tcgen05 (S and P.V on
- *   the 5th-generation tensor cores); head_dim 32 on mma.sync. */
+ *   seq_len.  Runs on tcgen05 (S and P.V on the 5th-generation tensor cores)
+ *   unless nebw_set_attention_kernel chose mma.sync. */
 int nebw_attention(nebw_dev *dev, const void *qkv_bf16, int64_t rows, const int32_t *seq_off,
                    const int32_t *seq_len, int32_t B, int32_t max_len, int32_t heads,
                    int32_t head_dim, void *ctx_bf16, void *stream);
@@ -256,6 +256,20 @@ int nebw_npue_gemm_kn(const char *path, const char *name, float *out_kn, int64_t
  * (tools/lib/npue.py:777-785's scheme).  No reference counterpart as a
  * function: the reference reads it from a design's design.json. */
 const char *nebw_tma_layout_hash(void);
+/* The weight packer: a Hugging Face BERT checkpoint directory (config.json,
+ * 1_Pooling/config.json, model.safetensors, optional vocab.txt and
+ * CHECKPOINT.json) -> a `.npue` container at out_path.  layout "tma_bf16"
+ * (NULL: the default) stores GEMM operands as bf16 [N, K] for
+ * nebw_model_load_npue to upload as they are; "host" writes the reference
+ * packer's --dtype f32 container (F32 [K, N]).  QKV fused, weights
+ * transposed to [K, N], 1/sqrt(head_dim) folded into Q unless fold_scale is
+ * 0, the position table cut to max_seq (<= 0: 256).  Replaces the BERT
+ * branch of tools/pack/pack_npue.py (:2620-2835) and the runtime's
+ * --prepare-model (runtime/src/common/npue_pack.cpp).  Host only; *bytes
+ * (may be NULL) gets the file size.  NEBW_EIO names what is missing or
+ * refused. */
+int nebw_pack_checkpoint(const char *model_dir, const char *out_path, const char *layout,
+                         int32_t max_seq, int32_t fold_scale, uint64_t *bytes);
 int nebw_model_destroy(nebw_model *m);
 int nebw_model_get_config(const nebw_model *m, nebw_config *cfg);
 

@@ -20,10 +20,10 @@ from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 REPO = PKG.parent
-SOURCES = ["csrc/nebw.cu", "csrc/npue_file.cpp"]
+SOURCES = ["csrc/nebw.cu", "csrc/npue_file.cpp", "csrc/npue_pack.cpp"]
 # every header the library includes: a change to any of them rebuilds it
 DEPS = SOURCES + sorted(str(p.relative_to(PKG)) for p in (PKG / "csrc").glob("*.cuh")) + [
-    "csrc/npue_file.h", "../include/nebw.h"]
+    "csrc/npue_file.h", "csrc/npue_pack.h", "../include/nebw.h"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
               "-Xcompiler", "-fPIC", "-shared"]
 
@@ -75,6 +75,10 @@ def build_oracle(verbose: bool = False):
     ref = Path(os.environ.get("NEBW_REFERENCE", str(REPO.parent / "reference")))
     if (ref / "runtime" / "src" / "encoders" / "bert_encoder.cpp").exists():
         subprocess.run([make, "-s", "-j8", "-C", str(REPO / "oracle"), "ref", f"REF={ref}"],
+                       check=True)
+        # the serving drop-in against the reference's headers and tokenizer
+        # (needs libnebw.so, built first by build_lib)
+        subprocess.run([make, "-s", "-C", str(REPO / "oracle"), "encoder_check", f"REF={ref}"],
                        check=True)
 
 

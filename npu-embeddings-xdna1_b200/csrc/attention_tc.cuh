@@ -1,4 +1,5 @@
-// Fused masked attention on the 5th-generation tensor cores (head_dim 64).
+// Fused masked attention on the 5th-generation tensor cores, head_dim D of
+// 64 (bge-base/large, ViT-base) or 32 (MiniLM, bge-small).
 //
 // Persistent CTAs over (sequence, 128-query tile, head) work items,
 // flash-style over key blocks of up to 64 with an online softmax,
@@ -7,8 +8,9 @@
 //
 //   warp 0      TMA: the Q tile once per item through a 2-slot ring (the
 //               next item's Q lands while this one runs), then K_j and V_j
-//               (64-key tiles) of the packed Q|K|V rows (128-byte swizzled)
-//               in issue order through a 3-slot ring
+//               (64-key tiles) of the packed Q|K|V rows (128-byte swizzled
+//               for D 64, 64-byte for D 32) in issue order through a 3-slot
+//               ring
 //   warp 1      tcgen05.mma from one elected lane (the whole warp walks the
 //               schedule, so loop state and descriptors stay warp-uniform),
 //               software-pipelined inside an
@@ -16,9 +18,9 @@
 //               P_j-1 V_j-1 runs (an item's last P V is issued as soon as its
 //               P is written):
 //                 S_j  = Q K_j^T  (M=128, N = the block's valid keys rounded
-//                                  up to 16, K=16 x 4)     -> TMEM [0, 64)
-//                 O += P_j-1 V_j-1 (M=128, N=64, K = 16 x that block's
-//                                  N/16; V read MN-major)  -> TMEM [64, 128)
+//                                  up to 16, K=16 x D/16)  -> TMEM [0, 64)
+//                 O += P_j-1 V_j-1 (M=128, N=D, K = 16 x that block's
+//                                  N/16; V read MN-major)  -> TMEM [64, 64+D)
 //   warps 2-5   one query row per thread (its TMEM lane); a warp whose 32
 //               rows all lie past the sequence only keeps the barrier
 //               protocol.  S_j is read from TMEM once, into registers; row
@@ -30,18 +32,18 @@
 //               when a row's max grows past it by more than a factor 2^8,
 //               so p <= 2^8 and O is rarely touched before the end, where
 //               ctx = O / sum as bf16, staged through shared memory into
-//               whole 128-byte row slices per store
+//               whole 2D-byte row slices per store
 //
 // Only the valid keys of a block are multiplied and exponentiated (in
 // 16-key groups), so short sequences -- most of an embedding batch -- cost
 // what their length needs rather than a full 128 x 128 tile.
 //
-// 72 KB of shared memory, 128 TMEM columns and at most 112 registers per
-// thread per CTA, so three CTAs share an SM (three softmax warps per SM
-// sub-partition) and one's softmax overlaps the others' waits on loads and
-// products; the 64-key block is what makes the third CTA fit.  Q is
-// pre-scaled by 1/sqrt(64) (the packer's fold, tools/pack/pack_npue.py:
-// 2742-2750); no scale is applied here.
+// 72 KB (D 64) or 44 KB (D 32) of shared memory, 128 TMEM columns and at
+// most 112 registers per thread per CTA, so three CTAs share an SM (three
+// softmax warps per SM sub-partition) and one's softmax overlaps the others'
+// waits on loads and products; the 64-key block is what makes the third CTA
+// fit.  Q is pre-scaled by 1/sqrt(D) (the packer's fold,
+// tools/pack/pack_npue.py:2742-2750); no scale is applied here.
 //
 // Replaces qk_impl / softmax_cpu / av_impl (runtime/src/encoders/
 // bert_encoder.cpp:995-1135, :481-530).  The reference's padded keys carry
@@ -63,20 +65,38 @@
 namespace nebw {
 
 constexpr int kAttnTcThreads = 192;  // TMA warp, MMA warp, 4 softmax warps
-constexpr int kAttnTcD = 64;
 constexpr int kAttnTcKeys = 64;       // keys per block
-constexpr int kAttnTcTmemCols = 128;  // S [0,64), O [64,128)
+constexpr int kAttnTcTmemCols = 128;  // S [0,64), O [64, 64 + head_dim)
 
+// head_dim the tcgen05 kernel is built for: 64 (bge-base/large, ViT-base)
+// and 32 (MiniLM, bge-small).  Rows of a 64-wide head tile are 128 bytes
+// (128-byte swizzle), of a 32-wide one 64 bytes (64-byte swizzle).
+__host__ __device__ constexpr bool attn_tc_head_dim(int d) { return d == 32 || d == 64; }
+
+template <int D>
 struct AttnTcShape {
-  static constexpr int kTile = 16384;               // one 128 x 64 bf16 Q tile
-  static constexpr int kKvTile = 8192;              // one 64 x 64 bf16 K or V tile
+  static_assert(attn_tc_head_dim(D), "head_dim 32 or 64");
+  static constexpr int kTile = 128 * D * 2;             // one 128 x D bf16 Q tile
+  static constexpr int kKvTile = kAttnTcKeys * D * 2;   // one 64 x D bf16 K or V tile
   static constexpr int kQSlots = 2, kKvSlots = 3;
   static constexpr int kQ0 = 0;                     // Q ring: 2 slots
   static constexpr int kKv0 = kQSlots * kTile;      // K/V ring: 3 slots, K_j V_j K_j+1 ...
   static constexpr int kP = kKv0 + kKvSlots * kKvTile;  // P, 16 KB (128 rows x 64 keys)
   static constexpr int kBars = kP + 16384;          // barriers
-  static constexpr int kSmemBytes = kBars + 256;    // 73,984 B: three CTAs per SM
+  static constexpr int kSmemBytes = kBars + 256;    // 73,984 B (D 64) / 45,312 B (D 32)
+  static_assert(kKv0 % 1024 == 0 && kP % 1024 == 0 && kKvTile % 1024 == 0,
+                "swizzled tiles stay 1 KB aligned");
 };
+
+// Shared-memory descriptors of the head tiles: K-major Q and K, MN-major V.
+template <int D>
+__device__ __forceinline__ uint64_t attn_desc_kmajor(uint32_t a) {
+  return D == 64 ? sdesc_kmajor_sw128(a) : sdesc_kmajor_sw64(a);
+}
+template <int D>
+__device__ __forceinline__ uint64_t attn_desc_v(uint32_t a) {
+  return D == 64 ? sdesc_mnmajor_sw128(a) : sdesc_mnmajor_sw64(a);
+}
 
 template <typename T>
 __device__ __forceinline__ T *smem_at(uint8_t *base, int off) {
@@ -108,14 +128,15 @@ __device__ __forceinline__ int attn_block_cols(int L, int j) {
 // load / product / softmax pipeline running across items.  With `items`
 // null, the items are every (b, qt < qtiles) and tiles past a sequence's
 // length are skipped.
+template <int D>
 __global__ void __launch_bounds__(kAttnTcThreads, 3)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV,
                         const __grid_constant__ CUtensorMap tmKV, const int *__restrict__ seq_off,
                         const int *__restrict__ seq_len, const int *__restrict__ items,
                         const int *__restrict__ items_count, int n_items_host, int qtiles,
                         int heads, __nv_bfloat16 *__restrict__ ctx, int *err) {
-  using S = AttnTcShape;
-  const int H = heads * kAttnTcD;
+  using S = AttnTcShape<D>;
+  const int H = heads * D;
   const int n_items = items_count ? __ldg(items_count) : n_items_host;
   const int n_work = n_items * heads;
 
@@ -185,7 +206,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
             break;
           }
           mbar_arrive_expect_tx(q_full + qs, S::kTile);
-          tma_load_2d(smem + S::kQ0 + qs * S::kTile, &tmQKV, q_full + qs, h * kAttnTcD, base + q0);
+          tma_load_2d(smem + S::kQ0 + qs * S::kTile, &tmQKV, q_full + qs, h * D, base + q0);
           ++t;
         }
         for (int j = 0; j < nk && ok; ++j) {
@@ -197,7 +218,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
             }
             mbar_arrive_expect_tx(kv_full + ss, S::kKvTile);
             tma_load_2d(smem + S::kKv0 + ss * S::kKvTile, &tmKV, kv_full + ss,
-                        (1 + kv) * H + h * kAttnTcD, base + j * kAttnTcKeys);
+                        (1 + kv) * H + h * D, base + j * kAttnTcKeys);
           }
         }
       }
@@ -220,7 +241,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
     // The whole warp walks the schedule and waits (so that the loop state
     // and the descriptors are warp-uniform); one elected lane issues the
     // tcgen05 instructions.
-    constexpr uint32_t idO = idesc_bf16_f32(128, kAttnTcD) | (1u << 16);  // B (V) MN-major
+    constexpr uint32_t idO = idesc_bf16_f32(128, D) | (1u << 16);  // B (V) MN-major
     const uint32_t pa = smem_u32(smem + S::kP);
     const bool leader = elect_one_sync();
     auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
@@ -238,14 +259,14 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
       if (!wait_all(kv_full + vs, (vq / S::kKvSlots) & 1) || !wait_all(p_full, b & 1)) return false;
       tc_fence_after();
       const uint64_t da = sdesc_kmajor_sw128(pa);
-      const uint64_t db = sdesc_mnmajor_sw128(smem_u32(smem + S::kKv0 + vs * S::kKvTile));
+      const uint64_t db = attn_desc_v<D>(smem_u32(smem + S::kKv0 + vs * S::kKvTile));
       if (leader) {
         // descriptor start addresses advance in 16-byte units: P by 32 B per
-        // 16 keys, V by 2048 B per 16 keys
+        // 16 keys, V by 16 rows of 2 D bytes per 16 keys
 #pragma unroll
         for (int ks = 0; ks < kAttnTcKeys / 16; ++ks)
           if (ks < cols / 16)
-            umma_bf16(tO, da + ks * 2, db + ks * 128, idO, (!first || ks > 0) ? 1u : 0u);
+            umma_bf16(tO, da + ks * 2, db + ks * (2 * D), idO, (!first || ks > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(kv_empty + vs);
       }
@@ -263,7 +284,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
         break;
       }
       ++t;
-      const uint64_t dq = sdesc_kmajor_sw128(smem_u32(smem + S::kQ0 + qs * S::kTile));
+      const uint64_t dq = attn_desc_kmajor<D>(smem_u32(smem + S::kQ0 + qs * S::kTile));
       for (int j = 0; j < nk; ++j, ++gb, g += 2) {
         const int ks = g % S::kKvSlots;  // K_j at sequence g, V_j at g + 1
         const int cols = attn_block_cols(L, j);
@@ -271,11 +292,11 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
              (gb == 0 || wait_all(s_free, (gb - 1) & 1));
         if (!ok) break;
         tc_fence_after();
-        const uint64_t dk = sdesc_kmajor_sw128(smem_u32(smem + S::kKv0 + ks * S::kKvTile));
+        const uint64_t dk = attn_desc_kmajor<D>(smem_u32(smem + S::kKv0 + ks * S::kKvTile));
         const uint32_t idS = idesc_bf16_f32(128, cols);
         if (leader) {
 #pragma unroll
-          for (int k = 0; k < kAttnTcD / 16; ++k)  // +32 B per 16 elements of K
+          for (int k = 0; k < D / 16; ++k)  // +32 B per 16 elements of K
             umma_bf16(tS, dq + k * 2, dk + k * 2, idS, k > 0 ? 1u : 0u);
           umma_commit(s_full);
           umma_commit(kv_empty + ks);
@@ -391,7 +412,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
           if (j > 0) {
             // 16 columns at a time: S_j is still held in 128 registers
 #pragma unroll 1
-            for (int q = 0; q < kAttnTcD / 16; ++q) {
+            for (int q = 0; q < D / 16; ++q) {
               uint32_t va[16];
               tmem_ld_32x32b_x16(tO + lane_off + q * 16, va);
               tmem_wait_ld_regs(va);
@@ -451,10 +472,10 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
       if (active) {
         // ctx rows = O / sum as bf16, staged through this warp's own 32
         // rows of the P tile (free: the last P V has completed) so that
-        // each global store writes four whole 128-byte row slices
+        // each global store writes whole 2D-byte row slices
         const float inv = 1.0f / l;
 #pragma unroll 1
-        for (int q = 0; q < kAttnTcD / 16; ++q) {
+        for (int q = 0; q < D / 16; ++q) {
           uint32_t va[16];
           tmem_ld_32x32b_x16(tO + lane_off + q * 16, va);
           tmem_wait_ld_regs(va);
@@ -468,13 +489,15 @@ __global__ void __launch_bounds__(kAttnTcThreads, 3)
               make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
         __syncwarp();
-        const int ch = lane & 7;  // 16-byte chunk of a row slice
+        constexpr int kChunks = D / 8;          // 16-byte chunks of a row slice
+        constexpr int kRowsPer = 32 / kChunks;  // rows one warp-wide store covers
+        const int ch = lane % kChunks;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int rr = w4 * 32 + 4 * i + (lane >> 3);  // query row within the tile
+        for (int i = 0; i < kChunks; ++i) {
+          const int rr = w4 * 32 + kRowsPer * i + lane / kChunks;  // query row within the tile
           if (q0 + rr < L)
-            *reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + rr) * H +
-                                       h * kAttnTcD + ch * 8) =
+            *reinterpret_cast<uint4 *>(ctx + static_cast<int64_t>(base + q0 + rr) * H + h * D +
+                                       ch * 8) =
                 *reinterpret_cast<const uint4 *>(smem + S::kP + rr * 128 + ((ch ^ (rr & 7)) << 4));
         }
         __syncwarp();

@@ -47,6 +47,7 @@
 #include "gated.cuh"
 #include "gemm_tc.cuh"
 #include "npue_file.h"
+#include "npue_pack.h"
 #include "ptx.cuh"
 #include "rowops.cuh"
 
@@ -133,6 +134,29 @@ int make_tmap_kmajor(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K,
   return NEBW_OK;
 }
 
+// The attention kernel's head tiles: a bf16 [rows, cols] map with a
+// {head_dim, box_rows} box over the packed Q|K|V rows, 128-byte swizzle for
+// head_dim 64 (128-byte box rows), 64-byte swizzle for head_dim 32.
+int make_tmap_head(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int head_dim,
+                   int box_rows) {
+  if (int rc = load_tensor_map_encoder()) return rc;
+  NEBW_REQUIRE(head_dim == 32 || head_dim == 64, "head tile of width %d refused", head_dim);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return set_error(NEBW_EINVAL, "Q|K|V address is not 16-byte aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              head_dim == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NEBW_ECUDA, "cuTensorMapEncodeTiled (head tiles) failed (%d) for [%lld, %lld]",
+                     static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(cols));
+  return NEBW_OK;
+}
+
 // A 2-D row-major output tensor map [rows, N] with a 32 x 32 box (the GEMM
 // epilogue's TMA store chunk): fp32 rows of the box are 128 bytes (128-byte
 // swizzle), bf16 rows 64 bytes (64-byte swizzle).
@@ -179,8 +203,8 @@ struct nebw_dev {
   // CTA pairs the GPU can hold at once for the 2-CTA GEMM (0: use the
   // single-CTA kernel); NEBW_GEMM_CTAS=1 in the environment forces 0.
   int gemm_pairs = 0;
-  // attention kernel for head_dim 64: NEBW_ATTN_MMA (mma.sync flash) or
-  // NEBW_ATTN_TCGEN05 (UMMA/TMEM); see nebw_set_attention_kernel
+  // attention kernel: NEBW_ATTN_MMA (mma.sync flash) or NEBW_ATTN_TCGEN05
+  // (UMMA/TMEM); see nebw_set_attention_kernel
   int attn_kind = NEBW_ATTN_TCGEN05;
 };
 
@@ -416,14 +440,16 @@ int launch_attention(const __nv_bfloat16 *qkv, const int *off, const int *len, i
   return NEBW_OK;
 }
 
-// tcgen05 attention for head_dim 64: a persistent launch (three CTAs per SM)
+// tcgen05 attention for head_dim 64 or 32: a persistent launch (three CTAs per SM)
 // over the work items -- the device-built, longest-first list `items` with
 // its count `items_count`, or, when `items` is null, every (sequence,
 // 128-query tile < max_len) pair.
 int launch_attention_tc(nebw_dev *d, const CUtensorMap &map, const CUtensorMap &map_kv,
                         const int *off, const int *len,
                         const int *items, const int *items_count, int B, int max_len, int heads,
-                        __nv_bfloat16 *ctx, cudaStream_t st) {
+                        int head_dim, __nv_bfloat16 *ctx, cudaStream_t st) {
+  NEBW_REQUIRE(nebw::attn_tc_head_dim(head_dim), "head_dim %d refused by the tcgen05 attention",
+               head_dim);
   NEBW_REQUIRE(B > 0 && B <= 65535 && heads > 0 && heads <= 65535 && max_len > 0 &&
                    max_len <= 32767,
                "attention grid refused (B %d, heads %d, max_len %d)", B, heads, max_len);
@@ -431,8 +457,14 @@ int launch_attention_tc(nebw_dev *d, const CUtensorMap &map, const CUtensorMap &
   const int64_t n_items = static_cast<int64_t>(B) * qtiles;
   NEBW_REQUIRE(n_items * heads < (1ll << 31), "attention work too large");
   const dim3 grid(3 * d->sm_count);
-  nebw::attention_tc_kernel<<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape::kSmemBytes, st>>>(
-      map, map_kv, off, len, items, items_count, static_cast<int>(n_items), qtiles, heads, ctx, d->d_err);
+  if (head_dim == 64)
+    nebw::attention_tc_kernel<64><<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape<64>::kSmemBytes, st>>>(
+        map, map_kv, off, len, items, items_count, static_cast<int>(n_items), qtiles, heads, ctx,
+        d->d_err);
+  else
+    nebw::attention_tc_kernel<32><<<grid, nebw::kAttnTcThreads, nebw::AttnTcShape<32>::kSmemBytes, st>>>(
+        map, map_kv, off, len, items, items_count, static_cast<int>(n_items), qtiles, heads, ctx,
+        d->d_err);
   NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }
@@ -491,10 +523,15 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
   NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
   if (int rc = set_all_gemm_attrs()) return rc;
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::AttnTcShape::kSmemBytes));
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::AttnTcShape<64>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  cudaSharedmemCarveoutMaxShared));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::AttnTcShape<32>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<32>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared));
+
   if (int rc = query_gemm_pairs(&d->gemm_pairs)) return rc;
   if (int rc = load_tensor_map_encoder()) return rc;
   *out = d.release();
@@ -762,13 +799,13 @@ extern "C" int nebw_attention(nebw_dev *d, const void *qkv, int64_t rows, const 
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(qkv && off && len && ctx, "null attention operand");
   NEBW_REQUIRE(rows > 0 && rows < (1ll << 31), "rows %lld refused", static_cast<long long>(rows));
-  if (d->attn_kind == NEBW_ATTN_TCGEN05 && hd == nebw::kAttnTcD) {
+  if (d->attn_kind == NEBW_ATTN_TCGEN05 && nebw::attn_tc_head_dim(hd)) {
     CUtensorMap map, map_kv;
-    if (int rc = make_tmap_kmajor(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 128))
+    if (int rc = make_tmap_head(&map, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, hd, 128))
       return rc;
-    if (int rc = make_tmap_kmajor(&map_kv, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, 64))
+    if (int rc = make_tmap_head(&map_kv, qkv, rows, 3 * static_cast<int64_t>(heads) * hd, hd, 64))
       return rc;
-    return launch_attention_tc(d, map, map_kv, off, len, nullptr, nullptr, B, max_len, heads,
+    return launch_attention_tc(d, map, map_kv, off, len, nullptr, nullptr, B, max_len, heads, hd,
                                static_cast<__nv_bfloat16 *>(ctx), pick_stream(d, stream));
   }
   return launch_attention(static_cast<const __nv_bfloat16 *>(qkv), off, len, B, max_len, heads, hd,
@@ -839,7 +876,7 @@ struct Workspace {
   // rotary positions applied in the QKV GEMM's epilogue (CTA pairs,
   // head_dim 64): the position of each packed row, [rows_cap] ints
   int *row_pos = nullptr;
-  CUtensorMap map_qkv_att, map_kv_att;  // Q|K|V rows as 64 x 128 / 64 x 64 TMA tiles
+  CUtensorMap map_qkv_att, map_kv_att;  // Q|K|V head tiles, head_dim x 128 / head_dim x 64 rows
   CUtensorMap map_a, map_ctx, map_h;    // GEMM A operands (TMA loads)
   CUtensorMap out_qkv, out_y, out_h;    // GEMM outputs (TMA stores)
 };
@@ -913,8 +950,10 @@ int make_workspace_maps(const nebw_model *m, Workspace &w, int64_t R) {
   if ((rc = make_tmap_out(&w.out_qkv, w.qkv, R, 3 * H, true))) return rc;
   if ((rc = make_tmap_out(&w.out_y, w.y, R, H, true))) return rc;
   if ((rc = make_tmap_out(&w.out_h, w.h, R, FW, true))) return rc;
-  if ((rc = make_tmap_kmajor(&w.map_qkv_att, w.qkv, R, 3 * H, 128))) return rc;
-  if ((rc = make_tmap_kmajor(&w.map_kv_att, w.qkv, R, 3 * H, 64))) return rc;
+  if (nebw::attn_tc_head_dim(m->cfg.head_dim)) {
+    if ((rc = make_tmap_head(&w.map_qkv_att, w.qkv, R, 3 * H, m->cfg.head_dim, 128))) return rc;
+    if ((rc = make_tmap_head(&w.map_kv_att, w.qkv, R, 3 * H, m->cfg.head_dim, 64))) return rc;
+  }
   return NEBW_OK;
 }
 
@@ -1133,7 +1172,7 @@ int encode_device(nebw_model *m, Workspace &ws, bool prof, const int *ids, const
   if ((rc = prof_mark(m, prof, NEBW_K_PACK, st))) return rc;
   if ((rc = launch_pack(len_in, B, S, ws.len, ws.off, d->d_err, st))) return rc;
   const bool tc_attention =
-      d->attn_kind == NEBW_ATTN_TCGEN05 && c.head_dim == nebw::kAttnTcD;
+      d->attn_kind == NEBW_ATTN_TCGEN05 && nebw::attn_tc_head_dim(c.head_dim);
   if (tc_attention) {
     // with the work list, zero the Q|K|V and A rows just past the packed
     // rows, up to the workspace's extent (the attention's last partial key
@@ -1186,8 +1225,8 @@ int encode_device(nebw_model *m, Workspace &ws, bool prof, const int *ids, const
     if ((rc = prof_mark(m, prof, NEBW_K_ATTENTION, st))) return rc;
     if (c.rope && !rope_fused && (rc = launch_rope(m, ws, B, S, st))) return rc;
     if (tc_attention)
-      rc = launch_attention_tc(d, ws.map_qkv_att, ws.map_kv_att, ws.off, ws.len, ws.att_items + 1, ws.att_items, B, S,
-                               c.num_heads, ws.ctx, st);
+      rc = launch_attention_tc(d, ws.map_qkv_att, ws.map_kv_att, ws.off, ws.len, ws.att_items + 1,
+                               ws.att_items, B, S, c.num_heads, c.head_dim, ws.ctx, st);
     else
       rc = launch_attention(ws.qkv, ws.off, ws.len, B, S, c.num_heads, c.head_dim, ws.ctx, st);
     if (rc)
@@ -1460,6 +1499,23 @@ constexpr char kTmaLayoutHash[] =
 }  // namespace
 
 extern "C" const char *nebw_tma_layout_hash(void) { return kTmaLayoutHash; }
+
+extern "C" int nebw_pack_checkpoint(const char *model_dir, const char *out_path,
+                                    const char *layout, int32_t max_seq, int32_t fold_scale,
+                                    uint64_t *bytes) {
+  NEBW_REQUIRE(model_dir && out_path, "null path");
+  nebw::PackOptions opt;
+  if (layout) opt.layout = layout;
+  if (max_seq > 0) opt.max_seq = max_seq;
+  opt.fold_scale = fold_scale != 0;
+  try {
+    const uint64_t n = nebw::pack_checkpoint(model_dir, out_path, opt);
+    if (bytes) *bytes = n;
+  } catch (const std::exception &e) {
+    return set_error(NEBW_EIO, "pack %s: %s", model_dir, e.what());
+  }
+  return NEBW_OK;
+}
 
 namespace {
 // A block_panel GEMM operand -- the reference's pre-tiled array layout, BF16
@@ -1786,7 +1842,7 @@ extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   if (!m) return set_error(NEBW_EINVAL, "null model"), -1;
   const int S = seq > 0 ? seq : m->cfg.max_seq_len;
   const bool tc =
-      m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD;
+      m->dev->attn_kind == NEBW_ATTN_TCGEN05 && nebw::attn_tc_head_dim(m->cfg.head_dim);
   const bool rope_fused = rope_in_epilogue(m);
   const int per_layer = 6 + attention_launches(tc ? 64 : 0, S) +
                         (m->cfg.rope && !rope_fused ? 1 : 0) +

@@ -314,6 +314,23 @@ __device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr) {
          (static_cast<uint64_t>(2) << 61);
 }
 
+// The same two layouts with 64-byte swizzle, for tiles whose rows are 32
+// bf16 (64 B): eight rows per 512-byte atom, so the stride between 8-row
+// groups is 512 B; layout type 4 = 64-byte swizzle.  K-major: advancing K by
+// 16 elements inside a row is +32 B.  MN-major ([K rows x 32 MN-elements],
+// one atom wide): advancing K by 16 rows is +1024 B.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw64(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(512 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(4) << 61);
+}
+
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw64(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(512 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(4) << 61);
+}
+
 // Instruction descriptor for tcgen05.mma kind::f16 with bf16 A and B, fp32
 // D, both operands K-major, dense:
 //   bits 4-5 D format (1 = f32); 7-9 A format (1 = bf16); 10-12 B format

@@ -121,8 +121,10 @@ int vit_ensure_workspace(nebw_vit *m, int64_t n) {
   if ((rc = make_tmap_out(&m->out_h, m->h, R, F, true))) return rc;
   if ((rc = make_tmap_out(&m->out_y, m->y, R, H, true))) return rc;
   if ((rc = make_tmap_out(&m->out_pe, m->h, NP, H, false))) return rc;
-  if ((rc = make_tmap_kmajor(&m->map_qkv_att, m->qkv, R, 3 * H, 128))) return rc;
-  if ((rc = make_tmap_kmajor(&m->map_kv_att, m->qkv, R, 3 * H, 64))) return rc;
+  if (nebw::attn_tc_head_dim(m->cfg.head_dim)) {
+    if ((rc = make_tmap_head(&m->map_qkv_att, m->qkv, R, 3 * H, m->cfg.head_dim, 128))) return rc;
+    if ((rc = make_tmap_head(&m->map_kv_att, m->qkv, R, 3 * H, m->cfg.head_dim, 64))) return rc;
+  }
   return NEBW_OK;
 }
 
@@ -193,7 +195,7 @@ int launch_ln_rows(float *x, const __nv_bfloat16 *y, int64_t stride, int64_t row
 }
 
 bool vit_tc_attention(const nebw_vit *m) {
-  return m->dev->attn_kind == NEBW_ATTN_TCGEN05 && m->cfg.head_dim == nebw::kAttnTcD;
+  return m->dev->attn_kind == NEBW_ATTN_TCGEN05 && nebw::attn_tc_head_dim(m->cfg.head_dim);
 }
 
 int vit_encode_device(nebw_vit *m, const float *images, int n, float *out, cudaStream_t st) {
@@ -266,8 +268,8 @@ int vit_encode_device(nebw_vit *m, const float *images, int n, float *out, cudaS
     if ((rc = launch_gemm(d, w.qkv, m->map_a, m->out_qkv, nebw::kEpiBf16, a, st))) return rc;
     if ((rc = vit_mark(m, NEBW_K_ATTENTION, st))) return rc;
     if (tc)
-      rc = launch_attention_tc(d, m->map_qkv_att, m->map_kv_att, m->off, m->len, m->att_items + 1, m->att_items,
-                               n, m->n_pos, c.num_heads, m->ctx, st);
+      rc = launch_attention_tc(d, m->map_qkv_att, m->map_kv_att, m->off, m->len, m->att_items + 1,
+                               m->att_items, n, m->n_pos, c.num_heads, c.head_dim, m->ctx, st);
     else
       rc = launch_attention(m->qkv, m->off, m->len, n, m->n_pos, c.num_heads, c.head_dim, m->ctx,
                             st);

@@ -12,6 +12,9 @@
 //       --vocab, then encoded on the GPU
 //   nebw_embed --tokenize <model.npue|vocab.txt> <texts.txt> <seq> <ids.i32> <mask.i32>
 //       the tokenizer alone (no GPU): the ids and mask files of the first form
+//   nebw_embed --prepare-model <checkpoint_dir> <out.npue> [tma_bf16|host] [max_seq]
+//       the packer (no GPU): a Hugging Face BERT checkpoint -> a container
+//       (the runtime's --prepare-model, runtime/src/cli/cli.cpp:60)
 //
 // Exit status 0 on success, 1 with the cause on stderr otherwise.
 #include <cstdio>
@@ -88,14 +91,25 @@ int usage(const char *argv0) {
   std::fprintf(stderr,
                "usage: %s <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [device]\n"
                "       %s --text <model.npue> <texts.txt> <seq> <out.f32> [device] [--vocab v.txt]\n"
-               "       %s --tokenize <model.npue|vocab.txt> <texts.txt> <seq> <ids.i32> <mask.i32>\n",
-               argv0, argv0, argv0);
+               "       %s --tokenize <model.npue|vocab.txt> <texts.txt> <seq> <ids.i32> <mask.i32>\n"
+               "       %s --prepare-model <checkpoint_dir> <out.npue> [tma_bf16|host] [max_seq]\n",
+               argv0, argv0, argv0, argv0);
   return 2;
 }
 }  // namespace
 
 int main(int argc, char **argv) {
   try {
+    if (argc >= 2 && std::strcmp(argv[1], "--prepare-model") == 0) {
+      if (argc < 4 || argc > 6) return usage(argv[0]);
+      const char *layout = argc > 4 ? argv[4] : "tma_bf16";
+      const int max_seq = argc > 5 ? std::atoi(argv[5]) : 0;
+      uint64_t bytes = 0;
+      nebw::check(nebw_pack_checkpoint(argv[2], argv[3], layout, max_seq, 1, &bytes));
+      std::printf("%s: %llu bytes, layout %s\n", argv[3], static_cast<unsigned long long>(bytes),
+                  layout);
+      return 0;
+    }
     if (argc >= 2 && std::strcmp(argv[1], "--tokenize") == 0) {
       if (argc != 7) return usage(argv[0]);
       const nebw::WordPiece wp = load_vocab(argv[2]);

@@ -117,6 +117,8 @@ def lib() -> C.CDLL:
         "nebw_vit_profile": ([vp, C.c_int], C.c_int),
         "nebw_vit_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
         "nebw_check_bounded_wait": ([vp, i64, C.POINTER(i32)], C.c_int),
+        "nebw_pack_checkpoint": ([C.c_char_p, C.c_char_p, C.c_char_p, i32, i32,
+                                  C.POINTER(C.c_uint64)], C.c_int),
         "nebw_comm_unique_id": ([vp], C.c_int),
         "nebw_comm_init_rank": ([vp, i32, i32, vp, C.c_double, C.POINTER(vp)], C.c_int),
         "nebw_comm_init_all": ([i32, C.POINTER(vp), C.c_double, C.POINTER(vp)], C.c_int),
@@ -573,3 +575,13 @@ def encode_multi(models, comms, ids: np.ndarray, lens: np.ndarray) -> np.ndarray
     _check(lib().nebw_encode_multi(n, mh, ch, ids.ctypes.data, lens.ctypes.data, B, S,
                                    out.ctypes.data))
     return out
+
+
+def pack_checkpoint(model_dir, out, layout: str = "tma_bf16", max_seq: int = 0,
+                    fold_scale: bool = True) -> int:
+    """The library's C++ packer (nebw_pack_checkpoint); returns the bytes written."""
+    n = C.c_uint64()
+    _check(lib().nebw_pack_checkpoint(str(model_dir).encode(), str(out).encode(),
+                                      layout.encode(), int(max_seq), int(fold_scale),
+                                      C.byref(n)))
+    return n.value

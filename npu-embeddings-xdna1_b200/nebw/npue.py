@@ -237,7 +237,8 @@ def _add_gemm_operand(w, name, kn, pretiled: bool, i8: bool, tile, mac, srng):
 
 def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synthetic/random-init",
                          config_overrides: dict | None = None, gemm_layout: str = "host",
-                         a_dtype: str = "bf16", tile=(64, 32), mac=(8, 8), smooth_seed: int = 0):
+                         a_dtype: str = "bf16", tile=(64, 32), mac=(8, 8), smooth_seed: int = 0,
+                         vocab: bytes | None = None):
     """Write a BERT (arch 0) container in the host layout the reference's CPU
     path reads: GEMM operands F32 row-major [K, N] (`gemm_b_host`), biases and
     LayerNorm F32, embeddings F32.  Tensor names and config keys follow the
@@ -251,7 +252,10 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
     layout_hash, as bf16 (a_dtype "bf16") or as int8 (a_dtype "i8") with its
     per-column `.wscale` and the activation's SmoothQuant divisor `.asmooth`
     (seeded positive factors, not calibrated: any factors describe the same
-    model, W' = diag(asmooth) W against A / asmooth)."""
+    model, W' = diag(asmooth) W against A / asmooth).
+
+    vocab: the WordPiece vocabulary file's bytes, stored as the packer stores
+    it (`tokenizer.vocab`, U8), for the runtime's tokenizer."""
     if gemm_layout not in ("host", "pretiled_bf16") or a_dtype not in ("bf16", "i8"):
         raise ValueError(f"gemm_layout {gemm_layout!r} / a_dtype {a_dtype!r}")
     pretiled = gemm_layout == "pretiled_bf16"
@@ -321,6 +325,9 @@ def write_bert_container(path, model, max_seq_len: int, source_repo: str = "synt
     w.add("embeddings.token_type", model.typ, "F32", "embedding", [model.typ.shape[0], H])
     w.add("embeddings.ln.weight", model.emb_ln_g, "F32", "layernorm", [H])
     w.add("embeddings.ln.bias", model.emb_ln_b, "F32", "layernorm", [H])
+    if vocab is not None:
+        vb = np.frombuffer(vocab, dtype=np.uint8)
+        w.add("tokenizer.vocab", vb, "U8", "tokenizer", [int(vb.size)])
     for i in range(L):
         p = f"layer.{i}."
         gemm(p + "qkv", model.w_qkv[i])

@@ -85,15 +85,17 @@ def test_bge_base_geometry_vs_oracle(device, port_oracle):
     m.close()
 
 
+@pytest.mark.parametrize("arch", ["BGE_BASE", "BGE_SMALL"])
 @pytest.mark.parametrize("kind", [0, 1])
-def test_attention_kind_encoder_vs_oracle(device, port_oracle, kind):
+def test_attention_kind_encoder_vs_oracle(device, port_oracle, kind, arch):
     """The whole pass with each attention kernel (0 mma.sync, 1 tcgen05, the
-    default) across key-block and query-tile boundaries: lengths on, just
-    under and just over multiples of 64 (the tcgen05 kernel's key block) and
-    128 (its query tile), partial 16-key groups, 1 and 512."""
+    default) at head_dim 64 (bge-base) and 32 (bge-small) across key-block
+    and query-tile boundaries: lengths on, just under and just over multiples
+    of 64 (the tcgen05 kernel's key block) and 128 (its query tile), partial
+    16-key groups, 1 and 512."""
     import nebw
     from nebw import synth
-    w = synth.make_weights(synth.BGE_BASE, seed=19, cls_pool=True, layers=2)
+    w = synth.make_weights(getattr(synth, arch), seed=19, cls_pool=True, layers=2)
     lens = np.array([512, 300, 8, 129, 128, 1, 256, 257, 63, 64, 65, 200, 17], np.int32)
     ids, mask = synth.make_tokens(len(lens), 512, lens, seed=20)
     device.set_attention_kernel(kind)
@@ -104,7 +106,7 @@ def test_attention_kind_encoder_vs_oracle(device, port_oracle, kind):
     finally:
         device.set_attention_kernel(device.ATTN_TCGEN05)
     want = port_oracle.encode(w, ids, mask)
-    check(got, want, f"attention kind {kind}")
+    check(got, want, f"attention kind {kind}, {arch}")
 
 
 def test_npue_container_roundtrip(device, port_oracle, minilm, tmp_path):

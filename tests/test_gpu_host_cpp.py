@@ -1,13 +1,15 @@
 """The C++ host side (host/gpu_bert_encoder.hpp through host/nebw_embed) on a
 B200: file in, file out, against the CPU oracle, including the reference's
-empty-row behaviour (mean pooling: zero vector; CLS pooling: refused)."""
+empty-row behaviour (mean pooling: zero vector; CLS pooling: refused); and
+the serving drop-in (host/npue_gpu_encoder.hpp) compiled against the
+reference's own headers and tokenizer (oracle/_ref/npue_encoder_check)."""
 
 import subprocess
 
 import numpy as np
 import pytest
 
-from conftest import PKG, parity
+from conftest import PKG, REPO, parity
 
 pytestmark = pytest.mark.gpu
 
@@ -89,3 +91,71 @@ def test_cpp_tool_text_path(tmp_path, port_oracle):
     want = port_oracle.encode(_weights_from_container(tmp_path / "host.npue"), ids, mask)
     cos, err = parity(got, want)
     assert np.isfinite(got).all() and cos >= 0.9999 and err <= 2e-3, (cos, err)
+
+
+CHECK = REPO / "oracle" / "_ref" / "npue_encoder_check"
+
+
+def synthetic_vocab(n: int) -> bytes:
+    """A WordPiece vocabulary of n entries: the specials, whole words w0..,
+    and '##' continuations of single digits."""
+    words = ["[PAD]", "[UNK]", "[CLS]", "[SEP]", "[MASK]"] + [f"##{d}" for d in range(10)]
+    words += [f"w{i}" for i in range(n - len(words))]
+    return ("\n".join(words) + "\n").encode()
+
+
+def synthetic_texts(n: int, seed: int, max_words: int) -> list:
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(n):
+        k = int(rng.integers(1, max_words + 1))
+        ws = [f"w{int(x)}" for x in rng.integers(0, 30000, k)]
+        if i % 7 == 0:
+            ws.append(f"W{int(rng.integers(0, 99))}99999!")  # case fold, "##" digits, punctuation
+        out.append(" ".join(ws))
+    return out
+
+
+@pytest.mark.skipif(not CHECK.exists(),
+                    reason="built only where the reference tree is (oracle/Makefile encoder_check)")
+def test_npue_encoder_adapter_through_reference_interface(tmp_path, port_oracle):
+    """nebw::GpuNpueEncoder as the reference's npue::Encoder, with the
+    reference's own tokenizer (app::load_tokenizer on the container): texts
+    -> embeddings, against the CPU oracle on the very ids and mask that
+    tokenizer produced; those ids equal this repo's WordPiece's."""
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    w = synth.make_weights(synth.BGE_SMALL, seed=71, cls_pool=True, layers=2)
+    vocab = synthetic_vocab(w.vocab)
+    model = tmp_path / "m.npue"
+    write_bert_container(model, w, max_seq_len=128, vocab=vocab)
+    texts = synthetic_texts(24, 72, 140) + ["", "W1 w2, w3."]
+    (tmp_path / "t.txt").write_text("\n".join(texts) + "\n")
+    r = subprocess.run([str(CHECK), str(model), str(tmp_path / "t.txt"), "128",
+                        str(tmp_path / "out.f32"), str(tmp_path / "ids.i32"),
+                        str(tmp_path / "mask.i32")], capture_output=True, text=True, timeout=300)
+    # a text longer than 128 tokens is refused, as the runtime refuses it
+    assert r.returncode == 1 and "tokens; the limit is 128" in r.stderr, r.stdout + r.stderr
+    texts = synthetic_texts(24, 72, 90) + ["", "W1 w2, w3."]
+    (tmp_path / "t.txt").write_text("\n".join(texts) + "\n")
+    r = subprocess.run([str(CHECK), str(model), str(tmp_path / "t.txt"), "128",
+                        str(tmp_path / "out.f32"), str(tmp_path / "ids.i32"),
+                        str(tmp_path / "mask.i32")], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    n = len(texts)
+    got = np.fromfile(tmp_path / "out.f32", np.float32).reshape(n, w.hidden)
+    ids = np.fromfile(tmp_path / "ids.i32", np.int32).reshape(n, 128)
+    mask = np.fromfile(tmp_path / "mask.i32", np.int32).reshape(n, 128)
+    assert (ids[:, 0] == 2).all() and int(r.stdout.split()[3]) == int(mask.sum())
+    want = port_oracle.encode(w, ids, mask)
+    cos, err = parity(got, want)
+    assert np.isfinite(got).all() and cos >= 0.9999 and err <= 2e-3, (cos, err)
+    # this repo's tokenizer gives the same ids and mask
+    (tmp_path / "v.txt").write_bytes(vocab)
+    r = subprocess.run([str(TOOL), "--tokenize", str(tmp_path / "v.txt"), str(tmp_path / "t.txt"),
+                        "128", str(tmp_path / "ids2.i32"), str(tmp_path / "mask2.i32")],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "ids2.i32", np.int32).reshape(n, 128), ids)
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "mask2.i32", np.int32).reshape(n, 128),
+                                  mask)

@@ -209,9 +209,11 @@ def _packed(lens):
     return off, int(off[-1])
 
 
-@pytest.mark.parametrize("D,heads,kind", [(32, 12, 0), (64, 16, 0), (64, 16, 1), (64, 12, 1)])
+@pytest.mark.parametrize("D,heads,kind", [(32, 12, 0), (64, 16, 0), (64, 16, 1), (64, 12, 1),
+                                          (32, 12, 1), (32, 16, 1)])
 def test_attention_matches_float64(device, D, heads, kind):
-    """kind 0: mma.sync flash kernel; kind 1: tcgen05 kernel (head_dim 64)."""
+    """kind 0: mma.sync flash kernel; kind 1: tcgen05 kernel (head_dim 64
+    with 128-byte swizzled head tiles, head_dim 32 with 64-byte ones)."""
     rng = np.random.default_rng(D + kind)
     lens = np.array([1, 8, 63, 64, 65, 127, 128, 129, 130, 512, 200, 257], np.int32)
     off, T = _packed(lens)

@@ -162,6 +162,79 @@ def test_pack_refuses_other_models(tmp_path):
         pack_bert(d, tmp_path / "x.npue")
 
 
+# ---- the C++ packer in the library (nebw_pack_checkpoint) ----
+
+@pytest.mark.parametrize("layout", ["host", "tma_bf16"])
+@pytest.mark.parametrize("fold", [True, False])
+def test_cpp_packer_is_byte_identical(tmp_path, layout, fold):
+    """nebw_pack_checkpoint (C++, host only) writes the very bytes nebw.pack
+    writes -- header, JSON directory (config keys and number formatting,
+    source SHA-256, layout hash) and every tensor; the host layout is thereby
+    pinned to the reference packer's golden through the test above."""
+    from make_pack_golden import MAX_SEQ, describe
+
+    import nebw
+    from nebw.pack import pack_bert
+    d = _checkpoint(tmp_path)
+    pack_bert(d, tmp_path / "py.npue", layout=layout, max_seq=MAX_SEQ, fold_scale=fold)
+    n = nebw.pack_checkpoint(d, tmp_path / "cc.npue", layout, MAX_SEQ, fold)
+    want = (tmp_path / "py.npue").read_bytes()
+    assert n == len(want)
+    assert (tmp_path / "cc.npue").read_bytes() == want
+    if layout == "host" and fold:
+        golden = json.loads((GOLDEN / "pack_tiny_bert.json").read_text())
+        got = describe(tmp_path / "cc.npue")
+        assert got["config"] == golden["config"] and got["order"] == golden["order"]
+
+
+def test_cpp_packer_reads_bf16_and_f16_checkpoints(tmp_path):
+    """A checkpoint stored as BF16 / F16 safetensors (widened exactly) packs
+    to the same bytes in C++ and Python, prefixed tensor names included."""
+    import nebw
+    from nebw.pack import pack_bert, read_safetensors
+    d = _checkpoint(tmp_path)
+    src = read_safetensors(d / "model.safetensors")
+    hdr, blobs, off = {}, [], 0
+    for i, (name, a) in enumerate(sorted(src.items())):
+        if i % 2:
+            b = (a.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
+            dt = "BF16"
+        else:
+            b = a.astype(np.float16).tobytes()
+            dt = "F16"
+        hdr["bert." + name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(hdr).encode()
+    (d / "model.safetensors").write_bytes(len(h).to_bytes(8, "little") + h + b"".join(blobs))
+    pack_bert(d, tmp_path / "py.npue", layout="tma_bf16", max_seq=32)
+    nebw.pack_checkpoint(d, tmp_path / "cc.npue", "tma_bf16", 32, True)
+    assert (tmp_path / "cc.npue").read_bytes() == (tmp_path / "py.npue").read_bytes()
+
+
+def test_cpp_packer_refusals(tmp_path):
+    import nebw
+    d = _checkpoint(tmp_path)
+    with pytest.raises(nebw.NebwError, match="layout"):
+        nebw.pack_checkpoint(d, tmp_path / "x.npue", "panels", 32, True)
+    cfg = json.loads((d / "config.json").read_text())
+    cfg["model_type"] = "vit"
+    (d / "config.json").write_text(json.dumps(cfg))
+    with pytest.raises(nebw.NebwError, match="model_type"):
+        nebw.pack_checkpoint(d, tmp_path / "x.npue", "host", 32, True)
+    cfg["model_type"] = "bert"
+    (d / "config.json").write_text(json.dumps(cfg))
+    (d / "1_Pooling" / "config.json").write_text(json.dumps({"pooling_mode_max_tokens": True}))
+    with pytest.raises(nebw.NebwError, match="pooling"):
+        nebw.pack_checkpoint(d, tmp_path / "x.npue", "host", 32, True)
+    with pytest.raises(nebw.NebwError, match="config.json"):
+        nebw.pack_checkpoint(tmp_path, tmp_path / "x.npue", "host", 32, True)
+    (d / "model.safetensors").unlink()
+    (d / "1_Pooling" / "config.json").write_text(json.dumps({"pooling_mode_cls_token": True}))
+    with pytest.raises(nebw.NebwError, match="safetensors"):
+        nebw.pack_checkpoint(d, tmp_path / "x.npue", "host", 32, True)
+
+
 # ---- the reference's pre-tiled containers (block panels, bf16 / int8) ----
 
 def test_block_panel_order_and_round_trip():
