@@ -177,6 +177,35 @@ int nebw_pool_l2(nebw_dev *dev, const float *h, const int32_t *seq_off, const in
  * host_kernels.hpp:157-161). */
 int nebw_narrow_bf16(nebw_dev *dev, const float *x, int64_t n, void *y_bf16, void *stream);
 
+/* ---- the int8 datapath (the reference's --dtype i8 array path) ------------
+ * The array path of an int8 container quantises each GEMM input per row,
+ * multiplies int8 x int8 into int32 and dequantises C on the host
+ * (host_kernels.hpp:263-614).  These run those steps on the GPU and return
+ * the reference's bits (the product is exact; each floating-point step is
+ * the reference's single IEEE operation). */
+
+/* app::quantise_a_int8 (host_kernels.hpp:263-315), per row of x [rows, K]
+ * fp32 with the SmoothQuant divisor ias [K]: sc = max|x * ias| / 127 (1 for
+ * an all-zero row), q = rne(clamp(x * ias * (1 / sc), -127, 127)).  q int8
+ * [rows, K], scale fp32 [rows]; device buffers, asynchronous. */
+int nebw_quantise_rows(nebw_dev *dev, const float *x, int64_t rows, int64_t K, const float *ias,
+                       int8_t *q, float *scale, void *stream);
+/* An int8 GEMM operand, the container's int8 panel untiled to row-major
+ * [K, N] (host), staged once as [N, K] (the tensor-core B layout).
+ * K % 16 == 0, N % 8 == 0.  Released with nebw_release_weight. */
+int nebw_stage_weight_i8(nebw_dev *dev, const int8_t *host_kn, int64_t K, int64_t N,
+                         uint64_t *handle);
+/* C = dequant(A . W) on tcgen05.mma kind::i8: A int8 [M, K] device (rows
+ * quantised with scale sa [M]), int32 accumulation, then app::dequantise_c
+ * (host_kernels.hpp:575-613) y = fma(float(acc) * sa[row], ws[col], bias[col])
+ * (bias NULL: 0), act NEBW_ACT_GELU8 applies gelu8 after it (the FFN-up step
+ * of app::dequant_act_quant, host_kernels.hpp:404-526, whose quantisation for
+ * the next GEMM is then nebw_quantise_rows).  C fp32 [M, N] device; C, ws and
+ * bias 16-byte aligned.  Asynchronous on `stream`. */
+int nebw_gemm_i8(nebw_dev *dev, uint64_t weight, const int8_t *A, const float *sa, int64_t M,
+                 int64_t K, int64_t N, const float *ws, const float *bias, int act, float *C,
+                 void *stream);
+
 /* ---- the whole encoder -------------------------------------------------- */
 
 /* Geometry a container's config carries (set_model_shape,

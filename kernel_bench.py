@@ -119,6 +119,39 @@ def bench_layernorm(dev, M, H, iters, copies):
     return {"kernel": "layernorm", "M": M, "H": H, "ms": ms, "gbs": by / ms / 1e6}
 
 
+def bench_gemm_i8(dev, M, K, N, epi, iters, copies):
+    """The int8 GEMM (tcgen05 kind::i8) with the dequantise (or dequantise +
+    gelu8) epilogue, fp32 out."""
+    import torch
+    rng = np.random.default_rng(0)
+    h = dev.stage_weight_i8(rng.integers(-127, 128, (K, N), dtype=np.int8))
+    ws = torch.rand(N, device="cuda") * 1e-3
+    bias = torch.randn(N, device="cuda") * 0.02
+    As = [torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda") for _ in range(copies)]
+    sa = torch.rand(M, device="cuda") * 1e-2
+    Cs = [torch.empty(M, N, device="cuda") for _ in range(copies)]
+    act = 1 if epi == "gelu8" else 0
+
+    def run(i):
+        dev.gemm_i8(h, As[i % copies], sa, M, K, N, ws, Cs[i % copies], bias=bias, act=act,
+                    stream=torch.cuda.current_stream())
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    ms = e0.elapsed_time(e1) / iters
+    ops = 2.0 * M * N * K
+    return {"kernel": "gemm_i8", "M": M, "K": K, "N": N, "epi": epi, "ms": ms,
+            "tops": ops / (ms / 1e3) / 1e12}
+
+
 def bench_encoder(dev, config, layers, iters):
     """Whole passes of a benchmark configuration's batch through a model of
     `layers` layers (the production launch sequence, attention work list
@@ -159,7 +192,7 @@ def bench_encoder(dev, config, layers, iters):
 def main(argv=None):
     import nebw
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "attention", "layernorm", "encoder"])
+    ap.add_argument("op", choices=["gemm", "gemm_i8", "attention", "layernorm", "encoder"])
     ap.add_argument("--config", default="bge-large")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--M", type=int, default=16384)
@@ -179,6 +212,8 @@ def main(argv=None):
     dev.set_attention_kernel(a.attn_kind)
     if a.op == "gemm":
         r = bench_gemm(dev, a.M, a.K, a.N, a.epi, a.iters, a.copies)
+    elif a.op == "gemm_i8":
+        r = bench_gemm_i8(dev, a.M, a.K, a.N, a.epi, a.iters, a.copies)
     elif a.op == "attention":
         r = bench_attention(dev, a.B, a.len, a.heads, a.hd, a.iters, a.copies)
     elif a.op == "layernorm":

@@ -1,0 +1,292 @@
+// The int8 datapath of the reference's `--dtype i8` containers on the
+// sm_100a tensor cores.
+//
+// The reference's array path quantises each GEMM input per row to int8 with
+// its SmoothQuant divisor folded in, multiplies int8 x int8 into int32 on the
+// NPU, and dequantises C on the host (app::quantise_a_int8,
+// app::dequantise_c, app::dequant_act_quant; runtime/include/common/
+// host_kernels.hpp:263-614).  Here:
+//
+//   quantise_rows_kernel   q = rne(clamp(x * ias * (1 / sc), +-127)),
+//                          sc = max|x * ias| / 127 (1 when the row is 0);
+//                          one warp per row
+//   gemm_i8_kernel         C = A_q . W_q^T in int32 on tcgen05.mma kind::i8
+//                          (exact), dequantised in the epilogue as
+//                          y = fma(float(C) * sa[row], ws[col], bias[col]),
+//                          optionally gelu8(y) (dequant_act_quant's act),
+//                          fp32 out
+//
+// The integer product is exact and every floating-point step is the
+// reference's single IEEE operation in its order (int -> float round to
+// nearest even, the product, one fused multiply-add; the divisions are
+// IEEE), so both kernels reproduce the reference's steps bit for bit.  The
+// FFN-up step dequant_act_quant is gemm_i8 with gelu8 followed by
+// quantise_rows with the next GEMM's divisor.
+//
+// The GEMM is the single-CTA structure of gemm_tc_kernel (TMA producer warp,
+// one MMA-issuing warp, eight epilogue warps, a double-buffered TMEM
+// accumulator) with 128-byte K-blocks: 128 int8 per row instead of 64 bf16,
+// the same swizzled tiles and stage sizes, four K=32 MMAs per block.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+#include "gemm_tc.cuh"
+#include "ptx.cuh"
+
+namespace nebw {
+
+constexpr int kGemmI8BK = 128;  // int8 elements per K-block (one 128-byte row)
+
+struct GemmI8Args {
+  int M, N, K;
+  const float *sa;    // [M] row scales of A (quantise_rows' sc)
+  const float *ws;    // [N] column scales of W
+  const float *bias;  // [N] or null (then 0)
+  float *out;         // [M, N] fp32
+  int *err;
+};
+
+// Instruction descriptor for tcgen05.mma kind::i8: s8 A and B, s32 D, both
+// K-major, dense: bits 4-5 D format (2 = s32), 7-9 A (1 = signed 8-bit),
+// 10-12 B (1 = signed 8-bit), 17-22 N >> 3, 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, s8 in, s32 accumulate, K = 32.
+__device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// One row per warp: quantise_a_int8 (host_kernels.hpp:263-315).  The row
+// maximum is order-independent, so the warp reduction gives the reference's
+// value exactly; sc = mx / 127 and inv = 1 / sc are IEEE divisions.
+__global__ void __launch_bounds__(256)
+    quantise_rows_kernel(const float *__restrict__ x, int rows, int K,
+                         const float *__restrict__ ias, int8_t *__restrict__ q,
+                         float *__restrict__ scale) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *xr = x + static_cast<int64_t>(row) * K;
+  float mx = 0.0f;
+  for (int j = lane; j < K; j += 32) mx = fmaxf(mx, fabsf(xr[j] * __ldg(ias + j)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+  const float inv = 1.0f / sc;
+  if (lane == 0) scale[row] = sc;
+  int8_t *qr = q + static_cast<int64_t>(row) * K;
+  for (int j = lane; j < K; j += 32) {
+    const float t = fminf(fmaxf((xr[j] * __ldg(ias + j)) * inv, -127.0f), 127.0f);
+    qr[j] = static_cast<int8_t>(__float2int_rn(t));
+  }
+}
+
+// Dequantise (and gelu8) 32 accumulator columns [col0, col0 + 32) of one row
+// and store them as fp32.
+template <bool GELU>
+__device__ __forceinline__ void i8_store32(const GemmI8Args &p, int row, int col0,
+                                           const uint32_t (&r)[32]) {
+  const int ncols = min(32, p.N - col0);  // N % 8 == 0
+  const float sa = __ldg(p.sa + row);
+  float4 *o4 = reinterpret_cast<float4 *>(p.out + static_cast<size_t>(row) * p.N + col0);
+  const float4 *w4 = reinterpret_cast<const float4 *>(p.ws + col0);
+  const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i * 4 >= ncols) break;
+    const float4 w = __ldg(w4 + i);
+    const float4 b = p.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float y[4];
+    const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float c = __int2float_rn(static_cast<int>(r[4 * i + e]));
+      y[e] = fmaf(c * sa, ws[e], bs[e]);
+      if constexpr (GELU) y[e] = gelu8(y[e]);
+    }
+    o4[i] = make_float4(y[0], y[1], y[2], y[3]);
+  }
+}
+
+// C[M, N] = dequant(A_q[M, K] . W_q[N, K]^T): A and W int8, K-major, read by
+// TMA in 128 x 128-byte (A) and BN x 128-byte (W) swizzled boxes.  One CTA
+// per SM, persistent over 128 x BN tiles.  Every wait is bounded.
+template <int BN, bool GELU>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const GemmI8Args p) {
+  using S = GemmShape<BN>;  // a 128-byte row of int8 is the size of one of bf16
+  constexpr int kStages = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sW = smem + kStages * S::kABytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *tfull = empty + kStages;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = p.M;
+  const int m_blocks = (M + kGemmBM - 1) / kGemmBM;
+  const int n_blocks = (p.N + BN - 1) / BN;
+  const int num_tiles = m_blocks * n_blocks;
+  const int num_kb = (p.K + kGemmI8BK - 1) / kGemmI8BK;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile / n_blocks, nb = tile % n_blocks;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          tma_load_2d(sA + stage * S::kABytes, &tmA, &full[stage], kb * kGemmI8BK, mb * kGemmBM);
+          tma_load_2d(sW + stage * S::kBBytes, &tmW, &full[stage], kb * kGemmI8BK, nb * BN);
+          issued_mask |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      for (int s = 0; s < kStages; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_phase >> s) & 1u, p.err);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: four K=32 int8 MMAs per 128-byte block ----
+    constexpr uint32_t idesc = idesc_s8_s32(kGemmBM, BN);
+    const bool elect = elect_one_sync();
+    auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
+    };
+    int stage = 0;
+    uint32_t phase = 0;
+    bool issued_any = false, ok = true;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!wait_all(&tempty[acc], acc_phase ^ 1u)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!wait_all(&full[stage], phase)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + stage * S::kABytes));
+        const uint64_t dw = sdesc_kmajor_sw128(smem_u32(sW + stage * S::kBBytes));
+        if (elect) {
+#pragma unroll
+          for (int k = 0; k < kGemmI8BK / 32; ++k)  // +32 B per 32 int8 of K
+            umma_s8(d_tmem, da + k * 2, dw + k * 2, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        issued_any = true;
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok && elect) umma_commit(&tfull[acc]);
+      __syncwarp();
+    }
+    if (issued_any) {
+      if (elect) umma_commit(drain);
+      __syncwarp();
+      wait_all(drain, 0);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9): int32 rows out of TMEM ----------
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / 32;
+    const int quarter = warp & 3;
+    const int col_half = ((warp - 2) >> 2) * kHalf;
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, p.err))) break;
+      tc_fence_after();
+      const int mb = tile / n_blocks, nb = tile % n_blocks;
+      const int row = mb * kGemmBM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + col_half);
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(t_row, ra);
+      tmem_wait_ld_regs(ra);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        if (c + 1 < kChunks) tmem_ld_32x32b_x32(t_row + (c + 1) * 32, nxt);
+        if (c + 1 == kChunks) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        const int col0 = nb * BN + col_half + c * 32;
+        if (row < M && col0 < p.N) i8_store32<GELU>(p, row, col0, cur);
+        if (c + 1 < kChunks) tmem_wait_ld_regs(nxt);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::kTmemCols);
+  }
+}
+
+}  // namespace nebw

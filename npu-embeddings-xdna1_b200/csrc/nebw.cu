@@ -45,6 +45,7 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "gated.cuh"
+#include "gemm_i8.cuh"
 #include "gemm_tc.cuh"
 #include "npue_file.h"
 #include "npue_pack.h"
@@ -157,6 +158,26 @@ int make_tmap_head(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols
   return NEBW_OK;
 }
 
+// An int8 K-major map [rows, K] with {128, box_rows} boxes (128-byte rows,
+// 128-byte swizzle): the int8 GEMM's A and W tiles.  K % 16 == 0.
+int make_tmap_i8(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int box_rows) {
+  if (int rc = load_tensor_map_encoder()) return rc;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return set_error(NEBW_EINVAL, "int8 GEMM operand address is not 16-byte aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(nebw::kGemmI8BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NEBW_ECUDA, "cuTensorMapEncodeTiled (int8) failed (%d) for [%lld, %lld]",
+                     static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(K));
+  return NEBW_OK;
+}
+
 // A 2-D row-major output tensor map [rows, N] with a 32 x 32 box (the GEMM
 // epilogue's TMA store chunk): fp32 rows of the box are 128 bytes (128-byte
 // swizzle), bf16 rows 64 bytes (64-byte swizzle).
@@ -192,6 +213,12 @@ struct Weight {
   CUtensorMap map64, map128, map256;  // box rows 64 / 128 / 256
 };
 
+struct WeightI8 {
+  int8_t *ptr = nullptr;  // [N, K] int8
+  int64_t K = 0, N = 0;
+  CUtensorMap map128, map256;  // box rows 128 / 256, 128-byte K boxes
+};
+
 struct nebw_dev {
   int device = 0;
   int sm_count = 0;
@@ -199,6 +226,7 @@ struct nebw_dev {
   cudaStream_t stream = nullptr;
   int *d_err = nullptr;
   std::map<uint64_t, Weight> weights;
+  std::map<uint64_t, WeightI8> weights_i8;  // int8 GEMM operands (nebw_stage_weight_i8)
   uint64_t next_handle = 1;
   // CTA pairs the GPU can hold at once for the 2-CTA GEMM (0: use the
   // single-CTA kernel); NEBW_GEMM_CTAS=1 in the environment forces 0.
@@ -523,6 +551,18 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
   NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
   if (int rc = set_all_gemm_attrs()) return rc;
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<128, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::GemmShape<128>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<128, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::GemmShape<128>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<256, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::GemmShape<256>::kSmemBytes));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<256, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 nebw::GemmShape<256>::kSmemBytes));
   NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  nebw::AttnTcShape<64>::kSmemBytes));
   NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -543,6 +583,7 @@ extern "C" int nebw_close(nebw_dev *d) {
   cudaSetDevice(d->device);
   cudaStreamSynchronize(d->stream);
   for (auto &kv : d->weights) cudaFree(kv.second.ptr);
+  for (auto &kv : d->weights_i8) cudaFree(kv.second.ptr);
   cudaFree(d->d_err);
   cudaStreamDestroy(d->stream);
   delete d;
@@ -730,11 +771,17 @@ extern "C" int nebw_stage_weight(nebw_dev *d, const void *host_kn, int dtype, in
 extern "C" int nebw_release_weight(nebw_dev *d, uint64_t handle) {
   if (int rc = use_dev(d)) return rc;
   auto it = d->weights.find(handle);
-  NEBW_REQUIRE(it != d->weights.end(), "unknown weight handle %llu",
-               static_cast<unsigned long long>(handle));
+  auto it8 = d->weights_i8.find(handle);
+  NEBW_REQUIRE(it != d->weights.end() || it8 != d->weights_i8.end(),
+               "unknown weight handle %llu", static_cast<unsigned long long>(handle));
   NEBW_CUDA(cudaStreamSynchronize(d->stream));
-  cudaFree(it->second.ptr);
-  d->weights.erase(it);
+  if (it != d->weights.end()) {
+    cudaFree(it->second.ptr);
+    d->weights.erase(it);
+  } else {
+    cudaFree(it8->second.ptr);
+    d->weights_i8.erase(it8);
+  }
   return NEBW_OK;
 }
 
@@ -849,6 +896,99 @@ extern "C" int nebw_narrow_bf16(nebw_dev *d, const float *x, int64_t n, void *y,
   const int64_t blocks = (n + threads * per - 1) / (threads * per);
   nebw::narrow_bf16_kernel<<<static_cast<unsigned>(blocks), threads, 0, pick_stream(d, stream)>>>(
       x, n, static_cast<__nv_bfloat16 *>(y));
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+// ---- the int8 datapath (the reference's --dtype i8 array path) -------------
+
+extern "C" int nebw_stage_weight_i8(nebw_dev *d, const int8_t *host_kn, int64_t K, int64_t N,
+                                    uint64_t *handle) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(host_kn && handle, "null argument");
+  NEBW_REQUIRE(K > 0 && N > 0 && K % 16 == 0 && N % 8 == 0,
+               "int8 weight [%lld, %lld] refused: K %% 16 == 0 and N %% 8 == 0 required",
+               static_cast<long long>(K), static_cast<long long>(N));
+  std::vector<int8_t> nk(static_cast<size_t>(K * N));
+  for (int64_t k = 0; k < K; ++k)
+    for (int64_t n = 0; n < N; ++n) nk[static_cast<size_t>(n * K + k)] = host_kn[k * N + n];
+  WeightI8 w;
+  w.K = K;
+  w.N = N;
+  NEBW_CUDA(cudaMalloc(&w.ptr, nk.size()));
+  NEBW_CUDA(cudaMemcpy(w.ptr, nk.data(), nk.size(), cudaMemcpyHostToDevice));
+  int rc = make_tmap_i8(&w.map128, w.ptr, N, K, 128);
+  if (!rc) rc = make_tmap_i8(&w.map256, w.ptr, N, K, 256);
+  if (rc) {
+    cudaFree(w.ptr);
+    return rc;
+  }
+  const uint64_t h = d->next_handle++;
+  d->weights_i8[h] = w;
+  *handle = h;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_gemm_i8(nebw_dev *d, uint64_t weight, const int8_t *A, const float *sa,
+                            int64_t M, int64_t K, int64_t N, const float *ws, const float *bias,
+                            int act, float *C, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  auto it = d->weights_i8.find(weight);
+  NEBW_REQUIRE(it != d->weights_i8.end(), "unknown int8 weight handle %llu",
+               static_cast<unsigned long long>(weight));
+  const WeightI8 &w = it->second;
+  NEBW_REQUIRE(K == w.K && N == w.N, "int8 GEMM [%lld x %lld] . [%lld x %lld] mismatch",
+               static_cast<long long>(M), static_cast<long long>(K),
+               static_cast<long long>(w.K), static_cast<long long>(w.N));
+  NEBW_REQUIRE(A && sa && ws && C, "null int8 GEMM operand");
+  NEBW_REQUIRE(M >= 0 && M < (1ll << 31), "M %lld refused", static_cast<long long>(M));
+  NEBW_REQUIRE(act == NEBW_ACT_NONE || act == NEBW_ACT_GELU8, "int8 GEMM act %d refused", act);
+  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(ws) % 16 == 0 &&
+                   (!bias || reinterpret_cast<uintptr_t>(bias) % 16 == 0),
+               "int8 GEMM C, ws and bias must be 16-byte aligned");
+  if (M == 0) return NEBW_OK;
+  CUtensorMap mA;
+  if (int rc = make_tmap_i8(&mA, A, M, K, nebw::kGemmBM)) return rc;
+  nebw::GemmI8Args a{};
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.sa = sa;
+  a.ws = ws;
+  a.bias = bias;
+  a.out = C;
+  a.err = d->d_err;
+  const bool wide = N % 256 == 0;
+  const int BN = wide ? 256 : 128;
+  const int64_t tiles = ((M + nebw::kGemmBM - 1) / nebw::kGemmBM) * ((N + BN - 1) / BN);
+  const dim3 g(static_cast<unsigned>(std::min<int64_t>(tiles, d->sm_count))), b(nebw::kGemmThreads);
+  cudaStream_t st = pick_stream(d, stream);
+  const bool gelu = act == NEBW_ACT_GELU8;
+  if (wide) {
+    const size_t smem = nebw::GemmShape<256>::kSmemBytes;
+    if (gelu) nebw::gemm_i8_kernel<256, true><<<g, b, smem, st>>>(mA, w.map256, a);
+    else nebw::gemm_i8_kernel<256, false><<<g, b, smem, st>>>(mA, w.map256, a);
+  } else {
+    const size_t smem = nebw::GemmShape<128>::kSmemBytes;
+    if (gelu) nebw::gemm_i8_kernel<128, true><<<g, b, smem, st>>>(mA, w.map128, a);
+    else nebw::gemm_i8_kernel<128, false><<<g, b, smem, st>>>(mA, w.map128, a);
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+extern "C" int nebw_quantise_rows(nebw_dev *d, const float *x, int64_t rows, int64_t K,
+                                  const float *ias, int8_t *q, float *scale, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(x && ias && q && scale, "null quantise operand");
+  NEBW_REQUIRE(rows >= 0 && rows < (1ll << 31) && K > 0 && K < (1ll << 31),
+               "quantise [%lld, %lld] refused", static_cast<long long>(rows),
+               static_cast<long long>(K));
+  if (rows == 0) return NEBW_OK;
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  nebw::quantise_rows_kernel<<<grid, 256, 0, pick_stream(d, stream)>>>(
+      x, static_cast<int>(rows), static_cast<int>(K), ias, q, scale);
   NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }

@@ -117,6 +117,9 @@ def lib() -> C.CDLL:
         "nebw_vit_profile": ([vp, C.c_int], C.c_int),
         "nebw_vit_profile_collect": ([vp, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
         "nebw_check_bounded_wait": ([vp, i64, C.POINTER(i32)], C.c_int),
+        "nebw_quantise_rows": ([vp, vp, i64, i64, vp, vp, vp, vp], C.c_int),
+        "nebw_stage_weight_i8": ([vp, vp, i64, i64, C.POINTER(C.c_uint64)], C.c_int),
+        "nebw_gemm_i8": ([vp, C.c_uint64, vp, vp, i64, i64, i64, vp, vp, C.c_int, vp, vp], C.c_int),
         "nebw_pack_checkpoint": ([C.c_char_p, C.c_char_p, C.c_char_p, i32, i32,
                                   C.POINTER(C.c_uint64)], C.c_int),
         "nebw_comm_unique_id": ([vp], C.c_int),
@@ -235,6 +238,22 @@ class Device:
         hnd = C.c_uint64()
         _check(lib().nebw_stage_weight(self.h, w.ctypes.data, dt, K, N, C.byref(hnd)))
         return hnd.value
+
+    def stage_weight_i8(self, w_kn: np.ndarray) -> int:
+        """An int8 [K, N] GEMM operand (nebw_stage_weight_i8)."""
+        w = np.ascontiguousarray(w_kn, np.int8)
+        K, N = w.shape
+        hnd = C.c_uint64()
+        _check(lib().nebw_stage_weight_i8(self.h, w.ctypes.data, K, N, C.byref(hnd)))
+        return hnd.value
+
+    def gemm_i8(self, weight, A, sa, M, K, N, ws, C_out, bias=None, act=ACT_NONE, stream=None):
+        _check(lib().nebw_gemm_i8(self.h, weight, _addr(A), _addr(sa), M, K, N, _addr(ws),
+                                  _addr(bias), act, _addr(C_out), self._s(stream)))
+
+    def quantise_rows(self, x, rows, K, ias, q, scale, stream=None):
+        _check(lib().nebw_quantise_rows(self.h, _addr(x), rows, K, _addr(ias), _addr(q),
+                                        _addr(scale), self._s(stream)))
 
     def release_weight(self, handle: int):
         _check(lib().nebw_release_weight(self.h, handle))
