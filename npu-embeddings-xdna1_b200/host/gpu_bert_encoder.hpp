@@ -39,20 +39,41 @@ class GpuBertEncoder {
  public:
   // Open GPU `device` and stage every tensor of the `.npue` container at
   // `npue_path` (the reference's npue::File + set_model_shape + stage_all).
-  GpuBertEncoder(const std::string &npue_path, int device = 0) {
-    check(nebw_open(device, &dev_));
-    const int rc = nebw_model_load_npue(dev_, npue_path.c_str(), &model_);
-    if (rc != NEBW_OK) {
-      const std::string msg = nebw_last_error();
-      nebw_close(dev_);
-      throw std::runtime_error("nebw: " + msg);
+  GpuBertEncoder(const std::string &npue_path, int device = 0)
+      : GpuBertEncoder(npue_path, std::vector<int>{device}) {}
+
+  // The same over several GPUs of this process: one weight replica per GPU,
+  // each batch split by the library's length-balanced plan and gathered back
+  // in request order over NCCL (nebw_comm_init_all + nebw_encode_multi), one
+  // host thread per GPU -- the reference's --pipeline lanes
+  // (embed_service.cpp:66-108) over GPUs.  `timeout_s` bounds every
+  // collective wait.
+  GpuBertEncoder(const std::string &npue_path, const std::vector<int> &devices,
+                 double timeout_s = 60.0) {
+    if (devices.empty()) throw std::runtime_error("nebw: no GPU given");
+    try {
+      for (int d : devices) {
+        nebw_dev *dev = nullptr;
+        check(nebw_open(d, &dev));
+        devs_.push_back(dev);
+        nebw_model *m = nullptr;
+        check(nebw_model_load_npue(dev, npue_path.c_str(), &m));
+        models_.push_back(m);
+      }
+      if (devs_.size() > 1) {
+        comms_.assign(devs_.size(), nullptr);
+        check(nebw_comm_init_all(static_cast<int32_t>(devs_.size()), devs_.data(), timeout_s,
+                                 comms_.data()));
+      }
+      check(nebw_model_get_config(models_[0], &cfg_));
+    } catch (...) {
+      release();
+      throw;
     }
-    check(nebw_model_get_config(model_, &cfg_));
+    dev_ = devs_[0];
+    model_ = models_[0];
   }
-  ~GpuBertEncoder() {
-    nebw_model_destroy(model_);
-    nebw_close(dev_);
-  }
+  ~GpuBertEncoder() { release(); }
   GpuBertEncoder(const GpuBertEncoder &) = delete;
   GpuBertEncoder &operator=(const GpuBertEncoder &) = delete;
 
@@ -90,8 +111,13 @@ class GpuBertEncoder {
     }
     if (keep.empty()) return out;
     std::vector<float> got(keep.size() * cfg_.hidden);
-    check(nebw_encode(model_, keep_ids.data(), lens.data(), static_cast<int32_t>(keep.size()),
-                      static_cast<int32_t>(seq), got.data()));
+    if (comms_.empty())
+      check(nebw_encode(model_, keep_ids.data(), lens.data(), static_cast<int32_t>(keep.size()),
+                        static_cast<int32_t>(seq), got.data()));
+    else
+      check(nebw_encode_multi(static_cast<int32_t>(models_.size()), models_.data(), comms_.data(),
+                              keep_ids.data(), lens.data(), static_cast<int32_t>(keep.size()),
+                              static_cast<int32_t>(seq), got.data()));
     for (size_t i = 0; i < keep.size(); ++i)
       std::copy(got.begin() + i * cfg_.hidden, got.begin() + (i + 1) * cfg_.hidden,
                 out.begin() + keep[i] * cfg_.hidden);
@@ -100,8 +126,21 @@ class GpuBertEncoder {
 
   nebw_model *model() { return model_; }
   nebw_dev *device() { return dev_; }
+  size_t gpus() const { return devs_.size(); }
 
  private:
+  void release() {
+    for (nebw_comm *c : comms_) nebw_comm_destroy(c);
+    for (nebw_model *m : models_) nebw_model_destroy(m);
+    for (nebw_dev *d : devs_) nebw_close(d);
+    comms_.clear();
+    models_.clear();
+    devs_.clear();
+  }
+
+  std::vector<nebw_dev *> devs_;
+  std::vector<nebw_model *> models_;
+  std::vector<nebw_comm *> comms_;  // empty on one GPU
   nebw_dev *dev_ = nullptr;
   nebw_model *model_ = nullptr;
   nebw_config cfg_{};

@@ -2,11 +2,11 @@
 // runtime/include/runtime/run_execute.hpp:150-258, embed_service.cpp:29-64)
 // with the encoder on a B200, through the C++ host side of the library.
 //
-//   nebw_embed <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [device]
+//   nebw_embed <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [devices]
 //       token ids and the 1/0 attention mask as raw little-endian int32
 //       [n, seq] (as a tokenizer emits them, padded to seq) -> raw fp32
 //       [n, hidden] pooled embeddings
-//   nebw_embed --text <model.npue> <texts.txt> <seq> <out.f32> [device] [--vocab v.txt]
+//   nebw_embed --text <model.npue> <texts.txt> <seq> <out.f32> [devices] [--vocab v.txt]
 //       one text per line, WordPiece-tokenized on the host (wordpiece.hpp)
 //       with the vocabulary the container carries (tokenizer.vocab) or
 //       --vocab, then encoded on the GPU
@@ -15,6 +15,10 @@
 //   nebw_embed --prepare-model <checkpoint_dir> <out.npue> [tma_bf16|host] [max_seq]
 //       the packer (no GPU): a Hugging Face BERT checkpoint -> a container
 //       (the runtime's --prepare-model, runtime/src/cli/cli.cpp:60)
+//
+// `devices` is one GPU index or a comma-separated list ("0,1,2,3"): with
+// several, the batch is sharded over them and gathered back in request
+// order (one weight replica per GPU).
 //
 // Exit status 0 on success, 1 with the cause on stderr otherwise.
 #include <cstdio>
@@ -87,10 +91,26 @@ void tokenize_all(const nebw::WordPiece &wp, const std::vector<std::string> &tex
   }
 }
 
+// "0" or "0,1,3" -> GPU indices
+std::vector<int> parse_devices(const std::string &s) {
+  std::vector<int> v;
+  size_t at = 0;
+  while (at <= s.size()) {
+    const size_t c = s.find(',', at);
+    const std::string part = s.substr(at, c == std::string::npos ? std::string::npos : c - at);
+    if (part.empty() || part.find_first_not_of("0123456789") != std::string::npos)
+      throw std::runtime_error("bad device list '" + s + "'");
+    v.push_back(std::atoi(part.c_str()));
+    if (c == std::string::npos) break;
+    at = c + 1;
+  }
+  return v;
+}
+
 int usage(const char *argv0) {
   std::fprintf(stderr,
-               "usage: %s <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [device]\n"
-               "       %s --text <model.npue> <texts.txt> <seq> <out.f32> [device] [--vocab v.txt]\n"
+               "usage: %s <model.npue> <ids.i32> <mask.i32> <seq> <out.f32> [devices]\n"
+               "       %s --text <model.npue> <texts.txt> <seq> <out.f32> [devices] [--vocab v.txt]\n"
                "       %s --tokenize <model.npue|vocab.txt> <texts.txt> <seq> <ids.i32> <mask.i32>\n"
                "       %s --prepare-model <checkpoint_dir> <out.npue> [tma_bf16|host] [max_seq]\n",
                argv0, argv0, argv0, argv0);
@@ -122,17 +142,17 @@ int main(int argc, char **argv) {
     if (argc >= 2 && std::strcmp(argv[1], "--text") == 0) {
       if (argc < 6) return usage(argv[0]);
       std::string vocab = argv[2];
-      int device = 0;
+      std::vector<int> devices{0};
       for (int i = 6; i < argc; ++i) {
         if (std::strcmp(argv[i], "--vocab") == 0 && i + 1 < argc) vocab = argv[++i];
-        else device = std::atoi(argv[i]);
+        else devices = parse_devices(argv[i]);
       }
       const int seq = std::atoi(argv[4]);
       const nebw::WordPiece wp = load_vocab(vocab);
       const std::vector<std::string> texts = read_lines(argv[3]);
       std::vector<int32_t> ids, mask;
       tokenize_all(wp, texts, seq, ids, mask);
-      nebw::GpuBertEncoder enc(argv[2], device);
+      nebw::GpuBertEncoder enc(argv[2], devices);
       const std::vector<float> out =
           enc.encode(ids, mask, static_cast<int64_t>(texts.size()), seq);
       write_raw(argv[5], out);
@@ -142,12 +162,12 @@ int main(int argc, char **argv) {
     }
     if (argc < 6) return usage(argv[0]);
     const int64_t seq = std::atoll(argv[4]);
-    const int device = argc > 6 ? std::atoi(argv[6]) : 0;
+    const std::vector<int> devices = argc > 6 ? parse_devices(argv[6]) : std::vector<int>{0};
     const std::vector<int32_t> ids = read_i32(argv[2]), mask = read_i32(argv[3]);
     if (seq <= 0 || ids.size() % seq || mask.size() != ids.size())
       throw std::runtime_error("ids/mask sizes do not match seq");
     const int64_t n = static_cast<int64_t>(ids.size()) / seq;
-    nebw::GpuBertEncoder enc(argv[1], device);
+    nebw::GpuBertEncoder enc(argv[1], devices);
     const std::vector<float> out = enc.encode(ids, mask, n, seq);
     write_raw(argv[5], out);
     std::printf("%lld embeddings of %lld dims -> %s\n", static_cast<long long>(n),

@@ -159,3 +159,25 @@ def test_npue_encoder_adapter_through_reference_interface(tmp_path, port_oracle)
     np.testing.assert_array_equal(np.fromfile(tmp_path / "ids2.i32", np.int32).reshape(n, 128), ids)
     np.testing.assert_array_equal(np.fromfile(tmp_path / "mask2.i32", np.int32).reshape(n, 128),
                                   mask)
+
+
+def test_cpp_tool_over_several_gpus(tmp_path):
+    """`nebw_embed ... 0,1,...`: GpuBertEncoder over every visible GPU
+    (nebw_comm_init_all + nebw_encode_multi) gives the single-GPU bytes."""
+    import torch
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    from nebw import synth
+    w = synth.make_weights(synth.MINILM, seed=16, cls_pool=False, layers=2)
+    lens = np.random.default_rng(17).integers(1, 129, 37).astype(np.int32)
+    ids, mask = synth.make_tokens(37, 128, lens, seed=18)
+    r = _run(tmp_path, w, ids, mask, 128)
+    assert r.returncode == 0, r.stderr
+    one = np.fromfile(tmp_path / "out.f32", np.float32)
+    devs = ",".join(str(i) for i in range(min(n, 8)))
+    r = subprocess.run([str(TOOL), str(tmp_path / "m.npue"), str(tmp_path / "ids.i32"),
+                        str(tmp_path / "mask.i32"), "128", str(tmp_path / "multi.f32"), devs],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "multi.f32", np.float32), one)
