@@ -78,8 +78,8 @@ def build_oracle(verbose: bool = False):
                        check=True)
         # the serving drop-in against the reference's headers and tokenizer
         # (needs libnebw.so, built first by build_lib)
-        subprocess.run([make, "-s", "-C", str(REPO / "oracle"), "encoder_check", f"REF={ref}"],
-                       check=True)
+        subprocess.run([make, "-s", "-C", str(REPO / "oracle"), "encoder_check", "serve_check",
+                        f"REF={ref}"], check=True)
 
 
 def main(argv):

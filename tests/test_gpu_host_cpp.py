@@ -181,3 +181,89 @@ def test_cpp_tool_over_several_gpus(tmp_path):
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr
     np.testing.assert_array_equal(np.fromfile(tmp_path / "multi.f32", np.float32), one)
+
+
+SERVE = REPO / "oracle" / "_ref" / "npue_serve_gpu"
+
+
+@pytest.mark.skipif(not SERVE.exists(),
+                    reason="built only where the reference tree is (oracle/Makefile serve_check)")
+def test_reference_http_serve_with_gpu_backend(tmp_path, port_oracle):
+    """`serve` as the runtime runs it: the reference's own HTTP server and
+    /v1/embeddings handler (app::serve_http) with the reference's tokenizer,
+    the GPU encoder behind its EmbedBackend.  base64 embeddings equal the
+    adapter's bytes; float ones the oracle's within the gate; an over-long
+    input is the runtime's 400; SIGTERM stops the server."""
+    import base64
+    import json
+    import signal
+    import socket
+    import time
+    import urllib.error
+    import urllib.request
+
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    w = synth.make_weights(synth.BGE_SMALL, seed=81, cls_pool=True, layers=2)
+    model = tmp_path / "m.npue"
+    write_bert_container(model, w, max_seq_len=128, vocab=synthetic_vocab(w.vocab))
+    texts = synthetic_texts(9, 82, 60)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    proc = subprocess.Popen([str(SERVE), str(model), str(port), "128"], stdout=subprocess.PIPE,
+                            stderr=subprocess.PIPE, text=True)
+    try:
+        def post(body, path="/v1/embeddings"):
+            req = urllib.request.Request(f"http://127.0.0.1:{port}{path}",
+                                         data=json.dumps(body).encode(),
+                                         headers={"Content-Type": "application/json"})
+            try:
+                with urllib.request.urlopen(req, timeout=60) as r:
+                    return r.status, json.loads(r.read())
+            except urllib.error.HTTPError as e:
+                return e.code, json.loads(e.read())
+
+        deadline = time.time() + 120
+        while True:
+            try:
+                with urllib.request.urlopen(f"http://127.0.0.1:{port}/health", timeout=5) as r:
+                    assert json.loads(r.read())["status"] == "ok"
+                break
+            except (urllib.error.URLError, ConnectionError):
+                assert proc.poll() is None, proc.communicate()[1]
+                assert time.time() < deadline, "server did not come up"
+                time.sleep(0.5)
+        st, b64 = post({"input": texts, "encoding_format": "base64"})
+        assert st == 200, b64
+        got = np.stack([np.frombuffer(base64.b64decode(d["embedding"]), np.float32)
+                        for d in b64["data"]])
+        st, fl = post({"input": texts})
+        assert st == 200
+        np.testing.assert_allclose(np.array([d["embedding"] for d in fl["data"]], np.float32), got,
+                                   rtol=1e-6, atol=1e-7)  # %.7g text of the same floats
+        # the adapter on the same texts gives the same bytes
+        (tmp_path / "t.txt").write_text("\n".join(texts) + "\n")
+        r = subprocess.run([str(CHECK), str(model), str(tmp_path / "t.txt"), "128",
+                            str(tmp_path / "o.f32"), str(tmp_path / "i.i32"), str(tmp_path / "m.i32")],
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr
+        np.testing.assert_array_equal(got, np.fromfile(tmp_path / "o.f32", np.float32).reshape(got.shape))
+        ids = np.fromfile(tmp_path / "i.i32", np.int32).reshape(len(texts), 128)
+        mask = np.fromfile(tmp_path / "m.i32", np.int32).reshape(len(texts), 128)
+        assert b64["usage"]["prompt_tokens"] == int(mask.sum())
+        cos, err = parity(got, port_oracle.encode(w, ids, mask))
+        assert cos >= 0.9999 and err <= 2e-3, (cos, err)
+        st, e = post({"input": ["w1 " * 200]})
+        assert st == 400 and "128" in e["error"]["message"], e
+        st, e = post({"input": texts}, path="/v1/nothing")
+        assert st == 404
+    finally:
+        proc.send_signal(signal.SIGTERM)
+        try:
+            proc.wait(timeout=60)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+            proc.wait(timeout=30)
+    assert proc.returncode == 0, proc.stderr.read() if proc.stderr else ""
