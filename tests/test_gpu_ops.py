@@ -244,6 +244,54 @@ def test_attention_matches_float64(device, D, heads, kind):
             assert err <= 1.5e-2 * max(1.0, np.abs(want).max()), (b, h, err)
 
 
+@pytest.mark.parametrize("D,heads", [(64, 4), (32, 4)])
+def test_attention_running_max_rescale(device, D, heads):
+    """The tcgen05 kernel takes p against a running row max that it raises
+    (rescaling O in tensor memory and the row sums) only when a block's max
+    grows past it by more than 2^8.  Scores that climb along the keys
+    (s = 0.1 j: +6.4 per 64 keys, above the threshold's 5.55) raise it in
+    nearly every block and in each half of a block; one sequence instead
+    holds a single key 60 above the rest late in the row, so every earlier
+    contribution is scaled by about 2^-86.  Against float64 on the same
+    bf16 inputs."""
+    rng = np.random.default_rng(17 + D)
+    lens = np.array([130, 512, 70, 300, 200, 1], np.int32)
+    off, T = _packed(lens)
+    H = D * heads
+    u = rng.standard_normal(D)
+    u /= np.linalg.norm(u)
+    qkv = np.zeros((T, 3 * H), np.float32)
+    for b, L in enumerate(lens):
+        r = slice(off[b], off[b] + L)
+        j = np.arange(L, dtype=np.float64)
+        score = np.where(j == 250, 60.0, 0.01 * j) if b == 3 else 0.1 * j
+        for h in range(heads):
+            qkv[r, h * D:(h + 1) * D] = u + 0.01 * rng.standard_normal((L, D))
+            qkv[r, H + h * D:H + (h + 1) * D] = (score[:, None] * u +
+                                                 0.01 * rng.standard_normal((L, D)))
+            qkv[r, 2 * H + h * D:2 * H + (h + 1) * D] = 0.5 * rng.standard_normal((L, D))
+    qkv = bf16_bits(qkv)
+    ctx = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
+    device.attention(dev_tensor(qkv), T, dev_tensor(off), dev_tensor(lens), len(lens), 512,
+                     heads, D, ctx)
+    device.sync()
+    got = bits_to_f32(host_bits(ctx)).astype(np.float64)
+    q = bits_to_f32(qkv).astype(np.float64)
+    assert np.isfinite(got).all()
+    for b, L in enumerate(lens):
+        r = slice(off[b], off[b] + L)
+        for h in range(heads):
+            Q = q[r, h * D:(h + 1) * D]
+            Kt = q[r, H + h * D:H + (h + 1) * D]
+            V = q[r, 2 * H + h * D:2 * H + (h + 1) * D]
+            s = Q @ Kt.T
+            p = np.exp(s - s.max(1, keepdims=True))
+            p /= p.sum(1, keepdims=True)
+            want = p @ V
+            err = np.abs(got[r, h * D:(h + 1) * D] - want).max()
+            assert err <= 1.5e-2 * max(1.0, np.abs(want).max()), (b, h, err)
+
+
 @pytest.mark.parametrize("cls", [0, 1])
 def test_pool_l2(device, port_oracle, cls):
     rng = np.random.default_rng(11 + cls)
