@@ -590,6 +590,109 @@ int nebw_oracle_dequant_gelu_quant(const int32_t *C, int64_t rows, int64_t N, co
   return 0;
 }
 
+/* ---- int8 encoder pass: BertEncoder::run's array path -------------------
+ * (bert_encoder.cpp:1419-1598 with gemm_on_array() and the fused epilogues,
+ * fuse_ffn_epilogue's default; gemm()'s array branch :763-923;
+ * add_norm_quant :1196-1302).  Per layer:
+ *   QKV  A = quantise(x, ias_qkv) on layer 0, else the rows the previous
+ *        layer's add_norm_quant wrote; C = A.W; qkv = dequantise(C) (fp32)
+ *   attention on the host (qk_impl / softmax_cpu / av_impl) -> ctx
+ *   AO   A = quantise(ctx, ias_ao); proj = dequantise(A.W)
+ *   x = LN1(proj + residual); residual = x; A = quantise(x, ias_up)
+ *   UP   A' = dequant_act_quant(A.W): gelu8, quantised with ias_dn
+ *   DOWN down = dequantise(A'.W)
+ *   x = LN2(down + residual); residual = x; A = quantise(x, ias_qkv of the
+ *        next layer) unless this is the last
+ * add_norm_quant's LayerNorm is layer_norm_cpu's arithmetic (ln_row), its
+ * quantisation quantise_a_int8's (quant_row). */
+int nebw_oracle_encode_i8(const nebw_oracle_model *m, const nebw_oracle_i8_gemm *gq,
+                          const nebw_oracle_i8_gemm *ga, const nebw_oracle_i8_gemm *gu,
+                          const nebw_oracle_i8_gemm *gd, const int32_t *ids,
+                          const int32_t *mask, int32_t batch, int32_t seq, int32_t threads,
+                          float *out, float *hidden_out) {
+  const int64_t H = m->hidden, F = m->ffn, S = seq, B = batch;
+  const int64_t rows = B * S;
+  if (seq <= 0 || seq % 8) return fail("seq must be positive and a multiple of 8");
+  if (H % 8 || F % 8 || m->head_dim % 8 || m->head_dim * m->heads != H)
+    return fail("hidden/ffn/head_dim geometry refused (multiples of 8, heads*head_dim == hidden)");
+  if (m->gated || m->rope_inv_freq) return fail("the int8 pass restates plain BERT only");
+  const int64_t KM = F > H ? F : H, NM = 3 * H > F ? 3 * H : F;
+  float *x = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *res = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *qkv = (float *)malloc((size_t)rows * 3 * H * sizeof(float));
+  float *ctx = (float *)malloc((size_t)rows * H * sizeof(float));
+  float *y = (float *)malloc((size_t)rows * H * sizeof(float));
+  int8_t *aq = (int8_t *)malloc((size_t)rows * KM);
+  float *sa = (float *)malloc((size_t)rows * sizeof(float));
+  int32_t *c = (int32_t *)malloc((size_t)rows * NM * sizeof(int32_t));
+  float *amask = (float *)malloc((size_t)rows * sizeof(float));
+  float *cam = (float *)malloc((size_t)rows * sizeof(float));
+  int rc = 0;
+  if (!x || !res || !qkv || !ctx || !y || !aq || !sa || !c || !amask || !cam) {
+    rc = fail("out of host memory");
+    goto done;
+  }
+
+  /* EmbedService::chunk (embed_service.cpp:29-64), then LN of the embeddings */
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t s2 = 0; s2 < S; ++s2) {
+      const int32_t id = ids[b * S + s2];
+      const float mk = (float)mask[b * S + s2];
+      cam[b * S + s2] = mk;
+      amask[b * S + s2] = mk > 0 ? 0.f : -1.0e30f;
+      float *dst = x + (b * S + s2) * H;
+      const float *wv = m->word + (int64_t)id * H;
+      const float *pv = m->pos + s2 * H;
+      for (int64_t j = 0; j < H; ++j) dst[j] = wv[j] + pv[j] + m->typ[j];
+    }
+  ln_ctx lc = {x, H, m->emb_ln_g, m->emb_ln_b, m->ln_eps};
+  parallel_for(rows, threads, ln_rows, &lc);
+
+  for (int32_t L = 0; L < m->layers; ++L) {
+    if (L == 0) {
+      memcpy(res, x, (size_t)rows * H * sizeof(float));
+      nebw_oracle_quantise_rows(x, rows, H, gq[0].ias, aq, sa);
+    }
+    nebw_oracle_gemm_i8(aq, rows, gq[L].w, H, 3 * H, c, threads);
+    if ((rc = nebw_oracle_dequantise(c, rows, 3 * H, sa, gq[L].ws, m->b_qkv[L], qkv))) goto done;
+    attn_ctx ac = {qkv, amask, ctx, S, H, m->heads, m->head_dim};
+    parallel_for(B * m->heads, threads, attn_pairs, &ac);
+
+    nebw_oracle_quantise_rows(ctx, rows, H, ga[L].ias, aq, sa);
+    nebw_oracle_gemm_i8(aq, rows, ga[L].w, H, H, c, threads);
+    if ((rc = nebw_oracle_dequantise(c, rows, H, sa, ga[L].ws, m->b_ao[L], y))) goto done;
+    /* add_norm_quant(x, proj, ln1, 1 / asmooth of FFN-up) */
+    for (int64_t i = 0; i < rows * H; ++i) x[i] = y[i] + res[i];
+    lc.g = m->ln1_g[L];
+    lc.b = m->ln1_b[L];
+    lc.eps = 1e-12f;
+    parallel_for(rows, threads, ln_rows, &lc);
+    memcpy(res, x, (size_t)rows * H * sizeof(float));
+    nebw_oracle_quantise_rows(x, rows, H, gu[L].ias, aq, sa);
+
+    nebw_oracle_gemm_i8(aq, rows, gu[L].w, H, F, c, threads);
+    if ((rc = nebw_oracle_dequant_gelu_quant(c, rows, F, sa, gu[L].ws, m->b_up[L], gd[L].ias, aq,
+                                             sa)))
+      goto done;
+    nebw_oracle_gemm_i8(aq, rows, gd[L].w, F, H, c, threads);
+    if ((rc = nebw_oracle_dequantise(c, rows, H, sa, gd[L].ws, m->b_dn[L], y))) goto done;
+    /* add_norm_quant(x, down, ln2, 1 / asmooth of the next QKV, or none) */
+    for (int64_t i = 0; i < rows * H; ++i) x[i] = y[i] + res[i];
+    lc.g = m->ln2_g[L];
+    lc.b = m->ln2_b[L];
+    parallel_for(rows, threads, ln_rows, &lc);
+    memcpy(res, x, (size_t)rows * H * sizeof(float));
+    if (L + 1 < m->layers) nebw_oracle_quantise_rows(x, rows, H, gq[L + 1].ias, aq, sa);
+  }
+
+  if (hidden_out) memcpy(hidden_out, x, (size_t)rows * H * sizeof(float));
+  rc = nebw_oracle_pool_rows(x, cam, B, S, H, m->cls_pool, m->l2_normalize, out);
+done:
+  free(x); free(res); free(qkv); free(ctx); free(y); free(aq); free(sa); free(c); free(amask);
+  free(cam);
+  return rc;
+}
+
 void nebw_oracle_vit_im2col(const float *chw, int32_t channels, int32_t image,
                             int32_t patch, float *out) {
   const int64_t n = image / patch, pd = (int64_t)channels * patch * patch;

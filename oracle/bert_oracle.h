@@ -89,6 +89,26 @@ int nebw_oracle_dequant_gelu_quant(const int32_t *C, int64_t rows, int64_t N, co
                                    int8_t *q, float *sa_next);
 
 /* ViT (arch vit_patch16_prenorm_gelu): pre-LN encoder over image patches. */
+/* One GEMM of an int8 container on the array path: the int8 operand [K, N]
+ * (the panel untiled), its column scales (.wscale) and the reciprocal of its
+ * SmoothQuant divisor (1 / .asmooth, as the encoder computes it). */
+typedef struct nebw_oracle_i8_gemm {
+  const int8_t *w;    /* [K, N] */
+  const float *ws;    /* [N]    */
+  const float *ias;   /* [K]    */
+} nebw_oracle_i8_gemm;
+
+/* BertEncoder::run's array path for an int8 container (every GEMM on the
+ * array, the fused host epilogues).  `m` supplies the geometry, embeddings,
+ * biases and LayerNorm parameters (its fp32 GEMM operands are not read);
+ * qkv / ao / up / dn hold `layers` operands each.  Plain BERT only (m->gated
+ * 0, no rotary). */
+int nebw_oracle_encode_i8(const nebw_oracle_model *m, const nebw_oracle_i8_gemm *qkv,
+                          const nebw_oracle_i8_gemm *ao, const nebw_oracle_i8_gemm *up,
+                          const nebw_oracle_i8_gemm *dn, const int32_t *ids,
+                          const int32_t *mask, int32_t batch, int32_t seq, int32_t threads,
+                          float *out, float *hidden_out);
+
 typedef struct nebw_oracle_vit {
   int32_t layers, hidden, heads, head_dim, ffn;
   int32_t image_size, patch_size, channels;  /* hidden == channels*patch^2 */

@@ -31,6 +31,7 @@ REF_LIB = HERE / "_ref" / "libnebw_ref.so"
 
 _f32p = C.POINTER(C.c_float)
 _i32p = C.POINTER(C.c_int32)
+_i8p = C.POINTER(C.c_int8)
 
 
 def _ptr(a: np.ndarray, t=_f32p):
@@ -69,6 +70,36 @@ class _Vit(C.Structure):
                                          "w_up", "b_up", "w_dn", "b_dn", "ln2_g", "ln2_b")]
 
 
+class _I8Gemm(C.Structure):
+    _fields_ = [("w", _i8p), ("ws", _f32p), ("ias", _f32p)]
+
+
+def i8_operands(path, layers: int) -> dict:
+    """An int8 container's GEMM operands as the array path consumes them:
+    {kind: [(int8 [K, N], wscale [N], 1 / asmooth [K]) per layer]}, the panel
+    untiled, the reciprocal taken in float32 as the encoder takes it
+    (bert_encoder.cpp:767-772)."""
+    import sys
+    sys.path.insert(0, str(HERE.parent / "npu-embeddings-xdna1_b200"))
+    from nebw.npue import ContainerReader, untile_block_panel  # noqa: E402
+    out = {}
+    with ContainerReader(path) as r:
+        for g in ("qkv", "attn_out", "ffn_up", "ffn_down"):
+            lst = []
+            for L in range(layers):
+                n = f"layer.{L}.{g}"
+                e = r.entries[n]
+                if e["dtype"] != "I8":
+                    raise ValueError(f"{n} is {e['dtype']}, not an int8 panel")
+                K, N = e["padded_shape"]
+                q = untile_block_panel(np.array(r.tensor(n)).reshape(-1), K, N, e["layout"])
+                ws = np.array(r.tensor(n + ".wscale"), np.float32)
+                ias = (np.float32(1.0) / np.array(r.tensor(n + ".asmooth"), np.float32))
+                lst.append((np.ascontiguousarray(q, np.int8), ws, ias.astype(np.float32)))
+            out[g] = lst
+    return out
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -76,7 +107,6 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-_i8p = C.POINTER(C.c_int8)
 
 
 class _Int8Steps:
@@ -150,6 +180,9 @@ class PortOracle(_Int8Steps):
         L.nebw_oracle_encode.argtypes = [C.POINTER(_Model), _i32p, _i32p, C.c_int32, C.c_int32,
                                          C.c_int32, _f32p, _f32p]
         L.nebw_oracle_encode.restype = C.c_int
+        L.nebw_oracle_encode_i8.argtypes = [C.POINTER(_Model)] + [C.POINTER(_I8Gemm)] * 4 + [
+            _i32p, _i32p, C.c_int32, C.c_int32, C.c_int32, _f32p, _f32p]
+        L.nebw_oracle_encode_i8.restype = C.c_int
         L.nebw_oracle_last_error.restype = C.c_char_p
         L.nebw_oracle_gemm_nt.argtypes = [_f32p, C.c_int64, _f32p, C.c_int64, C.c_int64, _f32p,
                                           _f32p, C.c_int32]
@@ -242,6 +275,35 @@ class PortOracle(_Int8Steps):
             raise RuntimeError(self.lib.nebw_oracle_last_error().decode())
         return (out, hid) if hidden else out
 
+    def encode_i8(self, w, path, ids, mask, threads: int | None = None, hidden: bool = False):
+        """The int8 array path (nebw_oracle_encode_i8) of the int8 container
+        at `path`, packed from `w`: its GEMM operands from the container,
+        embeddings, biases and LayerNorm parameters from `w` (the container
+        holds them as the same fp32 values)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        mask = np.ascontiguousarray(mask, np.int32)
+        B, S = ids.shape
+        m, keep = self._struct(w)
+        ops = i8_operands(path, w.layers)
+        keep.append(ops)
+
+        def arr(kind):
+            a = (_I8Gemm * w.layers)(*[_I8Gemm(_ptr(q, _i8p), _ptr(ws), _ptr(ias))
+                                       for q, ws, ias in ops[kind]])
+            keep.append(a)
+            return a
+
+        out = np.zeros((B, w.hidden), np.float32)
+        hid = np.zeros((B * S, w.hidden), np.float32) if hidden else None
+        rc = self.lib.nebw_oracle_encode_i8(C.byref(m), arr("qkv"), arr("attn_out"),
+                                            arr("ffn_up"), arr("ffn_down"), _ptr(ids, _i32p),
+                                            _ptr(mask, _i32p), B, S, threads or host_threads(),
+                                            _ptr(out), _ptr(hid) if hidden else None)
+        del keep
+        if rc:
+            raise RuntimeError(self.lib.nebw_oracle_last_error().decode())
+        return (out, hid) if hidden else out
+
     def gemm_nt(self, A, B, bias, threads=1):
         A = np.ascontiguousarray(A, np.float32)
         B = np.ascontiguousarray(B, np.float32)
@@ -315,6 +377,8 @@ class RefOracle(_Int8Steps):
         L.nebw_ref_encode.argtypes = [C.c_char_p, C.c_int32, _i32p, _i32p, C.c_int32, C.c_int32,
                                       _f32p, _f32p, C.c_char_p, C.c_int32]
         L.nebw_ref_encode.restype = C.c_int
+        L.nebw_ref_encode_array.argtypes = L.nebw_ref_encode.argtypes
+        L.nebw_ref_encode_array.restype = C.c_int
         L.nebw_ref_gemm_nt.argtypes = [_f32p, C.c_int64, _f32p, C.c_int64, C.c_int64, _f32p,
                                        _f32p, C.c_int32]
         L.nebw_ref_gelu8.argtypes = [_f32p, C.c_int64]
@@ -369,7 +433,12 @@ class RefOracle(_Int8Steps):
             return self.vit_encode_container(path, images, w.arch.hidden, w.arch.n_pos,
                                              threads, hidden)
 
-    def encode_container(self, path, seq, ids, mask, threads=None, hidden=False, hidden_size=None):
+    def encode_container(self, path, seq, ids, mask, threads=None, hidden=False, hidden_size=None,
+                         array=False):
+        """The reference's host path on a container; with `array`, an int8
+        container's array path instead (nebw_ref_encode_array: the GEMMs as
+        the exact int32 products of the array, the int8 host steps around
+        them)."""
         ids = np.ascontiguousarray(ids, np.int32)
         mask = np.ascontiguousarray(mask, np.int32)
         B, S = ids.shape
@@ -377,9 +446,9 @@ class RefOracle(_Int8Steps):
         out = np.zeros((B, hidden_size), np.float32)
         hid = np.zeros((B * S, hidden_size), np.float32) if hidden else None
         err = C.create_string_buffer(4096)
-        rc = self.lib.nebw_ref_encode(str(path).encode(), seq, _ptr(ids, _i32p), _ptr(mask, _i32p),
-                                      B, threads or host_threads(), _ptr(out),
-                                      _ptr(hid) if hidden else None, err, 4096)
+        fn = self.lib.nebw_ref_encode_array if array else self.lib.nebw_ref_encode
+        rc = fn(str(path).encode(), seq, _ptr(ids, _i32p), _ptr(mask, _i32p), B,
+                threads or host_threads(), _ptr(out), _ptr(hid) if hidden else None, err, 4096)
         if rc:
             raise RuntimeError(err.value.decode())
         return (out, hid) if hidden else out

@@ -22,24 +22,31 @@
 // (gemm_nt, gelu8, to_bf16, exp2_avx2, pool_rows) so the CPU restatement in
 // oracle/bert_oracle.c can be pinned op by op as well as end to end.
 
+#include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
 #include "common/app_state.hpp"
 #include "common/conv_host.hpp"
+#include "common/host_b.hpp"
 #include "common/host_kernels.hpp"
+#include "common/npu_ops_flag.hpp"
 #include "encoders/bert_encoder.hpp"
 #include "runtime/design.hpp"
 #include "runtime/device.hpp"
 #include "runtime/model.hpp"
 #include "runtime/pool.hpp"
+#include "ref_array.hpp"
 #include "tokenizers/wordpiece.hpp"
 
 void nebw_oracle_describe_design(const npue::File &f);  // oracle/ref_stub.cpp
+extern size_t nebw_oracle_a_elem_bytes;                 // oracle/ref_stub.cpp
 
 namespace {
 void set_err(char *err, int32_t errlen, const char *msg) {
@@ -47,6 +54,47 @@ void set_err(char *err, int32_t errlen, const char *msg) {
   std::strncpy(err, msg, static_cast<size_t>(errlen) - 1);
   err[errlen - 1] = '\0';
 }
+
+// The EmbedService::chunk gather into x, the encoder's add_mask and the
+// pooling mask, for `batch` sequences of `seq` ids (embed_service.cpp:29-64).
+void gather_rows(const npue::File &f, int64_t seq, const int32_t *ids, const int32_t *attn_mask,
+                 int64_t batch, std::vector<float> &x, std::vector<float> &cmask,
+                 std::vector<float> &cam) {
+  const int64_t H = app::g_hidden;
+  const float *w_word = f.raw("embeddings.word").as<float>();
+  const float *w_pos = f.raw("embeddings.position").as<float>();
+  const float *w_typ = f.raw("embeddings.token_type").as<float>();
+  x.assign(static_cast<size_t>(batch) * seq * H, 0.f);
+  cmask.assign(static_cast<size_t>(batch) * seq, -1.0e30f);
+  cam.assign(static_cast<size_t>(batch) * seq, 0.f);
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t s = 0; s < seq; ++s) {
+      const int32_t id = ids[b * seq + s];
+      const float m = static_cast<float>(attn_mask[b * seq + s]);
+      cam[b * seq + s] = m;
+      cmask[b * seq + s] = m > 0 ? 0.f : -1.0e30f;
+      float *dst = x.data() + (b * seq + s) * H;
+      const float *wv = w_word + static_cast<size_t>(id) * H;
+      const float *pv = w_pos + static_cast<size_t>(s) * H;
+      for (int64_t c = 0; c < H; ++c) dst[c] = wv[c] + pv[c] + w_typ[c];
+    }
+}
+
+// Switches the stand-in design's array emulation on for one encode and off
+// again however the encode ends.
+struct ArrayEmulation {
+  ArrayEmulation() {
+    nebw_array_registry.clear();
+    app::g_npu_ops = {"gemm"};
+  }
+  ~ArrayEmulation() {
+    nebw_array_on = false;
+    nebw_array_registry.clear();
+    nebw_array_a.clear();
+    nebw_array_c.clear();
+    app::g_npu_ops.clear();
+  }
+};
 
 }  // namespace
 
@@ -96,6 +144,86 @@ int nebw_ref_encode(const char *npue_path, int32_t seq, const int32_t *ids,
     }
     enc.add_mask = cmask;
     std::vector<float> h = enc.run(buf);
+    if (hidden_out) std::memcpy(hidden_out, h.data(), h.size() * sizeof(float));
+    app::pool_rows(h.data(), cam.data(), batch, out);
+    return 0;
+  } catch (const std::exception &e) {
+    set_err(err, errlen, e.what());
+    return 1;
+  }
+}
+
+// The reference's int8 ARRAY path on an int8 container (a_dtype "i8", int8
+// block panels with .wscale / .asmooth): BertEncoder::run as `--npu-ops gemm`
+// runs it (bert_encoder.cpp:741-923, 1419-1598) -- each of the four GEMMs a
+// dispatch on the array, everything else on the host, the fused epilogues on
+// (fuse_ffn_epilogue's default, run_setup.hpp:694):
+//   QKV   quantise_a_int8(x) (layer 0) or the previous add_norm_quant's rows,
+//         int32 product, dequantise_c -> fp32 qkv; host attention -> fp32 ctx
+//   AO    quantise_a_int8(ctx), int32 product, dequantise_c -> proj;
+//         add_norm_quant(x, proj) quantises FFN-up's A
+//   UP    int32 product, dequant_act_quant (gelu8, FFN-down's A)
+//   DOWN  int32 product, dequantise_c; add_norm_quant quantises the next
+//         layer's QKV A (the last layer: LayerNorm only)
+// The dispatches are the stand-in design's emulation (ref_stub.cpp): the
+// exact int32 product of the int8 rows and the operand, recovered as int8
+// [K, N] from the reference's own untiler (host_b_kn hands back
+// float(q) * wscale, and rint(that / wscale) = q exactly for |q| <= 127).
+// Arguments and result as nebw_ref_encode.
+int nebw_ref_encode_array(const char *npue_path, int32_t seq, const int32_t *ids,
+                          const int32_t *attn_mask, int32_t batch, int32_t threads, float *out,
+                          float *hidden_out, char *err, int32_t errlen) {
+  try {
+    ArrayEmulation emu;
+    npue::File f(npue_path);
+    nebw_oracle_describe_design(f);
+    if (nebw_oracle_a_elem_bytes != 1)
+      throw std::runtime_error("the array emulation runs int8 containers (a_dtype i8) only");
+    app::set_model_shape(f);
+    app::set_design_seq(seq);
+    const int64_t rows = static_cast<int64_t>(batch) * seq;
+    int64_t max_k = 0, max_n = 0;
+    for (int64_t L = 0; L < app::g_layers; ++L)
+      for (const char *g : {"qkv", "attn_out", "ffn_up", "ffn_down"}) {
+        const std::string name = "layer." + std::to_string(L) + "." + g;
+        const npue::TensorInfo &t = f.info(name);
+        if (t.dtype != "I8") throw std::runtime_error(name + ": the emulation takes I8 panels");
+        const npue::Panel panel = npue::gemm_b_panel(f, name, 1);
+        const std::vector<float> w = npue::hostb::host_b_kn(f, name);
+        const float *ws = f.raw(name + ".wscale").as<float>();
+        NebwArrayOperand op;
+        op.K = t.padded_shape[0];
+        op.N = t.padded_shape[1];
+        op.kn.resize(static_cast<size_t>(op.K * op.N));
+        for (int64_t k = 0; k < op.K; ++k)
+          for (int64_t n = 0; n < op.N; ++n) {
+            const float v = w[k * op.N + n];
+            const float q = ws[n] != 0.f ? std::rint(v / ws[n]) : 0.f;
+            if (!(q >= -127.f && q <= 127.f) || (ws[n] == 0.f && v != 0.f))
+              throw std::runtime_error(name + ": operand does not recover as int8");
+            op.kn[k * op.N + n] = static_cast<int8_t>(q);
+          }
+        max_k = std::max(max_k, op.K);
+        max_n = std::max(max_n, op.N);
+        nebw_array_registry[panel.bytes.data] = std::move(op);
+      }
+    nebw_array_rows = rows;
+    nebw_array_a.assign(static_cast<size_t>(rows * max_k + 64), 0);
+    nebw_array_c.assign(static_cast<size_t>(rows * max_n + 16), 0);
+    nebw_array_on = true;
+
+    app::Pool pool(threads > 0 ? threads : 1);
+    npu::Device dev;
+    npu::Design d(dev, "oracle-array");
+    npue::BertEncoder enc(f, d, d, d, d, d, d, d, pool);
+    enc.host_ln = enc.host_sm = enc.host_gelu = true;
+    enc.batch = batch;
+    enc.rows = rows;
+    enc.stage_all();
+    std::vector<float> x, cmask, cam;
+    gather_rows(f, seq, ids, attn_mask, batch, x, cmask, cam);
+    enc.add_mask = cmask;
+    std::vector<float> h = enc.run(x);
     if (hidden_out) std::memcpy(hidden_out, h.data(), h.size() * sizeof(float));
     app::pool_rows(h.data(), cam.data(), batch, out);
     return 0;

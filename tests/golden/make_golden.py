@@ -36,6 +36,14 @@ is sampled as well as its median):
                      with .wscale / .asmooth), 8 rows through the reference's
                      host path on that container (host_b.hpp untiles it);
                      the container is regenerated (its SHA-256 is stored).
+  i8_array_c1.npz, i8_array_c2.npz
+                     MiniLM (8 rows) and bge-small (4 rows) through the
+                     reference's int8 ARRAY path on the int8 container above:
+                     BertEncoder::run with every GEMM on the array (int8 host
+                     quantisation, the int32 product, dequantisation, the fused
+                     add_norm_quant / dequant_act_quant epilogues), each
+                     dispatch the exact int32 product computed by the oracle's
+                     stand-in design; container SHA-256 stored.
   vit_pretiled_bf16_c5.npz, vit_pretiled_i8_c5.npz
                      vit-base written by nebw.npue with pre-tiled encoder
                      operands (bf16, or int8 with .wscale / .asmooth), the
@@ -205,6 +213,33 @@ def make_pretiled(ref, name, key, a_dtype):
     print(f"{name}: {len(rows)} rows")
 
 
+I8_ARRAY = {"i8_array_c1": ("minilm", 8), "i8_array_c2": ("bge-small", 4)}
+
+
+def make_i8_array(ref, name, key, n):
+    """The reference's int8 ARRAY path (BertEncoder::run with the GEMMs on the
+    array: int8 host steps around exact int32 products) on the configuration's
+    int8 pre-tiled container, the one make_pretiled writes."""
+    import tempfile
+    cfg = synth.CONFIGS[key]
+    ids, mask, lens = synth.config_batch(cfg)
+    rows = sample_rows(lens, n)
+    t0 = time.time()
+    with tempfile.TemporaryDirectory(dir=HERE) as td:
+        path = Path(td) / "c.npue"
+        digest = write_pretiled(path, key, "i8")
+        out = ref.encode_container(path, cfg.seq, ids[rows], mask[rows],
+                                   hidden_size=cfg.arch.hidden, array=True)
+    np.savez_compressed(
+        HERE / f"{name}.npz", config=key, a_dtype="i8", container_sha256=digest,
+        rows=rows.astype(np.int32), ids=ids[rows], mask=mask[rows],
+        lens=lens[rows].astype(np.int32), embeddings=out,
+        provenance="reference int8 array path (BertEncoder::run with --npu-ops gemm and the "
+                   "fused epilogues; each dispatch the exact int32 product, oracle/ref_stub.cpp "
+                   "array emulation) via oracle/ref_driver.cpp nebw_ref_encode_array")
+    print(f"{name}: {len(rows)} rows in {time.time() - t0:.1f} s")
+
+
 VIT_PRETILED = {"vit_pretiled_bf16_c5": ("vit-base", "bf16"),
                 "vit_pretiled_i8_c5": ("vit-base", "i8")}
 
@@ -263,6 +298,9 @@ def main():
     for name, (key, a_dtype) in PRETILED.items():
         if not only or name in only:
             make_pretiled(ref, name, key, a_dtype)
+    for name, (key, n) in I8_ARRAY.items():
+        if not only or name in only:
+            make_i8_array(ref, name, key, n)
     for name, (key, a_dtype) in VIT_PRETILED.items():
         if not only or name in only:
             make_vit_pretiled(ref, name, key, a_dtype)

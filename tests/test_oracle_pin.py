@@ -256,3 +256,49 @@ def test_port_gemm_i8_exact(port_oracle):
         B = rng.integers(-127, 128, (K, N), dtype=np.int8)
         want = (A.astype(np.int64) @ B.astype(np.int64)).astype(np.int32)
         np.testing.assert_array_equal(port_oracle.gemm_i8(A, B, threads=2), want)
+
+
+# ---- the int8 pass: BertEncoder::run's array path ---------------------------
+
+def test_port_int8_pass_bit_exact_vs_reference(port_oracle, ref_oracle, tmp_path):
+    """The C restatement of the int8 array path (nebw_oracle_encode_i8)
+    against the reference's own BertEncoder::run with every GEMM on the array
+    (oracle/ref_driver.cpp nebw_ref_encode_array: the reference's int8 host
+    steps and fused epilogues, each dispatch the exact int32 product), on the
+    int8 pre-tiled MiniLM container: embeddings and every hidden row bit for
+    bit.  The array path really quantises: it differs from the reference's
+    host path on the same container, within int8 rounding."""
+    mg = _int8_golden_module()
+    from nebw import synth
+    cfg = synth.CONFIGS["minilm"]
+    w = synth.config_weights(cfg)
+    ids, mask, lens = synth.config_batch(cfg)
+    rows = mg.sample_rows(lens, 4)
+    path = tmp_path / "c.npue"
+    mg.write_pretiled(path, "minilm", "i8")
+    want, want_h = ref_oracle.encode_container(path, cfg.seq, ids[rows], mask[rows],
+                                               hidden_size=cfg.arch.hidden, array=True,
+                                               hidden=True)
+    got, got_h = port_oracle.encode_i8(w, path, ids[rows], mask[rows], hidden=True)
+    _bits_equal(got, want)
+    _bits_equal(got_h, want_h)
+    host = ref_oracle.encode_container(path, cfg.seq, ids[rows], mask[rows],
+                                       hidden_size=cfg.arch.hidden)
+    cos = (host * got).sum(1) / np.linalg.norm(host, axis=1) / np.linalg.norm(got, axis=1)
+    assert not np.array_equal(host, got) and cos.min() >= 0.999, cos.min()
+
+
+@pytest.mark.parametrize("name", ["i8_array_c1", "i8_array_c2"])
+def test_port_matches_golden_i8_array(port_oracle, tmp_path, name):
+    """The int8 restatement against the reference's array-path rows committed
+    in tests/golden (made by make_golden.py on the regenerated container, whose
+    SHA-256 is checked), bit for bit."""
+    mg = _int8_golden_module()
+    from nebw import synth
+    g = load_golden(name)
+    key, _n = mg.I8_ARRAY[name]
+    path = tmp_path / "c.npue"
+    assert mg.write_pretiled(path, key, "i8") == str(g["container_sha256"])
+    w = synth.config_weights(synth.CONFIGS[key])
+    got = port_oracle.encode_i8(w, path, g["ids"], g["mask"])
+    _bits_equal(got, g["embeddings"])
