@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NEBW_ABI_VERSION 4
+#define NEBW_ABI_VERSION 5
 
 typedef enum nebw_status {
   NEBW_OK = 0,
@@ -205,6 +205,27 @@ int nebw_stage_weight_i8(nebw_dev *dev, const int8_t *host_kn, int64_t K, int64_
 int nebw_gemm_i8(nebw_dev *dev, uint64_t weight, const int8_t *A, const float *sa, int64_t M,
                  int64_t K, int64_t N, const float *ws, const float *bias, int act, float *C,
                  void *stream);
+/* nebw_gemm_i8 with the output type chosen: c_dtype NEBW_F32 (as above) or
+ * NEBW_BF16, the dequantised value narrowed RNE (app::to_bf16,
+ * host_kernels.hpp:157-161) -- the form the int8 pass feeds the tensor-core
+ * attention with.  C 16-byte (F32) or 8-byte (BF16) aligned. */
+int nebw_gemm_i8_ex(nebw_dev *dev, uint64_t weight, const int8_t *A, const float *sa, int64_t M,
+                    int64_t K, int64_t N, const float *ws, const float *bias, int act, void *C,
+                    int c_dtype, void *stream);
+/* nebw_quantise_rows over bf16 rows (x_bf16 [rows, K] bf16 bits, widened
+ * exactly): the attention output's quantisation for the attention-out GEMM
+ * in the int8 pass. */
+int nebw_quantise_rows_bf16(nebw_dev *dev, const void *x_bf16, int64_t rows, int64_t K,
+                            const float *ias, int8_t *q, float *scale, void *stream);
+/* BertEncoder::add_norm_quant (runtime/src/encoders/bert_encoder.cpp:
+ * 1196-1302): x = LN(x + y) in place (y fp32 [rows, H], or NULL), then, when
+ * q is not NULL, the normalised rows quantised for the next int8 GEMM with
+ * its divisor ias [H]: the steps of nebw_quantise_rows on the rows in
+ * registers.  x, y, gamma, beta, ias 16-byte aligned; H a multiple of 128
+ * up to 2048. */
+int nebw_layernorm_quant(nebw_dev *dev, float *x, const float *y, const float *gamma,
+                         const float *beta, float eps, int64_t rows, int64_t H, const float *ias,
+                         int8_t *q, float *scale, void *stream);
 
 /* ---- the whole encoder -------------------------------------------------- */
 
@@ -254,6 +275,29 @@ int nebw_model_set_tensor(nebw_model *m, const char *name, const void *host, int
  * (runtime/src/design.cpp:394) for the array's block-panel layout. */
 int nebw_model_set_gemm_nk(nebw_model *m, const char *name, const uint16_t *host_bf16_nk,
                            int64_t n_rows, int64_t k_cols);
+/* An int8 GEMM operand for the int8 datapath: "layer.{i}.{qkv,attn_out,
+ * ffn_up,ffn_down}" as the container's int8 panel untiled to [K, N] (host),
+ * its per-column scale wscale [N] (.wscale) and the activation's SmoothQuant
+ * divisor asmooth [K] (.asmooth; the pass multiplies by 1 / asmooth taken in
+ * float, bert_encoder.cpp:767-772).  K and N as the model's GEMM.
+ * nebw_model_load_npue sets these for an int8 container. */
+int nebw_model_set_int8_operand(nebw_model *m, const char *name, const int8_t *host_kn,
+                                const float *wscale, const float *asmooth, int64_t K, int64_t N);
+/* Which arithmetic the encoder passes run.  NEBW_DATAPATH_BF16 (the
+ * default): bf16 tensor-core GEMMs over the staged operands -- for an int8
+ * container, its weights dequantised, as the reference's default host path
+ * multiplies them (--npu-ops empty).  NEBW_DATAPATH_I8: the reference's
+ * array path for an int8 container (`--npu-ops gemm`, BertEncoder::run,
+ * bert_encoder.cpp:1419-1598 with gemm()'s array branch :763-923): every
+ * GEMM int8 x int8 -> int32 on tcgen05.mma kind::i8 between the reference's
+ * host steps -- quantise the A rows, dequantise C, gelu8 + quantise after
+ * FFN-up, add + LayerNorm + quantise (add_norm_quant) -- with the attention
+ * on the bf16 tensor cores.  Needs every layer's four int8 operands and a
+ * plain BERT model (no gated FFN, no rotary); refused otherwise.  The static
+ * entry point (nebw_encode_device_static) runs the bf16 datapath only and
+ * refuses a model set to NEBW_DATAPATH_I8. */
+enum { NEBW_DATAPATH_BF16 = 0, NEBW_DATAPATH_I8 = 1 };
+int nebw_model_set_datapath(nebw_model *m, int32_t datapath);
 /* The rotary frequency set as data (gte_new_rope_geglu's rope_inv_freq):
  * n = head_dim / 2 values, angle(s, j) = s * inv_freq[j] in double, as
  * apply_rope_qkv builds its tables (bert_encoder.cpp:929-945). */

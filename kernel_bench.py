@@ -152,16 +152,29 @@ def bench_gemm_i8(dev, M, K, N, epi, iters, copies):
             "tops": ops / (ms / 1e3) / 1e12}
 
 
-def bench_encoder(dev, config, layers, iters):
+def bench_encoder(dev, config, layers, iters, datapath="bf16"):
     """Whole passes of a benchmark configuration's batch through a model of
     `layers` layers (the production launch sequence, attention work list
-    included), with per-kernel device times from the model's profiler."""
+    included), with per-kernel device times from the model's profiler.
+    datapath "i8": the same weights written as an int8 pre-tiled container
+    (the reference's --dtype i8 form) and run on the int8 datapath."""
+    import tempfile
     import torch
     import nebw
     from nebw import synth
     cfg = synth.CONFIGS[config]
     ids, _, lens = synth.config_batch(cfg)
-    m = nebw.Model.from_weights(dev, synth.config_weights(cfg, layers=layers), max_seq_len=cfg.seq)
+    w = synth.config_weights(cfg, layers=layers)
+    if datapath == "i8":
+        from nebw.npue import write_bert_container
+        with tempfile.TemporaryDirectory() as td:
+            path = f"{td}/i8.npue"
+            write_bert_container(path, w, max_seq_len=cfg.seq, gemm_layout="pretiled_bf16",
+                                 a_dtype="i8", tile=(64, 64), mac=(8, 8), smooth_seed=1)
+            m = nebw.Model.from_npue(dev, path)
+        m.set_datapath("i8")
+    else:
+        m = nebw.Model.from_weights(dev, w, max_seq_len=cfg.seq)
     ids_d = torch.from_numpy(ids).cuda()
     lens_d = torch.from_numpy(lens.astype(np.int32)).cuda()
     out = torch.empty(cfg.batch, m.hidden, device="cuda")
@@ -185,7 +198,7 @@ def bench_encoder(dev, config, layers, iters):
     per = {k: round(ms / iters, 4) for k, (n, ms) in m.profile_collect().items() if n}
     m.profile(False)
     m.close()
-    return {"kernel": "encoder", "config": config, "layers": layers,
+    return {"kernel": "encoder", "config": config, "layers": layers, "datapath": datapath,
             "ms": e0.elapsed_time(e1) / iters, "kernels_ms": per}
 
 
@@ -207,6 +220,8 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=2)
     ap.add_argument("--attn-kind", type=int, default=1, help="0 mma.sync, 1 tcgen05")
+    ap.add_argument("--datapath", default="bf16", choices=["bf16", "i8"],
+                    help="encoder: bf16 weights, or an int8 container on the int8 datapath")
     a = ap.parse_args(argv)
     dev = nebw.Device(0, torch_stream=True)
     dev.set_attention_kernel(a.attn_kind)
@@ -219,7 +234,7 @@ def main(argv=None):
     elif a.op == "layernorm":
         r = bench_layernorm(dev, a.M, a.H, a.iters, a.copies)
     else:
-        r = bench_encoder(dev, a.config, a.layers, a.iters)
+        r = bench_encoder(dev, a.config, a.layers, a.iters, a.datapath)
     print(json.dumps(r), flush=True)
     dev.close()
 

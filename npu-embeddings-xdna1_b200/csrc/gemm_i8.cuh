@@ -14,7 +14,8 @@
 //                          (exact), dequantised in the epilogue as
 //                          y = fma(float(C) * sa[row], ws[col], bias[col]),
 //                          optionally gelu8(y) (dequant_act_quant's act),
-//                          fp32 out
+//                          fp32 out -- or bf16 RNE of y for the encoder's
+//                          QKV product, which the tensor-core attention reads
 //
 // The integer product is exact and every floating-point step is the
 // reference's single IEEE operation in its order (int -> float round to
@@ -30,6 +31,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cstdint>
 
 #include "gemm_tc.cuh"
@@ -41,10 +43,12 @@ constexpr int kGemmI8BK = 128;  // int8 elements per K-block (one 128-byte row)
 
 struct GemmI8Args {
   int M, N, K;
+  const int *M_dev;   // if set, the live row count is min(*M_dev, M)
   const float *sa;    // [M] row scales of A (quantise_rows' sc)
   const float *ws;    // [N] column scales of W
   const float *bias;  // [N] or null (then 0)
-  float *out;         // [M, N] fp32
+  float *out;         // [M, N] fp32, or
+  __nv_bfloat16 *out_bf16;  // [M, N] bf16 RNE of the dequantised value (out null)
   int *err;
 };
 
@@ -67,18 +71,25 @@ __device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+__device__ __forceinline__ float widen(float v) { return v; }
+__device__ __forceinline__ float widen(__nv_bfloat16 v) { return __bfloat162float(v); }
+
 // One row per warp: quantise_a_int8 (host_kernels.hpp:263-315).  The row
 // maximum is order-independent, so the warp reduction gives the reference's
-// value exactly; sc = mx / 127 and inv = 1 / sc are IEEE divisions.
+// value exactly; sc = mx / 127 and inv = 1 / sc are IEEE divisions.  x is
+// fp32, or bf16 widened exactly (the attention's output); rows past
+// *rows_dev (when set) are left alone.
+template <typename XT>
 __global__ void __launch_bounds__(256)
-    quantise_rows_kernel(const float *__restrict__ x, int rows, int K,
-                         const float *__restrict__ ias, int8_t *__restrict__ q,
+    quantise_rows_kernel(const XT *__restrict__ x, int rows, const int *__restrict__ rows_dev,
+                         int K, const float *__restrict__ ias, int8_t *__restrict__ q,
                          float *__restrict__ scale) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (rows_dev) rows = min(rows, __ldg(rows_dev));
   if (row >= rows) return;
-  const float *xr = x + static_cast<int64_t>(row) * K;
+  const XT *xr = x + static_cast<int64_t>(row) * K;
   float mx = 0.0f;
-  for (int j = lane; j < K; j += 32) mx = fmaxf(mx, fabsf(xr[j] * __ldg(ias + j)));
+  for (int j = lane; j < K; j += 32) mx = fmaxf(mx, fabsf(widen(xr[j]) * __ldg(ias + j)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
@@ -86,19 +97,20 @@ __global__ void __launch_bounds__(256)
   if (lane == 0) scale[row] = sc;
   int8_t *qr = q + static_cast<int64_t>(row) * K;
   for (int j = lane; j < K; j += 32) {
-    const float t = fminf(fmaxf((xr[j] * __ldg(ias + j)) * inv, -127.0f), 127.0f);
+    const float t = fminf(fmaxf((widen(xr[j]) * __ldg(ias + j)) * inv, -127.0f), 127.0f);
     qr[j] = static_cast<int8_t>(__float2int_rn(t));
   }
 }
 
 // Dequantise (and gelu8) 32 accumulator columns [col0, col0 + 32) of one row
-// and store them as fp32.
+// and store them as fp32, or as bf16 RNE (p.out_bf16).
 template <bool GELU>
 __device__ __forceinline__ void i8_store32(const GemmI8Args &p, int row, int col0,
                                            const uint32_t (&r)[32]) {
   const int ncols = min(32, p.N - col0);  // N % 8 == 0
   const float sa = __ldg(p.sa + row);
   float4 *o4 = reinterpret_cast<float4 *>(p.out + static_cast<size_t>(row) * p.N + col0);
+  uint2 *o2 = reinterpret_cast<uint2 *>(p.out_bf16 + static_cast<size_t>(row) * p.N + col0);
   const float4 *w4 = reinterpret_cast<const float4 *>(p.ws + col0);
   const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
 #pragma unroll
@@ -114,7 +126,10 @@ __device__ __forceinline__ void i8_store32(const GemmI8Args &p, int row, int col
       y[e] = fmaf(c * sa, ws[e], bs[e]);
       if constexpr (GELU) y[e] = gelu8(y[e]);
     }
-    o4[i] = make_float4(y[0], y[1], y[2], y[3]);
+    if (p.out_bf16)
+      o2[i] = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+    else
+      o4[i] = make_float4(y[0], y[1], y[2], y[3]);
   }
 }
 
@@ -141,7 +156,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int M = p.M;
+  int M = p.M;
+  if (p.M_dev) M = min(M, __ldg(p.M_dev));
   const int m_blocks = (M + kGemmBM - 1) / kGemmBM;
   const int n_blocks = (p.N + BN - 1) / BN;
   const int num_tiles = m_blocks * n_blocks;

@@ -424,6 +424,83 @@ int launch_layernorm(float *x, const void *y, bool y_bf16, const float *g, const
 }
 
 template <int NV>
+void launch_lnq_nv(float *x, const float *y, const float *g, const float *b, float eps, int rows,
+                   const int *rows_dev, const float *ias, int8_t *q, float *scale,
+                   cudaStream_t st) {
+  const int grid = (rows + nebw::kRowWarps - 1) / nebw::kRowWarps;
+  nebw::layernorm_quant_kernel<NV><<<grid, nebw::kRowWarps * 32, 0, st>>>(
+      x, y, g, b, eps, rows, rows_dev, ias, q, scale);
+}
+
+// add_norm_quant: x = LN(x + y) for the live rows, and the rows quantised
+// for the next int8 GEMM when q is set.
+int launch_layernorm_quant(float *x, const float *y, const float *g, const float *b, float eps,
+                           int64_t rows, int64_t H, const int *rows_dev, const float *ias,
+                           int8_t *q, float *scale, cudaStream_t st) {
+  NEBW_REQUIRE(H % 128 == 0 && H >= 128 && H <= 2048,
+               "LayerNorm width %lld refused: a multiple of 128 up to 2048 is required",
+               static_cast<long long>(H));
+  NEBW_REQUIRE(!q || (ias && scale), "quantised LayerNorm output without its divisor or scales");
+  NEBW_REQUIRE(rows < (1ll << 31), "LayerNorm rows %lld refused", static_cast<long long>(rows));
+  if (rows <= 0) return NEBW_OK;
+  const int r = static_cast<int>(rows);
+  switch (H / 128) {
+#define NEBW_LNQ_CASE(n) \
+  case n: launch_lnq_nv<n>(x, y, g, b, eps, r, rows_dev, ias, q, scale, st); break;
+    NEBW_LNQ_CASE(1) NEBW_LNQ_CASE(2) NEBW_LNQ_CASE(3) NEBW_LNQ_CASE(4) NEBW_LNQ_CASE(5)
+    NEBW_LNQ_CASE(6) NEBW_LNQ_CASE(7) NEBW_LNQ_CASE(8) NEBW_LNQ_CASE(9) NEBW_LNQ_CASE(10)
+    NEBW_LNQ_CASE(11) NEBW_LNQ_CASE(12) NEBW_LNQ_CASE(13) NEBW_LNQ_CASE(14) NEBW_LNQ_CASE(15)
+    NEBW_LNQ_CASE(16)
+#undef NEBW_LNQ_CASE
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+// quantise_a_int8 over fp32 or bf16 rows [rows, K] (the live rows when
+// rows_dev is set).
+int launch_quantise(const void *x, bool x_bf16, int64_t rows, const int *rows_dev, int64_t K,
+                    const float *ias, int8_t *q, float *scale, cudaStream_t st) {
+  NEBW_REQUIRE(rows >= 0 && rows < (1ll << 31) && K > 0 && K < (1ll << 31),
+               "quantise [%lld, %lld] refused", static_cast<long long>(rows),
+               static_cast<long long>(K));
+  if (rows == 0) return NEBW_OK;
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  if (x_bf16)
+    nebw::quantise_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16 *>(x), static_cast<int>(rows), rows_dev,
+        static_cast<int>(K), ias, q, scale);
+  else
+    nebw::quantise_rows_kernel<float><<<grid, 256, 0, st>>>(
+        static_cast<const float *>(x), static_cast<int>(rows), rows_dev, static_cast<int>(K), ias,
+        q, scale);
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+// The int8 GEMM over a staged operand: A's tensor map `mA` (128-row boxes),
+// a.M the row bound (a.M_dev the live count), fp32 or bf16 out as `a` says.
+int launch_gemm_i8(nebw_dev *d, const WeightI8 &w, const CUtensorMap &mA,
+                   const nebw::GemmI8Args &a, bool gelu, cudaStream_t st) {
+  if (a.M <= 0) return NEBW_OK;
+  const bool wide = w.N % 256 == 0;
+  const int BN = wide ? 256 : 128;
+  const int64_t tiles = ((int64_t{a.M} + nebw::kGemmBM - 1) / nebw::kGemmBM) * ((w.N + BN - 1) / BN);
+  const dim3 g(static_cast<unsigned>(std::min<int64_t>(tiles, d->sm_count))), b(nebw::kGemmThreads);
+  if (wide) {
+    const size_t smem = nebw::GemmShape<256>::kSmemBytes;
+    if (gelu) nebw::gemm_i8_kernel<256, true><<<g, b, smem, st>>>(mA, w.map256, a);
+    else nebw::gemm_i8_kernel<256, false><<<g, b, smem, st>>>(mA, w.map256, a);
+  } else {
+    const size_t smem = nebw::GemmShape<128>::kSmemBytes;
+    if (gelu) nebw::gemm_i8_kernel<128, true><<<g, b, smem, st>>>(mA, w.map128, a);
+    else nebw::gemm_i8_kernel<128, false><<<g, b, smem, st>>>(mA, w.map128, a);
+  }
+  NEBW_CUDA(cudaGetLastError());
+  return NEBW_OK;
+}
+
+template <int NV>
 void launch_embed_nv(const int *ids, int B, int S, const int *off, const int *len,
                      const float *word, int vocab, const float *pos, const float *typ,
                      const float *g, const float *b, float eps, float *x, __nv_bfloat16 *a,
@@ -902,36 +979,51 @@ extern "C" int nebw_narrow_bf16(nebw_dev *d, const float *x, int64_t n, void *y,
 
 // ---- the int8 datapath (the reference's --dtype i8 array path) -------------
 
-extern "C" int nebw_stage_weight_i8(nebw_dev *d, const int8_t *host_kn, int64_t K, int64_t N,
-                                    uint64_t *handle) {
-  if (int rc = use_dev(d)) return rc;
-  NEBW_REQUIRE(host_kn && handle, "null argument");
+namespace {
+// An int8 operand [K, N] (host, row-major) staged as [N, K] (the tensor-core
+// B layout) with its 128- and 256-row tensor maps.
+int stage_i8(const int8_t *host_kn, int64_t K, int64_t N, WeightI8 &w) {
   NEBW_REQUIRE(K > 0 && N > 0 && K % 16 == 0 && N % 8 == 0,
                "int8 weight [%lld, %lld] refused: K %% 16 == 0 and N %% 8 == 0 required",
                static_cast<long long>(K), static_cast<long long>(N));
   std::vector<int8_t> nk(static_cast<size_t>(K * N));
   for (int64_t k = 0; k < K; ++k)
     for (int64_t n = 0; n < N; ++n) nk[static_cast<size_t>(n * K + k)] = host_kn[k * N + n];
-  WeightI8 w;
+  w = WeightI8{};
   w.K = K;
   w.N = N;
   NEBW_CUDA(cudaMalloc(&w.ptr, nk.size()));
-  NEBW_CUDA(cudaMemcpy(w.ptr, nk.data(), nk.size(), cudaMemcpyHostToDevice));
+  if (cudaMemcpy(w.ptr, nk.data(), nk.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(w.ptr);
+    w.ptr = nullptr;
+    return set_error(NEBW_ECUDA, "int8 weight upload failed");
+  }
   int rc = make_tmap_i8(&w.map128, w.ptr, N, K, 128);
   if (!rc) rc = make_tmap_i8(&w.map256, w.ptr, N, K, 256);
   if (rc) {
     cudaFree(w.ptr);
-    return rc;
+    w.ptr = nullptr;
   }
+  return rc;
+}
+}  // namespace
+
+extern "C" int nebw_stage_weight_i8(nebw_dev *d, const int8_t *host_kn, int64_t K, int64_t N,
+                                    uint64_t *handle) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(host_kn && handle, "null argument");
+  WeightI8 w;
+  if (int rc = stage_i8(host_kn, K, N, w)) return rc;
   const uint64_t h = d->next_handle++;
   d->weights_i8[h] = w;
   *handle = h;
   return NEBW_OK;
 }
 
-extern "C" int nebw_gemm_i8(nebw_dev *d, uint64_t weight, const int8_t *A, const float *sa,
-                            int64_t M, int64_t K, int64_t N, const float *ws, const float *bias,
-                            int act, float *C, void *stream) {
+extern "C" int nebw_gemm_i8_ex(nebw_dev *d, uint64_t weight, const int8_t *A, const float *sa,
+                               int64_t M, int64_t K, int64_t N, const float *ws, const float *bias,
+                               int act, void *C, int c_dtype, void *stream) {
   if (int rc = use_dev(d)) return rc;
   auto it = d->weights_i8.find(weight);
   NEBW_REQUIRE(it != d->weights_i8.end(), "unknown int8 weight handle %llu",
@@ -943,10 +1035,12 @@ extern "C" int nebw_gemm_i8(nebw_dev *d, uint64_t weight, const int8_t *A, const
   NEBW_REQUIRE(A && sa && ws && C, "null int8 GEMM operand");
   NEBW_REQUIRE(M >= 0 && M < (1ll << 31), "M %lld refused", static_cast<long long>(M));
   NEBW_REQUIRE(act == NEBW_ACT_NONE || act == NEBW_ACT_GELU8, "int8 GEMM act %d refused", act);
-  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+  NEBW_REQUIRE(c_dtype == NEBW_F32 || c_dtype == NEBW_BF16, "int8 GEMM c_dtype %d refused",
+               c_dtype);
+  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(C) % (c_dtype == NEBW_F32 ? 16 : 8) == 0 &&
                    reinterpret_cast<uintptr_t>(ws) % 16 == 0 &&
                    (!bias || reinterpret_cast<uintptr_t>(bias) % 16 == 0),
-               "int8 GEMM C, ws and bias must be 16-byte aligned");
+               "int8 GEMM C (16 bytes fp32, 8 bytes bf16), ws and bias must be aligned");
   if (M == 0) return NEBW_OK;
   CUtensorMap mA;
   if (int rc = make_tmap_i8(&mA, A, M, K, nebw::kGemmBM)) return rc;
@@ -957,40 +1051,45 @@ extern "C" int nebw_gemm_i8(nebw_dev *d, uint64_t weight, const int8_t *A, const
   a.sa = sa;
   a.ws = ws;
   a.bias = bias;
-  a.out = C;
+  if (c_dtype == NEBW_F32) a.out = static_cast<float *>(C);
+  else a.out_bf16 = static_cast<__nv_bfloat16 *>(C);
   a.err = d->d_err;
-  const bool wide = N % 256 == 0;
-  const int BN = wide ? 256 : 128;
-  const int64_t tiles = ((M + nebw::kGemmBM - 1) / nebw::kGemmBM) * ((N + BN - 1) / BN);
-  const dim3 g(static_cast<unsigned>(std::min<int64_t>(tiles, d->sm_count))), b(nebw::kGemmThreads);
-  cudaStream_t st = pick_stream(d, stream);
-  const bool gelu = act == NEBW_ACT_GELU8;
-  if (wide) {
-    const size_t smem = nebw::GemmShape<256>::kSmemBytes;
-    if (gelu) nebw::gemm_i8_kernel<256, true><<<g, b, smem, st>>>(mA, w.map256, a);
-    else nebw::gemm_i8_kernel<256, false><<<g, b, smem, st>>>(mA, w.map256, a);
-  } else {
-    const size_t smem = nebw::GemmShape<128>::kSmemBytes;
-    if (gelu) nebw::gemm_i8_kernel<128, true><<<g, b, smem, st>>>(mA, w.map128, a);
-    else nebw::gemm_i8_kernel<128, false><<<g, b, smem, st>>>(mA, w.map128, a);
-  }
-  NEBW_CUDA(cudaGetLastError());
-  return NEBW_OK;
+  return launch_gemm_i8(d, w, mA, a, act == NEBW_ACT_GELU8, pick_stream(d, stream));
+}
+
+extern "C" int nebw_gemm_i8(nebw_dev *d, uint64_t weight, const int8_t *A, const float *sa,
+                            int64_t M, int64_t K, int64_t N, const float *ws, const float *bias,
+                            int act, float *C, void *stream) {
+  return nebw_gemm_i8_ex(d, weight, A, sa, M, K, N, ws, bias, act, C, NEBW_F32, stream);
 }
 
 extern "C" int nebw_quantise_rows(nebw_dev *d, const float *x, int64_t rows, int64_t K,
                                   const float *ias, int8_t *q, float *scale, void *stream) {
   if (int rc = use_dev(d)) return rc;
   NEBW_REQUIRE(x && ias && q && scale, "null quantise operand");
-  NEBW_REQUIRE(rows >= 0 && rows < (1ll << 31) && K > 0 && K < (1ll << 31),
-               "quantise [%lld, %lld] refused", static_cast<long long>(rows),
-               static_cast<long long>(K));
-  if (rows == 0) return NEBW_OK;
-  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
-  nebw::quantise_rows_kernel<<<grid, 256, 0, pick_stream(d, stream)>>>(
-      x, static_cast<int>(rows), static_cast<int>(K), ias, q, scale);
-  NEBW_CUDA(cudaGetLastError());
-  return NEBW_OK;
+  return launch_quantise(x, false, rows, nullptr, K, ias, q, scale, pick_stream(d, stream));
+}
+
+extern "C" int nebw_quantise_rows_bf16(nebw_dev *d, const void *x, int64_t rows, int64_t K,
+                                       const float *ias, int8_t *q, float *scale, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(x && ias && q && scale, "null quantise operand");
+  return launch_quantise(x, true, rows, nullptr, K, ias, q, scale, pick_stream(d, stream));
+}
+
+extern "C" int nebw_layernorm_quant(nebw_dev *d, float *x, const float *y, const float *g,
+                                    const float *b, float eps, int64_t rows, int64_t H,
+                                    const float *ias, int8_t *q, float *scale, void *stream) {
+  if (int rc = use_dev(d)) return rc;
+  NEBW_REQUIRE(x && g && b, "null LayerNorm operand");
+  for (const void *p : {static_cast<const void *>(x), static_cast<const void *>(y),
+                        static_cast<const void *>(g), static_cast<const void *>(b),
+                        static_cast<const void *>(ias)})
+    NEBW_REQUIRE(reinterpret_cast<uintptr_t>(p) % 16 == 0,
+                 "LayerNorm operands must be 16-byte aligned");
+  NEBW_REQUIRE(!q || reinterpret_cast<uintptr_t>(q) % 4 == 0, "q must be 4-byte aligned");
+  return launch_layernorm_quant(x, y, g, b, eps, rows, H, nullptr, ias, q, scale,
+                                pick_stream(d, stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -1001,6 +1100,18 @@ struct LayerW {
   Weight qkv, ao, up, dn;
   float *b_qkv = nullptr, *b_ao = nullptr, *b_up = nullptr, *b_dn = nullptr;
   float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+};
+
+// An int8 GEMM operand of the int8 datapath (nebw_model_set_int8_operand):
+// int8 [N, K] on the device with its tensor maps, the column scales and the
+// reciprocals of the activation's SmoothQuant divisors.
+struct OperandI8 {
+  WeightI8 w;
+  float *ws = nullptr;   // [N]
+  float *ias = nullptr;  // [K], 1 / asmooth in float
+};
+struct LayerI8 {
+  OperandI8 qkv, ao, up, dn;
 };
 
 // The activation buffers of one encoder pass: the model's own (grown with
@@ -1019,6 +1130,13 @@ struct Workspace {
   CUtensorMap map_qkv_att, map_kv_att;  // Q|K|V head tiles, head_dim x 128 / head_dim x 64 rows
   CUtensorMap map_a, map_ctx, map_h;    // GEMM A operands (TMA loads)
   CUtensorMap out_qkv, out_y, out_h;    // GEMM outputs (TMA stores)
+  // the int8 datapath's buffers (allocated only for it): the quantised A
+  // rows [rows, max(H, F)] with their scales [rows], the dequantised fp32
+  // outputs of the attention-out / FFN-down GEMMs [rows, H] and of FFN-up
+  // [rows, F]; A's tensor maps at K = H and K = F
+  int8_t *aq = nullptr;
+  float *sa = nullptr, *y32 = nullptr, *h32 = nullptr;
+  CUtensorMap map_aq_h, map_aq_f;
 };
 
 struct nebw_model {
@@ -1035,6 +1153,10 @@ struct nebw_model {
   bool glu_fused = false;
   std::vector<LayerW> layers;
   std::map<std::string, bool> staged;  // container name -> set
+  // the int8 datapath: its operands (sized to the layers on the first set)
+  // and the arithmetic the passes run (NEBW_DATAPATH_BF16 / _I8)
+  std::vector<LayerI8> i8;
+  int datapath = NEBW_DATAPATH_BF16;
   Workspace ws;                        // capacity ws.rows_cap = B * S of the largest call so far
   // host-buffer entry point (nebw_encode): device copies of its inputs and output
   int64_t ids_cap = 0;
@@ -1056,6 +1178,8 @@ void free_workspace(nebw_model *m) {
                   static_cast<void *>(w.qkv), static_cast<void *>(w.ctx), static_cast<void *>(w.h),
                   static_cast<void *>(w.len), static_cast<void *>(w.off),
                   static_cast<void *>(w.att_items), static_cast<void *>(w.row_pos),
+                  static_cast<void *>(w.aq), static_cast<void *>(w.sa),
+                  static_cast<void *>(w.y32), static_cast<void *>(w.h32),
                   static_cast<void *>(m->ids), static_cast<void *>(m->len_in),
                   static_cast<void *>(m->out)})
     cudaFree(p);
@@ -1094,12 +1218,17 @@ int make_workspace_maps(const nebw_model *m, Workspace &w, int64_t R) {
     if ((rc = make_tmap_head(&w.map_qkv_att, w.qkv, R, 3 * H, m->cfg.head_dim, 128))) return rc;
     if ((rc = make_tmap_head(&w.map_kv_att, w.qkv, R, 3 * H, m->cfg.head_dim, 64))) return rc;
   }
+  if (w.aq) {
+    if ((rc = make_tmap_i8(&w.map_aq_h, w.aq, R, H, nebw::kGemmBM))) return rc;
+    if ((rc = make_tmap_i8(&w.map_aq_f, w.aq, R, F, nebw::kGemmBM))) return rc;
+  }
   return NEBW_OK;
 }
 
 int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   const int64_t rows = B * S;
-  if (rows <= m->ws.rows_cap && B <= m->ws.batch_cap) return NEBW_OK;
+  const bool need_i8 = m->datapath == NEBW_DATAPATH_I8;
+  if (rows <= m->ws.rows_cap && B <= m->ws.batch_cap && (!need_i8 || m->ws.aq)) return NEBW_OK;
   NEBW_CUDA(cudaStreamSynchronize(m->dev->stream));
   const int64_t R = std::max(rows, m->ws.rows_cap), Bc = std::max(B, m->ws.batch_cap);
   free_workspace(m);
@@ -1123,6 +1252,13 @@ int ensure_workspace(nebw_model *m, int64_t B, int64_t S) {
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.off), (Bc + 1) * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.att_items), (R / 128 + Bc + 1) * 4);
   if (rope_in_epilogue(m)) rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.row_pos), R * 4);
+  if (need_i8) {
+    const int64_t F = m->cfg.intermediate;
+    rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.aq), R * std::max(H, F));
+    rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.sa), R * 4);
+    rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.y32), R * H * 4);
+    rc = rc ? rc : alloc(reinterpret_cast<void **>(&w.h32), R * F * 4);
+  }
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->ids), R * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->len_in), Bc * 4);
   rc = rc ? rc : alloc(reinterpret_cast<void **>(&m->out), Bc * H * 4);
@@ -1299,8 +1435,8 @@ int check_pass(const nebw_model *m, int B, int S) {
 // One encoder pass of B sequences padded to S into `out`, on the
 // workspace `ws` (which holds at least B * S rows and B sequences).  `prof`:
 // bracket each launch with the model's profiling events.
-int encode_device(nebw_model *m, Workspace &ws, bool prof, const int *ids, const int *len_in,
-                  int B, int S, float *out, cudaStream_t st) {
+int encode_device_bf16(nebw_model *m, Workspace &ws, bool prof, const int *ids, const int *len_in,
+                       int B, int S, float *out, cudaStream_t st) {
   nebw_dev *d = m->dev;
   const nebw_config &c = m->cfg;
   if (B * static_cast<int64_t>(S) > ws.rows_cap || B > ws.batch_cap)
@@ -1415,6 +1551,135 @@ int encode_device(nebw_model *m, Workspace &ws, bool prof, const int *ids, const
   if ((rc = launch_pool(ws.x, ws.off, ws.len, B, c.hidden, c.pooling, c.l2_normalize, out, st)))
     return rc;
   return prof_mark(m, prof, -1, st);
+}
+
+// One pass of the int8 datapath (NEBW_DATAPATH_I8): BertEncoder::run's
+// array path for an int8 container (bert_encoder.cpp:1419-1598, gemm()'s
+// array branch :763-923, with the fused epilogues), the GEMMs on
+// tcgen05.mma kind::i8:
+//   x = LN(embeddings); A = quantise(x, 1/asmooth_qkv) (layer 0)
+//   per layer:
+//     qkv  = dequantise(A . W_qkv), narrowed to bf16 for the attention
+//     ctx  = attention(qkv) (the bf16 tensor-core kernel)
+//     A    = quantise(ctx, 1/asmooth_ao); y = dequantise(A . W_ao) (fp32)
+//     x    = LN1(x + y); A = quantise(x, 1/asmooth_up)    (add_norm_quant)
+//     h    = gelu8(dequantise(A . W_up)); A = quantise(h, 1/asmooth_down)
+//                                                      (dequant_act_quant)
+//     y    = dequantise(A . W_down)
+//     x    = LN2(x + y); A = quantise(x, 1/asmooth_qkv of the next layer)
+//   pool + L2.
+// Every step runs over the packed rows (T on the device); the quantiser, the
+// dequantisation and gelu8 are the reference's operations bit for bit (the
+// int32 products are exact).  The bf16 narrow of qkv and the bf16 attention
+// are this library's, as on the bf16 datapath.
+int encode_device_i8(nebw_model *m, Workspace &ws, bool prof, const int *ids, const int *len_in,
+                     int B, int S, float *out, cudaStream_t st) {
+  nebw_dev *d = m->dev;
+  const nebw_config &c = m->cfg;
+  if (!ws.aq || B * static_cast<int64_t>(S) > ws.rows_cap || B > ws.batch_cap)
+    return set_error(NEBW_EINVAL, "internal: int8 workspace missing or too small for batch %d x "
+                     "seq %d", B, S);
+  if (static_cast<int>(m->i8.size()) != c.num_layers)
+    return set_error(NEBW_ESTATE, "the int8 datapath has no operands");
+  const int64_t H = c.hidden, F = c.intermediate;
+  const int rows = static_cast<int>(static_cast<int64_t>(B) * S);
+  const int *T_dev = ws.off + B;
+  int rc;
+  if ((rc = prof_mark(m, prof, NEBW_K_PACK, st))) return rc;
+  if ((rc = launch_pack(len_in, B, S, ws.len, ws.off, d->d_err, st))) return rc;
+  const bool tc_attention =
+      d->attn_kind == NEBW_ATTN_TCGEN05 && nebw::attn_tc_head_dim(c.head_dim);
+  if (tc_attention) {
+    // the work list; and the Q|K|V rows just past the packed rows zeroed
+    // (the attention's last partial key group reads V there; the int8 GEMM
+    // writes only the packed rows)
+    nebw::attn_work_kernel<<<1 + nebw::kAttnTailBlocks, 1024, 0, st>>>(
+        ws.len, B, ws.att_items + 1, ws.att_items, T_dev, ws.rows_cap, ws.qkv,
+        static_cast<int>(3 * H), ws.a, static_cast<int>(H));
+    NEBW_CUDA(cudaGetLastError());
+  }
+  if ((rc = prof_mark(m, prof, NEBW_K_EMBED_LN, st))) return rc;
+  if ((rc = launch_embed_ln(ids, B, S, ws.off, ws.len, m->word, c.vocab_size, m->pos, m->typ,
+                            m->emb_g, m->emb_b, c.layer_norm_eps, c.hidden, ws.x, nullptr,
+                            d->d_err, st)))
+    return rc;
+  if ((rc = launch_quantise(ws.x, false, rows, T_dev, H, m->i8[0].qkv.ias, ws.aq, ws.sa, st)))
+    return rc;
+  for (int L = 0; L < c.num_layers; ++L) {
+    const LayerW &w = m->layers[L];
+    const LayerI8 &q = m->i8[L];
+    nebw::GemmI8Args a{};
+    a.M = rows;
+    a.M_dev = T_dev;
+    a.sa = ws.sa;
+    a.err = d->d_err;
+    // QKV -> bf16 Q|K|V
+    a.N = static_cast<int>(3 * H);
+    a.K = static_cast<int>(H);
+    a.ws = q.qkv.ws;
+    a.bias = w.b_qkv;
+    a.out = nullptr;
+    a.out_bf16 = ws.qkv;
+    if ((rc = prof_mark(m, prof, NEBW_K_GEMM_QKV, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.qkv.w, ws.map_aq_h, a, false, st))) return rc;
+    if ((rc = prof_mark(m, prof, NEBW_K_ATTENTION, st))) return rc;
+    if (tc_attention)
+      rc = launch_attention_tc(d, ws.map_qkv_att, ws.map_kv_att, ws.off, ws.len, ws.att_items + 1,
+                               ws.att_items, B, S, c.num_heads, c.head_dim, ws.ctx, st);
+    else
+      rc = launch_attention(ws.qkv, ws.off, ws.len, B, S, c.num_heads, c.head_dim, ws.ctx, st);
+    if (rc) return rc;
+    // attention-out: quantise ctx, product, dequantise (fp32)
+    if ((rc = prof_mark(m, prof, NEBW_K_GEMM_AO, st))) return rc;
+    if ((rc = launch_quantise(ws.ctx, true, rows, T_dev, H, q.ao.ias, ws.aq, ws.sa, st))) return rc;
+    a.N = static_cast<int>(H);
+    a.K = static_cast<int>(H);
+    a.ws = q.ao.ws;
+    a.bias = w.b_ao;
+    a.out = ws.y32;
+    a.out_bf16 = nullptr;
+    if ((rc = launch_gemm_i8(d, q.ao.w, ws.map_aq_h, a, false, st))) return rc;
+    if ((rc = prof_mark(m, prof, NEBW_K_LN, st))) return rc;
+    if ((rc = launch_layernorm_quant(ws.x, ws.y32, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H,
+                                     T_dev, q.up.ias, ws.aq, ws.sa, st)))
+      return rc;
+    // FFN-up with gelu8, then quantised for FFN-down (dequant_act_quant)
+    a.N = static_cast<int>(F);
+    a.K = static_cast<int>(H);
+    a.ws = q.up.ws;
+    a.bias = w.b_up;
+    a.out = ws.h32;
+    if ((rc = prof_mark(m, prof, NEBW_K_GEMM_UP, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.up.w, ws.map_aq_h, a, true, st))) return rc;
+    if ((rc = launch_quantise(ws.h32, false, rows, T_dev, F, q.dn.ias, ws.aq, ws.sa, st)))
+      return rc;
+    // FFN-down (fp32), then add + LayerNorm + the next layer's quantisation
+    a.N = static_cast<int>(H);
+    a.K = static_cast<int>(F);
+    a.ws = q.dn.ws;
+    a.bias = w.b_dn;
+    a.out = ws.y32;
+    if ((rc = prof_mark(m, prof, NEBW_K_GEMM_DOWN, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.dn.w, ws.map_aq_f, a, false, st))) return rc;
+    if ((rc = prof_mark(m, prof, NEBW_K_LN, st))) return rc;
+    const bool last = L + 1 == c.num_layers;
+    if ((rc = launch_layernorm_quant(ws.x, ws.y32, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H,
+                                     T_dev, last ? nullptr : m->i8[L + 1].qkv.ias,
+                                     last ? nullptr : ws.aq, last ? nullptr : ws.sa, st)))
+      return rc;
+  }
+  if ((rc = prof_mark(m, prof, NEBW_K_POOL, st))) return rc;
+  if ((rc = launch_pool(ws.x, ws.off, ws.len, B, c.hidden, c.pooling, c.l2_normalize, out, st)))
+    return rc;
+  return prof_mark(m, prof, -1, st);
+}
+
+// One encoder pass on the model's datapath.
+int encode_device(nebw_model *m, Workspace &ws, bool prof, const int *ids, const int *len_in,
+                  int B, int S, float *out, cudaStream_t st) {
+  if (m->datapath == NEBW_DATAPATH_I8)
+    return encode_device_i8(m, ws, prof, ids, len_in, B, S, out, st);
+  return encode_device_bf16(m, ws, prof, ids, len_in, B, S, out, st);
 }
 
 }  // namespace
@@ -1602,7 +1867,84 @@ extern "C" int nebw_model_destroy(nebw_model *m) {
     for (float *p : {w.b_qkv, w.b_ao, w.b_up, w.b_dn, w.ln1_g, w.ln1_b, w.ln2_g, w.ln2_b})
       cudaFree(p);
   }
+  for (auto &l : m->i8)
+    for (OperandI8 *o : {&l.qkv, &l.ao, &l.up, &l.dn}) {
+      cudaFree(o->w.ptr);
+      cudaFree(o->ws);
+      cudaFree(o->ias);
+    }
   delete m;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_set_int8_operand(nebw_model *m, const char *name, const int8_t *host_kn,
+                                           const float *wscale, const float *asmooth, int64_t K,
+                                           int64_t N) {
+  NEBW_REQUIRE(m && name && host_kn && wscale && asmooth, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  const nebw_config &c = m->cfg;
+  int layer = -1;
+  char kind[16] = {0};
+  char tail = 0;
+  NEBW_REQUIRE(std::sscanf(name, "layer.%d.%15[a-z_]%c", &layer, kind, &tail) == 2 && layer >= 0 &&
+                   layer < c.num_layers,
+               "int8 operand name '%s' refused: layer.{i}.{qkv,attn_out,ffn_up,ffn_down}", name);
+  const std::string k = kind;
+  const int64_t H = c.hidden, F = c.intermediate;
+  int64_t wantK = 0, wantN = 0;
+  if (k == "qkv") wantK = H, wantN = 3 * H;
+  else if (k == "attn_out") wantK = H, wantN = H;
+  else if (k == "ffn_up") wantK = H, wantN = c.gated_ffn ? 2 * F : F;
+  else if (k == "ffn_down") wantK = F, wantN = H;
+  else return set_error(NEBW_EINVAL, "int8 operand '%s': unknown GEMM '%s'", name, kind);
+  NEBW_REQUIRE(K == wantK && N == wantN, "int8 operand '%s' is [%lld, %lld]; the model's is "
+               "[%lld, %lld]", name, static_cast<long long>(K), static_cast<long long>(N),
+               static_cast<long long>(wantK), static_cast<long long>(wantN));
+  std::vector<float> ias(static_cast<size_t>(K));
+  for (int64_t j = 0; j < K; ++j) {
+    const float a = asmooth[j];
+    // the reference divides by it (bert_encoder.cpp:767-772) and would carry
+    // inf / NaN into every row; refused by name instead
+    NEBW_REQUIRE(a > 0.0f && std::isfinite(a), "%s.asmooth[%lld] = %g: SmoothQuant divisors must "
+                 "be positive and finite", name, static_cast<long long>(j), static_cast<double>(a));
+    ias[static_cast<size_t>(j)] = 1.0f / a;
+  }
+  for (int64_t j = 0; j < N; ++j)
+    NEBW_REQUIRE(std::isfinite(wscale[j]), "%s.wscale[%lld] is not finite", name,
+                 static_cast<long long>(j));
+  if (m->i8.empty()) m->i8.resize(static_cast<size_t>(c.num_layers));
+  LayerI8 &l = m->i8[static_cast<size_t>(layer)];
+  OperandI8 &o = k == "qkv" ? l.qkv : k == "attn_out" ? l.ao : k == "ffn_up" ? l.up : l.dn;
+  NEBW_CUDA(cudaDeviceSynchronize());  // a pass may still read the operand being replaced
+  cudaFree(o.w.ptr);
+  cudaFree(o.ws);
+  cudaFree(o.ias);
+  o = OperandI8{};
+  if (int rc = stage_i8(host_kn, K, N, o.w)) return rc;
+  NEBW_CUDA(cudaMalloc(&o.ws, N * 4));
+  NEBW_CUDA(cudaMalloc(&o.ias, K * 4));
+  NEBW_CUDA(cudaMemcpy(o.ws, wscale, N * 4, cudaMemcpyHostToDevice));
+  NEBW_CUDA(cudaMemcpy(o.ias, ias.data(), K * 4, cudaMemcpyHostToDevice));
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_set_datapath(nebw_model *m, int32_t datapath) {
+  NEBW_REQUIRE(m, "null model");
+  NEBW_REQUIRE(datapath == NEBW_DATAPATH_BF16 || datapath == NEBW_DATAPATH_I8,
+               "datapath %d refused: NEBW_DATAPATH_BF16 or NEBW_DATAPATH_I8", datapath);
+  if (datapath == NEBW_DATAPATH_I8) {
+    const nebw_config &c = m->cfg;
+    NEBW_REQUIRE(!c.gated_ffn && !c.rope && c.activation == NEBW_ACT_GELU8,
+                 "the int8 datapath runs the plain BERT encoder (gelu8 FFN, absolute positions): "
+                 "this model is gated, rotary or uses another activation");
+    for (int L = 0; L < c.num_layers; ++L) {
+      const bool have = !m->i8.empty() && m->i8[L].qkv.w.ptr && m->i8[L].ao.w.ptr &&
+                        m->i8[L].up.w.ptr && m->i8[L].dn.w.ptr;
+      NEBW_REQUIRE(have, "the int8 datapath needs the four int8 operands of every layer; layer "
+                   "%d lacks one (nebw_model_set_int8_operand, or an int8 container)", L);
+    }
+  }
+  m->datapath = datapath;
   return NEBW_OK;
 }
 
@@ -1663,8 +2005,10 @@ namespace {
 // operand's `.wscale`, as the reference's host_b_kn (runtime/include/common/
 // host_b.hpp:74-224) reads it.  The flat panel runs over the axes (kb, nb,
 // ri, ci, si, ti), ti fastest, with k = kb*tile_k + ri*mac_s + si and
-// n = nb*tile_n + ci*mac_t + ti.
-int panel_to_kn(const nebw::NpueFile &f, const std::string &name, std::vector<float> &out) {
+// n = nb*tile_n + ci*mac_t + ti.  For an I8 panel, `raw` (when given) gets
+// the int8 values themselves, [K, N] row-major.
+int panel_to_kn(const nebw::NpueFile &f, const std::string &name, std::vector<float> &out,
+                std::vector<int8_t> *raw = nullptr) {
   const nebw::NpueTensor &t = f.tensor(name);
   NEBW_REQUIRE(t.shape.size() == 2, "'%s' is not a 2-D GEMM operand", name.c_str());
   const int64_t K = t.shape[0], N = t.shape[1];
@@ -1702,6 +2046,7 @@ int panel_to_kn(const nebw::NpueFile &f, const std::string &name, std::vector<fl
     std::memcpy(ws.data(), w.data, static_cast<size_t>(N) * 4);
   }
   out.assign(static_cast<size_t>(K * N), 0.0f);
+  if (raw) raw->assign(i8 ? static_cast<size_t>(K * N) : 0, 0);
   const int64_t R0 = tk / s, C0 = tn / tt;
   int64_t idx = 0;
   for (int64_t kb = 0; kb < K / tk; ++kb)
@@ -1709,10 +2054,12 @@ int panel_to_kn(const nebw::NpueFile &f, const std::string &name, std::vector<fl
       for (int64_t ri = 0; ri < R0; ++ri)
         for (int64_t ci = 0; ci < C0; ++ci)
           for (int64_t si = 0; si < s; ++si) {
-            float *row = out.data() + (kb * tk + ri * s + si) * N + nb * tn + ci * tt;
+            const int64_t at = (kb * tk + ri * s + si) * N + nb * tn + ci * tt;
+            float *row = out.data() + at;
             for (int64_t ti = 0; ti < tt; ++ti, ++idx) {
               if (i8) {
                 const int8_t q = reinterpret_cast<const int8_t *>(t.data)[idx];
+                if (raw) (*raw)[static_cast<size_t>(at + ti)] = q;
                 row[ti] = static_cast<float>(q) * ws[static_cast<size_t>(nb * tn + ci * tt + ti)];
               } else {
                 uint16_t h;
@@ -1904,7 +2251,8 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
         // (a / asmooth) . W == a . (W / asmooth[k]), the reference's host
         // product (host_gemm, bert_encoder.cpp:714-739) moved onto W
         std::vector<float> kn;
-        rc = panel_to_kn(f, n, kn);
+        std::vector<int8_t> q8;
+        rc = panel_to_kn(f, n, kn, a_dtype == "i8" ? &q8 : nullptr);
         if (!rc && a_dtype == "i8") {
           const std::string an = n + ".asmooth";
           if (!f.has(an) || f.tensor(an).dtype != "F32" ||
@@ -1927,6 +2275,10 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
             }
             for (int64_t j = 0; j < cc; ++j) kn[static_cast<size_t>(k * cc + j)] /= a;
           }
+          // and the int8 operand itself, for the int8 datapath
+          rc = nebw_model_set_int8_operand(
+              m, n.c_str(), q8.data(), reinterpret_cast<const float *>(f.tensor(n + ".wscale").data),
+              as.data(), r, cc);
         }
         if (!rc) rc = nebw_model_set_tensor(m, n.c_str(), kn.data(), NEBW_F32, r, cc);
       } else if (nk_layout && gemm_operand) {
@@ -1984,6 +2336,8 @@ extern "C" int nebw_encode_launch_count(const nebw_model *m, int32_t seq) {
   const bool tc =
       m->dev->attn_kind == NEBW_ATTN_TCGEN05 && nebw::attn_tc_head_dim(m->cfg.head_dim);
   const bool rope_fused = rope_in_epilogue(m);
+  if (m->datapath == NEBW_DATAPATH_I8)  // pack, work list, embed, quantise, 9 per layer, pool
+    return 4 + (tc ? 1 : 0) + m->cfg.num_layers * (8 + attention_launches(tc ? 64 : 0, S));
   const int per_layer = 6 + attention_launches(tc ? 64 : 0, S) +
                         (m->cfg.rope && !rope_fused ? 1 : 0) +
                         (m->cfg.gated_ffn && !m->glu_fused ? 1 : 0);
@@ -2119,6 +2473,9 @@ extern "C" int nebw_encode_device_static(nebw_model *m, const int32_t *ids, cons
   NEBW_REQUIRE(m && ids && lens && out, "null argument");
   if (int rc = use_dev(m->dev)) return rc;
   if (int rc = check_pass(m, B, S)) return rc;
+  NEBW_REQUIRE(m->datapath == NEBW_DATAPATH_BF16,
+               "nebw_encode_device_static runs the bf16 datapath; this model is set to the int8 "
+               "datapath (use nebw_encode_device)");
   const int64_t rows = static_cast<int64_t>(B) * S;
   const size_t need = static_scratch_need(m, rows, B);
   NEBW_REQUIRE(need <= kStaticScratchBytes,

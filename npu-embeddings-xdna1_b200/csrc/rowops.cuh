@@ -60,12 +60,12 @@ __global__ void __launch_bounds__(1024)
   if (tid == blockDim.x - 1) seq_off[B] = part[tid];
 }
 
-// LayerNorm of one warp-owned row held as NV float4 per lane (H = 128*NV).
+// LayerNorm of one warp-owned row held as NV float4 per lane (H = 128*NV),
+// in place.
 template <int NV>
-__device__ __forceinline__ void ln_row_regs(float4 (&v)[NV], const float *__restrict__ g,
-                                            const float *__restrict__ bta, float eps, int H,
-                                            int lane, float *__restrict__ xo,
-                                            __nv_bfloat16 *__restrict__ ao) {
+__device__ __forceinline__ void ln_normalise(float4 (&v)[NV], const float *__restrict__ g,
+                                             const float *__restrict__ bta, float eps, int H,
+                                             int lane) {
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
@@ -86,16 +86,29 @@ __device__ __forceinline__ void ln_row_regs(float4 (&v)[NV], const float *__rest
     const int c = (i * 32 + lane) * 4;
     const float4 gg = __ldg(reinterpret_cast<const float4 *>(g + c));
     const float4 bb = __ldg(reinterpret_cast<const float4 *>(bta + c));
-    float4 y;
-    y.x = fmaf((v[i].x - mean) * is, gg.x, bb.x);
-    y.y = fmaf((v[i].y - mean) * is, gg.y, bb.y);
-    y.z = fmaf((v[i].z - mean) * is, gg.z, bb.z);
-    y.w = fmaf((v[i].w - mean) * is, gg.w, bb.w);
-    if (xo) *reinterpret_cast<float4 *>(xo + c) = y;
+    v[i].x = fmaf((v[i].x - mean) * is, gg.x, bb.x);
+    v[i].y = fmaf((v[i].y - mean) * is, gg.y, bb.y);
+    v[i].z = fmaf((v[i].z - mean) * is, gg.z, bb.z);
+    v[i].w = fmaf((v[i].w - mean) * is, gg.w, bb.w);
+  }
+}
+
+// LayerNorm of one warp-owned row, stored as fp32 (xo) and as the bf16 RNE
+// operand of the next GEMM (ao), either may be null.
+template <int NV>
+__device__ __forceinline__ void ln_row_regs(float4 (&v)[NV], const float *__restrict__ g,
+                                            const float *__restrict__ bta, float eps, int H,
+                                            int lane, float *__restrict__ xo,
+                                            __nv_bfloat16 *__restrict__ ao) {
+  ln_normalise<NV>(v, g, bta, eps, H, lane);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (xo) *reinterpret_cast<float4 *>(xo + c) = v[i];
     if (ao) {
       uint2 pk;
-      pk.x = pack_bf16x2(y.x, y.y);
-      pk.y = pack_bf16x2(y.z, y.w);
+      pk.x = pack_bf16x2(v[i].x, v[i].y);
+      pk.y = pack_bf16x2(v[i].z, v[i].w);
       *reinterpret_cast<uint2 *>(ao + c) = pk;
     }
   }
@@ -140,6 +153,72 @@ __global__ void __launch_bounds__(kRowWarps * 32)
   }
   ln_row_regs<NV>(v, g, bta, eps, H, lane, xr,
                   a ? a + static_cast<int64_t>(row) * H : nullptr);
+}
+
+// The int8 pass's add + LayerNorm: x[r] = LN(x[r] + y[r]) for r < T (y the
+// dequantised fp32 output of an int8 GEMM, or null), and, when q is set, the
+// normalised row quantised for the next int8 GEMM as add_norm_quant does
+// (runtime/src/encoders/bert_encoder.cpp:1196-1302) -- quantise_a_int8's
+// steps on the row held in registers: sc = max|x * ias| / 127 (1 for a zero
+// row), q = rne(clamp((x * ias) * (1 / sc), +-127)).
+template <int NV>
+__global__ void __launch_bounds__(kRowWarps * 32)
+    layernorm_quant_kernel(float *__restrict__ x, const float *__restrict__ y,
+                           const float *__restrict__ g, const float *__restrict__ bta, float eps,
+                           int rows, const int *__restrict__ rows_dev,
+                           const float *__restrict__ ias, int8_t *__restrict__ q,
+                           float *__restrict__ scale) {
+  const int H = NV * 128;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  int T = rows;
+  if (rows_dev) T = min(T, __ldg(rows_dev));
+  if (row >= T) return;
+  float *xr = x + static_cast<int64_t>(row) * H;
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    v[i] = *reinterpret_cast<const float4 *>(xr + c);
+    if (y) {
+      const float4 w = *reinterpret_cast<const float4 *>(y + static_cast<int64_t>(row) * H + c);
+      v[i].x = w.x + v[i].x;
+      v[i].y = w.y + v[i].y;
+      v[i].z = w.z + v[i].z;
+      v[i].w = w.w + v[i].w;
+    }
+  }
+  ln_normalise<NV>(v, g, bta, eps, H, lane);
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+    *reinterpret_cast<float4 *>(xr + (i * 32 + lane) * 4) = v[i];
+  if (!q) return;
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 s = __ldg(reinterpret_cast<const float4 *>(ias + (i * 32 + lane) * 4));
+    mx = fmaxf(fmaxf(mx, fabsf(v[i].x * s.x)), fabsf(v[i].y * s.y));
+    mx = fmaxf(fmaxf(mx, fabsf(v[i].z * s.z)), fabsf(v[i].w * s.w));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+  const float inv = 1.0f / sc;
+  if (lane == 0) scale[row] = sc;
+  int8_t *qr = q + static_cast<int64_t>(row) * H;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    const float4 s = __ldg(reinterpret_cast<const float4 *>(ias + c));
+    const float e[4] = {v[i].x * s.x, v[i].y * s.y, v[i].z * s.z, v[i].w * s.w};
+    uint32_t pk = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float t = fminf(fmaxf(e[k] * inv, -127.0f), 127.0f);
+      pk |= (static_cast<uint32_t>(__float2int_rn(t)) & 0xffu) << (8 * k);
+    }
+    *reinterpret_cast<uint32_t *>(qr + c) = pk;
+  }
 }
 
 // Embedding gather + LayerNorm for the packed rows of a padded id batch.

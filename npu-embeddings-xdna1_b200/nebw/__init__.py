@@ -120,6 +120,13 @@ def lib() -> C.CDLL:
         "nebw_quantise_rows": ([vp, vp, i64, i64, vp, vp, vp, vp], C.c_int),
         "nebw_stage_weight_i8": ([vp, vp, i64, i64, C.POINTER(C.c_uint64)], C.c_int),
         "nebw_gemm_i8": ([vp, C.c_uint64, vp, vp, i64, i64, i64, vp, vp, C.c_int, vp, vp], C.c_int),
+        "nebw_gemm_i8_ex": ([vp, C.c_uint64, vp, vp, i64, i64, i64, vp, vp, C.c_int, vp, C.c_int,
+                             vp], C.c_int),
+        "nebw_quantise_rows_bf16": ([vp, vp, i64, i64, vp, vp, vp, vp], C.c_int),
+        "nebw_layernorm_quant": ([vp, vp, vp, vp, vp, C.c_float, i64, i64, vp, vp, vp, vp],
+                                 C.c_int),
+        "nebw_model_set_int8_operand": ([vp, C.c_char_p, vp, vp, vp, i64, i64], C.c_int),
+        "nebw_model_set_datapath": ([vp, i32], C.c_int),
         "nebw_pack_checkpoint": ([C.c_char_p, C.c_char_p, C.c_char_p, i32, i32,
                                   C.POINTER(C.c_uint64)], C.c_int),
         "nebw_comm_unique_id": ([vp], C.c_int),
@@ -247,13 +254,25 @@ class Device:
         _check(lib().nebw_stage_weight_i8(self.h, w.ctypes.data, K, N, C.byref(hnd)))
         return hnd.value
 
-    def gemm_i8(self, weight, A, sa, M, K, N, ws, C_out, bias=None, act=ACT_NONE, stream=None):
-        _check(lib().nebw_gemm_i8(self.h, weight, _addr(A), _addr(sa), M, K, N, _addr(ws),
-                                  _addr(bias), act, _addr(C_out), self._s(stream)))
+    def gemm_i8(self, weight, A, sa, M, K, N, ws, C_out, bias=None, act=ACT_NONE, stream=None,
+                c_dtype=F32):
+        """C = dequant(A . W) (nebw_gemm_i8_ex): fp32 C, or bf16 RNE with c_dtype BF16."""
+        _check(lib().nebw_gemm_i8_ex(self.h, weight, _addr(A), _addr(sa), M, K, N, _addr(ws),
+                                     _addr(bias), act, _addr(C_out), c_dtype, self._s(stream)))
 
     def quantise_rows(self, x, rows, K, ias, q, scale, stream=None):
-        _check(lib().nebw_quantise_rows(self.h, _addr(x), rows, K, _addr(ias), _addr(q),
-                                        _addr(scale), self._s(stream)))
+        """quantise_a_int8 per row; x fp32, or a torch bf16 tensor (widened exactly)."""
+        fn = (lib().nebw_quantise_rows_bf16 if str(getattr(x, "dtype", "")) == "torch.bfloat16"
+              else lib().nebw_quantise_rows)
+        _check(fn(self.h, _addr(x), rows, K, _addr(ias), _addr(q), _addr(scale), self._s(stream)))
+
+    def layernorm_quant(self, x, gamma, beta, rows, H, y=None, ias=None, q=None, scale=None,
+                        eps=1e-12, stream=None):
+        """add_norm_quant: x = LN(x + y) in place (y fp32 or None), then the rows
+        quantised with ias into q / scale when q is given."""
+        _check(lib().nebw_layernorm_quant(self.h, _addr(x), _addr(y), _addr(gamma), _addr(beta),
+                                          eps, rows, H, _addr(ias), _addr(q), _addr(scale),
+                                          self._s(stream)))
 
     def release_weight(self, handle: int):
         _check(lib().nebw_release_weight(self.h, handle))
@@ -343,6 +362,22 @@ class Model:
         h = C.c_void_p()
         _check(lib().nebw_model_load_npue(dev.h, str(path).encode(), C.byref(h)))
         return cls(dev, h)
+
+    DATAPATHS = {"bf16": 0, "i8": 1}
+
+    def set_datapath(self, datapath: str):
+        """"bf16" (default) or "i8": the int8 array path of an int8 container
+        (nebw_model_set_datapath)."""
+        _check(lib().nebw_model_set_datapath(self.h, self.DATAPATHS[datapath]))
+
+    def set_int8_operand(self, name: str, kn, wscale, asmooth):
+        """An int8 GEMM operand [K, N] with its .wscale [N] and .asmooth [K]."""
+        q = np.ascontiguousarray(kn, np.int8)
+        ws = np.ascontiguousarray(wscale, np.float32)
+        asm = np.ascontiguousarray(asmooth, np.float32)
+        K, N = q.shape
+        _check(lib().nebw_model_set_int8_operand(self.h, name.encode(), q.ctypes.data,
+                                                 ws.ctypes.data, asm.ctypes.data, K, N))
 
     def close(self):
         if self.h:

@@ -18,7 +18,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version():
     import nebw
-    assert nebw.lib().nebw_abi_version() == 4
+    assert nebw.lib().nebw_abi_version() == 5
 
 
 def test_no_gpu_is_an_error_by_name():
