@@ -120,21 +120,25 @@ def bench_layernorm(dev, M, H, iters, copies):
 
 
 def bench_gemm_i8(dev, M, K, N, epi, iters, copies):
-    """The int8 GEMM (tcgen05 kind::i8) with the dequantise (or dequantise +
-    gelu8) epilogue, fp32 out."""
+    """The int8 GEMM (tcgen05 kind::i8) with the dequantise epilogue: epi
+    "f32" fp32 out, "gelu8" dequantise + gelu8, fp32 out, "bf16" bf16 RNE out
+    (the int8 encoder pass's QKV form)."""
     import torch
+    import nebw
     rng = np.random.default_rng(0)
     h = dev.stage_weight_i8(rng.integers(-127, 128, (K, N), dtype=np.int8))
     ws = torch.rand(N, device="cuda") * 1e-3
     bias = torch.randn(N, device="cuda") * 0.02
     As = [torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda") for _ in range(copies)]
     sa = torch.rand(M, device="cuda") * 1e-2
-    Cs = [torch.empty(M, N, device="cuda") for _ in range(copies)]
+    bf16 = epi == "bf16"
+    Cs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
+          for _ in range(copies)]
     act = 1 if epi == "gelu8" else 0
 
     def run(i):
         dev.gemm_i8(h, As[i % copies], sa, M, K, N, ws, Cs[i % copies], bias=bias, act=act,
-                    stream=torch.cuda.current_stream())
+                    stream=torch.cuda.current_stream(), c_dtype=nebw.BF16 if bf16 else nebw.F32)
 
     for i in range(3):
         run(i)

@@ -27,7 +27,11 @@
 // The GEMM is the single-CTA structure of gemm_tc_kernel (TMA producer warp,
 // one MMA-issuing warp, eight epilogue warps, a double-buffered TMEM
 // accumulator) with 128-byte K-blocks: 128 int8 per row instead of 64 bf16,
-// the same swizzled tiles and stage sizes, four K=32 MMAs per block.
+// the same swizzled tiles, four K=32 MMAs per block.  The epilogue stages
+// each warp's 32 x 32 output chunks in shared memory, in the output tensor
+// map's swizzle, and writes them with TMA bulk-tensor stores (whole-row
+// segments, not one 16-byte piece per row per instruction), so an fp32
+// output of many columns is written at the HBM rate.
 #pragma once
 
 #include <cuda.h>
@@ -40,6 +44,22 @@
 namespace nebw {
 
 constexpr int kGemmI8BK = 128;  // int8 elements per K-block (one 128-byte row)
+
+template <int BN>
+struct GemmI8Shape {
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static constexpr int kABytes = kGemmBM * kGemmI8BK;  // 16 KB
+  static constexpr int kBBytes = BN * kGemmI8BK;       // 16 or 32 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BN == 256 ? 3 : 5;
+  static constexpr int kTmemCols = 2 * BN;
+  // epilogue staging: per epilogue warp two fp32 (or four bf16) 32 x 32 chunks
+  static constexpr int kChunkBytes = 32 * 32 * 4;
+  static constexpr int kStagingBytes = 8 * 2 * kChunkBytes;  // 64 KB
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kStagingBytes + kBarBytes;
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
 
 struct GemmI8Args {
   int M, N, K;
@@ -102,52 +122,188 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Dequantise (and gelu8) 32 accumulator columns [col0, col0 + 32) of one row
-// and store them as fp32, or as bf16 RNE (p.out_bf16).
-template <bool GELU>
-__device__ __forceinline__ void i8_store32(const GemmI8Args &p, int row, int col0,
-                                           const uint32_t (&r)[32]) {
-  const int ncols = min(32, p.N - col0);  // N % 8 == 0
-  const float sa = __ldg(p.sa + row);
-  float4 *o4 = reinterpret_cast<float4 *>(p.out + static_cast<size_t>(row) * p.N + col0);
-  uint2 *o2 = reinterpret_cast<uint2 *>(p.out_bf16 + static_cast<size_t>(row) * p.N + col0);
+// The same quantisation with the row held in registers, so that it is read
+// from memory once (the form above reads it twice, once for its maximum):
+// here one CTA of 256 threads per row, NV float4 (or 4 x bf16) per thread,
+// for rows too wide for one warp's registers.  K % 4 == 0, K <= 1024 * NV.
+constexpr int kQuantThreads = 256;
+
+__device__ __forceinline__ float4 load_widen4(const float *p) {
+  return *reinterpret_cast<const float4 *>(p);
+}
+__device__ __forceinline__ float4 load_widen4(const __nv_bfloat16 *p) {
+  const uint2 u = *reinterpret_cast<const uint2 *>(p);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
+template <typename XT, int NV>
+__global__ void __launch_bounds__(kQuantThreads)
+    quantise_rows_cta_kernel(const XT *__restrict__ x, int rows, const int *__restrict__ rows_dev,
+                             int K, const float *__restrict__ ias, int8_t *__restrict__ q,
+                             float *__restrict__ scale) {
+  __shared__ float red[kQuantThreads / 32];
+  const int row = blockIdx.x, t = threadIdx.x;
+  if (rows_dev) rows = min(rows, __ldg(rows_dev));
+  if (row >= rows) return;  // CTA-uniform
+  const XT *xr = x + static_cast<int64_t>(row) * K;
+  float4 v[NV];
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * kQuantThreads + t) * 4;
+    if (c < K) {
+      const float4 a = load_widen4(xr + c);
+      const float4 s = __ldg(reinterpret_cast<const float4 *>(ias + c));
+      v[i] = make_float4(a.x * s.x, a.y * s.y, a.z * s.z, a.w * s.w);  // x * ias, rounded once
+      mx = fmaxf(fmaxf(mx, fabsf(v[i].x)), fabsf(v[i].y));
+      mx = fmaxf(fmaxf(mx, fabsf(v[i].z)), fabsf(v[i].w));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((t & 31) == 0) red[t >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+  const float inv = 1.0f / sc;
+  if (t == 0) scale[row] = sc;
+  int8_t *qr = q + static_cast<int64_t>(row) * K;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * kQuantThreads + t) * 4;
+    if (c < K) {
+      const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      uint32_t pk = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float tq = fminf(fmaxf(e[k] * inv, -127.0f), 127.0f);
+        pk |= (static_cast<uint32_t>(__float2int_rn(tq)) & 0xffu) << (8 * k);
+      }
+      *reinterpret_cast<uint32_t *>(qr + c) = pk;
+    }
+  }
+}
+
+// The same with a warp per row and the row in its registers (NV float4, or
+// 4 x bf16, per lane): the form for rows of up to 128 * NV values, eight rows
+// per CTA.  K % 4 == 0, K <= 128 * NV.
+template <typename XT, int NV>
+__global__ void __launch_bounds__(256)
+    quantise_rows_warp_kernel(const XT *__restrict__ x, int rows, const int *__restrict__ rows_dev,
+                              int K, const float *__restrict__ ias, int8_t *__restrict__ q,
+                              float *__restrict__ scale) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (rows_dev) rows = min(rows, __ldg(rows_dev));
+  if (row >= rows) return;  // warp-uniform
+  const XT *xr = x + static_cast<int64_t>(row) * K;
+  float4 v[NV];
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < K) {
+      const float4 a = load_widen4(xr + c);
+      const float4 s = __ldg(reinterpret_cast<const float4 *>(ias + c));
+      v[i] = make_float4(a.x * s.x, a.y * s.y, a.z * s.z, a.w * s.w);  // x * ias, rounded once
+      mx = fmaxf(fmaxf(mx, fabsf(v[i].x)), fabsf(v[i].y));
+      mx = fmaxf(fmaxf(mx, fabsf(v[i].z)), fabsf(v[i].w));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float sc = mx > 0.0f ? mx / 127.0f : 1.0f;
+  const float inv = 1.0f / sc;
+  if (lane == 0) scale[row] = sc;
+  int8_t *qr = q + static_cast<int64_t>(row) * K;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < K) {
+      const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      uint32_t pk = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float tq = fminf(fmaxf(e[k] * inv, -127.0f), 127.0f);
+        pk |= (static_cast<uint32_t>(__float2int_rn(tq)) & 0xffu) << (8 * k);
+      }
+      *reinterpret_cast<uint32_t *>(qr + c) = pk;
+    }
+  }
+}
+
+// Dequantise (and gelu8) the 32 accumulator columns [col0, col0 + 32) of this
+// thread's row into its row of a 32-row chunk staged in shared memory, in the
+// output map's swizzle: fp32 rows of 128 bytes (16-byte piece q at q ^ (r % 8)),
+// or bf16 RNE rows of 64 bytes (q ^ ((r / 2) % 4)).  Columns past N and rows
+// past the live count are staged as 0 (the bulk store clips columns past the
+// map's N; rows past the live count but inside the buffer are written, and a
+// zero row is what the encoder's later readers of those rows expect).
+template <bool GELU, bool BF16>
+__device__ __forceinline__ void i8_stage32(const GemmI8Args &p, bool live_row, int row, int col0,
+                                           const uint32_t (&r)[32], uint8_t *chunk, int lane) {
+  const int ncols = live_row ? min(32, p.N - col0) : 0;  // N % 8 == 0
+  const float sa = live_row ? __ldg(p.sa + row) : 0.0f;
   const float4 *w4 = reinterpret_cast<const float4 *>(p.ws + col0);
   const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
+  float y[32];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    if (i * 4 >= ncols) break;
-    const float4 w = __ldg(w4 + i);
-    const float4 b = p.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float y[4];
-    const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
+    if (i * 4 < ncols) {
+      const float4 w = __ldg(w4 + i);
+      const float4 b = p.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float c = __int2float_rn(static_cast<int>(r[4 * i + e]));
-      y[e] = fmaf(c * sa, ws[e], bs[e]);
-      if constexpr (GELU) y[e] = gelu8(y[e]);
+      for (int e = 0; e < 4; ++e) {
+        const float c = __int2float_rn(static_cast<int>(r[4 * i + e]));
+        float v = fmaf(c * sa, ws[e], bs[e]);
+        if constexpr (GELU) v = gelu8(v);
+        y[4 * i + e] = v;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[4 * i + e] = 0.0f;
     }
-    if (p.out_bf16)
-      o2[i] = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
-    else
-      o4[i] = make_float4(y[0], y[1], y[2], y[3]);
+  }
+  if constexpr (BF16) {
+    uint8_t *rowp = chunk + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(rowp + ((q ^ sw) << 4)) =
+          make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                     pack_bf16x2(y[8 * q + 4], y[8 * q + 5]),
+                     pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+  } else {
+    uint8_t *rowp = chunk + lane * 128;
+    const int sw = lane & 7;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4 *>(rowp + ((q ^ sw) << 4)) =
+          make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
   }
 }
 
 // C[M, N] = dequant(A_q[M, K] . W_q[N, K]^T): A and W int8, K-major, read by
-// TMA in 128 x 128-byte (A) and BN x 128-byte (W) swizzled boxes.  One CTA
-// per SM, persistent over 128 x BN tiles.  Every wait is bounded.
-template <int BN, bool GELU>
+// TMA in 128 x 128-byte (A) and BN x 128-byte (W) swizzled boxes; C written
+// through tmC (32 x 32 boxes: fp32 with the 128-byte swizzle, or bf16 with
+// the 64-byte one, as BF16 says).  One CTA per SM, persistent over 128 x BN
+// tiles.  Every wait is bounded.
+template <int BN, bool GELU, bool BF16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const GemmI8Args p) {
-  using S = GemmShape<BN>;  // a 128-byte row of int8 is the size of one of bf16
+                   const __grid_constant__ CUtensorMap tmC, const GemmI8Args p) {
+  using S = GemmI8Shape<BN>;
   constexpr int kStages = S::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sW = smem + kStages * S::kABytes;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+  uint8_t *staging = smem + kStages * S::kStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(staging + S::kStagingBytes);
   uint64_t *empty = full + kStages;
   uint64_t *tfull = empty + kStages;
   uint64_t *tempty = tfull + 2;
@@ -166,6 +322,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmC);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -267,6 +424,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quarter = warp & 3;
     const int col_half = ((warp - 2) >> 2) * kHalf;
     const int row_in_tile = quarter * 32 + lane;
+    uint8_t *my_staging = staging + (warp - 2) * 2 * S::kChunkBytes;
+    // a warp's 8 KB of staging holds two fp32 or four bf16 32 x 32 chunks:
+    // that many stores may still be reading it while the next is written
+    constexpr int kOutChunk = BF16 ? S::kChunkBytes / 2 : S::kChunkBytes;
+    constexpr int kSlots = 2 * S::kChunkBytes / kOutChunk;
+    int nstore = 0;  // bulk stores this warp has issued (lane 0)
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -274,6 +437,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, p.err))) break;
       tc_fence_after();
       const int mb = tile / n_blocks, nb = tile % n_blocks;
+      const int row0 = mb * kGemmBM + quarter * 32;  // this warp's 32 rows
       const int row = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col_half);
@@ -291,10 +455,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) mbar_arrive(&tempty[acc]);
         }
         const int col0 = nb * BN + col_half + c * 32;
-        if (row < M && col0 < p.N) i8_store32<GELU>(p, row, col0, cur);
+        if (row0 < M && col0 < p.N) {  // warp-uniform
+          uint8_t *chunk = my_staging + (nstore % kSlots) * kOutChunk;
+          // the store that last read `chunk` is done
+          if (lane == 0) bulk_wait_group_read<kSlots - 1>();
+          __syncwarp();
+          i8_stage32<GELU, BF16>(p, row < M, row, col0, cur, chunk, lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, chunk, col0, row0);
+            bulk_commit_group();
+          }
+          ++nstore;
+        }
         if (c + 1 < kChunks) tmem_wait_ld_regs(nxt);
       }
     }
+    if (lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();

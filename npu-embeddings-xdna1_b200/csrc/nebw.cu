@@ -465,6 +465,46 @@ int launch_quantise(const void *x, bool x_bf16, int64_t rows, const int *rows_de
                "quantise [%lld, %lld] refused", static_cast<long long>(rows),
                static_cast<long long>(K));
   if (rows == 0) return NEBW_OK;
+  const bool aligned = reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(ias) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(q) % 4 == 0;
+  const int r = static_cast<int>(rows), k = static_cast<int>(K);
+  const unsigned g8 = static_cast<unsigned>((rows + 7) / 8);
+#define NEBW_QW(n)                                                                                 \
+  do {                                                                                             \
+    if (x_bf16)                                                                                    \
+      nebw::quantise_rows_warp_kernel<__nv_bfloat16, n><<<g8, 256, 0, st>>>(                       \
+          static_cast<const __nv_bfloat16 *>(x), r, rows_dev, k, ias, q, scale);                   \
+    else                                                                                           \
+      nebw::quantise_rows_warp_kernel<float, n><<<g8, 256, 0, st>>>(                               \
+          static_cast<const float *>(x), r, rows_dev, k, ias, q, scale);                           \
+  } while (0)
+#define NEBW_QC(n)                                                                                 \
+  do {                                                                                             \
+    if (x_bf16)                                                                                    \
+      nebw::quantise_rows_cta_kernel<__nv_bfloat16, n><<<static_cast<unsigned>(rows),              \
+                                                         nebw::kQuantThreads, 0, st>>>(            \
+          static_cast<const __nv_bfloat16 *>(x), r, rows_dev, k, ias, q, scale);                   \
+    else                                                                                           \
+      nebw::quantise_rows_cta_kernel<float, n><<<static_cast<unsigned>(rows),                      \
+                                                 nebw::kQuantThreads, 0, st>>>(                    \
+          static_cast<const float *>(x), r, rows_dev, k, ias, q, scale);                           \
+  } while (0)
+  if (K % 4 == 0 && K <= 8192 && aligned) {
+    // the row held in registers and read once: a warp per row up to 2048
+    // values, a CTA per row beyond
+    if (K <= 128) NEBW_QW(1);
+    else if (K <= 256) NEBW_QW(2);
+    else if (K <= 512) NEBW_QW(4);
+    else if (K <= 1024) NEBW_QW(8);
+    else if (K <= 2048) NEBW_QW(16);
+    else if (K <= 4096) NEBW_QC(4);
+    else NEBW_QC(8);
+    NEBW_CUDA(cudaGetLastError());
+    return NEBW_OK;
+  }
+#undef NEBW_QW
+#undef NEBW_QC
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
   if (x_bf16)
     nebw::quantise_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
@@ -478,24 +518,30 @@ int launch_quantise(const void *x, bool x_bf16, int64_t rows, const int *rows_de
   return NEBW_OK;
 }
 
+template <int BN>
+void launch_gemm_i8_bn(const CUtensorMap &mA, const CUtensorMap &mW, const CUtensorMap &mC,
+                       const nebw::GemmI8Args &a, bool gelu, dim3 g, cudaStream_t st) {
+  const size_t smem = nebw::GemmI8Shape<BN>::kSmemBytes;
+  const dim3 b(nebw::kGemmThreads);
+  const bool bf16 = a.out_bf16 != nullptr;
+  if (gelu && bf16) nebw::gemm_i8_kernel<BN, true, true><<<g, b, smem, st>>>(mA, mW, mC, a);
+  else if (gelu) nebw::gemm_i8_kernel<BN, true, false><<<g, b, smem, st>>>(mA, mW, mC, a);
+  else if (bf16) nebw::gemm_i8_kernel<BN, false, true><<<g, b, smem, st>>>(mA, mW, mC, a);
+  else nebw::gemm_i8_kernel<BN, false, false><<<g, b, smem, st>>>(mA, mW, mC, a);
+}
+
 // The int8 GEMM over a staged operand: A's tensor map `mA` (128-row boxes),
-// a.M the row bound (a.M_dev the live count), fp32 or bf16 out as `a` says.
-int launch_gemm_i8(nebw_dev *d, const WeightI8 &w, const CUtensorMap &mA,
+// the output's `mC` (make_tmap_out: fp32, or bf16 when a.out_bf16 is set),
+// a.M the row bound (a.M_dev the live count).
+int launch_gemm_i8(nebw_dev *d, const WeightI8 &w, const CUtensorMap &mA, const CUtensorMap &mC,
                    const nebw::GemmI8Args &a, bool gelu, cudaStream_t st) {
   if (a.M <= 0) return NEBW_OK;
   const bool wide = w.N % 256 == 0;
   const int BN = wide ? 256 : 128;
   const int64_t tiles = ((int64_t{a.M} + nebw::kGemmBM - 1) / nebw::kGemmBM) * ((w.N + BN - 1) / BN);
-  const dim3 g(static_cast<unsigned>(std::min<int64_t>(tiles, d->sm_count))), b(nebw::kGemmThreads);
-  if (wide) {
-    const size_t smem = nebw::GemmShape<256>::kSmemBytes;
-    if (gelu) nebw::gemm_i8_kernel<256, true><<<g, b, smem, st>>>(mA, w.map256, a);
-    else nebw::gemm_i8_kernel<256, false><<<g, b, smem, st>>>(mA, w.map256, a);
-  } else {
-    const size_t smem = nebw::GemmShape<128>::kSmemBytes;
-    if (gelu) nebw::gemm_i8_kernel<128, true><<<g, b, smem, st>>>(mA, w.map128, a);
-    else nebw::gemm_i8_kernel<128, false><<<g, b, smem, st>>>(mA, w.map128, a);
-  }
+  const dim3 g(static_cast<unsigned>(std::min<int64_t>(tiles, d->sm_count)));
+  if (wide) launch_gemm_i8_bn<256>(mA, w.map256, mC, a, gelu, g, st);
+  else launch_gemm_i8_bn<128>(mA, w.map128, mC, a, gelu, g, st);
   NEBW_CUDA(cudaGetLastError());
   return NEBW_OK;
 }
@@ -606,6 +652,20 @@ int launch_pack(const int *len_in, int B, int S, int *len_out, int *off, int *er
 extern "C" const char *nebw_last_error(void) { return g_last_error.c_str(); }
 extern "C" int nebw_abi_version(void) { return NEBW_ABI_VERSION; }
 
+template <int BN>
+int set_gemm_i8_attrs() {
+  const int smem = nebw::GemmI8Shape<BN>::kSmemBytes;
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<BN, false, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<BN, true, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<BN, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<BN, true, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  return NEBW_OK;
+}
+
 extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_REQUIRE(out != nullptr, "null output handle");
   *out = nullptr;
@@ -628,18 +688,8 @@ extern "C" int nebw_open(int device, nebw_dev **out) {
   NEBW_CUDA(cudaMalloc(&d->d_err, sizeof(int)));
   NEBW_CUDA(cudaMemset(d->d_err, 0, sizeof(int)));
   if (int rc = set_all_gemm_attrs()) return rc;
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<128, false>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::GemmShape<128>::kSmemBytes));
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<128, true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::GemmShape<128>::kSmemBytes));
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<256, false>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::GemmShape<256>::kSmemBytes));
-  NEBW_CUDA(cudaFuncSetAttribute(nebw::gemm_i8_kernel<256, true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 nebw::GemmShape<256>::kSmemBytes));
+  if (int rc = set_gemm_i8_attrs<128>()) return rc;
+  if (int rc = set_gemm_i8_attrs<256>()) return rc;
   NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  nebw::AttnTcShape<64>::kSmemBytes));
   NEBW_CUDA(cudaFuncSetAttribute(nebw::attention_tc_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -1037,13 +1087,14 @@ extern "C" int nebw_gemm_i8_ex(nebw_dev *d, uint64_t weight, const int8_t *A, co
   NEBW_REQUIRE(act == NEBW_ACT_NONE || act == NEBW_ACT_GELU8, "int8 GEMM act %d refused", act);
   NEBW_REQUIRE(c_dtype == NEBW_F32 || c_dtype == NEBW_BF16, "int8 GEMM c_dtype %d refused",
                c_dtype);
-  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(C) % (c_dtype == NEBW_F32 ? 16 : 8) == 0 &&
+  NEBW_REQUIRE(reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(ws) % 16 == 0 &&
                    (!bias || reinterpret_cast<uintptr_t>(bias) % 16 == 0),
-               "int8 GEMM C (16 bytes fp32, 8 bytes bf16), ws and bias must be aligned");
+               "int8 GEMM C, ws and bias must be 16-byte aligned");
   if (M == 0) return NEBW_OK;
-  CUtensorMap mA;
+  CUtensorMap mA, mC;
   if (int rc = make_tmap_i8(&mA, A, M, K, nebw::kGemmBM)) return rc;
+  if (int rc = make_tmap_out(&mC, C, M, N, c_dtype == NEBW_BF16)) return rc;
   nebw::GemmI8Args a{};
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
@@ -1054,7 +1105,7 @@ extern "C" int nebw_gemm_i8_ex(nebw_dev *d, uint64_t weight, const int8_t *A, co
   if (c_dtype == NEBW_F32) a.out = static_cast<float *>(C);
   else a.out_bf16 = static_cast<__nv_bfloat16 *>(C);
   a.err = d->d_err;
-  return launch_gemm_i8(d, w, mA, a, act == NEBW_ACT_GELU8, pick_stream(d, stream));
+  return launch_gemm_i8(d, w, mA, mC, a, act == NEBW_ACT_GELU8, pick_stream(d, stream));
 }
 
 extern "C" int nebw_gemm_i8(nebw_dev *d, uint64_t weight, const int8_t *A, const float *sa,
@@ -1137,6 +1188,7 @@ struct Workspace {
   int8_t *aq = nullptr;
   float *sa = nullptr, *y32 = nullptr, *h32 = nullptr;
   CUtensorMap map_aq_h, map_aq_f;
+  CUtensorMap out_y32, out_h32;  // int8 GEMM outputs (TMA stores)
 };
 
 struct nebw_model {
@@ -1221,6 +1273,8 @@ int make_workspace_maps(const nebw_model *m, Workspace &w, int64_t R) {
   if (w.aq) {
     if ((rc = make_tmap_i8(&w.map_aq_h, w.aq, R, H, nebw::kGemmBM))) return rc;
     if ((rc = make_tmap_i8(&w.map_aq_f, w.aq, R, F, nebw::kGemmBM))) return rc;
+    if ((rc = make_tmap_out(&w.out_y32, w.y32, R, H, false))) return rc;
+    if ((rc = make_tmap_out(&w.out_h32, w.h32, R, F, false))) return rc;
   }
   return NEBW_OK;
 }
@@ -1621,7 +1675,7 @@ int encode_device_i8(nebw_model *m, Workspace &ws, bool prof, const int *ids, co
     a.out = nullptr;
     a.out_bf16 = ws.qkv;
     if ((rc = prof_mark(m, prof, NEBW_K_GEMM_QKV, st))) return rc;
-    if ((rc = launch_gemm_i8(d, q.qkv.w, ws.map_aq_h, a, false, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.qkv.w, ws.map_aq_h, ws.out_qkv, a, false, st))) return rc;
     if ((rc = prof_mark(m, prof, NEBW_K_ATTENTION, st))) return rc;
     if (tc_attention)
       rc = launch_attention_tc(d, ws.map_qkv_att, ws.map_kv_att, ws.off, ws.len, ws.att_items + 1,
@@ -1638,7 +1692,7 @@ int encode_device_i8(nebw_model *m, Workspace &ws, bool prof, const int *ids, co
     a.bias = w.b_ao;
     a.out = ws.y32;
     a.out_bf16 = nullptr;
-    if ((rc = launch_gemm_i8(d, q.ao.w, ws.map_aq_h, a, false, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.ao.w, ws.map_aq_h, ws.out_y32, a, false, st))) return rc;
     if ((rc = prof_mark(m, prof, NEBW_K_LN, st))) return rc;
     if ((rc = launch_layernorm_quant(ws.x, ws.y32, w.ln1_g, w.ln1_b, c.layer_norm_eps, rows, H,
                                      T_dev, q.up.ias, ws.aq, ws.sa, st)))
@@ -1650,7 +1704,7 @@ int encode_device_i8(nebw_model *m, Workspace &ws, bool prof, const int *ids, co
     a.bias = w.b_up;
     a.out = ws.h32;
     if ((rc = prof_mark(m, prof, NEBW_K_GEMM_UP, st))) return rc;
-    if ((rc = launch_gemm_i8(d, q.up.w, ws.map_aq_h, a, true, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.up.w, ws.map_aq_h, ws.out_h32, a, true, st))) return rc;
     if ((rc = launch_quantise(ws.h32, false, rows, T_dev, F, q.dn.ias, ws.aq, ws.sa, st)))
       return rc;
     // FFN-down (fp32), then add + LayerNorm + the next layer's quantisation
@@ -1660,7 +1714,7 @@ int encode_device_i8(nebw_model *m, Workspace &ws, bool prof, const int *ids, co
     a.bias = w.b_dn;
     a.out = ws.y32;
     if ((rc = prof_mark(m, prof, NEBW_K_GEMM_DOWN, st))) return rc;
-    if ((rc = launch_gemm_i8(d, q.dn.w, ws.map_aq_f, a, false, st))) return rc;
+    if ((rc = launch_gemm_i8(d, q.dn.w, ws.map_aq_f, ws.out_y32, a, false, st))) return rc;
     if ((rc = prof_mark(m, prof, NEBW_K_LN, st))) return rc;
     const bool last = L + 1 == c.num_layers;
     if ((rc = launch_layernorm_quant(ws.x, ws.y32, w.ln2_g, w.ln2_b, c.layer_norm_eps, rows, H,

@@ -38,6 +38,32 @@ def test_quantise_rows_bit_exact(device, port_oracle):
         np.testing.assert_array_equal(sc.cpu().numpy(), want_sc)
 
 
+@pytest.mark.parametrize("K", [12, 36, 200, 384, 1000, 1536, 3072, 4096, 5120, 8192, 8196])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_quantise_rows_widths(device, port_oracle, K, bf16):
+    """Every row width the quantiser dispatches on -- the row in one warp's
+    registers (K % 4 == 0 up to 2048: 1 to 16 float4 per lane), in one CTA's
+    (up to 8192: 4 or 8 float4 per thread), past-K lanes idle, or read twice
+    by a warp (else) -- against the oracle, bit for bit, fp32 and bf16 rows,
+    with an all-zero row and rows of very different magnitude."""
+    rng = np.random.default_rng(K + 7 * bf16)
+    rows = 37
+    a = (rng.standard_normal((rows, K)) * rng.lognormal(0, 2, (rows, 1))).astype(np.float32)
+    a[5] = 0
+    x = torch.from_numpy(a).cuda()
+    if bf16:
+        x = x.to(torch.bfloat16)
+        a = x.float().cpu().numpy()
+    ias = (1.0 / rng.lognormal(0.0, 0.5, K)).astype(np.float32)
+    q = torch.empty((rows, K), dtype=torch.int8, device="cuda")
+    sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+    device.quantise_rows(x, rows, K, _dev(ias), q, sc)
+    device.sync()
+    want_q, want_sc = port_oracle.quantise_rows(a, ias)
+    np.testing.assert_array_equal(q.cpu().numpy(), want_q)
+    np.testing.assert_array_equal(sc.cpu().numpy(), want_sc)
+
+
 @pytest.mark.parametrize("M,K,N", [(16, 512, 512), (1, 128, 8), (300, 1024, 4096),
                                    (257, 384, 1152), (1000, 4096, 1024), (77, 48, 40)])
 @pytest.mark.parametrize("act", [0, 1])
