@@ -72,25 +72,6 @@ struct GemmI8Args {
   int *err;
 };
 
-// Instruction descriptor for tcgen05.mma kind::i8: s8 A and B, s32 D, both
-// K-major, dense: bits 4-5 D format (2 = s32), 7-9 A (1 = signed 8-bit),
-// 10-12 B (1 = signed 8-bit), 17-22 N >> 3, 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t idesc_s8_s32(int m, int n) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, s8 in, s32 accumulate, K = 32.
-__device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 __device__ __forceinline__ float widen(float v) { return v; }
 __device__ __forceinline__ float widen(__nv_bfloat16 v) { return __bfloat162float(v); }
 
@@ -231,58 +212,6 @@ __global__ void __launch_bounds__(256)
       }
       *reinterpret_cast<uint32_t *>(qr + c) = pk;
     }
-  }
-}
-
-// Dequantise (and gelu8) the 32 accumulator columns [col0, col0 + 32) of this
-// thread's row into its row of a 32-row chunk staged in shared memory, in the
-// output map's swizzle: fp32 rows of 128 bytes (16-byte piece q at q ^ (r % 8)),
-// or bf16 RNE rows of 64 bytes (q ^ ((r / 2) % 4)).  Columns past N and rows
-// past the live count are staged as 0 (the bulk store clips columns past the
-// map's N; rows past the live count but inside the buffer are written, and a
-// zero row is what the encoder's later readers of those rows expect).
-template <bool GELU, bool BF16>
-__device__ __forceinline__ void i8_stage32(const GemmI8Args &p, bool live_row, int row, int col0,
-                                           const uint32_t (&r)[32], uint8_t *chunk, int lane) {
-  const int ncols = live_row ? min(32, p.N - col0) : 0;  // N % 8 == 0
-  const float sa = live_row ? __ldg(p.sa + row) : 0.0f;
-  const float4 *w4 = reinterpret_cast<const float4 *>(p.ws + col0);
-  const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
-  float y[32];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i * 4 < ncols) {
-      const float4 w = __ldg(w4 + i);
-      const float4 b = p.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float ws[4] = {w.x, w.y, w.z, w.w}, bs[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float c = __int2float_rn(static_cast<int>(r[4 * i + e]));
-        float v = fmaf(c * sa, ws[e], bs[e]);
-        if constexpr (GELU) v = gelu8(v);
-        y[4 * i + e] = v;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) y[4 * i + e] = 0.0f;
-    }
-  }
-  if constexpr (BF16) {
-    uint8_t *rowp = chunk + lane * 64;
-    const int sw = (lane >> 1) & 3;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint4 *>(rowp + ((q ^ sw) << 4)) =
-          make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
-                     pack_bf16x2(y[8 * q + 4], y[8 * q + 5]),
-                     pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
-  } else {
-    uint8_t *rowp = chunk + lane * 128;
-    const int sw = lane & 7;
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      *reinterpret_cast<float4 *>(rowp + ((q ^ sw) << 4)) =
-          make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
   }
 }
 
@@ -460,7 +389,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // the store that last read `chunk` is done
           if (lane == 0) bulk_wait_group_read<kSlots - 1>();
           __syncwarp();
-          i8_stage32<GELU, BF16>(p, row < M, row, col0, cur, chunk, lane);
+          i8_stage32<GELU, BF16>(p.N, p.ws, p.bias, row < M ? __ldg(p.sa + row) : 0.0f, row < M,
+                                 col0, cur, chunk, lane);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {

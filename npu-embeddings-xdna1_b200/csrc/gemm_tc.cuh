@@ -55,7 +55,16 @@ enum GemmEpi : int {
   // head_dim-64 head by the row's position (row_pos) before the narrow, V
   // columns plain.  CTA-pair kernel only.
   kEpiBf16Rope = 7,
+  // int8 operands (tcgen05 kind::i8, s32 accumulators, 128-int8 K-blocks:
+  // the same 128-byte rows), dequantised in the epilogue as
+  // app::dequantise_c does, y = fma(float(acc) * sa[row], ws[col], bias[col]);
+  // rows past the live count are written as 0.  CTA-pair kernel only.
+  kEpiI8F32 = 8,    // out f32  = y
+  kEpiI8Gelu8 = 9,  // out f32  = gelu8(y)
+  kEpiI8Bf16 = 10,  // out bf16 = y
 };
+
+__host__ __device__ constexpr bool epi_int8(int e) { return e >= kEpiI8F32 && e <= kEpiI8Bf16; }
 
 struct GemmArgs {
   int M;             // row bound (the A tensor map's row extent)
@@ -70,6 +79,8 @@ struct GemmArgs {
   const int *row_pos;
   const float *rope_cos, *rope_sin;
   int rope_rows, rope_cols;
+  // int8 epilogues: A's row scales [M] and W's column scales [N]
+  const float *sa, *ws;
 };
 
 constexpr int kGemmBM = 128;
@@ -519,6 +530,66 @@ __device__ __forceinline__ void epi_stage32(const GemmArgs &p, int col0, const u
   }
 }
 
+// The int8 epilogue: dequantise (and gelu8) the 32 int32 accumulator columns
+// [col0, col0 + 32) of this thread's row -- app::dequantise_c's
+// y = fma(float(c) * sa, ws[col], bias[col]) -- into its row of a 32-row
+// chunk staged in shared memory, in the output map's swizzle: fp32 rows of 128 bytes (16-byte piece q at q ^ (r % 8)),
+// or bf16 RNE rows of 64 bytes (q ^ ((r / 2) % 4)).  Columns past N and rows
+// past the live count are staged as 0 (the bulk store clips columns past the
+// map's N; rows past the live count but inside the buffer are written, and a
+// zero row is what the encoder's later readers of those rows expect).
+template <bool GELU, bool BF16>
+__device__ __forceinline__ void i8_stage32(int N, const float *ws, const float *bias, float sa,
+                                           bool live_row, int col0, const uint32_t (&r)[32],
+                                           uint8_t *chunk, int lane) {
+  const int ncols = live_row ? min(32, N - col0) : 0;  // N % 8 == 0
+  const float4 *w4 = reinterpret_cast<const float4 *>(ws + col0);
+  const float4 *b4 = reinterpret_cast<const float4 *>(bias + col0);
+  // two columns at a time on the packed fp32 pipe: the same IEEE product and
+  // fused multiply-add per value as the scalar form, half the instructions
+  const uint64_t sa2 = pk2(sa, sa);
+  float y[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i * 4 < ncols) {
+      const float4 w = __ldg(w4 + i);
+      const float4 b = bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float c0 = __int2float_rn(static_cast<int>(r[4 * i + 0]));
+      const float c1 = __int2float_rn(static_cast<int>(r[4 * i + 1]));
+      const float c2 = __int2float_rn(static_cast<int>(r[4 * i + 2]));
+      const float c3 = __int2float_rn(static_cast<int>(r[4 * i + 3]));
+      unpk2(fma_x2(mul_x2(pk2(c0, c1), sa2), pk2(w.x, w.y), pk2(b.x, b.y)), y[4 * i + 0],
+            y[4 * i + 1]);
+      unpk2(fma_x2(mul_x2(pk2(c2, c3), sa2), pk2(w.z, w.w), pk2(b.z, b.w)), y[4 * i + 2],
+            y[4 * i + 3]);
+      if constexpr (GELU) {
+        gelu8_x2(y[4 * i + 0], y[4 * i + 1]);
+        gelu8_x2(y[4 * i + 2], y[4 * i + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[4 * i + e] = 0.0f;
+    }
+  }
+  if constexpr (BF16) {
+    uint8_t *rowp = chunk + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(rowp + ((q ^ sw) << 4)) =
+          make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                     pack_bf16x2(y[8 * q + 4], y[8 * q + 5]),
+                     pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+  } else {
+    uint8_t *rowp = chunk + lane * 128;
+    const int sw = lane & 7;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4 *>(rowp + ((q ^ sw) << 4)) =
+          make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+  }
+}
+
 // Gated epilogue: the up chunk (GEMM columns col0 .. col0+31) and the gate
 // chunk (col0+32 .. col0+63) of this thread's row -> 32 bf16 outputs
 // up * act(gate), biases added first, staged as one bf16 32 x 32 chunk in
@@ -619,6 +690,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   constexpr int kStages = S::kStages;
   constexpr int kPairM = 2 * kGemmBM;
   constexpr bool kTmaStore = EPI != kEpiF32Resid;
+  constexpr bool kInt8 = epi_int8(EPI);
+  // elements per 128-byte K-block: 64 bf16 or 128 int8 (the same tiles)
+  constexpr int kBK = kInt8 ? 2 * kGemmBK : kGemmBK;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -642,7 +716,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int m_blocks = (M + kPairM - 1) / kPairM;
   const int n_blocks = (p.N + BN - 1) / BN;
   const int num_tiles = m_blocks * n_blocks;
-  const int num_kb = (p.K + kGemmBK - 1) / kGemmBK;
+  const int num_kb = (p.K + kBK - 1) / kBK;
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
 
   if (warp == 0 && lane == 0) {
@@ -685,8 +759,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           }
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
           const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
-          tma_load_2d_pair(sA + stage * S::kABytes, &tmA, bar, kb * kGemmBK, a_row);
-          tma_load_2d_pair(sW + stage * S::kBBytes, &tmW, bar, kb * kGemmBK, w_row);
+          tma_load_2d_pair(sA + stage * S::kABytes, &tmA, bar, kb * kBK, a_row);
+          tma_load_2d_pair(sW + stage * S::kBBytes, &tmW, bar, kb * kBK, w_row);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -709,7 +783,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     // The whole warp walks the schedule and waits (so that the loop state
     // and the descriptors are warp-uniform); one elected lane issues.
     if (leader) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kPairM, BN);
+      constexpr uint32_t idesc = kInt8 ? idesc_s8_s32(kPairM, BN) : idesc_bf16_f32(kPairM, BN);
       const bool elect = elect_one_sync();
       auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
@@ -733,9 +807,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const uint64_t da = sdesc_kmajor_sw128(smem_u32(sA + stage * S::kABytes));
           const uint64_t dw = sdesc_kmajor_sw128(smem_u32(sW + stage * S::kBBytes));
           if (elect) {
+            // four MMAs per 128-byte K-block, +32 B each (16 bf16 or 32 int8 of K)
 #pragma unroll
-            for (int k = 0; k < kGemmBK / 16; ++k)  // +32 B per 16 elements of K
-              umma_bf16_pair(d_tmem, da + k * 2, dw + k * 2, idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < 4; ++k) {
+              if constexpr (kInt8)
+                umma_s8_pair(d_tmem, da + k * 2, dw + k * 2, idesc, (kb | k) != 0 ? 1u : 0u);
+              else
+                umma_bf16_pair(d_tmem, da + k * 2, dw + k * 2, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
             umma_commit_pair(&empty[stage], 0x3);
           }
           __syncwarp();
@@ -764,7 +843,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     uint8_t *my_staging = staging + (warp - 2) * 2 * S::kChunkBytes;
     // a warp's 8 KB of staging holds two fp32 or four bf16 32 x 32 chunks:
     // that many stores may still be reading it while the next is written
-    constexpr bool kF32Out = EPI == kEpiF32 || EPI == kEpiF32Resid;
+    constexpr bool kF32Out =
+        EPI == kEpiF32 || EPI == kEpiF32Resid || EPI == kEpiI8F32 || EPI == kEpiI8Gelu8;
     constexpr int kOutChunk = kF32Out ? S::kChunkBytes : S::kChunkBytes / 2;
     constexpr int kSlots = 2 * S::kChunkBytes / kOutChunk;
     int nstore = 0;  // bulk stores this warp has issued (lane 0)
@@ -867,7 +947,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             // the store that last read `chunk` is done
             if (lane == 0) bulk_wait_group_read<kSlots - 1>();
             __syncwarp();
-            epi_stage32<EPI>(p, col0, cur, chunk, lane);
+            if constexpr (kInt8)
+              i8_stage32<EPI == kEpiI8Gelu8, EPI == kEpiI8Bf16>(
+                  p.N, p.ws, p.bias, row < M ? __ldg(p.sa + row) : 0.0f, row < M, col0, cur,
+                  chunk, lane);
+            else
+              epi_stage32<EPI>(p, col0, cur, chunk, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {

@@ -216,7 +216,7 @@ struct Weight {
 struct WeightI8 {
   int8_t *ptr = nullptr;  // [N, K] int8
   int64_t K = 0, N = 0;
-  CUtensorMap map128, map256;  // box rows 128 / 256, 128-byte K boxes
+  CUtensorMap map64, map128, map256;  // box rows 64 / 128 / 256, 128-byte K boxes
 };
 
 struct nebw_dev {
@@ -292,6 +292,12 @@ int set_all_gemm_attrs() {
   rc |= set_pair_attr<128, nebw::kEpiBf16Rope>();
   rc |= set_pair_attr<256, nebw::kEpiBf16Rope>();
   rc |= set_pair_attr<256, nebw::kEpiF32Resid>();
+  rc |= set_pair_attr<128, nebw::kEpiI8F32>();
+  rc |= set_pair_attr<128, nebw::kEpiI8Gelu8>();
+  rc |= set_pair_attr<128, nebw::kEpiI8Bf16>();
+  rc |= set_pair_attr<256, nebw::kEpiI8F32>();
+  rc |= set_pair_attr<256, nebw::kEpiI8Gelu8>();
+  rc |= set_pair_attr<256, nebw::kEpiI8Bf16>();
   return rc ? NEBW_ECUDA : NEBW_OK;
 }
 
@@ -370,6 +376,9 @@ int launch_gemm_pair(nebw_dev *d, int epi, const CUtensorMap &mA, const CUtensor
     case nebw::kEpiBf16SwiGLU: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16SwiGLU><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     case nebw::kEpiBf16GeGLU: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16GeGLU><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     case nebw::kEpiBf16Rope: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiBf16Rope><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiI8F32: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiI8F32><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiI8Gelu8: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiI8Gelu8><<<g, b, smem, st>>>(mA, mW, mC, a); break;
+    case nebw::kEpiI8Bf16: nebw::gemm_tc_pair_kernel<BN, nebw::kEpiI8Bf16><<<g, b, smem, st>>>(mA, mW, mC, a); break;
     default: return set_error(NEBW_EINVAL, "unknown GEMM epilogue %d", epi);
   }
   NEBW_CUDA(cudaGetLastError());
@@ -537,6 +546,27 @@ int launch_gemm_i8(nebw_dev *d, const WeightI8 &w, const CUtensorMap &mA, const 
                    const nebw::GemmI8Args &a, bool gelu, cudaStream_t st) {
   if (a.M <= 0) return NEBW_OK;
   const bool wide = w.N % 256 == 0;
+  if (d->gemm_pairs > 0 && a.K >= 2048) {
+    // the CTA-pair GEMM (256-row tiles: a third less operand traffic per SM
+    // than the single-CTA tile) with the int8 MMA and epilogue.  Measured
+    // faster at K 4096 (2.87 against 2.43 POPS at M 65,536, N 1024) and
+    // slower at K 1024 (0.83 against 0.71 ms at M 135,792, N 4096 with
+    // gelu8), where the epilogue bounds the tile and the pair's shared
+    // accumulator barrier waits on both CTAs' epilogues.
+    GemmArgs g{};
+    g.M = a.M;
+    g.M_dev = a.M_dev;
+    g.N = a.N;
+    g.K = a.K;
+    g.bias = a.bias;
+    g.sa = a.sa;
+    g.ws = a.ws;
+    g.err = a.err;
+    g.out = a.out_bf16 ? static_cast<void *>(a.out_bf16) : static_cast<void *>(a.out);
+    const int epi = a.out_bf16 ? nebw::kEpiI8Bf16 : gelu ? nebw::kEpiI8Gelu8 : nebw::kEpiI8F32;
+    if (wide) return launch_gemm_pair<256>(d, epi, mA, w.map128, mC, g, st);
+    return launch_gemm_pair<128>(d, epi, mA, w.map64, mC, g, st);
+  }
   const int BN = wide ? 256 : 128;
   const int64_t tiles = ((int64_t{a.M} + nebw::kGemmBM - 1) / nebw::kGemmBM) * ((w.N + BN - 1) / BN);
   const dim3 g(static_cast<unsigned>(std::min<int64_t>(tiles, d->sm_count)));
@@ -1049,7 +1079,8 @@ int stage_i8(const int8_t *host_kn, int64_t K, int64_t N, WeightI8 &w) {
     w.ptr = nullptr;
     return set_error(NEBW_ECUDA, "int8 weight upload failed");
   }
-  int rc = make_tmap_i8(&w.map128, w.ptr, N, K, 128);
+  int rc = make_tmap_i8(&w.map64, w.ptr, N, K, 64);
+  if (!rc) rc = make_tmap_i8(&w.map128, w.ptr, N, K, 128);
   if (!rc) rc = make_tmap_i8(&w.map256, w.ptr, N, K, 256);
   if (rc) {
     cudaFree(w.ptr);

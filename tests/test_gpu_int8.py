@@ -260,6 +260,36 @@ def test_int8_pass_matches_reference_array_path(device, port_oracle, tmp_path, n
     assert not np.array_equal(got, bf16)
 
 
+def test_int8_pass_bge_large_layers_vs_oracle(device, port_oracle, tmp_path):
+    """bge-large's geometry (hidden 1024, FFN 4096: the FFN-down product runs
+    on the CTA-pair int8 GEMM, the others on the single-CTA one), 2 layers,
+    as an int8 container: the GPU's int8 pass against the oracle's int8
+    array path (pinned bit-exact to the reference's) on 6 rows of the
+    benchmark batch, the shortest and the longest among them."""
+    import make_golden
+    import nebw
+    from nebw import synth
+    from nebw.npue import write_bert_container
+    cfg = synth.CONFIGS["bge-large"]
+    w = synth.config_weights(cfg, layers=2)
+    ids, mask, lens = synth.config_batch(cfg)
+    rows = make_golden.sample_rows(lens, 6)
+    path = tmp_path / "large_i8.npue"
+    write_bert_container(path, w, max_seq_len=cfg.seq, gemm_layout="pretiled_bf16", a_dtype="i8",
+                         tile=make_golden.PRETILED_TILE, mac=make_golden.PRETILED_MAC,
+                         smooth_seed=make_golden.PRETILED_SMOOTH_SEED)
+    m = nebw.Model.from_npue(device, path)
+    try:
+        m.set_datapath("i8")
+        got = m.encode(ids[rows], lens[rows])
+    finally:
+        m.close()
+    want = port_oracle.encode_i8(w, path, ids[rows], mask[rows])
+    cos, err = parity(got, want)
+    print(f"bge-large 2-layer int8 pass vs oracle: cos {cos:.7f} max-abs {err:.3e}")
+    assert np.isfinite(got).all() and cos >= 0.9995 and err <= 6e-3, (cos, err)
+
+
 def test_int8_pass_full_batch_and_order(device, tmp_path):
     """The whole MiniLM batch through the int8 datapath: every row finite, and
     each row independent of its batch neighbours (a permuted batch gives the
