@@ -206,10 +206,43 @@ def bench_encoder(dev, config, layers, iters, datapath="bf16"):
             "ms": e0.elapsed_time(e1) / iters, "kernels_ms": per}
 
 
+def bench_latency(dev, config, layers, B, seq, iters):
+    """Per-request wall time of the host-buffer entry point (nebw_encode: ids
+    and lengths copied in, the pass, embeddings copied out) for requests of B
+    sequences padded to `seq`, lengths drawn from the configuration's batch,
+    with the pass launched kernel by kernel and replayed as a CUDA graph."""
+    import time
+    import nebw
+    from nebw import synth
+    cfg = synth.CONFIGS[config]
+    ids, _, lens = synth.config_batch(cfg)
+    ids = np.ascontiguousarray(ids[:, :seq])
+    lens = np.minimum(lens, seq).astype(np.int32)
+    w = synth.config_weights(cfg, layers=layers if layers > 0 else None)  # <= 0: every layer
+    m = nebw.Model.from_weights(dev, w, max_seq_len=cfg.seq)
+    out = {}
+    try:
+        for graphs in (False, True):
+            m.set_graphs(graphs)
+            reqs = [(ids[i * B:(i + 1) * B], lens[i * B:(i + 1) * B])
+                    for i in range(len(lens) // B)]
+            for r in reqs[:3]:
+                m.encode(*r)
+            t0 = time.perf_counter()
+            for i in range(iters):
+                m.encode(*reqs[i % len(reqs)])
+            out["graphs" if graphs else "direct"] = (time.perf_counter() - t0) / iters * 1e3
+    finally:
+        m.close()
+    return {"kernel": "latency", "config": config, "layers": w.layers, "B": B, "seq": seq,
+            "ms_per_request": out}
+
+
 def main(argv=None):
     import nebw
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemm_i8", "attention", "layernorm", "encoder"])
+    ap.add_argument("op", choices=["gemm", "gemm_i8", "attention", "layernorm", "encoder",
+                                   "latency"])
     ap.add_argument("--config", default="bge-large")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--M", type=int, default=16384)
@@ -237,6 +270,8 @@ def main(argv=None):
         r = bench_attention(dev, a.B, a.len, a.heads, a.hd, a.iters, a.copies)
     elif a.op == "layernorm":
         r = bench_layernorm(dev, a.M, a.H, a.iters, a.copies)
+    elif a.op == "latency":
+        r = bench_latency(dev, a.config, a.layers, a.B, a.len, a.iters)
     else:
         r = bench_encoder(dev, a.config, a.layers, a.iters, a.datapath)
     print(json.dumps(r), flush=True)

@@ -1240,6 +1240,16 @@ struct nebw_model {
   // and the arithmetic the passes run (NEBW_DATAPATH_BF16 / _I8)
   std::vector<LayerI8> i8;
   int datapath = NEBW_DATAPATH_BF16;
+  // CUDA graphs of whole passes (nebw_model_set_graphs): one per (B, S,
+  // datapath, attention kernel), replayed by nebw_encode between its input
+  // and output copies; dropped whenever what they captured changes (the
+  // weights, the workspace, the datapath)
+  struct PassGraph {
+    int B, S, datapath, attn;
+    cudaGraphExec_t exec;
+  };
+  bool use_graphs = false;
+  std::vector<PassGraph> graphs;
   Workspace ws;                        // capacity ws.rows_cap = B * S of the largest call so far
   // host-buffer entry point (nebw_encode): device copies of its inputs and output
   int64_t ids_cap = 0;
@@ -1255,7 +1265,17 @@ struct nebw_model {
 
 namespace {
 
+constexpr size_t kMaxPassGraphs = 16;
+
+void drop_graphs(nebw_model *m) {
+  if (m->graphs.empty()) return;
+  cudaStreamSynchronize(m->dev->stream);  // no replay may still be running
+  for (auto &g : m->graphs) cudaGraphExecDestroy(g.exec);
+  m->graphs.clear();
+}
+
 void free_workspace(nebw_model *m) {
+  drop_graphs(m);
   Workspace &w = m->ws;
   for (void *p : {static_cast<void *>(w.x), static_cast<void *>(w.y), static_cast<void *>(w.a),
                   static_cast<void *>(w.qkv), static_cast<void *>(w.ctx), static_cast<void *>(w.h),
@@ -1808,6 +1828,7 @@ extern "C" int nebw_model_set_tensor(nebw_model *m, const char *name, const void
                                      int64_t rows, int64_t cols) {
   NEBW_REQUIRE(m && name && host, "null argument");
   if (int rc = use_dev(m->dev)) return rc;
+  drop_graphs(m);  // a captured pass reads the tensors being replaced
   const nebw_config &c = m->cfg;
   const std::string n(name);
   const int64_t H = c.hidden, F = c.intermediate;
@@ -1903,6 +1924,7 @@ extern "C" int nebw_model_set_gemm_nk(nebw_model *m, const char *name, const uin
                                       int64_t n_rows, int64_t k_cols) {
   NEBW_REQUIRE(m && name && host, "null argument");
   if (int rc = use_dev(m->dev)) return rc;
+  drop_graphs(m);  // a captured pass reads the tensors being replaced
   const nebw_config &c = m->cfg;
   const std::string n(name);
   const int64_t H = c.hidden, F = c.intermediate;
@@ -1967,6 +1989,7 @@ extern "C" int nebw_model_set_int8_operand(nebw_model *m, const char *name, cons
                                            int64_t N) {
   NEBW_REQUIRE(m && name && host_kn && wscale && asmooth, "null argument");
   if (int rc = use_dev(m->dev)) return rc;
+  drop_graphs(m);  // a captured pass reads the tensors being replaced
   const nebw_config &c = m->cfg;
   int layer = -1;
   char kind[16] = {0};
@@ -2029,13 +2052,23 @@ extern "C" int nebw_model_set_datapath(nebw_model *m, int32_t datapath) {
                    "%d lacks one (nebw_model_set_int8_operand, or an int8 container)", L);
     }
   }
+  if (datapath != m->datapath) drop_graphs(m);
   m->datapath = datapath;
+  return NEBW_OK;
+}
+
+extern "C" int nebw_model_set_graphs(nebw_model *m, int32_t on) {
+  NEBW_REQUIRE(m, "null model");
+  if (int rc = use_dev(m->dev)) return rc;
+  if (!on) drop_graphs(m);
+  m->use_graphs = on != 0;
   return NEBW_OK;
 }
 
 extern "C" int nebw_model_set_rope_freq(nebw_model *m, const double *inv_freq, int32_t n) {
   NEBW_REQUIRE(m && inv_freq, "null argument");
   if (int rc = use_dev(m->dev)) return rc;
+  drop_graphs(m);  // a captured pass reads the tensors being replaced
   NEBW_REQUIRE(m->cfg.rope, "the model is not rotary (config.rope is 0)");
   NEBW_REQUIRE(n == m->cfg.head_dim / 2, "%d rotary frequencies given, head_dim / 2 = %d expected",
                n, m->cfg.head_dim / 2);
@@ -2398,6 +2431,51 @@ extern "C" int nebw_encode_device(nebw_model *m, const int32_t *ids, const int32
   return encode_device(m, m->ws, m->prof, ids, lens, B, S, out, pick_stream(m->dev, stream));
 }
 
+namespace {
+// The graph of one pass of B x S on the model's own workspace, inputs
+// (m->ids, m->len_in) and output (m->out): found in the model's cache, or
+// captured from encode_device on the model's stream and instantiated (the
+// oldest of kMaxPassGraphs is dropped to make room).  The packed row count
+// and the attention work list are computed on the device inside the pass,
+// so one graph serves every length pattern of that shape.
+int pass_graph(nebw_model *m, int B, int S, cudaGraphExec_t *out) {
+  const int attn = m->dev->attn_kind;
+  for (const auto &g : m->graphs)
+    if (g.B == B && g.S == S && g.datapath == m->datapath && g.attn == attn) {
+      *out = g.exec;
+      return NEBW_OK;
+    }
+  cudaStream_t st = m->dev->stream;
+  if (m->graphs.size() >= kMaxPassGraphs) {
+    NEBW_CUDA(cudaStreamSynchronize(st));
+    cudaGraphExecDestroy(m->graphs.front().exec);
+    m->graphs.erase(m->graphs.begin());
+  }
+  cudaGraph_t graph = nullptr;
+  NEBW_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  const int rc = encode_device(m, m->ws, false, m->ids, m->len_in, B, S, m->out, st);
+  const std::string why = rc ? g_last_error : std::string();
+  const cudaError_t e = cudaStreamEndCapture(st, &graph);
+  if (rc || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    if (rc) return set_error(rc, "%s", why.c_str());
+    return set_error(NEBW_ECUDA, "capturing the pass as a CUDA graph failed: %s",
+                     cudaGetErrorString(e));
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(NEBW_ECUDA, "instantiating the pass graph failed: %s", cudaGetErrorString(ei));
+  }
+  m->graphs.push_back({B, S, m->datapath, attn, exec});
+  *out = exec;
+  return NEBW_OK;
+}
+}  // namespace
+
 extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B,
                            int32_t S, float *out) {
   NEBW_REQUIRE(m && ids && lens && out, "null argument");
@@ -2407,9 +2485,16 @@ extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *len
   if (int rc = ensure_workspace(m, B, S)) return rc;
   nebw_dev *d = m->dev;
   cudaStream_t st = d->stream;
+  cudaGraphExec_t graph = nullptr;
+  if (m->use_graphs && !m->prof)
+    if (int rc = pass_graph(m, B, S, &graph)) return rc;
   NEBW_CUDA(cudaMemcpyAsync(m->ids, ids, static_cast<size_t>(B) * S * 4, cudaMemcpyHostToDevice, st));
   NEBW_CUDA(cudaMemcpyAsync(m->len_in, lens, static_cast<size_t>(B) * 4, cudaMemcpyHostToDevice, st));
-  if (int rc = encode_device(m, m->ws, m->prof, m->ids, m->len_in, B, S, m->out, st)) return rc;
+  if (graph) {
+    NEBW_CUDA(cudaGraphLaunch(graph, st));
+  } else if (int rc = encode_device(m, m->ws, m->prof, m->ids, m->len_in, B, S, m->out, st)) {
+    return rc;
+  }
   NEBW_CUDA(cudaMemcpyAsync(out, m->out, static_cast<size_t>(B) * m->cfg.hidden * 4,
                             cudaMemcpyDeviceToHost, st));
   return nebw_sync(d);

@@ -124,6 +124,17 @@ class GpuBertEncoder {
     return out;
   }
 
+  // Replay each (batch, seq) shape's pass as a CUDA graph (nebw_model_set_graphs):
+  // the same embeddings bit for bit, one launch per request instead of ~7 per
+  // layer (measured: one bge-large sequence 2.45 -> 2.11 ms, one bge-small
+  // sequence 0.78 -> 0.61 ms).  Worth it when requests come in a few batch
+  // shapes, as a server's do; each new shape is captured once (up to 16 kept).
+  // Single-GPU encoders only.
+  void use_graphs(bool on) {
+    if (!comms_.empty()) throw std::runtime_error("nebw: graphs are for the single-GPU encoder");
+    check(nebw_model_set_graphs(model_, on ? 1 : 0));
+  }
+
   nebw_model *model() { return model_; }
   nebw_dev *device() { return dev_; }
   size_t gpus() const { return devs_.size(); }

@@ -127,6 +127,7 @@ def lib() -> C.CDLL:
                                  C.c_int),
         "nebw_model_set_int8_operand": ([vp, C.c_char_p, vp, vp, vp, i64, i64], C.c_int),
         "nebw_model_set_datapath": ([vp, i32], C.c_int),
+        "nebw_model_set_graphs": ([vp, i32], C.c_int),
         "nebw_pack_checkpoint": ([C.c_char_p, C.c_char_p, C.c_char_p, i32, i32,
                                   C.POINTER(C.c_uint64)], C.c_int),
         "nebw_comm_unique_id": ([vp], C.c_int),
@@ -369,6 +370,10 @@ class Model:
         """"bf16" (default) or "i8": the int8 array path of an int8 container
         (nebw_model_set_datapath)."""
         _check(lib().nebw_model_set_datapath(self.h, self.DATAPATHS[datapath]))
+
+    def set_graphs(self, on: bool = True):
+        """encode() replays each (B, S) shape's pass as a CUDA graph (nebw_model_set_graphs)."""
+        _check(lib().nebw_model_set_graphs(self.h, int(bool(on))))
 
     def set_int8_operand(self, name: str, kn, wscale, asmooth):
         """An int8 GEMM operand [K, N] with its .wscale [N] and .asmooth [K]."""

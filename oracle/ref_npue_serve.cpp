@@ -9,7 +9,8 @@
 // tokenizer (app::load_tokenizer), with nebw::GpuNpueEncoder
 // (host/npue_gpu_encoder.hpp) as the app::EmbedBackend's embed function and
 // the runtime's own truncation policy (app::check_truncation: an input over
-// the sequence length is npue::InputTooLong, HTTP 400).  This is the wiring
+// the sequence length is npue::InputTooLong, HTTP 400), each request shape's
+// pass replayed as a CUDA graph.  This is the wiring
 // a maintainer adds to the runtime's `serve` subcommand
 // (runtime/src/cli/subcommand.cpp:202-274) in place of make_service's
 // BertEncoder lanes.  Serves on 127.0.0.1 until SIGINT / SIGTERM.
@@ -35,6 +36,7 @@ int main(int argc, char **argv) {
     const int64_t seq = argc > 3 ? std::stoll(argv[3]) : file.config_int("max_seq_len");
     const app::AnyTokenizer tok = app::load_tokenizer(file, model);
     nebw::GpuNpueEncoder<app::AnyTokenizer> gpu(model, tok, seq, 0, app::check_truncation);
+    gpu.gpu().use_graphs(true);  // a server's requests come in a few batch shapes
     app::EmbedBackend be;
     be.vocab_size = tok.vocab_size();
     be.hidden = gpu.hidden();

@@ -276,3 +276,43 @@ def test_gated_single_cta_path_vs_oracle(port_oracle, key, tmp_path):
     lens = np.array([512, 1, 63, 64, 65, 129, 200, 17], np.int32)
     ids, mask = synth.make_tokens(len(lens), 512, lens, seed=43)
     check(np.load(out), port_oracle.encode(w, ids, mask), f"{key} single-CTA path")
+
+
+def test_graph_replay_matches_direct_launches(device):
+    """nebw_model_set_graphs: a (B, S) shape's pass is captured once as a CUDA
+    graph and replayed by nebw_encode.  Bit for bit the direct launches'
+    results: for new rows of a shape already captured (the packed row count
+    and the attention work list are computed on the device, so one graph
+    serves every length pattern), across shapes, after the workspace grows
+    (the graphs are dropped and captured again), and with the mma.sync
+    attention kernel (the kernel choice is part of a graph's key)."""
+    import nebw
+    from nebw import synth
+    cfg = synth.CONFIGS["bge-small"]
+    w = synth.config_weights(cfg, layers=2)
+    ids, _mask, lens = synth.config_batch(cfg)
+    rng = np.random.default_rng(0)
+    cases = []
+    for B, S in [(4, 128), (4, 128), (7, 512), (64, 512), (4, 128), (7, 512), (1, 64)]:
+        sel = rng.choice(len(lens), B, replace=False)
+        cases.append((np.ascontiguousarray(ids[sel, :S]),
+                      np.minimum(lens[sel], S).astype(np.int32)))
+    m = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)
+    try:
+        want = [m.encode(i, l) for i, l in cases]
+    finally:
+        m.close()
+    m = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)  # a fresh, unsized workspace
+    try:
+        m.set_graphs(True)
+        for k, (i, l) in enumerate(cases):
+            np.testing.assert_array_equal(m.encode(i, l), want[k], err_msg=f"case {k}")
+            np.testing.assert_array_equal(m.encode(i, l), want[k], err_msg=f"case {k} again")
+        device.set_attention_kernel(device.ATTN_MMA)
+        m.set_graphs(False)
+        direct = m.encode(*cases[2])
+        m.set_graphs(True)
+        np.testing.assert_array_equal(m.encode(*cases[2]), direct)
+    finally:
+        device.set_attention_kernel(device.ATTN_TCGEN05)
+        m.close()

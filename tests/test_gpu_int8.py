@@ -293,7 +293,8 @@ def test_int8_pass_bge_large_layers_vs_oracle(device, port_oracle, tmp_path):
 def test_int8_pass_full_batch_and_order(device, tmp_path):
     """The whole MiniLM batch through the int8 datapath: every row finite, and
     each row independent of its batch neighbours (a permuted batch gives the
-    same rows bit for bit, as every step is row-local or per sequence)."""
+    same rows bit for bit, as every step is row-local or per sequence), also
+    when the pass is replayed as a CUDA graph."""
     import nebw
     from nebw import synth
     cfg = synth.CONFIGS["minilm"]
@@ -305,10 +306,13 @@ def test_int8_pass_full_batch_and_order(device, tmp_path):
         full = m.encode(ids, lens)
         order = np.random.default_rng(3).permutation(len(lens))
         perm = m.encode(ids[order], lens[order])
+        m.set_graphs(True)  # the int8 pass replayed as a CUDA graph: the same rows
+        graphed = m.encode(ids[order], lens[order])
     finally:
         m.close()
     assert np.isfinite(full).all()
     np.testing.assert_array_equal(perm, full[order])
+    np.testing.assert_array_equal(graphed, perm)
 
 
 def test_int8_datapath_refusals(device, tmp_path):
