@@ -36,13 +36,14 @@
 //
 // Only the valid keys of a block are multiplied and exponentiated (in
 // 16-key groups), so short sequences -- most of an embedding batch -- cost
-// what their length needs rather than a full 128 x 128 tile.
+// what their length needs rather than a full 128 x 64 tile.
 //
-// 72 KB (D 64) or 44 KB (D 32) of shared memory, 128 TMEM columns and at
-// most 112 registers per thread per CTA, so three CTAs share an SM (three
-// softmax warps per SM sub-partition) and one's softmax overlaps the others'
-// waits on loads and products; the 64-key block is what makes the third CTA
-// fit.  Q is pre-scaled by 1/sqrt(D) (the packer's fold,
+// 72 KB (D 64) or 44 KB (D 32) of shared memory, 128 TMEM columns and 96
+// registers per thread per CTA (three CTAs of 18 warps put five warps on one
+// SM sub-partition, whose 16K registers allow 96 a thread), so three CTAs
+// share an SM (three softmax warps per SM sub-partition) and one's softmax
+// overlaps the others' waits on loads and products; the 64-key block is what
+// makes the third CTA fit.  Q is pre-scaled by 1/sqrt(D) (the packer's fold,
 // tools/pack/pack_npue.py:2742-2750); no scale is applied here.
 //
 // Replaces qk_impl / softmax_cpu / av_impl (runtime/src/encoders/
