@@ -119,6 +119,63 @@ def bench_layernorm(dev, M, H, iters, copies):
     return {"kernel": "layernorm", "M": M, "H": H, "ms": ms, "gbs": by / ms / 1e6}
 
 
+def bench_pool(dev, config, cls, iters):
+    """Pooling + L2 over a configuration's packed batch (fp32 hidden rows
+    [T, H]): mean reads every row (T x H x 4 bytes), CLS one row a sequence."""
+    import torch
+    from nebw import synth
+    cfg = synth.CONFIGS[config]
+    _, _, lens = synth.config_batch(cfg)
+    lens = lens.astype(np.int32)
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T, B, H = int(off[-1]), len(lens), cfg.arch.hidden
+    h = torch.randn(T, H, device="cuda")
+    off_d = torch.from_numpy(off).cuda()
+    len_d = torch.from_numpy(lens).cuda()
+    out = torch.empty(B, H, device="cuda")
+
+    def run():
+        dev.pool_l2(h, off_d, len_d, B, H, int(cls), out, stream=torch.cuda.current_stream())
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    ms = e0.elapsed_time(e1) / iters
+    by = (B if cls else T) * H * 4 + B * H * 4
+    return {"kernel": "pool_l2", "config": config, "cls": bool(cls), "T": T, "B": B, "H": H,
+            "ms": ms, "gbs": by / ms / 1e6}
+
+
+def bench_narrow(dev, M, iters, copies):
+    """The standalone fp32 -> bf16 RNE narrow over M elements: 6 bytes each."""
+    import torch
+    xs = [torch.randn(M, device="cuda") for _ in range(copies)]
+    y = torch.empty(M, device="cuda", dtype=torch.bfloat16)
+
+    def run(i):
+        dev.narrow_bf16(xs[i % copies], M, y, stream=torch.cuda.current_stream())
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dev.sync()
+    ms = e0.elapsed_time(e1) / iters
+    return {"kernel": "narrow_bf16", "M": M, "ms": ms, "gbs": M * 6 / ms / 1e6}
+
+
 def bench_gemm_i8(dev, M, K, N, epi, iters, copies):
     """The int8 GEMM (tcgen05 kind::i8) with the dequantise epilogue: epi
     "f32" fp32 out, "gelu8" dequantise + gelu8, fp32 out, "bf16" bf16 RNE out
@@ -242,7 +299,8 @@ def main(argv=None):
     import nebw
     ap = argparse.ArgumentParser()
     ap.add_argument("op", choices=["gemm", "gemm_i8", "attention", "layernorm", "encoder",
-                                   "latency"])
+                                   "latency", "pool", "narrow"])
+    ap.add_argument("--cls", type=int, default=0, help="pool: 1 CLS row, 0 masked mean")
     ap.add_argument("--config", default="bge-large")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--M", type=int, default=16384)
@@ -270,6 +328,10 @@ def main(argv=None):
         r = bench_attention(dev, a.B, a.len, a.heads, a.hd, a.iters, a.copies)
     elif a.op == "layernorm":
         r = bench_layernorm(dev, a.M, a.H, a.iters, a.copies)
+    elif a.op == "pool":
+        r = bench_pool(dev, a.config, a.cls, a.iters)
+    elif a.op == "narrow":
+        r = bench_narrow(dev, a.M, a.iters, a.copies)
     elif a.op == "latency":
         r = bench_latency(dev, a.config, a.layers, a.B, a.len, a.iters)
     else:
