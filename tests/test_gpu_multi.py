@@ -111,6 +111,40 @@ def test_encode_multi_over_every_visible_gpu(device):
             d.close()
 
 
+def test_encode_multi_int8_datapath(device, tmp_path):
+    """The sharded pass runs the model's datapath: an int8 container on the
+    int8 datapath (its FFN-down on the CTA-pair int8 GEMM at bge-base's FFN
+    of 3072) gives the single-GPU int8 pass's rows bit for bit, over every
+    visible GPU (one rank on a 1-GPU box)."""
+    import nebw
+    from nebw.npue import write_bert_container
+    n = min(_gpus(), 8)
+    w = _weights()
+    ids, lens = _batch(n=40, S=128, seed=65)
+    path = tmp_path / "i8.npue"
+    write_bert_container(path, w, max_seq_len=128, gemm_layout="pretiled_bf16", a_dtype="i8",
+                         tile=(64, 64), mac=(8, 8), smooth_seed=3)
+    ref = nebw.Model.from_npue(device, path)
+    ref.set_datapath("i8")
+    want = ref.encode(ids, lens)
+    ref.close()
+    devs = [device] + [nebw.Device(i) for i in range(1, n)]
+    models = [nebw.Model.from_npue(d, path) for d in devs]
+    for m in models:
+        m.set_datapath("i8")
+    comms = nebw.Comm.init_all(devs, timeout_s=60.0)
+    try:
+        got = nebw.encode_multi(models, comms, ids, lens)
+        np.testing.assert_array_equal(got, want)
+    finally:
+        for c in comms:
+            c.close()
+        for m in models:
+            m.close()
+        for d in devs[1:]:
+            d.close()
+
+
 _RANK = textwrap.dedent("""
     import os, sys
     import numpy as np
