@@ -377,6 +377,9 @@ def gpu_arm(args, cfg):
                                            out_d if rank == 0 else None, stream=stream)
 
     # ---- device-resident throughput --------------------------------------
+    # each pass replayed as a CUDA graph (nebw_model_set_graphs: the same
+    # kernels, one launch; bit-identical rows) unless --no-graphs
+    model.set_graphs(args.graphs)
     for _ in range(args.warmup):
         step()
     ranks.barrier()
@@ -384,7 +387,6 @@ def gpu_arm(args, cfg):
     if sampler:
         sampler.start()
         time.sleep(0.6)
-    model.profile(True)
     ranks.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -394,11 +396,20 @@ def gpu_arm(args, cfg):
     ranks.barrier()
     if sampler:
         sampler.stop()
-    model.profile(False)
-    prof = model.profile_collect()
     ms = e0.elapsed_time(e1)
     dev.sync()
     ms_max = ranks.max(ms)
+    # the per-kernel split: the same steps again with a CUDA event before
+    # every kernel (the profiler launches the kernels one by one)
+    model.profile(True)
+    model.profile_collect()
+    ranks.barrier()
+    for _ in range(args.steps):
+        step()
+    ranks.barrier()
+    model.profile(False)
+    prof = model.profile_collect()
+    dev.sync()
 
     # ---- end to end through the public API with host buffers ------------
     # N = 1: nebw_encode (H2D of ids and lengths, the pass, D2H); N > 1:
@@ -501,7 +512,14 @@ def gpu_arm(args, cfg):
                        "parallelism": f"dp{world} (libnebw: length-balanced shards, "
                                       "NCCL gather to rank 0)" if world > 1 else "single GPU",
                        "l2": "no flush: every step streams the 0.6 GB bf16 weights and GBs of "
-                             "activations, far above the 126 MB L2"},
+                             "activations, far above the 126 MB L2",
+                       "graphs": bool(args.graphs),
+                       "timing": ("timed steps replay each pass as a CUDA graph "
+                                  "(nebw_model_set_graphs)" if args.graphs else
+                                  "timed steps launch kernel by kernel") +
+                                 "; the per-kernel split and the roofline figures come from a "
+                                 "second run of the same steps with a CUDA event on the "
+                                 "launching stream before every kernel"},
             "e2e": {"value": e2e, "unit": "embeddings/s",
                     "h2d_bytes_per_step": int(B * S * 4 + B * 4),
                     "d2h_bytes_per_step": int(B * H * 4),
@@ -819,6 +837,8 @@ def main():
     ap.add_argument("--config", default="bge-large",
                     choices=sorted(synth.CONFIGS) + sorted(synth.VIT_CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graphs", action=argparse.BooleanOptionalAction, default=True,
+                    help="replay each pass as a CUDA graph (BERT configurations)")
     ap.add_argument("--attention", choices=["mma", "tcgen05"], default="tcgen05",
                     help="attention kernel for head_dim 64")
     args = ap.parse_args()

@@ -298,16 +298,19 @@ int nebw_model_set_int8_operand(nebw_model *m, const char *name, const int8_t *h
  * refuses a model set to NEBW_DATAPATH_I8. */
 enum { NEBW_DATAPATH_BF16 = 0, NEBW_DATAPATH_I8 = 1 };
 int nebw_model_set_datapath(nebw_model *m, int32_t datapath);
-/* on != 0: nebw_encode replays each batch shape's pass as a CUDA graph --
- * captured on the first call of a (B, S) shape (with the model's datapath
- * and the device's attention kernel), then launched in one call between
- * the input and output copies -- instead of launching its ~7 kernels per
- * layer one by one.  The packed row count is computed on the device inside
- * the pass, so one graph serves every length pattern of its shape.  Up to 16
- * shapes are kept; setting a tensor, the datapath or growing the workspace
- * drops them.  Off by default; profiling (nebw_model_profile) launches
- * directly.  The results are the direct launches' bit for bit.  The
- * device-buffer entry points launch directly. */
+/* on != 0: the model's passes are replayed as CUDA graphs instead of
+ * launching their ~7 kernels per layer one by one -- by nebw_encode (between
+ * its input and output copies), nebw_encode_device and the sharded passes of
+ * the several-GPU entry points.  A graph is captured (on a stream of the
+ * library's own) on the first pass of a (B, S) shape with given device input
+ * / output buffers (and the model's datapath and the device's attention
+ * kernel), then launched in one call, on the caller's stream, whenever they
+ * recur; the packed row count is computed
+ * on the device inside the pass, so one graph serves every length pattern of
+ * its shape.  Up to 16 are kept; setting a tensor, the datapath or growing
+ * the workspace drops them.  Off by default; profiling (nebw_model_profile)
+ * launches directly.  The results are the direct launches' bit for bit.  The
+ * static entry point launches directly. */
 int nebw_model_set_graphs(nebw_model *m, int32_t on);
 /* The rotary frequency set as data (gte_new_rope_geglu's rope_inv_freq):
  * n = head_dim / 2 values, angle(s, j) = s * inv_freq[j] in double, as

@@ -218,19 +218,25 @@ def bench_gemm_i8(dev, M, K, N, epi, iters, copies):
             "tops": ops / (ms / 1e3) / 1e12}
 
 
-def bench_encoder(dev, config, layers, iters, datapath="bf16"):
+def bench_encoder(dev, config, layers, iters, datapath="bf16", graphs=False, batch=0):
     """Whole passes of a benchmark configuration's batch through a model of
     `layers` layers (the production launch sequence, attention work list
     included), with per-kernel device times from the model's profiler.
     datapath "i8": the same weights written as an int8 pre-tiled container
-    (the reference's --dtype i8 form) and run on the int8 datapath."""
+    (the reference's --dtype i8 form) and run on the int8 datapath.  graphs:
+    the passes replayed as CUDA graphs (timed without the per-kernel
+    profiler, which launches directly).  batch > 0: the first `batch`
+    sequences only (8 GPUs' share of the batch is batch / 8)."""
     import tempfile
     import torch
     import nebw
     from nebw import synth
     cfg = synth.CONFIGS[config]
     ids, _, lens = synth.config_batch(cfg)
-    w = synth.config_weights(cfg, layers=layers)
+    if batch > 0:
+        ids, lens = ids[:batch], lens[:batch]
+    n = len(lens)
+    w = synth.config_weights(cfg, layers=layers if layers > 0 else None)
     if datapath == "i8":
         from nebw.npue import write_bert_container
         with tempfile.TemporaryDirectory() as td:
@@ -241,19 +247,21 @@ def bench_encoder(dev, config, layers, iters, datapath="bf16"):
         m.set_datapath("i8")
     else:
         m = nebw.Model.from_weights(dev, w, max_seq_len=cfg.seq)
-    ids_d = torch.from_numpy(ids).cuda()
+    ids_d = torch.from_numpy(np.ascontiguousarray(ids)).cuda()
     lens_d = torch.from_numpy(lens.astype(np.int32)).cuda()
-    out = torch.empty(cfg.batch, m.hidden, device="cuda")
+    out = torch.empty(n, m.hidden, device="cuda")
     st = torch.cuda.current_stream()
+    m.set_graphs(graphs)
 
     def run():
-        m.encode_into(ids_d, lens_d, out, cfg.batch, cfg.seq, stream=st)
+        m.encode_into(ids_d, lens_d, out, n, cfg.seq, stream=st)
 
     for _ in range(3):
         run()
     torch.cuda.synchronize()
-    m.profile(True)
-    m.profile_collect()
+    if not graphs:
+        m.profile(True)
+        m.profile_collect()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(iters):
@@ -261,11 +269,14 @@ def bench_encoder(dev, config, layers, iters, datapath="bf16"):
     e1.record()
     torch.cuda.synchronize()
     dev.sync()
-    per = {k: round(ms / iters, 4) for k, (n, ms) in m.profile_collect().items() if n}
-    m.profile(False)
+    per = {}
+    if not graphs:
+        per = {k: round(ms / iters, 4) for k, (c, ms) in m.profile_collect().items() if c}
+        m.profile(False)
     m.close()
-    return {"kernel": "encoder", "config": config, "layers": layers, "datapath": datapath,
-            "ms": e0.elapsed_time(e1) / iters, "kernels_ms": per}
+    return {"kernel": "encoder", "config": config, "layers": w.layers, "batch": n,
+            "datapath": datapath, "graphs": graphs, "ms": e0.elapsed_time(e1) / iters,
+            "kernels_ms": per}
 
 
 def bench_latency(dev, config, layers, B, seq, iters):
@@ -306,6 +317,8 @@ def main(argv=None):
     ap.add_argument("op", choices=["gemm", "gemm_i8", "attention", "layernorm", "encoder",
                                    "latency", "pool", "narrow"])
     ap.add_argument("--cls", type=int, default=0, help="pool: 1 CLS row, 0 masked mean")
+    ap.add_argument("--graphs", type=int, default=0, help="encoder: replay the pass as a CUDA graph")
+    ap.add_argument("--batch", type=int, default=0, help="encoder: first N sequences (0: all)")
     ap.add_argument("--config", default="bge-large")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--M", type=int, default=16384)
@@ -340,7 +353,7 @@ def main(argv=None):
     elif a.op == "latency":
         r = bench_latency(dev, a.config, a.layers, a.B, a.len, a.iters)
     else:
-        r = bench_encoder(dev, a.config, a.layers, a.iters, a.datapath)
+        r = bench_encoder(dev, a.config, a.layers, a.iters, a.datapath, bool(a.graphs), a.batch)
     print(json.dumps(r), flush=True)
     dev.close()
 

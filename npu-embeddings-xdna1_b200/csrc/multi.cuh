@@ -492,7 +492,7 @@ int encode_gather(nebw_model *m, nebw_comm *c, const int32_t *ids_dev, const int
   if (b_r > 0) {
     if (int rc = check_pass(m, b_r, S)) return rc;
     if (int rc = ensure_workspace(m, b_r, S)) return rc;
-    if (int rc = encode_device(m, m->ws, m->prof, ids_dev, lens_dev, b_r, S, c->shard_out, st))
+    if (int rc = run_pass(m, ids_dev, lens_dev, b_r, S, c->shard_out, st))
       return rc;
   }
   float *land = c->rank == 0 ? (order_dev ? c->gathered : out_dev) : nullptr;

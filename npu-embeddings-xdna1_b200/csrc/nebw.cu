@@ -224,6 +224,10 @@ struct nebw_dev {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
   cudaStream_t stream = nullptr;
+  // where passes are captured as CUDA graphs (nebw_model_set_graphs); created
+  // on first use.  A graph is launched on the caller's stream, which may be
+  // one capture is not allowed on (the legacy default stream).
+  cudaStream_t cap_stream = nullptr;
   int *d_err = nullptr;
   std::map<uint64_t, Weight> weights;
   std::map<uint64_t, WeightI8> weights_i8;  // int8 GEMM operands (nebw_stage_weight_i8)
@@ -743,6 +747,7 @@ extern "C" int nebw_close(nebw_dev *d) {
   for (auto &kv : d->weights_i8) cudaFree(kv.second.ptr);
   cudaFree(d->d_err);
   cudaStreamDestroy(d->stream);
+  if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
   delete d;
   return NEBW_OK;
 }
@@ -1246,6 +1251,8 @@ struct nebw_model {
   // weights, the workspace, the datapath)
   struct PassGraph {
     int B, S, datapath, attn;
+    const int *ids, *lens;
+    float *out;
     cudaGraphExec_t exec;
   };
   bool use_graphs = false;
@@ -1269,7 +1276,7 @@ constexpr size_t kMaxPassGraphs = 16;
 
 void drop_graphs(nebw_model *m) {
   if (m->graphs.empty()) return;
-  cudaStreamSynchronize(m->dev->stream);  // no replay may still be running
+  cudaDeviceSynchronize();  // no replay may still be running, on whatever stream
   for (auto &g : m->graphs) cudaGraphExecDestroy(g.exec);
   m->graphs.clear();
 }
@@ -2422,40 +2429,37 @@ extern "C" int nebw_model_load_npue(nebw_dev *d, const char *path, nebw_model **
   }
 }
 
-extern "C" int nebw_encode_device(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B,
-                                  int32_t S, float *out, void *stream) {
-  NEBW_REQUIRE(m && ids && lens && out, "null argument");
-  if (int rc = use_dev(m->dev)) return rc;
-  if (int rc = check_pass(m, B, S)) return rc;
-  if (int rc = ensure_workspace(m, B, S)) return rc;
-  return encode_device(m, m->ws, m->prof, ids, lens, B, S, out, pick_stream(m->dev, stream));
-}
-
 namespace {
-// The graph of one pass of B x S on the model's own workspace, inputs
-// (m->ids, m->len_in) and output (m->out): found in the model's cache, or
-// captured from encode_device on the model's stream and instantiated (the
-// oldest of kMaxPassGraphs is dropped to make room).  The packed row count
-// and the attention work list are computed on the device inside the pass,
-// so one graph serves every length pattern of that shape.
-int pass_graph(nebw_model *m, int B, int S, cudaGraphExec_t *out) {
+// The graph of one pass of B x S on the model's workspace, from device ids /
+// lens to device out: found in the model's cache (keyed by the shape, the
+// datapath, the attention kernel and the three buffers), or captured from
+// encode_device on the device's capture stream and instantiated (the oldest
+// of kMaxPassGraphs is dropped to make room).  The caller launches it on its
+// own stream.  The packed row count and the attention work list are computed
+// on the device inside the pass, so one graph serves every length pattern of
+// that shape.
+int pass_graph(nebw_model *m, int B, int S, const int *ids, const int *lens, float *out,
+               cudaGraphExec_t *exec_out) {
   const int attn = m->dev->attn_kind;
   for (const auto &g : m->graphs)
-    if (g.B == B && g.S == S && g.datapath == m->datapath && g.attn == attn) {
-      *out = g.exec;
+    if (g.B == B && g.S == S && g.datapath == m->datapath && g.attn == attn && g.ids == ids &&
+        g.lens == lens && g.out == out) {
+      *exec_out = g.exec;
       return NEBW_OK;
     }
-  cudaStream_t st = m->dev->stream;
   if (m->graphs.size() >= kMaxPassGraphs) {
-    NEBW_CUDA(cudaStreamSynchronize(st));
+    NEBW_CUDA(cudaDeviceSynchronize());  // the oldest may still run, on any stream
     cudaGraphExecDestroy(m->graphs.front().exec);
     m->graphs.erase(m->graphs.begin());
   }
+  nebw_dev *d = m->dev;
+  if (!d->cap_stream) NEBW_CUDA(cudaStreamCreateWithFlags(&d->cap_stream, cudaStreamNonBlocking));
+  cudaStream_t cs = d->cap_stream;
   cudaGraph_t graph = nullptr;
-  NEBW_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-  const int rc = encode_device(m, m->ws, false, m->ids, m->len_in, B, S, m->out, st);
+  NEBW_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  const int rc = encode_device(m, m->ws, false, ids, lens, B, S, out, cs);
   const std::string why = rc ? g_last_error : std::string();
-  const cudaError_t e = cudaStreamEndCapture(st, &graph);
+  const cudaError_t e = cudaStreamEndCapture(cs, &graph);
   if (rc || e != cudaSuccess) {
     if (graph) cudaGraphDestroy(graph);
     cudaGetLastError();
@@ -2470,11 +2474,33 @@ int pass_graph(nebw_model *m, int B, int S, cudaGraphExec_t *out) {
     cudaGetLastError();
     return set_error(NEBW_ECUDA, "instantiating the pass graph failed: %s", cudaGetErrorString(ei));
   }
-  m->graphs.push_back({B, S, m->datapath, attn, exec});
-  *out = exec;
+  m->graphs.push_back({B, S, m->datapath, attn, ids, lens, out, exec});
+  *exec_out = exec;
   return NEBW_OK;
 }
 }  // namespace
+
+// One pass on the model's own workspace: replayed from the graph cache when
+// the model has graphs on (and is not profiling), else launched directly.
+int run_pass(nebw_model *m, const int *ids, const int *lens, int B, int S, float *out,
+             cudaStream_t st) {
+  if (m->use_graphs && !m->prof) {
+    cudaGraphExec_t exec = nullptr;
+    if (int rc = pass_graph(m, B, S, ids, lens, out, &exec)) return rc;
+    NEBW_CUDA(cudaGraphLaunch(exec, st));
+    return NEBW_OK;
+  }
+  return encode_device(m, m->ws, m->prof, ids, lens, B, S, out, st);
+}
+
+extern "C" int nebw_encode_device(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B,
+                                  int32_t S, float *out, void *stream) {
+  NEBW_REQUIRE(m && ids && lens && out, "null argument");
+  if (int rc = use_dev(m->dev)) return rc;
+  if (int rc = check_pass(m, B, S)) return rc;
+  if (int rc = ensure_workspace(m, B, S)) return rc;
+  return run_pass(m, ids, lens, B, S, out, pick_stream(m->dev, stream));
+}
 
 extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *lens, int32_t B,
                            int32_t S, float *out) {
@@ -2485,16 +2511,9 @@ extern "C" int nebw_encode(nebw_model *m, const int32_t *ids, const int32_t *len
   if (int rc = ensure_workspace(m, B, S)) return rc;
   nebw_dev *d = m->dev;
   cudaStream_t st = d->stream;
-  cudaGraphExec_t graph = nullptr;
-  if (m->use_graphs && !m->prof)
-    if (int rc = pass_graph(m, B, S, &graph)) return rc;
   NEBW_CUDA(cudaMemcpyAsync(m->ids, ids, static_cast<size_t>(B) * S * 4, cudaMemcpyHostToDevice, st));
   NEBW_CUDA(cudaMemcpyAsync(m->len_in, lens, static_cast<size_t>(B) * 4, cudaMemcpyHostToDevice, st));
-  if (graph) {
-    NEBW_CUDA(cudaGraphLaunch(graph, st));
-  } else if (int rc = encode_device(m, m->ws, m->prof, m->ids, m->len_in, B, S, m->out, st)) {
-    return rc;
-  }
+  if (int rc = run_pass(m, m->ids, m->len_in, B, S, m->out, st)) return rc;
   NEBW_CUDA(cudaMemcpyAsync(out, m->out, static_cast<size_t>(B) * m->cfg.hidden * 4,
                             cudaMemcpyDeviceToHost, st));
   return nebw_sync(d);

@@ -316,3 +316,40 @@ def test_graph_replay_matches_direct_launches(device):
     finally:
         device.set_attention_kernel(device.ATTN_TCGEN05)
         m.close()
+
+
+def test_graph_replay_device_path(device):
+    """The device-buffer entry point with graphs on: a graph per (shape,
+    buffers), replayed for new ids and lengths written into the same buffers
+    -- bit for bit the direct launches' rows -- on whichever stream the call
+    names, torch's legacy default stream (where no capture is allowed: the
+    library captures on a stream of its own) and a side stream alike."""
+    import torch
+
+    import nebw
+    from nebw import synth
+    cfg = synth.CONFIGS["bge-small"]
+    w = synth.config_weights(cfg, layers=2)
+    ids, _mask, lens = synth.config_batch(cfg)
+    B, S = 16, 512
+    m = nebw.Model.from_weights(device, w, max_seq_len=S)
+    try:
+        ids_d = torch.empty((B, S), dtype=torch.int32, device="cuda")
+        lens_d = torch.empty(B, dtype=torch.int32, device="cuda")
+        out = torch.empty((B, m.hidden), device="cuda")
+        batches = [(ids[k * B:(k + 1) * B], lens[k * B:(k + 1) * B].astype(np.int32))
+                   for k in range(3)]
+        want = [m.encode(i, l) for i, l in batches]
+        m.set_graphs(True)
+        side = torch.cuda.Stream()
+        for st in (torch.cuda.current_stream(), side, torch.cuda.current_stream()):
+            for k, (i, l) in enumerate(batches):
+                with torch.cuda.stream(st):
+                    ids_d.copy_(torch.from_numpy(np.ascontiguousarray(i)))
+                    lens_d.copy_(torch.from_numpy(l))
+                    m.encode_into(ids_d, lens_d, out, B, S, stream=st)
+                st.synchronize()
+                device.sync()
+                np.testing.assert_array_equal(out.cpu().numpy(), want[k])
+    finally:
+        m.close()
