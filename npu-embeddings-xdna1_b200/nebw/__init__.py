@@ -364,6 +364,12 @@ class Model:
         _check(lib().nebw_model_load_npue(dev.h, str(path).encode(), C.byref(h)))
         return cls(dev, h)
 
+    def set_tensor(self, name: str, arr):
+        """(Re)stage one tensor by its container name, fp32 (nebw_model_set_tensor)."""
+        a = np.ascontiguousarray(arr, np.float32)
+        rows, cols = (a.shape[0], a.shape[1]) if a.ndim == 2 else (1, a.shape[0])
+        _check(lib().nebw_model_set_tensor(self.h, name.encode(), a.ctypes.data, F32, rows, cols))
+
     DATAPATHS = {"bf16": 0, "i8": 1}
 
     def set_datapath(self, datapath: str):

@@ -353,3 +353,33 @@ def test_graph_replay_device_path(device):
                 np.testing.assert_array_equal(out.cpu().numpy(), want[k])
     finally:
         m.close()
+
+
+def test_graph_cache_eviction_and_invalidation(device):
+    """More shapes than the graph cache keeps (16): the oldest are dropped
+    and captured again when they recur, every result still the direct
+    launches' bit for bit; and setting a tensor drops the graphs, so that a
+    replay never runs on the weights it was captured with after they change."""
+    import nebw
+    from nebw import synth
+    cfg = synth.CONFIGS["minilm"]
+    w = synth.config_weights(cfg, layers=1)
+    ids, _mask, lens = synth.config_batch(cfg)
+    shapes = [(b, 128) for b in range(1, 19)] + [(1, 128), (2, 128)]
+    m = nebw.Model.from_weights(device, w, max_seq_len=cfg.seq)
+    try:
+        want = [m.encode(ids[:b, :S], lens[:b]) for b, S in shapes]
+        m.set_graphs(True)
+        for k, (b, S) in enumerate(shapes):
+            np.testing.assert_array_equal(m.encode(ids[:b, :S], lens[:b]), want[k],
+                                          err_msg=f"shape {b} x {S}")
+        g = w.ln1_g[0] * 1.5
+        m.set_tensor("layer.0.ln1.weight", g)
+        m.set_graphs(False)
+        direct = m.encode(ids[:4], lens[:4])
+        m.set_graphs(True)
+        got = m.encode(ids[:4], lens[:4])
+        np.testing.assert_array_equal(got, direct)
+        assert not np.array_equal(got, want[3])  # the new weights took effect
+    finally:
+        m.close()
