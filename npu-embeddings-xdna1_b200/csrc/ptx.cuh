@@ -72,14 +72,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
+// One try: the thread may be suspended until the phase completes or for at
+// most kTryWaitHintNs (the suspend-time hint), whichever comes first.
+constexpr uint32_t kTryWaitHintNs = 20000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(bar_addr), "r"(parity)
+      : "r"(bar_addr), "r"(parity), "n"(kTryWaitHintNs)
       : "memory");
   return done != 0;
 }
