@@ -2594,7 +2594,7 @@ extern "C" int nebw_model_profile_collect(nebw_model *m, int64_t launches[NEBW_K
 namespace {
 
 constexpr size_t kStaticScratchBytes = 64ull << 20;  // 64 MiB per GPU
-__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 constexpr int kMaxStaticDevices = 64;
 std::mutex g_static_mu;
