@@ -133,10 +133,14 @@ __global__ void __launch_bounds__(kRowWarps * 32)
                      int rows, const int *__restrict__ rows_dev, __nv_bfloat16 *__restrict__ a) {
   const int H = NV * 128;
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int idx = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   int T = rows;
   if (rows_dev) T = min(T, __ldg(rows_dev));
-  if (row >= T) return;
+  if (idx >= T) return;
+  // Rows from the last one down: the GEMM that wrote y ended on its last
+  // rows, which are still in L2, and the next GEMM starts on the first rows,
+  // which this kernel writes last.  Each row's arithmetic is the same.
+  const int row = T - 1 - idx;
   float *xr = x + static_cast<int64_t>(row) * H;
   float4 v[NV];
 #pragma unroll
@@ -170,10 +174,14 @@ __global__ void __launch_bounds__(kRowWarps * 32)
                            float *__restrict__ scale) {
   const int H = NV * 128;
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int idx = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   int T = rows;
   if (rows_dev) T = min(T, __ldg(rows_dev));
-  if (row >= T) return;
+  if (idx >= T) return;
+  // Rows from the last one down: the GEMM that wrote y ended on its last
+  // rows, which are still in L2, and the next GEMM starts on the first rows,
+  // which this kernel writes last.  Each row's arithmetic is the same.
+  const int row = T - 1 - idx;
   float *xr = x + static_cast<int64_t>(row) * H;
   float4 v[NV];
 #pragma unroll
